@@ -1,0 +1,126 @@
+/*
+ * onnxsharp_cuda.h — C ABI of libonnxsharp_cuda, the B200 (sm_100a) kernels
+ * behind OnnxSharp's matrix-multiply operators.
+ *
+ * Boundary. OnnxSharp (pure C#) reaches its operators through
+ * LayerRegistry.Register(type, factory) (src/OnnxSharp/Core/LayerRegistry.cs:14)
+ * and calls the Layer virtuals GetMemoryShapes -> PrepackWeights/Finalize ->
+ * Forward (src/OnnxSharp/Core/LayerInfo.cs:75-218, Core/Interpreter.cs:87-146).
+ * A CUDA-backed layer keeps that contract and forwards to this library through
+ * P/Invoke: PrepackWeights maps to the osc_*_prepack calls (once per constant
+ * weight, as the reference caches packed panels by tensor identity,
+ * Ops/DnnOps.cs:2823-2832), Forward maps to the kernel entry points.
+ *
+ * Conventions.
+ *  - Every call returns an int status (OSC_OK == 0). The message of the last
+ *    failure on the calling thread is returned by osc_last_error(). No call
+ *    throws, aborts or resets the device.
+ *  - Tensor pointers passed to kernel entry points are DEVICE pointers
+ *    (from osc_malloc, cudaMalloc or a framework allocator) in the context's
+ *    device. FP32 tensors are dense row-major (NCHW for images) unless a
+ *    stride argument says otherwise. Host pointers are accepted only by
+ *    osc_memcpy_htod / osc_memcpy_dtoh / osc_*_prepack_host.
+ *  - Work is enqueued on the context's stream and is asynchronous;
+ *    osc_synchronize() waits (with a bound) and reports device-side errors
+ *    (a kernel whose internal wait ran out reports OSC_ETIMEDOUT).
+ *  - One context per GPU. Calls on one context must be serialised by the
+ *    caller (the reference interpreter is single-threaded, Interpreter.cs:30);
+ *    different contexts may be driven from different host threads.
+ */
+#ifndef ONNXSHARP_CUDA_H
+#define ONNXSHARP_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(_WIN32)
+#define OSC_API __declspec(dllexport)
+#else
+#define OSC_API __attribute__((visibility("default")))
+#endif
+
+/* ------------------------------------------------------------ status codes */
+enum osc_status {
+  OSC_OK = 0,
+  OSC_EINVAL = 1,            /* bad argument (shape, null pointer, unsupported attribute) */
+  OSC_ENOMEM = 2,            /* device allocation failed */
+  OSC_ECUDA = 3,             /* a CUDA runtime/driver call failed */
+  OSC_ENCCL = 4,             /* reserved for collective failures */
+  OSC_ETIMEDOUT = 5,         /* a bounded wait (host or device) ran out */
+  OSC_EFAULT_INJECTED = 6,   /* host-side fault injection (env OSC_FAULT) */
+  OSC_EUNSUPPORTED = 7       /* valid ONNX, not implemented by this backend */
+};
+
+/* Fused activation codes (Conv.FusedActivation, Ops/DnnOps.cs:104, :493-499). */
+enum osc_act { OSC_ACT_NONE = 0, OSC_ACT_SILU = 1, OSC_ACT_RELU = 2, OSC_ACT_SIGMOID = 3 };
+
+typedef struct osc_ctx osc_ctx;
+typedef struct osc_gemm_weights osc_gemm_weights;
+
+/* ------------------------------------------------------------ context */
+
+/* Version of this ABI (major*10000 + minor*100 + patch). */
+OSC_API int osc_version(void);
+
+/* Message of the last failed call on this thread ("" if none). */
+OSC_API const char* osc_last_error(void);
+
+/* Create a context on `device` with its own non-blocking stream.
+ * Replaces the per-Net state of NetImpl (src/OnnxSharp/Core/NetImpl.cs:10). */
+OSC_API int osc_create(int device, osc_ctx** out);
+OSC_API int osc_destroy(osc_ctx* ctx);
+
+/* Make the context enqueue on a caller-owned stream (cudaStream_t), e.g. a
+ * framework's current stream. The handle is taken literally: NULL is the
+ * CUDA legacy default stream. osc_own_stream() returns the context's own
+ * stream, to switch back. */
+OSC_API int osc_set_stream(osc_ctx* ctx, void* stream);
+OSC_API void* osc_get_stream(osc_ctx* ctx);
+OSC_API void* osc_own_stream(osc_ctx* ctx);
+
+/* Wait (bounded by timeout_ms; <= 0 means 60 s) for all work on the context's
+ * stream and report device-side error words. */
+OSC_API int osc_synchronize(osc_ctx* ctx, int timeout_ms);
+
+/* Grow the context's scratch arena to at least `bytes` (per-call
+ * temporaries such as the TF32 hi/lo split of activations). Call before
+ * stream capture: a call that would need to grow it while capturing fails. */
+OSC_API int osc_reserve_scratch(osc_ctx* ctx, size_t bytes);
+
+/* Device memory and copies, for callers without a framework allocator (the
+ * reference's Tensor buffers are pinned host arrays, Tensors/Tensor.cs:65-155). */
+OSC_API int osc_malloc(osc_ctx* ctx, size_t bytes, void** out);
+OSC_API int osc_free(osc_ctx* ctx, void* ptr);
+OSC_API int osc_memcpy_htod(osc_ctx* ctx, void* dst, const void* src, size_t bytes);
+OSC_API int osc_memcpy_dtoh(osc_ctx* ctx, void* dst, const void* src, size_t bytes);
+
+/* ------------------------------------------------------------ MatMul (+FusedBias)
+ * Replaces MatMulLayer.Forward with FusedBias (src/OnnxSharp/Ops/DnnOps.cs:2789-3102)
+ * over GemmKernel.Pack / MultiplyPacked (src/OnnxSharp/Tensors/GemmKernel.cs:503, :675-852).
+ *
+ * osc_gemm_prepack_f32: pack constant B once. b_layout 0: B is [k, n] row-major
+ * (ONNX MatMul); 1: B is [n, k] row-major (ONNX Gemm transB=1). The packed
+ * form is the 3xTF32 hi/lo split in the tensor-core operand layout.
+ * `b` is a device pointer (osc_gemm_prepack_f32) or host pointer (_host). */
+OSC_API int osc_gemm_prepack_f32(osc_ctx* ctx, const float* b, int k, int n, int b_layout,
+                                 osc_gemm_weights** out);
+OSC_API int osc_gemm_prepack_f32_host(osc_ctx* ctx, const float* b, int k, int n, int b_layout,
+                                      osc_gemm_weights** out);
+OSC_API int osc_gemm_weights_free(osc_gemm_weights* w);
+
+/* C[m, n] = A[m, k] * B + col_bias[n] (col_bias may be NULL), then `act`.
+ * lda / ldc are row strides in elements (0 = dense). FP32 in and out,
+ * computed with 3xTF32 on the tensor cores (tcgen05 kind::tf32). */
+OSC_API int osc_gemm_bias_f32(osc_ctx* ctx, const float* a, int m, int k, int lda,
+                              const osc_gemm_weights* w, const float* col_bias, int act, float* c,
+                              int ldc);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ONNXSHARP_CUDA_H */

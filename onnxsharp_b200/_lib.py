@@ -1,0 +1,128 @@
+"""ctypes binding of libonnxsharp_cuda (the C ABI declared in include/onnxsharp_cuda.h).
+
+The library is loaded from the package directory (built in-tree by
+``onnxsharp_b200.build``). There is no fallback: if the shared object is
+missing or fails to load, every call raises :class:`OscUnavailable`.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libonnxsharp_cuda.so"
+
+# status codes (enum osc_status)
+OSC_OK = 0
+OSC_EINVAL = 1
+OSC_ENOMEM = 2
+OSC_ECUDA = 3
+OSC_ENCCL = 4
+OSC_ETIMEDOUT = 5
+OSC_EFAULT_INJECTED = 6
+OSC_EUNSUPPORTED = 7
+
+STATUS_NAMES = {
+    OSC_OK: "OSC_OK", OSC_EINVAL: "OSC_EINVAL", OSC_ENOMEM: "OSC_ENOMEM", OSC_ECUDA: "OSC_ECUDA",
+    OSC_ENCCL: "OSC_ENCCL", OSC_ETIMEDOUT: "OSC_ETIMEDOUT", OSC_EFAULT_INJECTED: "OSC_EFAULT_INJECTED",
+    OSC_EUNSUPPORTED: "OSC_EUNSUPPORTED",
+}
+
+# activation codes (enum osc_act)
+ACT_NONE, ACT_SILU, ACT_RELU, ACT_SIGMOID = 0, 1, 2, 3
+
+
+class OscError(RuntimeError):
+    """A non-zero status returned by the C ABI (mirrors OnnxSharpException)."""
+
+    def __init__(self, status: int, message: str, call: str):
+        self.status = status
+        self.call = call
+        super().__init__(f"{call}: {STATUS_NAMES.get(status, status)}: {message}")
+
+
+class OscUnavailable(RuntimeError):
+    """The CUDA library could not be loaded (not built, or no CUDA driver)."""
+
+
+vp = C.c_void_p
+i32 = C.c_int
+f32 = C.c_float
+sz = C.c_size_t
+pp = C.POINTER(C.c_void_p)
+
+# name -> (restype, argtypes). Kept in the order of include/onnxsharp_cuda.h.
+SIGNATURES: dict[str, tuple] = {
+    "osc_version": (i32, []),
+    "osc_last_error": (C.c_char_p, []),
+    "osc_create": (i32, [i32, pp]),
+    "osc_destroy": (i32, [vp]),
+    "osc_set_stream": (i32, [vp, vp]),
+    "osc_get_stream": (vp, [vp]),
+    "osc_own_stream": (vp, [vp]),
+    "osc_synchronize": (i32, [vp, i32]),
+    "osc_reserve_scratch": (i32, [vp, sz]),
+    "osc_malloc": (i32, [vp, sz, pp]),
+    "osc_free": (i32, [vp, vp]),
+    "osc_memcpy_htod": (i32, [vp, vp, vp, sz]),
+    "osc_memcpy_dtoh": (i32, [vp, vp, vp, sz]),
+    # MatMul + FusedBias
+    "osc_gemm_prepack_f32": (i32, [vp, vp, i32, i32, i32, pp]),
+    "osc_gemm_prepack_f32_host": (i32, [vp, vp, i32, i32, i32, pp]),
+    "osc_gemm_weights_free": (i32, [vp]),
+    "osc_gemm_bias_f32": (i32, [vp, vp, i32, i32, i32, vp, vp, i32, vp, i32]),
+}
+
+_lib: C.CDLL | None = None
+_load_error: str | None = None
+
+
+def load() -> C.CDLL:
+    """Load the shared library once and attach the signatures."""
+    global _lib, _load_error
+    if _lib is not None:
+        return _lib
+    if _load_error is not None:
+        raise OscUnavailable(_load_error)
+    path = Path(os.environ.get("OSC_LIB", LIB_PATH))
+    if not path.exists():
+        _load_error = f"{path} is not built (run python -m onnxsharp_b200.build)"
+        raise OscUnavailable(_load_error)
+    try:
+        lib = C.CDLL(str(path))
+    except OSError as e:  # pragma: no cover - depends on the machine
+        _load_error = f"cannot load {path}: {e}"
+        raise OscUnavailable(_load_error) from e
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+def last_error() -> str:
+    msg = load().osc_last_error()
+    return msg.decode("utf-8", "replace") if msg else ""
+
+
+def call(name: str, *args):
+    """Call an int-returning ABI function; raise OscError on a non-zero status."""
+    fn = getattr(load(), name)
+    st = fn(*args)
+    if st != OSC_OK:
+        raise OscError(st, last_error(), name)
+    return st
+
+
+def ptr(x) -> int | None:
+    """Device or host address of a torch tensor / numpy array / int / None."""
+    if x is None:
+        return None
+    if isinstance(x, int):
+        return x
+    if hasattr(x, "data_ptr"):
+        return x.data_ptr()
+    if hasattr(x, "ctypes"):
+        return x.ctypes.data
+    raise TypeError(f"cannot take the address of {type(x).__name__}")

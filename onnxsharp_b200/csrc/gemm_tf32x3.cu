@@ -1,0 +1,308 @@
+// gemm_tf32x3.cu — FP32 MatMul(+FusedBias, +activation) on the sm_100a tensor
+// cores with the 3xTF32 split.
+//
+// Replaces GemmKernel.MultiplyPacked (src/OnnxSharp/Tensors/GemmKernel.cs:675-852)
+// behind MatMulLayer with FusedBias (src/OnnxSharp/Ops/DnnOps.cs:2789-3102).
+// The reference accumulates each C element as one FMA chain from bias[j]
+// (GemmKernel.cs:1156-1208); on the tensor cores the summation order differs,
+// so parity is the reference's own tolerance |d|/max(1,|ref|) <= 1e-4
+// (tests/OnnxSharp.Tests/GemmKernelTests.cs:116-120).
+//
+// Numerics: every FP32 operand x is split into hi = tf32(x) and lo = x - hi
+// (exact in FP32); C += Ahi*Bhi + Ahi*Blo + Alo*Bhi with FP32 accumulation in
+// TMEM. The dropped Alo*Blo term is ~2^-22 relative.
+//
+// Kernel shape: one 128 x BN output tile per CTA, BK = 32 (one 128-byte
+// swizzle row per operand row). Warp 0 issues TMA loads of the four operand
+// tiles (A hi/lo, B hi/lo) into a STAGES-deep shared-memory ring; warp 1
+// allocates TMEM and issues tcgen05.mma (3 per 8-wide K step) from one
+// thread, releasing each stage with tcgen05.commit; warps 2-5 read the
+// accumulator back from TMEM and apply bias + activation.
+#include <cstdlib>
+
+#include "runtime.h"
+#include "sm100.cuh"
+#include "tf32x3_core.cuh"
+#include "vmath.cuh"
+
+struct osc_gemm_weights {
+  int device = 0;
+  int k = 0, n = 0, kp = 0;  // kp: K padded to a multiple of 4 (16-byte TMA row pitch)
+  float* hi = nullptr;       // [n][kp] tf32(B^T)
+  float* lo = nullptr;       // [n][kp] B^T - hi
+};
+
+namespace osc {
+namespace {
+
+template <class Cfg>
+__global__ void __launch_bounds__(Cfg::THREADS, 1)
+    k_gemm_tf32x3(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUtensorMap mAl,
+                  const __grid_constant__ CUtensorMap mBh, const __grid_constant__ CUtensorMap mBl, int M, int N,
+                  int Kp, const float* __restrict__ col_bias, int act, float* __restrict__ C, int ldc,
+                  int* __restrict__ err) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* tiles = tiles_base<Cfg>(smem_raw);
+  PipeBarriers* pb = barriers<Cfg>(tiles);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int m0 = blockIdx.y * kBM;
+  const int n0 = blockIdx.x * Cfg::BN;
+  const int num_kb = (Kp + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    tma_prefetch(&mAh);
+    tma_prefetch(&mAl);
+    tma_prefetch(&mBh);
+    tma_prefetch(&mBl);
+  }
+  const uint32_t tmem = pipe_setup<Cfg>(pb);
+
+  if (warp == 0) {
+    if (lane == 0)
+      producer_loop<Cfg>(tiles, pb, num_kb, err, [&](int kb, uint8_t* st, uint64_t* bar) {
+        const int kc = kb * kBK;
+        tma_load_2d(st, &mAh, bar, kc, m0);
+        tma_load_2d(st + Cfg::A_BYTES, &mAl, bar, kc, m0);
+        tma_load_2d(st + 2 * Cfg::A_BYTES, &mBh, bar, kc, n0);
+        tma_load_2d(st + 2 * Cfg::A_BYTES + Cfg::B_BYTES, &mBl, bar, kc, n0);
+      });
+  } else if (warp == 1) {
+    if (lane == 0) mma_loop<Cfg>(tiles, pb, tmem, num_kb, err);
+  } else {
+    float acc[128];
+    if (drain_loop<Cfg>(pb, tmem, num_kb, acc, err)) {
+      const int row = m0 + (warp & 3) * 32 + lane;
+      const int col0 = n0 + ((warp - 2) >> 2) * 128;
+      if (row < M && col0 < N) {
+        float* crow = C + static_cast<size_t>(row) * ldc + col0;
+        const int ncols = min(128, N - col0);
+        const bool vec = ncols == 128 && ((ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(C) & 15u) == 0);
+#pragma unroll
+        for (int j = 0; j < 128; j += 4) {
+          float v[4];
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            float x = acc[j + t];
+            if (col_bias != nullptr && j + t < ncols) x = __fadd_rn(x, __ldg(col_bias + col0 + j + t));
+            v[t] = apply_act(x, act);
+          }
+          if (vec) {
+            *reinterpret_cast<float4*>(crow + j) = make_float4(v[0], v[1], v[2], v[3]);
+          } else {
+#pragma unroll
+            for (int t = 0; t < 4; ++t)
+              if (j + t < ncols) crow[j + t] = v[t];
+          }
+        }
+      }
+    }
+  }
+  pipe_teardown<Cfg>(pb, tmem);
+}
+
+// [rows][k] (row pitch ld) -> hi/lo [rows][kp], zero-padded for k <= c < kp.
+__global__ void k_split_rows(const float* __restrict__ src, int rows, int k, int ld, int kp, float* __restrict__ hi,
+                             float* __restrict__ lo) {
+  const size_t total4 = static_cast<size_t>(rows) * (kp >> 2);
+  const bool vec = ((ld & 3) == 0) && ((reinterpret_cast<uintptr_t>(src) & 15u) == 0);
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total4;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const size_t r = i / (kp >> 2);
+    const int c = static_cast<int>(i - r * (kp >> 2)) * 4;
+    const float* s = src + r * static_cast<size_t>(ld);
+    float v[4];
+    if (vec && c + 4 <= k) {
+      const float4 t = __ldg(reinterpret_cast<const float4*>(s + c));
+      v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) v[j] = (c + j < k) ? s[c + j] : 0.0f;
+    }
+    float h[4], l[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      h[j] = to_tf32(v[j]);
+      l[j] = __fsub_rn(v[j], h[j]);
+    }
+    const size_t o = r * static_cast<size_t>(kp) + c;
+    *reinterpret_cast<float4*>(hi + o) = make_float4(h[0], h[1], h[2], h[3]);
+    *reinterpret_cast<float4*>(lo + o) = make_float4(l[0], l[1], l[2], l[3]);
+  }
+}
+
+// B[k][n] (row-major, MatMul layout) -> hi/lo [n][kp] (transposed, split, zero-padded).
+__global__ void k_pack_b_kn(const float* __restrict__ b, int k, int n, int kp, float* __restrict__ hi,
+                            float* __restrict__ lo) {
+  __shared__ float tile[32][33];
+  const int n0 = blockIdx.x * 32, k0 = blockIdx.y * 32;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8 threads
+  for (int yy = ty; yy < 32; yy += 8) {
+    const int kk = k0 + yy, nn = n0 + tx;
+    tile[yy][tx] = (kk < k && nn < n) ? b[static_cast<size_t>(kk) * n + nn] : 0.0f;
+  }
+  __syncthreads();
+  for (int yy = ty; yy < 32; yy += 8) {
+    const int nn = n0 + yy, kk = k0 + tx;
+    if (nn < n && kk < kp) {
+      const float v = tile[tx][yy];
+      const float h = to_tf32(v);
+      hi[static_cast<size_t>(nn) * kp + kk] = h;
+      lo[static_cast<size_t>(nn) * kp + kk] = __fsub_rn(v, h);
+    }
+  }
+}
+
+template <class Cfg>
+int launch_gemm(osc_ctx* ctx, const float* ahi, const float* alo, int M, int Kp, const osc_gemm_weights* w,
+                const float* bias, int act, float* C, int ldc) {
+  CUtensorMap mAh, mAl, mBh, mBl;
+  const uint64_t dimsA[2] = {static_cast<uint64_t>(Kp), static_cast<uint64_t>(M)};
+  const uint64_t dimsB[2] = {static_cast<uint64_t>(Kp), static_cast<uint64_t>(w->n)};
+  const uint64_t pitch[1] = {static_cast<uint64_t>(Kp) * 4};
+  const uint32_t boxA[2] = {kBK, kBM};
+  const uint32_t boxB[2] = {kBK, static_cast<uint32_t>(Cfg::BN)};
+  OSC_TRY(encode_tiled(&mAh, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, ahi, dimsA, pitch, boxA, CU_TENSOR_MAP_SWIZZLE_128B));
+  OSC_TRY(encode_tiled(&mAl, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, alo, dimsA, pitch, boxA, CU_TENSOR_MAP_SWIZZLE_128B));
+  OSC_TRY(encode_tiled(&mBh, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, w->hi, dimsB, pitch, boxB, CU_TENSOR_MAP_SWIZZLE_128B));
+  OSC_TRY(encode_tiled(&mBl, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, w->lo, dimsB, pitch, boxB, CU_TENSOR_MAP_SWIZZLE_128B));
+  auto kern = k_gemm_tf32x3<Cfg>;
+  OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(kern), Cfg::SMEM_BYTES));
+  dim3 grid((w->n + Cfg::BN - 1) / Cfg::BN, (M + kBM - 1) / kBM);
+  kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, ctx->stream>>>(mAh, mAl, mBh, mBl, M, w->n, Kp, bias, act, C, ldc,
+                                                              ctx->d_err);
+  return check_launch(ctx, "k_gemm_tf32x3");
+}
+
+int grid_for(osc_ctx* ctx, size_t work, int per_thread) {
+  size_t blocks = (work + static_cast<size_t>(256) * per_thread - 1) / (static_cast<size_t>(256) * per_thread);
+  const size_t cap = static_cast<size_t>(ctx->num_sms) * 8;
+  if (blocks > cap) blocks = cap;
+  return static_cast<int>(blocks < 1 ? 1 : blocks);
+}
+
+}  // namespace
+
+// Shared with the other kernels that consume split activations.
+int split_tf32(osc_ctx* ctx, const float* src, int rows, int k, int ld, int kp, float* hi, float* lo) {
+  const size_t work = static_cast<size_t>(rows) * (kp / 4);
+  k_split_rows<<<grid_for(ctx, work, 1), 256, 0, ctx->stream>>>(src, rows, k, ld, kp, hi, lo);
+  return check_launch(ctx, "k_split_rows");
+}
+
+int gemm_tf32x3(osc_ctx* ctx, const float* a, int m, int k, int lda, const osc_gemm_weights* w,
+                const float* col_bias, int act, float* c, int ldc) {
+  const int kp = w->kp;
+  void* buf = nullptr;
+  const size_t half = round_up(static_cast<size_t>(m) * kp * sizeof(float), 256);
+  OSC_TRY(scratch(ctx, 2 * half, &buf));
+  float* ahi = static_cast<float*>(buf);
+  float* alo = reinterpret_cast<float*>(static_cast<uint8_t*>(buf) + half);
+  OSC_TRY(split_tf32(ctx, a, m, k, lda, kp, ahi, alo));
+  static const int bn_env = [] {
+    const char* v = std::getenv("OSC_GEMM_BN");
+    return v ? std::atoi(v) : 0;
+  }();
+  int bn = bn_env;
+  if (bn != 128 && bn != 256) {
+    // Prefer the wider tile (less operand traffic per FLOP) unless it leaves
+    // most SMs idle.
+    const long tiles256 = static_cast<long>((w->n + 255) / 256) * ((m + kBM - 1) / kBM);
+    bn = (tiles256 >= ctx->num_sms * 3 / 4 || w->n <= 128) ? (w->n <= 128 ? 128 : 256) : 128;
+  }
+  if (bn == 256) return launch_gemm<Tf32x3Cfg<256, 2, 2>>(ctx, ahi, alo, m, kp, w, col_bias, act, c, ldc);
+  return launch_gemm<Tf32x3Cfg<128, 3, 2>>(ctx, ahi, alo, m, kp, w, col_bias, act, c, ldc);
+}
+
+}  // namespace osc
+
+using namespace osc;
+
+static int gemm_prepack(osc_ctx* ctx, const float* b, int k, int n, int b_layout, bool host, osc_gemm_weights** out) {
+  if (out == nullptr) return fail(OSC_EINVAL, "osc_gemm_prepack_f32: out is null");
+  *out = nullptr;
+  OSC_TRY(enter(ctx));
+  if (b == nullptr || k <= 0 || n <= 0) return fail(OSC_EINVAL, "osc_gemm_prepack_f32: bad B [%d, %d]", k, n);
+  if (b_layout != 0 && b_layout != 1) return fail(OSC_EINVAL, "osc_gemm_prepack_f32: b_layout must be 0 or 1");
+  if (fault_injected("prepack")) return fail(OSC_EFAULT_INJECTED, "injected failure (prepack)");
+  auto* w = new osc_gemm_weights();
+  w->device = ctx->device;
+  w->k = k;
+  w->n = n;
+  w->kp = static_cast<int>(round_up(static_cast<size_t>(k), 4));
+  const size_t bytes = static_cast<size_t>(n) * w->kp * sizeof(float);
+  float* staged = nullptr;
+  cudaError_t e = cudaMalloc(&w->hi, bytes);
+  if (e == cudaSuccess) e = cudaMalloc(&w->lo, bytes);
+  if (e == cudaSuccess && host) {
+    e = cudaMalloc(&staged, static_cast<size_t>(k) * n * sizeof(float));
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(staged, b, static_cast<size_t>(k) * n * sizeof(float), cudaMemcpyHostToDevice, ctx->stream);
+    b = staged;
+  }
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    cudaFree(w->hi);
+    cudaFree(w->lo);
+    cudaFree(staged);
+    delete w;
+    return fail(OSC_ENOMEM, "osc_gemm_prepack_f32: %s", cudaGetErrorString(e));
+  }
+  int st;
+  if (b_layout == 0) {
+    dim3 grid((n + 31) / 32, (w->kp + 31) / 32);
+    k_pack_b_kn<<<grid, 256, 0, ctx->stream>>>(b, k, n, w->kp, w->hi, w->lo);
+    st = check_launch(ctx, "k_pack_b_kn");
+  } else {
+    st = split_tf32(ctx, b, n, k, k, w->kp, w->hi, w->lo);
+  }
+  if (staged) {
+    cudaStreamSynchronize(ctx->stream);
+    cudaFree(staged);
+  }
+  if (st != OSC_OK) {
+    osc_gemm_weights_free(w);
+    return st;
+  }
+  *out = w;
+  return OSC_OK;
+}
+
+extern "C" {
+
+OSC_API int osc_gemm_prepack_f32(osc_ctx* ctx, const float* b, int k, int n, int b_layout, osc_gemm_weights** out) {
+  return gemm_prepack(ctx, b, k, n, b_layout, false, out);
+}
+
+OSC_API int osc_gemm_prepack_f32_host(osc_ctx* ctx, const float* b, int k, int n, int b_layout,
+                                      osc_gemm_weights** out) {
+  return gemm_prepack(ctx, b, k, n, b_layout, true, out);
+}
+
+OSC_API int osc_gemm_weights_free(osc_gemm_weights* w) {
+  if (w == nullptr) return OSC_OK;
+  cudaSetDevice(w->device);
+  cudaDeviceSynchronize();
+  cudaFree(w->hi);
+  cudaFree(w->lo);
+  delete w;
+  return OSC_OK;
+}
+
+OSC_API int osc_gemm_bias_f32(osc_ctx* ctx, const float* a, int m, int k, int lda, const osc_gemm_weights* w,
+                              const float* col_bias, int act, float* c, int ldc) {
+  OSC_TRY(enter(ctx));
+  if (w == nullptr || a == nullptr || c == nullptr) return fail(OSC_EINVAL, "osc_gemm_bias_f32: null pointer");
+  if (w->device != ctx->device) return fail(OSC_EINVAL, "osc_gemm_bias_f32: weights live on another device");
+  if (k != w->k) return fail(OSC_EINVAL, "osc_gemm_bias_f32: A has k=%d, packed B has k=%d", k, w->k);
+  if (m < 0) return fail(OSC_EINVAL, "osc_gemm_bias_f32: m=%d", m);
+  if (act < OSC_ACT_NONE || act > OSC_ACT_SIGMOID) return fail(OSC_EINVAL, "osc_gemm_bias_f32: act=%d", act);
+  if (lda == 0) lda = k;
+  if (ldc == 0) ldc = w->n;
+  if (lda < k || ldc < w->n) return fail(OSC_EINVAL, "osc_gemm_bias_f32: lda=%d ldc=%d too small", lda, ldc);
+  if (m == 0) return OSC_OK;
+  if (fault_injected("launch")) return fail(OSC_EFAULT_INJECTED, "injected failure (launch)");
+  return gemm_tf32x3(ctx, a, m, k, lda, w, col_bias, act, c, ldc);
+}
+
+}  // extern "C"

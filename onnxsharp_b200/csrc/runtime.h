@@ -1,0 +1,75 @@
+// runtime.h — internal state behind the C ABI: the per-GPU context (stream,
+// device error word, scratch arena), error reporting, host-side fault
+// injection and the TMA descriptor encoder.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstddef>
+#include <cstdint>
+#include <string>
+
+#include "../../include/onnxsharp_cuda.h"
+
+struct osc_ctx {
+  int device = 0;
+  int num_sms = 0;
+  cudaStream_t own_stream = nullptr;
+  cudaStream_t stream = nullptr;  // where work is enqueued (own or caller's)
+  int* d_err = nullptr;           // device error word, written by kernels on failure
+  void* scratch = nullptr;        // grow-only per-call temporaries
+  size_t scratch_bytes = 0;
+};
+
+namespace osc {
+
+// Records a formatted message for osc_last_error() and returns `code`.
+int fail(int code, const char* fmt, ...);
+
+// Maps a CUDA error to OSC_ECUDA with a message naming the call site.
+int cuda_fail(cudaError_t e, const char* what);
+
+// Host-side fault injection: OSC_FAULT=<site>[,<site>...] makes the named
+// sites ("alloc", "launch", "sync", "prepack", "all") fail with
+// OSC_EFAULT_INJECTED before touching the device.
+bool fault_injected(const char* site);
+
+// Makes `ctx->device` current; returns OSC_OK or an error code.
+int enter(osc_ctx* ctx);
+
+// Scratch arena of at least `bytes`, 256-byte aligned. Fails during stream
+// capture if it would have to grow.
+int scratch(osc_ctx* ctx, size_t bytes, void** out);
+
+// True while ctx->stream is being captured into a CUDA graph.
+bool capturing(osc_ctx* ctx);
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
+int encode_tiled(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base,
+                 const uint64_t* dims, const uint64_t* strides_bytes /* rank-1 */, const uint32_t* box,
+                 CUtensorMapSwizzle swizzle);
+
+// Checks a kernel launch and (when OSC_SYNC_CHECK=1) synchronises to surface
+// faults at the call that caused them.
+int check_launch(osc_ctx* ctx, const char* what);
+
+// Raises a kernel's dynamic shared memory limit once per (device, kernel).
+int set_smem_attr(osc_ctx* ctx, const void* func, int bytes);
+
+inline size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+}  // namespace osc
+
+#define OSC_TRY(expr)          \
+  do {                         \
+    int _st = (expr);          \
+    if (_st != OSC_OK) return _st; \
+  } while (0)
+
+#define OSC_CUDA(expr, what)                                  \
+  do {                                                        \
+    cudaError_t _e = (expr);                                  \
+    if (_e != cudaSuccess) return ::osc::cuda_fail(_e, what); \
+  } while (0)

@@ -1,0 +1,52 @@
+// vmath.cuh — the reference engine's vector transcendental functions, restated
+// for the device so that fused epilogues produce the same bits as the CPU
+// path's AVX2 bulk loop.
+//
+// Reference: src/OnnxSharp/Tensors/VectorMath.cs:21-43 (Exp: clamp to
+// [-87.3, 88.7], n = rint(x*log2e), two-step Cody-Waite reduction, degree-6
+// Horner polynomial with explicit FMAs, 2^n built from exponent bits),
+// :70-74 (Sigmoid = 1/(1+exp(-x))), :77 (Silu = x*sigmoid(x)).
+// Every operation uses an explicitly rounded intrinsic so nvcc cannot contract
+// or reorder it.
+#pragma once
+
+#include <cuda_runtime.h>
+
+namespace osc {
+
+__device__ __forceinline__ float ref_exp(float x) {
+  // Avx.Max(x, c) returns c for NaN x, as fmaxf does.
+  x = fminf(fmaxf(x, -87.3f), 88.7f);
+  const float n = rintf(__fmul_rn(x, 1.4426950408889634f));
+  float r = __fmaf_rn(n, -0.693145751953125f, x);
+  r = __fmaf_rn(n, -1.4286067653e-6f, r);
+  float p = 1.0f / 720.0f;
+  p = __fmaf_rn(p, r, 1.0f / 120.0f);
+  p = __fmaf_rn(p, r, 1.0f / 24.0f);
+  p = __fmaf_rn(p, r, 1.0f / 6.0f);
+  p = __fmaf_rn(p, r, 0.5f);
+  p = __fmaf_rn(p, r, 1.0f);
+  p = __fmaf_rn(p, r, 1.0f);
+  const int e = (__float2int_rn(n) + 127) << 23;
+  return __fmul_rn(p, __int_as_float(e));
+}
+
+__device__ __forceinline__ float ref_sigmoid(float x) {
+  return __fdiv_rn(1.0f, __fadd_rn(1.0f, ref_exp(__fmul_rn(x, -1.0f))));
+}
+
+__device__ __forceinline__ float ref_silu(float x) { return __fmul_rn(x, ref_sigmoid(x)); }
+
+// Activation codes shared by every fused epilogue (match osc_act in the C ABI).
+enum : int { ACT_NONE = 0, ACT_SILU = 1, ACT_RELU = 2, ACT_SIGMOID = 3 };
+
+__device__ __forceinline__ float apply_act(float v, int act) {
+  switch (act) {
+    case ACT_SILU: return ref_silu(v);
+    case ACT_RELU: return v > 0.0f ? v : 0.0f;
+    case ACT_SIGMOID: return ref_sigmoid(v);
+    default: return v;
+  }
+}
+
+}  // namespace osc

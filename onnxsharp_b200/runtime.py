@@ -1,0 +1,75 @@
+"""Host-side handles over the C ABI: the per-GPU context and packed weights.
+
+Mirrors the reference's split between a one-time weight prepack
+(Layer.PrepackWeights, src/OnnxSharp/Core/LayerInfo.cs:75-218, with packed
+panels cached by tensor identity, Ops/DnnOps.cs:2823-2832) and a per-inference
+Forward. Tensors are torch tensors on the context's device; torch is used for
+device memory and streams only, every computation runs in libonnxsharp_cuda.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import weakref
+
+from . import _lib
+from ._lib import call, ptr
+
+
+class Context:
+    """One GPU: a stream, a device error word and a scratch arena (osc_ctx)."""
+
+    def __init__(self, device: int = 0, stream: int | None = None):
+        _lib.load()
+        h = C.c_void_p()
+        call("osc_create", int(device), C.byref(h))
+        self.handle = h
+        self.device = int(device)
+        self._finalizer = weakref.finalize(self, _lib.load().osc_destroy, h)
+        if stream is not None:
+            self.set_stream(stream)
+
+    def set_stream(self, stream: int | None) -> None:
+        call("osc_set_stream", self.handle, stream)
+
+    def use_torch_stream(self) -> None:
+        import torch
+
+        self.set_stream(torch.cuda.current_stream(self.device).cuda_stream)
+
+    def synchronize(self, timeout_ms: int = 60000) -> None:
+        call("osc_synchronize", self.handle, int(timeout_ms))
+
+    def reserve_scratch(self, nbytes: int) -> None:
+        call("osc_reserve_scratch", self.handle, int(nbytes))
+
+    def close(self) -> None:
+        self._finalizer()
+
+
+class GemmWeights:
+    """Constant B of a MatMul/Gemm, prepacked once into the 3xTF32 operand form."""
+
+    def __init__(self, ctx: Context, b, k: int, n: int, layout: int = 0):
+        h = C.c_void_p()
+        name = "osc_gemm_prepack_f32" if _is_device(b) else "osc_gemm_prepack_f32_host"
+        call(name, ctx.handle, ptr(b), int(k), int(n), int(layout), C.byref(h))
+        self.handle = h
+        self.k, self.n = int(k), int(n)
+        self._finalizer = weakref.finalize(self, _lib.load().osc_gemm_weights_free, h)
+
+
+def _is_device(x) -> bool:
+    return bool(getattr(x, "is_cuda", False))
+
+
+def gemm_bias(ctx: Context, a, w: GemmWeights, bias=None, act: int = _lib.ACT_NONE, out=None, lda: int = 0,
+              ldc: int = 0):
+    """C = A @ B + bias (FusedBias), then `act`; A is [m, k] FP32 on the device."""
+    import torch
+
+    m, k = a.shape[0], w.k
+    if out is None:
+        out = torch.empty((m, w.n), dtype=torch.float32, device=a.device)
+    call("osc_gemm_bias_f32", ctx.handle, ptr(a), int(m), int(k), int(lda or a.stride(0)), w.handle, ptr(bias),
+         int(act), ptr(out), int(ldc or out.stride(0)))
+    return out
