@@ -1,0 +1,546 @@
+#!/usr/bin/env python
+"""bench.py — throughput of OnnxSharp's matrix-multiply hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
+
+One process per GPU (torchrun for N > 1, NCCL process group for the barrier
+and the max-over-ranks reduction). Each rank runs the same workload on its own
+seeded synthetic data (weak scaling: images / rows are independent, so the
+path shards with no data-path collective). Rank 0 prints ONE JSON line.
+
+Timed region: W untimed warm-up steps, then exactly K steps bracketed by a
+barrier + cuda synchronize on both sides. Every step is timed with CUDA events
+on the stream the kernels run on; L2 is flushed (a 512 MiB device write)
+between steps, outside the events. `value` is the whole-job throughput with
+inputs resident in HBM; `e2e` is the same metric through the public API with
+pinned host buffers (H2D of the step's inputs + D2H of its output inside the
+timed region). `roofline` reports the dominant kernel against the measured
+peaks in MEASURED_PEAKS.json; `cpu_baseline` times the CPU oracle (a
+restatement of the reference's CPU kernels) on a bounded sample.
+
+--impl reference times the reference's CPU algorithm (the oracle port: the
+reference is C# and cannot run here) on the host cores, same metric/config.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "GEMM/Conv TFLOPS (% roofline); YOLO11n-shape images/sec at 1/2/4/8 B200"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def load_peaks() -> tuple[dict, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text()), "measured"
+        except (OSError, ValueError):
+            pass
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def load_traffic(workload: str):
+    """DRAM bytes per dominant-kernel launch from a committed ncu summary (profiles/traffic.json)."""
+    p = ROOT / "profiles" / "traffic.json"
+    try:
+        entry = json.loads(p.read_text()).get(workload)
+    except (OSError, ValueError):
+        return None
+    return None if entry is None else entry.get("bytes_per_launch")
+
+
+def physical_cores() -> int:
+    try:
+        out = subprocess.run(["lscpu", "-p=core,socket"], capture_output=True, text=True, timeout=10).stdout
+        cores = {tuple(l.split(",")) for l in out.splitlines() if l and not l.startswith("#")}
+        if cores:
+            return len(cores)
+    except (OSError, subprocess.SubprocessError):
+        pass
+    return os.cpu_count() or 1
+
+
+def cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+# ----------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=self.file, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=10)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.file.flush()
+        rows = []
+        for line in Path(self.file.name).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), float(parts[3]), parts[5:9]))
+            except ValueError:
+                continue
+        os.unlink(self.file.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
+        loaded = [r for r in rows if r[2] > 250.0] or rows
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in loaded for i, v in enumerate(r[3]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in loaded), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": reasons, "samples": len(rows), "samples_under_load": len(loaded)}
+
+
+# ----------------------------------------------------------------- workloads
+class Workload:
+    """One pass of the hot path over one batch of synthetic input."""
+
+    name = ""
+    unit = "TFLOP/s"
+    main_kernel = ""   # dominant kernel (profile prefix)
+    bound = "tensor"
+
+    def units_per_step(self) -> float:       # FLOPs (or images) per step
+        raise NotImplementedError
+
+    def step(self):                           # device-resident inputs
+        raise NotImplementedError
+
+    def e2e_step(self):                       # pinned host in, pinned host out
+        raise NotImplementedError
+
+    def e2e_bytes(self) -> tuple[int, int]:
+        raise NotImplementedError
+
+    def main_kernel_units(self) -> float:     # algorithmic FLOPs (or bytes) of one dominant-kernel launch
+        return self.units_per_step()
+
+    def cpu_sample(self, threads: int) -> dict:
+        raise NotImplementedError
+
+
+def _scale(v: float) -> float:
+    return v / 1e12
+
+
+class GemmWorkload(Workload):
+    """MatMul+Add(bias) A[2048,512] x B[512,2048] + bias[2048], U(-1,1)."""
+
+    name = "matmul_bias_f32_2048x512x2048"
+    main_kernel = "k_gemm_tf32x3"
+
+    def __init__(self, ctx, rank: int, m=2048, k=512, n=2048):
+        import torch
+
+        from onnxsharp_b200.runtime import GemmWeights
+
+        self.m, self.k, self.n = m, k, n
+        rng = np.random.default_rng(1234 + rank)
+        self.a_h = rng.uniform(-1, 1, (m, k)).astype(np.float32)
+        self.b_h = rng.uniform(-1, 1, (k, n)).astype(np.float32)
+        self.bias_h = rng.uniform(-1, 1, n).astype(np.float32)
+        dev = torch.device("cuda", torch.cuda.current_device())
+        self.ctx = ctx
+        self.a = torch.from_numpy(self.a_h).to(dev)
+        self.bias = torch.from_numpy(self.bias_h).to(dev)
+        self.c = torch.empty((m, n), dtype=torch.float32, device=dev)
+        self.w = GemmWeights(ctx, torch.from_numpy(self.b_h).to(dev), k, n)
+        # e2e: pinned host buffers and device staging
+        self.a_pin = torch.from_numpy(self.a_h).pin_memory()
+        self.c_pin = torch.empty((m, n), dtype=torch.float32).pin_memory()
+        self.a_dev2 = torch.empty_like(self.a)
+        self.c_dev2 = torch.empty_like(self.c)
+        self.config = {"workload": self.name, "m": m, "k": k, "n": n, "bias": True,
+                       "precision": "3xTF32 (tcgen05 kind::tf32), FP32 in/out"}
+
+    def units_per_step(self) -> float:
+        return 2.0 * self.m * self.k * self.n
+
+    def step(self):
+        from onnxsharp_b200.runtime import gemm_bias
+
+        gemm_bias(self.ctx, self.a, self.w, self.bias, out=self.c)
+
+    def e2e_step(self):
+        from onnxsharp_b200.runtime import gemm_bias
+
+        self.ctx.memcpy_htod(self.a_dev2, self.a_pin, self.a_pin.numel() * 4)
+        gemm_bias(self.ctx, self.a_dev2, self.w, self.bias, out=self.c_dev2)
+        self.ctx.memcpy_dtoh(self.c_pin, self.c_dev2, self.c_pin.numel() * 4)
+
+    def e2e_bytes(self):
+        return self.m * self.k * 4, self.m * self.n * 4
+
+    def cpu_sample(self, threads: int) -> dict:
+        import oracle
+
+        rows = self.m
+        t0 = time.perf_counter()
+        reps = 0
+        while True:
+            oracle.gemm(self.a_h[:rows], self.b_h, col_bias=self.bias_h, threads=threads)
+            reps += 1
+            if time.perf_counter() - t0 > 1.5:
+                break
+        dt = time.perf_counter() - t0
+        flops = 2.0 * rows * self.k * self.n * reps
+        return {"value": _scale(flops / dt), "unit": self.unit, "cores": threads,
+                "sample": f"{reps} x full GEMM {rows}x{self.k}x{self.n}+bias ({dt:.2f} s wall)"}
+
+
+def conv_inputs(seed: int, batch: int):
+    """BASELINE config 2 synthetic data: x U(0,1), W He-normal, b N(0, 0.01)."""
+    rng = np.random.default_rng(seed)
+    x = rng.uniform(0, 1, (batch, 64, 160, 160)).astype(np.float32)
+    w = (rng.normal(0, 1, (128, 64, 3, 3)) * np.sqrt(2.0 / (64 * 9))).astype(np.float32)
+    b = rng.normal(0, 0.01, 128).astype(np.float32)
+    return x, w, b
+
+
+CONV_FLOPS_PER_IMAGE = 2.0 * 128 * 160 * 160 * 64 * 9
+
+
+class ConvWorkload(Workload):
+    """fused Conv+SiLU, x[16,64,160,160] -> y[16,128,160,160], 3x3 s1 p1."""
+
+    name = "conv3x3_silu_f32_b16_64to128_160x160"
+    main_kernel = "k_conv_tf32x3"
+
+    def __init__(self, ctx, rank: int, batch: int = 16):
+        import torch
+
+        from onnxsharp_b200.runtime import ConvWeights
+
+        self.batch = batch
+        x, w, b = conv_inputs(4321 + rank, batch)
+        self.x_h, self.w_h, self.b_h = x, w, b
+        dev = torch.device("cuda", torch.cuda.current_device())
+        self.ctx = ctx
+        self.x = torch.from_numpy(x).to(dev)
+        self.b = torch.from_numpy(b).to(dev)
+        self.w = ConvWeights(ctx, torch.from_numpy(w).to(dev), w.shape)
+        self.y = torch.empty((batch, 128, 160, 160), dtype=torch.float32, device=dev)
+        self.x_pin = torch.from_numpy(x).pin_memory()
+        self.y_pin = torch.empty(self.y.shape, dtype=torch.float32).pin_memory()
+        self.x2 = torch.empty_like(self.x)
+        self.y2 = torch.empty_like(self.y)
+        self.config = {"workload": self.name, "batch": batch, "in": [batch, 64, 160, 160], "weight": [128, 64, 3, 3],
+                       "stride": 1, "pad": 1, "act": "SiLU",
+                       "precision": "3xTF32 implicit GEMM (tcgen05 kind::tf32), FP32 in/out"}
+
+    def units_per_step(self) -> float:
+        return CONV_FLOPS_PER_IMAGE * self.batch
+
+    def _run(self, x, y):
+        from onnxsharp_b200 import ACT_SILU
+        from onnxsharp_b200.runtime import conv2d
+
+        conv2d(self.ctx, x, self.w, self.b, (1, 1), (1, 1, 1, 1), (1, 1), 1, ACT_SILU, out=y)
+
+    def step(self):
+        self._run(self.x, self.y)
+
+    def e2e_step(self):
+        self.ctx.memcpy_htod(self.x2, self.x_pin, self.x_pin.numel() * 4)
+        self._run(self.x2, self.y2)
+        self.ctx.memcpy_dtoh(self.y_pin, self.y2, self.y_pin.numel() * 4)
+
+    def e2e_bytes(self):
+        return self.x_pin.numel() * 4, self.y_pin.numel() * 4
+
+    def cpu_sample(self, threads: int) -> dict:
+        return CpuConv(self.x_h[:1], self.w_h, self.b_h).cpu_sample(threads)
+
+
+WORKLOADS = {"gemm": GemmWorkload, "conv": ConvWorkload}
+DEFAULT_WORKLOAD = "conv"
+DEFAULT_STEPS = {"gemm": 2000, "conv": 1000}
+
+
+# ----------------------------------------------------------------- timing
+def flush_l2(buf):
+    buf.add_(1.0)
+
+
+def run_ours(args, peaks, peaks_kind) -> dict | None:
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+
+    from onnxsharp_b200.runtime import Context
+
+    ctx = Context(local)
+    ctx.use_torch_stream()
+    wl = WORKLOADS[args.workload](ctx, rank)
+    stream = torch.cuda.current_stream()
+    flush = torch.empty(512 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    # warm-up
+    for _ in range(args.warmup):
+        wl.step()
+        flush_l2(flush)
+    ctx.synchronize()
+
+    K = args.steps
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    stops = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    ctx.profile_reset()
+    ctx.profile(True)
+    launches0 = ctx.launch_count()
+    barrier()
+    torch.cuda.synchronize()
+    for i in range(K):
+        starts[i].record(stream)
+        wl.step()
+        stops[i].record(stream)
+        flush_l2(flush)
+    torch.cuda.synchronize()
+    barrier()
+    launches = ctx.launch_count() - launches0
+    ctx.profile(False)
+    ctx.synchronize()
+    step_ms = sum(s.elapsed_time(e) for s, e in zip(starts, stops)) / K
+    kern_ms, kern_n = ctx.profile_read(wl.main_kernel)
+    all_ms, _ = ctx.profile_read("")
+    ctx.profile_reset()
+
+    # e2e through the public API with pinned host buffers
+    for _ in range(max(1, args.warmup)):
+        wl.e2e_step()
+    ctx.synchronize()
+    KE = max(1, min(K, args.e2e_steps))
+    e_starts = [torch.cuda.Event(enable_timing=True) for _ in range(KE)]
+    e_stops = [torch.cuda.Event(enable_timing=True) for _ in range(KE)]
+    barrier()
+    torch.cuda.synchronize()
+    for i in range(KE):
+        e_starts[i].record(stream)
+        wl.e2e_step()
+        e_stops[i].record(stream)
+        flush_l2(flush)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = sum(s.elapsed_time(e) for s, e in zip(e_starts, e_stops)) / KE
+    clocks = sampler.stop()
+
+    t = torch.tensor([step_ms, e2e_ms], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    step_ms_max, e2e_ms_max = t.tolist()
+
+    result = None
+    if rank == 0:
+        units = wl.units_per_step() * world
+        value = _scale(units / (step_ms_max * 1e-3)) if wl.unit == "TFLOP/s" else units / (step_ms_max * 1e-3)
+        e2e_value = _scale(units / (e2e_ms_max * 1e-3)) if wl.unit == "TFLOP/s" else units / (e2e_ms_max * 1e-3)
+        kern_avg_ms = kern_ms / max(1, kern_n)
+        if wl.bound == "tensor":
+            peak = peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]) / 2.0 / 3.0
+            achieved = _scale(wl.main_kernel_units() / (kern_avg_ms * 1e-3))
+            rl = {"bound": "tensor", "achieved": round(achieved, 2), "peak": round(peak, 2), "unit": "TFLOP/s",
+                  "frac": round(achieved / peak, 4), "traffic": args.traffic,
+                  "kernel": wl.main_kernel, "kernel_ms": round(kern_avg_ms, 5), "kernel_share": round(kern_ms / max(all_ms, 1e-12), 4),
+                  "peak_basis": f"3xTF32 = bf16_tflops/2 (kind::tf32 rate) /3 products, bf16_tflops of {peaks_kind} "
+                                f"{peaks.get('bf16_tflops')}; frac of {peaks_kind}"}
+        else:
+            peak = peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
+            achieved = wl.main_kernel_units() / (kern_avg_ms * 1e-3) / 1e9
+            rl = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                  "frac": round(achieved / peak, 4), "traffic": args.traffic, "kernel": wl.main_kernel,
+                  "kernel_ms": round(kern_avg_ms, 5), "peak_basis": f"hbm_gbs of {peaks_kind}"}
+        bi, bo = wl.e2e_bytes()
+        result = {
+            "metric": METRIC, "value": round(value, 3), "unit": wl.unit, "n_gpus": world, "steps": K,
+            "warmup": args.warmup, "ms_per_step": round(step_ms_max, 5), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded numpy), per rank",
+            "config": dict(wl.config, l2="flushed between steps (512 MiB write outside the events)",
+                           parallelism=f"dp{world} (independent shards, no data-path collective)"),
+            "e2e": {"value": round(e2e_value, 3), "unit": wl.unit, "h2d_bytes_per_step": bi, "d2h_bytes_per_step": bo,
+                    "ms_per_step": round(e2e_ms_max, 5)},
+            "roofline": rl,
+            "gpu_launches": int(launches),
+            "clocks": clocks,
+        }
+        if not args.no_cpu_baseline and world == 1:
+            cores = physical_cores()
+            base = wl.cpu_sample(cores)
+            base.update(kind="port", cpu=cpu_model())
+            try:
+                b4 = wl.cpu_sample(min(4, cores))
+                base["value_4_threads"] = b4["value"]
+            except Exception:  # pragma: no cover
+                pass
+            result["cpu_baseline"] = base
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    ctx.close()
+    return result
+
+
+def run_reference(args) -> dict | None:
+    """Time the reference's CPU algorithm (oracle port) on the host cores."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return None
+    cores = physical_cores()
+    os.environ.setdefault("ONNXSHARP_THREADS", str(cores))
+
+    class _Ctx:  # the CPU arm needs no GPU context
+        pass
+
+    wl = CPU_WORKLOADS[args.workload]()
+    vals = []
+    for _ in range(max(1, args.warmup)):
+        wl.cpu_sample(cores)
+    t0 = time.perf_counter()
+    for _ in range(args.ref_steps):
+        vals.append(wl.cpu_sample(cores))
+    dt = time.perf_counter() - t0
+    value = statistics.median(v["value"] for v in vals)
+    return {
+        "metric": METRIC, "impl": "reference", "value": round(value, 5), "unit": wl.unit, "n_gpus": world,
+        "steps": args.ref_steps, "warmup": args.warmup, "ms_per_step": round(dt / args.ref_steps * 1e3, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": wl.config,
+        "cpu_baseline": {"value": round(value, 5), "unit": wl.unit, "cores": cores, "kind": "port",
+                         "sample": vals[0]["sample"], "cpu": cpu_model()},
+        "e2e": {"value": round(value, 5), "unit": wl.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "reference is C# (OnnxSharp); no .NET runtime on this box, so the CPU restatement of its kernels "
+                "(oracle/) is timed with all physical cores",
+    }
+
+
+class CpuGemm:
+    unit = "TFLOP/s"
+
+    def __init__(self):
+        m, k, n = 2048, 512, 2048
+        rng = np.random.default_rng(1234)
+        self.a = rng.uniform(-1, 1, (m, k)).astype(np.float32)
+        self.b = rng.uniform(-1, 1, (k, n)).astype(np.float32)
+        self.bias = rng.uniform(-1, 1, n).astype(np.float32)
+        self.config = {"workload": GemmWorkload.name, "m": m, "k": k, "n": n, "bias": True}
+
+    def cpu_sample(self, threads):
+        import oracle
+
+        t0 = time.perf_counter()
+        oracle.gemm(self.a, self.b, col_bias=self.bias, threads=threads)
+        dt = time.perf_counter() - t0
+        return {"value": 2.0 * self.a.shape[0] * self.a.shape[1] * self.b.shape[1] / dt / 1e12,
+                "sample": "one full 2048x512x2048 GEMM+bias per step"}
+
+
+class CpuConv:
+    """One image of BASELINE config 2 per step through the oracle's im2col-order conv + SiLU."""
+
+    unit = "TFLOP/s"
+
+    def __init__(self, x=None, w=None, b=None):
+        if x is None:
+            x, w, b = conv_inputs(4321, 1)
+        self.x, self.w, self.b = x[:1], w, b
+        self.config = {"workload": ConvWorkload.name, "batch": 16, "in": [16, 64, 160, 160],
+                       "weight": [128, 64, 3, 3], "stride": 1, "pad": 1, "act": "SiLU"}
+
+    def cpu_sample(self, threads):
+        import oracle
+
+        t0 = time.perf_counter()
+        oracle.conv2d(self.x, self.w, self.b, pads=(1, 1, 1, 1), act=1, threads=threads)
+        dt = time.perf_counter() - t0
+        return {"value": CONV_FLOPS_PER_IMAGE / dt / 1e12, "unit": self.unit, "cores": threads,
+                "sample": f"1 of 16 images per step (3x3 conv 64->128 @160x160 + SiLU), {dt:.2f} s"}
+
+
+CPU_WORKLOADS = {"gemm": CpuGemm, "conv": CpuConv}
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=None)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", default=DEFAULT_WORKLOAD, choices=sorted(WORKLOADS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--e2e-steps", type=int, default=200)
+    ap.add_argument("--ref-steps", type=int, default=5)
+    ap.add_argument("--traffic", type=float, default=None,
+                    help="dram bytes per dominant-kernel launch from an ncu capture (reported as-is)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.traffic is None:
+        args.traffic = load_traffic(args.workload)
+    if args.steps is None:
+        args.steps = DEFAULT_STEPS.get(args.workload, 100)
+    args.warmup = max(3, args.warmup)
+    if args.impl == "reference":
+        res = run_reference(args)
+    else:
+        peaks, kind = load_peaks()
+        res = run_ours(args, peaks, kind)
+    if res is not None:
+        print(json.dumps(res), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -91,6 +91,18 @@ OSC_API int osc_synchronize(osc_ctx* ctx, int timeout_ms);
  * stream capture: a call that would need to grow it while capturing fails. */
 OSC_API int osc_reserve_scratch(osc_ctx* ctx, size_t bytes);
 
+/* Per-kernel timing (the CUDA counterpart of Net.ProfileAll,
+ * src/OnnxSharp/Core/Net.cs:282-332): while enabled, every kernel launch made
+ * through this context outside stream capture is bracketed by CUDA events on
+ * the context's stream. osc_profile_read sums the durations (ms) and counts
+ * the launches whose kernel name starts with `prefix` (NULL or "" = all);
+ * osc_profile_reset drops the records. osc_launch_count counts every kernel
+ * launch the context has made (profiling on or off). */
+OSC_API int osc_profile_enable(osc_ctx* ctx, int on);
+OSC_API int osc_profile_read(osc_ctx* ctx, const char* prefix, double* total_ms, int* launches);
+OSC_API int osc_profile_reset(osc_ctx* ctx);
+OSC_API unsigned long long osc_launch_count(osc_ctx* ctx);
+
 /* Device memory and copies, for callers without a framework allocator (the
  * reference's Tensor buffers are pinned host arrays, Tensors/Tensor.cs:65-155). */
 OSC_API int osc_malloc(osc_ctx* ctx, size_t bytes, void** out);
@@ -118,6 +130,29 @@ OSC_API int osc_gemm_weights_free(osc_gemm_weights* w);
 OSC_API int osc_gemm_bias_f32(osc_ctx* ctx, const float* a, int m, int k, int lda,
                               const osc_gemm_weights* w, const float* col_bias, int act, float* c,
                               int ldc);
+
+/* ------------------------------------------------------------ Conv (+FusedActivation)
+ * Replaces ConvLayer.Forward (src/OnnxSharp/Ops/DnnOps.cs:411-500) and its
+ * kernel chain (Kernels/ConvKernels.cs Im2Col/Pointwise, NchwcConv,
+ * Winograd, PackedConv, FirstConv) plus the in-place fused activation
+ * (DnnOps.cs:493-499), for group == 1.
+ *
+ * osc_conv_prepack_f32: pack constant W [M, C, kh, kw] once (host != 0: `w` is
+ * a host pointer). kh*kw <= 49. */
+typedef struct osc_conv_weights osc_conv_weights;
+OSC_API int osc_conv_prepack_f32(osc_ctx* ctx, const float* w, int M, int C, int kh, int kw, int host,
+                                 osc_conv_weights** out);
+OSC_API int osc_conv_weights_free(osc_conv_weights* w);
+
+/* y[N, M, OH, OW] = act(conv(x[N, C, H, W], W) + bias[M]) with ONNX Conv
+ * semantics (strides, pads top/left/bottom/right, dilations; group must be 1;
+ * equal strides). OH/OW must equal the ONNX output size (floor mode,
+ * DnnOps.cs:53-66). bias may be NULL. NCHW FP32 in and out; computed as an
+ * implicit GEMM with 3xTF32 on the tensor cores. */
+OSC_API int osc_conv2d_bias_act_f32(osc_ctx* ctx, const float* x, int N, int C, int H, int W,
+                                    const osc_conv_weights* w, int stride_h, int stride_w, int pad_t, int pad_l,
+                                    int pad_b, int pad_r, int dil_h, int dil_w, int group, const float* bias, int act,
+                                    float* y, int OH, int OW);
 
 #ifdef __cplusplus
 }

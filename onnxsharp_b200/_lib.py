@@ -62,6 +62,10 @@ SIGNATURES: dict[str, tuple] = {
     "osc_own_stream": (vp, [vp]),
     "osc_synchronize": (i32, [vp, i32]),
     "osc_reserve_scratch": (i32, [vp, sz]),
+    "osc_profile_enable": (i32, [vp, i32]),
+    "osc_profile_read": (i32, [vp, C.c_char_p, C.POINTER(C.c_double), C.POINTER(i32)]),
+    "osc_profile_reset": (i32, [vp]),
+    "osc_launch_count": (C.c_ulonglong, [vp]),
     "osc_malloc": (i32, [vp, sz, pp]),
     "osc_free": (i32, [vp, vp]),
     "osc_memcpy_htod": (i32, [vp, vp, vp, sz]),
@@ -71,6 +75,10 @@ SIGNATURES: dict[str, tuple] = {
     "osc_gemm_prepack_f32_host": (i32, [vp, vp, i32, i32, i32, pp]),
     "osc_gemm_weights_free": (i32, [vp]),
     "osc_gemm_bias_f32": (i32, [vp, vp, i32, i32, i32, vp, vp, i32, vp, i32]),
+    # Conv + FusedActivation
+    "osc_conv_prepack_f32": (i32, [vp, vp, i32, i32, i32, i32, i32, pp]),
+    "osc_conv_weights_free": (i32, [vp]),
+    "osc_conv2d_bias_act_f32": (i32, [vp, vp, i32, i32, i32, i32, vp] + [i32] * 9 + [vp, i32, vp, i32, i32]),
 }
 
 _lib: C.CDLL | None = None

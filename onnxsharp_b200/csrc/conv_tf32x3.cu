@@ -1,0 +1,376 @@
+// conv_tf32x3.cu — Conv(+bias, +fused activation) as an implicit GEMM on the
+// sm_100a tensor cores (3xTF32), replacing the reference's CPU conv chain
+// (ConvLayer.Forward, src/OnnxSharp/Ops/DnnOps.cs:411-500: depthwise /
+// first-layer / NCHWc / Winograd / packed / im2col kernels, then an in-place
+// SiLU pass, :493-499) for group == 1 convolutions.
+//
+// Mapping: D[oc][px] = W[oc][K] * X[px][K]^T with K ordered (ky, kx, c).
+//  - A operand (M = 128 output channels): weights prepacked once into the
+//    3xTF32 hi/lo split, [Mp][taps*Cp] K-major (osc_conv_prepack_f32).
+//  - B operand (N = 256 output pixels, a BW x BH box of one image): the input
+//    is transformed once per call from NCHW into "phase images" in NHWC with
+//    the hi/lo split and channels padded to Cp = roundup(C, 32):
+//    P[phase][n][h'][w'][c] = X[n][c][h'*s + py][w'*s + px], phase = py*s+px.
+//    Tap (ky, kx) of a stride-s conv then reads a stride-1 box from one phase
+//    image at offset (floor((ky*d-pt)/s), floor((kx*d-pl)/s)); pixels outside
+//    the image are zeros written by the transform or TMA's out-of-bounds
+//    fill (negative box coordinates are legal for loads; the channel
+//    coordinate, innermost, is always a multiple of 32).
+//  - Epilogue: bias[oc] + activation (VectorMath SiLU restated) and
+//    coalesced NCHW stores through a shared-memory staging tile.
+// The reference's im2col path accumulates acc = b[oc], then FMA over
+// (ic, ky, kx) (Kernels/ConvKernels.cs:262-462); the tensor cores sum in a
+// different order, so parity is |d| / max(1, |ref|) <= 1e-4.
+#include <algorithm>
+#include <cstdlib>
+
+#include "runtime.h"
+#include "sm100.cuh"
+#include "tf32x3_core.cuh"
+#include "vmath.cuh"
+
+struct osc_conv_weights {
+  int device = 0;
+  int M = 0, C = 0, kh = 0, kw = 0;
+  int Cp = 0, Kp = 0;    // channels padded to 32; Kp = kh*kw*Cp
+  float* hi = nullptr;   // [M][Kp]
+  float* lo = nullptr;
+};
+
+namespace osc {
+namespace {
+
+using ConvCfg = Tf32x3Cfg<256, 2, 2>;
+constexpr int kMaxTaps = 49;
+
+struct ConvTaps {
+  int n_taps;
+  int cp_blocks;                  // Cp / 32
+  short phase[kMaxTaps];          // phase image index (py * s + px)
+  short dy[kMaxTaps], dx[kMaxTaps];  // offsets inside the phase image
+};
+
+struct ConvGeom {
+  int N, M, OH, OW;   // output
+  int BW, BH;         // pixel box (BW * BH == 256)
+  int tiles_w, tiles_h;
+  int act;
+};
+
+__global__ void __launch_bounds__(ConvCfg::THREADS, 1)
+    k_conv_tf32x3(const __grid_constant__ CUtensorMap mWh, const __grid_constant__ CUtensorMap mWl,
+                  const __grid_constant__ CUtensorMap mXh, const __grid_constant__ CUtensorMap mXl,
+                  const __grid_constant__ ConvTaps taps, const __grid_constant__ ConvGeom g,
+                  const float* __restrict__ bias, float* __restrict__ y, int* __restrict__ err) {
+  using Cfg = ConvCfg;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* tiles = tiles_base<Cfg>(smem_raw);
+  PipeBarriers* pb = barriers<Cfg>(tiles);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  int t = blockIdx.x;
+  const int tx = t % g.tiles_w;
+  t /= g.tiles_w;
+  const int ty = t % g.tiles_h;
+  const int n = t / g.tiles_h;
+  const int ox0 = tx * g.BW, oy0 = ty * g.BH;
+  const int m0 = blockIdx.y * kBM;
+  const int num_kb = taps.n_taps * taps.cp_blocks;
+
+  if (threadIdx.x == 0) {
+    tma_prefetch(&mWh);
+    tma_prefetch(&mWl);
+    tma_prefetch(&mXh);
+    tma_prefetch(&mXl);
+  }
+  const uint32_t tmem = pipe_setup<Cfg>(pb);
+
+  if (warp == 0) {
+    if (lane == 0)
+      producer_loop<Cfg>(tiles, pb, num_kb, err, [&](int kb, uint8_t* st, uint64_t* bar) {
+        const int tap = kb / taps.cp_blocks;
+        const int c0 = (kb - tap * taps.cp_blocks) * 32;
+        const int kcol = kb * 32;  // == tap * Cp + c0
+        tma_load_2d(st, &mWh, bar, kcol, m0);
+        tma_load_2d(st + Cfg::A_BYTES, &mWl, bar, kcol, m0);
+        const int x = ox0 + taps.dx[tap], yy = oy0 + taps.dy[tap];
+        const int nn = taps.phase[tap] * g.N + n;
+        tma_load_4d(st + 2 * Cfg::A_BYTES, &mXh, bar, c0, x, yy, nn);
+        tma_load_4d(st + 2 * Cfg::A_BYTES + Cfg::B_BYTES, &mXl, bar, c0, x, yy, nn);
+      });
+  } else if (warp == 1) {
+    if (lane == 0) mma_loop<Cfg>(tiles, pb, tmem, num_kb, err);
+  } else {
+    float acc[128];
+    const bool ok = drain_loop<Cfg>(pb, tmem, num_kb, acc, err);
+    if (ok) stage_tile<Cfg>(tiles, acc);
+    epi_sync<Cfg>();
+    if (ok) {
+      constexpr int kPitch = Cfg::BN + 4;
+      const float* stage = reinterpret_cast<const float*>(tiles);
+      const int e = warp - 2;
+      for (int r = e; r < kBM; r += Cfg::EPI_WARPS) {
+        const int oc = m0 + r;
+        if (oc >= g.M) break;
+        const float b = bias ? __ldg(bias + oc) : 0.0f;
+        float* yplane = y + (static_cast<size_t>(n) * g.M + oc) * g.OH * g.OW;
+#pragma unroll
+        for (int h = 0; h < Cfg::BN; h += 128) {
+          const int p = h + lane * 4;  // 4 consecutive pixels of one box row (BW >= 8)
+          const int oy = oy0 + p / g.BW, ox = ox0 + p % g.BW;
+          if (oy >= g.OH) continue;
+          const float4 s = *reinterpret_cast<const float4*>(stage + r * kPitch + p);
+          float v[4] = {s.x, s.y, s.z, s.w};
+          float* dst = yplane + static_cast<size_t>(oy) * g.OW + ox;
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            if (ox + q < g.OW) dst[q] = apply_act(__fadd_rn(v[q], b), g.act);
+        }
+      }
+    }
+  }
+  pipe_teardown<Cfg>(pb, tmem);
+}
+
+// NCHW x -> phase-split NHWC hi/lo: out[(phase*N + n)][h'][w'][c], Cp channels.
+// One block per (n, phase-row h' of phase py, 32-wide w' strip, 32-channel
+// strip): reads 32 channels x 32 pixels of one input row, writes them
+// channel-innermost.
+__global__ void k_nchw_to_phase_nhwc(const float* __restrict__ x, int N, int C, int H, int W, int s, int Hp,
+                                     int Wp, int Cp, int z_base, float* __restrict__ hi, float* __restrict__ lo) {
+  __shared__ float tile[32][33];
+  const int wq = blockIdx.x * 32;        // w' strip start
+  const int c0 = blockIdx.y * 32;        // channel strip
+  int z = z_base + blockIdx.z;           // ((py*s + px) * N + n) * Hp + h'
+  const int hq = z % Hp;
+  z /= Hp;
+  const int n = z % N;
+  const int phase = z / N;
+  const int py = phase / s, px = phase % s;
+  const int ih = hq * s + py;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8
+  for (int yy = ty; yy < 32; yy += 8) {
+    const int c = c0 + yy;
+    const int iw = (wq + tx) * s + px;
+    float v = 0.0f;
+    if (c < C && ih < H && iw < W && (wq + tx) < Wp) v = x[((static_cast<size_t>(n) * C + c) * H + ih) * W + iw];
+    tile[yy][tx] = v;
+  }
+  __syncthreads();
+  for (int yy = ty; yy < 32; yy += 8) {
+    const int wqq = wq + yy;
+    const int c = c0 + tx;
+    if (wqq < Wp && c < Cp) {
+      const float v = tile[tx][yy];
+      const float h = to_tf32(v);
+      const size_t o = (((static_cast<size_t>(phase) * N + n) * Hp + hq) * Wp + wqq) * Cp + c;
+      hi[o] = h;
+      lo[o] = __fsub_rn(v, h);
+    }
+  }
+}
+
+// W[M][C][kh][kw] -> hi/lo [M][(ky*kw + kx)*Cp + c], zero for c >= C.
+__global__ void k_pack_conv_w(const float* __restrict__ w, int M, int C, int kh, int kw, int Cp, float* __restrict__ hi,
+                              float* __restrict__ lo) {
+  const size_t total = static_cast<size_t>(M) * kh * kw * Cp;
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const int c = static_cast<int>(i % Cp);
+    const size_t r = i / Cp;
+    const int tap = static_cast<int>(r % (kh * kw));
+    const int m = static_cast<int>(r / (kh * kw));
+    const int ky = tap / kw, kx = tap % kw;
+    const float v = c < C ? w[((static_cast<size_t>(m) * C + c) * kh + ky) * kw + kx] : 0.0f;
+    const float h = to_tf32(v);
+    hi[i] = h;
+    lo[i] = __fsub_rn(v, h);
+  }
+}
+
+int floor_div(int a, int b) { return a >= 0 ? a / b : -((-a + b - 1) / b); }
+
+}  // namespace
+
+// Chooses the pixel box (BW x BH = 256) that wastes the least MMA work.
+static void choose_box(int OH, int OW, int* BW, int* BH) {
+  const int cands[5] = {32, 16, 64, 8, 128};
+  long best = -1;
+  for (int bw : cands) {
+    const int bh = 256 / bw;
+    const long cost = static_cast<long>((OW + bw - 1) / bw) * bw * (static_cast<long>((OH + bh - 1) / bh) * bh);
+    if (best < 0 || cost < best) {
+      best = cost;
+      *BW = bw;
+      *BH = bh;
+    }
+  }
+}
+
+int conv_tf32x3(osc_ctx* ctx, const float* x, int N, int C, int H, int W, const osc_conv_weights* w, int sh, int sw,
+                int pt, int pl, int dh, int dw, const float* bias, int act, float* y, int OH, int OW) {
+  if (sh != sw) return fail(OSC_EUNSUPPORTED, "conv: unequal strides %d x %d", sh, sw);
+  const int s = sh;
+  const int Hp = (H + s - 1) / s, Wp = (W + s - 1) / s;
+  const int Cp = w->Cp;
+  // 1. input transform into the scratch arena
+  const size_t plane = static_cast<size_t>(s) * s * N * Hp * Wp * Cp;
+  const size_t half = round_up(plane * sizeof(float), 256);
+  void* buf = nullptr;
+  OSC_TRY(scratch(ctx, 2 * half, &buf));
+  float* xh = static_cast<float*>(buf);
+  float* xl = reinterpret_cast<float*>(static_cast<uint8_t*>(buf) + half);
+  {
+    const long zt = static_cast<long>(s) * s * N * Hp;
+    const long zmax = 65535;  // gridDim.z limit: split into several launches
+    for (long z0 = 0; z0 < zt; z0 += zmax) {
+      dim3 grid((Wp + 31) / 32, Cp / 32, static_cast<unsigned>(std::min(zmax, zt - z0)));
+      prof_begin(ctx);
+      k_nchw_to_phase_nhwc<<<grid, 256, 0, ctx->stream>>>(x, N, C, H, W, s, Hp, Wp, Cp, static_cast<int>(z0), xh, xl);
+      OSC_TRY(check_launch(ctx, "k_nchw_to_phase_nhwc"));
+    }
+  }
+  // 2. tap table
+  ConvTaps taps{};
+  taps.n_taps = w->kh * w->kw;
+  taps.cp_blocks = Cp / 32;
+  for (int ky = 0; ky < w->kh; ++ky)
+    for (int kx = 0; kx < w->kw; ++kx) {
+      const int t = ky * w->kw + kx;
+      const int oy = ky * dh - pt, ox = kx * dw - pl;
+      const int py = ((oy % s) + s) % s, px = ((ox % s) + s) % s;
+      taps.phase[t] = static_cast<short>(py * s + px);
+      taps.dy[t] = static_cast<short>(floor_div(oy - py, s));
+      taps.dx[t] = static_cast<short>(floor_div(ox - px, s));
+    }
+  ConvGeom g{};
+  g.N = N;
+  g.M = w->M;
+  g.OH = OH;
+  g.OW = OW;
+  g.act = act;
+  choose_box(OH, OW, &g.BW, &g.BH);
+  g.tiles_w = (OW + g.BW - 1) / g.BW;
+  g.tiles_h = (OH + g.BH - 1) / g.BH;
+  // 3. tensor maps
+  CUtensorMap mWh, mWl, mXh, mXl;
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(w->Kp), static_cast<uint64_t>(w->M)};
+    const uint64_t pitch[1] = {static_cast<uint64_t>(w->Kp) * 4};
+    const uint32_t box[2] = {kBK, kBM};
+    OSC_TRY(encode_tiled(&mWh, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, w->hi, dims, pitch, box, CU_TENSOR_MAP_SWIZZLE_128B));
+    OSC_TRY(encode_tiled(&mWl, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, w->lo, dims, pitch, box, CU_TENSOR_MAP_SWIZZLE_128B));
+  }
+  {
+    const uint64_t dims[4] = {static_cast<uint64_t>(Cp), static_cast<uint64_t>(Wp), static_cast<uint64_t>(Hp),
+                              static_cast<uint64_t>(s) * s * N};
+    const uint64_t pitch[3] = {static_cast<uint64_t>(Cp) * 4, static_cast<uint64_t>(Cp) * 4 * Wp,
+                               static_cast<uint64_t>(Cp) * 4 * Wp * Hp};
+    const uint32_t box[4] = {32, static_cast<uint32_t>(g.BW), static_cast<uint32_t>(g.BH), 1};
+    OSC_TRY(encode_tiled(&mXh, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, xh, dims, pitch, box, CU_TENSOR_MAP_SWIZZLE_128B));
+    OSC_TRY(encode_tiled(&mXl, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, xl, dims, pitch, box, CU_TENSOR_MAP_SWIZZLE_128B));
+  }
+  OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(k_conv_tf32x3), ConvCfg::SMEM_BYTES));
+  const long tiles = static_cast<long>(g.tiles_w) * g.tiles_h * N;
+  if (tiles > 2147483647L) return fail(OSC_EINVAL, "conv: too many tiles");
+  dim3 grid(static_cast<unsigned>(tiles), (w->M + kBM - 1) / kBM);
+  prof_begin(ctx);
+  k_conv_tf32x3<<<grid, ConvCfg::THREADS, ConvCfg::SMEM_BYTES, ctx->stream>>>(mWh, mWl, mXh, mXl, taps, g, bias, y,
+                                                                             ctx->d_err);
+  return check_launch(ctx, "k_conv_tf32x3");
+}
+
+}  // namespace osc
+
+using namespace osc;
+
+extern "C" {
+
+OSC_API int osc_conv_prepack_f32(osc_ctx* ctx, const float* w, int M, int C, int kh, int kw, int host,
+                                 osc_conv_weights** out) {
+  if (out == nullptr) return fail(OSC_EINVAL, "osc_conv_prepack_f32: out is null");
+  *out = nullptr;
+  OSC_TRY(enter(ctx));
+  if (w == nullptr || M <= 0 || C <= 0 || kh <= 0 || kw <= 0 || kh * kw > kMaxTaps)
+    return fail(OSC_EINVAL, "osc_conv_prepack_f32: bad weight shape [%d,%d,%d,%d]", M, C, kh, kw);
+  if (fault_injected("prepack")) return fail(OSC_EFAULT_INJECTED, "injected failure (prepack)");
+  auto* cw = new osc_conv_weights();
+  cw->device = ctx->device;
+  cw->M = M;
+  cw->C = C;
+  cw->kh = kh;
+  cw->kw = kw;
+  cw->Cp = static_cast<int>(round_up(static_cast<size_t>(C), 32));
+  cw->Kp = kh * kw * cw->Cp;
+  const size_t n = static_cast<size_t>(M) * cw->Kp;
+  const size_t src_bytes = static_cast<size_t>(M) * C * kh * kw * sizeof(float);
+  float* staged = nullptr;
+  cudaError_t e = cudaMalloc(&cw->hi, n * sizeof(float));
+  if (e == cudaSuccess) e = cudaMalloc(&cw->lo, n * sizeof(float));
+  if (e == cudaSuccess && host) {
+    e = cudaMalloc(&staged, src_bytes);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(staged, w, src_bytes, cudaMemcpyHostToDevice, ctx->stream);
+    w = staged;
+  }
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    cudaFree(cw->hi);
+    cudaFree(cw->lo);
+    cudaFree(staged);
+    delete cw;
+    return fail(OSC_ENOMEM, "osc_conv_prepack_f32: %s", cudaGetErrorString(e));
+  }
+  const int blocks = static_cast<int>(std::min<size_t>((n + 255) / 256, static_cast<size_t>(ctx->num_sms) * 8));
+  prof_begin(ctx);
+  k_pack_conv_w<<<blocks, 256, 0, ctx->stream>>>(w, M, C, kh, kw, cw->Cp, cw->hi, cw->lo);
+  int st = check_launch(ctx, "k_pack_conv_w");
+  if (staged) {
+    cudaStreamSynchronize(ctx->stream);
+    cudaFree(staged);
+  }
+  if (st != OSC_OK) {
+    cudaFree(cw->hi);
+    cudaFree(cw->lo);
+    delete cw;
+    return st;
+  }
+  *out = cw;
+  return OSC_OK;
+}
+
+OSC_API int osc_conv_weights_free(osc_conv_weights* w) {
+  if (w == nullptr) return OSC_OK;
+  cudaSetDevice(w->device);
+  cudaDeviceSynchronize();
+  cudaFree(w->hi);
+  cudaFree(w->lo);
+  delete w;
+  return OSC_OK;
+}
+
+OSC_API int osc_conv2d_bias_act_f32(osc_ctx* ctx, const float* x, int N, int C, int H, int W,
+                                    const osc_conv_weights* w, int stride_h, int stride_w, int pad_t, int pad_l,
+                                    int pad_b, int pad_r, int dil_h, int dil_w, int group, const float* bias, int act,
+                                    float* y, int OH, int OW) {
+  OSC_TRY(enter(ctx));
+  if (w == nullptr) return fail(OSC_EINVAL, "osc_conv2d_bias_act_f32: null weights");
+  if (w->device != ctx->device) return fail(OSC_EINVAL, "osc_conv2d_bias_act_f32: weights live on another device");
+  if (group != 1) return fail(OSC_EUNSUPPORTED, "osc_conv2d_bias_act_f32: group=%d (use osc_conv2d_depthwise_f32)", group);
+  if (C != w->C) return fail(OSC_EINVAL, "osc_conv2d_bias_act_f32: input has %d channels, weights %d", C, w->C);
+  if (N < 0 || H <= 0 || W <= 0 || stride_h <= 0 || stride_w <= 0 || dil_h <= 0 || dil_w <= 0 || pad_t < 0 ||
+      pad_l < 0 || pad_b < 0 || pad_r < 0)
+    return fail(OSC_EINVAL, "osc_conv2d_bias_act_f32: bad geometry");
+  if (act < OSC_ACT_NONE || act > OSC_ACT_SIGMOID) return fail(OSC_EINVAL, "osc_conv2d_bias_act_f32: act=%d", act);
+  // Output size as Ops/DnnOps.cs:53-66 (floor mode).
+  const int eh = (w->kh - 1) * dil_h + 1, ew = (w->kw - 1) * dil_w + 1;
+  const int oh = (H + pad_t + pad_b - eh) / stride_h + 1;
+  const int ow = (W + pad_l + pad_r - ew) / stride_w + 1;
+  if (oh != OH || ow != OW || oh <= 0 || ow <= 0)
+    return fail(OSC_EINVAL, "osc_conv2d_bias_act_f32: output must be %dx%d, got %dx%d", oh, ow, OH, OW);
+  if (N == 0) return OSC_OK;
+  if (x == nullptr || y == nullptr) return fail(OSC_EINVAL, "osc_conv2d_bias_act_f32: null pointer");
+  if (fault_injected("launch")) return fail(OSC_EFAULT_INJECTED, "injected failure (launch)");
+  return conv_tf32x3(ctx, x, N, C, H, W, w, stride_h, stride_w, pad_t, pad_l, dil_h, dil_w, bias, act, y, OH, OW);
+}
+
+}  // extern "C"

@@ -71,28 +71,37 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
     if (lane == 0) mma_loop<Cfg>(tiles, pb, tmem, num_kb, err);
   } else {
     float acc[128];
-    if (drain_loop<Cfg>(pb, tmem, num_kb, acc, err)) {
-      const int row = m0 + (warp & 3) * 32 + lane;
-      const int col0 = n0 + ((warp - 2) >> 2) * 128;
-      if (row < M && col0 < N) {
-        float* crow = C + static_cast<size_t>(row) * ldc + col0;
-        const int ncols = min(128, N - col0);
-        const bool vec = ncols == 128 && ((ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(C) & 15u) == 0);
+    const bool ok = drain_loop<Cfg>(pb, tmem, num_kb, acc, err);
+    if (ok) stage_tile<Cfg>(tiles, acc);
+    epi_sync<Cfg>();
+    if (ok) {
+      // Coalesced write-out: warp e copies rows e, e+EPI_WARPS, ...; lane l
+      // handles columns 4l.. of each 128-column half (bias + activation here).
+      constexpr int kPitch = Cfg::BN + 4;
+      const float* stage = reinterpret_cast<const float*>(tiles);
+      const int e = warp - 2;
+      const bool vec = ((ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(C) & 15u) == 0);
+      for (int r = e; r < kBM; r += Cfg::EPI_WARPS) {
+        const int row = m0 + r;
+        if (row >= M) break;
+        float* crow = C + static_cast<size_t>(row) * ldc;
 #pragma unroll
-        for (int j = 0; j < 128; j += 4) {
-          float v[4];
+        for (int h = 0; h < Cfg::BN; h += 128) {
+          const int c = n0 + h + lane * 4;
+          if (c >= N) continue;
+          const float4 s = *reinterpret_cast<const float4*>(stage + r * kPitch + h + lane * 4);
+          float v[4] = {s.x, s.y, s.z, s.w};
 #pragma unroll
           for (int t = 0; t < 4; ++t) {
-            float x = acc[j + t];
-            if (col_bias != nullptr && j + t < ncols) x = __fadd_rn(x, __ldg(col_bias + col0 + j + t));
-            v[t] = apply_act(x, act);
+            if (col_bias != nullptr && c + t < N) v[t] = __fadd_rn(v[t], __ldg(col_bias + c + t));
+            v[t] = apply_act(v[t], act);
           }
-          if (vec) {
-            *reinterpret_cast<float4*>(crow + j) = make_float4(v[0], v[1], v[2], v[3]);
+          if (vec && c + 4 <= N) {
+            *reinterpret_cast<float4*>(crow + c) = make_float4(v[0], v[1], v[2], v[3]);
           } else {
 #pragma unroll
             for (int t = 0; t < 4; ++t)
-              if (j + t < ncols) crow[j + t] = v[t];
+              if (c + t < N) crow[c + t] = v[t];
           }
         }
       }
@@ -169,6 +178,7 @@ int launch_gemm(osc_ctx* ctx, const float* ahi, const float* alo, int M, int Kp,
   auto kern = k_gemm_tf32x3<Cfg>;
   OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(kern), Cfg::SMEM_BYTES));
   dim3 grid((w->n + Cfg::BN - 1) / Cfg::BN, (M + kBM - 1) / kBM);
+  prof_begin(ctx);
   kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, ctx->stream>>>(mAh, mAl, mBh, mBl, M, w->n, Kp, bias, act, C, ldc,
                                                               ctx->d_err);
   return check_launch(ctx, "k_gemm_tf32x3");
@@ -186,6 +196,7 @@ int grid_for(osc_ctx* ctx, size_t work, int per_thread) {
 // Shared with the other kernels that consume split activations.
 int split_tf32(osc_ctx* ctx, const float* src, int rows, int k, int ld, int kp, float* hi, float* lo) {
   const size_t work = static_cast<size_t>(rows) * (kp / 4);
+  prof_begin(ctx);
   k_split_rows<<<grid_for(ctx, work, 1), 256, 0, ctx->stream>>>(src, rows, k, ld, kp, hi, lo);
   return check_launch(ctx, "k_split_rows");
 }
@@ -251,6 +262,7 @@ static int gemm_prepack(osc_ctx* ctx, const float* b, int k, int n, int b_layout
   int st;
   if (b_layout == 0) {
     dim3 grid((n + 31) / 32, (w->kp + 31) / 32);
+    prof_begin(ctx);
     k_pack_b_kn<<<grid, 256, 0, ctx->stream>>>(b, k, n, w->kp, w->hi, w->lo);
     st = check_launch(ctx, "k_pack_b_kn");
   } else {
@@ -292,7 +304,9 @@ OSC_API int osc_gemm_weights_free(osc_gemm_weights* w) {
 OSC_API int osc_gemm_bias_f32(osc_ctx* ctx, const float* a, int m, int k, int lda, const osc_gemm_weights* w,
                               const float* col_bias, int act, float* c, int ldc) {
   OSC_TRY(enter(ctx));
-  if (w == nullptr || a == nullptr || c == nullptr) return fail(OSC_EINVAL, "osc_gemm_bias_f32: null pointer");
+  if (w == nullptr) return fail(OSC_EINVAL, "osc_gemm_bias_f32: null weights");
+  if (m == 0 && k == w->k) return OSC_OK;  // empty batch: nothing to read or write
+  if (a == nullptr || c == nullptr) return fail(OSC_EINVAL, "osc_gemm_bias_f32: null pointer");
   if (w->device != ctx->device) return fail(OSC_EINVAL, "osc_gemm_bias_f32: weights live on another device");
   if (k != w->k) return fail(OSC_EINVAL, "osc_gemm_bias_f32: A has k=%d, packed B has k=%d", k, w->k);
   if (m < 0) return fail(OSC_EINVAL, "osc_gemm_bias_f32: m=%d", m);

@@ -124,9 +124,33 @@ int encode_tiled(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const vo
   return OSC_OK;
 }
 
+static cudaEvent_t pool_event(osc_ctx* ctx) {
+  if (!ctx->prof_pool.empty()) {
+    cudaEvent_t ev = ctx->prof_pool.back();
+    ctx->prof_pool.pop_back();
+    return ev;
+  }
+  cudaEvent_t ev = nullptr;
+  if (cudaEventCreate(&ev) != cudaSuccess) return nullptr;
+  return ev;
+}
+
+void prof_begin(osc_ctx* ctx) {
+  if (!ctx->prof_on || capturing(ctx)) return;
+  cudaEvent_t ev = pool_event(ctx);
+  if (ev != nullptr && cudaEventRecord(ev, ctx->stream) == cudaSuccess) ctx->prof_pending = ev;
+}
+
 int check_launch(osc_ctx* ctx, const char* what) {
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, what);
+  ctx->launches += 1;
+  if (ctx->prof_pending != nullptr) {
+    cudaEvent_t stop = pool_event(ctx);
+    if (stop != nullptr && cudaEventRecord(stop, ctx->stream) == cudaSuccess)
+      ctx->prof_recs.push_back({what, ctx->prof_pending, stop});
+    ctx->prof_pending = nullptr;
+  }
   static const bool sync_check = [] {
     const char* v = std::getenv("OSC_SYNC_CHECK");
     return v != nullptr && v[0] == '1';
@@ -193,10 +217,51 @@ OSC_API int osc_create(int device, osc_ctx** out) {
   return OSC_OK;
 }
 
+OSC_API int osc_profile_enable(osc_ctx* ctx, int on) {
+  if (ctx == nullptr) return fail(OSC_EINVAL, "null context");
+  ctx->prof_on = on != 0;
+  return OSC_OK;
+}
+
+OSC_API int osc_profile_read(osc_ctx* ctx, const char* prefix, double* total_ms, int* launches) {
+  OSC_TRY(enter(ctx));
+  double ms = 0.0;
+  int count = 0;
+  const size_t plen = prefix ? std::strlen(prefix) : 0;
+  for (const auto& r : ctx->prof_recs) {
+    if (plen && r.name.compare(0, plen, prefix) != 0) continue;
+    OSC_CUDA(cudaEventSynchronize(r.stop), "cudaEventSynchronize (profile)");
+    float t = 0.0f;
+    OSC_CUDA(cudaEventElapsedTime(&t, r.start, r.stop), "cudaEventElapsedTime (profile)");
+    ms += t;
+    count += 1;
+  }
+  if (total_ms) *total_ms = ms;
+  if (launches) *launches = count;
+  return OSC_OK;
+}
+
+OSC_API int osc_profile_reset(osc_ctx* ctx) {
+  OSC_TRY(enter(ctx));
+  for (auto& r : ctx->prof_recs) {
+    ctx->prof_pool.push_back(r.start);
+    ctx->prof_pool.push_back(r.stop);
+  }
+  ctx->prof_recs.clear();
+  return OSC_OK;
+}
+
+OSC_API unsigned long long osc_launch_count(osc_ctx* ctx) { return ctx ? ctx->launches : 0ull; }
+
 OSC_API int osc_destroy(osc_ctx* ctx) {
   if (ctx == nullptr) return OSC_OK;
   cudaSetDevice(ctx->device);
   cudaStreamSynchronize(ctx->stream);
+  for (auto& r : ctx->prof_recs) {
+    cudaEventDestroy(r.start);
+    cudaEventDestroy(r.stop);
+  }
+  for (auto ev : ctx->prof_pool) cudaEventDestroy(ev);
   if (ctx->scratch) cudaFree(ctx->scratch);
   if (ctx->d_err) cudaFree(ctx->d_err);
   if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);

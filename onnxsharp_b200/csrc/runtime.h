@@ -10,8 +10,14 @@
 #include <cstddef>
 #include <cstdint>
 #include <string>
+#include <vector>
 
-#include "../../include/onnxsharp_cuda.h"
+#include "onnxsharp_cuda.h"
+
+struct osc_prof_rec {
+  std::string name;
+  cudaEvent_t start, stop;
+};
 
 struct osc_ctx {
   int device = 0;
@@ -21,6 +27,12 @@ struct osc_ctx {
   int* d_err = nullptr;           // device error word, written by kernels on failure
   void* scratch = nullptr;        // grow-only per-call temporaries
   size_t scratch_bytes = 0;
+  // Launch accounting and per-kernel event timing (osc_profile_*).
+  unsigned long long launches = 0;
+  bool prof_on = false;
+  cudaEvent_t prof_pending = nullptr;  // start event of the launch being made
+  std::vector<osc_prof_rec> prof_recs;
+  std::vector<cudaEvent_t> prof_pool;
 };
 
 namespace osc {
@@ -51,8 +63,13 @@ int encode_tiled(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const vo
                  const uint64_t* dims, const uint64_t* strides_bytes /* rank-1 */, const uint32_t* box,
                  CUtensorMapSwizzle swizzle);
 
-// Checks a kernel launch and (when OSC_SYNC_CHECK=1) synchronises to surface
-// faults at the call that caused them.
+// Call right before every kernel launch: when profiling is on (and the
+// stream is not being captured) it records the launch's start event.
+void prof_begin(osc_ctx* ctx);
+
+// Checks a kernel launch, counts it, records its stop event when profiling,
+// and (when OSC_SYNC_CHECK=1) synchronises to surface faults at the call that
+// caused them. `what` is the kernel name used by osc_profile_read.
 int check_launch(osc_ctx* ctx, const char* what);
 
 // Raises a kernel's dynamic shared memory limit once per (device, kernel).

@@ -208,4 +208,30 @@ __device__ __forceinline__ bool drain_loop(PipeBarriers* pb, uint32_t tmem, int 
   return true;
 }
 
+// Output staging: after the last chunk every MMA has completed, so the
+// operand ring is free and holds the 128 x BN tile at a pitch of BN+4 floats
+// (the +4 keeps a quarter-warp's float4 stores to 8 different rows on 8
+// different bank groups). Each epilogue thread writes its row's 128 columns;
+// after epi_sync() the warps copy whole rows out with coalesced stores.
+template <class Cfg>
+__device__ __forceinline__ float* stage_tile(uint8_t* tiles, const float (&acc)[128]) {
+  constexpr int kPitch = Cfg::BN + 4;
+  float* stage = reinterpret_cast<float*>(tiles);
+  const int warp = threadIdx.x >> 5;
+  const int row = (warp & 3) * 32 + (threadIdx.x & 31);
+  float* dst = stage + row * kPitch + ((warp - 2) >> 2) * 128;
+#pragma unroll
+  for (int j = 0; j < 128; j += 4)
+    *reinterpret_cast<float4*>(dst + j) = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+  return stage;
+}
+
+// Barrier among the epilogue warps only (named barrier 1).
+template <class Cfg>
+__device__ __forceinline__ void epi_sync() {
+  asm volatile("bar.sync 1, %0;" ::"r"(Cfg::EPI_WARPS * 32) : "memory");
+}
+
+static_assert(kBM * (256 + 4) * 4 <= Tf32x3Cfg<256, 2, 2>::TILE_BYTES, "staging fits the operand ring");
+
 }  // namespace osc

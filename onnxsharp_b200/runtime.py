@@ -42,6 +42,29 @@ class Context:
     def reserve_scratch(self, nbytes: int) -> None:
         call("osc_reserve_scratch", self.handle, int(nbytes))
 
+    # -- per-kernel event timing (osc_profile_*) and launch accounting
+    def profile(self, on: bool = True) -> None:
+        call("osc_profile_enable", self.handle, 1 if on else 0)
+
+    def profile_read(self, prefix: str = "") -> tuple[float, int]:
+        """(total milliseconds, launches) of recorded kernels whose name starts with prefix."""
+        ms = C.c_double()
+        n = C.c_int()
+        call("osc_profile_read", self.handle, prefix.encode(), C.byref(ms), C.byref(n))
+        return ms.value, n.value
+
+    def profile_reset(self) -> None:
+        call("osc_profile_reset", self.handle)
+
+    def launch_count(self) -> int:
+        return int(_lib.load().osc_launch_count(self.handle))
+
+    def memcpy_htod(self, dst, src, nbytes: int) -> None:
+        call("osc_memcpy_htod", self.handle, ptr(dst), ptr(src), int(nbytes))
+
+    def memcpy_dtoh(self, dst, src, nbytes: int) -> None:
+        call("osc_memcpy_dtoh", self.handle, ptr(dst), ptr(src), int(nbytes))
+
     def close(self) -> None:
         self._finalizer()
 
@@ -56,6 +79,39 @@ class GemmWeights:
         self.handle = h
         self.k, self.n = int(k), int(n)
         self._finalizer = weakref.finalize(self, _lib.load().osc_gemm_weights_free, h)
+
+
+class ConvWeights:
+    """Constant W [M, C, kh, kw] of a Conv, prepacked once (tap-major K, 3xTF32 split)."""
+
+    def __init__(self, ctx: Context, w, shape):
+        M, Cc, kh, kw = (int(v) for v in shape)
+        h = C.c_void_p()
+        call("osc_conv_prepack_f32", ctx.handle, ptr(w), M, Cc, kh, kw, 0 if _is_device(w) else 1, C.byref(h))
+        self.handle = h
+        self.shape = (M, Cc, kh, kw)
+        self._finalizer = weakref.finalize(self, _lib.load().osc_conv_weights_free, h)
+
+
+def conv_out(size: int, k: int, s: int, p0: int, p1: int, d: int) -> int:
+    """ONNX Conv output size, floor mode (Ops/DnnOps.cs:53-66)."""
+    return (size + p0 + p1 - ((k - 1) * d + 1)) // s + 1
+
+
+def conv2d(ctx: Context, x, w: ConvWeights, bias=None, stride=(1, 1), pads=(0, 0, 0, 0), dil=(1, 1), group: int = 1,
+           act: int = _lib.ACT_NONE, out=None):
+    """y = act(conv(x, W) + bias); x NCHW FP32 on the device; pads = (top, left, bottom, right)."""
+    import torch
+
+    N, Cc, H, W = x.shape
+    M, _, kh, kw = w.shape
+    OH = conv_out(H, kh, stride[0], pads[0], pads[2], dil[0])
+    OW = conv_out(W, kw, stride[1], pads[1], pads[3], dil[1])
+    if out is None:
+        out = torch.empty((N, M, OH, OW), dtype=torch.float32, device=x.device)
+    call("osc_conv2d_bias_act_f32", ctx.handle, ptr(x), N, Cc, H, W, w.handle, stride[0], stride[1], pads[0], pads[1],
+         pads[2], pads[3], dil[0], dil[1], group, ptr(bias), int(act), ptr(out), OH, OW)
+    return out
 
 
 def _is_device(x) -> bool:

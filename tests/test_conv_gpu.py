@@ -1,0 +1,101 @@
+"""Conv(+bias, +fused SiLU) on the B200 tensor cores (implicit GEMM, 3xTF32)
+against the CPU oracle's restatement of the reference im2col conv
+(Kernels/ConvKernels.cs:262-462), tolerance |d| / max(1, |ref|) <= 1e-4."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import oracle
+from conftest import rel_err
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-4
+
+
+def _conv(ctx, x, w, b=None, stride=(1, 1), pads=(0, 0, 0, 0), dil=(1, 1), act=0):
+    import torch
+
+    from onnxsharp_b200.runtime import ConvWeights, conv2d
+
+    cw = ConvWeights(ctx, torch.from_numpy(w).cuda(), w.shape)
+    y = conv2d(ctx, torch.from_numpy(x).cuda(), cw, None if b is None else torch.from_numpy(b).cuda(), stride, pads,
+               dil, 1, act)
+    ctx.synchronize()
+    return y.cpu().numpy()
+
+
+def _case(seed, N, C, H, W, M, k, std=None):
+    rng = np.random.default_rng(seed)
+    x = rng.uniform(0, 1, (N, C, H, W)).astype(np.float32)
+    fan = C * k * k
+    w = (rng.normal(0, 1, (M, C, k, k)) * (std or np.sqrt(2.0 / fan))).astype(np.float32)
+    b = rng.normal(0, 0.01, M).astype(np.float32)
+    return x, w, b
+
+
+def test_conv_golden_fixture(ctx, golden):
+    g = golden
+    y = _conv(ctx, g["conv_x"], g["conv_w"], g["conv_b"], pads=(1, 1, 1, 1), act=1)
+    assert rel_err(y, g["conv_y"]) <= TOL
+
+
+def test_conv_config2_batch1_full_spatial(ctx):
+    """BASELINE config 2 at B=1: [1,64,160,160] -> [1,128,160,160], 3x3 s1 p1, SiLU."""
+    x, w, b = _case(2, 1, 64, 160, 160, 128, 3)
+    y = _conv(ctx, x, w, b, pads=(1, 1, 1, 1), act=1)
+    assert rel_err(y, oracle.conv2d(x, w, b, pads=(1, 1, 1, 1), act=1)) <= TOL
+
+
+def test_conv_config2_batch16_checked_images(ctx):
+    """BASELINE config 2 at B=16; images 0, 7 and 15 are checked against the oracle."""
+    x, w, b = _case(3, 16, 64, 160, 160, 128, 3)
+    y = _conv(ctx, x, w, b, pads=(1, 1, 1, 1), act=1)
+    for i in (0, 7, 15):
+        ref = oracle.conv2d(x[i:i + 1], w, b, pads=(1, 1, 1, 1), act=1)
+        assert rel_err(y[i:i + 1], ref) <= TOL, f"image {i}"
+
+
+@pytest.mark.parametrize(
+    "N,C,H,W,M,k,stride,pads,dil,act",
+    [
+        (2, 3, 33, 35, 16, 3, 2, (1, 1, 1, 1), 1, 1),      # stem-like: C=3, stride 2
+        (1, 16, 40, 40, 32, 3, 2, (1, 1, 1, 1), 1, 1),     # stride 2
+        (2, 48, 20, 20, 200, 1, 1, (0, 0, 0, 0), 1, 0),    # 1x1, M > 128 and not a multiple
+        (1, 32, 21, 19, 64, 3, 1, (1, 0, 2, 1), 1, 2),     # asymmetric pads, ReLU
+        (1, 32, 24, 24, 32, 3, 1, (2, 2, 2, 2), 2, 3),     # dilation 2, Sigmoid
+        (3, 64, 9, 7, 96, 5, 1, (2, 2, 2, 2), 1, 1),       # 5x5, tiny spatial
+        (1, 256, 20, 20, 256, 3, 1, (1, 1, 1, 1), 1, 1),   # K = 2304
+        (1, 8, 17, 17, 8, 7, 3, (3, 3, 3, 3), 1, 0),       # stride 3, 7x7
+    ],
+)
+def test_conv_geometries(ctx, N, C, H, W, M, k, stride, pads, dil, act):
+    x, w, b = _case(N * 1000 + C + k, N, C, H, W, M, k)
+    y = _conv(ctx, x, w, b, (stride, stride), pads, (dil, dil), act)
+    ref = oracle.conv2d(x, w, b, (stride, stride), pads, (dil, dil), 1, act)
+    assert y.shape == ref.shape
+    assert rel_err(y, ref) <= TOL
+
+
+def test_conv_without_bias(ctx):
+    x, w, _ = _case(9, 1, 32, 12, 12, 32, 3)
+    y = _conv(ctx, x, w, None, pads=(1, 1, 1, 1))
+    assert rel_err(y, oracle.conv2d(x, w, None, pads=(1, 1, 1, 1))) <= TOL
+
+
+def test_conv_rejects_bad_output_size_and_groups(ctx):
+    import torch
+
+    from onnxsharp_b200 import OscError
+    from onnxsharp_b200 import _lib
+    from onnxsharp_b200.runtime import ConvWeights
+
+    x = torch.zeros(1, 8, 10, 10, device="cuda")
+    cw = ConvWeights(ctx, torch.zeros(8, 8, 3, 3, device="cuda"), (8, 8, 3, 3))
+    y = torch.zeros(1, 8, 10, 10, device="cuda")
+    with pytest.raises(OscError):  # pad 0 gives 8x8, not 10x10
+        _lib.call("osc_conv2d_bias_act_f32", ctx.handle, x.data_ptr(), 1, 8, 10, 10, cw.handle, 1, 1, 0, 0, 0, 0, 1,
+                  1, 1, None, 0, y.data_ptr(), 10, 10)
+    with pytest.raises(OscError):  # grouped conv is a different entry point
+        _lib.call("osc_conv2d_bias_act_f32", ctx.handle, x.data_ptr(), 1, 8, 10, 10, cw.handle, 1, 1, 1, 1, 1, 1, 1,
+                  1, 2, None, 0, y.data_ptr(), 10, 10)
