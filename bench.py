@@ -293,9 +293,76 @@ class ConvWorkload(Workload):
         return CpuConv(self.x_h[:1], self.w_h, self.b_h).cpu_sample(threads)
 
 
-WORKLOADS = {"gemm": GemmWorkload, "conv": ConvWorkload}
+def dqmm_inputs(seed: int, m=4096, k=512, n=2048):
+    """A N(0,1), W int8 U[-127,127], w_scale U(0.001,0.02), bias N(0, 0.01)."""
+    rng = np.random.default_rng(seed)
+    a = rng.normal(0, 1, (m, k)).astype(np.float32)
+    w = rng.integers(-127, 128, (k, n)).astype(np.int8)
+    ws = rng.uniform(0.001, 0.02, n).astype(np.float32)
+    b = rng.normal(0, 0.01, n).astype(np.float32)
+    return a, w, ws, b
+
+
+class DqmmWorkload(Workload):
+    """DynamicQuantizeMatMul A[4096,512] f32 x W int8 [512,2048] -> Y[4096,2048] f32."""
+
+    name = "dqmm_u8s8_4096x512x2048"
+    unit = "TOP/s"
+    main_kernel = "k_dqmm_i8"
+    bound = "hbm"
+
+    def __init__(self, ctx, rank: int, m=4096, k=512, n=2048):
+        import torch
+
+        from onnxsharp_b200.runtime import DqmmWeights
+
+        self.m, self.k, self.n = m, k, n
+        a, w, ws, b = dqmm_inputs(777 + rank, m, k, n)
+        self.a_h, self.w_h, self.ws_h, self.b_h = a, w, ws, b
+        dev = torch.device("cuda", torch.cuda.current_device())
+        self.ctx = ctx
+        self.a = torch.from_numpy(a).to(dev)
+        self.ws = torch.from_numpy(ws).to(dev)
+        self.b = torch.from_numpy(b).to(dev)
+        self.w = DqmmWeights(ctx, torch.from_numpy(w).to(dev), k, n, None)
+        self.y = torch.empty((m, n), dtype=torch.float32, device=dev)
+        self.a_pin = torch.from_numpy(a).pin_memory()
+        self.y_pin = torch.empty((m, n), dtype=torch.float32).pin_memory()
+        self.a2 = torch.empty_like(self.a)
+        self.y2 = torch.empty_like(self.y)
+        self.config = {"workload": self.name, "m": m, "k": k, "n": n,
+                       "precision": "dynamic per-tensor u8 activations x s8 weights -> s32 (tcgen05 kind::i8), "
+                                    "FP32 epilogue bit-identical to the reference"}
+
+    def units_per_step(self) -> float:
+        return 2.0 * self.m * self.k * self.n
+
+    def main_kernel_units(self) -> float:
+        kp = (self.k + 127) // 128 * 128
+        return self.m * kp + self.n * kp + self.m * self.n * 4 + self.n * 16
+
+    def step(self):
+        from onnxsharp_b200.runtime import dqmm
+
+        dqmm(self.ctx, self.a, self.w, self.ws, self.b, out=self.y)
+
+    def e2e_step(self):
+        from onnxsharp_b200.runtime import dqmm
+
+        self.ctx.memcpy_htod(self.a2, self.a_pin, self.a_pin.numel() * 4)
+        dqmm(self.ctx, self.a2, self.w, self.ws, self.b, out=self.y2)
+        self.ctx.memcpy_dtoh(self.y_pin, self.y2, self.y_pin.numel() * 4)
+
+    def e2e_bytes(self):
+        return self.m * self.k * 4, self.m * self.n * 4
+
+    def cpu_sample(self, threads: int) -> dict:
+        return CpuDqmm(self.a_h, self.w_h, self.ws_h, self.b_h).cpu_sample(threads)
+
+
+WORKLOADS = {"gemm": GemmWorkload, "conv": ConvWorkload, "dqmm": DqmmWorkload}
 DEFAULT_WORKLOAD = "conv"
-DEFAULT_STEPS = {"gemm": 2000, "conv": 1000}
+DEFAULT_STEPS = {"gemm": 2000, "conv": 1000, "dqmm": 2000}
 
 
 # ----------------------------------------------------------------- timing
@@ -387,8 +454,8 @@ def run_ours(args, peaks, peaks_kind) -> dict | None:
     result = None
     if rank == 0:
         units = wl.units_per_step() * world
-        value = _scale(units / (step_ms_max * 1e-3)) if wl.unit == "TFLOP/s" else units / (step_ms_max * 1e-3)
-        e2e_value = _scale(units / (e2e_ms_max * 1e-3)) if wl.unit == "TFLOP/s" else units / (e2e_ms_max * 1e-3)
+        value = _scale(units / (step_ms_max * 1e-3)) if wl.unit in ("TFLOP/s", "TOP/s") else units / (step_ms_max * 1e-3)
+        e2e_value = _scale(units / (e2e_ms_max * 1e-3)) if wl.unit in ("TFLOP/s", "TOP/s") else units / (e2e_ms_max * 1e-3)
         kern_avg_ms = kern_ms / max(1, kern_n)
         if wl.bound == "tensor":
             peak = peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]) / 2.0 / 3.0
@@ -511,7 +578,29 @@ class CpuConv:
                 "sample": f"1 of 16 images per step (3x3 conv 64->128 @160x160 + SiLU), {dt:.2f} s"}
 
 
-CPU_WORKLOADS = {"gemm": CpuGemm, "conv": CpuConv}
+class CpuDqmm:
+    """The full config-3 DynamicQuantizeMatMul per step through the oracle (F32-substitute GEMM, as the reference)."""
+
+    unit = "TOP/s"
+
+    def __init__(self, a=None, w=None, ws=None, b=None):
+        if a is None:
+            a, w, ws, b = dqmm_inputs(777)
+        self.a, self.w, self.ws, self.b = a, w, ws, b
+        self.config = {"workload": DqmmWorkload.name, "m": a.shape[0], "k": a.shape[1], "n": w.shape[1]}
+
+    def cpu_sample(self, threads):
+        import oracle
+
+        t0 = time.perf_counter()
+        oracle.dqmm(self.a, self.w, 0, self.ws, self.b, threads=threads)
+        dt = time.perf_counter() - t0
+        ops = 2.0 * self.a.shape[0] * self.a.shape[1] * self.w.shape[1]
+        return {"value": ops / dt / 1e12, "unit": self.unit, "cores": threads,
+                "sample": f"full {self.a.shape[0]}x{self.a.shape[1]}x{self.w.shape[1]} DQMM per step, {dt:.2f} s"}
+
+
+CPU_WORKLOADS = {"gemm": CpuGemm, "conv": CpuConv, "dqmm": CpuDqmm}
 
 
 def main() -> int:

@@ -154,6 +154,39 @@ OSC_API int osc_conv2d_bias_act_f32(osc_ctx* ctx, const float* x, int N, int C, 
                                     int pad_b, int pad_r, int dil_h, int dil_w, int group, const float* bias, int act,
                                     float* y, int OH, int OW);
 
+/* ------------------------------------------------------------ DynamicQuantizeMatMul (int8)
+ * Replaces DynamicQuantizeMatMulLayer (src/OnnxSharp/Ops/QuantizedMatMulOps.cs:28-376)
+ * with Quantizer.MinMax (Tensors/Quantization.cs:109-181): per-tensor dynamic
+ * uint8 quantisation of A, int8/uint8 weights with per-column zero points,
+ * exact int32 accumulation on the tensor cores (tcgen05 kind::i8), then
+ * y = acc * (a_scale * w_scale[j]) + bias[j] with the reference's rounding
+ * (one FMA on full 16-column panels of 12/6/4-row groups, mul then add on
+ * tail columns / leftover rows), so y is bit-identical to the reference's
+ * single-threaded (row-block = all rows) result.
+ *
+ * osc_dqmm_prepack: W [k, n] row-major bytes (is_signed: int8, else uint8),
+ * n_zp zero points (0: none, 1: per tensor, n: per column; host array).
+ * host != 0: `w` is a host pointer. */
+typedef struct osc_dqmm_weights osc_dqmm_weights;
+OSC_API int osc_dqmm_prepack(osc_ctx* ctx, const void* w, int k, int n, int is_signed, const int32_t* w_zp,
+                             int n_zp, int host, osc_dqmm_weights** out);
+OSC_API int osc_dqmm_weights_free(osc_dqmm_weights* w);
+
+/* y[m, n] = DynamicQuantizeMatMul(A[m, k]); all pointers are device pointers.
+ * w_scale has n_scale entries (1 or n); bias may be NULL.
+ * minmax_override (NULL or 2 floats {min, max}) replaces the range of A: a
+ * row-sharded multi-GPU caller all-reduces the shards' ranges (see
+ * osc_minmax_f32) so every shard quantises exactly as the whole tensor would.
+ * Optional outputs (NULL to skip): q_out [m, k] uint8 quantised A, acc_out
+ * [m, n] int32 accumulators sum (q - zp)(w - wzp), params_out {scale, zp}. */
+OSC_API int osc_dqmm_f32(osc_ctx* ctx, const float* a, int m, int k, int lda, const osc_dqmm_weights* w,
+                         const float* w_scale, int n_scale, const float* bias, float* y, const float* minmax_override,
+                         uint8_t* q_out, int32_t* acc_out, float* params_out);
+
+/* minmax_out[0..1] (device) = {min(x, 0), max(x, 0)} over `count` floats, NaN
+ * skipped (Quantizer.MinMax). */
+OSC_API int osc_minmax_f32(osc_ctx* ctx, const float* x, long count, float* minmax_out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -79,6 +79,11 @@ SIGNATURES: dict[str, tuple] = {
     "osc_conv_prepack_f32": (i32, [vp, vp, i32, i32, i32, i32, i32, pp]),
     "osc_conv_weights_free": (i32, [vp]),
     "osc_conv2d_bias_act_f32": (i32, [vp, vp, i32, i32, i32, i32, vp] + [i32] * 9 + [vp, i32, vp, i32, i32]),
+    # DynamicQuantizeMatMul
+    "osc_dqmm_prepack": (i32, [vp, vp, i32, i32, i32, vp, i32, i32, pp]),
+    "osc_dqmm_weights_free": (i32, [vp]),
+    "osc_dqmm_f32": (i32, [vp, vp, i32, i32, i32, vp, vp, i32, vp, vp, vp, vp, vp, vp]),
+    "osc_minmax_f32": (i32, [vp, vp, C.c_long, vp]),
 }
 
 _lib: C.CDLL | None = None

@@ -104,15 +104,20 @@ __global__ void __launch_bounds__(ConvCfg::THREADS, 1)
     float acc[128];
     const bool ok = drain_loop<Cfg>(pb, tmem, num_kb, acc, err);
     if (ok) stage_tile<Cfg>(tiles, acc);
+    constexpr int kPitch = Cfg::BN + 4;
+    float* sbias = reinterpret_cast<float*>(tiles) + kBM * kPitch;  // bias of this tile's 128 channels
+    {
+      const int jj = threadIdx.x - 64;
+      if (jj < kBM) sbias[jj] = (bias != nullptr && m0 + jj < g.M) ? __ldg(bias + m0 + jj) : 0.0f;
+    }
     epi_sync<Cfg>();
     if (ok) {
-      constexpr int kPitch = Cfg::BN + 4;
       const float* stage = reinterpret_cast<const float*>(tiles);
       const int e = warp - 2;
       for (int r = e; r < kBM; r += Cfg::EPI_WARPS) {
         const int oc = m0 + r;
         if (oc >= g.M) break;
-        const float b = bias ? __ldg(bias + oc) : 0.0f;
+        const float b = sbias[r];
         float* yplane = y + (static_cast<size_t>(n) * g.M + oc) * g.OH * g.OW;
 #pragma unroll
         for (int h = 0; h < Cfg::BN; h += 128) {
@@ -166,6 +171,53 @@ __global__ void k_nchw_to_phase_nhwc(const float* __restrict__ x, int N, int C, 
       const size_t o = (((static_cast<size_t>(phase) * N + n) * Hp + hq) * Wp + wqq) * Cp + c;
       hi[o] = h;
       lo[o] = __fsub_rn(v, h);
+    }
+  }
+}
+
+// Stride-1 fast path of the transform (a single phase image): each block
+// moves a 32-channel x 32-pixel tile of one input row with one float4 load
+// and one float4 store (hi and lo) per thread.
+__global__ void __launch_bounds__(256) k_nchw_to_nhwc_split(const float* __restrict__ x, int N, int C, int H, int W,
+                                                            int Cp, int z_base, float* __restrict__ hi,
+                                                            float* __restrict__ lo) {
+  __shared__ float tile[32][33];
+  const int w0 = blockIdx.x * 32;
+  const int c0 = blockIdx.y * 32;
+  const int z = z_base + blockIdx.z;  // n * H + h
+  const int h = z % H, n = z / H;
+  const int tid = threadIdx.x;
+  {
+    const int c = c0 + (tid >> 3), w = w0 + (tid & 7) * 4;
+    float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    if (c < C) {
+      const float* src = x + ((static_cast<size_t>(n) * C + c) * H + h) * W + w;
+      if (w + 4 <= W && (reinterpret_cast<uintptr_t>(src) & 15u) == 0) {
+        const float4 t = __ldg(reinterpret_cast<const float4*>(src));
+        v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+      } else {
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          if (w + q < W) v[q] = src[q];
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) tile[tid >> 3][(tid & 7) * 4 + q] = v[q];
+  }
+  __syncthreads();
+  {
+    const int w = w0 + (tid >> 3), cq = (tid & 7) * 4;
+    if (w < W && c0 + cq < Cp) {
+      float h4[4], l4[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float v = tile[cq + q][tid >> 3];
+        h4[q] = to_tf32(v);
+        l4[q] = __fsub_rn(v, h4[q]);
+      }
+      const size_t o = ((static_cast<size_t>(n) * H + h) * W + w) * Cp + c0 + cq;
+      *reinterpret_cast<float4*>(hi + o) = make_float4(h4[0], h4[1], h4[2], h4[3]);
+      *reinterpret_cast<float4*>(lo + o) = make_float4(l4[0], l4[1], l4[2], l4[3]);
     }
   }
 }
@@ -226,8 +278,14 @@ int conv_tf32x3(osc_ctx* ctx, const float* x, int N, int C, int H, int W, const 
     for (long z0 = 0; z0 < zt; z0 += zmax) {
       dim3 grid((Wp + 31) / 32, Cp / 32, static_cast<unsigned>(std::min(zmax, zt - z0)));
       prof_begin(ctx);
-      k_nchw_to_phase_nhwc<<<grid, 256, 0, ctx->stream>>>(x, N, C, H, W, s, Hp, Wp, Cp, static_cast<int>(z0), xh, xl);
-      OSC_TRY(check_launch(ctx, "k_nchw_to_phase_nhwc"));
+      if (s == 1) {
+        k_nchw_to_nhwc_split<<<grid, 256, 0, ctx->stream>>>(x, N, C, H, W, Cp, static_cast<int>(z0), xh, xl);
+        OSC_TRY(check_launch(ctx, "k_nchw_to_nhwc_split"));
+      } else {
+        k_nchw_to_phase_nhwc<<<grid, 256, 0, ctx->stream>>>(x, N, C, H, W, s, Hp, Wp, Cp, static_cast<int>(z0), xh,
+                                                            xl);
+        OSC_TRY(check_launch(ctx, "k_nchw_to_phase_nhwc"));
+      }
     }
   }
   // 2. tap table

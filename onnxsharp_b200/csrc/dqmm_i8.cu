@@ -1,0 +1,626 @@
+// dqmm_i8.cu — DynamicQuantizeMatMul on the sm_100a integer tensor cores.
+//
+// Replaces DynamicQuantizeMatMulLayer.Forward (src/OnnxSharp/Ops/
+// QuantizedMatMulOps.cs:115-201), which fuses DynamicQuantizeLinear ->
+// MatMulInteger -> Cast -> Mul -> Add:
+//   1. (min, max) of A including 0, NaN skipped (Tensors/Quantization.cs:109-181)
+//   2. scale = (max-min)/255 (1 if !(scale > 0)); zp = clamp(rne(-min/scale), 0, 255)
+//      (QuantizedMatMulOps.cs:146-156)
+//   3. q = clamp(rne(x * (1/scale)) + zp, 0, 255)        (QuantizeAndWiden :280-335)
+//   4. acc = sum_t (q - zp)(w - wzp[j])  — exact integers (the reference
+//      accumulates them in F32, exact while |partial sums| < 2^24)
+//   5. y = acc * (scale * wscale[j]) + bias[j], as one FMA on the 16-column
+//      panels of 12/6/4-row groups and as mul-then-add on tail columns and
+//      leftover rows (GemmKernel.cs:1210-1241 vs ScaleColumns :1594-1608),
+//      reproduced here element by element so y is bit-identical.
+// Kernels: k_minmax_partial -> k_dql_params (1 thread) -> k_quantize_rows
+// (u8 q, per-row sum of q, NaN-row flag) -> k_dqmm_i8 (TMA -> smem ->
+// tcgen05.mma kind::i8, u8 x s8|u8 -> s32 in TMEM, then the corrections
+// acc = sum(q*w) - wzp[j]*rowsum[i] - zp*colsum[j] + k*zp*wzp[j] and the
+// epilogue above, coalesced stores through shared memory).
+#include <algorithm>
+#include <cmath>
+#include <vector>
+
+#include "runtime.h"
+#include "sm100.cuh"
+
+struct osc_dqmm_weights {
+  int device = 0;
+  int k = 0, n = 0, kp = 0;  // kp: K padded to a multiple of 128 (one SW128 row of int8)
+  int is_signed = 1;
+  int8_t* wt = nullptr;       // [n][kp] raw weight bytes, transposed
+  int32_t* colsum = nullptr;  // [n] sum_t w[t][j] (as signed/unsigned integers)
+  int32_t* zp = nullptr;      // [n] weight zero point per column
+};
+
+namespace osc {
+namespace {
+
+constexpr int kQBM = 128, kQBN = 256, kQBK = 128, kQStages = 4;
+constexpr int kQThreads = 64 + 8 * 32;  // producer, MMA, 8 epilogue warps
+constexpr int kQA = kQBM * kQBK;        // 16 KB
+constexpr int kQB = kQBN * kQBK;        // 32 KB
+constexpr int kQStage = kQA + kQB;
+constexpr int kQTiles = kQStages * kQStage;
+constexpr int kQSmem = kQTiles + 1024 + 256;
+static_assert(kQBM * (kQBN + 4) * 4 + 4 * kQBN * 4 + 2 * kQBM * 4 <= kQTiles, "staging + tile constants fit");
+
+// Device-side quantisation parameters, written by k_dql_params.
+struct QParams {
+  float scale, inverse;
+  int zp, pad;
+};
+
+__device__ __forceinline__ float maxps(float a, float b) { return a > b ? a : b; }
+__device__ __forceinline__ float minps(float a, float b) { return a < b ? a : b; }
+
+__global__ void k_minmax_partial(const float* __restrict__ a, long n, float2* __restrict__ part) {
+  float mn = 0.0f, mx = 0.0f;  // 0 is always inside the range
+  const long i4 = n / 4;
+  const bool vec = (reinterpret_cast<uintptr_t>(a) & 15u) == 0;
+  if (vec) {
+    for (long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < i4;
+         i += static_cast<long>(gridDim.x) * blockDim.x) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(a) + i);
+      const float e[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int t = 0; t < 4; ++t)
+        if (e[t] == e[t]) {
+          mn = fminf(mn, e[t]);
+          mx = fmaxf(mx, e[t]);
+        }
+    }
+  }
+  for (long i = (vec ? i4 * 4 : 0) + blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long>(gridDim.x) * blockDim.x) {
+    const float e = a[i];
+    if (e == e) {
+      mn = fminf(mn, e);
+      mx = fmaxf(mx, e);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  }
+  __shared__ float smn[32], smx[32];
+  const int w = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) == 0) {
+    smn[w] = mn;
+    smx[w] = mx;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int i = 1; i < (blockDim.x >> 5); ++i) {
+      mn = fminf(mn, smn[i]);
+      mx = fmaxf(mx, smx[i]);
+    }
+    part[blockIdx.x] = make_float2(mn, mx);
+  }
+}
+
+__global__ void k_minmax_final(const float2* __restrict__ part, int nparts, float* __restrict__ out) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  float mn = 0.0f, mx = 0.0f;
+  for (int i = 0; i < nparts; ++i) {
+    mn = fminf(mn, part[i].x);
+    mx = fmaxf(mx, part[i].y);
+  }
+  out[0] = mn;
+  out[1] = mx;
+}
+
+// Reduces the partials (or takes a caller-supplied global range) and derives
+// scale / zero point exactly as the reference does.
+__global__ void k_dql_params(const float2* __restrict__ part, int nparts, const float* __restrict__ override_mm,
+                             QParams* __restrict__ out, float* __restrict__ params_out) {
+  // One warp: strided partial reduction, then a shuffle tree (min/max are
+  // order-independent, so the result equals a serial scan).
+  float mn = 0.0f, mx = 0.0f;
+  if (override_mm != nullptr) {
+    mn = fminf(0.0f, override_mm[0]);
+    mx = fmaxf(0.0f, override_mm[1]);
+  } else {
+    for (int i = threadIdx.x; i < nparts; i += 32) {
+      const float2 p = part[i];
+      mn = fminf(mn, p.x);
+      mx = fmaxf(mx, p.y);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    }
+  }
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  float scale = __fdiv_rn(__fsub_rn(mx, mn), 255.0f);
+  if (!(scale > 0.0f)) scale = 1.0f;
+  const float z = rintf(__fdiv_rn(-mn, scale));
+  int zp = (z != z) ? 0 : (z >= 2147483520.0f ? 2147483647 : (z <= -2147483648.0f ? (-2147483647 - 1) : static_cast<int>(z)));
+  zp = zp < 0 ? 0 : (zp > 255 ? 255 : zp);
+  QParams p;
+  p.scale = scale;
+  p.inverse = __fdiv_rn(1.0f, scale);
+  p.zp = zp;
+  p.pad = 0;
+  *out = p;
+  if (params_out != nullptr) {
+    params_out[0] = scale;
+    params_out[1] = static_cast<float>(zp);
+  }
+}
+
+// One warp per row: q = clamp(rne(x*inv) + zp, 0, 255) as u8 into [m][kp]
+// (zero padding), rowsum[i] = sum q, nanrow[i] = 1 if any x*inv is NaN.
+__global__ void k_quantize_rows(const float* __restrict__ a, int m, int k, int lda, int kp,
+                                const QParams* __restrict__ qp, uint8_t* __restrict__ q, int32_t* __restrict__ rowsum,
+                                int32_t* __restrict__ nanrow) {
+  const int warps = (blockDim.x >> 5) * gridDim.x;
+  const int lane = threadIdx.x & 31;
+  const float inv = qp->inverse;
+  const float zpf = static_cast<float>(qp->zp);
+  for (int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < m; r += warps) {
+    const float* ar = a + static_cast<size_t>(r) * lda;
+    uint8_t* qr = q + static_cast<size_t>(r) * kp;
+    int sum = 0, nan = 0;
+    const bool vec = ((lda & 3) == 0) && ((reinterpret_cast<uintptr_t>(a) & 15u) == 0);
+    for (int c0 = lane * 4; c0 < kp; c0 += 128) {
+      uint32_t packed = 0;
+      float xv[4];
+      if (vec && c0 + 4 <= k) {
+        const float4 t4 = __ldg(reinterpret_cast<const float4*>(ar + c0));
+        xv[0] = t4.x; xv[1] = t4.y; xv[2] = t4.z; xv[3] = t4.w;
+      } else {
+#pragma unroll
+        for (int t = 0; t < 4; ++t) xv[t] = (c0 + t < k) ? ar[c0 + t] : 0.0f;
+      }
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const int c = c0 + t;
+        uint32_t v = 0;
+        if (c < k) {
+          const float s = __fmul_rn(xv[t], inv);
+          if (s != s) {
+            nan = 1;
+          } else {
+            const float f = minps(255.0f, maxps(0.0f, __fadd_rn(rintf(s), zpf)));
+            v = static_cast<uint32_t>(f);
+          }
+        }
+        sum += static_cast<int>(v);
+        packed |= v << (8 * t);
+      }
+      *reinterpret_cast<uint32_t*>(qr + c0) = packed;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      nan |= __shfl_xor_sync(0xffffffffu, nan, o);
+    }
+    if (lane == 0) {
+      rowsum[r] = sum;
+      nanrow[r] = nan;
+    }
+  }
+}
+
+// Rows [0, grouped) went through the reference's 12/6/4-row micro-kernels
+// (fused FMA epilogue); see GemmKernel.cs:746-790.
+__host__ __device__ inline int grouped_rows(int m) {
+  int row = 0;
+  while (row + 12 <= m) row += 12;
+  while (row + 6 <= m) row += 6;
+  while (row + 4 <= m) row += 4;
+  return row;
+}
+
+struct DqmmArgs {
+  int M, N, K, num_kb;
+  int fused_rows, full_cols;
+  const QParams* qp;
+  const int32_t* rowsum;
+  const int32_t* nanrow;
+  const int32_t* colsum;
+  const int32_t* wzp;
+  const float* wscale;
+  int n_scale;
+  const float* bias;
+  float* y;
+  int32_t* acc_out;
+};
+
+__global__ void __launch_bounds__(kQThreads, 1)
+    k_dqmm_i8(const __grid_constant__ CUtensorMap mQ, const __grid_constant__ CUtensorMap mW,
+              const __grid_constant__ DqmmArgs args, uint32_t idesc, int* __restrict__ err) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* tiles = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(tiles + kQTiles);
+  uint64_t* empty = full + kQStages;
+  uint64_t* done = empty + kQStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.y * kQBM, n0 = blockIdx.x * kQBN;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kQStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch(&mQ);
+    tma_prefetch(&mW);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kQBN);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int num_kb = args.num_kb;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int issued = 0;
+      for (int kb = 0; kb < num_kb; ++kb) {
+        const int s = kb % kQStages;
+        const uint32_t ph = (kb / kQStages) & 1u;
+        if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, err)) break;
+        uint8_t* st = tiles + s * kQStage;
+        mbar_arrive_expect_tx(&full[s], kQStage);
+        tma_load_2d(st, &mQ, &full[s], kb * kQBK, m0);
+        tma_load_2d(st + kQA, &mW, &full[s], kb * kQBK, n0);
+        issued = kb + 1;
+      }
+      if (*abort_flag) {
+        const int first = issued > kQStages ? issued - kQStages : 0;
+        for (int kb = first; kb < issued; ++kb) {
+          const uint64_t t0 = globaltimer_ns();
+          while (!mbar_try_wait(&full[kb % kQStages], (kb / kQStages) & 1u) &&
+                 globaltimer_ns() - t0 < 50ull * 1000ull * 1000ull) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      for (int kb = 0; kb < num_kb; ++kb) {
+        const int s = kb % kQStages;
+        const uint32_t ph = (kb / kQStages) & 1u;
+        if (!mbar_wait(&full[s], ph, abort_flag, err)) break;
+        tc_fence_after();
+        const uint32_t base = smem_addr(tiles + s * kQStage);
+        const uint64_t dA = sdesc_kmajor_sw128(base);
+        const uint64_t dB = sdesc_kmajor_sw128(base + kQA);
+#pragma unroll
+        for (int kk = 0; kk < kQBK / 32; ++kk) {
+          const uint64_t off = static_cast<uint64_t>(kk * 2);  // +32 bytes per 32-wide K step
+          mma_i8(tmem, dA + off, dB + off, idesc, (kb | kk) != 0 ? 1u : 0u);
+        }
+        mma_commit(&empty[s]);
+      }
+      mma_commit(done);
+    }
+  } else {
+    const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
+    bool ok = mbar_wait(done, 0, abort_flag, err);
+    ok = __all_sync(0xffffffffu, ok);
+    tc_fence_after();
+    constexpr int kPitch = kQBN + 4;
+    uint32_t* stage = reinterpret_cast<uint32_t*>(tiles);
+    if (ok) {
+      const int row = q * 32 + lane;
+      const uint32_t base = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(half * 128);
+#pragma unroll
+      for (int g = 0; g < 8; g += 2) {
+        uint32_t r0[16], r1[16];
+        tmem_ld16(base + g * 16, r0);
+        tmem_ld16(base + (g + 1) * 16, r1);
+        tmem_wait_ld();
+        uint32_t* dst = stage + row * kPitch + half * 128 + g * 16;
+#pragma unroll
+        for (int j = 0; j < 16; j += 4) {
+          *reinterpret_cast<uint4*>(dst + j) = make_uint4(r0[j], r0[j + 1], r0[j + 2], r0[j + 3]);
+          *reinterpret_cast<uint4*>(dst + 16 + j) = make_uint4(r1[j], r1[j + 1], r1[j + 2], r1[j + 3]);
+        }
+      }
+    }
+    // Per-column constants of this tile, one epilogue thread per column:
+    // comb = a_scale * w_scale[j], bias, corr = -zp*colsum[j] + K*zp*wzp[j], wzp.
+    float* c_comb = reinterpret_cast<float*>(stage + kQBM * kPitch);
+    float* c_bias = c_comb + kQBN;
+    int32_t* c_corr = reinterpret_cast<int32_t*>(c_bias + kQBN);
+    int32_t* c_wzp = c_corr + kQBN;
+    int32_t* r_sum = c_wzp + kQBN;  // per-row sum of q and NaN flag of this tile
+    int32_t* r_nan = r_sum + kQBM;
+    const QParams p = *args.qp;
+    {
+      const int jj = threadIdx.x - 64;  // 0..255
+      const int j = n0 + jj;
+      if (j < args.N) {
+        const int wz = __ldg(args.wzp + j);
+        c_comb[jj] = __fmul_rn(p.scale, __ldg(args.wscale + (args.n_scale > 1 ? j : 0)));
+        c_bias[jj] = args.bias ? __ldg(args.bias + j) : 0.0f;
+        c_corr[jj] = -p.zp * __ldg(args.colsum + j) + args.K * p.zp * wz;
+        c_wzp[jj] = wz;
+      }
+      if (jj < kQBM && m0 + jj < args.M) {
+        r_sum[jj] = __ldg(args.rowsum + m0 + jj);
+        r_nan[jj] = __ldg(args.nanrow + m0 + jj);
+      }
+    }
+    asm volatile("bar.sync 1, %0;" ::"r"(8 * 32) : "memory");
+    if (ok) {
+      const int e = warp - 2;
+      for (int r = e; r < kQBM; r += 8) {
+        const int i = m0 + r;
+        if (i >= args.M) break;
+        const int rs = r_sum[r];
+        const bool nanr = r_nan[r] != 0;
+        const bool fused_row = i < args.fused_rows;
+        float* yr = args.y + static_cast<size_t>(i) * args.N;
+        for (int h = 0; h < kQBN; h += 128) {
+          const int jl = h + lane * 4;
+          const int j0 = n0 + jl;
+          if (j0 >= args.N) continue;
+          const uint4 raw = *reinterpret_cast<const uint4*>(stage + r * kPitch + jl);
+          const int32_t s4[4] = {static_cast<int32_t>(raw.x), static_cast<int32_t>(raw.y),
+                                 static_cast<int32_t>(raw.z), static_cast<int32_t>(raw.w)};
+          float out[4];
+          int32_t accs[4];
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            const int j = j0 + t;
+            if (j >= args.N) {
+              out[t] = 0.0f;
+              accs[t] = 0;
+              continue;
+            }
+            const int32_t acc = s4[t] - c_wzp[jl + t] * rs + c_corr[jl + t];
+            accs[t] = acc;
+            const float comb = c_comb[jl + t];
+            const float b = c_bias[jl + t];
+            const float af = static_cast<float>(acc);
+            float v;
+            if (fused_row && j < args.full_cols) {
+              v = __fmaf_rn(af, comb, b);
+            } else {
+              v = __fmul_rn(af, comb);
+              if (args.bias) v = __fadd_rn(v, b);
+            }
+            out[t] = nanr ? __int_as_float(0x7fc00000) : v;
+          }
+          if (j0 + 4 <= args.N && (args.N & 3) == 0) {
+            *reinterpret_cast<float4*>(yr + j0) = make_float4(out[0], out[1], out[2], out[3]);
+            if (args.acc_out)
+              *reinterpret_cast<int4*>(args.acc_out + static_cast<size_t>(i) * args.N + j0) =
+                  make_int4(accs[0], accs[1], accs[2], accs[3]);
+          } else {
+            for (int t = 0; t < 4; ++t)
+              if (j0 + t < args.N) {
+                yr[j0 + t] = out[t];
+                if (args.acc_out) args.acc_out[static_cast<size_t>(i) * args.N + j0 + t] = accs[t];
+              }
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kQBN);
+  }
+}
+
+// W [k][n] (s8 or u8) -> Wt [n][kp] + column sums; one thread per output column strip.
+__global__ void k_pack_dqmm_w(const int8_t* __restrict__ w, int k, int n, int kp, int is_signed,
+                              int8_t* __restrict__ wt, int32_t* __restrict__ colsum) {
+  __shared__ int8_t tile[32][33];
+  const int n0 = blockIdx.x * 32, k0 = blockIdx.y * 32;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  for (int yy = ty; yy < 32; yy += 8) {
+    const int kk = k0 + yy, nn = n0 + tx;
+    tile[yy][tx] = (kk < k && nn < n) ? w[static_cast<size_t>(kk) * n + nn] : 0;
+  }
+  __syncthreads();
+  for (int yy = ty; yy < 32; yy += 8) {
+    const int nn = n0 + yy, kk = k0 + tx;
+    if (nn < n && kk < kp) {
+      const int8_t v = tile[tx][yy];
+      wt[static_cast<size_t>(nn) * kp + kk] = v;
+      int iv = is_signed ? static_cast<int>(v) : static_cast<int>(static_cast<uint8_t>(v));
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) iv += __shfl_xor_sync(0xffffffffu, iv, o);
+      if (tx == 0) atomicAdd(colsum + nn, iv);
+    }
+  }
+}
+
+}  // namespace
+
+static int minmax_params(osc_ctx* ctx, const float* a, long count, const float* override_mm, void* work,
+                         QParams* qp, float* params_out) {
+  float2* part = static_cast<float2*>(work);
+  int blocks = 0;
+  if (override_mm == nullptr) {
+    blocks = static_cast<int>(std::min<long>(std::max<long>((count / 4 + 255) / 256, 1), ctx->num_sms * 4L));
+    prof_begin(ctx);
+    k_minmax_partial<<<blocks, 256, 0, ctx->stream>>>(a, count, part);
+    OSC_TRY(check_launch(ctx, "k_minmax_partial"));
+  }
+  prof_begin(ctx);
+  k_dql_params<<<1, 32, 0, ctx->stream>>>(part, blocks, override_mm, qp, params_out);
+  return check_launch(ctx, "k_dql_params");
+}
+
+}  // namespace osc
+
+using namespace osc;
+
+extern "C" {
+
+OSC_API int osc_dqmm_prepack(osc_ctx* ctx, const void* w, int k, int n, int is_signed, const int32_t* w_zp,
+                             int n_zp, int host, osc_dqmm_weights** out) {
+  if (out == nullptr) return fail(OSC_EINVAL, "osc_dqmm_prepack: out is null");
+  *out = nullptr;
+  OSC_TRY(enter(ctx));
+  if (w == nullptr || k <= 0 || n <= 0) return fail(OSC_EINVAL, "osc_dqmm_prepack: bad W [%d, %d]", k, n);
+  if (n_zp != 0 && n_zp != 1 && n_zp != n) return fail(OSC_EINVAL, "osc_dqmm_prepack: %d zero points for %d columns", n_zp, n);
+  if (n_zp > 0 && w_zp == nullptr) return fail(OSC_EINVAL, "osc_dqmm_prepack: null zero points");
+  if (fault_injected("prepack")) return fail(OSC_EFAULT_INJECTED, "injected failure (prepack)");
+  auto* d = new osc_dqmm_weights();
+  d->device = ctx->device;
+  d->k = k;
+  d->n = n;
+  d->kp = static_cast<int>(round_up(static_cast<size_t>(k), kQBK));
+  d->is_signed = is_signed ? 1 : 0;
+  std::vector<int32_t> zp(static_cast<size_t>(n), 0);
+  for (int j = 0; j < n; ++j) zp[j] = n_zp == 0 ? 0 : (n_zp == 1 ? w_zp[0] : w_zp[j]);
+  const size_t wbytes = static_cast<size_t>(k) * n;
+  int8_t* staged = nullptr;
+  cudaError_t e = cudaMalloc(&d->wt, static_cast<size_t>(n) * d->kp);
+  if (e == cudaSuccess) e = cudaMalloc(&d->colsum, sizeof(int32_t) * n);
+  if (e == cudaSuccess) e = cudaMalloc(&d->zp, sizeof(int32_t) * n);
+  if (e == cudaSuccess) e = cudaMemsetAsync(d->colsum, 0, sizeof(int32_t) * n, ctx->stream);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(d->zp, zp.data(), sizeof(int32_t) * n, cudaMemcpyHostToDevice, ctx->stream);
+  if (e == cudaSuccess && host) {
+    e = cudaMalloc(&staged, wbytes);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(staged, w, wbytes, cudaMemcpyHostToDevice, ctx->stream);
+    w = staged;
+  }
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    cudaFree(d->wt);
+    cudaFree(d->colsum);
+    cudaFree(d->zp);
+    cudaFree(staged);
+    delete d;
+    return fail(OSC_ENOMEM, "osc_dqmm_prepack: %s", cudaGetErrorString(e));
+  }
+  dim3 grid((n + 31) / 32, (d->kp + 31) / 32);
+  prof_begin(ctx);
+  k_pack_dqmm_w<<<grid, 256, 0, ctx->stream>>>(static_cast<const int8_t*>(w), k, n, d->kp, d->is_signed, d->wt,
+                                               d->colsum);
+  int st = check_launch(ctx, "k_pack_dqmm_w");
+  cudaStreamSynchronize(ctx->stream);  // the host zero-point vector above must outlive its copy
+  if (staged) cudaFree(staged);
+  if (st != OSC_OK) {
+    osc_dqmm_weights_free(d);
+    return st;
+  }
+  *out = d;
+  return OSC_OK;
+}
+
+OSC_API int osc_dqmm_weights_free(osc_dqmm_weights* w) {
+  if (w == nullptr) return OSC_OK;
+  cudaSetDevice(w->device);
+  cudaDeviceSynchronize();
+  cudaFree(w->wt);
+  cudaFree(w->colsum);
+  cudaFree(w->zp);
+  delete w;
+  return OSC_OK;
+}
+
+OSC_API int osc_minmax_f32(osc_ctx* ctx, const float* x, long count, float* minmax_out) {
+  OSC_TRY(enter(ctx));
+  if (x == nullptr || minmax_out == nullptr || count < 0) return fail(OSC_EINVAL, "osc_minmax_f32: bad arguments");
+  void* buf = nullptr;
+  const int blocks = static_cast<int>(std::min<long>(std::max<long>((count / 4 + 255) / 256, 1), ctx->num_sms * 4L));
+  OSC_TRY(scratch(ctx, sizeof(float2) * blocks + 256, &buf));
+  prof_begin(ctx);
+  k_minmax_partial<<<blocks, 256, 0, ctx->stream>>>(x, count, static_cast<float2*>(buf));
+  OSC_TRY(check_launch(ctx, "k_minmax_partial"));
+  prof_begin(ctx);
+  k_minmax_final<<<1, 32, 0, ctx->stream>>>(static_cast<const float2*>(buf), blocks, minmax_out);
+  return check_launch(ctx, "k_minmax_final");
+}
+
+OSC_API int osc_dqmm_f32(osc_ctx* ctx, const float* a, int m, int k, int lda, const osc_dqmm_weights* w,
+                         const float* w_scale, int n_scale, const float* bias, float* y, const float* minmax_override,
+                         uint8_t* q_out, int32_t* acc_out, float* params_out) {
+  OSC_TRY(enter(ctx));
+  if (w == nullptr) return fail(OSC_EINVAL, "osc_dqmm_f32: null weights");
+  if (w->device != ctx->device) return fail(OSC_EINVAL, "osc_dqmm_f32: weights live on another device");
+  if (k != w->k) return fail(OSC_EINVAL, "osc_dqmm_f32: A has k=%d, W has k=%d", k, w->k);
+  if (n_scale != 1 && n_scale != w->n) return fail(OSC_EINVAL, "osc_dqmm_f32: %d scales for %d columns", n_scale, w->n);
+  if (m < 0 || w_scale == nullptr) return fail(OSC_EINVAL, "osc_dqmm_f32: bad arguments");
+  if (lda == 0) lda = k;
+  if (lda < k) return fail(OSC_EINVAL, "osc_dqmm_f32: lda=%d < k=%d", lda, k);
+  if (m == 0) return OSC_OK;
+  if (a == nullptr || y == nullptr) return fail(OSC_EINVAL, "osc_dqmm_f32: null pointer");
+  if (lda != k && minmax_override == nullptr)
+    return fail(OSC_EUNSUPPORTED, "osc_dqmm_f32: strided A needs minmax_override (the range is per tensor)");
+  if (fault_injected("launch")) return fail(OSC_EFAULT_INJECTED, "injected failure (launch)");
+  const int kp = w->kp;
+  // scratch: partials | params | q [m][kp] | rowsum [m] | nanrow [m]
+  const size_t off_params = 8192, off_q = 8192 + 256;
+  const size_t q_bytes = round_up(static_cast<size_t>(m) * kp, 256);
+  const size_t off_rs = off_q + q_bytes, off_nan = off_rs + round_up(sizeof(int32_t) * m, 256);
+  const size_t total = off_nan + round_up(sizeof(int32_t) * m, 256);
+  void* buf = nullptr;
+  OSC_TRY(scratch(ctx, total, &buf));
+  uint8_t* base = static_cast<uint8_t*>(buf);
+  QParams* qp = reinterpret_cast<QParams*>(base + off_params);
+  uint8_t* q = base + off_q;
+  int32_t* rowsum = reinterpret_cast<int32_t*>(base + off_rs);
+  int32_t* nanrow = reinterpret_cast<int32_t*>(base + off_nan);
+  OSC_TRY(minmax_params(ctx, a, static_cast<long>(m) * k, minmax_override, base, qp, params_out));
+  {
+    const int blocks = std::min((m + 7) / 8, ctx->num_sms * 8);
+    prof_begin(ctx);
+    k_quantize_rows<<<blocks, 256, 0, ctx->stream>>>(a, m, k, lda, kp, qp, q, rowsum, nanrow);
+    OSC_TRY(check_launch(ctx, "k_quantize_rows"));
+  }
+  if (q_out != nullptr)
+    OSC_CUDA(cudaMemcpy2DAsync(q_out, k, q, kp, k, m, cudaMemcpyDeviceToDevice, ctx->stream), "copy q_out");
+  CUtensorMap mQ, mW;
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(kp), static_cast<uint64_t>(m)};
+    const uint64_t pitch[1] = {static_cast<uint64_t>(kp)};
+    const uint32_t box[2] = {kQBK, kQBM};
+    OSC_TRY(encode_tiled(&mQ, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, q, dims, pitch, box, CU_TENSOR_MAP_SWIZZLE_128B));
+  }
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(kp), static_cast<uint64_t>(w->n)};
+    const uint64_t pitch[1] = {static_cast<uint64_t>(kp)};
+    const uint32_t box[2] = {kQBK, kQBN};
+    OSC_TRY(encode_tiled(&mW, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, w->wt, dims, pitch, box, CU_TENSOR_MAP_SWIZZLE_128B));
+  }
+  DqmmArgs args{};
+  args.M = m;
+  args.N = w->n;
+  args.K = k;
+  args.num_kb = kp / kQBK;
+  args.fused_rows = grouped_rows(m);
+  args.full_cols = (w->n / 16) * 16;
+  args.qp = qp;
+  args.rowsum = rowsum;
+  args.nanrow = nanrow;
+  args.colsum = w->colsum;
+  args.wzp = w->zp;
+  args.wscale = w_scale;
+  args.n_scale = n_scale;
+  args.bias = bias;
+  args.y = y;
+  args.acc_out = acc_out;
+  const uint32_t idesc = (2u << 4) | (0u << 7) | ((w->is_signed ? 1u : 0u) << 10) |
+                         (static_cast<uint32_t>(kQBN >> 3) << 17) | (static_cast<uint32_t>(kQBM >> 4) << 24);
+  OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(k_dqmm_i8), kQSmem));
+  dim3 grid((w->n + kQBN - 1) / kQBN, (m + kQBM - 1) / kQBM);
+  prof_begin(ctx);
+  k_dqmm_i8<<<grid, kQThreads, kQSmem, ctx->stream>>>(mQ, mW, args, idesc, ctx->d_err);
+  return check_launch(ctx, "k_dqmm_i8");
+}
+
+}  // extern "C"

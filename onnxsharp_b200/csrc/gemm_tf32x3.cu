@@ -73,11 +73,18 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
     float acc[128];
     const bool ok = drain_loop<Cfg>(pb, tmem, num_kb, acc, err);
     if (ok) stage_tile<Cfg>(tiles, acc);
+    constexpr int kPitch = Cfg::BN + 4;
+    // The tile's column bias goes to shared memory once (one epilogue thread
+    // per column) instead of one global load per element.
+    float* sbias = reinterpret_cast<float*>(tiles) + kBM * kPitch;
+    {
+      const int jj = threadIdx.x - 64;
+      sbias[jj] = (col_bias != nullptr && n0 + jj < N) ? __ldg(col_bias + n0 + jj) : 0.0f;
+    }
     epi_sync<Cfg>();
     if (ok) {
       // Coalesced write-out: warp e copies rows e, e+EPI_WARPS, ...; lane l
       // handles columns 4l.. of each 128-column half (bias + activation here).
-      constexpr int kPitch = Cfg::BN + 4;
       const float* stage = reinterpret_cast<const float*>(tiles);
       const int e = warp - 2;
       const bool vec = ((ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(C) & 15u) == 0);
@@ -93,7 +100,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
           float v[4] = {s.x, s.y, s.z, s.w};
 #pragma unroll
           for (int t = 0; t < 4; ++t) {
-            if (col_bias != nullptr && c + t < N) v[t] = __fadd_rn(v[t], __ldg(col_bias + c + t));
+            if (col_bias != nullptr) v[t] = __fadd_rn(v[t], sbias[h + lane * 4 + t]);
             v[t] = apply_act(v[t], act);
           }
           if (vec && c + 4 <= N) {

@@ -21,9 +21,10 @@ enum : int {
   DEV_ERR_BOUNDS = 2,    // a kernel's own argument check failed
 };
 
-// A wait gives up after this many nanoseconds of %globaltimer, or after
-// kWaitMaxIters polls, whichever comes first.
-constexpr uint64_t kWaitLimitNs = 1500ull * 1000ull * 1000ull;  // 1.5 s
+// A wait gives up after kWaitLimitCycles SM clock cycles (~1.5 s at the
+// 1965 MHz maximum clock, longer at lower clocks), or after kWaitMaxIters
+// polls, whichever comes first.
+constexpr long long kWaitLimitCycles = 3000ll * 1000ll * 1000ll;
 constexpr uint32_t kWaitMaxIters = 1u << 30;
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
@@ -77,13 +78,16 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // On a timeout the launch's global error word gets DEV_ERR_TIMEOUT.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                           int* err) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
+  // Fast path: poll without touching any timer (the common case completes
+  // within a few polls); the SM cycle counter is only read every 256 polls.
+  for (int i = 0; i < 256; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  const long long c0 = clock64();
   for (uint32_t it = 1; it < kWaitMaxIters; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 31u) == 0u) {
+    if ((it & 255u) == 0u) {
       if (*abort_flag) return false;
-      if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+      if (clock64() - c0 > kWaitLimitCycles) break;
     }
   }
   *abort_flag = 1;

@@ -114,6 +114,45 @@ def conv2d(ctx: Context, x, w: ConvWeights, bias=None, stride=(1, 1), pads=(0, 0
     return out
 
 
+class DqmmWeights:
+    """Constant int8/uint8 W [k, n] of a DynamicQuantizeMatMul with its zero points."""
+
+    def __init__(self, ctx: Context, w, k: int, n: int, zero_points=None):
+        import numpy as np
+
+        is_signed = 1 if str(getattr(w, "dtype", "")).endswith("int8") and "uint8" not in str(w.dtype) else 0
+        zp = None if zero_points is None else np.ascontiguousarray(np.atleast_1d(zero_points), dtype=np.int32)
+        h = C.c_void_p()
+        call("osc_dqmm_prepack", ctx.handle, ptr(w), int(k), int(n), is_signed, None if zp is None else zp.ctypes.data,
+             0 if zp is None else zp.size, 0 if _is_device(w) else 1, C.byref(h))
+        self.handle = h
+        self.k, self.n, self.signed = int(k), int(n), bool(is_signed)
+        self._finalizer = weakref.finalize(self, _lib.load().osc_dqmm_weights_free, h)
+
+
+def dqmm(ctx: Context, a, w: DqmmWeights, w_scale, bias=None, out=None, minmax_override=None, q_out=None,
+         acc_out=None, params_out=None):
+    """DynamicQuantizeMatMul: y = (quant_u8(A) - zp) @ (W - wzp) * (a_scale * w_scale) + bias."""
+    import torch
+
+    m = a.shape[0]
+    if out is None:
+        out = torch.empty((m, w.n), dtype=torch.float32, device=a.device)
+    call("osc_dqmm_f32", ctx.handle, ptr(a), int(m), w.k, int(a.stride(0)), w.handle, ptr(w_scale),
+         int(w_scale.numel()), ptr(bias), ptr(out), ptr(minmax_override), ptr(q_out), ptr(acc_out), ptr(params_out))
+    return out
+
+
+def minmax(ctx: Context, x, out=None):
+    """{min(x, 0), max(x, 0)} over all elements of x (NaN skipped), as a 2-float device tensor."""
+    import torch
+
+    if out is None:
+        out = torch.empty(2, dtype=torch.float32, device=x.device)
+    call("osc_minmax_f32", ctx.handle, ptr(x), int(x.numel()), ptr(out))
+    return out
+
+
 def _is_device(x) -> bool:
     return bool(getattr(x, "is_cuda", False))
 
