@@ -153,6 +153,21 @@ def minmax(ctx: Context, x, out=None):
     return out
 
 
+def attention(ctx: Context, q, k, v, heads: int, scale: float, mask=None, out_head_space: bool = False, out=None):
+    """FusedAttention, heads form: q/k/v [B, T, H*D] on the device."""
+    import torch
+
+    B, T, width = q.shape
+    D = width // heads
+    if out is None:
+        shape = (B, heads, T, D) if out_head_space else (B, T, width)
+        out = torch.empty(shape, dtype=torch.float32, device=q.device)
+    mask_rows = 0 if mask is None else int(mask.shape[2])
+    call("osc_attention_f32", ctx.handle, ptr(q), ptr(k), ptr(v), ptr(mask), mask_rows, int(B), int(T), int(heads),
+         int(D), float(scale), 1 if out_head_space else 0, ptr(out))
+    return out
+
+
 def _is_device(x) -> bool:
     return bool(getattr(x, "is_cuda", False))
 

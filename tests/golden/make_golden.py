@@ -102,7 +102,7 @@ def small_fixtures() -> dict[str, np.ndarray]:
     qa = rng.normal(0, 1, (2, 80, 64)).astype(np.float32)
     ka = rng.normal(0, 1, (2, 80, 64)).astype(np.float32)
     va = rng.normal(0, 1, (2, 80, 64)).astype(np.float32)
-    out.update(attn_q=qa, attn_k=ka, attn_v=va, attn_o=oracle.attention(qa, ka, va, heads=4, scale=0.25, threads=1))
+    out.update(attn_q=qa, attn_k=ka, attn_v=va, attn_o=oracle.attention(qa, ka, va, heads=2, scale=0.25, threads=1))
     # DFL
     xd = rng.normal(0, 2, (2, 64, 100)).astype(np.float32)
     out.update(dfl_x=xd, dfl_y=oracle.dfl(xd, 16, threads=1))
