@@ -131,6 +131,23 @@ OSC_API int osc_gemm_bias_f32(osc_ctx* ctx, const float* a, int m, int k, int ld
                               const osc_gemm_weights* w, const float* col_bias, int act, float* c,
                               int ldc);
 
+/* Same as osc_gemm_bias_f32, but allocates no device memory: for callers that
+ * must not call cudaMalloc while serving (a host that fixes its GPU memory
+ * budget at start-up, or one sharing the GPU with other work, where an
+ * allocation can synchronise the whole device at an arbitrary moment). This
+ * entry point has no counterpart in the reference (which has no device).
+ * Its temporaries live in a fixed 8 MiB array compiled into the library (held
+ * by every GPU that loads it, until the process exits): a call needs
+ * m * round_up(k, 4) <= 1048576 (e.g. 2048 x 512) and is rejected with
+ * OSC_EINVAL beyond that. The first call on a device looks up that array's
+ * device address (cudaGetSymbolAddress) and should come before any stream
+ * capture. All calls share the array: calls whose kernels may overlap on the
+ * GPU (other streams or contexts on the same device) race and must be
+ * serialised by the caller. */
+OSC_API int osc_gemm_bias_f32_noalloc(osc_ctx* ctx, const float* a, int m, int k, int lda,
+                                      const osc_gemm_weights* w, const float* col_bias, int act, float* c,
+                                      int ldc);
+
 /* ------------------------------------------------------------ Conv (+FusedActivation)
  * Replaces ConvLayer.Forward (src/OnnxSharp/Ops/DnnOps.cs:411-500) and its
  * kernel chain (Kernels/ConvKernels.cs Im2Col/Pointwise, NchwcConv,

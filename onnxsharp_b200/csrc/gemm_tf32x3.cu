@@ -19,6 +19,7 @@
 // thread, releasing each stage with tcgen05.commit; warps 2-5 read the
 // accumulator back from TMEM and apply bias + activation.
 #include <cstdlib>
+#include <mutex>
 
 #include "runtime.h"
 #include "sm100.cuh"
@@ -324,6 +325,124 @@ OSC_API int osc_gemm_bias_f32(osc_ctx* ctx, const float* a, int m, int k, int ld
   if (m == 0) return OSC_OK;
   if (fault_injected("launch")) return fail(OSC_EFAULT_INJECTED, "injected failure (launch)");
   return gemm_tf32x3(ctx, a, m, k, lda, w, col_bias, act, c, ldc);
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// MatMul + bias without any device allocation (osc_gemm_bias_f32_noalloc).
+//
+// Some callers cannot allocate device memory while they run inference: a host
+// that sizes all of its GPU memory once at start-up and must not grow it per
+// request, or one serving several models from the same GPU, where a
+// cudaMalloc / cudaFree can synchronise the whole device and stall every
+// other stream at an unpredictable point. osc_gemm_bias_f32 takes its
+// per-call temporaries (the TF32 hi/lo split of A) from the context's
+// scratch arena, which grows with cudaMalloc; this variant takes them from a
+// fixed array compiled into the library instead, so a call never allocates.
+//
+// The array below is in every GPU that loads the library, for the life of the
+// process: 2 x kNoAllocMaxElems floats = 8 MiB. A call needs
+// m * round_up(k, 4) <= kNoAllocMaxElems (e.g. 2048 x 512); larger calls are
+// rejected with OSC_EINVAL. All calls on a device share the array and it keeps
+// the previous call's contents: every element a call reads is first written by
+// that call's split kernel (including the zero padding of K), so nothing needs
+// clearing, but two calls whose kernels overlap on the GPU (different streams,
+// or different contexts on the same device) race on it and must be serialised
+// by the caller.
+namespace osc {
+namespace {
+
+constexpr size_t kNoAllocMaxElems = size_t(1) << 20;  // per hi / lo part
+
+__device__ __align__(256) float g_noalloc_scratch[2 * kNoAllocMaxElems];
+
+// In host code g_noalloc_scratch names a host-side stand-in, not device
+// memory; the device address is looked up once per device with that device
+// current and cached here.
+std::mutex g_noalloc_mu;
+float* g_noalloc_ptr[64] = {};
+
+int noalloc_scratch(int device, float** out) {
+  if (device < 0 || device >= 64) return fail(OSC_EINVAL, "osc_gemm_bias_f32_noalloc: device %d out of range", device);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[device] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress (no-alloc scratch)");
+    g_noalloc_ptr[device] = static_cast<float*>(p);
+  }
+  *out = g_noalloc_ptr[device];
+  return OSC_OK;
+}
+
+// Same kernels and launch shapes as gemm_tf32x3(), minus the scratch arena and
+// the profiling events.
+template <class Cfg>
+int launch_gemm_noalloc(osc_ctx* ctx, const float* ahi, const float* alo, int M, int Kp, const osc_gemm_weights* w,
+                        const float* bias, int act, float* C, int ldc) {
+  CUtensorMap mAh, mAl, mBh, mBl;
+  const uint64_t dimsA[2] = {static_cast<uint64_t>(Kp), static_cast<uint64_t>(M)};
+  const uint64_t dimsB[2] = {static_cast<uint64_t>(Kp), static_cast<uint64_t>(w->n)};
+  const uint64_t pitch[1] = {static_cast<uint64_t>(Kp) * 4};
+  const uint32_t boxA[2] = {kBK, kBM};
+  const uint32_t boxB[2] = {kBK, static_cast<uint32_t>(Cfg::BN)};
+  OSC_TRY(encode_tiled(&mAh, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, ahi, dimsA, pitch, boxA, CU_TENSOR_MAP_SWIZZLE_128B));
+  OSC_TRY(encode_tiled(&mAl, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, alo, dimsA, pitch, boxA, CU_TENSOR_MAP_SWIZZLE_128B));
+  OSC_TRY(encode_tiled(&mBh, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, w->hi, dimsB, pitch, boxB, CU_TENSOR_MAP_SWIZZLE_128B));
+  OSC_TRY(encode_tiled(&mBl, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, w->lo, dimsB, pitch, boxB, CU_TENSOR_MAP_SWIZZLE_128B));
+  auto kern = k_gemm_tf32x3<Cfg>;
+  OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(kern), Cfg::SMEM_BYTES));
+  dim3 grid((w->n + Cfg::BN - 1) / Cfg::BN, (M + kBM - 1) / kBM);
+  kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, ctx->stream>>>(mAh, mAl, mBh, mBl, M, w->n, Kp, bias, act, C, ldc,
+                                                              ctx->d_err);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "k_gemm_tf32x3 (no-alloc)");
+  return OSC_OK;
+}
+
+}  // namespace
+}  // namespace osc
+
+extern "C" {
+
+OSC_API int osc_gemm_bias_f32_noalloc(osc_ctx* ctx, const float* a, int m, int k, int lda, const osc_gemm_weights* w,
+                                      const float* col_bias, int act, float* c, int ldc) {
+  OSC_TRY(enter(ctx));
+  if (w == nullptr) return fail(OSC_EINVAL, "osc_gemm_bias_f32_noalloc: null weights");
+  if (w->device != ctx->device) return fail(OSC_EINVAL, "osc_gemm_bias_f32_noalloc: weights live on another device");
+  if (k != w->k) return fail(OSC_EINVAL, "osc_gemm_bias_f32_noalloc: A has k=%d, packed B has k=%d", k, w->k);
+  if (m < 0) return fail(OSC_EINVAL, "osc_gemm_bias_f32_noalloc: m=%d", m);
+  if (act < OSC_ACT_NONE || act > OSC_ACT_SIGMOID) return fail(OSC_EINVAL, "osc_gemm_bias_f32_noalloc: act=%d", act);
+  if (lda == 0) lda = k;
+  if (ldc == 0) ldc = w->n;
+  if (lda < k || ldc < w->n) return fail(OSC_EINVAL, "osc_gemm_bias_f32_noalloc: lda=%d ldc=%d too small", lda, ldc);
+  const size_t elems = static_cast<size_t>(m) * static_cast<size_t>(w->kp);
+  if (elems > kNoAllocMaxElems)
+    return fail(OSC_EINVAL,
+                "osc_gemm_bias_f32_noalloc: m * round_up(k, 4) = %zu exceeds the fixed scratch limit of %zu "
+                "elements (%d rows at k=%d); use osc_gemm_bias_f32 or split the rows",
+                elems, kNoAllocMaxElems, static_cast<int>(kNoAllocMaxElems / static_cast<size_t>(w->kp)), k);
+  if (m == 0) return OSC_OK;
+  if (a == nullptr || c == nullptr) return fail(OSC_EINVAL, "osc_gemm_bias_f32_noalloc: null pointer");
+  float* base = nullptr;
+  OSC_TRY(noalloc_scratch(ctx->device, &base));
+  float* ahi = base;
+  float* alo = base + kNoAllocMaxElems;
+  const int kp = w->kp;
+  {
+    const size_t work = static_cast<size_t>(m) * (kp / 4);
+    size_t blocks = (work + 255) / 256;
+    const size_t cap = static_cast<size_t>(ctx->num_sms) * 8;
+    if (blocks > cap) blocks = cap;
+    k_split_rows<<<static_cast<int>(blocks < 1 ? 1 : blocks), 256, 0, ctx->stream>>>(a, m, k, lda, kp, ahi, alo);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "k_split_rows (no-alloc)");
+  }
+  const long tiles256 = static_cast<long>((w->n + 255) / 256) * ((m + kBM - 1) / kBM);
+  const bool wide = w->n > 128 && tiles256 >= ctx->num_sms * 3 / 4;
+  if (wide) return launch_gemm_noalloc<Tf32x3Cfg<256, 2, 2>>(ctx, ahi, alo, m, kp, w, col_bias, act, c, ldc);
+  return launch_gemm_noalloc<Tf32x3Cfg<128, 3, 2>>(ctx, ahi, alo, m, kp, w, col_bias, act, c, ldc);
 }
 
 }  // extern "C"
