@@ -103,6 +103,18 @@ OSC_API int osc_profile_read(osc_ctx* ctx, const char* prefix, double* total_ms,
 OSC_API int osc_profile_reset(osc_ctx* ctx);
 OSC_API unsigned long long osc_launch_count(osc_ctx* ctx);
 
+/* Static-plan capture: the executor runs a shape-specialised plan once to
+ * size the scratch arena, then records it between osc_graph_begin and
+ * osc_graph_end (stream capture of the context's stream) and replays it with
+ * osc_graph_launch — one CUDA graph per input signature, the device
+ * counterpart of the reference's per-signature plan cache
+ * (Core/LayerPlan.cs:32-94, Core/Interpreter.cs:87-146). */
+typedef struct osc_graph osc_graph;
+OSC_API int osc_graph_begin(osc_ctx* ctx);
+OSC_API int osc_graph_end(osc_ctx* ctx, osc_graph** out);
+OSC_API int osc_graph_launch(osc_ctx* ctx, const osc_graph* graph);
+OSC_API int osc_graph_free(osc_graph* graph);
+
 /* Device memory and copies, for callers without a framework allocator (the
  * reference's Tensor buffers are pinned host arrays, Tensors/Tensor.cs:65-155). */
 OSC_API int osc_malloc(osc_ctx* ctx, size_t bytes, void** out);
@@ -215,6 +227,74 @@ OSC_API int osc_minmax_f32(osc_ctx* ctx, const float* x, long count, float* minm
 OSC_API int osc_attention_f32(osc_ctx* ctx, const float* q, const float* k, const float* v, const float* mask,
                               int mask_rows, int B, int T, int H, int D, float scale, int out_head_space,
                               float* out);
+
+/* ------------------------------------------------------------ graph glue (YOLO11n-shaped graph)
+ * NCHW tensors may be channel slices of larger buffers: *_nstride is the
+ * element distance between consecutive images (0 = dense), so a Split output
+ * is a pointer offset and a Concat input can be produced in place. */
+
+/* Conv with image strides and an optional residual added after the
+ * activation: y = residual + act(conv(x) + bias) (the C3k2 / PSA bottleneck
+ * Add of the exported graph fused into the conv). group must be 1. */
+OSC_API int osc_conv2d_ex_f32(osc_ctx* ctx, const float* x, long long x_nstride, int N, int C, int H, int W,
+                              const osc_conv_weights* w, int stride_h, int stride_w, int pad_t, int pad_l, int pad_b,
+                              int pad_r, int dil_h, int dil_w, const float* bias, int act, const float* residual,
+                              long long res_nstride, float* y, long long y_nstride, int OH, int OW);
+
+/* Direct (CUDA-core) conv for grouped / depthwise convs and first layers with
+ * few input channels (Kernels/DepthwiseConv.cs:25-93, Kernels/FirstConv.cs:54-121).
+ * w is the raw [M, C/group, kh, kw] device tensor. */
+OSC_API int osc_conv2d_direct_f32(osc_ctx* ctx, const float* x, long long x_nstride, int N, int C, int H, int W,
+                                  const float* w, int M, int kh, int kw, int stride_h, int stride_w, int pad_t,
+                                  int pad_l, int pad_b, int pad_r, int dil_h, int dil_w, int group, const float* bias,
+                                  int act, const float* residual, long long res_nstride, float* y, long long y_nstride,
+                                  int OH, int OW);
+
+/* MaxPool (Ops/DnnOps.cs:1335), floor mode, padding ignored in the max. */
+OSC_API int osc_maxpool2d_f32(osc_ctx* ctx, const float* x, long long x_nstride, int N, int C, int H, int W, int kh,
+                              int kw, int stride_h, int stride_w, int pad_t, int pad_l, int pad_b, int pad_r, float* y,
+                              long long y_nstride, int OH, int OW);
+
+/* Resize, nearest, integer up-scale factors (Ops/DnnOps.cs:2215). */
+OSC_API int osc_resize_nearest_f32(osc_ctx* ctx, const float* x, long long x_nstride, int N, int C, int H, int W,
+                                   int scale_h, int scale_w, float* y, long long y_nstride);
+
+/* y = a (op) b with numpy broadcasting, rank <= 4, dense tensors;
+ * op: 0 Add, 1 Sub, 2 Mul, 3 Div (Ops/BroadcastOps.cs). Shapes are host arrays. */
+OSC_API int osc_binary_f32(osc_ctx* ctx, int op, const float* a, const long long* a_shape, int a_rank, const float* b,
+                           const long long* b_shape, int b_rank, float* y);
+
+/* y[i] = act(x[i]) with the reference's VectorMath formulas (SiLU / Sigmoid / ReLU). */
+OSC_API int osc_unary_f32(osc_ctx* ctx, const float* x, float* y, long long n, int act);
+
+/* Softmax over the last axis of a [rows, len] tensor (Ops/DnnOps.cs:2547 ->
+ * VectorMath.SoftmaxRow, VectorMath.cs:282). */
+OSC_API int osc_softmax_f32(osc_ctx* ctx, const float* x, float* y, long long rows, int len);
+
+/* DflSoftmax (Ops/DflOps.cs:90-250): x [B, sides*bins, pixels] ->
+ * out [B, sides, pixels] = sum_b b * softmax_b. bins <= 32. */
+OSC_API int osc_dfl_f32(osc_ctx* ctx, const float* x, int B, int sides, int bins, int pixels, float* out);
+
+/* The YOLO Detect tail fused: per scale i (3 scales) the box logits box[i]
+ * [B, 64, hs[i], ws[i]] and class logits cls[i] [B, nc, hs[i], ws[i]] (views)
+ * -> out [B, 4 + nc, A] (A = sum hs*ws): DFL (reg_max 16), dist2bbox with
+ * anchor points (x + 0.5, y + 0.5) in the exported graph's op order, times
+ * strides[i]; sigmoid of the class logits. Pointer arrays are host arrays. */
+OSC_API int osc_yolo_decode_f32(osc_ctx* ctx, int B, int nc, const float* const* box, const long long* box_nstride,
+                                const float* const* cls, const long long* cls_nstride, const int* hs, const int* ws,
+                                const float* strides, float* out);
+
+/* LayerNormalization over the trailing `inner` elements (Ops/AttnOps.cs:199-358).
+ * gamma / beta may be NULL. */
+OSC_API int osc_layernorm_f32(osc_ctx* ctx, const float* x, int outer, int inner, const float* gamma,
+                              const float* beta, float eps, float* y);
+
+/* Attention of YOLO11's PSA block (sequence T = H*W, not limited to 128):
+ * qkv [B, heads*(2*kd + hd), T] -> out [B, heads*hd, T] with
+ * out = v softmax(scale * q^T k)^T per head (the exported MatMul / Mul /
+ * Softmax / MatMul sequence). */
+OSC_API int osc_psa_attention_f32(osc_ctx* ctx, const float* qkv, long long qkv_nstride, int B, int heads, int kd,
+                                  int hd, int T, float scale, float* out, long long out_nstride);
 
 #ifdef __cplusplus
 }

@@ -47,6 +47,7 @@ class OscUnavailable(RuntimeError):
 
 vp = C.c_void_p
 i32 = C.c_int
+i64 = C.c_longlong
 f32 = C.c_float
 sz = C.c_size_t
 pp = C.POINTER(C.c_void_p)
@@ -66,6 +67,10 @@ SIGNATURES: dict[str, tuple] = {
     "osc_profile_read": (i32, [vp, C.c_char_p, C.POINTER(C.c_double), C.POINTER(i32)]),
     "osc_profile_reset": (i32, [vp]),
     "osc_launch_count": (C.c_ulonglong, [vp]),
+    "osc_graph_begin": (i32, [vp]),
+    "osc_graph_end": (i32, [vp, pp]),
+    "osc_graph_launch": (i32, [vp, vp]),
+    "osc_graph_free": (i32, [vp]),
     "osc_malloc": (i32, [vp, sz, pp]),
     "osc_free": (i32, [vp, vp]),
     "osc_memcpy_htod": (i32, [vp, vp, vp, sz]),
@@ -87,6 +92,20 @@ SIGNATURES: dict[str, tuple] = {
     "osc_minmax_f32": (i32, [vp, vp, C.c_long, vp]),
     # FusedAttention
     "osc_attention_f32": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, f32, i32, vp]),
+    # graph glue
+    "osc_conv2d_ex_f32": (i32, [vp, vp, i64, i32, i32, i32, i32, vp] + [i32] * 8 + [vp, i32, vp, i64, vp, i64, i32,
+                                                                                   i32]),
+    "osc_conv2d_direct_f32": (i32, [vp, vp, i64, i32, i32, i32, i32, vp, i32, i32, i32] + [i32] * 9 +
+                              [vp, i32, vp, i64, vp, i64, i32, i32]),
+    "osc_maxpool2d_f32": (i32, [vp, vp, i64, i32, i32, i32, i32] + [i32] * 8 + [vp, i64, i32, i32]),
+    "osc_resize_nearest_f32": (i32, [vp, vp, i64, i32, i32, i32, i32, i32, i32, vp, i64]),
+    "osc_binary_f32": (i32, [vp, i32, vp, vp, i32, vp, vp, i32, vp]),
+    "osc_unary_f32": (i32, [vp, vp, vp, i64, i32]),
+    "osc_softmax_f32": (i32, [vp, vp, vp, i64, i32]),
+    "osc_dfl_f32": (i32, [vp, vp, i32, i32, i32, i32, vp]),
+    "osc_yolo_decode_f32": (i32, [vp, i32, i32, vp, vp, vp, vp, vp, vp, vp, vp]),
+    "osc_layernorm_f32": (i32, [vp, vp, i32, i32, vp, vp, f32, vp]),
+    "osc_psa_attention_f32": (i32, [vp, vp, i64, i32, i32, i32, i32, i32, f32, vp, i64]),
 }
 
 _lib: C.CDLL | None = None

@@ -55,6 +55,9 @@ struct ConvGeom {
   int BW, BH;         // pixel box (BW * BH == 256)
   int tiles_w, tiles_h;
   int act;
+  long long y_nstride;      // elements between images of y (>= M*OH*OW: y may be a channel slice)
+  const float* res;         // optional residual added after the activation (same geometry as y)
+  long long res_nstride;
 };
 
 __global__ void __launch_bounds__(ConvCfg::THREADS, 1)
@@ -118,7 +121,9 @@ __global__ void __launch_bounds__(ConvCfg::THREADS, 1)
         const int oc = m0 + r;
         if (oc >= g.M) break;
         const float b = sbias[r];
-        float* yplane = y + (static_cast<size_t>(n) * g.M + oc) * g.OH * g.OW;
+        const size_t plane_off = static_cast<size_t>(oc) * g.OH * g.OW;
+        float* yplane = y + static_cast<size_t>(n) * g.y_nstride + plane_off;
+        const float* rplane = g.res ? g.res + static_cast<size_t>(n) * g.res_nstride + plane_off : nullptr;
 #pragma unroll
         for (int h = 0; h < Cfg::BN; h += 128) {
           const int p = h + lane * 4;  // 4 consecutive pixels of one box row (BW >= 8)
@@ -127,9 +132,14 @@ __global__ void __launch_bounds__(ConvCfg::THREADS, 1)
           const float4 s = *reinterpret_cast<const float4*>(stage + r * kPitch + p);
           float v[4] = {s.x, s.y, s.z, s.w};
           float* dst = yplane + static_cast<size_t>(oy) * g.OW + ox;
+          const float* rsrc = rplane ? rplane + static_cast<size_t>(oy) * g.OW + ox : nullptr;
 #pragma unroll
           for (int q = 0; q < 4; ++q)
-            if (ox + q < g.OW) dst[q] = apply_act(__fadd_rn(v[q], b), g.act);
+            if (ox + q < g.OW) {
+              float o = apply_act(__fadd_rn(v[q], b), g.act);
+              if (rsrc) o = __fadd_rn(rsrc[q], o);  // residual Add(x, act(conv)) as in the graph
+              dst[q] = o;
+            }
         }
       }
     }
@@ -141,8 +151,9 @@ __global__ void __launch_bounds__(ConvCfg::THREADS, 1)
 // One block per (n, phase-row h' of phase py, 32-wide w' strip, 32-channel
 // strip): reads 32 channels x 32 pixels of one input row, writes them
 // channel-innermost.
-__global__ void k_nchw_to_phase_nhwc(const float* __restrict__ x, int N, int C, int H, int W, int s, int Hp,
-                                     int Wp, int Cp, int z_base, float* __restrict__ hi, float* __restrict__ lo) {
+__global__ void k_nchw_to_phase_nhwc(const float* __restrict__ x, long long x_nstride, int N, int C, int H, int W,
+                                     int s, int Hp, int Wp, int Cp, int z_base, float* __restrict__ hi,
+                                     float* __restrict__ lo) {
   __shared__ float tile[32][33];
   const int wq = blockIdx.x * 32;        // w' strip start
   const int c0 = blockIdx.y * 32;        // channel strip
@@ -158,7 +169,8 @@ __global__ void k_nchw_to_phase_nhwc(const float* __restrict__ x, int N, int C, 
     const int c = c0 + yy;
     const int iw = (wq + tx) * s + px;
     float v = 0.0f;
-    if (c < C && ih < H && iw < W && (wq + tx) < Wp) v = x[((static_cast<size_t>(n) * C + c) * H + ih) * W + iw];
+    if (c < C && ih < H && iw < W && (wq + tx) < Wp)
+      v = x[static_cast<size_t>(n) * x_nstride + (static_cast<size_t>(c) * H + ih) * W + iw];
     tile[yy][tx] = v;
   }
   __syncthreads();
@@ -178,9 +190,9 @@ __global__ void k_nchw_to_phase_nhwc(const float* __restrict__ x, int N, int C, 
 // Stride-1 fast path of the transform (a single phase image): each block
 // moves a 32-channel x 32-pixel tile of one input row with one float4 load
 // and one float4 store (hi and lo) per thread.
-__global__ void __launch_bounds__(256) k_nchw_to_nhwc_split(const float* __restrict__ x, int N, int C, int H, int W,
-                                                            int Cp, int z_base, float* __restrict__ hi,
-                                                            float* __restrict__ lo) {
+__global__ void __launch_bounds__(256) k_nchw_to_nhwc_split(const float* __restrict__ x, long long x_nstride, int N,
+                                                            int C, int H, int W, int Cp, int z_base,
+                                                            float* __restrict__ hi, float* __restrict__ lo) {
   __shared__ float tile[32][33];
   const int w0 = blockIdx.x * 32;
   const int c0 = blockIdx.y * 32;
@@ -191,7 +203,7 @@ __global__ void __launch_bounds__(256) k_nchw_to_nhwc_split(const float* __restr
     const int c = c0 + (tid >> 3), w = w0 + (tid & 7) * 4;
     float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
     if (c < C) {
-      const float* src = x + ((static_cast<size_t>(n) * C + c) * H + h) * W + w;
+      const float* src = x + static_cast<size_t>(n) * x_nstride + (static_cast<size_t>(c) * H + h) * W + w;
       if (w + 4 <= W && (reinterpret_cast<uintptr_t>(src) & 15u) == 0) {
         const float4 t = __ldg(reinterpret_cast<const float4*>(src));
         v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
@@ -259,8 +271,9 @@ static void choose_box(int OH, int OW, int* BW, int* BH) {
   }
 }
 
-int conv_tf32x3(osc_ctx* ctx, const float* x, int N, int C, int H, int W, const osc_conv_weights* w, int sh, int sw,
-                int pt, int pl, int dh, int dw, const float* bias, int act, float* y, int OH, int OW) {
+int conv_tf32x3(osc_ctx* ctx, const float* x, long long x_nstride, int N, int C, int H, int W, const osc_conv_weights* w,
+                int sh, int sw, int pt, int pl, int dh, int dw, const float* bias, int act, const float* res,
+                long long res_nstride, float* y, long long y_nstride, int OH, int OW) {
   if (sh != sw) return fail(OSC_EUNSUPPORTED, "conv: unequal strides %d x %d", sh, sw);
   const int s = sh;
   const int Hp = (H + s - 1) / s, Wp = (W + s - 1) / s;
@@ -279,11 +292,12 @@ int conv_tf32x3(osc_ctx* ctx, const float* x, int N, int C, int H, int W, const 
       dim3 grid((Wp + 31) / 32, Cp / 32, static_cast<unsigned>(std::min(zmax, zt - z0)));
       prof_begin(ctx);
       if (s == 1) {
-        k_nchw_to_nhwc_split<<<grid, 256, 0, ctx->stream>>>(x, N, C, H, W, Cp, static_cast<int>(z0), xh, xl);
+        k_nchw_to_nhwc_split<<<grid, 256, 0, ctx->stream>>>(x, x_nstride, N, C, H, W, Cp, static_cast<int>(z0), xh,
+                                                             xl);
         OSC_TRY(check_launch(ctx, "k_nchw_to_nhwc_split"));
       } else {
-        k_nchw_to_phase_nhwc<<<grid, 256, 0, ctx->stream>>>(x, N, C, H, W, s, Hp, Wp, Cp, static_cast<int>(z0), xh,
-                                                            xl);
+        k_nchw_to_phase_nhwc<<<grid, 256, 0, ctx->stream>>>(x, x_nstride, N, C, H, W, s, Hp, Wp, Cp,
+                                                            static_cast<int>(z0), xh, xl);
         OSC_TRY(check_launch(ctx, "k_nchw_to_phase_nhwc"));
       }
     }
@@ -307,6 +321,9 @@ int conv_tf32x3(osc_ctx* ctx, const float* x, int N, int C, int H, int W, const 
   g.OH = OH;
   g.OW = OW;
   g.act = act;
+  g.y_nstride = y_nstride;
+  g.res = res;
+  g.res_nstride = res_nstride;
   choose_box(OH, OW, &g.BW, &g.BH);
   g.tiles_w = (OW + g.BW - 1) / g.BW;
   g.tiles_h = (OH + g.BH - 1) / g.BH;
@@ -406,29 +423,52 @@ OSC_API int osc_conv_weights_free(osc_conv_weights* w) {
   return OSC_OK;
 }
 
-OSC_API int osc_conv2d_bias_act_f32(osc_ctx* ctx, const float* x, int N, int C, int H, int W,
-                                    const osc_conv_weights* w, int stride_h, int stride_w, int pad_t, int pad_l,
-                                    int pad_b, int pad_r, int dil_h, int dil_w, int group, const float* bias, int act,
-                                    float* y, int OH, int OW) {
+static int conv_entry(osc_ctx* ctx, const char* fn, const float* x, long long x_nstride, int N, int C, int H, int W,
+                      const osc_conv_weights* w, int stride_h, int stride_w, int pad_t, int pad_l, int pad_b,
+                      int pad_r, int dil_h, int dil_w, int group, const float* bias, int act, const float* res,
+                      long long res_nstride, float* y, long long y_nstride, int OH, int OW) {
   OSC_TRY(enter(ctx));
-  if (w == nullptr) return fail(OSC_EINVAL, "osc_conv2d_bias_act_f32: null weights");
-  if (w->device != ctx->device) return fail(OSC_EINVAL, "osc_conv2d_bias_act_f32: weights live on another device");
-  if (group != 1) return fail(OSC_EUNSUPPORTED, "osc_conv2d_bias_act_f32: group=%d (use osc_conv2d_depthwise_f32)", group);
-  if (C != w->C) return fail(OSC_EINVAL, "osc_conv2d_bias_act_f32: input has %d channels, weights %d", C, w->C);
+  if (w == nullptr) return fail(OSC_EINVAL, "%s: null weights", fn);
+  if (w->device != ctx->device) return fail(OSC_EINVAL, "%s: weights live on another device", fn);
+  if (group != 1) return fail(OSC_EUNSUPPORTED, "%s: group=%d (use osc_conv2d_direct_f32)", fn, group);
+  if (C != w->C) return fail(OSC_EINVAL, "%s: input has %d channels, weights %d", fn, C, w->C);
   if (N < 0 || H <= 0 || W <= 0 || stride_h <= 0 || stride_w <= 0 || dil_h <= 0 || dil_w <= 0 || pad_t < 0 ||
       pad_l < 0 || pad_b < 0 || pad_r < 0)
-    return fail(OSC_EINVAL, "osc_conv2d_bias_act_f32: bad geometry");
-  if (act < OSC_ACT_NONE || act > OSC_ACT_SIGMOID) return fail(OSC_EINVAL, "osc_conv2d_bias_act_f32: act=%d", act);
+    return fail(OSC_EINVAL, "%s: bad geometry", fn);
+  if (act < OSC_ACT_NONE || act > OSC_ACT_SIGMOID) return fail(OSC_EINVAL, "%s: act=%d", fn, act);
   // Output size as Ops/DnnOps.cs:53-66 (floor mode).
   const int eh = (w->kh - 1) * dil_h + 1, ew = (w->kw - 1) * dil_w + 1;
   const int oh = (H + pad_t + pad_b - eh) / stride_h + 1;
   const int ow = (W + pad_l + pad_r - ew) / stride_w + 1;
   if (oh != OH || ow != OW || oh <= 0 || ow <= 0)
-    return fail(OSC_EINVAL, "osc_conv2d_bias_act_f32: output must be %dx%d, got %dx%d", oh, ow, OH, OW);
+    return fail(OSC_EINVAL, "%s: output must be %dx%d, got %dx%d", fn, oh, ow, OH, OW);
+  const long long dense_x = static_cast<long long>(C) * H * W, dense_y = static_cast<long long>(w->M) * OH * OW;
+  if (x_nstride == 0) x_nstride = dense_x;
+  if (y_nstride == 0) y_nstride = dense_y;
+  if (res_nstride == 0) res_nstride = dense_y;
+  if (x_nstride < dense_x || y_nstride < dense_y || (res != nullptr && res_nstride < dense_y))
+    return fail(OSC_EINVAL, "%s: image stride smaller than one image", fn);
   if (N == 0) return OSC_OK;
-  if (x == nullptr || y == nullptr) return fail(OSC_EINVAL, "osc_conv2d_bias_act_f32: null pointer");
+  if (x == nullptr || y == nullptr) return fail(OSC_EINVAL, "%s: null pointer", fn);
   if (fault_injected("launch")) return fail(OSC_EFAULT_INJECTED, "injected failure (launch)");
-  return conv_tf32x3(ctx, x, N, C, H, W, w, stride_h, stride_w, pad_t, pad_l, dil_h, dil_w, bias, act, y, OH, OW);
+  return conv_tf32x3(ctx, x, x_nstride, N, C, H, W, w, stride_h, stride_w, pad_t, pad_l, dil_h, dil_w, bias, act, res,
+                     res_nstride, y, y_nstride, OH, OW);
+}
+
+OSC_API int osc_conv2d_bias_act_f32(osc_ctx* ctx, const float* x, int N, int C, int H, int W,
+                                    const osc_conv_weights* w, int stride_h, int stride_w, int pad_t, int pad_l,
+                                    int pad_b, int pad_r, int dil_h, int dil_w, int group, const float* bias, int act,
+                                    float* y, int OH, int OW) {
+  return conv_entry(ctx, "osc_conv2d_bias_act_f32", x, 0, N, C, H, W, w, stride_h, stride_w, pad_t, pad_l, pad_b,
+                    pad_r, dil_h, dil_w, group, bias, act, nullptr, 0, y, 0, OH, OW);
+}
+
+OSC_API int osc_conv2d_ex_f32(osc_ctx* ctx, const float* x, long long x_nstride, int N, int C, int H, int W,
+                              const osc_conv_weights* w, int stride_h, int stride_w, int pad_t, int pad_l, int pad_b,
+                              int pad_r, int dil_h, int dil_w, const float* bias, int act, const float* residual,
+                              long long res_nstride, float* y, long long y_nstride, int OH, int OW) {
+  return conv_entry(ctx, "osc_conv2d_ex_f32", x, x_nstride, N, C, H, W, w, stride_h, stride_w, pad_t, pad_l, pad_b,
+                    pad_r, dil_h, dil_w, 1, bias, act, residual, res_nstride, y, y_nstride, OH, OW);
 }
 
 }  // extern "C"

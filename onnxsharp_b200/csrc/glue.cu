@@ -1,0 +1,634 @@
+// glue.cu — the memory-bound operators around the tensor-core kernels on the
+// YOLO11n-shaped graph and the attention block: direct conv (first layer /
+// depthwise), MaxPool, nearest Resize, broadcasting binary ops, unary
+// activations, Softmax, DflSoftmax, the fused YOLO head decode, LayerNorm and
+// the C2PSA attention (T = H*W > 128). CUDA cores, 128-bit accesses where the
+// layout allows, warp-shuffle reductions. Reference file:line per kernel.
+//
+// NCHW tensors may be channel slices of larger buffers: `*_nstride` is the
+// element distance between consecutive images (0 = dense), so Split outputs
+// are pointer offsets and Concat inputs are written in place.
+#include <algorithm>
+#include <cmath>
+
+#include "runtime.h"
+#include "vmath.cuh"
+
+namespace osc {
+namespace {
+
+inline int blocks_for(osc_ctx* ctx, long long work, int threads = 256, int per_sm = 16) {
+  long long b = (work + threads - 1) / threads;
+  const long long cap = static_cast<long long>(ctx->num_sms) * per_sm;
+  if (b > cap) b = cap;
+  return static_cast<int>(b < 1 ? 1 : b);
+}
+
+__device__ __forceinline__ float maxps(float a, float b) { return a > b ? a : b; }
+
+// ---------------------------------------------------------------- direct conv
+// Ops/DnnOps.cs:411-500 via Kernels/DepthwiseConv.cs:25-93 (groups == C == M)
+// and Kernels/FirstConv.cs:54-121 (few input channels). One thread per output
+// pixel and group, OCB output channels at a time; acc = bias, then FMA over
+// (ic, ky, kx) ascending with padded taps contributing fmaf(w, 0, acc) (the
+// im2col order of ConvKernels.cs:525-654).
+template <int OCB>
+__global__ void k_conv_direct(const float* __restrict__ x, long long x_nstride, int N, int C, int H, int W,
+                              const float* __restrict__ w, int M, int kh, int kw, int sh, int sw, int pt, int pl,
+                              int dh, int dw, int group, const float* __restrict__ bias, int act,
+                              const float* __restrict__ res, long long res_nstride, float* __restrict__ y,
+                              long long y_nstride, int OH, int OW) {
+  const int cpg = C / group, mpg = M / group;
+  const int ocb_per_group = (mpg + OCB - 1) / OCB;
+  const long long total = static_cast<long long>(N) * group * ocb_per_group * OH * OW;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    long long t = i;
+    const int ox = static_cast<int>(t % OW);
+    t /= OW;
+    const int oy = static_cast<int>(t % OH);
+    t /= OH;
+    const int ob = static_cast<int>(t % ocb_per_group);
+    t /= ocb_per_group;
+    const int g = static_cast<int>(t % group);
+    const int n = static_cast<int>(t / group);
+    const int oc0 = g * mpg + ob * OCB;
+    const int noc = min(OCB, mpg - ob * OCB);
+    float acc[OCB];
+#pragma unroll
+    for (int o = 0; o < OCB; ++o) acc[o] = (o < noc && bias) ? __ldg(bias + oc0 + o) : 0.0f;
+    const float* xn = x + static_cast<size_t>(n) * x_nstride;
+    for (int ic = 0; ic < cpg; ++ic) {
+      const float* xc = xn + static_cast<size_t>(g * cpg + ic) * H * W;
+      for (int ky = 0; ky < kh; ++ky) {
+        const int iy = oy * sh - pt + ky * dh;
+        for (int kx = 0; kx < kw; ++kx) {
+          const int ix = ox * sw - pl + kx * dw;
+          const float xv = (iy >= 0 && iy < H && ix >= 0 && ix < W) ? __ldg(xc + static_cast<size_t>(iy) * W + ix) : 0.0f;
+#pragma unroll
+          for (int o = 0; o < OCB; ++o)
+            if (o < noc)
+              acc[o] = __fmaf_rn(__ldg(w + ((static_cast<size_t>(oc0 + o) * cpg + ic) * kh + ky) * kw + kx), xv, acc[o]);
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 0; o < OCB; ++o) {
+      if (o >= noc) continue;
+      const size_t off = (static_cast<size_t>(oc0 + o) * OH + oy) * OW + ox;
+      float v = apply_act(acc[o], act);
+      if (res) v = __fadd_rn(__ldg(res + static_cast<size_t>(n) * res_nstride + off), v);
+      y[static_cast<size_t>(n) * y_nstride + off] = v;
+    }
+  }
+}
+
+// ---------------------------------------------------------------- MaxPool
+// Ops/DnnOps.cs:1335 (MaxPoolLayer): max over the window's in-bounds elements.
+__global__ void k_maxpool(const float* __restrict__ x, long long x_nstride, int N, int C, int H, int W, int kh, int kw,
+                          int sh, int sw, int pt, int pl, float* __restrict__ y, long long y_nstride, int OH, int OW) {
+  const long long total = static_cast<long long>(N) * C * OH * OW;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    long long t = i;
+    const int ox = static_cast<int>(t % OW);
+    t /= OW;
+    const int oy = static_cast<int>(t % OH);
+    t /= OH;
+    const int c = static_cast<int>(t % C);
+    const int n = static_cast<int>(t / C);
+    const float* xc = x + static_cast<size_t>(n) * x_nstride + static_cast<size_t>(c) * H * W;
+    float m = -INFINITY;
+    for (int ky = 0; ky < kh; ++ky) {
+      const int iy = oy * sh - pt + ky;
+      if (iy < 0 || iy >= H) continue;
+      for (int kx = 0; kx < kw; ++kx) {
+        const int ix = ox * sw - pl + kx;
+        if (ix < 0 || ix >= W) continue;
+        m = maxps(__ldg(xc + static_cast<size_t>(iy) * W + ix), m);
+      }
+    }
+    y[static_cast<size_t>(n) * y_nstride + (static_cast<size_t>(c) * OH + oy) * OW + ox] = m;
+  }
+}
+
+// ---------------------------------------------------------------- Resize (nearest, integer up-scale)
+// Ops/DnnOps.cs:2215 (ResizeLayer), nearest mode with integer scales:
+// out[y][x] = in[y / sy][x / sx].
+__global__ void k_resize_nearest(const float* __restrict__ x, long long x_nstride, int N, int C, int H, int W, int sy,
+                                 int sx, float* __restrict__ y, long long y_nstride) {
+  const int OH = H * sy, OW = W * sx;
+  const long long total = static_cast<long long>(N) * C * OH * OW;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    long long t = i;
+    const int ox = static_cast<int>(t % OW);
+    t /= OW;
+    const int oy = static_cast<int>(t % OH);
+    t /= OH;
+    const int c = static_cast<int>(t % C);
+    const int n = static_cast<int>(t / C);
+    y[static_cast<size_t>(n) * y_nstride + (static_cast<size_t>(c) * OH + oy) * OW + ox] =
+        __ldg(x + static_cast<size_t>(n) * x_nstride + (static_cast<size_t>(c) * H + oy / sy) * W + ox / sx);
+  }
+}
+
+// ---------------------------------------------------------------- binary (numpy broadcasting, rank <= 4)
+// Ops/BroadcastOps.cs / Tensors/TensorOps.cs: elementwise Add/Sub/Mul/Div.
+struct Bcast {
+  int rank;
+  long long out_dims[4];
+  long long a_strides[4], b_strides[4];  // 0 on broadcast dimensions
+};
+
+__global__ void k_binary(const float* __restrict__ a, const float* __restrict__ b, float* __restrict__ y, Bcast bc,
+                         long long total, int op) {
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    long long t = i, ia = 0, ib = 0;
+    for (int d = bc.rank - 1; d >= 0; --d) {
+      const long long c = t % bc.out_dims[d];
+      t /= bc.out_dims[d];
+      ia += c * bc.a_strides[d];
+      ib += c * bc.b_strides[d];
+    }
+    const float x = __ldg(a + ia), z = __ldg(b + ib);
+    float v;
+    switch (op) {
+      case 0: v = __fadd_rn(x, z); break;
+      case 1: v = __fsub_rn(x, z); break;
+      case 2: v = __fmul_rn(x, z); break;
+      default: v = __fdiv_rn(x, z); break;
+    }
+    y[i] = v;
+  }
+}
+
+// ---------------------------------------------------------------- unary (VectorMath bulk path)
+__global__ void k_unary(const float* __restrict__ x, float* __restrict__ y, long long n, int act) {
+  const long long n4 = n / 4;
+  const bool vec = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15u) == 0;
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  const long long start = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+  if (vec) {
+    for (long long i = start; i < n4; i += stride) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(x) + i);
+      reinterpret_cast<float4*>(y)[i] =
+          make_float4(apply_act(v.x, act), apply_act(v.y, act), apply_act(v.z, act), apply_act(v.w, act));
+    }
+  }
+  for (long long i = (vec ? n4 * 4 : 0) + start; i < n; i += stride) y[i] = apply_act(x[i], act);
+}
+
+// ---------------------------------------------------------------- softmax over the last axis
+// Ops/DnnOps.cs:2547 (SoftmaxLayer, inner == 1) -> VectorMath.SoftmaxRow
+// (VectorMath.cs:282): max, exp (polynomial on 8-lane groups, MathF.Exp on the
+// tail) summed in 8 lane partials then in order, then x * (1/sum).
+// One warp per row; lane l holds the running partial of elements j with
+// j % 8 == l % 8 for the vector part, combined in the reference's order.
+__global__ void k_softmax_rows(const float* __restrict__ x, float* __restrict__ y, long long rows, int len) {
+  const int lane = threadIdx.x & 31;
+  const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
+  for (long long r = blockIdx.x * static_cast<long long>(blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps) {
+    const float* xr = x + r * len;
+    float* yr = y + r * len;
+    float mx = -INFINITY;
+    for (int j = lane; j < len; j += 32) mx = fmaxf(mx, xr[j]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const int vend = len & ~7;
+    // lane l (< 8) accumulates elements l, l+8, l+16, ... of the vector part in order.
+    float part = 0.0f;
+    if (lane < 8)
+      for (int j = lane; j < vend; j += 8) {
+        const float e = ref_exp(__fsub_rn(xr[j], mx));
+        yr[j] = e;
+        part = __fadd_rn(part, e);
+      }
+    float total = 0.0f;
+    for (int l = 0; l < 8; ++l) total = __fadd_rn(total, __shfl_sync(0xffffffffu, part, l));
+    for (int j = vend; j < len; ++j) {  // scalar tail (uniform across the warp)
+      const float e = expf(__fsub_rn(xr[j], mx));
+      if (lane == 0) yr[j] = e;
+      total = __fadd_rn(total, e);
+    }
+    __syncwarp();
+    const float inv = __fdiv_rn(1.0f, total);
+    for (int j = lane; j < len; j += 32) yr[j] = __fmul_rn(yr[j], inv);
+  }
+}
+
+// ---------------------------------------------------------------- DflSoftmax
+// Ops/DflOps.cs:167-250 (ApplyBlock): per column, max over bins, e_b = exp(x - max)
+// (polynomial for the 8-aligned columns of each 64-column block, MathF.Exp on
+// the tail), total = sum_b e_b in order, inv = 1/total, out = sum_b fma(e_b*inv, b, .)
+// (tail columns: out += (e_b*inv)*b, unfused).
+__device__ __forceinline__ float dfl_column(const float* src, long long stride, int bins, bool vector_col) {
+  float mx = -INFINITY;
+  for (int b = 0; b < bins; ++b) {
+    const float v = __ldg(src + b * stride);
+    mx = vector_col ? maxps(mx, v) : fmaxf(mx, v);
+  }
+  float e[32];
+  float total = 0.0f;
+#pragma unroll
+  for (int b = 0; b < 32; ++b) {
+    if (b >= bins) break;
+    const float sh = __fsub_rn(__ldg(src + b * stride), mx);
+    e[b] = vector_col ? ref_exp(sh) : expf(sh);
+    total = __fadd_rn(total, e[b]);
+  }
+  const float inv = __fdiv_rn(1.0f, total);
+  float acc = 0.0f;
+#pragma unroll
+  for (int b = 0; b < 32; ++b) {
+    if (b >= bins) break;
+    const float p = __fmul_rn(e[b], inv);
+    acc = vector_col ? __fmaf_rn(p, static_cast<float>(b), acc) : __fadd_rn(acc, __fmul_rn(p, static_cast<float>(b)));
+  }
+  return acc;
+}
+
+__device__ __forceinline__ bool dfl_vector_col(int j, int pixels) {
+  const int column = (j / 64) * 64;
+  const int width = min(64, pixels - column);
+  return (j - column) < (width & ~7);
+}
+
+__global__ void k_dfl(const float* __restrict__ x, int B, int sides, int bins, int pixels, float* __restrict__ out) {
+  const long long total = static_cast<long long>(B) * sides * pixels;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int j = static_cast<int>(i % pixels);
+    const long long gs = i / pixels;  // batch * sides + side
+    out[i] = dfl_column(x + gs * bins * pixels + j, pixels, bins, dfl_vector_col(j, pixels));
+  }
+}
+
+// ---------------------------------------------------------------- fused YOLO head decode
+// The Detect head tail of the YOLO11n-shaped graph (model.23, nodes 302-319):
+// per scale the box branch (64 = 4*16 DFL logits) and class branch (nc
+// logits) are read in place from the head convs' outputs; DFL as above;
+// dist2bbox exactly as the exported graph: x1y1 = anchor - lt, x2y2 =
+// anchor + rb, c = (x1y1 + x2y2) / 2, wh = x2y2 - x1y1, both * stride; classes
+// through Sigmoid (VectorMath.cs:70-74). Output [B, 4 + nc, A].
+struct YoloScales {
+  const float* box[3];   // [B, 64, h, w] views
+  const float* cls[3];   // [B, nc, h, w] views
+  long long box_nstride[3], cls_nstride[3];
+  int h[3], w[3];
+  float stride[3];
+  int nc, total_anchors;
+};
+
+__global__ void k_yolo_decode(const __grid_constant__ YoloScales s, int B, float* __restrict__ out) {
+  const int A = s.total_anchors;
+  const long long total = static_cast<long long>(B) * A;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int a = static_cast<int>(i % A);
+    const int n = static_cast<int>(i / A);
+    int sc = 0, base = 0;
+    while (sc < 2 && a >= base + s.h[sc] * s.w[sc]) {
+      base += s.h[sc] * s.w[sc];
+      ++sc;
+    }
+    const int p = a - base;
+    const int hw = s.h[sc] * s.w[sc];
+    const float ax = static_cast<float>(p % s.w[sc]) + 0.5f, ay = static_cast<float>(p / s.w[sc]) + 0.5f;
+    const float* bx = s.box[sc] + static_cast<size_t>(n) * s.box_nstride[sc] + p;
+    // The exported graph concatenates the three scales to [B, 144, A] before
+    // DflSoftmax, so the 64-column block structure runs over A, not per scale.
+    const bool vcol = dfl_vector_col(a, A);
+    float d[4];
+#pragma unroll
+    for (int side = 0; side < 4; ++side) d[side] = dfl_column(bx + static_cast<size_t>(side) * 16 * hw, hw, 16, vcol);
+    const float x1 = __fsub_rn(ax, d[0]), y1 = __fsub_rn(ay, d[1]);
+    const float x2 = __fadd_rn(ax, d[2]), y2 = __fadd_rn(ay, d[3]);
+    const float cx = __fdiv_rn(__fadd_rn(x1, x2), 2.0f), cy = __fdiv_rn(__fadd_rn(y1, y2), 2.0f);
+    const float bw = __fsub_rn(x2, x1), bh = __fsub_rn(y2, y1);
+    float* o = out + static_cast<size_t>(n) * (4 + s.nc) * A + a;
+    const float st = s.stride[sc];
+    o[0] = __fmul_rn(cx, st);
+    o[static_cast<size_t>(A)] = __fmul_rn(cy, st);
+    o[2 * static_cast<size_t>(A)] = __fmul_rn(bw, st);
+    o[3 * static_cast<size_t>(A)] = __fmul_rn(bh, st);
+    const float* cl = s.cls[sc] + static_cast<size_t>(n) * s.cls_nstride[sc] + p;
+    for (int c = 0; c < s.nc; ++c)
+      o[static_cast<size_t>(4 + c) * A] = ref_sigmoid(__ldg(cl + static_cast<size_t>(c) * hw));
+  }
+}
+
+// ---------------------------------------------------------------- LayerNorm
+// Ops/AttnOps.cs:199-358: sums of x and x^2 in 16 float lanes (AVX-512 path),
+// lanes combined in double in order, tail in double; mean/var in double;
+// y = ((x - mean) * inv_std) * gamma + beta. One warp per row; lanes 0..15
+// own the 16 float lanes.
+__global__ void k_layernorm(const float* __restrict__ x, int outer, int inner, const float* __restrict__ gamma,
+                            const float* __restrict__ beta, float eps, float* __restrict__ y) {
+  const int lane = threadIdx.x & 31;
+  const int warps = gridDim.x * (blockDim.x >> 5);
+  for (int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < outer; r += warps) {
+    const float* xr = x + static_cast<size_t>(r) * inner;
+    float* yr = y + static_cast<size_t>(r) * inner;
+    const int vend = inner >= 16 ? (inner / 16) * 16 : 0;
+    float s = 0.0f, q = 0.0f;
+    if (lane < 16)
+      for (int i = lane; i < vend; i += 16) {
+        const float v = xr[i];
+        s = __fadd_rn(s, v);
+        q = __fadd_rn(q, __fmul_rn(v, v));
+      }
+    double sum = 0.0, sumsq = 0.0;
+    for (int l = 0; l < 16; ++l) {
+      sum += static_cast<double>(__shfl_sync(0xffffffffu, s, l));
+      sumsq += static_cast<double>(__shfl_sync(0xffffffffu, q, l));
+    }
+    for (int i = vend; i < inner; ++i) {
+      const float v = xr[i];
+      sum += v;
+      sumsq += static_cast<double>(v) * v;
+    }
+    const double mean_d = sum / inner;
+    double var_d = sumsq / inner - mean_d * mean_d;
+    if (var_d < 0) var_d = 0;
+    const float mean = static_cast<float>(mean_d);
+    const float inv_std = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(static_cast<float>(var_d), eps)));
+    for (int j = lane; j < inner; j += 32) {
+      float v = __fmul_rn(__fsub_rn(xr[j], mean), inv_std);
+      if (gamma) v = __fmul_rn(v, __ldg(gamma + j));
+      if (beta) v = __fadd_rn(v, __ldg(beta + j));
+      yr[j] = v;
+    }
+  }
+}
+
+// ---------------------------------------------------------------- C2PSA attention (T = H*W)
+// The attention of YOLO11's PSA block (model.10.m.0.attn, exported as
+// Reshape/Split/Transpose/MatMul/Mul/Softmax/MatMul, shapes in the reference's
+// tests/data/yolo11n.shapes.tsv nodes 123-134): from qkv [B, heads*(2*kd+hd), T]
+// per head q [kd][T], k [kd][T], v [hd][T];
+//   S[i][j] = (sum_c q[c][i] * k[c][j]) * scale   (MatMul FMA chain, then Mul)
+//   P = SoftmaxRow(S)                            (VectorMath.SoftmaxRow)
+//   out[d][i] = sum_j v[d][j] * P[i][j]           (MatMul FMA chain over j)
+// One CTA per (b, head, block of 16 query rows); S rows live in shared memory.
+constexpr int kPsaRows = 16;
+
+__global__ void k_psa_attention(const float* __restrict__ qkv, long long qkv_nstride, int heads, int kd, int hd,
+                                int T, float scale, float* __restrict__ out, long long out_nstride) {
+  extern __shared__ float sm[];
+  float* S = sm;                         // [kPsaRows][T]
+  float* qs = sm + kPsaRows * T;         // [kd][kPsaRows]
+  const int bh = blockIdx.y;
+  const int b = bh / heads, h = bh % heads;
+  const int i0 = blockIdx.x * kPsaRows;
+  const int rows = min(kPsaRows, T - i0);
+  const int per_head = 2 * kd + hd;
+  const float* base = qkv + static_cast<size_t>(b) * qkv_nstride + static_cast<size_t>(h) * per_head * T;
+  const float* q = base;
+  const float* k = base + static_cast<size_t>(kd) * T;
+  const float* v = base + static_cast<size_t>(2 * kd) * T;
+  for (int idx = threadIdx.x; idx < kd * kPsaRows; idx += blockDim.x) {
+    const int c = idx / kPsaRows, r = idx % kPsaRows;
+    qs[idx] = r < rows ? __ldg(q + static_cast<size_t>(c) * T + i0 + r) : 0.0f;
+  }
+  __syncthreads();
+  // S = (q^T k) * scale
+  for (int idx = threadIdx.x; idx < kPsaRows * T; idx += blockDim.x) {
+    const int r = idx / T, j = idx % T;
+    float acc = 0.0f;
+    for (int c = 0; c < kd; ++c) acc = __fmaf_rn(qs[c * kPsaRows + r], __ldg(k + static_cast<size_t>(c) * T + j), acc);
+    S[idx] = __fmul_rn(acc, scale);
+  }
+  __syncthreads();
+  // softmax rows: one warp per row (same reduction order as k_softmax_rows)
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+  for (int r = warp; r < rows; r += nwarps) {
+    float* sr = S + r * T;
+    float mx = -INFINITY;
+    for (int j = lane; j < T; j += 32) mx = fmaxf(mx, sr[j]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const int vend = T & ~7;
+    float part = 0.0f;
+    if (lane < 8)
+      for (int j = lane; j < vend; j += 8) {
+        const float e = ref_exp(__fsub_rn(sr[j], mx));
+        sr[j] = e;
+        part = __fadd_rn(part, e);
+      }
+    float total = 0.0f;
+    for (int l = 0; l < 8; ++l) total = __fadd_rn(total, __shfl_sync(0xffffffffu, part, l));
+    __syncwarp();
+    for (int j = vend; j < T; ++j) {
+      const float e = expf(__fsub_rn(sr[j], mx));
+      total = __fadd_rn(total, e);
+      __syncwarp();
+      if (lane == 0) sr[j] = e;
+      __syncwarp();
+    }
+    const float inv = __fdiv_rn(1.0f, total);
+    __syncwarp();
+    for (int j = lane; j < T; j += 32) sr[j] = __fmul_rn(sr[j], inv);
+  }
+  __syncthreads();
+  // out[h*hd + d][i0 + r] = sum_j v[d][j] * P[r][j]
+  float* ob = out + static_cast<size_t>(b) * out_nstride + static_cast<size_t>(h) * hd * T;
+  for (int idx = threadIdx.x; idx < hd * rows; idx += blockDim.x) {
+    const int d = idx / rows, r = idx % rows;
+    const float* vd = v + static_cast<size_t>(d) * T;
+    const float* pr = S + r * T;
+    float acc = 0.0f;
+    for (int j = 0; j < T; ++j) acc = __fmaf_rn(__ldg(vd + j), pr[j], acc);
+    ob[static_cast<size_t>(d) * T + i0 + r] = acc;
+  }
+}
+
+}  // namespace
+}  // namespace osc
+
+using namespace osc;
+
+extern "C" {
+
+OSC_API int osc_conv2d_direct_f32(osc_ctx* ctx, const float* x, long long x_nstride, int N, int C, int H, int W,
+                                  const float* w, int M, int kh, int kw, int stride_h, int stride_w, int pad_t,
+                                  int pad_l, int pad_b, int pad_r, int dil_h, int dil_w, int group, const float* bias,
+                                  int act, const float* residual, long long res_nstride, float* y, long long y_nstride,
+                                  int OH, int OW) {
+  OSC_TRY(enter(ctx));
+  if (group <= 0 || C % group || M % group) return fail(OSC_EINVAL, "osc_conv2d_direct_f32: group=%d", group);
+  if (N < 0 || C <= 0 || H <= 0 || W <= 0 || M <= 0 || kh <= 0 || kw <= 0 || stride_h <= 0 || stride_w <= 0 ||
+      dil_h <= 0 || dil_w <= 0 || pad_t < 0 || pad_l < 0 || pad_b < 0 || pad_r < 0)
+    return fail(OSC_EINVAL, "osc_conv2d_direct_f32: bad geometry");
+  const int oh = (H + pad_t + pad_b - ((kh - 1) * dil_h + 1)) / stride_h + 1;
+  const int ow = (W + pad_l + pad_r - ((kw - 1) * dil_w + 1)) / stride_w + 1;
+  if (oh != OH || ow != OW || oh <= 0 || ow <= 0)
+    return fail(OSC_EINVAL, "osc_conv2d_direct_f32: output must be %dx%d, got %dx%d", oh, ow, OH, OW);
+  if (act < OSC_ACT_NONE || act > OSC_ACT_SIGMOID) return fail(OSC_EINVAL, "osc_conv2d_direct_f32: act=%d", act);
+  if (x_nstride == 0) x_nstride = static_cast<long long>(C) * H * W;
+  if (y_nstride == 0) y_nstride = static_cast<long long>(M) * OH * OW;
+  if (res_nstride == 0) res_nstride = static_cast<long long>(M) * OH * OW;
+  if (N == 0) return OSC_OK;
+  if (x == nullptr || w == nullptr || y == nullptr) return fail(OSC_EINVAL, "osc_conv2d_direct_f32: null pointer");
+  if (fault_injected("launch")) return fail(OSC_EFAULT_INJECTED, "injected failure (launch)");
+  const int mpg = M / group;
+  prof_begin(ctx);
+  if (mpg >= 8) {
+    const long long work = static_cast<long long>(N) * group * ((mpg + 15) / 16) * OH * OW;
+    k_conv_direct<16><<<blocks_for(ctx, work), 256, 0, ctx->stream>>>(x, x_nstride, N, C, H, W, w, M, kh, kw, stride_h,
+                                                                       stride_w, pad_t, pad_l, dil_h, dil_w, group, bias,
+                                                                       act, residual, res_nstride, y, y_nstride, OH, OW);
+  } else {
+    const long long work = static_cast<long long>(N) * group * mpg * OH * OW;
+    k_conv_direct<1><<<blocks_for(ctx, work), 256, 0, ctx->stream>>>(x, x_nstride, N, C, H, W, w, M, kh, kw, stride_h,
+                                                                      stride_w, pad_t, pad_l, dil_h, dil_w, group, bias,
+                                                                      act, residual, res_nstride, y, y_nstride, OH, OW);
+  }
+  return check_launch(ctx, "k_conv_direct");
+}
+
+OSC_API int osc_maxpool2d_f32(osc_ctx* ctx, const float* x, long long x_nstride, int N, int C, int H, int W, int kh,
+                              int kw, int stride_h, int stride_w, int pad_t, int pad_l, int pad_b, int pad_r, float* y,
+                              long long y_nstride, int OH, int OW) {
+  OSC_TRY(enter(ctx));
+  const int oh = (H + pad_t + pad_b - kh) / stride_h + 1, ow = (W + pad_l + pad_r - kw) / stride_w + 1;
+  if (kh <= 0 || kw <= 0 || stride_h <= 0 || stride_w <= 0 || oh != OH || ow != OW || oh <= 0 || ow <= 0)
+    return fail(OSC_EINVAL, "osc_maxpool2d_f32: bad geometry (expected %dx%d)", oh, ow);
+  if (x_nstride == 0) x_nstride = static_cast<long long>(C) * H * W;
+  if (y_nstride == 0) y_nstride = static_cast<long long>(C) * OH * OW;
+  if (N == 0) return OSC_OK;
+  prof_begin(ctx);
+  k_maxpool<<<blocks_for(ctx, static_cast<long long>(N) * C * OH * OW), 256, 0, ctx->stream>>>(
+      x, x_nstride, N, C, H, W, kh, kw, stride_h, stride_w, pad_t, pad_l, y, y_nstride, OH, OW);
+  return check_launch(ctx, "k_maxpool");
+}
+
+OSC_API int osc_resize_nearest_f32(osc_ctx* ctx, const float* x, long long x_nstride, int N, int C, int H, int W,
+                                   int scale_h, int scale_w, float* y, long long y_nstride) {
+  OSC_TRY(enter(ctx));
+  if (scale_h <= 0 || scale_w <= 0 || N < 0 || C <= 0 || H <= 0 || W <= 0)
+    return fail(OSC_EINVAL, "osc_resize_nearest_f32: bad arguments");
+  if (x_nstride == 0) x_nstride = static_cast<long long>(C) * H * W;
+  if (y_nstride == 0) y_nstride = static_cast<long long>(C) * H * scale_h * W * scale_w;
+  if (N == 0) return OSC_OK;
+  prof_begin(ctx);
+  k_resize_nearest<<<blocks_for(ctx, static_cast<long long>(N) * C * H * scale_h * W * scale_w), 256, 0,
+                     ctx->stream>>>(x, x_nstride, N, C, H, W, scale_h, scale_w, y, y_nstride);
+  return check_launch(ctx, "k_resize_nearest");
+}
+
+OSC_API int osc_binary_f32(osc_ctx* ctx, int op, const float* a, const long long* a_shape, int a_rank, const float* b,
+                           const long long* b_shape, int b_rank, float* y) {
+  OSC_TRY(enter(ctx));
+  if (op < 0 || op > 3 || a_rank < 0 || b_rank < 0 || a_rank > 4 || b_rank > 4)
+    return fail(OSC_EINVAL, "osc_binary_f32: op %d, ranks %d/%d (rank <= 4)", op, a_rank, b_rank);
+  Bcast bc{};
+  bc.rank = std::max(a_rank, b_rank);
+  if (bc.rank == 0) bc.rank = 1;
+  long long as[4], bs[4];
+  for (int d = 0; d < bc.rank; ++d) {
+    const int da = d - (bc.rank - a_rank), db = d - (bc.rank - b_rank);
+    as[d] = da >= 0 ? a_shape[da] : 1;
+    bs[d] = db >= 0 ? b_shape[db] : 1;
+    if (as[d] != bs[d] && as[d] != 1 && bs[d] != 1)
+      return fail(OSC_EINVAL, "osc_binary_f32: shapes do not broadcast at axis %d (%lld vs %lld)", d, as[d], bs[d]);
+    bc.out_dims[d] = std::max(as[d], bs[d]);
+  }
+  long long sa = 1, sb = 1, total = 1;
+  for (int d = bc.rank - 1; d >= 0; --d) {
+    bc.a_strides[d] = as[d] == 1 ? 0 : sa;
+    bc.b_strides[d] = bs[d] == 1 ? 0 : sb;
+    sa *= as[d];
+    sb *= bs[d];
+    total *= bc.out_dims[d];
+  }
+  if (total == 0) return OSC_OK;
+  if (a == nullptr || b == nullptr || y == nullptr) return fail(OSC_EINVAL, "osc_binary_f32: null pointer");
+  prof_begin(ctx);
+  k_binary<<<blocks_for(ctx, total), 256, 0, ctx->stream>>>(a, b, y, bc, total, op);
+  return check_launch(ctx, "k_binary");
+}
+
+OSC_API int osc_unary_f32(osc_ctx* ctx, const float* x, float* y, long long n, int act) {
+  OSC_TRY(enter(ctx));
+  if (act < OSC_ACT_NONE || act > OSC_ACT_SIGMOID || n < 0) return fail(OSC_EINVAL, "osc_unary_f32: bad arguments");
+  if (n == 0) return OSC_OK;
+  prof_begin(ctx);
+  k_unary<<<blocks_for(ctx, n / 4 + 1), 256, 0, ctx->stream>>>(x, y, n, act);
+  return check_launch(ctx, "k_unary");
+}
+
+OSC_API int osc_softmax_f32(osc_ctx* ctx, const float* x, float* y, long long rows, int len) {
+  OSC_TRY(enter(ctx));
+  if (rows < 0 || len <= 0) return fail(OSC_EINVAL, "osc_softmax_f32: bad shape");
+  if (rows == 0) return OSC_OK;
+  prof_begin(ctx);
+  k_softmax_rows<<<blocks_for(ctx, rows * 32), 256, 0, ctx->stream>>>(x, y, rows, len);
+  return check_launch(ctx, "k_softmax_rows");
+}
+
+OSC_API int osc_dfl_f32(osc_ctx* ctx, const float* x, int B, int sides, int bins, int pixels, float* out) {
+  OSC_TRY(enter(ctx));
+  if (B < 0 || sides <= 0 || bins <= 0 || bins > 32 || pixels <= 0)
+    return fail(OSC_EINVAL, "osc_dfl_f32: bad shape (bins <= 32)");
+  if (B == 0) return OSC_OK;
+  prof_begin(ctx);
+  k_dfl<<<blocks_for(ctx, static_cast<long long>(B) * sides * pixels), 256, 0, ctx->stream>>>(x, B, sides, bins,
+                                                                                               pixels, out);
+  return check_launch(ctx, "k_dfl");
+}
+
+OSC_API int osc_yolo_decode_f32(osc_ctx* ctx, int B, int nc, const float* const* box, const long long* box_nstride,
+                                const float* const* cls, const long long* cls_nstride, const int* hs, const int* ws,
+                                const float* strides, float* out) {
+  OSC_TRY(enter(ctx));
+  if (B < 0 || nc <= 0 || box == nullptr || cls == nullptr || hs == nullptr || ws == nullptr || strides == nullptr)
+    return fail(OSC_EINVAL, "osc_yolo_decode_f32: bad arguments");
+  YoloScales s{};
+  s.nc = nc;
+  s.total_anchors = 0;
+  for (int i = 0; i < 3; ++i) {
+    s.box[i] = box[i];
+    s.cls[i] = cls[i];
+    s.h[i] = hs[i];
+    s.w[i] = ws[i];
+    s.stride[i] = strides[i];
+    s.box_nstride[i] = box_nstride[i] ? box_nstride[i] : 64LL * hs[i] * ws[i];
+    s.cls_nstride[i] = cls_nstride[i] ? cls_nstride[i] : static_cast<long long>(nc) * hs[i] * ws[i];
+    s.total_anchors += hs[i] * ws[i];
+  }
+  if (B == 0) return OSC_OK;
+  prof_begin(ctx);
+  k_yolo_decode<<<blocks_for(ctx, static_cast<long long>(B) * s.total_anchors), 256, 0, ctx->stream>>>(s, B, out);
+  return check_launch(ctx, "k_yolo_decode");
+}
+
+OSC_API int osc_layernorm_f32(osc_ctx* ctx, const float* x, int outer, int inner, const float* gamma,
+                              const float* beta, float eps, float* y) {
+  OSC_TRY(enter(ctx));
+  if (outer < 0 || inner <= 0) return fail(OSC_EINVAL, "osc_layernorm_f32: bad shape");
+  if (outer == 0) return OSC_OK;
+  prof_begin(ctx);
+  k_layernorm<<<blocks_for(ctx, static_cast<long long>(outer) * 32), 256, 0, ctx->stream>>>(x, outer, inner, gamma,
+                                                                                             beta, eps, y);
+  return check_launch(ctx, "k_layernorm");
+}
+
+OSC_API int osc_psa_attention_f32(osc_ctx* ctx, const float* qkv, long long qkv_nstride, int B, int heads, int kd,
+                                  int hd, int T, float scale, float* out, long long out_nstride) {
+  OSC_TRY(enter(ctx));
+  if (B < 0 || heads <= 0 || kd <= 0 || hd <= 0 || T <= 0) return fail(OSC_EINVAL, "osc_psa_attention_f32: bad shape");
+  const size_t smem = (static_cast<size_t>(kPsaRows) * T + static_cast<size_t>(kd) * kPsaRows) * sizeof(float);
+  if (smem > 200 * 1024) return fail(OSC_EUNSUPPORTED, "osc_psa_attention_f32: T=%d too long", T);
+  if (qkv_nstride == 0) qkv_nstride = static_cast<long long>(heads) * (2 * kd + hd) * T;
+  if (out_nstride == 0) out_nstride = static_cast<long long>(heads) * hd * T;
+  if (B == 0) return OSC_OK;
+  OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(k_psa_attention), static_cast<int>(smem)));
+  dim3 grid((T + kPsaRows - 1) / kPsaRows, B * heads);
+  prof_begin(ctx);
+  k_psa_attention<<<grid, 256, smem, ctx->stream>>>(qkv, qkv_nstride, heads, kd, hd, T, scale, out, out_nstride);
+  return check_launch(ctx, "k_psa_attention");
+}
+
+}  // extern "C"

@@ -253,6 +253,56 @@ OSC_API int osc_profile_reset(osc_ctx* ctx) {
 
 OSC_API unsigned long long osc_launch_count(osc_ctx* ctx) { return ctx ? ctx->launches : 0ull; }
 
+// ---- static-plan capture: the executor's "one CUDA graph per input
+// signature" (the reference caches a plan per input signature, LayerPlan.cs:32-94).
+struct osc_graph {
+  int device;
+  cudaGraph_t graph;
+  cudaGraphExec_t exec;
+};
+
+OSC_API int osc_graph_begin(osc_ctx* ctx) {
+  OSC_TRY(enter(ctx));
+  if (ctx->stream == nullptr) return fail(OSC_EINVAL, "osc_graph_begin: cannot capture the legacy default stream");
+  if (capturing(ctx)) return fail(OSC_EINVAL, "osc_graph_begin: already capturing");
+  ctx->prof_on = false;  // event records are not captured
+  OSC_CUDA(cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal), "cudaStreamBeginCapture");
+  return OSC_OK;
+}
+
+OSC_API int osc_graph_end(osc_ctx* ctx, osc_graph** out) {
+  if (out == nullptr) return fail(OSC_EINVAL, "osc_graph_end: out is null");
+  *out = nullptr;
+  OSC_TRY(enter(ctx));
+  cudaGraph_t g = nullptr;
+  OSC_CUDA(cudaStreamEndCapture(ctx->stream, &g), "cudaStreamEndCapture");
+  cudaGraphExec_t ex = nullptr;
+  const cudaError_t e = cudaGraphInstantiate(&ex, g, 0);
+  if (e != cudaSuccess) {
+    cudaGraphDestroy(g);
+    return cuda_fail(e, "cudaGraphInstantiate");
+  }
+  *out = new osc_graph{ctx->device, g, ex};
+  return OSC_OK;
+}
+
+OSC_API int osc_graph_launch(osc_ctx* ctx, const osc_graph* graph) {
+  OSC_TRY(enter(ctx));
+  if (graph == nullptr || graph->device != ctx->device) return fail(OSC_EINVAL, "osc_graph_launch: bad graph");
+  if (fault_injected("launch")) return fail(OSC_EFAULT_INJECTED, "injected failure (launch)");
+  OSC_CUDA(cudaGraphLaunch(graph->exec, ctx->stream), "cudaGraphLaunch");
+  return OSC_OK;
+}
+
+OSC_API int osc_graph_free(osc_graph* graph) {
+  if (graph == nullptr) return OSC_OK;
+  cudaSetDevice(graph->device);
+  cudaGraphExecDestroy(graph->exec);
+  cudaGraphDestroy(graph->graph);
+  delete graph;
+  return OSC_OK;
+}
+
 OSC_API int osc_destroy(osc_ctx* ctx) {
   if (ctx == nullptr) return OSC_OK;
   cudaSetDevice(ctx->device);

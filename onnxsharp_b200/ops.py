@@ -1,0 +1,116 @@
+"""Python wrappers of the graph-glue entry points of libonnxsharp_cuda.
+
+Tensors are torch CUDA tensors in NCHW. A 4-D argument may be a channel
+slice of a larger buffer (``buf[:, c0:c1]``): its ``data_ptr()`` points at the
+first channel of image 0 and ``stride(0)`` is the image stride the C ABI takes
+as ``*_nstride``; the inner three dimensions must be dense.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+from . import _lib
+from ._lib import call, ptr
+
+OP_ADD, OP_SUB, OP_MUL, OP_DIV = 0, 1, 2, 3
+
+
+def _nchw(t):
+    n, c, h, w = t.shape
+    if t.stride(3) != 1 or t.stride(2) != w or t.stride(1) != h * w:
+        raise ValueError("inner dimensions of an NCHW view must be dense")
+    return n, c, h, w, t.stride(0)
+
+
+def out_size(size: int, k: int, s: int, p0: int, p1: int, d: int = 1) -> int:
+    return (size + p0 + p1 - ((k - 1) * d + 1)) // s + 1
+
+
+def conv2d_ex(ctx, x, w, bias, y, stride=1, pad=0, dil=1, act=_lib.ACT_NONE, residual=None):
+    """y = residual + act(conv(x, W) + bias) on the tensor cores (group 1; W is a runtime.ConvWeights)."""
+    n, c, h, wd, xs = _nchw(x)
+    _, m, oh, ow, ys = _nchw(y)
+    rs = 0 if residual is None else _nchw(residual)[4]
+    call("osc_conv2d_ex_f32", ctx.handle, ptr(x), xs, n, c, h, wd, w.handle, stride, stride, pad, pad, pad, pad, dil,
+         dil, ptr(bias), int(act), ptr(residual), rs, ptr(y), ys, oh, ow)
+    return y
+
+
+def conv2d_direct(ctx, x, w, bias, y, stride=1, pad=0, dil=1, group=1, act=_lib.ACT_NONE, residual=None):
+    """Direct conv on CUDA cores (depthwise / first layer); w is the raw [M, C/g, kh, kw] device tensor."""
+    n, c, h, wd, xs = _nchw(x)
+    _, m, oh, ow, ys = _nchw(y)
+    rs = 0 if residual is None else _nchw(residual)[4]
+    kh, kw = int(w.shape[2]), int(w.shape[3])
+    call("osc_conv2d_direct_f32", ctx.handle, ptr(x), xs, n, c, h, wd, ptr(w), m, kh, kw, stride, stride, pad, pad,
+         pad, pad, dil, dil, group, ptr(bias), int(act), ptr(residual), rs, ptr(y), ys, oh, ow)
+    return y
+
+
+def maxpool2d(ctx, x, y, k, stride, pad):
+    n, c, h, w, xs = _nchw(x)
+    _, _, oh, ow, ys = _nchw(y)
+    call("osc_maxpool2d_f32", ctx.handle, ptr(x), xs, n, c, h, w, k, k, stride, stride, pad, pad, pad, pad, ptr(y), ys,
+         oh, ow)
+    return y
+
+
+def resize_nearest(ctx, x, y, scale=2):
+    n, c, h, w, xs = _nchw(x)
+    ys = _nchw(y)[4]
+    call("osc_resize_nearest_f32", ctx.handle, ptr(x), xs, n, c, h, w, scale, scale, ptr(y), ys)
+    return y
+
+
+def binary(ctx, op, a, b, y):
+    """y = a (op) b with numpy broadcasting (dense tensors, rank <= 4)."""
+    ash = (C.c_longlong * max(1, a.dim()))(*a.shape)
+    bsh = (C.c_longlong * max(1, b.dim()))(*b.shape)
+    call("osc_binary_f32", ctx.handle, int(op), ptr(a), ash, a.dim(), ptr(b), bsh, b.dim(), ptr(y))
+    return y
+
+
+def unary(ctx, x, y, act):
+    call("osc_unary_f32", ctx.handle, ptr(x), ptr(y), x.numel(), int(act))
+    return y
+
+
+def softmax(ctx, x, y):
+    """Softmax over the last axis."""
+    call("osc_softmax_f32", ctx.handle, ptr(x), ptr(y), x.numel() // x.shape[-1], int(x.shape[-1]))
+    return y
+
+
+def dfl(ctx, x, out, bins=16):
+    b, cb, n = x.shape
+    call("osc_dfl_f32", ctx.handle, ptr(x), b, cb // bins, bins, n, ptr(out))
+    return out
+
+
+def layernorm(ctx, x, gamma, beta, eps, y, inner=None):
+    inner = int(inner or x.shape[-1])
+    call("osc_layernorm_f32", ctx.handle, ptr(x), x.numel() // inner, inner, ptr(gamma), ptr(beta), float(eps), ptr(y))
+    return y
+
+
+def psa_attention(ctx, qkv, out, heads, kd, hd, scale):
+    """qkv [B, heads*(2kd+hd), H, W] (view) -> out [B, heads*hd, H, W] (view)."""
+    n, _, h, w, qs = _nchw(qkv)
+    os_ = _nchw(out)[4]
+    call("osc_psa_attention_f32", ctx.handle, ptr(qkv), qs, n, heads, kd, hd, h * w, float(scale), ptr(out), os_)
+    return out
+
+
+def yolo_decode(ctx, boxes, classes, strides, out):
+    """boxes[i] [B, 64, h, w], classes[i] [B, nc, h, w] (views) -> out [B, 4+nc, A]."""
+    B = int(boxes[0].shape[0])
+    nc = int(classes[0].shape[1])
+    bp = (C.c_void_p * 3)(*[ptr(t) for t in boxes])
+    cp = (C.c_void_p * 3)(*[ptr(t) for t in classes])
+    bs = (C.c_longlong * 3)(*[t.stride(0) for t in boxes])
+    cs = (C.c_longlong * 3)(*[t.stride(0) for t in classes])
+    hs = (C.c_int * 3)(*[int(t.shape[2]) for t in boxes])
+    ws = (C.c_int * 3)(*[int(t.shape[3]) for t in boxes])
+    st = (C.c_float * 3)(*[float(s) for s in strides])
+    call("osc_yolo_decode_f32", ctx.handle, B, nc, bp, bs, cp, cs, hs, ws, st, ptr(out))
+    return out

@@ -31,6 +31,9 @@ class Context:
     def set_stream(self, stream: int | None) -> None:
         call("osc_set_stream", self.handle, stream)
 
+    def get_stream(self) -> int | None:
+        return _lib.load().osc_get_stream(self.handle)
+
     def use_torch_stream(self) -> None:
         import torch
 

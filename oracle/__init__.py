@@ -39,6 +39,7 @@ _SIGS = {
                           _int, _vp, _int, _vp, _int, _int, _int]),
     "orc_attention": (None, [_vp, _vp, _vp, _vp, _int, _int, _int, _int, _int, _flt, _int, _int, _int, _vp, _int]),
     "orc_dfl": (None, [_vp, _int, _int, _int, _int, _vp, _int]),
+    "orc_softmax_rows": (None, [_vp, _vp, _long, _int, _int]),
     "orc_layernorm": (None, [_vp, _int, _int, _vp, _vp, _flt, _vp, _int]),
 }
 
@@ -182,6 +183,14 @@ def attention(q, k, v, heads: int, scale: float, mask=None, out_head_space: int 
     lib().orc_attention(_p(q), _p(k), _p(v), _p(m), mask_rows, B, T, H, D, scale, heads_form, out_head_space,
                         block_min_seq, _p(out), threads)
     return out
+
+
+def softmax(x, threads: int = THREADS):
+    """Softmax over the last axis (VectorMath.SoftmaxRow per row)."""
+    x = _c(x)
+    y = np.empty_like(x)
+    lib().orc_softmax_rows(_p(x), _p(y), x.size // x.shape[-1], x.shape[-1], threads)
+    return y
 
 
 def dfl(x, bins: int = 16, threads: int = THREADS):

@@ -289,6 +289,19 @@ static float sum_exp(const float* src, float* dst, int n, float bias) {
   return total;
 }
 
+/* VectorMath.SoftmaxRow (VectorMath.cs:282): MaxRow, SumExp, Scale by 1/sum. */
+void orc_softmax_rows(const float* x, float* y, long rows, int len, int threads) {
+#pragma omp parallel for num_threads(nthreads(threads)) schedule(static)
+  for (long r = 0; r < rows; ++r) {
+    const float* s = x + (size_t)r * len;
+    float* d = y + (size_t)r * len;
+    const float mx = max_row(s, len);
+    const float total = sum_exp(s, d, len, mx);
+    const float inv = 1.0f / total;
+    for (int j = 0; j < len; ++j) d[j] = d[j] * inv;
+  }
+}
+
 /* AttentionOps.Dot (:692-711): 8-lane FMA partials, horizontal sum, unfused tail. */
 static float dot8(const float* a, const float* b, int n) {
   int i = 0;

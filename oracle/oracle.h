@@ -81,6 +81,9 @@ void orc_attention(const float* q, const float* k, const float* v, const float* 
                    int H, int D, float scale, int heads_form, int out_head_space, int block_min_seq, float* out,
                    int threads);
 
+/* SoftmaxLayer over the last axis (Ops/DnnOps.cs:2547) -> VectorMath.SoftmaxRow per row. */
+void orc_softmax_rows(const float* x, float* y, long rows, int len, int threads);
+
 /* DflLayer.ApplyBlock (Ops/DflOps.cs:167-250): x [B, sides*bins, pixels] ->
  * out [B, sides, pixels] = sum_b b * softmax_b. */
 void orc_dfl(const float* x, int B, int sides, int bins, int pixels, float* out, int threads);

@@ -1,0 +1,174 @@
+"""Glue operators on the B200 against the oracle / exact numpy: direct conv
+(first layer, depthwise), conv views + fused residual, MaxPool, nearest
+Resize, broadcasting binary ops, unary activations, Softmax, DflSoftmax,
+LayerNorm, the PSA attention and the fused YOLO decode."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import oracle
+from conftest import rel_err
+
+pytestmark = pytest.mark.gpu
+
+
+def T(a):
+    import torch
+
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+@pytest.mark.parametrize("C,M,k,s,group", [(3, 16, 3, 2, 1), (64, 64, 3, 1, 64), (80, 80, 3, 1, 80), (8, 16, 5, 2, 2)])
+def test_conv_direct(ctx, C, M, k, s, group):
+    import torch
+
+    from onnxsharp_b200 import ops
+
+    rng = np.random.default_rng(C + M + k)
+    x = rng.uniform(0, 1, (2, C, 33, 30)).astype(np.float32)
+    w = (rng.normal(0, 1, (M, C // group, k, k)) * np.sqrt(2 / (C // group * k * k))).astype(np.float32)
+    b = rng.normal(0, 0.01, M).astype(np.float32)
+    p = k // 2
+    oh, ow = ops.out_size(33, k, s, p, p), ops.out_size(30, k, s, p, p)
+    y = torch.empty(2, M, oh, ow, device="cuda")
+    ops.conv2d_direct(ctx, T(x), T(w), T(b), y, s, p, 1, group, 1)
+    ctx.synchronize()
+    ref = oracle.conv2d(x, w, b, (s, s), (p, p, p, p), (1, 1), group, 1)
+    assert rel_err(y.cpu().numpy(), ref) <= 1e-5
+
+
+def test_conv_ex_views_and_residual(ctx):
+    """Input and output are channel slices of larger buffers; y = res + SiLU(conv(x) + b)."""
+    import torch
+
+    from onnxsharp_b200 import ops
+    from onnxsharp_b200.runtime import ConvWeights
+
+    rng = np.random.default_rng(3)
+    big_x = rng.uniform(0, 1, (2, 96, 20, 24)).astype(np.float32)
+    w = (rng.normal(0, 0.1, (32, 48, 3, 3))).astype(np.float32)
+    b = rng.normal(0, 0.01, 32).astype(np.float32)
+    res = rng.normal(0, 1, (2, 32, 20, 24)).astype(np.float32)
+    out_big = torch.zeros(2, 80, 20, 24, device="cuda")
+    dx = T(big_x)
+    ops.conv2d_ex(ctx, dx[:, 40:88], ConvWeights(ctx, T(w), w.shape), T(b), out_big[:, 16:48], 1, 1, 1, 1,
+                  T(res))
+    ctx.synchronize()
+    ref = res + oracle.conv2d(np.ascontiguousarray(big_x[:, 40:88]), w, b, pads=(1, 1, 1, 1), act=1)
+    got = out_big.cpu().numpy()
+    assert rel_err(got[:, 16:48], ref) <= 1e-4
+    assert not got[:, :16].any() and not got[:, 48:].any()  # nothing outside the slice
+
+
+def test_maxpool_and_resize(ctx):
+    import torch
+
+    from onnxsharp_b200 import ops
+    from oracle import yolo_ref
+
+    rng = np.random.default_rng(4)
+    x = rng.normal(0, 1, (2, 16, 20, 20)).astype(np.float32)
+    y = torch.empty(2, 16, 20, 20, device="cuda")
+    ops.maxpool2d(ctx, T(x), y, 5, 1, 2)
+    z = torch.empty(2, 16, 40, 40, device="cuda")
+    ops.resize_nearest(ctx, T(x), z, 2)
+    ctx.synchronize()
+    assert np.array_equal(y.cpu().numpy(), yolo_ref._maxpool(x, 5, 1, 2))
+    assert np.array_equal(z.cpu().numpy(), np.repeat(np.repeat(x, 2, 2), 2, 3))
+
+
+@pytest.mark.parametrize("op,fn", [(0, np.add), (1, np.subtract), (2, np.multiply), (3, np.divide)])
+def test_binary_broadcast(ctx, op, fn):
+    import torch
+
+    from onnxsharp_b200 import ops
+
+    rng = np.random.default_rng(op)
+    a = rng.normal(0, 1, (2, 3, 4, 5)).astype(np.float32)
+    b = rng.uniform(0.5, 2, (3, 1, 5)).astype(np.float32)
+    y = torch.empty(2, 3, 4, 5, device="cuda")
+    ops.binary(ctx, op, T(a), T(b), y)
+    ctx.synchronize()
+    assert np.array_equal(y.cpu().numpy(), fn(a, b).astype(np.float32))
+
+
+@pytest.mark.parametrize("act", [1, 2, 3])
+def test_unary_bit_exact(ctx, act):
+    import torch
+
+    from onnxsharp_b200 import ops
+
+    x = np.linspace(-30, 30, 10007, dtype=np.float32)
+    y = torch.empty(10007, device="cuda")
+    ops.unary(ctx, T(x), y, act)
+    ctx.synchronize()
+    assert np.array_equal(y.cpu().numpy(), oracle.unary(x, act))  # VectorMath restated bit-for-bit
+
+
+@pytest.mark.parametrize("len_", [400, 16, 13, 1])
+def test_softmax_rows(ctx, len_):
+    import torch
+
+    from onnxsharp_b200 import ops
+
+    x = np.random.default_rng(len_).normal(0, 3, (37, len_)).astype(np.float32)
+    y = torch.empty(37, len_, device="cuda")
+    ops.softmax(ctx, T(x), y)
+    ctx.synchronize()
+    assert np.max(np.abs(y.cpu().numpy() - oracle.softmax(x))) <= 1e-7
+
+
+def test_dfl(ctx, golden):
+    import torch
+
+    from onnxsharp_b200 import ops
+
+    x = golden["dfl_x"]
+    y = torch.empty(x.shape[0], 4, x.shape[2], device="cuda")
+    ops.dfl(ctx, T(x), y)
+    ctx.synchronize()
+    assert np.max(np.abs(y.cpu().numpy() - golden["dfl_y"])) <= 1e-6
+
+
+def test_layernorm(ctx, golden):
+    import torch
+
+    from onnxsharp_b200 import ops
+
+    y = torch.empty(golden["ln_x"].shape, device="cuda")
+    ops.layernorm(ctx, T(golden["ln_x"]), T(golden["ln_g"]), T(golden["ln_b"]), 1e-5, y)
+    ctx.synchronize()
+    assert np.max(np.abs(y.cpu().numpy() - golden["ln_y"])) <= 1e-6
+
+
+def test_psa_attention(ctx):
+    import torch
+
+    from onnxsharp_b200 import ops
+    from oracle import yolo_ref
+
+    qkv = np.random.default_rng(9).normal(0, 1, (2, 256, 20, 20)).astype(np.float32)
+    out = torch.empty(2, 128, 20, 20, device="cuda")
+    ops.psa_attention(ctx, T(qkv), out, 2, 32, 64, 32 ** -0.5)
+    ctx.synchronize()
+    ref = yolo_ref._psa(qkv, 2, 32, 64, 32 ** -0.5, 0)
+    assert rel_err(out.cpu().numpy(), ref) <= 1e-5
+
+
+def test_yolo_decode(ctx):
+    import torch
+
+    from onnxsharp_b200 import ops
+    from oracle import yolo_ref
+
+    rng = np.random.default_rng(10)
+    boxes = [rng.normal(0, 2, (2, 64, n, n)).astype(np.float32) for n in (80, 40, 20)]
+    cls = [rng.normal(0, 2, (2, 80, n, n)).astype(np.float32) for n in (80, 40, 20)]
+    out = torch.empty(2, 84, 8400, device="cuda")
+    ops.yolo_decode(ctx, [T(b) for b in boxes], [T(c) for c in cls], (8, 16, 32), out)
+    ctx.synchronize()
+    ref = yolo_ref._decode(boxes, cls, (8, 16, 32), 0)
+    got = out.cpu().numpy()
+    assert np.max(np.abs(got[:, :4] - ref[:, :4])) <= 1e-4
+    assert np.array_equal(got[:, 4:], ref[:, 4:])

@@ -1,0 +1,66 @@
+"""The YOLO11n-shaped plan end to end on the B200 (CUDA graph replay) against
+the CPU oracle executing the same plan with the reference's kernels."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from conftest import rel_err
+
+pytestmark = pytest.mark.gpu
+
+
+def _run(ctx, g, params, images):
+    import torch
+
+    from onnxsharp_b200 import yolo
+
+    net = yolo.Net(ctx, g, params, images.shape[0])
+    net.input_view().copy_(torch.from_numpy(images))
+    out = net.forward(use_graph=True).clone()
+    ctx.synchronize()
+    # a second replay with new images (the graph must read the input buffer, not a copy)
+    net.input_view().copy_(torch.from_numpy(images[::-1].copy()))
+    out2 = net.forward(use_graph=True).clone()
+    ctx.synchronize()
+    net.close()
+    return out.cpu().numpy(), out2.cpu().numpy()
+
+
+
+@pytest.fixture(scope="module")
+def yolo_case():
+    from onnxsharp_b200 import yolo
+
+    g = yolo.build_yolo11n()
+    params = yolo.init_params(g, 5)
+    images = np.random.default_rng(5).uniform(0, 1, (2, 3, 640, 640)).astype(np.float32)
+    from oracle import yolo_ref
+
+    ref = yolo_ref.run(g, params, images)
+    return g, params, images, ref
+
+
+def test_yolo_end_to_end_matches_oracle(ctx, yolo_case):
+    g, params, images, ref = yolo_case
+    out, out2 = _run(ctx, g, params, images)
+    assert out.shape == ref.shape == (2, 84, 8400)
+    assert rel_err(out[:, :4], ref[:, :4]) <= 1e-4      # boxes (pixels)
+    assert np.max(np.abs(out[:, 4:] - ref[:, 4:])) <= 1e-4  # class scores
+    assert np.array_equal(out2, out[::-1])               # replay reads the new input
+
+
+def test_yolo_detections_identical_after_nms(ctx, yolo_case):
+    from oracle import yolo_ref
+
+    g, params, images, ref = yolo_case
+    out, _ = _run(ctx, g, params, images)
+    for i in range(2):
+        # Random-init class scores cluster near 0.5; a threshold in the upper tail keeps
+        # the comparison away from ties (scores within 1e-4 of each other are flagged).
+        thr = float(np.quantile(ref[i, 4:].max(0), 0.95))
+        dg = yolo_ref.detect(out[i], conf=thr)
+        dr = yolo_ref.detect(ref[i], conf=thr)
+        assert [d[0] for d in dg] == [d[0] for d in dr]
+        assert [d[6] for d in dg] == [d[6] for d in dr]
+        assert np.allclose([d[1:6] for d in dg], [d[1:6] for d in dr], rtol=1e-4, atol=1e-3)
