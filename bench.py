@@ -430,9 +430,76 @@ class YoloWorkload(Workload):
         return CpuYolo(self.g, self.params, self.images_h[:1]).cpu_sample(threads)
 
 
-WORKLOADS = {"gemm": GemmWorkload, "conv": ConvWorkload, "dqmm": DqmmWorkload, "yolo": YoloWorkload}
+ATTN_FLOPS = 4 * 2.0 * 8192 * 512 * 512 + 2 * 2.0 * 64 * 8 * 128 * 128 * 64
+
+
+class AttentionWorkload(Workload):
+    """X[64,128,512] N(0,1) -> Q/K/V projections (MatMul+bias, Xavier-uniform, zero bias)
+    -> FusedAttention (H=8, D=64, scale 1/8) -> output projection."""
+
+    name = "attention_block_b64_t128_h8_d64"
+    main_kernel = "k_gemm_tf32x3"
+
+    def __init__(self, ctx, rank: int):
+        import torch
+
+        from onnxsharp_b200.runtime import GemmWeights
+
+        rng = np.random.default_rng(5150 + rank)
+        self.B, self.T, self.C, self.H = 64, 128, 512, 8
+        x = rng.normal(0, 1, (self.B * self.T, self.C)).astype(np.float32)
+        lim = np.sqrt(6.0 / (self.C + self.C))
+        ws = [rng.uniform(-lim, lim, (self.C, self.C)).astype(np.float32) for _ in range(4)]
+        dev = torch.device("cuda", torch.cuda.current_device())
+        self.ctx = ctx
+        self.x_h = x
+        self.ws_h = ws
+        self.x = torch.from_numpy(x).to(dev)
+        self.bias = torch.zeros(self.C, device=dev)
+        self.w = [GemmWeights(ctx, torch.from_numpy(w).to(dev), self.C, self.C) for w in ws]
+        self.qkv = [torch.empty(self.B * self.T, self.C, device=dev) for _ in range(3)]
+        self.o = torch.empty(self.B, self.T, self.C, device=dev)
+        self.y = torch.empty(self.B * self.T, self.C, device=dev)
+        self.x_pin = torch.from_numpy(x).pin_memory()
+        self.y_pin = torch.empty(self.B * self.T, self.C).pin_memory()
+        self.x2 = torch.empty_like(self.x)
+        self.config = {"workload": self.name, "x": [64, 128, 512], "heads": 8, "head_dim": 64,
+                       "precision": "3xTF32 tcgen05 (projections and QK^T / PV), FP32 softmax"}
+
+    def units_per_step(self) -> float:
+        return ATTN_FLOPS
+
+    def main_kernel_units(self) -> float:
+        return 2.0 * 8192 * 512 * 512
+
+    def _run(self, x):
+        from onnxsharp_b200.runtime import attention, gemm_bias
+
+        for w, out in zip(self.w[:3], self.qkv):
+            gemm_bias(self.ctx, x, w, self.bias, out=out)
+        q, k, v = (t.view(self.B, self.T, self.C) for t in self.qkv)
+        attention(self.ctx, q, k, v, self.H, 0.125, out=self.o)
+        gemm_bias(self.ctx, self.o.view(self.B * self.T, self.C), self.w[3], self.bias, out=self.y)
+
+    def step(self):
+        self._run(self.x)
+
+    def e2e_step(self):
+        self.ctx.memcpy_htod(self.x2, self.x_pin, self.x_pin.numel() * 4)
+        self._run(self.x2)
+        self.ctx.memcpy_dtoh(self.y_pin, self.y, self.y_pin.numel() * 4)
+
+    def e2e_bytes(self):
+        return self.x_pin.numel() * 4, self.y_pin.numel() * 4
+
+    def cpu_sample(self, threads: int) -> dict:
+        return CpuAttention(self.x_h, self.ws_h).cpu_sample(threads)
+
+
+WORKLOADS = {"gemm": GemmWorkload, "conv": ConvWorkload, "dqmm": DqmmWorkload, "yolo": YoloWorkload,
+             "attention": AttentionWorkload}
 DEFAULT_WORKLOAD = "yolo"
-DEFAULT_STEPS = {"gemm": 2000, "conv": 1000, "dqmm": 2000, "yolo": 100}
+DEFAULT_STEPS = {"gemm": 2000, "conv": 1000, "dqmm": 2000, "yolo": 100, "attention": 500}
 
 
 # ----------------------------------------------------------------- timing
@@ -713,7 +780,33 @@ class CpuYolo:
                 "sample": f"1 image (of 64) per step through the plan, {dt:.2f} s"}
 
 
-CPU_WORKLOADS = {"gemm": CpuGemm, "conv": CpuConv, "dqmm": CpuDqmm, "yolo": CpuYolo}
+class CpuAttention:
+    """8 of the 64 sequences per step through the oracle (projection GEMMs + ComputeBlocks)."""
+
+    unit = "TFLOP/s"
+
+    def __init__(self, x=None, ws=None):
+        if x is None:
+            rng = np.random.default_rng(5150)
+            x = rng.normal(0, 1, (64 * 128, 512)).astype(np.float32)
+            lim = np.sqrt(6.0 / 1024)
+            ws = [rng.uniform(-lim, lim, (512, 512)).astype(np.float32) for _ in range(4)]
+        self.x, self.ws = x[:8 * 128], ws
+        self.config = {"workload": AttentionWorkload.name, "x": [64, 128, 512], "heads": 8, "head_dim": 64}
+
+    def cpu_sample(self, threads):
+        import oracle
+
+        t0 = time.perf_counter()
+        q, k, v = (oracle.gemm(self.x, w, threads=threads).reshape(8, 128, 512) for w in self.ws[:3])
+        o = oracle.attention(q, k, v, heads=8, scale=0.125, threads=threads)
+        oracle.gemm(o.reshape(8 * 128, 512), self.ws[3], threads=threads)
+        dt = time.perf_counter() - t0
+        return {"value": ATTN_FLOPS / 8 / dt / 1e12, "unit": self.unit, "cores": threads,
+                "sample": f"8 of 64 sequences per step, {dt:.2f} s"}
+
+
+CPU_WORKLOADS = {"gemm": CpuGemm, "conv": CpuConv, "dqmm": CpuDqmm, "yolo": CpuYolo, "attention": CpuAttention}
 
 
 def main() -> int:
