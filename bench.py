@@ -390,14 +390,15 @@ class YoloWorkload(Workload):
         self.out_pin = torch.empty(self.net.output.shape, dtype=torch.float32).pin_memory()
         self.flops_img = yolo.flops_per_image(self.g)
         self.tc_flops = sum(self._node_flops(n) for n in self.g.nodes
-                            if n.op == "conv" and yolo.Net._tensor_core(n)) * batch
-        self.tc_launches = sum(1 for n in self.g.nodes if n.op == "conv" and yolo.Net._tensor_core(n))
+                            if n.op == "conv" and yolo.Net.tensor_core(n)) * batch
+        self.tc_launches = sum(1 for n in self.g.nodes if n.op == "conv" and yolo.Net.tensor_core(n))
         self.net.forward(use_graph=True)  # capture
         ctx.synchronize()
         self.config = {"workload": self.name, "batch_per_gpu": batch, "input": [batch, 3, 640, 640],
                        "output": [batch, 84, 8400], "gflop_per_image": round(self.flops_img / 1e9, 3),
                        "arena_mib": round(self.net.arena_bytes / 2 ** 20, 1),
-                       "precision": "FP32 in/out; convs 3xTF32 tcgen05 implicit GEMM, glue FP32 CUDA cores",
+                       "precision": "FP32 in/out; wide convs 3xTF32 tcgen05 implicit GEMM, narrow and depthwise convs "
+                                    "FP32 CUDA-core FMA, glue FP32 CUDA cores",
                        "plan": "static plan replayed as one CUDA graph"}
 
     def _node_flops(self, n):

@@ -83,6 +83,295 @@ __global__ void k_conv_direct(const float* __restrict__ x, long long x_nstride, 
   }
 }
 
+// Direct conv with the whole weight tensor staged in shared memory (first
+// layers: few input channels, M*C*kh*kw small). One thread per output pixel
+// computes OCB output channels; same summation order as k_conv_direct.
+template <int OCB>
+__global__ void __launch_bounds__(256) k_conv_direct_smw(const float* __restrict__ x, long long x_nstride, int N,
+                                                         int C, int H, int W, const float* __restrict__ w, int M,
+                                                         int kh, int kw, int sh, int sw, int pt, int pl,
+                                                         const float* __restrict__ bias, int act,
+                                                         float* __restrict__ y, long long y_nstride, int OH, int OW) {
+  extern __shared__ float sw_[];
+  const int wn = M * C * kh * kw;
+  for (int i = threadIdx.x; i < wn; i += blockDim.x) sw_[i] = __ldg(w + i);
+  __syncthreads();
+  const int ocbs = (M + OCB - 1) / OCB;
+  const int plane = OH * OW;
+  const long long total = static_cast<long long>(N) * ocbs * plane;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int p = static_cast<int>(i % plane);
+    const long long t = i / plane;
+    const int ob = static_cast<int>(t % ocbs);
+    const int n = static_cast<int>(t / ocbs);
+    const int oy = p / OW, ox = p - oy * OW;
+    const int oc0 = ob * OCB;
+    float acc[OCB];
+#pragma unroll
+    for (int o = 0; o < OCB; ++o) acc[o] = (oc0 + o < M && bias) ? __ldg(bias + oc0 + o) : 0.0f;
+    const float* xn = x + static_cast<size_t>(n) * x_nstride;
+    for (int ic = 0; ic < C; ++ic) {
+      const float* xc = xn + static_cast<size_t>(ic) * H * W;
+      for (int ky = 0; ky < kh; ++ky) {
+        const int iy = oy * sh - pt + ky;
+        for (int kx = 0; kx < kw; ++kx) {
+          const int ix = ox * sw - pl + kx;
+          const float xv = (iy >= 0 && iy < H && ix >= 0 && ix < W) ? __ldg(xc + iy * W + ix) : 0.0f;
+          const float* wp = sw_ + ((oc0 * C + ic) * kh + ky) * kw + kx;
+#pragma unroll
+          for (int o = 0; o < OCB; ++o)
+            if (oc0 + o < M) acc[o] = __fmaf_rn(wp[o * C * kh * kw], xv, acc[o]);
+        }
+      }
+    }
+    float* yn = y + static_cast<size_t>(n) * y_nstride + p;
+#pragma unroll
+    for (int o = 0; o < OCB; ++o)
+      if (oc0 + o < M) yn[static_cast<size_t>(oc0 + o) * plane] = apply_act(acc[o], act);
+  }
+}
+
+// Depthwise conv (group == C == M), the head's and PSA's 3x3: one block per
+// (image, channel, band of TH output rows); the input band plus halo is
+// staged in shared memory, the k*k weights live in registers. Order per
+// output: acc = bias, FMA over (ky, kx) with zero taps outside the image.
+constexpr int kDwTH = 16;
+
+template <int KS>
+__global__ void __launch_bounds__(256) k_conv_depthwise(const float* __restrict__ x, long long x_nstride, int N, int C,
+                                                        int H, int W, const float* __restrict__ w, int sh, int sw,
+                                                        int pt, int pl, const float* __restrict__ bias, int act,
+                                                        const float* __restrict__ res, long long res_nstride,
+                                                        float* __restrict__ y, long long y_nstride, int OH, int OW) {
+  extern __shared__ float tile[];
+  const int nc = blockIdx.x;  // n * C + c
+  const int n = nc / C, c = nc - n * C;
+  const int oy0 = blockIdx.y * kDwTH;
+  const int rows = min(kDwTH, OH - oy0);
+  const int iy0 = oy0 * sh - pt;
+  const int in_rows = (rows - 1) * sh + KS;
+  const int in_cols = (OW - 1) * sw + KS;
+  const float* xc = x + static_cast<size_t>(n) * x_nstride + static_cast<size_t>(c) * H * W;
+  for (int i = threadIdx.x; i < in_rows * in_cols; i += blockDim.x) {
+    const int r = i / in_cols, q = i - r * in_cols;
+    const int iy = iy0 + r, ix = q - pl;
+    tile[i] = (iy >= 0 && iy < H && ix >= 0 && ix < W) ? __ldg(xc + iy * W + ix) : 0.0f;
+  }
+  float wr[KS * KS];
+  const float* wc = w + static_cast<size_t>(c) * KS * KS;
+#pragma unroll
+  for (int t = 0; t < KS * KS; ++t) wr[t] = __ldg(wc + t);
+  const float b = bias ? __ldg(bias + c) : 0.0f;
+  __syncthreads();
+  const size_t plane = static_cast<size_t>(OH) * OW;
+  float* yc = y + static_cast<size_t>(n) * y_nstride + static_cast<size_t>(c) * plane;
+  const float* rc = res ? res + static_cast<size_t>(n) * res_nstride + static_cast<size_t>(c) * plane : nullptr;
+  for (int i = threadIdx.x; i < rows * OW; i += blockDim.x) {
+    const int r = i / OW, ox = i - r * OW;
+    float acc = b;
+#pragma unroll
+    for (int ky = 0; ky < KS; ++ky) {
+      const float* trow = tile + (r * sh + ky) * in_cols + ox * sw;
+#pragma unroll
+      for (int kx = 0; kx < KS; ++kx) acc = __fmaf_rn(wr[ky * KS + kx], trow[kx], acc);
+    }
+    float v = apply_act(acc, act);
+    const size_t off = static_cast<size_t>(oy0 + r) * OW + ox;
+    if (rc) v = __fadd_rn(rc[off], v);
+    yc[off] = v;
+  }
+}
+
+// Register-blocked tiled conv on CUDA cores for group-1 K x K (K = 1, 3)
+// convs with few channels (the YOLO stem and the 8/16/32-channel layers, where
+// a 128-row tensor-core tile and 32-channel K padding would waste most of the
+// MMA and the hi/lo transform would dominate). Output tile per CTA: 8*G
+// channels x (4*P rows x 32 columns); each thread owns 8 channels x 4
+// adjacent pixels (32 accumulators). Input channels are staged CC at a time
+// (tile + halo, zero-filled padding via cp.async src-size 0) together with
+// the matching weights in [c][ky][kx][oc] order, double buffered. Per output
+// the chain is acc = bias, then fmaf over (ic, ky, kx) ascending, the im2col
+// order of ConvKernels.cs:525-654, so the result equals the reference's
+// im2col path (padded taps give fmaf(w, 0, acc)).
+__device__ __forceinline__ void cp_async4(float* dst, const float* src, bool valid) {
+  const unsigned d = static_cast<unsigned>(__cvta_generic_to_shared(dst));
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(d), "l"(src), "r"(valid ? 4 : 0) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int NPEND>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(NPEND) : "memory"); }
+
+template <int K, int S, int G, int P>
+struct TileConv {
+  static constexpr int OCB = 8 * G, TH = 4 * P, TW = 32;
+  static constexpr int IH = (TH - 1) * S + K, IW = (TW - 1) * S + K, IP = (IW + 3) / 4 * 4;
+  static constexpr int CC = S == 1 ? 8 : 4;
+  static constexpr int NX = 3 * S + K;  // input columns one thread reads per row
+  static constexpr int THREADS = 32 * G * P;
+  static constexpr int XS = CC * IH * IP, WS = CC * K * K * OCB, STAGE = XS + WS;
+  static constexpr int SMEM = 2 * STAGE * static_cast<int>(sizeof(float));
+};
+
+template <int K, int S, int G, int P>
+__global__ void __launch_bounds__(32 * G * P) k_conv_tile(
+    const float* __restrict__ x, long long x_nstride, int C, int H, int W, const float* __restrict__ w, int M, int pt,
+    int pl, const float* __restrict__ bias, int act, const float* __restrict__ res, long long res_nstride,
+    float* __restrict__ y, long long y_nstride, int OH, int OW, int tiles_x, bool vec4) {
+  using T = TileConv<K, S, G, P>;
+  extern __shared__ __align__(16) float smem_tile[];
+  const int tid = threadIdx.x;
+  const int n = blockIdx.z;
+  const int oc0 = blockIdx.y * T::OCB;
+  const int ty0 = (blockIdx.x / tiles_x) * T::TH, tx0 = (blockIdx.x % tiles_x) * T::TW;
+  const int gy0 = ty0 * S - pt, gx0 = tx0 * S - pl;
+  const float* xn = x + static_cast<size_t>(n) * x_nstride;
+  const int chunks = (C + T::CC - 1) / T::CC;
+
+  auto issue = [&](int chunk) {
+    float* xs = smem_tile + (chunk & 1) * T::STAGE;
+    float* ws = xs + T::XS;
+    const int c0 = chunk * T::CC;
+    const int nc = min(T::CC, C - c0);
+    for (int i = tid; i < nc * T::IH * T::IW; i += T::THREADS) {
+      const int c = i / (T::IH * T::IW);
+      const int rem = i - c * (T::IH * T::IW);
+      const int iy = rem / T::IW, ix = rem - iy * T::IW;
+      const int gy = gy0 + iy, gx = gx0 + ix;
+      const bool ok = gy >= 0 && gy < H && gx >= 0 && gx < W;
+      const float* src = ok ? xn + (static_cast<size_t>(c0 + c) * H + gy) * W + gx : xn;
+      cp_async4(xs + (c * T::IH + iy) * T::IP + ix, src, ok);
+    }
+    for (int i = tid; i < nc * K * K * T::OCB; i += T::THREADS) {
+      const int o = i % T::OCB;
+      const int ct = i / T::OCB;  // c * K*K + tap
+      const int c = ct / (K * K), tap = ct - c * (K * K);
+      const bool ok = oc0 + o < M;
+      const float* src = ok ? w + (static_cast<size_t>(oc0 + o) * C + c0 + c) * (K * K) + tap : w;
+      cp_async4(ws + i, src, ok);
+    }
+    cp_async_commit();
+  };
+
+  const int lane = tid & 31, wid = tid >> 5;
+  const int og = wid % G, pg = wid / G;
+  const int r = lane >> 3, cg = lane & 7;
+  float acc[8][4];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int oc = oc0 + og * 8 + i;
+    const float b = (bias && oc < M) ? __ldg(bias + oc) : 0.0f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = b;
+  }
+
+  issue(0);
+  for (int chunk = 0; chunk < chunks; ++chunk) {
+    if (chunk + 1 < chunks) {
+      issue(chunk + 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    const float* xs = smem_tile + (chunk & 1) * T::STAGE;
+    const float* ws = xs + T::XS + og * 8;
+    const int nc = min(T::CC, C - chunk * T::CC);
+    const float* xrow0 = xs + ((pg * 4 + r) * S) * T::IP + cg * 4 * S;
+    for (int c = 0; c < nc; ++c) {
+#pragma unroll
+      for (int ky = 0; ky < K; ++ky) {
+        const float* xp = xrow0 + (c * T::IH + ky) * T::IP;
+        float xr[T::NX];
+#pragma unroll
+        for (int q = 0; q + 4 <= T::NX; q += 4) {
+          const float4 v = *reinterpret_cast<const float4*>(xp + q);
+          xr[q] = v.x;
+          xr[q + 1] = v.y;
+          xr[q + 2] = v.z;
+          xr[q + 3] = v.w;
+        }
+#pragma unroll
+        for (int q = T::NX / 4 * 4; q < T::NX; ++q) xr[q] = xp[q];
+#pragma unroll
+        for (int kx = 0; kx < K; ++kx) {
+          const float* wp = ws + ((c * K + ky) * K + kx) * T::OCB;
+          const float4 w0 = *reinterpret_cast<const float4*>(wp);
+          const float4 w1 = *reinterpret_cast<const float4*>(wp + 4);
+          const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) acc[i][j] = __fmaf_rn(wv[i], xr[j * S + kx], acc[i][j]);
+        }
+      }
+    }
+    __syncthreads();
+  }
+
+  const int oy = ty0 + pg * 4 + r, ox = tx0 + cg * 4;
+  if (oy >= OH || ox >= OW) return;
+  const size_t plane = static_cast<size_t>(OH) * OW;
+  float* yn = y + static_cast<size_t>(n) * y_nstride + static_cast<size_t>(oy) * OW + ox;
+  const float* rn = res ? res + static_cast<size_t>(n) * res_nstride + static_cast<size_t>(oy) * OW + ox : nullptr;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int oc = oc0 + og * 8 + i;
+    if (oc >= M) break;
+    float v[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[j] = apply_act(acc[i][j], act);
+    const size_t off = static_cast<size_t>(oc) * plane;
+    if (vec4 && ox + 4 <= OW) {
+      if (rn) {
+        const float4 rv = *reinterpret_cast<const float4*>(rn + off);
+        v[0] = __fadd_rn(rv.x, v[0]);
+        v[1] = __fadd_rn(rv.y, v[1]);
+        v[2] = __fadd_rn(rv.z, v[2]);
+        v[3] = __fadd_rn(rv.w, v[3]);
+      }
+      *reinterpret_cast<float4*>(yn + off) = make_float4(v[0], v[1], v[2], v[3]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (ox + j >= OW) break;
+        yn[off + j] = rn ? __fadd_rn(rn[off + j], v[j]) : v[j];
+      }
+    }
+  }
+}
+
+template <int K, int S, int G, int P>
+int launch_conv_tile(osc_ctx* ctx, const float* x, long long x_nstride, int N, int C, int H, int W, const float* w,
+                     int M, int pt, int pl, const float* bias, int act, const float* res, long long res_nstride,
+                     float* y, long long y_nstride, int OH, int OW) {
+  using T = TileConv<K, S, G, P>;
+  OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(k_conv_tile<K, S, G, P>), T::SMEM));
+  const int tiles_x = (OW + T::TW - 1) / T::TW, tiles_y = (OH + T::TH - 1) / T::TH;
+  auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  const bool vec4 = OW % 4 == 0 && y_nstride % 4 == 0 && al16(y) &&
+                    (res == nullptr || (res_nstride % 4 == 0 && al16(res)));
+  dim3 grid(static_cast<unsigned>(tiles_x) * tiles_y, (M + T::OCB - 1) / T::OCB, N);
+  prof_begin(ctx);
+  k_conv_tile<K, S, G, P><<<grid, T::THREADS, T::SMEM, ctx->stream>>>(
+      x, x_nstride, C, H, W, w, M, pt, pl, bias, act, res, res_nstride, y, y_nstride, OH, OW, tiles_x, vec4);
+  return check_launch(ctx, "k_conv_tile");
+}
+
+template <int K, int S>
+int conv_tile_by_m(osc_ctx* ctx, const float* x, long long x_nstride, int N, int C, int H, int W, const float* w, int M,
+                   int pt, int pl, const float* bias, int act, const float* res, long long res_nstride, float* y,
+                   long long y_nstride, int OH, int OW) {
+  if (M <= 8)
+    return launch_conv_tile<K, S, 1, 4>(ctx, x, x_nstride, N, C, H, W, w, M, pt, pl, bias, act, res, res_nstride, y,
+                                        y_nstride, OH, OW);
+  if (M <= 16)
+    return launch_conv_tile<K, S, 2, 4>(ctx, x, x_nstride, N, C, H, W, w, M, pt, pl, bias, act, res, res_nstride, y,
+                                        y_nstride, OH, OW);
+  return launch_conv_tile<K, S, 4, 2>(ctx, x, x_nstride, N, C, H, W, w, M, pt, pl, bias, act, res, res_nstride, y,
+                                      y_nstride, OH, OW);
+}
+
 // ---------------------------------------------------------------- MaxPool
 // Ops/DnnOps.cs:1335 (MaxPoolLayer): max over the window's in-bounds elements.
 __global__ void k_maxpool(const float* __restrict__ x, long long x_nstride, int N, int C, int H, int W, int kh, int kw,
@@ -444,6 +733,101 @@ __global__ void k_psa_attention(const float* __restrict__ qkv, long long qkv_nst
   }
 }
 
+// Same computation with the head's K and V resident in shared memory and
+// register blocking (32 query rows per CTA, 256 threads): S rows are padded
+// to T+1 floats so the P reads of 32 different rows hit 32 banks.
+constexpr int kPsaR = 32;
+
+__global__ void __launch_bounds__(256) k_psa_attention_smem(const float* __restrict__ qkv, long long qkv_nstride,
+                                                            int heads, int kd, int hd, int T, float scale,
+                                                            float* __restrict__ out, long long out_nstride) {
+  extern __shared__ float sm[];
+  const int TP = T + 1;
+  float* ks = sm;                      // [kd][T]
+  float* vs = ks + kd * T;             // [hd][T]
+  float* S = vs + hd * T;              // [kPsaR][T+1]
+  float* qs = S + kPsaR * TP;          // [kd][kPsaR]
+  const int bh = blockIdx.y;
+  const int b = bh / heads, h = bh % heads;
+  const int i0 = blockIdx.x * kPsaR;
+  const int rows = min(kPsaR, T - i0);
+  const int per_head = 2 * kd + hd;
+  const float* base = qkv + static_cast<size_t>(b) * qkv_nstride + static_cast<size_t>(h) * per_head * T;
+  for (int i = threadIdx.x; i < (kd + hd) * T; i += blockDim.x) ks[i] = __ldg(base + static_cast<size_t>(kd) * T + i);
+  for (int idx = threadIdx.x; idx < kd * kPsaR; idx += blockDim.x) {
+    const int c = idx / kPsaR, r = idx % kPsaR;
+    qs[idx] = r < rows ? __ldg(base + static_cast<size_t>(c) * T + i0 + r) : 0.0f;
+  }
+  __syncthreads();
+  // S = (q^T k) * scale: each thread 4 rows x 1 key, FMA chain over c.
+  for (int idx = threadIdx.x; idx < (kPsaR / 4) * T; idx += blockDim.x) {
+    const int rg = idx / T, j = idx - rg * T;
+    float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+    for (int c = 0; c < kd; ++c) {
+      const float kv = ks[c * T + j];
+      const float* qc = qs + c * kPsaR + rg * 4;
+      a0 = __fmaf_rn(qc[0], kv, a0);
+      a1 = __fmaf_rn(qc[1], kv, a1);
+      a2 = __fmaf_rn(qc[2], kv, a2);
+      a3 = __fmaf_rn(qc[3], kv, a3);
+    }
+    float* sr = S + (rg * 4) * TP + j;
+    sr[0] = __fmul_rn(a0, scale);
+    sr[TP] = __fmul_rn(a1, scale);
+    sr[2 * TP] = __fmul_rn(a2, scale);
+    sr[3 * TP] = __fmul_rn(a3, scale);
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+  for (int r = warp; r < rows; r += nwarps) {
+    float* sr = S + r * TP;
+    float mx = -INFINITY;
+    for (int j = lane; j < T; j += 32) mx = fmaxf(mx, sr[j]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const int vend = T & ~7;
+    float part = 0.0f;
+    if (lane < 8)
+      for (int j = lane; j < vend; j += 8) {
+        const float e = ref_exp(__fsub_rn(sr[j], mx));
+        sr[j] = e;
+        part = __fadd_rn(part, e);
+      }
+    float total = 0.0f;
+    for (int l = 0; l < 8; ++l) total = __fadd_rn(total, __shfl_sync(0xffffffffu, part, l));
+    __syncwarp();
+    for (int j = vend; j < T; ++j) {
+      const float e = expf(__fsub_rn(sr[j], mx));
+      total = __fadd_rn(total, e);
+      __syncwarp();
+      if (lane == 0) sr[j] = e;
+      __syncwarp();
+    }
+    const float inv = __fdiv_rn(1.0f, total);
+    __syncwarp();
+    for (int j = lane; j < T; j += 32) sr[j] = __fmul_rn(sr[j], inv);
+  }
+  __syncthreads();
+  // out[h*hd + d][i0 + r]: lane = query row, warp = a group of hd/8 output channels.
+  float* ob = out + static_cast<size_t>(b) * out_nstride + static_cast<size_t>(h) * hd * T;
+  const int dper = (hd + nwarps - 1) / nwarps;
+  for (int d0 = warp * dper; d0 < min(hd, (warp + 1) * dper); d0 += 8) {
+    const int nd = min(8, min(hd, (warp + 1) * dper) - d0);
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    const float* pr = S + lane * TP;
+    for (int j = 0; j < T; ++j) {
+      const float p = pr[j];
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        if (q < nd) acc[q] = __fmaf_rn(vs[(d0 + q) * T + j], p, acc[q]);
+    }
+    if (lane < rows)
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        if (q < nd) ob[static_cast<size_t>(d0 + q) * T + i0 + lane] = acc[q];
+  }
+}
+
 }  // namespace
 }  // namespace osc
 
@@ -473,6 +857,56 @@ OSC_API int osc_conv2d_direct_f32(osc_ctx* ctx, const float* x, long long x_nstr
   if (x == nullptr || w == nullptr || y == nullptr) return fail(OSC_EINVAL, "osc_conv2d_direct_f32: null pointer");
   if (fault_injected("launch")) return fail(OSC_EFAULT_INJECTED, "injected failure (launch)");
   const int mpg = M / group;
+  const bool unit_dil = dil_h == 1 && dil_w == 1;
+  // Depthwise (group == C == M), square 3/5/7 kernels: band-tiled kernel.
+  if (group == C && group == M && kh == kw && (kh == 3 || kh == 5 || kh == 7) && unit_dil) {
+    const int in_cols = (OW - 1) * stride_w + kw;
+    const int in_rows = (kDwTH - 1) * stride_h + kh;
+    const size_t smem = static_cast<size_t>(in_rows) * in_cols * sizeof(float);
+    if (smem <= 48 * 1024) {
+      dim3 grid(static_cast<unsigned>(N) * C, (OH + kDwTH - 1) / kDwTH);
+      if (grid.x <= 2147483647u && grid.y <= 65535u) {
+        prof_begin(ctx);
+        if (kh == 3)
+          k_conv_depthwise<3><<<grid, 256, smem, ctx->stream>>>(x, x_nstride, N, C, H, W, w, stride_h, stride_w, pad_t,
+                                                                pad_l, bias, act, residual, res_nstride, y, y_nstride,
+                                                                OH, OW);
+        else if (kh == 5)
+          k_conv_depthwise<5><<<grid, 256, smem, ctx->stream>>>(x, x_nstride, N, C, H, W, w, stride_h, stride_w, pad_t,
+                                                                pad_l, bias, act, residual, res_nstride, y, y_nstride,
+                                                                OH, OW);
+        else
+          k_conv_depthwise<7><<<grid, 256, smem, ctx->stream>>>(x, x_nstride, N, C, H, W, w, stride_h, stride_w, pad_t,
+                                                                pad_l, bias, act, residual, res_nstride, y, y_nstride,
+                                                                OH, OW);
+        return check_launch(ctx, "k_conv_depthwise");
+      }
+    }
+  }
+  // Group-1 1x1 / 3x3 convs of stride 1 or 2: register-blocked tiles.
+  if (group == 1 && unit_dil && kh == kw && (kh == 1 || kh == 3) && stride_h == stride_w &&
+      (stride_h == 1 || stride_h == 2) && N <= 65535) {
+    if (kh == 1 && stride_h == 1)
+      return conv_tile_by_m<1, 1>(ctx, x, x_nstride, N, C, H, W, w, M, pad_t, pad_l, bias, act, residual, res_nstride,
+                                  y, y_nstride, OH, OW);
+    if (kh == 1)
+      return conv_tile_by_m<1, 2>(ctx, x, x_nstride, N, C, H, W, w, M, pad_t, pad_l, bias, act, residual, res_nstride,
+                                  y, y_nstride, OH, OW);
+    if (stride_h == 1)
+      return conv_tile_by_m<3, 1>(ctx, x, x_nstride, N, C, H, W, w, M, pad_t, pad_l, bias, act, residual, res_nstride,
+                                  y, y_nstride, OH, OW);
+    return conv_tile_by_m<3, 2>(ctx, x, x_nstride, N, C, H, W, w, M, pad_t, pad_l, bias, act, residual, res_nstride, y,
+                                y_nstride, OH, OW);
+  }
+  // First layers (group 1, small weight tensor): weights staged in shared memory.
+  const size_t wbytes = static_cast<size_t>(M) * C * kh * kw * sizeof(float);
+  if (group == 1 && unit_dil && residual == nullptr && wbytes <= 48 * 1024) {
+    const long long work = static_cast<long long>(N) * ((M + 15) / 16) * OH * OW;
+    prof_begin(ctx);
+    k_conv_direct_smw<16><<<blocks_for(ctx, work, 256, 32), 256, wbytes, ctx->stream>>>(
+        x, x_nstride, N, C, H, W, w, M, kh, kw, stride_h, stride_w, pad_t, pad_l, bias, act, y, y_nstride, OH, OW);
+    return check_launch(ctx, "k_conv_direct_smw");
+  }
   prof_begin(ctx);
   if (mpg >= 8) {
     const long long work = static_cast<long long>(N) * group * ((mpg + 15) / 16) * OH * OW;
@@ -624,6 +1058,17 @@ OSC_API int osc_psa_attention_f32(osc_ctx* ctx, const float* qkv, long long qkv_
   if (qkv_nstride == 0) qkv_nstride = static_cast<long long>(heads) * (2 * kd + hd) * T;
   if (out_nstride == 0) out_nstride = static_cast<long long>(heads) * hd * T;
   if (B == 0) return OSC_OK;
+  const size_t smem_full =
+      (static_cast<size_t>(kd + hd) * T + static_cast<size_t>(kPsaR) * (T + 1) + static_cast<size_t>(kd) * kPsaR) *
+      sizeof(float);
+  if (smem_full <= 220 * 1024) {
+    OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(k_psa_attention_smem), static_cast<int>(smem_full)));
+    dim3 grid((T + kPsaR - 1) / kPsaR, B * heads);
+    prof_begin(ctx);
+    k_psa_attention_smem<<<grid, 256, smem_full, ctx->stream>>>(qkv, qkv_nstride, heads, kd, hd, T, scale, out,
+                                                                out_nstride);
+    return check_launch(ctx, "k_psa_attention");
+  }
   OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(k_psa_attention), static_cast<int>(smem)));
   dim3 grid((T + kPsaRows - 1) / kPsaRows, B * heads);
   prof_begin(ctx);

@@ -38,6 +38,45 @@ def test_conv_direct(ctx, C, M, k, s, group):
     assert rel_err(y.cpu().numpy(), ref) <= 1e-5
 
 
+@pytest.mark.parametrize(
+    "C,M,k,s,H,W,resid",
+    [
+        (3, 16, 3, 2, 65, 64, False),   # stem: one partial channel chunk, odd rows
+        (16, 8, 3, 1, 33, 30, False),   # 8 output channels, width not a multiple of 4
+        (16, 32, 3, 2, 40, 40, False),  # stride 2, two full channel chunks
+        (12, 80, 1, 1, 20, 24, False),  # 1x1, partial output-channel block
+        (32, 16, 3, 1, 24, 36, True),   # fused residual
+        (5, 24, 1, 2, 17, 19, False),   # 1x1 stride 2, ragged everything
+    ],
+)
+def test_conv_tile_bit_exact(ctx, C, M, k, s, H, W, resid):
+    """The register-blocked CUDA-core conv keeps the im2col FMA order per
+    output (acc = bias, then (ic, ky, kx) ascending), so it reproduces the
+    oracle's bits; channel-slice views on input and output."""
+    import torch
+
+    from onnxsharp_b200 import ops
+
+    rng = np.random.default_rng(C * 7 + M + k + s)
+    x = rng.uniform(0, 1, (2, C + 3, H, W)).astype(np.float32)
+    w = (rng.normal(0, 1, (M, C, k, k)) * np.sqrt(2 / (C * k * k))).astype(np.float32)
+    b = rng.normal(0, 0.01, M).astype(np.float32)
+    p = k // 2
+    oh, ow = ops.out_size(H, k, s, p, p), ops.out_size(W, k, s, p, p)
+    res = rng.normal(0, 1, (2, M, oh, ow)).astype(np.float32) if resid else None
+    out_big = torch.zeros(2, M + 4, oh, ow, device="cuda")
+    dx = T(x)
+    ops.conv2d_direct(ctx, dx[:, 2:2 + C], T(w), T(b), out_big[:, 4:], s, p, 1, 1, 1,
+                      T(res) if resid else None)
+    ctx.synchronize()
+    ref = oracle.conv2d(np.ascontiguousarray(x[:, 2:2 + C]), w, b, (s, s), (p, p, p, p), (1, 1), 1, 1)
+    if resid:
+        ref = res + ref
+    got = out_big.cpu().numpy()
+    assert np.array_equal(got[:, 4:], ref)
+    assert not got[:, :4].any()
+
+
 def test_conv_ex_views_and_residual(ctx):
     """Input and output are channel slices of larger buffers; y = res + SiLU(conv(x) + b)."""
     import torch
