@@ -388,6 +388,10 @@ class YoloWorkload(Workload):
         self.net.input_view().copy_(torch.from_numpy(self.images_h))
         self.images_pin = torch.from_numpy(self.images_h).pin_memory()
         self.out_pin = torch.empty(self.net.output.shape, dtype=torch.float32).pin_memory()
+        # a second host batch and output for the pipelined serving loop
+        self.images_pin2 = torch.from_numpy(rng.uniform(0, 1, (batch, 3, 640, 640)).astype(np.float32)).pin_memory()
+        self.out_pin2 = torch.empty(self.net.output.shape, dtype=torch.float32).pin_memory()
+        self.pipe = None
         self.flops_img = yolo.flops_per_image(self.g)
         self.tc_flops = sum(self._node_flops(n) for n in self.g.nodes
                             if n.op == "conv" and yolo.Net.tensor_core(n)) * batch
@@ -426,6 +430,33 @@ class YoloWorkload(Workload):
 
     def e2e_bytes(self):
         return self.images_pin.numel() * 4, self.out_pin.numel() * 4
+
+    e2e_mode = ("pipelined: yolo.HostPipeline, depth 2 (H2D of batch i, plan of batch i-1 and D2H of batch "
+                "i-2 overlap on three streams); each step copies its own 315 MB input from pinned host memory "
+                "and reads its 181 MB output back; per-step inputs exceed L2, so no flush")
+
+    def e2e_pipelined(self, warmup: int, steps: int, barrier) -> float:
+        """ms per step of the serving loop, device-timed from the first H2D to the last D2H."""
+        import torch
+
+        from onnxsharp_b200 import yolo
+
+        if self.pipe is None:
+            self.pipe = yolo.HostPipeline(self.net, depth=2)
+        ins, outs = (self.images_pin, self.images_pin2), (self.out_pin, self.out_pin2)
+        for i in range(max(1, warmup)):
+            self.pipe.submit(ins[i % 2], outs[i % 2])
+        self.pipe.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(self.pipe.h2d)
+        for i in range(steps):
+            self.pipe.submit(ins[i % 2], outs[i % 2])
+        stop.record(self.pipe.d2h)
+        stop.synchronize()
+        barrier()
+        return start.elapsed_time(stop) / steps
 
     def cpu_sample(self, threads: int) -> dict:
         return CpuYolo(self.g, self.params, self.images_h[:1]).cpu_sample(threads)
@@ -581,22 +612,27 @@ def run_ours(args, peaks, peaks_kind) -> dict | None:
     ctx.profile_reset()
 
     # e2e through the public API with pinned host buffers
-    for _ in range(max(1, args.warmup)):
-        wl.e2e_step()
-    ctx.synchronize()
     KE = max(1, min(K, args.e2e_steps))
-    e_starts = [torch.cuda.Event(enable_timing=True) for _ in range(KE)]
-    e_stops = [torch.cuda.Event(enable_timing=True) for _ in range(KE)]
-    barrier()
-    torch.cuda.synchronize()
-    for i in range(KE):
-        e_starts[i].record(stream)
-        wl.e2e_step()
-        e_stops[i].record(stream)
-        flush_l2(flush)
-    torch.cuda.synchronize()
-    barrier()
-    e2e_ms = sum(s.elapsed_time(e) for s, e in zip(e_starts, e_stops)) / KE
+    if hasattr(wl, "e2e_pipelined"):
+        e2e_ms = wl.e2e_pipelined(args.warmup, KE, barrier)
+        e2e_mode = wl.e2e_mode
+    else:
+        for _ in range(max(1, args.warmup)):
+            wl.e2e_step()
+        ctx.synchronize()
+        e_starts = [torch.cuda.Event(enable_timing=True) for _ in range(KE)]
+        e_stops = [torch.cuda.Event(enable_timing=True) for _ in range(KE)]
+        barrier()
+        torch.cuda.synchronize()
+        for i in range(KE):
+            e_starts[i].record(stream)
+            wl.e2e_step()
+            e_stops[i].record(stream)
+            flush_l2(flush)
+        torch.cuda.synchronize()
+        barrier()
+        e2e_ms = sum(s.elapsed_time(e) for s, e in zip(e_starts, e_stops)) / KE
+        e2e_mode = "serial: H2D, compute, D2H per step, L2 flushed between steps"
     clocks = sampler.stop()
 
     t = torch.tensor([step_ms, e2e_ms], dtype=torch.float64, device="cuda")
@@ -634,7 +670,7 @@ def run_ours(args, peaks, peaks_kind) -> dict | None:
             "config": dict(wl.config, l2="flushed between steps (512 MiB write outside the events)",
                            parallelism=f"dp{world} (independent shards, no data-path collective)"),
             "e2e": {"value": round(e2e_value, 3), "unit": wl.unit, "h2d_bytes_per_step": bi, "d2h_bytes_per_step": bo,
-                    "ms_per_step": round(e2e_ms_max, 5)},
+                    "ms_per_step": round(e2e_ms_max, 5), "steps": KE, "mode": e2e_mode},
             "roofline": rl,
             "gpu_launches": int(launches),
             "clocks": clocks,

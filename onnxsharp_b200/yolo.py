@@ -240,6 +240,25 @@ def anchors(g: Graph, size: int = 640):
     return np.concatenate(out)
 
 
+def buffer_lifetimes(g: Graph):
+    """(names, first, last): the node index that first writes and last reads each
+    intermediate buffer (NetImpl.PrepareForGraph's live ranges). The graph input
+    is excluded: it is not in the arena but one of the plan's input slots (a
+    separate buffer per slot, so the next batch can be copied in while the
+    current one runs), read by every replay of the slot's captured graph."""
+    names = [n for n in g.buffers if n != g.input]
+    first = {n: -1 for n in names}
+    last = {n: 0 for n in names}
+    for i, node in enumerate(g.nodes):
+        for r in node.outs:
+            if first[r.buf] < 0:
+                first[r.buf] = i
+        for r in node.ins:
+            if r.buf != g.input:
+                last[r.buf] = max(last[r.buf], i)
+    return names, first, last
+
+
 # ---------------------------------------------------------------------------- device executor
 class Net:
     """The static plan on one GPU: arena-planned activations, prepacked
@@ -253,19 +272,7 @@ class Net:
 
         self.ctx, self.g, self.batch, self.size = ctx, g, batch, size
         dev = torch.device("cuda", ctx.device)
-        # lifetimes of buffers over the node sequence (input written before op 0, output never freed)
-        names = list(g.buffers)
-        first = {n: (-1 if n != g.input else 0) for n in names}
-        last = {n: 0 for n in names}
-        for i, node in enumerate(g.nodes):
-            for r in node.outs:
-                if first[r.buf] < 0:
-                    first[r.buf] = i
-            for r in node.ins:
-                last[r.buf] = max(last[r.buf], i)
-        # The graph input belongs to the caller and is re-read by every run (and by
-        # the captured graph): it stays live for the whole plan.
-        last[g.input] = len(g.nodes)
+        names, first, last = buffer_lifetimes(g)
         lts = []
         for n in names:
             c, h, w = g.buffers[n]
@@ -278,16 +285,18 @@ class Net:
             c, h, w = g.buffers[n]
             if off >= 0:
                 self.views[n] = self.arena[off // 4: off // 4 + batch * c * h * w].view(batch, c, h, w)
-        nc = g.nc
-        self.output = torch.empty((batch, 4 + nc, sum((size // s) ** 2 for s in g.strides)), dtype=torch.float32,
-                                  device=dev)
+        self.inputs = [torch.empty((batch,) + tuple(g.buffers[g.input]), dtype=torch.float32, device=dev)]
+        self.outputs = [torch.empty((batch, 4 + g.nc, sum((size // s) ** 2 for s in g.strides)),
+                                    dtype=torch.float32, device=dev)]
+        self.views[g.input] = self.inputs[0]
+        self.output = self.outputs[0]
         # weights
         self.dev_params = {k: torch.from_numpy(v).to(dev) for k, v in params.items()}
         self.packed = {}
         for node in g.nodes:
             if node.op == "conv" and self.tensor_core(node):
                 self.packed[node.name] = ConvWeights(ctx, self.dev_params[node.name + ".w"], g.params[node.name + ".w"])
-        self.graph_handle = None
+        self.graphs = [None]
         self.stream = None
 
     @staticmethod
@@ -306,8 +315,8 @@ class Net:
     def view(self, r: Ref):
         return self.views[r.buf][:, r.c0:r.c0 + r.c]
 
-    def input_view(self):
-        return self.views[self.g.input]
+    def input_view(self, slot: int = 0):
+        return self.inputs[slot]
 
     def _run_nodes(self):
         from . import ops
@@ -338,46 +347,132 @@ class Net:
             else:  # pragma: no cover
                 raise ValueError(node.op)
 
-    def forward(self, use_graph: bool = True):
-        """Run the plan on the contents of input_view(); returns the [B, 84, A] output tensor.
+    def _bind(self, slot: int):
+        """Point the plan at input/output slot `slot` (for eager runs and capture)."""
+        self.views[self.g.input] = self.inputs[slot]
+        self.output = self.outputs[slot]
 
-        The plan runs on its own stream (a capturable one), ordered after the
-        caller's current stream and before any later work on it."""
-        import ctypes as C
-
+    def add_slots(self, n: int):
+        """Make `n` input/output slots: each has its own input and output buffer
+        and its own captured graph; the activation arena is shared, so the slots'
+        graphs must run one after another on the plan's stream."""
         import torch
 
-        from ._lib import call
+        while len(self.inputs) < n:
+            self.inputs.append(torch.empty_like(self.inputs[0]))
+            self.outputs.append(torch.empty_like(self.outputs[0]))
+            self.graphs.append(None)
+
+    def plan_stream(self):
+        import torch
 
         if self.stream is None:
             self.stream = torch.cuda.Stream(device=self.ctx.device)
-        caller = torch.cuda.current_stream(self.ctx.device)
-        self.stream.wait_stream(caller)
+        return self.stream
+
+    def _launch(self, slot: int, use_graph: bool):
+        """Enqueue one run of the plan for `slot` on the plan's stream."""
+        import ctypes as C
+
+        from ._lib import call
+
         prev = self.ctx.get_stream()
-        self.ctx.set_stream(self.stream.cuda_stream)
+        self.ctx.set_stream(self.plan_stream().cuda_stream)
+        self._bind(slot)
         try:
             if not use_graph:
                 self._run_nodes()
-            else:
-                if self.graph_handle is None:
-                    self._run_nodes()  # sizes the scratch arena, sets kernel attributes
-                    self.ctx.synchronize()
-                    call("osc_graph_begin", self.ctx.handle)
-                    h = C.c_void_p()
-                    try:
-                        self._run_nodes()
-                    finally:
-                        call("osc_graph_end", self.ctx.handle, C.byref(h))
-                    self.graph_handle = h
-                call("osc_graph_launch", self.ctx.handle, self.graph_handle)
+                return
+            if self.graphs[slot] is None:
+                self._run_nodes()  # sizes the scratch arena, sets kernel attributes
+                self.ctx.synchronize()
+                call("osc_graph_begin", self.ctx.handle)
+                h = C.c_void_p()
+                try:
+                    self._run_nodes()
+                finally:
+                    call("osc_graph_end", self.ctx.handle, C.byref(h))
+                self.graphs[slot] = h
+            call("osc_graph_launch", self.ctx.handle, self.graphs[slot])
         finally:
+            self._bind(0)
             self.ctx.set_stream(prev)
-        caller.wait_stream(self.stream)
-        return self.output
+
+    def forward(self, use_graph: bool = True, slot: int = 0):
+        """Run the plan on the contents of input_view(slot); returns the slot's [B, 84, A] output tensor.
+
+        The plan runs on its own stream (a capturable one), ordered after the
+        caller's current stream and before any later work on it."""
+        import torch
+
+        stream = self.plan_stream()
+        caller = torch.cuda.current_stream(self.ctx.device)
+        stream.wait_stream(caller)
+        self._launch(slot, use_graph)
+        caller.wait_stream(stream)
+        return self.outputs[slot]
 
     def close(self):
         from . import _lib
 
-        if self.graph_handle is not None:
-            _lib.load().osc_graph_free(self.graph_handle)
-            self.graph_handle = None
+        for i, h in enumerate(self.graphs):
+            if h is not None:
+                _lib.load().osc_graph_free(h)
+                self.graphs[i] = None
+
+
+class HostPipeline:
+    """Serving loop from pinned host memory to pinned host memory.
+
+    Batch i's host->device copy, the plan for batch i-1 and the device->host
+    copy of batch i-2's detections run at the same time on three streams
+    (copy engines in both directions and the SMs), so a step costs
+    max(H2D, plan, D2H) instead of their sum. Each submission has its own
+    input and output slot (`depth` of them, round robin); a slot is reused
+    only after the plan that read its input and the copy that read its output
+    have finished (event waits, no host synchronisation)."""
+
+    def __init__(self, net: Net, depth: int = 2):
+        import torch
+
+        if depth < 1:
+            raise ValueError("depth must be >= 1")
+        self.net, self.depth, self.n = net, depth, 0
+        net.add_slots(depth)
+        dev = net.ctx.device
+        self.h2d = torch.cuda.Stream(device=dev)
+        self.d2h = torch.cuda.Stream(device=dev)
+        self.ev_h2d = [torch.cuda.Event() for _ in range(depth)]
+        self.ev_plan = [torch.cuda.Event() for _ in range(depth)]
+        self.ev_d2h = [torch.cuda.Event() for _ in range(depth)]
+        # capture every slot's graph up front (capture synchronises the device)
+        for slot in range(depth):
+            net.forward(use_graph=True, slot=slot)
+        torch.cuda.synchronize(dev)
+
+    def submit(self, host_in, host_out):
+        """Queue one batch: host_in [B,3,H,W] and host_out [B,84,A] are pinned
+        CPU tensors that must stay untouched until the returned event completes."""
+        import torch
+
+        net, s, reuse = self.net, self.n % self.depth, self.n >= self.depth
+        plan = net.plan_stream()
+        with torch.cuda.stream(self.h2d):
+            if reuse:
+                self.h2d.wait_event(self.ev_plan[s])  # the plan that read this input slot is done
+            net.inputs[s].copy_(host_in, non_blocking=True)
+            self.ev_h2d[s].record(self.h2d)
+        plan.wait_event(self.ev_h2d[s])
+        if reuse:
+            plan.wait_event(self.ev_d2h[s])  # the copy that read this output slot is done
+        net._launch(s, use_graph=True)
+        self.ev_plan[s].record(plan)
+        with torch.cuda.stream(self.d2h):
+            self.d2h.wait_event(self.ev_plan[s])
+            host_out.copy_(net.outputs[s], non_blocking=True)
+            self.ev_d2h[s].record(self.d2h)
+        self.n += 1
+        return self.ev_d2h[s]
+
+    def synchronize(self):
+        self.d2h.synchronize()

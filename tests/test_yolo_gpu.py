@@ -64,3 +64,29 @@ def test_yolo_detections_identical_after_nms(ctx, yolo_case):
         assert [d[0] for d in dg] == [d[0] for d in dr]
         assert [d[6] for d in dg] == [d[6] for d in dr]
         assert np.allclose([d[1:6] for d in dg], [d[1:6] for d in dr], rtol=1e-4, atol=1e-3)
+
+
+def test_host_pipeline_matches_forward(ctx, yolo_case):
+    """HostPipeline overlaps H2D / plan / D2H of consecutive batches over two
+    slots; every batch's host output must equal a plain forward of that batch
+    (same kernels, so bit-identical), including when slots are reused."""
+    import torch
+
+    from onnxsharp_b200 import yolo
+
+    g, params, images, _ = yolo_case
+    batches = [images, images[::-1].copy(), np.ascontiguousarray(images[:, :, ::-1]), images[:, ::-1].copy(), images]
+    net = yolo.Net(ctx, g, params, images.shape[0])
+    want = []
+    for b in batches:
+        net.input_view().copy_(torch.from_numpy(b))
+        want.append(net.forward(use_graph=True).cpu().numpy())
+    pipe = yolo.HostPipeline(net, depth=2)
+    ins = [torch.from_numpy(b).pin_memory() for b in batches]
+    outs = [torch.empty(net.outputs[0].shape, dtype=torch.float32).pin_memory() for _ in batches]
+    for i, o in zip(ins, outs):
+        pipe.submit(i, o)
+    pipe.synchronize()
+    net.close()
+    for w, o in zip(want, outs):
+        assert np.array_equal(o.numpy(), w)

@@ -51,16 +51,9 @@ def test_arena_strict_reuse_and_inplace():
 
 def test_yolo_arena_never_overlaps_live_buffers():
     g = yolo.build_yolo11n()
-    names = list(g.buffers)
-    first = {n: (0 if n == g.input else -1) for n in names}
-    last = {n: 0 for n in names}
-    for i, node in enumerate(g.nodes):
-        for r in node.outs:
-            if first[r.buf] < 0:
-                first[r.buf] = i
-        for r in node.ins:
-            last[r.buf] = max(last[r.buf], i)
-    last[g.input] = len(g.nodes)  # as Net: the caller's input stays live
+    names, first, last = yolo.buffer_lifetimes(g)
+    assert g.input not in names  # the input lives in the plan's slots, not the arena
+    assert all(first[n] >= 0 and last[n] >= first[n] for n in names)
     sizes = {n: 4 * int(np.prod(g.buffers[n])) for n in names}
     lts = [arena.Lifetime(first[n], last[n], sizes[n]) for n in names]
     offs, total = arena.plan_offsets(lts)
