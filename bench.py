@@ -167,6 +167,7 @@ def _scale(v: float) -> float:
 class GemmWorkload(Workload):
     """MatMul+Add(bias) A[2048,512] x B[512,2048] + bias[2048], U(-1,1)."""
 
+    graphed = True
     name = "matmul_bias_f32_2048x512x2048"
     main_kernel = "k_gemm_tf32x3"
 
@@ -244,6 +245,7 @@ CONV_FLOPS_PER_IMAGE = 2.0 * 128 * 160 * 160 * 64 * 9
 class ConvWorkload(Workload):
     """fused Conv+SiLU, x[16,64,160,160] -> y[16,128,160,160], 3x3 s1 p1."""
 
+    graphed = True
     name = "conv3x3_silu_f32_b16_64to128_160x160"
     main_kernel = "k_conv_tf32x3"
 
@@ -306,6 +308,7 @@ def dqmm_inputs(seed: int, m=4096, k=512, n=2048):
 class DqmmWorkload(Workload):
     """DynamicQuantizeMatMul A[4096,512] f32 x W int8 [512,2048] -> Y[4096,2048] f32."""
 
+    graphed = True
     name = "dqmm_u8s8_4096x512x2048"
     unit = "TOP/s"
     main_kernel = "k_dqmm_i8"
@@ -469,6 +472,7 @@ class AttentionWorkload(Workload):
     """X[64,128,512] N(0,1) -> Q/K/V projections (MatMul+bias, Xavier-uniform, zero bias)
     -> FusedAttention (H=8, D=64, scale 1/8) -> output projection."""
 
+    graphed = True
     name = "attention_block_b64_t128_h8_d64"
     main_kernel = "k_gemm_tf32x3"
 
@@ -554,10 +558,19 @@ def run_ours(args, peaks, peaks_kind) -> dict | None:
 
     from onnxsharp_b200.runtime import Context
 
+    # a capturable (non-legacy) stream for the library, the events and the L2 flush
+    torch.cuda.set_stream(torch.cuda.Stream())
     ctx = Context(local)
     ctx.use_torch_stream()
     wl = WORKLOADS[args.workload](ctx, rank)
     stream = torch.cuda.current_stream()
+    graph = None
+    if getattr(wl, "graphed", False):
+        # The executor's form: the op's launches replayed as one CUDA graph per step;
+        # per-kernel times come from profiled eager passes of the same launches.
+        graph = ctx.capture(wl.step)
+        wl.profile_step = wl.step
+        wl.step = graph.launch
     flush = torch.empty(512 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
 
     def barrier():
@@ -685,6 +698,8 @@ def run_ours(args, peaks, peaks_kind) -> dict | None:
             except Exception:  # pragma: no cover
                 pass
             result["cpu_baseline"] = base
+    if graph is not None:
+        graph.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -854,7 +869,7 @@ def main() -> int:
     ap.add_argument("--workload", default=DEFAULT_WORKLOAD, choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=None)
-    ap.add_argument("--profile-steps", type=int, default=5,
+    ap.add_argument("--profile-steps", type=int, default=None,
                     help="eager profiled steps for the dominant-kernel timing of graph-replayed workloads")
     ap.add_argument("--ref-steps", type=int, default=5)
     ap.add_argument("--traffic", type=float, default=None,
@@ -863,6 +878,8 @@ def main() -> int:
     args = ap.parse_args()
     if args.traffic is None:
         args.traffic = load_traffic(args.workload)
+    if args.profile_steps is None:
+        args.profile_steps = 5 if args.workload == "yolo" else 50
     if args.e2e_steps is None:
         args.e2e_steps = {"yolo": 10, "conv": 50}.get(args.workload, 200)
     if args.steps is None:

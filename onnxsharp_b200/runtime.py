@@ -68,6 +68,35 @@ class Context:
     def memcpy_dtoh(self, dst, src, nbytes: int) -> None:
         call("osc_memcpy_dtoh", self.handle, ptr(dst), ptr(src), int(nbytes))
 
+    def capture(self, fn) -> "CapturedGraph":
+        """Record the launches fn() makes on this context's stream into a CUDA
+        graph (osc_graph_begin / osc_graph_end). fn runs once eagerly first so
+        that scratch sizes and kernel attributes are settled outside the
+        capture. The stream must not be the legacy default stream."""
+        fn()
+        self.synchronize()
+        call("osc_graph_begin", self.handle)
+        h = C.c_void_p()
+        try:
+            fn()
+        finally:
+            call("osc_graph_end", self.handle, C.byref(h))
+        return CapturedGraph(self, h)
+
+    def close(self) -> None:
+        self._finalizer()
+
+
+class CapturedGraph:
+    """An instantiated CUDA graph of library launches (osc_graph_launch replays it on the context's stream)."""
+
+    def __init__(self, ctx: Context, handle):
+        self.ctx, self.handle = ctx, handle
+        self._finalizer = weakref.finalize(self, _lib.load().osc_graph_free, handle)
+
+    def launch(self) -> None:
+        call("osc_graph_launch", self.ctx.handle, self.handle)
+
     def close(self) -> None:
         self._finalizer()
 
