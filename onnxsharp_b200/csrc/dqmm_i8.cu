@@ -20,6 +20,7 @@
 // epilogue above, coalesced stores through shared memory).
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <vector>
 
 #include "runtime.h"
@@ -32,6 +33,7 @@ struct osc_dqmm_weights {
   int8_t* wt = nullptr;       // [n][kp] raw weight bytes, transposed
   int32_t* colsum = nullptr;  // [n] sum_t w[t][j] (as signed/unsigned integers)
   int32_t* zp = nullptr;      // [n] weight zero point per column
+  int has_zp = 0;             // any column has a non-zero weight zero point
 };
 
 namespace osc {
@@ -229,6 +231,7 @@ struct DqmmArgs {
   const float* bias;
   float* y;
   int32_t* acc_out;
+  int has_wzp;
 };
 
 __global__ void __launch_bounds__(kQThreads, 1)
@@ -421,6 +424,272 @@ __global__ void __launch_bounds__(kQThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------- persistent form
+// One CTA per SM walks 128 x 128 output tiles (tile t, t + grid, ...). The
+// TMEM holds two 128-column accumulators, so the MMA warp fills tile i+1
+// while the epilogue warps drain tile i; the epilogue writes each warp's
+// 32 x 64 result block into 128-byte-swizzled shared memory and one lane
+// stores it with two TMA tensor stores (async; the staging is reused once
+// the store engine has read it). Same arithmetic per element as k_dqmm_i8.
+constexpr int kPBN = 128, kPStages = 4;
+constexpr int kPA = kQBM * kQBK, kPB = kPBN * kQBK, kPStage = kPA + kPB;  // 16 + 16 KB
+constexpr int kPRing = kPStages * kPStage;                                  // 128 KB
+constexpr int kPEpiWarps = 8;
+constexpr int kPBox = 32 * 32 * 4;                                          // one 32x32 f32 store box
+constexpr int kPOut = kPEpiWarps * 2 * kPBox;                               // 64 KB
+constexpr int kPThreads = 64 + kPEpiWarps * 32;
+constexpr int kPSmem = 1024 + kPRing + kPOut + 256;
+static_assert(kPSmem <= 227 * 1024, "persistent DQMM smem");
+
+// Barrier over the epilogue warps that also ANDs a predicate across them, so a
+// wait that gave up in one warp stops every epilogue warp at the same tile.
+__device__ __forceinline__ bool epi_all_dqmm(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, 1, %2, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}\n"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(v)), "r"(kPEpiWarps * 32)
+      : "memory");
+  return r != 0;
+}
+
+// Raw per-column inputs of the epilogue constants (loaded one tile ahead).
+struct ColRaw {
+  int wz, cs;
+  float ws, b;
+};
+__device__ __forceinline__ ColRaw dqmm_col_load(const DqmmArgs& args, int j) {
+  ColRaw c{0, 0, 0.0f, 0.0f};
+  if (j < args.N) {
+    c.wz = __ldg(args.wzp + j);
+    c.cs = __ldg(args.colsum + j);
+    c.ws = __ldg(args.wscale + (args.n_scale > 1 ? j : 0));
+    c.b = args.bias ? __ldg(args.bias + j) : 0.0f;
+  }
+  return c;
+}
+
+// Transposed tiles: the MMA computes D = Wt[n0:n0+128] . q[m0:m0+128]^T, so a
+// TMEM lane is an output COLUMN j and a TMEM column an output row i. Each
+// epilogue thread therefore owns one column: its constants
+// (a_scale*w_scale[j], bias[j], the zero-point correction) sit in registers
+// for the whole tile and every element costs an integer add, a conversion,
+// one FMA and a 4-byte shared store. One CTA per SM walks the tiles (t,
+// t + grid, ...); two 128-column TMEM accumulators let the MMA warp fill
+// tile i+1 while the epilogue drains tile i. Each epilogue warp writes its
+// 64 rows x 32 columns into 128-byte-swizzled boxes that one lane stores
+// with TMA tensor stores. Same arithmetic per element as k_dqmm_i8.
+__global__ void __launch_bounds__(kPThreads, 1)
+    k_dqmm_i8_persistent(const __grid_constant__ CUtensorMap mQ, const __grid_constant__ CUtensorMap mW,
+                         const __grid_constant__ CUtensorMap mY, const __grid_constant__ DqmmArgs args,
+                         uint32_t idesc, int* __restrict__ err) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* ostage = ring + kPRing;
+  uint64_t* full = reinterpret_cast<uint64_t*>(ostage + kPOut);
+  uint64_t* empty = full + kPStages;
+  uint64_t* tfull = empty + kPStages;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int mt = (args.M + kPBN - 1) / kPBN;  // row tiles (the MMA's N side)
+  const int tiles = mt * ((args.N + kQBM - 1) / kQBM);
+  const int num_kb = args.num_kb;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], kPEpiWarps);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch(&mQ);
+    tma_prefetch(&mW);
+    tma_prefetch(&mY);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 2 * kPBN);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int g = 0, issued = 0;
+      for (int t = blockIdx.x; t < tiles && !*abort_flag; t += gridDim.x) {
+        const int m0 = (t % mt) * kPBN, n0 = (t / mt) * kQBM;
+        for (int kb = 0; kb < num_kb; ++kb, ++g) {
+          const int s = g % kPStages;
+          if (!mbar_wait(&empty[s], ((g / kPStages) & 1u) ^ 1u, abort_flag, err)) break;
+          uint8_t* st = ring + s * kPStage;
+          mbar_arrive_expect_tx(&full[s], kPStage);
+          tma_load_2d(st, &mW, &full[s], kb * kQBK, n0);        // A: 128 weight columns
+          tma_load_2d(st + kPA, &mQ, &full[s], kb * kQBK, m0);  // B: 128 quantised rows
+          issued = g + 1;
+        }
+      }
+      if (*abort_flag) {  // let in-flight loads land before the CTA's shared memory goes away
+        for (int x = issued > kPStages ? issued - kPStages : 0; x < issued; ++x) {
+          const uint64_t t0 = globaltimer_ns();
+          while (!mbar_try_wait(&full[x % kPStages], (x / kPStages) & 1u) &&
+                 globaltimer_ns() - t0 < 50ull * 1000ull * 1000ull) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int g = 0, lt = 0;
+      for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++lt) {
+        const int tb = lt & 1;
+        if (!mbar_wait(&tempty[tb], ((lt >> 1) & 1u) ^ 1u, abort_flag, err)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + static_cast<uint32_t>(tb * kPBN);
+        bool ok = true;
+        for (int kb = 0; kb < num_kb; ++kb, ++g) {
+          const int s = g % kPStages;
+          if (!mbar_wait(&full[s], (g / kPStages) & 1u, abort_flag, err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t base = smem_addr(ring + s * kPStage);
+          const uint64_t dA = sdesc_kmajor_sw128(base);
+          const uint64_t dB = sdesc_kmajor_sw128(base + kPA);
+#pragma unroll
+          for (int kk = 0; kk < kQBK / 32; ++kk) {
+            const uint64_t off = static_cast<uint64_t>(kk * 2);
+            mma_i8(d, dA + off, dB + off, idesc, (kb | kk) != 0 ? 1u : 0u);
+          }
+          mma_commit(&empty[s]);
+        }
+        if (!ok) break;
+        mma_commit(&tfull[tb]);
+      }
+    }
+  } else {
+    const int ew = warp - 2;
+    const int q = warp & 3;   // TMEM lane quadrant: output columns 32q .. 32q+31 of the tile
+    const int h = ew >> 2;    // output rows 64h .. 64h+63 of the tile
+    uint8_t* my_out = ostage + ew * 2 * kPBox;
+    const QParams p = *args.qp;
+    int t = blockIdx.x;
+    ColRaw raw{0, 0, 0.0f, 0.0f};
+    int rs_a = 0, rs_b = 0, nan_a = 0, nan_b = 0;  // rows 64h + lane and 64h + 32 + lane
+    auto load_tile_inputs = [&](int tt) {
+      const int mm = (tt % mt) * kPBN + h * 64, nn = (tt / mt) * kQBM;
+      raw = dqmm_col_load(args, nn + q * 32 + lane);
+      const int ia = mm + lane, ib = mm + 32 + lane;
+      nan_a = ia < args.M ? __ldg(args.nanrow + ia) : 0;
+      nan_b = ib < args.M ? __ldg(args.nanrow + ib) : 0;
+      if (args.has_wzp) {
+        rs_a = ia < args.M ? __ldg(args.rowsum + ia) : 0;
+        rs_b = ib < args.M ? __ldg(args.rowsum + ib) : 0;
+      }
+    };
+    if (t < tiles) load_tile_inputs(t);
+    for (int lt = 0; t < tiles; t += gridDim.x, ++lt) {
+      const int tb = lt & 1;
+      const int m0 = (t % mt) * kPBN, n0 = (t / mt) * kQBM;
+      const int j = n0 + q * 32 + lane;  // this thread's output column
+      const int i0 = m0 + h * 64;        // first of this warp's 64 output rows
+      const float comb = __fmul_rn(p.scale, raw.ws);
+      const float bias = raw.b;
+      const int corr = -p.zp * raw.cs + args.K * p.zp * raw.wz;
+      const int wz = raw.wz;
+      const bool full_col = j < args.full_cols;
+      const int my_rs_a = rs_a, my_rs_b = rs_b;
+      const bool any_nan = __any_sync(0xffffffffu, (nan_a | nan_b) != 0);
+      const int my_nan_a = nan_a, my_nan_b = nan_b;
+      if (t + static_cast<int>(gridDim.x) < tiles) load_tile_inputs(t + gridDim.x);  // in flight meanwhile
+      if (!epi_all_dqmm(mbar_wait(&tfull[tb], (lt >> 1) & 1u, abort_flag, err))) break;
+      tc_fence_after();
+      if (lane == 0) bulk_wait_read_all();  // the previous tile's stores have read the staging
+      __syncwarp();
+      const uint32_t tbase = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(tb * kPBN + h * 64);
+      const int nf = min(max(args.fused_rows - i0, 0), 64);  // rows of this block on the fused-FMA path
+      const bool fast = !args.has_wzp && __all_sync(0xffffffffu, full_col) && nf == 64;
+      const float bias_u = args.bias ? bias : -0.0f;  // x + (-0) == x for every x, -0 included
+      // element (row i0 + 32*half + e, column j) -> box `half`, row e, 16-byte chunk (lane/4) ^ (e%8)
+      float* ocol = reinterpret_cast<float*>(my_out + (lane & 3) * 4);
+      const int swz = lane >> 2;
+#pragma unroll 1
+      for (int half = 0; half < 2; ++half) {
+        uint32_t r[32];
+        tmem_ld32(tbase + half * 32, r);
+        tmem_wait_ld();
+        if (half == 1) {  // the accumulator buffer is free for the tile after next
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tempty[tb]);
+        }
+        float* obox = ocol + half * (kPBox / 4);
+        if (fast) {  // common case: every element is fma(acc, a_scale*w_scale[j], bias[j])
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const int32_t acc = static_cast<int32_t>(r[e]) + corr;
+            r[e] = static_cast<uint32_t>(acc);
+            obox[e * 32 + ((swz ^ (e & 7)) << 2)] = __fmaf_rn(static_cast<float>(acc), comb, bias);
+          }
+        } else {  // tails (unfused mul-then-add), weight zero points: selects, no branches per element
+          const int rs_h = half == 0 ? my_rs_a : my_rs_b;
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            int32_t acc = static_cast<int32_t>(r[e]) + corr;
+            acc -= args.has_wzp ? wz * __shfl_sync(0xffffffffu, rs_h, e) : 0;
+            r[e] = static_cast<uint32_t>(acc);
+            const float af = static_cast<float>(acc);
+            const float vf = __fmaf_rn(af, comb, bias);
+            const float vu = __fadd_rn(__fmul_rn(af, comb), bias_u);
+            obox[e * 32 + ((swz ^ (e & 7)) << 2)] = (half * 32 + e < nf && full_col) ? vf : vu;
+          }
+        }
+        if (any_nan) {  // rows whose input held a NaN are NaN throughout (rare)
+          const int nan_h = half == 0 ? my_nan_a : my_nan_b;
+#pragma unroll 1
+          for (int e = 0; e < 32; ++e)
+            if (__shfl_sync(0xffffffffu, nan_h, e) != 0) obox[e * 32 + ((swz ^ (e & 7)) << 2)] = __int_as_float(0x7fc00000);
+        }
+        if (args.acc_out != nullptr && j < args.N) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const int i = i0 + half * 32 + e;
+            if (i < args.M) args.acc_out[static_cast<size_t>(i) * args.N + j] = static_cast<int32_t>(r[e]);
+          }
+        }
+      }
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        const int col0 = n0 + q * 32;
+        if (col0 < args.N) {
+          if (i0 < args.M) tma_store_2d(&mY, my_out, col0, i0);
+          if (i0 + 32 < args.M) tma_store_2d(&mY, my_out + kPBox, col0, i0 + 32);
+        }
+        bulk_commit();
+      }
+    }
+    if (lane == 0) bulk_wait_all();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 2 * kPBN);
+  }
+}
+
 // W [k][n] (s8 or u8) -> Wt [n][kp] + column sums; one thread per output column strip.
 __global__ void k_pack_dqmm_w(const int8_t* __restrict__ w, int k, int n, int kp, int is_signed,
                               int8_t* __restrict__ wt, int32_t* __restrict__ colsum) {
@@ -484,7 +753,10 @@ OSC_API int osc_dqmm_prepack(osc_ctx* ctx, const void* w, int k, int n, int is_s
   d->kp = static_cast<int>(round_up(static_cast<size_t>(k), kQBK));
   d->is_signed = is_signed ? 1 : 0;
   std::vector<int32_t> zp(static_cast<size_t>(n), 0);
-  for (int j = 0; j < n; ++j) zp[j] = n_zp == 0 ? 0 : (n_zp == 1 ? w_zp[0] : w_zp[j]);
+  for (int j = 0; j < n; ++j) {
+    zp[j] = n_zp == 0 ? 0 : (n_zp == 1 ? w_zp[0] : w_zp[j]);
+    if (zp[j] != 0) d->has_zp = 1;
+  }
   const size_t wbytes = static_cast<size_t>(k) * n;
   int8_t* staged = nullptr;
   cudaError_t e = cudaMalloc(&d->wt, static_cast<size_t>(n) * d->kp);
@@ -614,7 +886,45 @@ OSC_API int osc_dqmm_f32(osc_ctx* ctx, const float* a, int m, int k, int lda, co
   args.bias = bias;
   args.y = y;
   args.acc_out = acc_out;
-  const uint32_t idesc = (2u << 4) | (0u << 7) | ((w->is_signed ? 1u : 0u) << 10) |
+  args.has_wzp = w->has_zp;
+  const uint32_t b_fmt = w->is_signed ? 1u : 0u;
+  static const bool force_tiles = [] {
+    const char* e = std::getenv("OSC_DQMM_PERSISTENT");
+    return e != nullptr && e[0] == '0';
+  }();
+  if (!force_tiles && w->n % 4 == 0 && (reinterpret_cast<uintptr_t>(y) & 15u) == 0) {
+    // persistent transposed tiles with TMA stores (row pitch N*4 bytes is a multiple of 16)
+    CUtensorMap mQp, mY;
+    {
+      const uint64_t dims[2] = {static_cast<uint64_t>(kp), static_cast<uint64_t>(m)};
+      const uint64_t pitch[1] = {static_cast<uint64_t>(kp)};
+      const uint32_t box[2] = {kQBK, kPBN};
+      OSC_TRY(encode_tiled(&mQp, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, q, dims, pitch, box, CU_TENSOR_MAP_SWIZZLE_128B));
+    }
+    CUtensorMap mWp;
+    {
+      const uint64_t dims[2] = {static_cast<uint64_t>(kp), static_cast<uint64_t>(w->n)};
+      const uint64_t pitch[1] = {static_cast<uint64_t>(kp)};
+      const uint32_t box[2] = {kQBK, kQBM};
+      OSC_TRY(encode_tiled(&mWp, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, w->wt, dims, pitch, box, CU_TENSOR_MAP_SWIZZLE_128B));
+    }
+    {
+      const uint64_t dims[2] = {static_cast<uint64_t>(w->n), static_cast<uint64_t>(m)};
+      const uint64_t pitch[1] = {static_cast<uint64_t>(w->n) * 4};
+      const uint32_t box[2] = {32, 32};
+      OSC_TRY(encode_tiled(&mY, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, y, dims, pitch, box, CU_TENSOR_MAP_SWIZZLE_128B));
+    }
+    // A = weights (s8 or u8), B = quantised activations (u8); M = 128 columns, N = 128 rows
+    const uint32_t idesc_p = (2u << 4) | (b_fmt << 7) | (0u << 10) | (static_cast<uint32_t>(kPBN >> 3) << 17) |
+                             (static_cast<uint32_t>(kQBM >> 4) << 24);
+    OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(k_dqmm_i8_persistent), kPSmem));
+    const int tiles = ((m + kPBN - 1) / kPBN) * ((w->n + kQBM - 1) / kQBM);
+    prof_begin(ctx);
+    k_dqmm_i8_persistent<<<std::min(tiles, ctx->num_sms), kPThreads, kPSmem, ctx->stream>>>(mQp, mWp, mY, args,
+                                                                                          idesc_p, ctx->d_err);
+    return check_launch(ctx, "k_dqmm_i8");
+  }
+  const uint32_t idesc = (2u << 4) | (0u << 7) | (b_fmt << 10) |
                          (static_cast<uint32_t>(kQBN >> 3) << 17) | (static_cast<uint32_t>(kQBM >> 4) << 24);
   OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(k_dqmm_i8), kQSmem));
   dim3 grid((w->n + kQBN - 1) / kQBN, (m + kQBM - 1) / kQBM);

@@ -58,6 +58,20 @@ def test_dqmm_config3_bit_exact(ctx):
     _check(_run(ctx, a, w, 0, ws, b), oracle.dqmm(a, w, 0, ws, b))
 
 
+def test_dqmm_without_debug_outputs_same_y(ctx):
+    """The serving call (no q / acc / params outputs) gives the same y bits."""
+    import torch
+
+    from onnxsharp_b200.runtime import DqmmWeights, dqmm
+
+    a, w, ws, b = _config3(4)
+    y_dbg = _run(ctx, a, w, 0, ws, b)[0]
+    W = DqmmWeights(ctx, torch.from_numpy(w).cuda(), 512, 2048, 0)
+    y = dqmm(ctx, torch.from_numpy(a).cuda(), W, torch.from_numpy(ws).cuda(), torch.from_numpy(b).cuda())
+    ctx.synchronize()
+    assert np.array_equal(y.cpu().numpy().view(np.uint32), y_dbg.view(np.uint32))
+
+
 def test_dqmm_golden_fixture_ragged(ctx, golden):
     g = golden
     got = _run(ctx, g["dqmm_a"], g["dqmm_w"], 0, g["dqmm_wscale"], g["dqmm_bias"])
