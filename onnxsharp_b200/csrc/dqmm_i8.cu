@@ -208,6 +208,226 @@ __global__ void k_quantize_rows(const float* __restrict__ a, int m, int k, int l
   }
 }
 
+// The whole DynamicQuantizeLinear as ONE cooperative kernel when A's rows fit
+// in the CTAs' shared memory: each CTA loads its contiguous rows of A once
+// (HBM -> smem, min/max on the fly), publishes a partial range, meets the other
+// CTAs at a grid barrier (bounded spin on a device counter), reduces the
+// partials to scale/zero point (same arithmetic as k_dql_params) and quantizes
+// its rows from shared memory (same arithmetic as k_quantize_rows). A is read
+// from HBM once and the range and quantisation need no extra launches.
+// Counters: sync[0] arrivals, sync[1] departures; the last CTA to leave
+// resets both, so every launch starts from zero.
+constexpr int kDqlThreads = 512;
+
+__device__ __forceinline__ QParams dql_params_from(float mn, float mx) {
+  float scale = __fdiv_rn(__fsub_rn(mx, mn), 255.0f);
+  if (!(scale > 0.0f)) scale = 1.0f;
+  const float z = rintf(__fdiv_rn(-mn, scale));
+  int zp = (z != z) ? 0 : (z >= 2147483520.0f ? 2147483647 : (z <= -2147483648.0f ? (-2147483647 - 1) : static_cast<int>(z)));
+  zp = zp < 0 ? 0 : (zp > 255 ? 255 : zp);
+  QParams p;
+  p.scale = scale;
+  p.inverse = __fdiv_rn(1.0f, scale);
+  p.zp = zp;
+  p.pad = 0;
+  return p;
+}
+
+__global__ void __launch_bounds__(kDqlThreads, 1)
+    k_dql_fused(const float* __restrict__ a, int m, int k, int lda, int kp, int rows_per_cta,
+                const float* __restrict__ override_mm, float2* __restrict__ part, unsigned* __restrict__ sync,
+                QParams* __restrict__ qp_out, float* __restrict__ params_out, uint8_t* __restrict__ q,
+                int32_t* __restrict__ rowsum, int32_t* __restrict__ nanrow, int* __restrict__ err) {
+  extern __shared__ float rows_s[];  // [rows_per_cta][k], then row sums and NaN flags
+  int* s_sum = reinterpret_cast<int*>(rows_s + static_cast<size_t>(rows_per_cta) * k);
+  int* s_nan = s_sum + rows_per_cta;
+  __shared__ float red_mn[kDqlThreads / 32], red_mx[kDqlThreads / 32];
+  __shared__ QParams sp;
+  __shared__ int s_ok;
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  const int r0 = blockIdx.x * rows_per_cta;
+  const int nrows = max(0, min(m, r0 + rows_per_cta) - r0);
+  const int count = nrows * k;
+  for (int r = tid; r < nrows; r += kDqlThreads) {
+    s_sum[r] = 0;
+    s_nan[r] = 0;
+  }
+  float mn = 0.0f, mx = 0.0f;  // 0 is always inside the range
+  auto take = [&](float e) {
+    if (e == e) {
+      mn = fminf(mn, e);
+      mx = fmaxf(mx, e);
+    }
+  };
+  if (lda == k && (k & 3) == 0 && (reinterpret_cast<uintptr_t>(a) & 15u) == 0) {
+    // the CTA's rows are one contiguous block: 8 independent 16-byte loads in flight per thread
+    const float4* src = reinterpret_cast<const float4*>(a + static_cast<size_t>(r0) * k);
+    float4* dst = reinterpret_cast<float4*>(rows_s);
+    const int n4 = count >> 2;
+    for (int base = 0; base < n4; base += 8 * kDqlThreads) {
+      float4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int i = base + u * kDqlThreads + tid;
+        if (i < n4) v[u] = __ldg(src + i);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int i = base + u * kDqlThreads + tid;
+        if (i < n4) {
+          dst[i] = v[u];
+          take(v[u].x);
+          take(v[u].y);
+          take(v[u].z);
+          take(v[u].w);
+        }
+      }
+    }
+  } else {
+    for (int i = tid; i < count; i += kDqlThreads) {
+      const int row = i / k, c = i - row * k;
+      const float e = a[static_cast<size_t>(r0 + row) * lda + c];
+      rows_s[i] = e;
+      take(e);
+    }
+  }
+  const int G = gridDim.x;
+  if (override_mm == nullptr) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    }
+    if (lane == 0) {
+      red_mn[wid] = mn;
+      red_mx[wid] = mx;
+    }
+    __syncthreads();
+    if (wid == 0) {
+      mn = lane < kDqlThreads / 32 ? red_mn[lane] : 0.0f;
+      mx = lane < kDqlThreads / 32 ? red_mx[lane] : 0.0f;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      }
+      if (lane == 0) {
+        part[blockIdx.x] = make_float2(mn, mx);
+        __threadfence();
+        atomicAdd(&sync[0], 1u);
+        // grid barrier: bounded spin until every CTA has published its range
+        const long long c0 = clock64();
+        int ok = 1;
+        while (*reinterpret_cast<volatile unsigned*>(&sync[0]) < static_cast<unsigned>(G)) {
+          if (clock64() - c0 > kWaitLimitCycles) {
+            ok = 0;
+            atomicExch(err, DEV_ERR_TIMEOUT);
+            break;
+          }
+        }
+        __threadfence();
+        s_ok = ok;
+      }
+      __syncwarp();
+      // every CTA reduces all partials (order-independent, equals a serial scan);
+      // each lane's loads are independent so they are in flight together
+      float2 pp[5];
+#pragma unroll
+      for (int u = 0; u < 5; ++u) {
+        const int i = lane + 32 * u;
+        pp[u] = i < G ? __ldcg(part + i) : make_float2(0.0f, 0.0f);
+      }
+      mn = 0.0f;
+      mx = 0.0f;
+#pragma unroll
+      for (int u = 0; u < 5; ++u) {
+        mn = fminf(mn, pp[u].x);
+        mx = fmaxf(mx, pp[u].y);
+      }
+      for (int i = lane + 160; i < G; i += 32) {
+        const float2 t = __ldcg(part + i);
+        mn = fminf(mn, t.x);
+        mx = fmaxf(mx, t.y);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      }
+      if (lane == 0) sp = dql_params_from(mn, mx);
+    }
+  } else if (tid == 0) {
+    s_ok = 1;
+    sp = dql_params_from(fminf(0.0f, override_mm[0]), fmaxf(0.0f, override_mm[1]));
+  }
+  __syncthreads();
+  if (!s_ok) return;
+  const QParams p = sp;
+  if (blockIdx.x == 0 && tid == 0) {
+    *qp_out = p;
+    if (params_out != nullptr) {
+      params_out[0] = p.scale;
+      params_out[1] = static_cast<float>(p.zp);
+    }
+  }
+  // quantize the CTA's rows from shared memory: 4-element groups over all
+  // threads (a row's kp/4 groups are a multiple of 32, so a warp stays in one row)
+  const float inv = p.inverse, zpf = static_cast<float>(p.zp);
+  const int gpr = kp >> 2;
+  const bool vk = (k & 3) == 0;
+  for (int g = tid; g < nrows * gpr; g += kDqlThreads) {
+    const int row = g / gpr, c0 = (g - row * gpr) * 4;
+    const float* xr = rows_s + static_cast<size_t>(row) * k;
+    float xv[4];
+    if (vk && c0 + 4 <= k) {
+      const float4 t4 = *reinterpret_cast<const float4*>(xr + c0);
+      xv[0] = t4.x;
+      xv[1] = t4.y;
+      xv[2] = t4.z;
+      xv[3] = t4.w;
+    } else {
+#pragma unroll
+      for (int t = 0; t < 4; ++t) xv[t] = c0 + t < k ? xr[c0 + t] : 0.0f;
+    }
+    uint32_t packed = 0;
+    int sum = 0, nan = 0;
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      uint32_t v = 0;
+      if (c0 + t < k) {
+        const float sv = __fmul_rn(xv[t], inv);
+        if (sv != sv) {
+          nan = 1;
+        } else {
+          v = static_cast<uint32_t>(minps(255.0f, maxps(0.0f, __fadd_rn(rintf(sv), zpf))));
+        }
+      }
+      sum += static_cast<int>(v);
+      packed |= v << (8 * t);
+    }
+    *reinterpret_cast<uint32_t*>(q + static_cast<size_t>(r0 + row) * kp + c0) = packed;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      nan |= __shfl_xor_sync(0xffffffffu, nan, o);
+    }
+    if (lane == 0) {
+      atomicAdd(&s_sum[row], sum);
+      if (nan) s_nan[row] = 1;
+    }
+  }
+  __syncthreads();
+  for (int r = tid; r < nrows; r += kDqlThreads) {
+    rowsum[r0 + r] = s_sum[r];
+    nanrow[r0 + r] = s_nan[r];
+  }
+  if (override_mm == nullptr && tid == 0 && atomicAdd(&sync[1], 1u) == static_cast<unsigned>(G) - 1u) {
+    sync[0] = 0u;  // every CTA has passed the barrier: reset for the next launch
+    sync[1] = 0u;
+    __threadfence();
+  }
+}
+
 // Rows [0, grouped) went through the reference's 12/6/4-row micro-kernels
 // (fused FMA epilogue); see GemmKernel.cs:746-790.
 __host__ __device__ inline int grouped_rows(int m) {
@@ -847,8 +1067,35 @@ OSC_API int osc_dqmm_f32(osc_ctx* ctx, const float* a, int m, int k, int lda, co
   uint8_t* q = base + off_q;
   int32_t* rowsum = reinterpret_cast<int32_t*>(base + off_rs);
   int32_t* nanrow = reinterpret_cast<int32_t*>(base + off_nan);
-  OSC_TRY(minmax_params(ctx, a, static_cast<long>(m) * k, minmax_override, base, qp, params_out));
-  {
+  const int dql_ctas = std::min(m, ctx->num_sms);
+  const int rows_per_cta = (m + dql_ctas - 1) / dql_ctas;
+  const size_t dql_smem = static_cast<size_t>(rows_per_cta) * (static_cast<size_t>(k) * sizeof(float) + 8);
+  static const bool split_dql = [] {
+    const char* e = std::getenv("OSC_DQL_FUSED");
+    return e != nullptr && e[0] == '0';
+  }();
+  if (!split_dql && dql_smem <= 200 * 1024) {
+    // one cooperative launch: range, grid barrier, quantisation
+    OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(k_dql_fused), static_cast<int>(dql_smem)));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(dql_ctas));
+    cfg.blockDim = dim3(kDqlThreads);
+    cfg.dynamicSmemBytes = dql_smem;
+    cfg.stream = ctx->stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    unsigned* sync = reinterpret_cast<unsigned*>(ctx->d_err) + 4;
+    prof_begin(ctx);
+    const cudaError_t le = cudaLaunchKernelEx(&cfg, k_dql_fused, a, m, k, lda, kp, rows_per_cta, minmax_override,
+                                              reinterpret_cast<float2*>(base), sync, qp, params_out, q, rowsum,
+                                              nanrow, ctx->d_err);
+    if (le != cudaSuccess) return cuda_fail(le, "k_dql_fused launch");
+    OSC_TRY(check_launch(ctx, "k_dql_fused"));
+  } else {
+    OSC_TRY(minmax_params(ctx, a, static_cast<long>(m) * k, minmax_override, base, qp, params_out));
     const int blocks = std::min((m + 7) / 8, ctx->num_sms * 8);
     prof_begin(ctx);
     k_quantize_rows<<<blocks, 256, 0, ctx->stream>>>(a, m, k, lda, kp, qp, q, rowsum, nanrow);

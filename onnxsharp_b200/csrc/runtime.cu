@@ -345,7 +345,9 @@ OSC_API int osc_synchronize(osc_ctx* ctx, int timeout_ms) {
   int word = 0;
   OSC_CUDA(cudaMemcpy(&word, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost), "read device error word");
   if (word != DEV_OK) {
-    OSC_CUDA(cudaMemset(ctx->d_err, 0, sizeof(int)), "reset device error word");
+    // also clears the grid-barrier counters that share the allocation (a kernel
+    // that gave up may have left them mid-count)
+    OSC_CUDA(cudaMemset(ctx->d_err, 0, 64), "reset device error word");
     if (word == DEV_ERR_TIMEOUT)
       return fail(OSC_ETIMEDOUT, "a kernel's bounded internal wait ran out (device error word %d)", word);
     return fail(OSC_EINVAL, "a kernel rejected its arguments (device error word %d)", word);

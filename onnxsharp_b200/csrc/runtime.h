@@ -24,7 +24,9 @@ struct osc_ctx {
   int num_sms = 0;
   cudaStream_t own_stream = nullptr;
   cudaStream_t stream = nullptr;  // where work is enqueued (own or caller's)
-  int* d_err = nullptr;           // device error word, written by kernels on failure
+  int* d_err = nullptr;           // device error word, written by kernels on failure;
+                                  // words 4..5 of the same 64-byte zeroed allocation are the
+                                  // arrival/departure counters of in-kernel grid barriers
   void* scratch = nullptr;        // grow-only per-call temporaries
   size_t scratch_bytes = 0;
   // Launch accounting and per-kernel event timing (osc_profile_*).
