@@ -296,6 +296,14 @@ OSC_API int osc_layernorm_f32(osc_ctx* ctx, const float* x, int outer, int inner
 OSC_API int osc_psa_attention_f32(osc_ctx* ctx, const float* qkv, long long qkv_nstride, int B, int heads, int kd,
                                   int hd, int T, float scale, float* out, long long out_nstride);
 
+/* Diagnostics (no counterpart in the reference): checks on the device that the
+ * branch-free reciprocal inside the fused Sigmoid/SiLU epilogues returns the
+ * same bits as the IEEE division 1/d for every float d in [1, 2^126) (the
+ * range of 1 + exp(-x) after the reference's clamp). *mismatches gets the
+ * count, *first_bad the first differing d's bits (0 if none); both are host
+ * pointers and the call synchronises the context's stream. */
+OSC_API int osc_selfcheck_recip(osc_ctx* ctx, unsigned long long* mismatches, unsigned int* first_bad);
+
 #ifdef __cplusplus
 }
 #endif

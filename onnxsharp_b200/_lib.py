@@ -67,6 +67,7 @@ SIGNATURES: dict[str, tuple] = {
     "osc_profile_read": (i32, [vp, C.c_char_p, C.POINTER(C.c_double), C.POINTER(i32)]),
     "osc_profile_reset": (i32, [vp]),
     "osc_launch_count": (C.c_ulonglong, [vp]),
+    "osc_selfcheck_recip": (i32, [vp, C.POINTER(C.c_ulonglong), C.POINTER(C.c_uint)]),
     "osc_graph_begin": (i32, [vp]),
     "osc_graph_end": (i32, [vp, pp]),
     "osc_graph_launch": (i32, [vp, vp]),

@@ -52,12 +52,14 @@ struct ConvTaps {
 
 struct ConvGeom {
   int N, M, OH, OW;   // output
-  int BW, BH;         // pixel box (BW * BH == 256)
+  int BW, BH;         // pixel box (BW * BH == 256, BW a power of two)
+  int bw_log2;
   int tiles_w, tiles_h;
   int act;
   long long y_nstride;      // elements between images of y (>= M*OH*OW: y may be a channel slice)
   const float* res;         // optional residual added after the activation (same geometry as y)
   long long res_nstride;
+  int vec4;                 // y (and res) rows allow 16-byte stores: OW, strides and bases multiples of 4 floats
 };
 
 __global__ void __launch_bounds__(ConvCfg::THREADS, 1)
@@ -127,19 +129,29 @@ __global__ void __launch_bounds__(ConvCfg::THREADS, 1)
 #pragma unroll
         for (int h = 0; h < Cfg::BN; h += 128) {
           const int p = h + lane * 4;  // 4 consecutive pixels of one box row (BW >= 8)
-          const int oy = oy0 + p / g.BW, ox = ox0 + p % g.BW;
+          const int oy = oy0 + (p >> g.bw_log2), ox = ox0 + (p & (g.BW - 1));
           if (oy >= g.OH) continue;
           const float4 s = *reinterpret_cast<const float4*>(stage + r * kPitch + p);
           float v[4] = {s.x, s.y, s.z, s.w};
           float* dst = yplane + static_cast<size_t>(oy) * g.OW + ox;
           const float* rsrc = rplane ? rplane + static_cast<size_t>(oy) * g.OW + ox : nullptr;
+          float o[4];
 #pragma unroll
-          for (int q = 0; q < 4; ++q)
-            if (ox + q < g.OW) {
-              float o = apply_act(__fadd_rn(v[q], b), g.act);
-              if (rsrc) o = __fadd_rn(rsrc[q], o);  // residual Add(x, act(conv)) as in the graph
-              dst[q] = o;
+          for (int q = 0; q < 4; ++q) o[q] = apply_act(__fadd_rn(v[q], b), g.act);
+          if (g.vec4 && ox + 4 <= g.OW) {  // one 16-byte store: whole 32-byte sectors per warp
+            if (rsrc) {
+              const float4 rv = __ldg(reinterpret_cast<const float4*>(rsrc));
+              o[0] = __fadd_rn(rv.x, o[0]);  // residual Add(x, act(conv)) as in the graph
+              o[1] = __fadd_rn(rv.y, o[1]);
+              o[2] = __fadd_rn(rv.z, o[2]);
+              o[3] = __fadd_rn(rv.w, o[3]);
             }
+            *reinterpret_cast<float4*>(dst) = make_float4(o[0], o[1], o[2], o[3]);
+          } else {
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              if (ox + q < g.OW) dst[q] = rsrc ? __fadd_rn(rsrc[q], o[q]) : o[q];
+          }
         }
       }
     }
@@ -325,6 +337,13 @@ int conv_tf32x3(osc_ctx* ctx, const float* x, long long x_nstride, int N, int C,
   g.res = res;
   g.res_nstride = res_nstride;
   choose_box(OH, OW, &g.BW, &g.BH);
+  g.bw_log2 = 0;
+  while ((1 << g.bw_log2) < g.BW) ++g.bw_log2;
+  {
+    auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+    g.vec4 = (OW % 4 == 0) && (y_nstride % 4 == 0) && al16(y) &&
+             (res == nullptr || (res_nstride % 4 == 0 && al16(res)));
+  }
   g.tiles_w = (OW + g.BW - 1) / g.BW;
   g.tiles_h = (OH + g.BH - 1) / g.BH;
   // 3. tensor maps
@@ -345,9 +364,9 @@ int conv_tf32x3(osc_ctx* ctx, const float* x, long long x_nstride, int N, int C,
     OSC_TRY(encode_tiled(&mXh, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, xh, dims, pitch, box, CU_TENSOR_MAP_SWIZZLE_128B));
     OSC_TRY(encode_tiled(&mXl, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, xl, dims, pitch, box, CU_TENSOR_MAP_SWIZZLE_128B));
   }
-  OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(k_conv_tf32x3), ConvCfg::SMEM_BYTES));
   const long tiles = static_cast<long>(g.tiles_w) * g.tiles_h * N;
   if (tiles > 2147483647L) return fail(OSC_EINVAL, "conv: too many tiles");
+  OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(k_conv_tf32x3), ConvCfg::SMEM_BYTES));
   dim3 grid(static_cast<unsigned>(tiles), (w->M + kBM - 1) / kBM);
   prof_begin(ctx);
   k_conv_tf32x3<<<grid, ConvCfg::THREADS, ConvCfg::SMEM_BYTES, ctx->stream>>>(mWh, mWl, mXh, mXl, taps, g, bias, y,

@@ -36,6 +36,55 @@ struct osc_gemm_weights {
 namespace osc {
 namespace {
 
+// Epilogue of one 128-row CTA tile: stage the drained accumulator in the
+// (free) operand ring, add the column bias (staged in shared memory once per
+// tile), apply the activation and write rows out with coalesced stores.
+template <class Cfg>
+__device__ __forceinline__ void gemm_epilogue(uint8_t* tiles, const float (&acc)[128], bool ok, int m0, int n0, int M,
+                                              int N, const float* __restrict__ col_bias, int act,
+                                              float* __restrict__ C, int ldc) {
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  if (ok) stage_tile<Cfg>(tiles, acc);
+  constexpr int kPitch = Cfg::BN + 4;
+  float* sbias = reinterpret_cast<float*>(tiles) + kBM * kPitch;
+  {
+    const int jj = threadIdx.x - 64;
+    sbias[jj] = (col_bias != nullptr && n0 + jj < N) ? __ldg(col_bias + n0 + jj) : 0.0f;
+  }
+  epi_sync<Cfg>();
+  if (!ok) return;
+  // Coalesced write-out: warp e copies rows e, e+EPI_WARPS, ...; lane l
+  // handles columns 4l.. of each 128-column half (bias + activation here).
+  const float* stage = reinterpret_cast<const float*>(tiles);
+  const int e = warp - 2;
+  const bool vec = ((ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(C) & 15u) == 0);
+  for (int r = e; r < kBM; r += Cfg::EPI_WARPS) {
+    const int row = m0 + r;
+    if (row >= M) break;
+    float* crow = C + static_cast<size_t>(row) * ldc;
+#pragma unroll
+    for (int h = 0; h < Cfg::BN; h += 128) {
+      const int c = n0 + h + lane * 4;
+      if (c >= N) continue;
+      const float4 sv = *reinterpret_cast<const float4*>(stage + r * kPitch + h + lane * 4);
+      float v[4] = {sv.x, sv.y, sv.z, sv.w};
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        if (col_bias != nullptr) v[t] = __fadd_rn(v[t], sbias[h + lane * 4 + t]);
+        v[t] = apply_act(v[t], act);
+      }
+      if (vec && c + 4 <= N) {
+        *reinterpret_cast<float4*>(crow + c) = make_float4(v[0], v[1], v[2], v[3]);
+      } else {
+#pragma unroll
+        for (int t = 0; t < 4; ++t)
+          if (c + t < N) crow[c + t] = v[t];
+      }
+    }
+  }
+}
+
 template <class Cfg>
 __global__ void __launch_bounds__(Cfg::THREADS, 1)
     k_gemm_tf32x3(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUtensorMap mAl,
@@ -73,49 +122,58 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
   } else {
     float acc[128];
     const bool ok = drain_loop<Cfg>(pb, tmem, num_kb, acc, err);
-    if (ok) stage_tile<Cfg>(tiles, acc);
-    constexpr int kPitch = Cfg::BN + 4;
-    // The tile's column bias goes to shared memory once (one epilogue thread
-    // per column) instead of one global load per element.
-    float* sbias = reinterpret_cast<float*>(tiles) + kBM * kPitch;
-    {
-      const int jj = threadIdx.x - 64;
-      sbias[jj] = (col_bias != nullptr && n0 + jj < N) ? __ldg(col_bias + n0 + jj) : 0.0f;
-    }
-    epi_sync<Cfg>();
-    if (ok) {
-      // Coalesced write-out: warp e copies rows e, e+EPI_WARPS, ...; lane l
-      // handles columns 4l.. of each 128-column half (bias + activation here).
-      const float* stage = reinterpret_cast<const float*>(tiles);
-      const int e = warp - 2;
-      const bool vec = ((ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(C) & 15u) == 0);
-      for (int r = e; r < kBM; r += Cfg::EPI_WARPS) {
-        const int row = m0 + r;
-        if (row >= M) break;
-        float* crow = C + static_cast<size_t>(row) * ldc;
-#pragma unroll
-        for (int h = 0; h < Cfg::BN; h += 128) {
-          const int c = n0 + h + lane * 4;
-          if (c >= N) continue;
-          const float4 s = *reinterpret_cast<const float4*>(stage + r * kPitch + h + lane * 4);
-          float v[4] = {s.x, s.y, s.z, s.w};
-#pragma unroll
-          for (int t = 0; t < 4; ++t) {
-            if (col_bias != nullptr) v[t] = __fadd_rn(v[t], sbias[h + lane * 4 + t]);
-            v[t] = apply_act(v[t], act);
-          }
-          if (vec && c + 4 <= N) {
-            *reinterpret_cast<float4*>(crow + c) = make_float4(v[0], v[1], v[2], v[3]);
-          } else {
-#pragma unroll
-            for (int t = 0; t < 4; ++t)
-              if (c + t < N) crow[c + t] = v[t];
-          }
-        }
-      }
-    }
+    gemm_epilogue<Cfg>(tiles, acc, ok, m0, n0, M, N, col_bias, act, C, ldc);
   }
   pipe_teardown<Cfg>(pb, tmem);
+}
+
+// CTA-pair form (cluster of 2, tcgen05 cta_group::2): the pair computes a
+// 256 x BN tile; CTA r of the pair owns rows m0 + 128r and loads columns
+// n0 + r*BN/2 .. of B, so each CTA streams 2/3 of the single-CTA operand bytes
+// for the same MMA work. Grid: x = 2 * column tiles (clusters of 2 along x),
+// y = 256-row tiles.
+template <class Cfg>
+__global__ void __launch_bounds__(Cfg::THREADS, 1)
+    k_gemm_tf32x3_pair(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUtensorMap mAl,
+                       const __grid_constant__ CUtensorMap mBh, const __grid_constant__ CUtensorMap mBl, int M, int N,
+                       int Kp, const float* __restrict__ col_bias, int act, float* __restrict__ C, int ldc,
+                       int* __restrict__ err) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* tiles = tiles_base<Cfg>(smem_raw);
+  PairBarriers* pb = pair_barriers<Cfg>(tiles);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int m0 = blockIdx.y * (2 * kBM) + static_cast<int>(rank) * kBM;
+  const int n0 = (blockIdx.x >> 1) * Cfg::BN;
+  const int nb = n0 + static_cast<int>(rank) * (Cfg::BN / 2);
+  const int num_kb = (Kp + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    tma_prefetch(&mAh);
+    tma_prefetch(&mAl);
+    tma_prefetch(&mBh);
+    tma_prefetch(&mBl);
+  }
+  const uint32_t tmem = pipe_setup_pair<Cfg>(pb);
+
+  if (warp == 0) {
+    if (lane == 0)
+      producer_loop_pair<Cfg>(tiles, pb, num_kb, rank, err, [&](int kb, uint8_t* st, uint32_t bar) {
+        const int kc = kb * kBK;
+        tma_load_2d_pair(st, &mAh, bar, kc, m0);
+        tma_load_2d_pair(st + Cfg::A_BYTES, &mAl, bar, kc, m0);
+        tma_load_2d_pair(st + 2 * Cfg::A_BYTES, &mBh, bar, kc, nb);
+        tma_load_2d_pair(st + 2 * Cfg::A_BYTES + Cfg::B_BYTES, &mBl, bar, kc, nb);
+      });
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) mma_loop_pair<Cfg>(tiles, pb, tmem, num_kb, err);
+  } else {
+    float acc[128];
+    const bool ok = drain_loop_pair<Cfg>(pb, tmem, num_kb, acc, err);
+    gemm_epilogue<Cfg>(tiles, acc, ok, m0, n0, M, N, col_bias, act, C, ldc);
+  }
+  pipe_teardown_pair<Cfg>(pb, tmem, rank, err);
 }
 
 // [rows][k] (row pitch ld) -> hi/lo [rows][kp], zero-padded for k <= c < kp.
@@ -192,6 +250,39 @@ int launch_gemm(osc_ctx* ctx, const float* ahi, const float* alo, int M, int Kp,
   return check_launch(ctx, "k_gemm_tf32x3");
 }
 
+template <class Cfg>
+int launch_gemm_pair(osc_ctx* ctx, const float* ahi, const float* alo, int M, int Kp, const osc_gemm_weights* w,
+                     const float* bias, int act, float* C, int ldc) {
+  CUtensorMap mAh, mAl, mBh, mBl;
+  const uint64_t dimsA[2] = {static_cast<uint64_t>(Kp), static_cast<uint64_t>(M)};
+  const uint64_t dimsB[2] = {static_cast<uint64_t>(Kp), static_cast<uint64_t>(w->n)};
+  const uint64_t pitch[1] = {static_cast<uint64_t>(Kp) * 4};
+  const uint32_t boxA[2] = {kBK, kBM};
+  const uint32_t boxB[2] = {kBK, static_cast<uint32_t>(Cfg::BN / 2)};
+  OSC_TRY(encode_tiled(&mAh, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, ahi, dimsA, pitch, boxA, CU_TENSOR_MAP_SWIZZLE_128B));
+  OSC_TRY(encode_tiled(&mAl, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, alo, dimsA, pitch, boxA, CU_TENSOR_MAP_SWIZZLE_128B));
+  OSC_TRY(encode_tiled(&mBh, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, w->hi, dimsB, pitch, boxB, CU_TENSOR_MAP_SWIZZLE_128B));
+  OSC_TRY(encode_tiled(&mBl, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, w->lo, dimsB, pitch, boxB, CU_TENSOR_MAP_SWIZZLE_128B));
+  auto kern = k_gemm_tf32x3_pair<Cfg>;
+  OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(kern), Cfg::SMEM_BYTES));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * ((w->n + Cfg::BN - 1) / Cfg::BN), (M + 2 * kBM - 1) / (2 * kBM));
+  cfg.blockDim = dim3(Cfg::THREADS);
+  cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+  cfg.stream = ctx->stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  prof_begin(ctx);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, mAh, mAl, mBh, mBl, M, w->n, Kp, bias, act, C, ldc, ctx->d_err);
+  if (e != cudaSuccess) return cuda_fail(e, "k_gemm_tf32x3_pair launch");
+  return check_launch(ctx, "k_gemm_tf32x3");
+}
+
 int grid_for(osc_ctx* ctx, size_t work, int per_thread) {
   size_t blocks = (work + static_cast<size_t>(256) * per_thread - 1) / (static_cast<size_t>(256) * per_thread);
   const size_t cap = static_cast<size_t>(ctx->num_sms) * 8;
@@ -229,6 +320,12 @@ int gemm_tf32x3(osc_ctx* ctx, const float* a, int m, int k, int lda, const osc_g
     const long tiles256 = static_cast<long>((w->n + 255) / 256) * ((m + kBM - 1) / kBM);
     bn = (tiles256 >= ctx->num_sms * 3 / 4 || w->n <= 128) ? (w->n <= 128 ? 128 : 256) : 128;
   }
+  static const bool pair_off = [] {
+    const char* v = std::getenv("OSC_GEMM_PAIR");
+    return v != nullptr && v[0] == '0';
+  }();
+  if (bn == 256 && !pair_off && m > kBM)
+    return launch_gemm_pair<Tf32x3PairCfg<256, 3, 2>>(ctx, ahi, alo, m, kp, w, col_bias, act, c, ldc);
   if (bn == 256) return launch_gemm<Tf32x3Cfg<256, 2, 2>>(ctx, ahi, alo, m, kp, w, col_bias, act, c, ldc);
   return launch_gemm<Tf32x3Cfg<128, 3, 2>>(ctx, ahi, alo, m, kp, w, col_bias, act, c, ldc);
 }

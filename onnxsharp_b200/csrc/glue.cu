@@ -828,12 +828,48 @@ __global__ void __launch_bounds__(256) k_psa_attention_smem(const float* __restr
   }
 }
 
+// Exhaustive check of recip_1up against the IEEE division over [1, 2^126).
+__global__ void k_selfcheck_recip(unsigned long long* mismatches, unsigned int* first_bad) {
+  const unsigned int lo = 0x3F800000u, hi = 0x7E800000u;  // bits of 1.0f and 2^126
+  unsigned long long bad = 0;
+  for (unsigned int i = lo + blockIdx.x * blockDim.x + threadIdx.x; i < hi; i += gridDim.x * blockDim.x) {
+    const float d = __uint_as_float(i);
+    if (__float_as_uint(recip_1up(d)) != __float_as_uint(__fdiv_rn(1.0f, d))) {
+      ++bad;
+      atomicMin(first_bad, i);
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) bad += __shfl_xor_sync(0xffffffffu, bad, o);
+  if ((threadIdx.x & 31) == 0 && bad) atomicAdd(mismatches, bad);
+}
+
 }  // namespace
 }  // namespace osc
 
 using namespace osc;
 
 extern "C" {
+
+OSC_API int osc_selfcheck_recip(osc_ctx* ctx, unsigned long long* mismatches, unsigned int* first_bad) {
+  OSC_TRY(enter(ctx));
+  if (mismatches == nullptr || first_bad == nullptr) return fail(OSC_EINVAL, "osc_selfcheck_recip: null output");
+  void* buf = nullptr;
+  OSC_TRY(scratch(ctx, 256, &buf));
+  auto* d_count = static_cast<unsigned long long*>(buf);
+  auto* d_first = reinterpret_cast<unsigned int*>(d_count + 1);
+  OSC_CUDA(cudaMemsetAsync(d_count, 0, sizeof(unsigned long long), ctx->stream), "selfcheck reset");
+  OSC_CUDA(cudaMemsetAsync(d_first, 0xFF, sizeof(unsigned int), ctx->stream), "selfcheck reset");
+  prof_begin(ctx);
+  k_selfcheck_recip<<<ctx->num_sms * 8, 256, 0, ctx->stream>>>(d_count, d_first);
+  OSC_TRY(check_launch(ctx, "k_selfcheck_recip"));
+  OSC_CUDA(cudaMemcpyAsync(mismatches, d_count, sizeof(unsigned long long), cudaMemcpyDeviceToHost, ctx->stream),
+           "selfcheck read");
+  OSC_CUDA(cudaMemcpyAsync(first_bad, d_first, sizeof(unsigned int), cudaMemcpyDeviceToHost, ctx->stream),
+           "selfcheck read");
+  OSC_CUDA(cudaStreamSynchronize(ctx->stream), "selfcheck sync");
+  if (*first_bad == 0xFFFFFFFFu) *first_bad = 0;
+  return OSC_OK;
+}
 
 OSC_API int osc_conv2d_direct_f32(osc_ctx* ctx, const float* x, long long x_nstride, int N, int C, int H, int W,
                                   const float* w, int M, int kh, int kw, int stride_h, int stride_w, int pad_t,

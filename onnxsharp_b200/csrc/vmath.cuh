@@ -5,7 +5,8 @@
 // Reference: src/OnnxSharp/Tensors/VectorMath.cs:21-43 (Exp: clamp to
 // [-87.3, 88.7], n = rint(x*log2e), two-step Cody-Waite reduction, degree-6
 // Horner polynomial with explicit FMAs, 2^n built from exponent bits),
-// :70-74 (Sigmoid = 1/(1+exp(-x))), :77 (Silu = x*sigmoid(x)).
+// :70-74 (Sigmoid = 1/(1+exp(-x)), the quotient correctly rounded as the
+// reference's IEEE division), :77 (Silu = x*sigmoid(x)).
 // Every operation uses an explicitly rounded intrinsic so nvcc cannot contract
 // or reorder it.
 #pragma once
@@ -31,8 +32,25 @@ __device__ __forceinline__ float ref_exp(float x) {
   return __fmul_rn(p, __int_as_float(e));
 }
 
+// Correctly rounded 1/d for d in [1, 2^126) without a branch: hardware
+// reciprocal approximation (rcp.approx.f32, relative error <= 2^-23), one
+// Newton-Raphson step and Markstein's final FMA correction
+// y = y1 + y1*(1 - d*y1) (P. Markstein, "IA-64 and Elementary Functions",
+// 2000). The sigmoid's divisor 1 + exp(-x) always lies in this range (the
+// exp argument is clamped to [-87.3, 88.7]), so the quotient is normal and
+// the result equals the IEEE division 1/d; tests/test_vmath_gpu.py checks
+// every float d in [1, 2^126) against __fdiv_rn(1, d).
+__device__ __forceinline__ float recip_1up(float d) {
+  float y;
+  asm("rcp.approx.f32 %0, %1;" : "=f"(y) : "f"(d));
+  const float e = __fmaf_rn(-d, y, 1.0f);
+  y = __fmaf_rn(y, e, y);
+  const float r = __fmaf_rn(-d, y, 1.0f);
+  return __fmaf_rn(y, r, y);
+}
+
 __device__ __forceinline__ float ref_sigmoid(float x) {
-  return __fdiv_rn(1.0f, __fadd_rn(1.0f, ref_exp(__fmul_rn(x, -1.0f))));
+  return recip_1up(__fadd_rn(1.0f, ref_exp(__fmul_rn(x, -1.0f))));
 }
 
 __device__ __forceinline__ float ref_silu(float x) { return __fmul_rn(x, ref_sigmoid(x)); }

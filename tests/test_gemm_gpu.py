@@ -54,6 +54,19 @@ def test_gemm_config1_full_size(ctx):
     assert rel_err(got, oracle.gemm(a, b, col_bias=bias)) <= TOL
 
 
+@pytest.mark.parametrize("m,k,n", [(2000, 300, 2000), (1800, 64, 3600), (4100, 1000, 1920)])
+def test_gemm_large_ragged_cta_pairs(ctx, m, k, n):
+    """Large GEMMs run on CTA pairs (cluster of 2, tcgen05 cta_group::2, 256 x 256
+    pair tiles); ragged M, N and K exercise the partial pair tiles."""
+    rng = np.random.default_rng(m + k + n)
+    a = rng.uniform(-1, 1, (m, k)).astype(np.float32)
+    b = rng.uniform(-1, 1, (k, n)).astype(np.float32)
+    bias = rng.uniform(-1, 1, n).astype(np.float32)
+    got = _run(ctx, a, b, bias)
+    ref = oracle.gemm(a, b, col_bias=bias)
+    assert rel_err(got, ref) <= TOL
+
+
 def test_gemm_golden_fixture(ctx, golden):
     got = _run(ctx, golden["gemm_a"], golden["gemm_b"], golden["gemm_bias"])
     assert rel_err(got, golden["gemm_c"]) <= TOL
