@@ -107,51 +107,51 @@ __global__ void __launch_bounds__(ConvCfg::THREADS, 1)
     if (lane == 0) mma_loop<Cfg>(tiles, pb, tmem, num_kb, err);
   } else {
     float acc[128];
-    const bool ok = drain_loop<Cfg>(pb, tmem, num_kb, acc, err);
-    if (ok) stage_tile<Cfg>(tiles, acc);
+    if (drain_loop<Cfg>(pb, tmem, num_kb, acc, err)) stage_tile<Cfg>(tiles, acc);
+    const int jj = threadIdx.x - 64;  // bias of this tile's 128 channels
+    if (jj < kBM)
+      reinterpret_cast<float*>(tiles)[kBM * (Cfg::BN + 4) + jj] =
+          (bias != nullptr && m0 + jj < g.M) ? __ldg(bias + m0 + jj) : 0.0f;
+  }
+  // All 10 warps (the producer and MMA warps are idle by now) write the staged
+  // tile out: bias + activation (+ residual) and 16-byte coalesced stores.
+  asm volatile("bar.sync 1, %0;" ::"r"(Cfg::THREADS) : "memory");
+  if (!pb->abort_flag) {
     constexpr int kPitch = Cfg::BN + 4;
-    float* sbias = reinterpret_cast<float*>(tiles) + kBM * kPitch;  // bias of this tile's 128 channels
-    {
-      const int jj = threadIdx.x - 64;
-      if (jj < kBM) sbias[jj] = (bias != nullptr && m0 + jj < g.M) ? __ldg(bias + m0 + jj) : 0.0f;
-    }
-    epi_sync<Cfg>();
-    if (ok) {
-      const float* stage = reinterpret_cast<const float*>(tiles);
-      const int e = warp - 2;
-      for (int r = e; r < kBM; r += Cfg::EPI_WARPS) {
-        const int oc = m0 + r;
-        if (oc >= g.M) break;
-        const float b = sbias[r];
-        const size_t plane_off = static_cast<size_t>(oc) * g.OH * g.OW;
-        float* yplane = y + static_cast<size_t>(n) * g.y_nstride + plane_off;
-        const float* rplane = g.res ? g.res + static_cast<size_t>(n) * g.res_nstride + plane_off : nullptr;
+    const float* stage = reinterpret_cast<const float*>(tiles);
+    const float* sbias = stage + kBM * kPitch;
+    for (int r = warp; r < kBM; r += Cfg::THREADS / 32) {
+      const int oc = m0 + r;
+      if (oc >= g.M) break;
+      const float b = sbias[r];
+      const size_t plane_off = static_cast<size_t>(oc) * g.OH * g.OW;
+      float* yplane = y + static_cast<size_t>(n) * g.y_nstride + plane_off;
+      const float* rplane = g.res ? g.res + static_cast<size_t>(n) * g.res_nstride + plane_off : nullptr;
 #pragma unroll
-        for (int h = 0; h < Cfg::BN; h += 128) {
-          const int p = h + lane * 4;  // 4 consecutive pixels of one box row (BW >= 8)
-          const int oy = oy0 + (p >> g.bw_log2), ox = ox0 + (p & (g.BW - 1));
-          if (oy >= g.OH) continue;
-          const float4 s = *reinterpret_cast<const float4*>(stage + r * kPitch + p);
-          float v[4] = {s.x, s.y, s.z, s.w};
-          float* dst = yplane + static_cast<size_t>(oy) * g.OW + ox;
-          const float* rsrc = rplane ? rplane + static_cast<size_t>(oy) * g.OW + ox : nullptr;
-          float o[4];
+      for (int h = 0; h < Cfg::BN; h += 128) {
+        const int p = h + lane * 4;  // 4 consecutive pixels of one box row (BW >= 8)
+        const int oy = oy0 + (p >> g.bw_log2), ox = ox0 + (p & (g.BW - 1));
+        if (oy >= g.OH) continue;
+        const float4 sv = *reinterpret_cast<const float4*>(stage + r * kPitch + p);
+        const float v[4] = {sv.x, sv.y, sv.z, sv.w};
+        float* dst = yplane + static_cast<size_t>(oy) * g.OW + ox;
+        const float* rsrc = rplane ? rplane + static_cast<size_t>(oy) * g.OW + ox : nullptr;
+        float o[4];
 #pragma unroll
-          for (int q = 0; q < 4; ++q) o[q] = apply_act(__fadd_rn(v[q], b), g.act);
-          if (g.vec4 && ox + 4 <= g.OW) {  // one 16-byte store: whole 32-byte sectors per warp
-            if (rsrc) {
-              const float4 rv = __ldg(reinterpret_cast<const float4*>(rsrc));
-              o[0] = __fadd_rn(rv.x, o[0]);  // residual Add(x, act(conv)) as in the graph
-              o[1] = __fadd_rn(rv.y, o[1]);
-              o[2] = __fadd_rn(rv.z, o[2]);
-              o[3] = __fadd_rn(rv.w, o[3]);
-            }
-            *reinterpret_cast<float4*>(dst) = make_float4(o[0], o[1], o[2], o[3]);
-          } else {
-#pragma unroll
-            for (int q = 0; q < 4; ++q)
-              if (ox + q < g.OW) dst[q] = rsrc ? __fadd_rn(rsrc[q], o[q]) : o[q];
+        for (int q = 0; q < 4; ++q) o[q] = apply_act(__fadd_rn(v[q], b), g.act);
+        if (g.vec4 && ox + 4 <= g.OW) {  // one 16-byte store: whole 32-byte sectors per warp
+          if (rsrc) {
+            const float4 rv = __ldg(reinterpret_cast<const float4*>(rsrc));
+            o[0] = __fadd_rn(rv.x, o[0]);  // residual Add(x, act(conv)) as in the graph
+            o[1] = __fadd_rn(rv.y, o[1]);
+            o[2] = __fadd_rn(rv.z, o[2]);
+            o[3] = __fadd_rn(rv.w, o[3]);
           }
+          *reinterpret_cast<float4*>(dst) = make_float4(o[0], o[1], o[2], o[3]);
+        } else {
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            if (ox + q < g.OW) dst[q] = rsrc ? __fadd_rn(rsrc[q], o[q]) : o[q];
         }
       }
     }

@@ -36,30 +36,33 @@ struct osc_gemm_weights {
 namespace osc {
 namespace {
 
-// Epilogue of one 128-row CTA tile: stage the drained accumulator in the
-// (free) operand ring, add the column bias (staged in shared memory once per
-// tile), apply the activation and write rows out with coalesced stores.
+// Epilogue of one 128-row CTA tile, in two parts. gemm_stage (epilogue warps):
+// the drained accumulator goes to the (free) operand ring at a pitch of BN+4
+// floats and the tile's column bias next to it. gemm_writeout (every warp of
+// the CTA, after a CTA-wide named barrier; the producer and MMA warps are
+// idle by then): bias + activation and coalesced 16-byte row stores.
 template <class Cfg>
-__device__ __forceinline__ void gemm_epilogue(uint8_t* tiles, const float (&acc)[128], bool ok, int m0, int n0, int M,
-                                              int N, const float* __restrict__ col_bias, int act,
-                                              float* __restrict__ C, int ldc) {
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
+__device__ __forceinline__ void gemm_stage(uint8_t* tiles, const float (&acc)[128], bool ok, int n0, int N,
+                                           const float* __restrict__ col_bias) {
   if (ok) stage_tile<Cfg>(tiles, acc);
   constexpr int kPitch = Cfg::BN + 4;
   float* sbias = reinterpret_cast<float*>(tiles) + kBM * kPitch;
-  {
-    const int jj = threadIdx.x - 64;
-    sbias[jj] = (col_bias != nullptr && n0 + jj < N) ? __ldg(col_bias + n0 + jj) : 0.0f;
-  }
-  epi_sync<Cfg>();
+  const int jj = threadIdx.x - 64;
+  sbias[jj] = (col_bias != nullptr && n0 + jj < N) ? __ldg(col_bias + n0 + jj) : 0.0f;
+}
+
+template <class Cfg>
+__device__ __forceinline__ void gemm_writeout(uint8_t* tiles, bool ok, int m0, int n0, int M, int N, bool has_bias,
+                                              int act, float* __restrict__ C, int ldc) {
+  asm volatile("bar.sync 1, %0;" ::"r"(Cfg::THREADS) : "memory");
   if (!ok) return;
-  // Coalesced write-out: warp e copies rows e, e+EPI_WARPS, ...; lane l
-  // handles columns 4l.. of each 128-column half (bias + activation here).
+  constexpr int kPitch = Cfg::BN + 4;
   const float* stage = reinterpret_cast<const float*>(tiles);
-  const int e = warp - 2;
+  const float* sbias = stage + kBM * kPitch;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
   const bool vec = ((ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(C) & 15u) == 0);
-  for (int r = e; r < kBM; r += Cfg::EPI_WARPS) {
+  for (int r = warp; r < kBM; r += Cfg::THREADS / 32) {
     const int row = m0 + r;
     if (row >= M) break;
     float* crow = C + static_cast<size_t>(row) * ldc;
@@ -71,7 +74,7 @@ __device__ __forceinline__ void gemm_epilogue(uint8_t* tiles, const float (&acc)
       float v[4] = {sv.x, sv.y, sv.z, sv.w};
 #pragma unroll
       for (int t = 0; t < 4; ++t) {
-        if (col_bias != nullptr) v[t] = __fadd_rn(v[t], sbias[h + lane * 4 + t]);
+        if (has_bias) v[t] = __fadd_rn(v[t], sbias[h + lane * 4 + t]);
         v[t] = apply_act(v[t], act);
       }
       if (vec && c + 4 <= N) {
@@ -122,8 +125,9 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
   } else {
     float acc[128];
     const bool ok = drain_loop<Cfg>(pb, tmem, num_kb, acc, err);
-    gemm_epilogue<Cfg>(tiles, acc, ok, m0, n0, M, N, col_bias, act, C, ldc);
+    gemm_stage<Cfg>(tiles, acc, ok, n0, N, col_bias);
   }
+  gemm_writeout<Cfg>(tiles, !pb->abort_flag, m0, n0, M, N, col_bias != nullptr, act, C, ldc);
   pipe_teardown<Cfg>(pb, tmem);
 }
 
@@ -171,8 +175,9 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
   } else {
     float acc[128];
     const bool ok = drain_loop_pair<Cfg>(pb, tmem, num_kb, acc, err);
-    gemm_epilogue<Cfg>(tiles, acc, ok, m0, n0, M, N, col_bias, act, C, ldc);
+    gemm_stage<Cfg>(tiles, acc, ok, n0, N, col_bias);
   }
+  gemm_writeout<Cfg>(tiles, !pb->abort_flag, m0, n0, M, N, col_bias != nullptr, act, C, ldc);
   pipe_teardown_pair<Cfg>(pb, tmem, rank, err);
 }
 

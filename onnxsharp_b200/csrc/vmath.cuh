@@ -18,7 +18,15 @@ namespace osc {
 __device__ __forceinline__ float ref_exp(float x) {
   // Avx.Max(x, c) returns c for NaN x, as fmaxf does.
   x = fminf(fmaxf(x, -87.3f), 88.7f);
-  const float n = rintf(__fmul_rn(x, 1.4426950408889634f));
+  // rint(x*log2e) by the round-to-nearest-even of an add to 1.5*2^23: for
+  // |v| < 2^22 the sum lies in [2^23, 2^24) where the float spacing is 1, so
+  // t = v + C rounds v to the nearest integer, ties to even, exactly as
+  // rint, and t - C is exact; the integer n also sits in t's low mantissa
+  // bits. Here |v| <= 128. Plain FP32 adds and integer ops instead of the
+  // quarter-rate round/convert instructions.
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+  const float t = __fadd_rn(__fmul_rn(x, 1.4426950408889634f), kRound);
+  const float n = __fsub_rn(t, kRound);
   float r = __fmaf_rn(n, -0.693145751953125f, x);
   r = __fmaf_rn(n, -1.4286067653e-6f, r);
   float p = 1.0f / 720.0f;
@@ -28,7 +36,7 @@ __device__ __forceinline__ float ref_exp(float x) {
   p = __fmaf_rn(p, r, 0.5f);
   p = __fmaf_rn(p, r, 1.0f);
   p = __fmaf_rn(p, r, 1.0f);
-  const int e = (__float2int_rn(n) + 127) << 23;
+  const int e = (__float_as_int(t) - 0x4B400000 + 127) << 23;  // (n + 127) << 23
   return __fmul_rn(p, __int_as_float(e));
 }
 
