@@ -34,11 +34,16 @@ namespace osc {
 namespace {
 
 constexpr int kAT = 128;                   // padded sequence length (TMEM lanes)
-constexpr int kAThreads = 6 * 32;          // warp 0 TMA, warp 1 MMA/TMEM, warps 2-5 compute
+constexpr int kACW = 16;                   // compute warps: 4 per TMEM lane quadrant, 32 keys each
+constexpr int kAThreads = (2 + kACW) * 32; // warp 0 TMA, warp 1 MMA/TMEM, warps 2-17 compute
 constexpr int kBox = kAT * 32 * 4;         // one [128][32] fp32 SW128 box = 16 KB
 constexpr int kRegion = 4 * kBox;          // hi (2 boxes) + lo (2 boxes) for D = 64
 constexpr int kVRaw = 2 * kBox;            // raw V as loaded: [128 keys][64 d] in two boxes
 constexpr int kVt = 2 * 4 * 64 * 128;      // V^T hi | lo: 4 key-blocks of [64 d][32 keys]
+// Softmax exchange (row maxima of the 4 key blocks, running lane sums, 1/sum):
+// kept in the tail of the raw-V region, free once V^T is split and dead
+// before the output staging reuses it.
+constexpr int kAXchg = 4 * kAT * 4 + kAT * 8 * 4 + kAT * 4;
 constexpr int kASmem = 2 * kRegion + kVRaw + kVt + 1024 + 256;
 static_assert(kASmem <= 232448, "attention shared memory budget");
 
@@ -86,6 +91,9 @@ __global__ void __launch_bounds__(kAThreads, 1)
   uint8_t* rk = smem + kRegion;       // K hi | K lo   (later P lo)
   uint8_t* rv = smem + 2 * kRegion;   // raw V [keys][d] (later the output staging tile)
   uint8_t* rvt = rv + kVRaw;          // V^T hi | lo, K-major over keys
+  float* xmax = reinterpret_cast<float*>(rv + kVRaw - kAXchg);  // [4 key blocks][128 rows] partial maxima
+  float* xlanes = xmax + 4 * kAT;                                // [128 rows][8] running lane sums
+  float* xpinv = xlanes + kAT * 8;                               // [128 rows] 1 / sum
   AttnBarriers* bar = reinterpret_cast<AttnBarriers*>(rvt + kVt);
   volatile int* abort_flag = &bar->abort_flag;
 
@@ -99,10 +107,10 @@ __global__ void __launch_bounds__(kAThreads, 1)
   if (threadIdx.x == 0) {
     mbar_init(&bar->full_qk, 1);
     mbar_init(&bar->full_v, 1);
-    mbar_init(&bar->qk_split, 4);
-    mbar_init(&bar->v_split, 4);
+    mbar_init(&bar->qk_split, kACW);
+    mbar_init(&bar->v_split, kACW);
     mbar_init(&bar->s_full, 1);
-    mbar_init(&bar->p_ready, 4);
+    mbar_init(&bar->p_ready, kACW);
     mbar_init(&bar->o_full, 1);
     bar->abort_flag = 0;
     fence_mbar_init();
@@ -173,15 +181,19 @@ __global__ void __launch_bounds__(kAThreads, 1)
       mma_commit(&bar->o_full);
     }
   } else {
-    const int ctid = threadIdx.x - 64;  // 0..127
-    const int q4 = warp & 3;
+    const int ctid = threadIdx.x - 64;  // 0..511
+    const int q4 = warp & 3;            // TMEM lane quadrant this warp may read
+    const int part = (warp - 2) >> 2;   // key block [32*part, 32*part + 32) of the row
     const int row = q4 * 32 + lane;     // query row == TMEM lane
+    constexpr int kCT = kACW * 32;
+    // named barrier 1: all compute warps
+    auto csync = [] { asm volatile("bar.sync 1, %0;" ::"n"(kACW * 32) : "memory"); };
     // 2. split Q (scaled) and K, then V.
     bool ok = mbar_wait(&bar->full_qk, 0, abort_flag, err);
     ok = __all_sync(0xffffffffu, ok);
     if (ok) {
-      split_inplace(reinterpret_cast<float*>(rq), half_bytes / 4, half_bytes / 16, args.scale, true, ctid, 128);
-      split_inplace(reinterpret_cast<float*>(rk), half_bytes / 4, half_bytes / 16, 1.0f, false, ctid, 128);
+      split_inplace(reinterpret_cast<float*>(rq), half_bytes / 4, half_bytes / 16, args.scale, true, ctid, kCT);
+      split_inplace(reinterpret_cast<float*>(rk), half_bytes / 4, half_bytes / 16, 1.0f, false, ctid, kCT);
       fence_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar->qk_split);
@@ -189,16 +201,16 @@ __global__ void __launch_bounds__(kAThreads, 1)
       ok = __all_sync(0xffffffffu, ok);
     }
     if (ok) {
-      // V^T split: thread ctid owns key ctid; reads its D values from the
-      // swizzled raw rows and scatters hi/lo into the K-major V^T blocks
-      // (a warp's 32 keys fill one 128-byte row of a block: no bank conflicts).
-      const int key = ctid;
+      // V^T split: thread (key, quarter) reads D/4 values of its key from the
+      // swizzled raw rows and scatters hi/lo into the K-major V^T blocks (a
+      // warp's 32 keys fill one 128-byte row of a block: no bank conflicts).
+      const int key = ctid & 127, dq = ctid >> 7;
       const int kb = key >> 5, kc = key & 31;
       const int vblk = D * 128;
       const float* raw = reinterpret_cast<const float*>(rv);
       float* vth = reinterpret_cast<float*>(rvt + kb * vblk);
       float* vtl = reinterpret_cast<float*>(rvt + 4 * vblk + kb * vblk);
-      for (int d = 0; d < D; ++d) {
+      for (int d = dq * (D / 4); d < (dq + 1) * (D / 4); ++d) {
         const int box = d >> 5, dc = d & 31;
         const float x = raw[(box * kBox + key * 128 + (((dc >> 2) ^ (key & 7)) << 4)) / 4 + (dc & 3)];
         const float hh = to_tf32(x);
@@ -209,108 +221,132 @@ __global__ void __launch_bounds__(kAThreads, 1)
       fence_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar->v_split);
+    }
+    // every compute warp takes the same barriers below, whatever `ok` says
+    csync();  // raw V is no longer read: its tail holds the softmax exchange
+    if (ok) {
       ok = mbar_wait(&bar->s_full, 0, abort_flag, err);
       ok = __all_sync(0xffffffffu, ok);
     }
-    float pinv = 0.0f;
+    float s[32];
+    const int j0 = part * 32;
     if (ok) {
       tc_fence_after();
-      float s[kAT];
-      const uint32_t base = tS + (static_cast<uint32_t>(q4 * 32) << 16);
+      uint32_t r[32];
+      tmem_ld32(tS + (static_cast<uint32_t>(q4 * 32) << 16) + static_cast<uint32_t>(j0), r);
+      tmem_wait_ld();
 #pragma unroll
-      for (int g = 0; g < kAT / 16; g += 2) {
-        uint32_t r0[16], r1[16];
-        tmem_ld16(base + g * 16, r0);
-        tmem_ld16(base + (g + 1) * 16, r1);
-        tmem_wait_ld();
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          s[g * 16 + j] = __uint_as_float(r0[j]);
-          s[(g + 1) * 16 + j] = __uint_as_float(r1[j]);
-        }
-      }
-      // 4. softmax of this row (keys >= T do not exist).
+      for (int j = 0; j < 32; ++j) s[j] = __uint_as_float(r[j]);
+      // 4. softmax of this row (keys >= T do not exist)
       if (args.mask != nullptr && row < T) {
         const float* mr = args.mask + (static_cast<size_t>(b) * args.mask_rows + (args.mask_rows == 1 ? 0 : row)) * T;
 #pragma unroll
-        for (int j = 0; j < kAT; ++j)
-          if (j < T) s[j] = __fadd_rn(s[j], __ldg(mr + j));
+        for (int j = 0; j < 32; ++j)
+          if (j0 + j < T) s[j] = __fadd_rn(s[j], __ldg(mr + j0 + j));
       }
       float mx = -INFINITY;
 #pragma unroll
-      for (int j = 0; j < kAT; ++j)
-        if (j < T) mx = fmaxf(mx, s[j]);
-      const int tv = T & ~7;  // vector part of VectorMath.SumExp
-      float lanes[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      for (int j = 0; j < 32; ++j)
+        if (j0 + j < T) mx = fmaxf(mx, s[j]);
+      xmax[part * kAT + row] = mx;
+    }
+    csync();
+    const int tv = T & ~7;  // vector part of VectorMath.SumExp
+    if (ok) {
+      const float mx = fmaxf(fmaxf(xmax[row], xmax[kAT + row]), fmaxf(xmax[2 * kAT + row], xmax[3 * kAT + row]));
 #pragma unroll
-      for (int j = 0; j < kAT; ++j) {
-        if (j < tv) {
-          s[j] = ref_exp(__fsub_rn(s[j], mx));
-          lanes[j & 7] = __fadd_rn(lanes[j & 7], s[j]);
-        }
+      for (int j = 0; j < 32; ++j) {
+        const int jj = j0 + j;
+        if (jj < tv) s[j] = ref_exp(__fsub_rn(s[j], mx));
+        else if (jj < T) s[j] = expf(__fsub_rn(s[j], mx));  // scalar tail: MathF.Exp
+        else s[j] = 0.0f;
       }
-      float total = 0.0f;
+      // e (unnormalised) -> P hi (over Q) / lo (over K): box `part` of 32 keys
 #pragma unroll
-      for (int l = 0; l < 8; ++l) total = __fadd_rn(total, lanes[l]);
+      for (int c = 0; c < 8; ++c) {
+        float hh[4], ll[4];
 #pragma unroll
-      for (int j = 0; j < kAT; ++j) {
-        if (j >= tv && j < T) {
-          s[j] = expf(__fsub_rn(s[j], mx));  // scalar tail: MathF.Exp
-          total = __fadd_rn(total, s[j]);
-        } else if (j >= T) {
-          s[j] = 0.0f;
+        for (int q = 0; q < 4; ++q) {
+          hh[q] = to_tf32(s[c * 4 + q]);
+          ll[q] = __fsub_rn(s[c * 4 + q], hh[q]);
         }
-      }
-      pinv = __fdiv_rn(1.0f, total);
-      // e (unnormalised) -> P hi (over Q) / lo (over K), K-major SW128 boxes of 32 keys.
-      uint8_t* ph = rq;
-      uint8_t* pl = rk;
-#pragma unroll
-      for (int kb = 0; kb < kAT / 32; ++kb) {
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          float hh[4], ll[4];
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const float v = s[kb * 32 + c * 4 + q];
-            hh[q] = to_tf32(v);
-            ll[q] = __fsub_rn(v, hh[q]);
-          }
-          const int off = kb * kBox + row * 128 + ((c ^ (row & 7)) << 4);
-          *reinterpret_cast<float4*>(ph + off) = make_float4(hh[0], hh[1], hh[2], hh[3]);
-          *reinterpret_cast<float4*>(pl + off) = make_float4(ll[0], ll[1], ll[2], ll[3]);
-        }
+        const int off = part * kBox + row * 128 + ((c ^ (row & 7)) << 4);
+        *reinterpret_cast<float4*>(rq + off) = make_float4(hh[0], hh[1], hh[2], hh[3]);
+        *reinterpret_cast<float4*>(rk + off) = make_float4(ll[0], ll[1], ll[2], ll[3]);
       }
       fence_async_smem();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar->p_ready);
+    }
+    // The row sum in the reference's order: 8 lane sums running over the
+    // keys in sequence (key block 0, then 1, 2, 3), then the lanes in order,
+    // then the scalar tail. The running sums pass from block to block through
+    // shared memory (named barriers 2..4 pair consecutive blocks).
+    {
+      float lanes[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      if (part > 0) {
+        asm volatile("bar.sync %0, %1;" ::"r"(1 + part), "n"(2 * 4 * 32) : "memory");
+#pragma unroll
+        for (int l = 0; l < 8; ++l) lanes[l] = xlanes[row * 8 + l];
+      }
+      if (ok) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (j0 + j < tv) lanes[j & 7] = __fadd_rn(lanes[j & 7], s[j]);
+      }
+      if (part < 3) {
+#pragma unroll
+        for (int l = 0; l < 8; ++l) xlanes[row * 8 + l] = lanes[l];
+        asm volatile("bar.arrive %0, %1;" ::"r"(2 + part), "n"(2 * 4 * 32) : "memory");
+      } else {
+        float total = 0.0f;
+#pragma unroll
+        for (int l = 0; l < 8; ++l) total = __fadd_rn(total, lanes[l]);
+        for (int j = tv; j < T; ++j) {  // the scalar tail, in key order (its e values live in other blocks)
+          const int pb = j >> 5, c = (j & 31) >> 2, qq = j & 3;
+          const int off = pb * kBox + row * 128 + ((c ^ (row & 7)) << 4) + qq * 4;
+          total = __fadd_rn(total, __fadd_rn(*reinterpret_cast<const float*>(rq + off),
+                                             *reinterpret_cast<const float*>(rk + off)));
+        }
+        xpinv[row] = __fdiv_rn(1.0f, total);
+      }
+    }
+    if (ok) {
       ok = mbar_wait(&bar->o_full, 0, abort_flag, err);
       ok = __all_sync(0xffffffffu, ok);
     }
-    // 5. O row -> * pinv -> staging (over V hi; the O MMA is complete) -> global.
+    csync();  // 1/sum of every row is in shared memory; O is complete
+    const float pinv = xpinv[row];
+    const bool all_ok = !*abort_flag;
+    csync();  // the exchange area is dead: the staging below overwrites it
+    // 5. O row -> * (1/sum) -> staging (over raw V and V^T; the O MMA is complete) -> global
     float* stage = reinterpret_cast<float*>(rv);
     const int pitch = D + 4;
-    if (ok) {
+    if (ok && all_ok) {
       tc_fence_after();
-      const uint32_t base = tO + (static_cast<uint32_t>(q4 * 32) << 16);
-      for (int g = 0; g < D / 16; ++g) {
-        uint32_t r[16];
-        tmem_ld16(base + g * 16, r);
+      const int dq = D / 4;  // this warp's output columns [part*dq, part*dq + dq)
+      const uint32_t base = tO + (static_cast<uint32_t>(q4 * 32) << 16) + static_cast<uint32_t>(part * dq);
+      for (int g = 0; g < dq; g += 8) {
+        uint32_t r[8];
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];\n"
+            : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+            : "r"(base + g));
         tmem_wait_ld();
 #pragma unroll
-        for (int j = 0; j < 16; j += 4)
-          *reinterpret_cast<float4*>(stage + row * pitch + g * 16 + j) =
+        for (int j = 0; j < 8; j += 4)
+          *reinterpret_cast<float4*>(stage + row * pitch + part * dq + g + j) =
               make_float4(__fmul_rn(__uint_as_float(r[j]), pinv), __fmul_rn(__uint_as_float(r[j + 1]), pinv),
                           __fmul_rn(__uint_as_float(r[j + 2]), pinv), __fmul_rn(__uint_as_float(r[j + 3]), pinv));
       }
     }
-    asm volatile("bar.sync 1, 128;" ::: "memory");
-    if (ok) {
-      // Each warp writes rows; a row is D floats = D/4 float4 (16 lanes for D = 64).
+    csync();
+    if (ok && all_ok) {
+      // rows of D floats = D/4 float4 (16 lanes for D = 64): 2 rows per warp instruction
       const int per_row = D / 4;
       const int rows_per_iter = 32 / per_row;
-      for (int r0 = (warp - 2) * rows_per_iter; r0 < T; r0 += 4 * rows_per_iter) {
+      for (int r0 = (warp - 2) * rows_per_iter; r0 < T; r0 += kACW * rows_per_iter) {
         const int r = r0 + lane / per_row;
         const int c = (lane % per_row) * 4;
         if (r < T) {
