@@ -296,6 +296,22 @@ OSC_API int osc_layernorm_f32(osc_ctx* ctx, const float* x, int outer, int inner
 OSC_API int osc_psa_attention_f32(osc_ctx* ctx, const float* qkv, long long qkv_nstride, int B, int heads, int kd,
                                   int hd, int T, float scale, float* out, long long out_nstride);
 
+/* DynamicQuantizeLinear as a standalone op (Ops/QuantOps.cs:155-231):
+ * x [count] f32 -> y [count] u8, *y_scale (f32) and *y_zero_point (u8), all
+ * device pointers (the scalars may be NULL). Same range, scale, zero point
+ * and rounding as osc_dqmm_f32's quantisation; NaN inputs give 0. */
+OSC_API int osc_dynamic_quantize_linear_f32(osc_ctx* ctx, const float* x, long long count, uint8_t* y,
+                                            float* y_scale, uint8_t* y_zero_point);
+
+/* MatMulInteger (Ops/QuantOps.cs:234-345, Kernels/Int8Gemm.cs:185-238):
+ * y [m, n] s32 = sum_t (a[i,t] - a_zero_point) * (W[t,j] - w_zp[j]) with A
+ * u8 (a_signed = 0) or s8 (a_signed = 1), row pitch lda bytes (0 = k), a
+ * scalar a_zero_point, and W prepacked by osc_dqmm_prepack (s8 or u8, per
+ * column or per tensor zero points). Exact integer arithmetic on the int8
+ * tensor cores. */
+OSC_API int osc_matmul_integer_i8(osc_ctx* ctx, const void* a, int a_signed, int m, int k, int lda, int a_zero_point,
+                                  const osc_dqmm_weights* w, int32_t* y);
+
 /* Diagnostics (no counterpart in the reference): checks on the device that the
  * branch-free reciprocal inside the fused Sigmoid/SiLU epilogues returns the
  * same bits as the IEEE division 1/d for every float d in [1, 2^126) (the

@@ -68,6 +68,8 @@ SIGNATURES: dict[str, tuple] = {
     "osc_profile_reset": (i32, [vp]),
     "osc_launch_count": (C.c_ulonglong, [vp]),
     "osc_selfcheck_recip": (i32, [vp, C.POINTER(C.c_ulonglong), C.POINTER(C.c_uint)]),
+    "osc_dynamic_quantize_linear_f32": (i32, [vp, vp, i64, vp, vp, vp]),
+    "osc_matmul_integer_i8": (i32, [vp, vp, i32, i32, i32, i32, i32, vp, vp]),
     "osc_graph_begin": (i32, [vp]),
     "osc_graph_end": (i32, [vp, pp]),
     "osc_graph_launch": (i32, [vp, vp]),

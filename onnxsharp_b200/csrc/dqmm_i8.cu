@@ -428,6 +428,65 @@ __global__ void __launch_bounds__(kDqlThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------- unfused ops
+// DynamicQuantizeLinear over a flat tensor (QuantOps.cs:155-231 via
+// Quantization.cs:68-103): q = clamp(rne(x * (1/scale)) + zp, 0, 255); NaN
+// inputs give 0 (the reference's saturating byte conversion of NaN). Block 0
+// also writes the scalar outputs y_scale (f32) and y_zero_point (u8).
+__global__ void k_quantize_flat(const float* __restrict__ x, long n, const QParams* __restrict__ qp,
+                                uint8_t* __restrict__ y, float* __restrict__ y_scale, uint8_t* __restrict__ y_zp) {
+  const float inv = qp->inverse;
+  const float zpf = static_cast<float>(qp->zp);
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    if (y_scale) *y_scale = qp->scale;
+    if (y_zp) *y_zp = static_cast<uint8_t>(qp->zp);
+  }
+  auto quant = [&](float v) -> uint32_t {
+    const float sv = __fmul_rn(v, inv);
+    if (sv != sv) return 0u;
+    return static_cast<uint32_t>(minps(255.0f, maxps(0.0f, __fadd_rn(rintf(sv), zpf))));
+  };
+  const bool vec = (reinterpret_cast<uintptr_t>(x) & 15u) == 0 && (reinterpret_cast<uintptr_t>(y) & 3u) == 0;
+  const long n4 = vec ? n / 4 : 0;
+  for (long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < n4;
+       i += static_cast<long>(gridDim.x) * blockDim.x) {
+    const float4 v = __ldg(reinterpret_cast<const float4*>(x) + i);
+    reinterpret_cast<uint32_t*>(y)[i] = quant(v.x) | (quant(v.y) << 8) | (quant(v.z) << 16) | (quant(v.w) << 24);
+  }
+  for (long i = n4 * 4 + blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long>(gridDim.x) * blockDim.x)
+    y[i] = static_cast<uint8_t>(quant(x[i]));
+}
+
+// MatMulInteger's activation side: the zero point goes into the same
+// QParams the int8 GEMM reads; per-row sums of A for the weight zero-point
+// correction (signed or unsigned bytes); no NaN rows.
+__global__ void k_set_qparams(QParams* __restrict__ qp, int zp) {
+  QParams p;
+  p.scale = 1.0f;
+  p.inverse = 1.0f;
+  p.zp = zp;
+  p.pad = 0;
+  *qp = p;
+}
+
+__global__ void k_rowsum_i8(const uint8_t* __restrict__ a, int m, int k, long long lda, int a_signed,
+                            int32_t* __restrict__ rowsum, int32_t* __restrict__ nanrow) {
+  const int warps = (blockDim.x >> 5) * gridDim.x;
+  const int lane = threadIdx.x & 31;
+  for (int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < m; r += warps) {
+    const uint8_t* ar = a + static_cast<size_t>(r) * lda;
+    int sum = 0;
+    for (int c = lane; c < k; c += 32) sum += a_signed ? static_cast<int>(static_cast<int8_t>(ar[c])) : ar[c];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (lane == 0) {
+      rowsum[r] = sum;
+      nanrow[r] = 0;
+    }
+  }
+}
+
 // Rows [0, grouped) went through the reference's 12/6/4-row micro-kernels
 // (fused FMA epilogue); see GemmKernel.cs:746-790.
 __host__ __device__ inline int grouped_rows(int m) {
@@ -452,6 +511,7 @@ struct DqmmArgs {
   float* y;
   int32_t* acc_out;
   int has_wzp;
+  int int_out;  // MatMulInteger: y receives the s32 accumulators (bit patterns) instead of the FP32 epilogue
 };
 
 __global__ void __launch_bounds__(kQThreads, 1)
@@ -618,7 +678,7 @@ __global__ void __launch_bounds__(kQThreads, 1)
               v = __fmul_rn(af, comb);
               if (args.bias) v = __fadd_rn(v, b);
             }
-            out[t] = nanr ? __int_as_float(0x7fc00000) : v;
+            out[t] = args.int_out ? __int_as_float(acc) : (nanr ? __int_as_float(0x7fc00000) : v);
           }
           if (j0 + 4 <= args.N && (args.N & 3) == 0) {
             *reinterpret_cast<float4*>(yr + j0) = make_float4(out[0], out[1], out[2], out[3]);
@@ -855,7 +915,15 @@ __global__ void __launch_bounds__(kPThreads, 1)
           if (lane == 0) mbar_arrive(&tempty[tb]);
         }
         float* obox = ocol + half * (kPBox / 4);
-        if (fast) {  // common case: every element is fma(acc, a_scale*w_scale[j], bias[j])
+        if (args.int_out) {  // MatMulInteger: the corrected s32 accumulators themselves
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            int32_t acc = static_cast<int32_t>(r[e]) + corr;
+            acc -= args.has_wzp ? wz * __shfl_sync(0xffffffffu, half == 0 ? my_rs_a : my_rs_b, e) : 0;
+            r[e] = static_cast<uint32_t>(acc);
+            obox[e * 32 + ((swz ^ (e & 7)) << 2)] = __int_as_float(acc);
+          }
+        } else if (fast) {  // common case: every element is fma(acc, a_scale*w_scale[j], bias[j])
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
             const int32_t acc = static_cast<int32_t>(r[e]) + corr;
@@ -875,7 +943,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
             obox[e * 32 + ((swz ^ (e & 7)) << 2)] = (half * 32 + e < nf && full_col) ? vf : vu;
           }
         }
-        if (any_nan) {  // rows whose input held a NaN are NaN throughout (rare)
+        if (any_nan && !args.int_out) {  // rows whose input held a NaN are NaN throughout (rare)
           const int nan_h = half == 0 ? my_nan_a : my_nan_b;
 #pragma unroll 1
           for (int e = 0; e < 32; ++e)
@@ -949,6 +1017,74 @@ static int minmax_params(osc_ctx* ctx, const float* a, long count, const float* 
   prof_begin(ctx);
   k_dql_params<<<1, 32, 0, ctx->stream>>>(part, blocks, override_mm, qp, params_out);
   return check_launch(ctx, "k_dql_params");
+}
+
+// The int8 GEMM of DynamicQuantizeMatMul and MatMulInteger: q [m][k] bytes
+// (row pitch q_pitch, the tensor map spans q_cols columns and zero-fills the
+// rest of the last 128-byte K block), prepacked weights, and the epilogue
+// described by `args` (FP32 with the reference's rounding, or s32 with
+// args.int_out). Persistent transposed tiles when y allows TMA stores.
+static int int8_gemm(osc_ctx* ctx, const uint8_t* q, size_t q_pitch, int q_cols, int q_signed, int m,
+                     const osc_dqmm_weights* w, DqmmArgs& args) {
+  float* y = args.y;
+  const uint32_t q_fmt = q_signed ? 1u : 0u;
+  CUtensorMap mQ, mW;
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(q_cols), static_cast<uint64_t>(m)};
+    const uint64_t pitch[1] = {static_cast<uint64_t>(q_pitch)};
+    const uint32_t box[2] = {kQBK, kQBM};
+    OSC_TRY(encode_tiled(&mQ, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, q, dims, pitch, box, CU_TENSOR_MAP_SWIZZLE_128B));
+  }
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(w->kp), static_cast<uint64_t>(w->n)};
+    const uint64_t pitch[1] = {static_cast<uint64_t>(w->kp)};
+    const uint32_t box[2] = {kQBK, kQBN};
+    OSC_TRY(encode_tiled(&mW, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, w->wt, dims, pitch, box, CU_TENSOR_MAP_SWIZZLE_128B));
+  }
+  const uint32_t b_fmt = w->is_signed ? 1u : 0u;
+  static const bool force_tiles = [] {
+    const char* e = std::getenv("OSC_DQMM_PERSISTENT");
+    return e != nullptr && e[0] == '0';
+  }();
+  if (!force_tiles && w->n % 4 == 0 && (reinterpret_cast<uintptr_t>(y) & 15u) == 0) {
+    // persistent transposed tiles with TMA stores (row pitch N*4 bytes is a multiple of 16)
+    CUtensorMap mQp, mY;
+    {
+      const uint64_t dims[2] = {static_cast<uint64_t>(q_cols), static_cast<uint64_t>(m)};
+      const uint64_t pitch[1] = {static_cast<uint64_t>(q_pitch)};
+      const uint32_t box[2] = {kQBK, kPBN};
+      OSC_TRY(encode_tiled(&mQp, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, q, dims, pitch, box, CU_TENSOR_MAP_SWIZZLE_128B));
+    }
+    CUtensorMap mWp;
+    {
+      const uint64_t dims[2] = {static_cast<uint64_t>(w->kp), static_cast<uint64_t>(w->n)};
+      const uint64_t pitch[1] = {static_cast<uint64_t>(w->kp)};
+      const uint32_t box[2] = {kQBK, kQBM};
+      OSC_TRY(encode_tiled(&mWp, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, w->wt, dims, pitch, box, CU_TENSOR_MAP_SWIZZLE_128B));
+    }
+    {
+      const uint64_t dims[2] = {static_cast<uint64_t>(w->n), static_cast<uint64_t>(m)};
+      const uint64_t pitch[1] = {static_cast<uint64_t>(w->n) * 4};
+      const uint32_t box[2] = {32, 32};
+      OSC_TRY(encode_tiled(&mY, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, y, dims, pitch, box, CU_TENSOR_MAP_SWIZZLE_128B));
+    }
+    // A = weights (s8 or u8), B = activations (u8 or s8); M = 128 columns, N = 128 rows
+    const uint32_t idesc_p = (2u << 4) | (b_fmt << 7) | (q_fmt << 10) | (static_cast<uint32_t>(kPBN >> 3) << 17) |
+                             (static_cast<uint32_t>(kQBM >> 4) << 24);
+    OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(k_dqmm_i8_persistent), kPSmem));
+    const int tiles = ((m + kPBN - 1) / kPBN) * ((w->n + kQBM - 1) / kQBM);
+    prof_begin(ctx);
+    k_dqmm_i8_persistent<<<std::min(tiles, ctx->num_sms), kPThreads, kPSmem, ctx->stream>>>(mQp, mWp, mY, args,
+                                                                                          idesc_p, ctx->d_err);
+    return check_launch(ctx, "k_dqmm_i8");
+  }
+  const uint32_t idesc = (2u << 4) | (q_fmt << 7) | (b_fmt << 10) |
+                         (static_cast<uint32_t>(kQBN >> 3) << 17) | (static_cast<uint32_t>(kQBM >> 4) << 24);
+  OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(k_dqmm_i8), kQSmem));
+  dim3 grid((w->n + kQBN - 1) / kQBN, (m + kQBM - 1) / kQBM);
+  prof_begin(ctx);
+  k_dqmm_i8<<<grid, kQThreads, kQSmem, ctx->stream>>>(mQ, mW, args, idesc, ctx->d_err);
+  return check_launch(ctx, "k_dqmm_i8");
 }
 
 }  // namespace osc
@@ -1103,19 +1239,6 @@ OSC_API int osc_dqmm_f32(osc_ctx* ctx, const float* a, int m, int k, int lda, co
   }
   if (q_out != nullptr)
     OSC_CUDA(cudaMemcpy2DAsync(q_out, k, q, kp, k, m, cudaMemcpyDeviceToDevice, ctx->stream), "copy q_out");
-  CUtensorMap mQ, mW;
-  {
-    const uint64_t dims[2] = {static_cast<uint64_t>(kp), static_cast<uint64_t>(m)};
-    const uint64_t pitch[1] = {static_cast<uint64_t>(kp)};
-    const uint32_t box[2] = {kQBK, kQBM};
-    OSC_TRY(encode_tiled(&mQ, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, q, dims, pitch, box, CU_TENSOR_MAP_SWIZZLE_128B));
-  }
-  {
-    const uint64_t dims[2] = {static_cast<uint64_t>(kp), static_cast<uint64_t>(w->n)};
-    const uint64_t pitch[1] = {static_cast<uint64_t>(kp)};
-    const uint32_t box[2] = {kQBK, kQBN};
-    OSC_TRY(encode_tiled(&mW, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, w->wt, dims, pitch, box, CU_TENSOR_MAP_SWIZZLE_128B));
-  }
   DqmmArgs args{};
   args.M = m;
   args.N = w->n;
@@ -1134,50 +1257,92 @@ OSC_API int osc_dqmm_f32(osc_ctx* ctx, const float* a, int m, int k, int lda, co
   args.y = y;
   args.acc_out = acc_out;
   args.has_wzp = w->has_zp;
-  const uint32_t b_fmt = w->is_signed ? 1u : 0u;
-  static const bool force_tiles = [] {
-    const char* e = std::getenv("OSC_DQMM_PERSISTENT");
-    return e != nullptr && e[0] == '0';
-  }();
-  if (!force_tiles && w->n % 4 == 0 && (reinterpret_cast<uintptr_t>(y) & 15u) == 0) {
-    // persistent transposed tiles with TMA stores (row pitch N*4 bytes is a multiple of 16)
-    CUtensorMap mQp, mY;
-    {
-      const uint64_t dims[2] = {static_cast<uint64_t>(kp), static_cast<uint64_t>(m)};
-      const uint64_t pitch[1] = {static_cast<uint64_t>(kp)};
-      const uint32_t box[2] = {kQBK, kPBN};
-      OSC_TRY(encode_tiled(&mQp, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, q, dims, pitch, box, CU_TENSOR_MAP_SWIZZLE_128B));
-    }
-    CUtensorMap mWp;
-    {
-      const uint64_t dims[2] = {static_cast<uint64_t>(kp), static_cast<uint64_t>(w->n)};
-      const uint64_t pitch[1] = {static_cast<uint64_t>(kp)};
-      const uint32_t box[2] = {kQBK, kQBM};
-      OSC_TRY(encode_tiled(&mWp, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, w->wt, dims, pitch, box, CU_TENSOR_MAP_SWIZZLE_128B));
-    }
-    {
-      const uint64_t dims[2] = {static_cast<uint64_t>(w->n), static_cast<uint64_t>(m)};
-      const uint64_t pitch[1] = {static_cast<uint64_t>(w->n) * 4};
-      const uint32_t box[2] = {32, 32};
-      OSC_TRY(encode_tiled(&mY, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, y, dims, pitch, box, CU_TENSOR_MAP_SWIZZLE_128B));
-    }
-    // A = weights (s8 or u8), B = quantised activations (u8); M = 128 columns, N = 128 rows
-    const uint32_t idesc_p = (2u << 4) | (b_fmt << 7) | (0u << 10) | (static_cast<uint32_t>(kPBN >> 3) << 17) |
-                             (static_cast<uint32_t>(kQBM >> 4) << 24);
-    OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(k_dqmm_i8_persistent), kPSmem));
-    const int tiles = ((m + kPBN - 1) / kPBN) * ((w->n + kQBM - 1) / kQBM);
-    prof_begin(ctx);
-    k_dqmm_i8_persistent<<<std::min(tiles, ctx->num_sms), kPThreads, kPSmem, ctx->stream>>>(mQp, mWp, mY, args,
-                                                                                          idesc_p, ctx->d_err);
-    return check_launch(ctx, "k_dqmm_i8");
-  }
-  const uint32_t idesc = (2u << 4) | (0u << 7) | (b_fmt << 10) |
-                         (static_cast<uint32_t>(kQBN >> 3) << 17) | (static_cast<uint32_t>(kQBM >> 4) << 24);
-  OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(k_dqmm_i8), kQSmem));
-  dim3 grid((w->n + kQBN - 1) / kQBN, (m + kQBM - 1) / kQBM);
+  args.int_out = 0;
+  return int8_gemm(ctx, q, kp, kp, 0, m, w, args);
+}
+
+OSC_API int osc_dynamic_quantize_linear_f32(osc_ctx* ctx, const float* x, long long count, uint8_t* y,
+                                            float* y_scale, uint8_t* y_zero_point) {
+  OSC_TRY(enter(ctx));
+  if (count < 0) return fail(OSC_EINVAL, "osc_dynamic_quantize_linear_f32: count=%lld", count);
+  if (count > 0 && (x == nullptr || y == nullptr))
+    return fail(OSC_EINVAL, "osc_dynamic_quantize_linear_f32: null pointer");
+  if (fault_injected("launch")) return fail(OSC_EFAULT_INJECTED, "injected failure (launch)");
+  void* buf = nullptr;
+  OSC_TRY(scratch(ctx, 8192 + 256, &buf));
+  uint8_t* base = static_cast<uint8_t*>(buf);
+  QParams* qp = reinterpret_cast<QParams*>(base + 8192);
+  // an empty tensor still has a range: {0, 0} -> scale 1, zero point 0
+  OSC_TRY(minmax_params(ctx, x, static_cast<long>(count), nullptr, base, qp, nullptr));
+  const int blocks = static_cast<int>(std::min<long long>(std::max<long long>((count / 4 + 255) / 256, 1),
+                                                          static_cast<long long>(ctx->num_sms) * 8));
   prof_begin(ctx);
-  k_dqmm_i8<<<grid, kQThreads, kQSmem, ctx->stream>>>(mQ, mW, args, idesc, ctx->d_err);
-  return check_launch(ctx, "k_dqmm_i8");
+  k_quantize_flat<<<blocks, 256, 0, ctx->stream>>>(x, static_cast<long>(count), qp, y, y_scale, y_zero_point);
+  return check_launch(ctx, "k_quantize_flat");
+}
+
+OSC_API int osc_matmul_integer_i8(osc_ctx* ctx, const void* a, int a_signed, int m, int k, int lda, int a_zero_point,
+                                  const osc_dqmm_weights* w, int32_t* y) {
+  OSC_TRY(enter(ctx));
+  if (w == nullptr) return fail(OSC_EINVAL, "osc_matmul_integer_i8: null weights");
+  if (w->device != ctx->device) return fail(OSC_EINVAL, "osc_matmul_integer_i8: weights live on another device");
+  if (k != w->k) return fail(OSC_EINVAL, "osc_matmul_integer_i8: A has k=%d, B has k=%d", k, w->k);
+  if (m < 0) return fail(OSC_EINVAL, "osc_matmul_integer_i8: m=%d", m);
+  if (lda == 0) lda = k;
+  if (lda < k) return fail(OSC_EINVAL, "osc_matmul_integer_i8: lda=%d < k=%d", lda, k);
+  if (a_signed ? (a_zero_point < -128 || a_zero_point > 127) : (a_zero_point < 0 || a_zero_point > 255))
+    return fail(OSC_EINVAL, "osc_matmul_integer_i8: a_zero_point %d out of range", a_zero_point);
+  if (m == 0) return OSC_OK;
+  if (a == nullptr || y == nullptr) return fail(OSC_EINVAL, "osc_matmul_integer_i8: null pointer");
+  if (fault_injected("launch")) return fail(OSC_EFAULT_INJECTED, "injected failure (launch)");
+  const int kp = w->kp;
+  // TMA reads A in place when its rows are 16-byte aligned; otherwise a pitched copy
+  const bool direct = (lda % 16) == 0 && (reinterpret_cast<uintptr_t>(a) & 15u) == 0;
+  const size_t off_params = 0, off_rs = 256;
+  const size_t off_nan = off_rs + round_up(sizeof(int32_t) * m, 256);
+  const size_t off_q = off_nan + round_up(sizeof(int32_t) * m, 256);
+  const size_t total = off_q + (direct ? 0 : round_up(static_cast<size_t>(m) * kp, 256));
+  void* buf = nullptr;
+  OSC_TRY(scratch(ctx, total, &buf));
+  uint8_t* base = static_cast<uint8_t*>(buf);
+  QParams* qp = reinterpret_cast<QParams*>(base + off_params);
+  int32_t* rowsum = reinterpret_cast<int32_t*>(base + off_rs);
+  int32_t* nanrow = reinterpret_cast<int32_t*>(base + off_nan);
+  const uint8_t* q = static_cast<const uint8_t*>(a);
+  size_t q_pitch = static_cast<size_t>(lda);
+  if (!direct) {
+    uint8_t* qc = base + off_q;
+    OSC_CUDA(cudaMemcpy2DAsync(qc, kp, a, lda, k, m, cudaMemcpyDeviceToDevice, ctx->stream), "copy A");
+    q = qc;
+    q_pitch = static_cast<size_t>(kp);
+  }
+  prof_begin(ctx);
+  k_set_qparams<<<1, 1, 0, ctx->stream>>>(qp, a_zero_point);
+  OSC_TRY(check_launch(ctx, "k_set_qparams"));
+  prof_begin(ctx);
+  k_rowsum_i8<<<std::min((m + 7) / 8, ctx->num_sms * 8), 256, 0, ctx->stream>>>(q, m, k, static_cast<long long>(q_pitch),
+                                                                              a_signed, rowsum, nanrow);
+  OSC_TRY(check_launch(ctx, "k_rowsum_i8"));
+  DqmmArgs args{};
+  args.M = m;
+  args.N = w->n;
+  args.K = k;
+  args.num_kb = kp / kQBK;
+  args.fused_rows = 0;
+  args.full_cols = 0;
+  args.qp = qp;
+  args.rowsum = rowsum;
+  args.nanrow = nanrow;
+  args.colsum = w->colsum;
+  args.wzp = w->zp;
+  args.wscale = &qp->scale;  // unused by the s32 epilogue, but a valid address (the kernels load it)
+  args.n_scale = 1;
+  args.bias = nullptr;
+  args.y = reinterpret_cast<float*>(y);
+  args.acc_out = nullptr;
+  args.has_wzp = w->has_zp;
+  args.int_out = 1;
+  return int8_gemm(ctx, q, q_pitch, k, a_signed, m, w, args);
 }
 
 }  // extern "C"

@@ -175,6 +175,34 @@ def dqmm(ctx: Context, a, w: DqmmWeights, w_scale, bias=None, out=None, minmax_o
     return out
 
 
+def dynamic_quantize_linear(ctx: Context, x, y=None, y_scale=None, y_zero_point=None):
+    """DynamicQuantizeLinear: (y u8 like x, y_scale f32 [1], y_zero_point u8 [1]) on the device."""
+    import torch
+
+    if y is None:
+        y = torch.empty(x.shape, dtype=torch.uint8, device=x.device)
+    if y_scale is None:
+        y_scale = torch.empty(1, dtype=torch.float32, device=x.device)
+    if y_zero_point is None:
+        y_zero_point = torch.empty(1, dtype=torch.uint8, device=x.device)
+    call("osc_dynamic_quantize_linear_f32", ctx.handle, ptr(x), int(x.numel()), ptr(y), ptr(y_scale),
+         ptr(y_zero_point))
+    return y, y_scale, y_zero_point
+
+
+def matmul_integer(ctx: Context, a, a_zero_point: int, w: "DqmmWeights", out=None):
+    """MatMulInteger: s32 [m, n] = (a - a_zero_point) @ (W - w_zp); a is a uint8 or int8 [m, k] device tensor."""
+    import torch
+
+    m = a.shape[0]
+    if out is None:
+        out = torch.empty((m, w.n), dtype=torch.int32, device=a.device)
+    signed = 1 if a.dtype == torch.int8 else 0
+    call("osc_matmul_integer_i8", ctx.handle, ptr(a), signed, int(m), w.k, int(a.stride(0)), int(a_zero_point),
+         w.handle, ptr(out))
+    return out
+
+
 def minmax(ctx: Context, x, out=None):
     """{min(x, 0), max(x, 0)} over all elements of x (NaN skipped), as a 2-float device tensor."""
     import torch

@@ -34,7 +34,7 @@ _SIGS = {
     "orc_dql_params": (None, [_flt, _flt, _f, C.POINTER(_int)]),
     "orc_quantize_u8": (None, [_vp, _long, _flt, _int, _vp, _int]),
     "orc_dqmm": (None, [_vp, _int, _int, _vp, _int, _vp, _int, _vp, _int, _vp, _int, _int, _vp, _vp, _vp, _vp, _int]),
-    "orc_matmul_integer": (None, [_vp, _int, _int, _int, _vp, _int, _vp, _int, _int, _vp, _int]),
+    "orc_matmul_integer": (None, [_vp, _int, _int, _int, _int, _vp, _int, _vp, _int, _int, _vp, _int]),
     "orc_conv2d": (None, [_vp, _int, _int, _int, _int, _vp, _int, _int, _int, _int, _int, _int, _int, _int, _int,
                           _int, _vp, _int, _vp, _int, _int, _int]),
     "orc_attention": (None, [_vp, _vp, _vp, _vp, _int, _int, _int, _int, _int, _flt, _int, _int, _int, _vp, _int]),
@@ -138,15 +138,18 @@ def dqmm(a, w, w_zp, w_scale, bias=None, mr12: int = 1, threads: int = THREADS):
     return y, q, acc, (float(params[0]), int(params[1]))
 
 
-def matmul_integer(a_u8, a_zp: int, w, w_zp, threads: int = THREADS):
-    a = np.ascontiguousarray(a_u8, dtype=np.uint8)
+def matmul_integer(a, a_zp: int, w, w_zp, threads: int = THREADS):
+    """MatMulInteger: s32 sum_t (a - a_zp)(w - w_zp[j]); a and w are uint8 or int8 arrays."""
+    a = np.ascontiguousarray(a)
+    assert a.dtype in (np.uint8, np.int8)
     w = np.ascontiguousarray(w)
     signed = 1 if w.dtype == np.int8 else 0
     zp = np.ascontiguousarray(np.atleast_1d(w_zp), dtype=np.int32)
     m, k = a.shape
     n = w.shape[1]
     acc = np.empty((m, n), np.int32)
-    lib().orc_matmul_integer(_p(a), m, k, a_zp, _p(w), signed, _p(zp), zp.size, n, _p(acc), threads)
+    lib().orc_matmul_integer(_p(a), 1 if a.dtype == np.int8 else 0, m, k, a_zp, _p(w), signed, _p(zp), zp.size, n,
+                             _p(acc), threads)
     return acc
 
 

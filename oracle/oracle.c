@@ -186,8 +186,8 @@ void orc_dqmm(const float* a, int m, int k, const void* w, int w_signed, const i
   free(combined);
 }
 
-void orc_matmul_integer(const uint8_t* a, int m, int k, int a_zp, const void* w, int w_signed, const int32_t* w_zp,
-                        int n_zp, int n, int32_t* acc, int threads) {
+void orc_matmul_integer(const void* a, int a_signed, int m, int k, int a_zp, const void* w, int w_signed,
+                        const int32_t* w_zp, int n_zp, int n, int32_t* acc, int threads) {
 #pragma omp parallel for num_threads(nthreads(threads)) schedule(static)
   for (int i = 0; i < m; ++i)
     for (int j = 0; j < n; ++j) {
@@ -195,7 +195,8 @@ void orc_matmul_integer(const uint8_t* a, int m, int k, int a_zp, const void* w,
       const int zpj = n_zp > 1 ? w_zp[j] : (n_zp == 1 ? w_zp[0] : 0);
       for (int t = 0; t < k; ++t) {
         const int wv = w_signed ? ((const int8_t*)w)[(size_t)t * n + j] : ((const uint8_t*)w)[(size_t)t * n + j];
-        s += (int64_t)((int)a[(size_t)i * k + t] - a_zp) * (wv - zpj);
+        const int av = a_signed ? ((const int8_t*)a)[(size_t)i * k + t] : ((const uint8_t*)a)[(size_t)i * k + t];
+        s += (int64_t)(av - a_zp) * (wv - zpj);
       }
       acc[(size_t)i * n + j] = (int32_t)s;
     }

@@ -61,8 +61,8 @@ void orc_dqmm(const float* a, int m, int k, const void* w, int w_signed, const i
 
 /* Exact integer MatMulInteger: acc[i,j] = sum_t (a[i,t]-a_zp) * (w[t,j]-w_zp[j])
  * (Kernels/Int8Gemm.cs:212-238, MultiplyIntegerScalar). */
-void orc_matmul_integer(const uint8_t* a, int m, int k, int a_zp, const void* w, int w_signed, const int32_t* w_zp,
-                        int n_zp, int n, int32_t* acc, int threads);
+void orc_matmul_integer(const void* a, int a_signed, int m, int k, int a_zp, const void* w, int w_signed,
+                        const int32_t* w_zp, int n_zp, int n, int32_t* acc, int threads);
 
 /* ConvKernels.Im2Col (Kernels/ConvKernels.cs:262-462, :525-654): NCHW, groups,
  * stride, dilation, pads; acc = bias[oc], then fmaf over K = (ic, ky, kx)
