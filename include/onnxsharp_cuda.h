@@ -296,6 +296,28 @@ OSC_API int osc_layernorm_f32(osc_ctx* ctx, const float* x, int outer, int inner
 OSC_API int osc_psa_attention_f32(osc_ctx* ctx, const float* qkv, long long qkv_nstride, int B, int heads, int kd,
                                   int hd, int T, float scale, float* out, long long out_nstride);
 
+/* Batched / transposed-view MatMul with a non-constant B (Ops/DnnOps.cs:2945-3094,
+ * the gemm_view strides folded in by Core/GraphFusion.cs:1424): for batch
+ * z = o * inner + i (o < outer, i < inner), y[z] [m, n] (dense) =
+ * A[z] [m, k] x B[z] [k, n] (+ col_bias [n]), element (r, c) of A[z] at
+ * a + o*a_outer + i*a_inner + r*a_row + c*a_col, element (t, j) of B[z] at
+ * b + o*b_outer + i*b_inner + t*b_row + j*b_col (strides in elements; 0
+ * broadcasts). 3xTF32. outer*inner <= 65535. */
+OSC_API int osc_matmul_batched_f32(osc_ctx* ctx, int outer, int inner, int m, int k, int n, const float* a,
+                                   long long a_outer, long long a_inner, long long a_row, long long a_col,
+                                   const float* b, long long b_outer, long long b_inner, long long b_row,
+                                   long long b_col, const float* col_bias, float* y);
+
+/* ONNX Gemm (Ops/AttnOps.cs:31-128): y [m, n] = alpha * A' B' + beta * C with
+ * A' = A [m, k] or A^T (trans_a, A stored [k, m]); B' from prepacked weights
+ * w (transB resolved by osc_gemm_prepack_f32's b_layout) or, with w = NULL,
+ * from a device B [k, n] (or [n, k] with trans_b). C (c_len elements, may be
+ * 0) broadcasts as the reference does: c_len >= m*n full, 1 scalar, else
+ * c[j % c_len]. The epilogue rounds alpha*acc, beta*c and their sum separately. */
+OSC_API int osc_gemm_onnx_f32(osc_ctx* ctx, const float* a, int trans_a, int m, int k, const osc_gemm_weights* w,
+                              const float* b, int trans_b, int n, float alpha, float beta, const float* c,
+                              long long c_len, float* y);
+
 /* DynamicQuantizeLinear as a standalone op (Ops/QuantOps.cs:155-231):
  * x [count] f32 -> y [count] u8, *y_scale (f32) and *y_zero_point (u8), all
  * device pointers (the scalars may be NULL). Same range, scale, zero point

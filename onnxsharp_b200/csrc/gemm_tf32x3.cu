@@ -181,6 +181,128 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
   pipe_teardown_pair<Cfg>(pb, tmem, rank, err);
 }
 
+// ------------------------------------------------------------ general / batched
+// Operands of a MatMul whose B is not a prepacked constant, of a batched
+// (or transposed-view) MatMul and of ONNX Gemm: any strided [batch][rows][K]
+// view is gathered into the K-major hi/lo layout the MMA reads, then a
+// batched kernel (3-D tensor maps over the batch) runs the same main loop.
+struct EpiAffine {
+  float alpha, beta;    // ONNX Gemm: y = alpha * acc + beta * C (as two rounded products and a rounded add)
+  const float* c;       // C broadcast as Gemm does: [M*N] full, 1 scalar, else c[j % c_len]
+  long long c_len;
+  long long y_bstride;  // elements between consecutive batches of y
+  long long y_ld;       // row pitch of y
+  int b_batched;        // B differs per batch (else batch 0 for all)
+};
+
+// src element (z, r, c) at src + (z / inner) * so + (z % inner) * si + r * sr + c * sc
+// -> hi/lo [z][r][kp] with c contiguous, zero for c >= cols. 32 x 32 tiles
+// through shared memory so both the read (along whichever source stride is 1)
+// and the write are coalesced.
+__global__ void k_gather_split(const float* __restrict__ src, int inner, long long so, long long si, long long sr,
+                               long long sc, int rows, int cols, int kp, float* __restrict__ hi,
+                               float* __restrict__ lo) {
+  __shared__ float tile[32][33];
+  const int z = blockIdx.z;
+  const int r0 = blockIdx.y * 32, c0 = blockIdx.x * 32;
+  const float* base = src + static_cast<long long>(z / inner) * so + static_cast<long long>(z % inner) * si;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8
+  const bool rows_contig = sr == 1 && sc != 1;
+  for (int yy = ty; yy < 32; yy += 8) {
+    // read: consecutive threads along the contiguous source dimension
+    const int r = rows_contig ? r0 + tx : r0 + yy;
+    const int c = rows_contig ? c0 + yy : c0 + tx;
+    const float v = (r < rows && c < cols) ? __ldg(base + r * sr + c * sc) : 0.0f;
+    if (rows_contig) tile[yy][tx] = v;  // tile[c][r]
+    else tile[tx][yy] = v;              // tile[c][r]
+  }
+  __syncthreads();
+  for (int yy = ty; yy < 32; yy += 8) {
+    const int r = r0 + yy, c = c0 + tx;
+    if (r < rows && c < kp) {
+      const float v = tile[tx][yy];
+      const float h = to_tf32(v);
+      const size_t o = (static_cast<size_t>(z) * rows + r) * kp + c;
+      hi[o] = h;
+      lo[o] = __fsub_rn(v, h);
+    }
+  }
+}
+
+template <class Cfg>
+__global__ void __launch_bounds__(Cfg::THREADS, 1)
+    k_gemm_tf32x3_batched(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUtensorMap mAl,
+                          const __grid_constant__ CUtensorMap mBh, const __grid_constant__ CUtensorMap mBl, int M,
+                          int N, int Kp, const float* __restrict__ col_bias, int act,
+                          const __grid_constant__ EpiAffine ep, float* __restrict__ Y, int* __restrict__ err) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* tiles = tiles_base<Cfg>(smem_raw);
+  PipeBarriers* pb = barriers<Cfg>(tiles);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int m0 = blockIdx.y * kBM;
+  const int n0 = blockIdx.x * Cfg::BN;
+  const int z = blockIdx.z, zb = ep.b_batched ? z : 0;
+  const int num_kb = (Kp + kBK - 1) / kBK;
+  if (threadIdx.x == 0) {
+    tma_prefetch(&mAh);
+    tma_prefetch(&mAl);
+    tma_prefetch(&mBh);
+    tma_prefetch(&mBl);
+  }
+  const uint32_t tmem = pipe_setup<Cfg>(pb);
+  if (warp == 0) {
+    if (lane == 0)
+      producer_loop<Cfg>(tiles, pb, num_kb, err, [&](int kb, uint8_t* st, uint64_t* bar) {
+        const int kc = kb * kBK;
+        tma_load_3d(st, &mAh, bar, kc, m0, z);
+        tma_load_3d(st + Cfg::A_BYTES, &mAl, bar, kc, m0, z);
+        tma_load_3d(st + 2 * Cfg::A_BYTES, &mBh, bar, kc, n0, zb);
+        tma_load_3d(st + 2 * Cfg::A_BYTES + Cfg::B_BYTES, &mBl, bar, kc, n0, zb);
+      });
+  } else if (warp == 1) {
+    if (lane == 0) mma_loop<Cfg>(tiles, pb, tmem, num_kb, err);
+  } else {
+    float acc[128];
+    const bool ok = drain_loop<Cfg>(pb, tmem, num_kb, acc, err);
+    gemm_stage<Cfg>(tiles, acc, ok, n0, N, col_bias);
+  }
+  asm volatile("bar.sync 1, %0;" ::"r"(Cfg::THREADS) : "memory");
+  if (!pb->abort_flag) {
+    constexpr int kPitch = Cfg::BN + 4;
+    const float* stage = reinterpret_cast<const float*>(tiles);
+    const float* sbias = stage + kBM * kPitch;
+    float* Yz = Y + static_cast<size_t>(z) * ep.y_bstride;
+    const bool affine = ep.alpha != 1.0f || (ep.beta != 0.0f && ep.c != nullptr && ep.c_len > 0);
+    const bool full_c = ep.c_len >= static_cast<long long>(M) * N;
+    for (int r = warp; r < kBM; r += Cfg::THREADS / 32) {
+      const int row = m0 + r;
+      if (row >= M) break;
+      float* yrow = Yz + static_cast<size_t>(row) * ep.y_ld;
+#pragma unroll
+      for (int h = 0; h < Cfg::BN; h += 128) {
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const int j = n0 + h + lane * 4 + t;
+          if (j >= N) break;
+          float v = stage[r * kPitch + h + lane * 4 + t];
+          if (col_bias != nullptr) v = __fadd_rn(v, sbias[h + lane * 4 + t]);
+          if (affine) {  // Gemm (AttnOps.cs:100-128): alpha * d, then + beta * c
+            if (ep.alpha != 1.0f) v = __fmul_rn(ep.alpha, v);
+            if (ep.beta != 0.0f && ep.c != nullptr && ep.c_len > 0) {
+              const float cv = full_c ? ep.c[static_cast<size_t>(row) * N + j]
+                                      : (ep.c_len == 1 ? ep.c[0] : ep.c[j % ep.c_len]);
+              v = __fadd_rn(v, __fmul_rn(ep.beta, cv));
+            }
+          }
+          yrow[j] = apply_act(v, act);
+        }
+      }
+    }
+  }
+  pipe_teardown<Cfg>(pb, tmem);
+}
+
 // [rows][k] (row pitch ld) -> hi/lo [rows][kp], zero-padded for k <= c < kp.
 __global__ void k_split_rows(const float* __restrict__ src, int rows, int k, int ld, int kp, float* __restrict__ hi,
                              float* __restrict__ lo) {
@@ -333,6 +455,43 @@ int gemm_tf32x3(osc_ctx* ctx, const float* a, int m, int k, int lda, const osc_g
     return launch_gemm_pair<Tf32x3PairCfg<256, 3, 2>>(ctx, ahi, alo, m, kp, w, col_bias, act, c, ldc);
   if (bn == 256) return launch_gemm<Tf32x3Cfg<256, 2, 2>>(ctx, ahi, alo, m, kp, w, col_bias, act, c, ldc);
   return launch_gemm<Tf32x3Cfg<128, 3, 2>>(ctx, ahi, alo, m, kp, w, col_bias, act, c, ldc);
+}
+
+// A strided view [batches][rows][cols] -> hi/lo [batches][rows][kp] in `dst_hi/lo`.
+static int gather_split(osc_ctx* ctx, const float* src, int batches, int inner, long long so, long long si,
+                        long long sr, long long sc, int rows, int cols, int kp, float* hi, float* lo) {
+  if (batches > 65535) return fail(OSC_EUNSUPPORTED, "matmul: %d batches (65535 at most)", batches);
+  dim3 grid((kp + 31) / 32, (rows + 31) / 32, batches);
+  prof_begin(ctx);
+  k_gather_split<<<grid, 256, 0, ctx->stream>>>(src, inner, so, si, sr, sc, rows, cols, kp, hi, lo);
+  return check_launch(ctx, "k_gather_split");
+}
+
+// C[z] = A[z] (M x K) * B[zb] (K x N) on split operands Ahi/lo [batches][M][Kp],
+// Bhi/lo [b_batches][N][Kp].
+static int gemm_batched(osc_ctx* ctx, const float* ahi, const float* alo, int batches, int M, int Kp,
+                        const float* bhi, const float* blo, int b_batches, int N, const float* col_bias, int act,
+                        const EpiAffine& ep, float* y) {
+  using Cfg = Tf32x3Cfg<128, 3, 2>;
+  CUtensorMap mAh, mAl, mBh, mBl;
+  const uint64_t dimsA[3] = {static_cast<uint64_t>(Kp), static_cast<uint64_t>(M), static_cast<uint64_t>(batches)};
+  const uint64_t dimsB[3] = {static_cast<uint64_t>(Kp), static_cast<uint64_t>(N), static_cast<uint64_t>(b_batches)};
+  const uint64_t pitchA[2] = {static_cast<uint64_t>(Kp) * 4, static_cast<uint64_t>(Kp) * 4 * M};
+  const uint64_t pitchB[2] = {static_cast<uint64_t>(Kp) * 4, static_cast<uint64_t>(Kp) * 4 * N};
+  const uint32_t boxA[3] = {kBK, kBM, 1};
+  const uint32_t boxB[3] = {kBK, static_cast<uint32_t>(Cfg::BN), 1};
+  OSC_TRY(encode_tiled(&mAh, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, ahi, dimsA, pitchA, boxA, CU_TENSOR_MAP_SWIZZLE_128B));
+  OSC_TRY(encode_tiled(&mAl, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, alo, dimsA, pitchA, boxA, CU_TENSOR_MAP_SWIZZLE_128B));
+  OSC_TRY(encode_tiled(&mBh, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, bhi, dimsB, pitchB, boxB, CU_TENSOR_MAP_SWIZZLE_128B));
+  OSC_TRY(encode_tiled(&mBl, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, blo, dimsB, pitchB, boxB, CU_TENSOR_MAP_SWIZZLE_128B));
+  auto kern = k_gemm_tf32x3_batched<Cfg>;
+  OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(kern), Cfg::SMEM_BYTES));
+  if (batches > 65535) return fail(OSC_EUNSUPPORTED, "matmul: %d batches (65535 at most)", batches);
+  dim3 grid((N + Cfg::BN - 1) / Cfg::BN, (M + kBM - 1) / kBM, batches);
+  prof_begin(ctx);
+  kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, ctx->stream>>>(mAh, mAl, mBh, mBl, M, N, Kp, col_bias, act, ep, y,
+                                                              ctx->d_err);
+  return check_launch(ctx, "k_gemm_tf32x3");
 }
 
 }  // namespace osc
@@ -545,6 +704,73 @@ OSC_API int osc_gemm_bias_f32_noalloc(osc_ctx* ctx, const float* a, int m, int k
   const bool wide = w->n > 128 && tiles256 >= ctx->num_sms * 3 / 4;
   if (wide) return launch_gemm_noalloc<Tf32x3Cfg<256, 2, 2>>(ctx, ahi, alo, m, kp, w, col_bias, act, c, ldc);
   return launch_gemm_noalloc<Tf32x3Cfg<128, 3, 2>>(ctx, ahi, alo, m, kp, w, col_bias, act, c, ldc);
+}
+
+OSC_API int osc_matmul_batched_f32(osc_ctx* ctx, int outer, int inner, int m, int k, int n, const float* a,
+                                   long long a_outer, long long a_inner, long long a_row, long long a_col,
+                                   const float* b, long long b_outer, long long b_inner, long long b_row,
+                                   long long b_col, const float* col_bias, float* y) {
+  OSC_TRY(enter(ctx));
+  if (outer < 0 || inner <= 0 || m < 0 || k <= 0 || n <= 0)
+    return fail(OSC_EINVAL, "osc_matmul_batched_f32: bad shape outer=%d inner=%d [%d,%d]x[%d,%d]", outer, inner, m,
+                k, k, n);
+  const long long batches = static_cast<long long>(outer) * inner;
+  if (batches == 0 || m == 0) return OSC_OK;
+  if (a == nullptr || b == nullptr || y == nullptr) return fail(OSC_EINVAL, "osc_matmul_batched_f32: null pointer");
+  if (batches > 65535) return fail(OSC_EUNSUPPORTED, "osc_matmul_batched_f32: %lld batches", batches);
+  if (fault_injected("launch")) return fail(OSC_EFAULT_INJECTED, "injected failure (launch)");
+  const int kp = static_cast<int>(round_up(static_cast<size_t>(k), 4));
+  const size_t abytes = round_up(static_cast<size_t>(batches) * m * kp * sizeof(float), 256);
+  const size_t bbytes = round_up(static_cast<size_t>(batches) * n * kp * sizeof(float), 256);
+  void* buf = nullptr;
+  OSC_TRY(scratch(ctx, 2 * abytes + 2 * bbytes, &buf));
+  uint8_t* p = static_cast<uint8_t*>(buf);
+  float* ahi = reinterpret_cast<float*>(p);
+  float* alo = reinterpret_cast<float*>(p + abytes);
+  float* bhi = reinterpret_cast<float*>(p + 2 * abytes);
+  float* blo = reinterpret_cast<float*>(p + 2 * abytes + bbytes);
+  const int nb = static_cast<int>(batches);
+  OSC_TRY(gather_split(ctx, a, nb, inner, a_outer, a_inner, a_row, a_col, m, k, kp, ahi, alo));
+  // B [k][n] with strides (b_row along k, b_col along n) -> K-major rows of n
+  OSC_TRY(gather_split(ctx, b, nb, inner, b_outer, b_inner, b_col, b_row, n, k, kp, bhi, blo));
+  EpiAffine ep{1.0f, 0.0f, nullptr, 0, static_cast<long long>(m) * n, n, 1};
+  return gemm_batched(ctx, ahi, alo, nb, m, kp, bhi, blo, nb, n, col_bias, OSC_ACT_NONE, ep, y);
+}
+
+OSC_API int osc_gemm_onnx_f32(osc_ctx* ctx, const float* a, int trans_a, int m, int k, const osc_gemm_weights* w,
+                              const float* b, int trans_b, int n, float alpha, float beta, const float* c,
+                              long long c_len, float* y) {
+  OSC_TRY(enter(ctx));
+  if (m < 0 || k <= 0) return fail(OSC_EINVAL, "osc_gemm_onnx_f32: bad shape m=%d k=%d", m, k);
+  if (w != nullptr) {
+    if (w->k != k) return fail(OSC_EINVAL, "osc_gemm_onnx_f32: A has k=%d, packed B has k=%d", k, w->k);
+    if (w->device != ctx->device) return fail(OSC_EINVAL, "osc_gemm_onnx_f32: weights live on another device");
+    n = w->n;
+  } else if (b == nullptr || n <= 0) {
+    return fail(OSC_EINVAL, "osc_gemm_onnx_f32: neither packed weights nor B");
+  }
+  if (c_len < 0) return fail(OSC_EINVAL, "osc_gemm_onnx_f32: c_len=%lld", c_len);
+  if (m == 0) return OSC_OK;
+  if (a == nullptr || y == nullptr || (c_len > 0 && c == nullptr))
+    return fail(OSC_EINVAL, "osc_gemm_onnx_f32: null pointer");
+  if (fault_injected("launch")) return fail(OSC_EFAULT_INJECTED, "injected failure (launch)");
+  const int kp = w != nullptr ? w->kp : static_cast<int>(round_up(static_cast<size_t>(k), 4));
+  const size_t abytes = round_up(static_cast<size_t>(m) * kp * sizeof(float), 256);
+  const size_t bbytes = w != nullptr ? 0 : round_up(static_cast<size_t>(n) * kp * sizeof(float), 256);
+  void* buf = nullptr;
+  OSC_TRY(scratch(ctx, 2 * abytes + 2 * bbytes, &buf));
+  uint8_t* p = static_cast<uint8_t*>(buf);
+  float* ahi = reinterpret_cast<float*>(p);
+  float* alo = reinterpret_cast<float*>(p + abytes);
+  // A stored [m][k] (or [k][m] with trans_a)
+  OSC_TRY(gather_split(ctx, a, 1, 1, 0, 0, trans_a ? 1 : k, trans_a ? m : 1, m, k, kp, ahi, alo));
+  const float* bhi = w != nullptr ? w->hi : reinterpret_cast<float*>(p + 2 * abytes);
+  const float* blo = w != nullptr ? w->lo : reinterpret_cast<float*>(p + 2 * abytes + bbytes);
+  if (w == nullptr)  // B stored [k][n] (or [n][k] with trans_b) -> K-major [n][kp]
+    OSC_TRY(gather_split(ctx, b, 1, 1, 0, 0, trans_b ? k : 1, trans_b ? 1 : n, n, k, kp, const_cast<float*>(bhi),
+                         const_cast<float*>(blo)));
+  EpiAffine ep{alpha, beta, c, c_len, 0, n, 0};
+  return gemm_batched(ctx, ahi, alo, 1, m, kp, bhi, blo, 1, n, nullptr, OSC_ACT_NONE, ep, y);
 }
 
 }  // extern "C"

@@ -175,6 +175,48 @@ def dqmm(ctx: Context, a, w: DqmmWeights, w_scale, bias=None, out=None, minmax_o
     return out
 
 
+def matmul_batched(ctx: Context, a, b, col_bias=None, out=None):
+    """Batched MatMul over torch views a [..., m, k] and b [..., k, n] (any strides, up to two batch
+    dimensions, size-1 or stride-0 batch dims broadcast); returns the dense [..., m, n] product."""
+    import torch
+
+    *ab, m, k = a.shape
+    *bb, k2, n = b.shape
+    if k2 != k:
+        raise ValueError(f"matmul_batched: K mismatch {tuple(a.shape)} x {tuple(b.shape)}")
+    nb = max(len(ab), len(bb))
+    if nb > 2:
+        raise ValueError("matmul_batched: at most two batch dimensions")
+    ab, bb = [1] * (nb - len(ab)) + list(ab), [1] * (nb - len(bb)) + list(bb)
+    batch = [max(x, y) for x, y in zip(ab, bb)]
+    a_st = [0] * (nb - (a.dim() - 2)) + list(a.stride()[:-2])
+    b_st = [0] * (nb - (b.dim() - 2)) + list(b.stride()[:-2])
+    a_st = [0 if ab[i] == 1 else a_st[i] for i in range(nb)]
+    b_st = [0 if bb[i] == 1 else b_st[i] for i in range(nb)]
+    outer, inner = ([1, 1] + batch)[-2:]
+    ao, ai = ([0, 0] + a_st)[-2:]
+    bo, bi = ([0, 0] + b_st)[-2:]
+    if out is None:
+        out = torch.empty(batch + [m, n], dtype=torch.float32, device=a.device)
+    call("osc_matmul_batched_f32", ctx.handle, outer, inner, m, k, n, ptr(a), ao, ai, a.stride(-2), a.stride(-1),
+         ptr(b), bo, bi, b.stride(-2), b.stride(-1), ptr(col_bias), ptr(out))
+    return out
+
+
+def gemm_onnx(ctx: Context, a, trans_a: bool, w=None, b=None, trans_b: bool = False, alpha: float = 1.0,
+              beta: float = 1.0, c=None, out=None):
+    """ONNX Gemm: alpha * A' B' + beta * C; B' from GemmWeights `w` or a device tensor `b`."""
+    import torch
+
+    m, k = (a.shape[1], a.shape[0]) if trans_a else (a.shape[0], a.shape[1])
+    n = w.n if w is not None else (b.shape[0] if trans_b else b.shape[1])
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.float32, device=a.device)
+    call("osc_gemm_onnx_f32", ctx.handle, ptr(a), int(trans_a), int(m), int(k), None if w is None else w.handle,
+         ptr(b), int(trans_b), int(n), float(alpha), float(beta), ptr(c), 0 if c is None else int(c.numel()), ptr(out))
+    return out
+
+
 def dynamic_quantize_linear(ctx: Context, x, y=None, y_scale=None, y_zero_point=None):
     """DynamicQuantizeLinear: (y u8 like x, y_scale f32 [1], y_zero_point u8 [1]) on the device."""
     import torch
