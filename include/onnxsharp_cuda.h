@@ -334,6 +334,29 @@ OSC_API int osc_dynamic_quantize_linear_f32(osc_ctx* ctx, const float* x, long l
 OSC_API int osc_matmul_integer_i8(osc_ctx* ctx, const void* a, int a_signed, int m, int k, int lda, int a_zero_point,
                                   const osc_dqmm_weights* w, int32_t* y);
 
+/* ImagePreprocessor.Letterbox (Vision/ImagePreprocessor.cs:57-100) on the device:
+ * u8 pixels [height][row_stride] (bytes_per_pixel 3 or 4; bgr = 1 for BGR(A)
+ * order) -> dst [3, target_h, target_w] f32 (a slice of the batch input):
+ * aspect-preserving bilinear resize (ImageGeometry.Contain, AxisMap.Bilinear),
+ * centred, pad 114/255, /255 normalisation; bit-identical to the reference.
+ * placement (host, may be NULL) gets {resized_w, resized_h, offset_x, offset_y}. */
+OSC_API int osc_letterbox_u8(osc_ctx* ctx, const uint8_t* pixels, int width, int height, int row_stride,
+                             int bytes_per_pixel, int bgr, int target_w, int target_h, float* dst, int* placement);
+
+/* The YOLO detect tail (YoloDecoder.Decode + DetectionNms.SuppressSorted,
+ * Vision/YoloDecoder.cs:68-188, Vision/Detection.cs:62-107) on the device, one
+ * image per CTA: output [B, fields, anchors] channels-first (fields = 4 +
+ * classes) -> dets [B, max_det, 6] (class, score, x, y, w, h) and counts [B].
+ * Candidates: first class maximum >= conf, finite, positive size; sorted by
+ * score (ties by anchor index); greedy NMS per class (or class_agnostic) with
+ * IoU > iou suppressing; at most max_candidates considered and max_det kept.
+ * transforms [B][6] (device, may be NULL) = {resized_w, resized_h, offset_x,
+ * offset_y, source_w, source_h} maps boxes back to source pixels (clamped,
+ * zero-area boxes dropped). anchors <= 16384, max_det <= 1024. */
+OSC_API int osc_yolo_detect_f32(osc_ctx* ctx, const float* output, int B, int fields, int anchors, float conf,
+                                float iou, int max_det, int max_candidates, int class_agnostic,
+                                const float* transforms, float* dets, int* counts);
+
 /* Diagnostics (no counterpart in the reference): checks on the device that the
  * branch-free reciprocal inside the fused Sigmoid/SiLU epilogues returns the
  * same bits as the IEEE division 1/d for every float d in [1, 2^126) (the

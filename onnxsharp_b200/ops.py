@@ -114,3 +114,26 @@ def yolo_decode(ctx, boxes, classes, strides, out):
     st = (C.c_float * 3)(*[float(s) for s in strides])
     call("osc_yolo_decode_f32", ctx.handle, B, nc, bp, bs, cp, cs, hs, ws, st, ptr(out))
     return out
+
+
+def letterbox(ctx, pixels, dst, bgr: bool = False):
+    """Letterbox an [H, W, 3|4] uint8 device image into dst [3, th, tw] (a slice of the batch
+    input); returns the placement (resized_w, resized_h, offset_x, offset_y)."""
+    h, w, bpp = pixels.shape
+    _, th, tw = dst.shape
+    pl = (C.c_int * 4)()
+    call("osc_letterbox_u8", ctx.handle, ptr(pixels), w, h, int(pixels.stride(0)), bpp, int(bgr), tw, th, ptr(dst), pl)
+    return tuple(pl)
+
+
+def yolo_detect(ctx, output, conf: float = 0.25, iou: float = 0.45, max_det: int = 300, max_candidates: int = 30000,
+                class_agnostic: bool = False, transforms=None):
+    """Detections of a [B, 4 + nc, A] output: (dets [B, max_det, 6] (class, score, x, y, w, h), counts [B])."""
+    import torch
+
+    B, fields, anchors = output.shape
+    dets = torch.zeros((B, max_det, 6), dtype=torch.float32, device=output.device)
+    counts = torch.zeros(B, dtype=torch.int32, device=output.device)
+    call("osc_yolo_detect_f32", ctx.handle, ptr(output), B, fields, anchors, float(conf), float(iou), max_det,
+         max_candidates, int(class_agnostic), ptr(transforms), ptr(dets), ptr(counts))
+    return dets, counts

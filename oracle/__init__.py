@@ -34,6 +34,7 @@ _SIGS = {
     "orc_dql_params": (None, [_flt, _flt, _f, C.POINTER(_int)]),
     "orc_quantize_u8": (None, [_vp, _long, _flt, _int, _vp, _int]),
     "orc_dqmm": (None, [_vp, _int, _int, _vp, _int, _vp, _int, _vp, _int, _vp, _int, _int, _vp, _vp, _vp, _vp, _int]),
+    "orc_letterbox": (None, [_vp, _int, _int, _int, _int, _int, _int, _int, _vp, _vp]),
     "orc_matmul_integer": (None, [_vp, _int, _int, _int, _int, _vp, _int, _vp, _int, _int, _vp, _int]),
     "orc_conv2d": (None, [_vp, _int, _int, _int, _int, _vp, _int, _int, _int, _int, _int, _int, _int, _int, _int,
                           _int, _vp, _int, _vp, _int, _int, _int]),
@@ -214,3 +215,14 @@ def layernorm(x, gamma=None, beta=None, eps: float = 1e-5, axis: int = -1, threa
     y = np.empty_like(x)
     lib().orc_layernorm(_p(x), outer, inner, _p(_c(gamma)), _p(_c(beta)), eps, _p(y), threads)
     return y
+
+
+def letterbox(pixels, bgr: bool = False, target=(640, 640), row_stride: int = 0):
+    """ImagePreprocessor.Letterbox of an [H, W, 3|4] uint8 image: ([3, th, tw] float32, (rw, rh, ox, oy))."""
+    px = np.ascontiguousarray(pixels, dtype=np.uint8)
+    h, w, bpp = px.shape
+    tw, th = target
+    dst = np.empty((3, th, tw), np.float32)
+    pl = np.zeros(4, np.int32)
+    lib().orc_letterbox(_p(px), w, h, row_stride or w * bpp, bpp, 1 if bgr else 0, tw, th, _p(dst), _p(pl))
+    return dst, tuple(int(v) for v in pl)

@@ -483,3 +483,43 @@ void orc_layernorm(const float* x, int outer, int inner, const float* gamma, con
     }
   }
 }
+
+/* ImageGeometry.Contain + AxisMap.Bilinear + ImageTensor.ToChw (see oracle.h). */
+void orc_letterbox(const uint8_t* pixels, int width, int height, int row_stride, int bytes_per_pixel, int bgr, int tw,
+                   int th, float* dst, int* placement) {
+  const float gx = (float)tw / (float)width, gy = (float)th / (float)height;
+  const float gain = gx < gy ? gx : gy; /* MathF.Min */
+  int rw = (int)nearbyintf((float)width * gain), rh = (int)nearbyintf((float)height * gain);
+  rw = rw < 1 ? 1 : (rw > tw ? tw : rw);
+  rh = rh < 1 ? 1 : (rh > th ? th : rh);
+  const int ox = (tw - rw) / 2, oy = (th - rh) / 2;
+  placement[0] = rw;
+  placement[1] = rh;
+  placement[2] = ox;
+  placement[3] = oy;
+  const float pad = 114.0f / 255.0f;
+  const float g = 1.0f / (255.0f * 1.0f);
+  const float bias = -0.0f / 1.0f;
+  const long plane = (long)th * tw;
+  for (long i = 0; i < 3 * plane; ++i) dst[i] = pad;
+  for (int dy = 0; dy < rh; ++dy) {
+    float sy = ((float)dy + 0.5f) * (float)height / (float)rh - 0.5f;
+    sy = sy < 0.0f ? 0.0f : (sy > (float)(height - 1) ? (float)(height - 1) : sy);
+    const int y0 = (int)sy, y1 = y0 + 1 < height - 1 ? y0 + 1 : height - 1;
+    const float fy = sy - (float)y0, omfy = 1.0f - fy;
+    for (int dx = 0; dx < rw; ++dx) {
+      float sx = ((float)dx + 0.5f) * (float)width / (float)rw - 0.5f;
+      sx = sx < 0.0f ? 0.0f : (sx > (float)(width - 1) ? (float)(width - 1) : sx);
+      const int x0 = (int)sx, x1 = x0 + 1 < width - 1 ? x0 + 1 : width - 1;
+      const float fx = sx - (float)x0, omfx = 1.0f - fx;
+      for (int c = 0; c < 3; ++c) {
+        const int co = bgr ? 2 - c : c;
+        const uint8_t* t = pixels + (long)y0 * row_stride;
+        const uint8_t* b = pixels + (long)y1 * row_stride;
+        const float top = (float)t[x0 * bytes_per_pixel + co] * omfx + (float)t[x1 * bytes_per_pixel + co] * fx;
+        const float bot = (float)b[x0 * bytes_per_pixel + co] * omfx + (float)b[x1 * bytes_per_pixel + co] * fx;
+        dst[c * plane + (long)(oy + dy) * tw + ox + dx] = (top * omfy + bot * fy) * g + bias;
+      }
+    }
+  }
+}

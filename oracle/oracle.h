@@ -92,6 +92,15 @@ void orc_dfl(const float* x, int B, int sides, int bins, int pixels, float* out,
 void orc_layernorm(const float* x, int outer, int inner, const float* gamma, const float* beta, float eps,
                    float* y, int threads);
 
+/* ImagePreprocessor.Letterbox (Vision/ImagePreprocessor.cs:57-100) with
+ * ImageGeometry.Contain (Imaging/AxisMap.cs:97-112), AxisMap.Bilinear
+ * (:22-40) and ImageTensor.ToChw (Imaging/ImageTensor.cs:13-170), Divide255
+ * normalisation: u8 pixels (bytes_per_pixel 3 or 4, channel c at byte
+ * offset bgr ? 2 - c : c) -> dst [3, th, tw], pad 114/255. placement gets
+ * {resized_w, resized_h, offset_x, offset_y}. */
+void orc_letterbox(const uint8_t* pixels, int width, int height, int row_stride, int bytes_per_pixel, int bgr, int tw,
+                   int th, float* dst, int* placement);
+
 #ifdef __cplusplus
 }
 #endif

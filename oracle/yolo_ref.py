@@ -155,3 +155,23 @@ def detect(output: np.ndarray, conf: float = 0.25, iou_thr: float = 0.45, max_de
             break
     _ = nc
     return kept
+
+
+def to_source(kept, placement, src_w: int, src_h: int) -> list[tuple]:
+    """YoloDecoder.Decode's last step (YoloDecoder.cs:170-186): letterbox boxes back to the
+    source image (Letterbox.ToSourceX/Y, ImagePreprocessor.cs:16-18), clamped, zero-area dropped."""
+    f = np.float32
+    rw, rh, ox, oy = placement
+    sx, sy = f(f(rw) / f(src_w)), f(f(rh) / f(src_h))
+    out = []
+    for cls, score, x, y, w, h, a in kept:
+        def clamp(v, hi):
+            return f(min(max(v, f(0)), f(hi)))
+        x1 = clamp(f(f(f(x) - f(ox)) / sx), src_w)
+        y1 = clamp(f(f(f(y) - f(oy)) / sy), src_h)
+        x2 = clamp(f(f(f(f(x) + f(w)) - f(ox)) / sx), src_w)
+        y2 = clamp(f(f(f(f(y) + f(h)) - f(oy)) / sy), src_h)
+        if x2 <= x1 or y2 <= y1:
+            continue
+        out.append((cls, score, float(x1), float(y1), float(f(x2 - x1)), float(f(y2 - y1)), a))
+    return out
