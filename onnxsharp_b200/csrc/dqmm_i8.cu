@@ -512,6 +512,7 @@ struct DqmmArgs {
   int32_t* acc_out;
   int has_wzp;
   int int_out;  // MatMulInteger: y receives the s32 accumulators (bit patterns) instead of the FP32 epilogue
+  int cpm;      // q-resident schedule: CTAs per 128-row block
 };
 
 __global__ void __launch_bounds__(kQThreads, 1)
@@ -720,6 +721,14 @@ constexpr int kPOut = kPEpiWarps * 2 * kPBox;                               // 6
 constexpr int kPThreads = 64 + kPEpiWarps * 32;
 constexpr int kPSmem = 1024 + kPRing + kPOut + 256;
 static_assert(kPSmem <= 227 * 1024, "persistent DQMM smem");
+// q-resident schedule (K <= 512): the CTA's 128 quantised rows stay in shared
+// memory (4 k-blocks, 64 KB) and only weight k-blocks stream through a
+// 6-stage ring (1.5 tiles ahead).
+constexpr int kRStages = 6, kRMaxKb = 4;
+constexpr int kRRes = kRMaxKb * kPB;                  // 64 KB
+constexpr int kRRing = kRStages * kPA;                // 96 KB
+constexpr int kRSmem = 1024 + kRRes + kRRing + kPOut + 256;
+static_assert(kRSmem <= 232448, "q-resident DQMM smem");
 
 // Barrier over the epilogue warps that also ANDs a predicate across them, so a
 // wait that gave up in one warp stops every epilogue warp at the same tile.
@@ -762,26 +771,46 @@ __device__ __forceinline__ ColRaw dqmm_col_load(const DqmmArgs& args, int j) {
 // tile i+1 while the epilogue drains tile i. Each epilogue warp writes its
 // 64 rows x 32 columns into 128-byte-swizzled boxes that one lane stores
 // with TMA tensor stores. Same arithmetic per element as k_dqmm_i8.
+template <bool QRES>
 __global__ void __launch_bounds__(kPThreads, 1)
     k_dqmm_i8_persistent(const __grid_constant__ CUtensorMap mQ, const __grid_constant__ CUtensorMap mW,
                          const __grid_constant__ CUtensorMap mY, const __grid_constant__ DqmmArgs args,
                          uint32_t idesc, int* __restrict__ err) {
+  constexpr int STAGES = QRES ? kRStages : kPStages;
+  constexpr int STAGE = QRES ? kPA : kPStage;  // q-resident: weight k-blocks only
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* ostage = ring + kPRing;
+  uint8_t* qres = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* ring = qres + (QRES ? kRRes : 0);
+  uint8_t* ostage = ring + STAGES * STAGE;
   uint64_t* full = reinterpret_cast<uint64_t*>(ostage + kPOut);
-  uint64_t* empty = full + kPStages;
-  uint64_t* tfull = empty + kPStages;
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* qfull = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(qfull + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int mt = (args.M + kPBN - 1) / kPBN;  // row tiles (the MMA's N side)
-  const int tiles = mt * ((args.N + kQBM - 1) / kQBM);
+  const int nt = (args.N + kQBM - 1) / kQBM;  // weight-column tiles
+  const int tiles = mt * nt;
   const int num_kb = args.num_kb;
+  // The CTA's tile lt: grid-strided over all tiles, or (q-resident) its own
+  // row block and every cpm-th column block.
+  auto tile_at = [&](int lt, int& m0, int& n0) -> bool {
+    if (QRES) {
+      const int mb = blockIdx.x / args.cpm, nb = static_cast<int>(blockIdx.x % args.cpm) + lt * args.cpm;
+      m0 = mb * kPBN;
+      n0 = nb * kQBM;
+      return mb < mt && nb < nt;
+    }
+    const int t = static_cast<int>(blockIdx.x) + lt * static_cast<int>(gridDim.x);
+    m0 = (t % mt) * kPBN;
+    n0 = (t / mt) * kQBM;
+    return t < tiles;
+  };
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kPStages; ++s) {
+    for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -789,6 +818,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], kPEpiWarps);
     }
+    mbar_init(qfull, 1);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch(&mQ);
@@ -807,46 +837,62 @@ __global__ void __launch_bounds__(kPThreads, 1)
   if (warp == 0) {
     if (lane == 0) {
       int g = 0, issued = 0;
-      for (int t = blockIdx.x; t < tiles && !*abort_flag; t += gridDim.x) {
-        const int m0 = (t % mt) * kPBN, n0 = (t / mt) * kQBM;
+      bool q_issued = false;
+      int m0, n0;
+      for (int lt = 0; tile_at(lt, m0, n0) && !*abort_flag; ++lt) {
+        if (QRES && !q_issued) {  // the CTA's quantised rows, once
+          mbar_arrive_expect_tx(qfull, num_kb * kPB);
+          for (int kb = 0; kb < num_kb; ++kb) tma_load_2d(qres + kb * kPB, &mQ, qfull, kb * kQBK, m0);
+          q_issued = true;
+        }
         for (int kb = 0; kb < num_kb; ++kb, ++g) {
-          const int s = g % kPStages;
-          if (!mbar_wait(&empty[s], ((g / kPStages) & 1u) ^ 1u, abort_flag, err)) break;
-          uint8_t* st = ring + s * kPStage;
-          mbar_arrive_expect_tx(&full[s], kPStage);
-          tma_load_2d(st, &mW, &full[s], kb * kQBK, n0);        // A: 128 weight columns
-          tma_load_2d(st + kPA, &mQ, &full[s], kb * kQBK, m0);  // B: 128 quantised rows
+          const int s = g % STAGES;
+          if (!mbar_wait(&empty[s], ((g / STAGES) & 1u) ^ 1u, abort_flag, err)) break;
+          uint8_t* st = ring + s * STAGE;
+          mbar_arrive_expect_tx(&full[s], STAGE);
+          tma_load_2d(st, &mW, &full[s], kb * kQBK, n0);           // A: 128 weight columns
+          if (!QRES) tma_load_2d(st + kPA, &mQ, &full[s], kb * kQBK, m0);  // B: 128 quantised rows
           issued = g + 1;
         }
       }
       if (*abort_flag) {  // let in-flight loads land before the CTA's shared memory goes away
-        for (int x = issued > kPStages ? issued - kPStages : 0; x < issued; ++x) {
+        for (int x = issued > STAGES ? issued - STAGES : 0; x < issued; ++x) {
           const uint64_t t0 = globaltimer_ns();
-          while (!mbar_try_wait(&full[x % kPStages], (x / kPStages) & 1u) &&
+          while (!mbar_try_wait(&full[x % STAGES], (x / STAGES) & 1u) &&
                  globaltimer_ns() - t0 < 50ull * 1000ull * 1000ull) {
+          }
+        }
+        if (q_issued) {
+          const uint64_t t0 = globaltimer_ns();
+          while (!mbar_try_wait(qfull, 0) && globaltimer_ns() - t0 < 50ull * 1000ull * 1000ull) {
           }
         }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      int g = 0, lt = 0;
-      for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++lt) {
+      int g = 0, m0, n0;
+      bool q_ready = !QRES;
+      for (int lt = 0; tile_at(lt, m0, n0); ++lt) {
         const int tb = lt & 1;
+        if (!q_ready) {
+          if (!mbar_wait(qfull, 0, abort_flag, err)) break;
+          q_ready = true;
+        }
         if (!mbar_wait(&tempty[tb], ((lt >> 1) & 1u) ^ 1u, abort_flag, err)) break;
         tc_fence_after();
         const uint32_t d = tmem + static_cast<uint32_t>(tb * kPBN);
         bool ok = true;
         for (int kb = 0; kb < num_kb; ++kb, ++g) {
-          const int s = g % kPStages;
-          if (!mbar_wait(&full[s], (g / kPStages) & 1u, abort_flag, err)) {
+          const int s = g % STAGES;
+          if (!mbar_wait(&full[s], (g / STAGES) & 1u, abort_flag, err)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t base = smem_addr(ring + s * kPStage);
+          const uint32_t base = smem_addr(ring + s * STAGE);
           const uint64_t dA = sdesc_kmajor_sw128(base);
-          const uint64_t dB = sdesc_kmajor_sw128(base + kPA);
+          const uint64_t dB = sdesc_kmajor_sw128(QRES ? smem_addr(qres + kb * kPB) : base + kPA);
 #pragma unroll
           for (int kk = 0; kk < kQBK / 32; ++kk) {
             const uint64_t off = static_cast<uint64_t>(kk * 2);
@@ -864,11 +910,10 @@ __global__ void __launch_bounds__(kPThreads, 1)
     const int h = ew >> 2;    // output rows 64h .. 64h+63 of the tile
     uint8_t* my_out = ostage + ew * 2 * kPBox;
     const QParams p = *args.qp;
-    int t = blockIdx.x;
     ColRaw raw{0, 0, 0.0f, 0.0f};
     int rs_a = 0, rs_b = 0, nan_a = 0, nan_b = 0;  // rows 64h + lane and 64h + 32 + lane
-    auto load_tile_inputs = [&](int tt) {
-      const int mm = (tt % mt) * kPBN + h * 64, nn = (tt / mt) * kQBM;
+    auto load_tile_inputs = [&](int mm, int nn) {
+      mm += h * 64;
       raw = dqmm_col_load(args, nn + q * 32 + lane);
       const int ia = mm + lane, ib = mm + 32 + lane;
       nan_a = ia < args.M ? __ldg(args.nanrow + ia) : 0;
@@ -878,10 +923,10 @@ __global__ void __launch_bounds__(kPThreads, 1)
         rs_b = ib < args.M ? __ldg(args.rowsum + ib) : 0;
       }
     };
-    if (t < tiles) load_tile_inputs(t);
-    for (int lt = 0; t < tiles; t += gridDim.x, ++lt) {
+    int m0, n0;
+    if (tile_at(0, m0, n0)) load_tile_inputs(m0, n0);
+    for (int lt = 0; tile_at(lt, m0, n0); ++lt) {
       const int tb = lt & 1;
-      const int m0 = (t % mt) * kPBN, n0 = (t / mt) * kQBM;
       const int j = n0 + q * 32 + lane;  // this thread's output column
       const int i0 = m0 + h * 64;        // first of this warp's 64 output rows
       const float comb = __fmul_rn(p.scale, raw.ws);
@@ -892,7 +937,10 @@ __global__ void __launch_bounds__(kPThreads, 1)
       const int my_rs_a = rs_a, my_rs_b = rs_b;
       const bool any_nan = __any_sync(0xffffffffu, (nan_a | nan_b) != 0);
       const int my_nan_a = nan_a, my_nan_b = nan_b;
-      if (t + static_cast<int>(gridDim.x) < tiles) load_tile_inputs(t + gridDim.x);  // in flight meanwhile
+      {
+        int mn, nn;
+        if (tile_at(lt + 1, mn, nn)) load_tile_inputs(mn, nn);  // in flight meanwhile
+      }
       if (!epi_all_dqmm(mbar_wait(&tfull[tb], (lt >> 1) & 1u, abort_flag, err))) break;
       tc_fence_after();
       if (lane == 0) bulk_wait_read_all();  // the previous tile's stores have read the staging
@@ -1071,11 +1119,24 @@ static int int8_gemm(osc_ctx* ctx, const uint8_t* q, size_t q_pitch, int q_cols,
     // A = weights (s8 or u8), B = activations (u8 or s8); M = 128 columns, N = 128 rows
     const uint32_t idesc_p = (2u << 4) | (b_fmt << 7) | (q_fmt << 10) | (static_cast<uint32_t>(kPBN >> 3) << 17) |
                              (static_cast<uint32_t>(kQBM >> 4) << 24);
-    OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(k_dqmm_i8_persistent), kPSmem));
-    const int tiles = ((m + kPBN - 1) / kPBN) * ((w->n + kQBM - 1) / kQBM);
+    const int mt = (m + kPBN - 1) / kPBN, nt = (w->n + kQBM - 1) / kQBM;
+    static const bool qres_off = [] {
+      const char* e = std::getenv("OSC_DQMM_QRES");
+      return e != nullptr && e[0] == '0';
+    }();
+    if (args.num_kb <= kRMaxKb && !qres_off) {
+      // q-resident: cpm CTAs share each 128-row block, each walking every cpm-th column block
+      args.cpm = std::max(1, std::min(nt, ctx->num_sms / std::max(1, mt)));
+      OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(k_dqmm_i8_persistent<true>), kRSmem));
+      prof_begin(ctx);
+      k_dqmm_i8_persistent<true><<<mt * args.cpm, kPThreads, kRSmem, ctx->stream>>>(mQp, mWp, mY, args, idesc_p,
+                                                                                    ctx->d_err);
+      return check_launch(ctx, "k_dqmm_i8");
+    }
+    OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(k_dqmm_i8_persistent<false>), kPSmem));
     prof_begin(ctx);
-    k_dqmm_i8_persistent<<<std::min(tiles, ctx->num_sms), kPThreads, kPSmem, ctx->stream>>>(mQp, mWp, mY, args,
-                                                                                          idesc_p, ctx->d_err);
+    k_dqmm_i8_persistent<false><<<std::min(mt * nt, ctx->num_sms), kPThreads, kPSmem, ctx->stream>>>(
+        mQp, mWp, mY, args, idesc_p, ctx->d_err);
     return check_launch(ctx, "k_dqmm_i8");
   }
   const uint32_t idesc = (2u << 4) | (q_fmt << 7) | (b_fmt << 10) |
