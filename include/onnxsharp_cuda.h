@@ -216,14 +216,16 @@ OSC_API int osc_dqmm_f32(osc_ctx* ctx, const float* a, int m, int k, int lda, co
  * skipped (Quantizer.MinMax). */
 OSC_API int osc_minmax_f32(osc_ctx* ctx, const float* x, long count, float* minmax_out);
 
-/* ------------------------------------------------------------ FusedAttention (T <= 128)
+/* ------------------------------------------------------------ FusedAttention
  * Replaces AttentionLayer.Forward (src/OnnxSharp/Ops/AttentionOps.cs:249-351),
  * heads form: q, k, v are [B, T, H*D] (the fused node's inputs
  * [Q, K, V, mask?] with attributes scale / heads / output_head_space,
  * GraphFusion.cs:1139-1162). out = softmax(scale*Q K^T + mask) V as
  * [B, T, H*D] (out_head_space = 0) or [B, H, T, D] (1). mask may be NULL or
- * [B, 1, mask_rows, T] with mask_rows 1 or T. Supported: T <= 128, D in {32, 64}
- * (one head per SM, QK^T / softmax / .V on chip; 3xTF32 tensor cores). */
+ * [B, 1, mask_rows, T] with mask_rows 1 or T. T <= 128 with D in {32, 64}: one
+ * head per SM, QK^T / softmax / .V on chip; otherwise (any T, any D) a composed
+ * path: batched QK^T, the reference's lazy softmax, e.V scaled by 1/sum. Both
+ * on the 3xTF32 tensor cores. */
 OSC_API int osc_attention_f32(osc_ctx* ctx, const float* q, const float* k, const float* v, const float* mask,
                               int mask_rows, int B, int T, int H, int D, float scale, int out_head_space,
                               float* out);

@@ -378,14 +378,15 @@ OSC_API int osc_attention_f32(osc_ctx* ctx, const float* q, const float* k, cons
                               float* out) {
   OSC_TRY(enter(ctx));
   if (B < 0 || T <= 0 || H <= 0 || D <= 0) return fail(OSC_EINVAL, "osc_attention_f32: bad shape");
-  if (T > kAT) return fail(OSC_EUNSUPPORTED, "osc_attention_f32: T=%d > %d (single-tile kernel)", T, kAT);
-  if (D != 32 && D != 64) return fail(OSC_EUNSUPPORTED, "osc_attention_f32: head dim %d (32 or 64 supported)", D);
   if (mask != nullptr && mask_rows != 1 && mask_rows != T)
     return fail(OSC_EINVAL, "osc_attention_f32: mask rows %d (1 or T)", mask_rows);
   if (B == 0) return OSC_OK;
   if (q == nullptr || k == nullptr || v == nullptr || out == nullptr)
     return fail(OSC_EINVAL, "osc_attention_f32: null pointer");
   if (fault_injected("launch")) return fail(OSC_EFAULT_INJECTED, "injected failure (launch)");
+  // one head resident per SM for T <= 128 and D in {32, 64}; otherwise the composed path
+  if (T > kAT || (D != 32 && D != 64))
+    return attention_composed(ctx, q, k, v, mask, mask_rows, B, T, H, D, scale, out_head_space, out);
   const int width = H * D;
   CUtensorMap mQ, mK, mV;
   const uint64_t dims[3] = {static_cast<uint64_t>(width), static_cast<uint64_t>(T), static_cast<uint64_t>(B)};

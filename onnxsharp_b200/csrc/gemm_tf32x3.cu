@@ -25,6 +25,7 @@
 #include "sm100.cuh"
 #include "tf32x3_core.cuh"
 #include "vmath.cuh"
+#include <algorithm>
 
 struct osc_gemm_weights {
   int device = 0;
@@ -187,12 +188,14 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
 // view is gathered into the K-major hi/lo layout the MMA reads, then a
 // batched kernel (3-D tensor maps over the batch) runs the same main loop.
 struct EpiAffine {
-  float alpha, beta;    // ONNX Gemm: y = alpha * acc + beta * C (as two rounded products and a rounded add)
-  const float* c;       // C broadcast as Gemm does: [M*N] full, 1 scalar, else c[j % c_len]
+  float alpha, beta;       // ONNX Gemm: y = alpha * acc + beta * C (as two rounded products and a rounded add)
+  const float* c;          // C broadcast as Gemm does: [M*N] full, 1 scalar, else c[j % c_len]
   long long c_len;
-  long long y_bstride;  // elements between consecutive batches of y
-  long long y_ld;       // row pitch of y
-  int b_batched;        // B differs per batch (else batch 0 for all)
+  long long y_outer, y_inner;  // y of batch z = o * inner + i starts at o * y_outer + i * y_inner
+  int inner;
+  long long y_ld;          // row pitch of y
+  int b_batched;           // B differs per batch (else batch 0 for all)
+  const float* row_scale;  // optional [batches][M]: y *= row_scale (FusedAttention's lazy 1/sum)
 };
 
 // src element (z, r, c) at src + (z / inner) * so + (z % inner) * si + r * sr + c * sc
@@ -272,13 +275,14 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
     constexpr int kPitch = Cfg::BN + 4;
     const float* stage = reinterpret_cast<const float*>(tiles);
     const float* sbias = stage + kBM * kPitch;
-    float* Yz = Y + static_cast<size_t>(z) * ep.y_bstride;
+    float* Yz = Y + static_cast<long long>(z / ep.inner) * ep.y_outer + static_cast<long long>(z % ep.inner) * ep.y_inner;
     const bool affine = ep.alpha != 1.0f || (ep.beta != 0.0f && ep.c != nullptr && ep.c_len > 0);
     const bool full_c = ep.c_len >= static_cast<long long>(M) * N;
     for (int r = warp; r < kBM; r += Cfg::THREADS / 32) {
       const int row = m0 + r;
       if (row >= M) break;
       float* yrow = Yz + static_cast<size_t>(row) * ep.y_ld;
+      const float rs = ep.row_scale != nullptr ? ep.row_scale[static_cast<size_t>(z) * M + row] : 1.0f;
 #pragma unroll
       for (int h = 0; h < Cfg::BN; h += 128) {
 #pragma unroll
@@ -295,6 +299,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
               v = __fadd_rn(v, __fmul_rn(ep.beta, cv));
             }
           }
+          if (ep.row_scale != nullptr) v = __fmul_rn(v, rs);
           yrow[j] = apply_act(v, act);
         }
       }
@@ -492,6 +497,139 @@ static int gemm_batched(osc_ctx* ctx, const float* ahi, const float* alo, int ba
   kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, ctx->stream>>>(mAh, mAl, mBh, mBl, M, N, Kp, col_bias, act, ep, y,
                                                               ctx->d_err);
   return check_launch(ctx, "k_gemm_tf32x3");
+}
+
+// Bytes of work space batched_strided needs for its split operands.
+static size_t batched_work_bytes(long long batches, int m, int k, int n) {
+  const size_t kp = round_up(static_cast<size_t>(k), 4);
+  return 2 * round_up(static_cast<size_t>(batches) * m * kp * sizeof(float), 256) +
+         2 * round_up(static_cast<size_t>(batches) * n * kp * sizeof(float), 256);
+}
+
+// Strided batched product into `y` with epilogue `ep` (its y strides), using
+// caller-provided `work` (batched_work_bytes) for the split operands.
+static int batched_strided(osc_ctx* ctx, int outer, int inner, int m, int k, int n, const float* a, long long a_outer,
+                           long long a_inner, long long a_row, long long a_col, const float* b, long long b_outer,
+                           long long b_inner, long long b_row, long long b_col, const float* col_bias,
+                           const EpiAffine& ep, float* y, void* work) {
+  const long long batches = static_cast<long long>(outer) * inner;
+  const int kp = static_cast<int>(round_up(static_cast<size_t>(k), 4));
+  const size_t abytes = round_up(static_cast<size_t>(batches) * m * kp * sizeof(float), 256);
+  const size_t bbytes = round_up(static_cast<size_t>(batches) * n * kp * sizeof(float), 256);
+  uint8_t* p = static_cast<uint8_t*>(work);
+  float* ahi = reinterpret_cast<float*>(p);
+  float* alo = reinterpret_cast<float*>(p + abytes);
+  float* bhi = reinterpret_cast<float*>(p + 2 * abytes);
+  float* blo = reinterpret_cast<float*>(p + 2 * abytes + bbytes);
+  const int nb = static_cast<int>(batches);
+  OSC_TRY(gather_split(ctx, a, nb, inner, a_outer, a_inner, a_row, a_col, m, k, kp, ahi, alo));
+  OSC_TRY(gather_split(ctx, b, nb, inner, b_outer, b_inner, b_col, b_row, n, k, kp, bhi, blo));
+  return gemm_batched(ctx, ahi, alo, nb, m, kp, bhi, blo, nb, n, col_bias, OSC_ACT_NONE, ep, y);
+}
+
+// y = x * s, each product rounded once (AttentionOps.cs:531-537: q' = q * scale).
+__global__ void k_scale_copy(const float* __restrict__ x, long long n, float s, float* __restrict__ y) {
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x)
+    y[i] = __fmul_rn(__ldg(x + i), s);
+}
+
+// The lazy softmax of AttentionOps.cs:590-604 on rows of S [B*H][T][T] in
+// place: optional additive mask, row max, e = exp(s - max) (the reference's
+// polynomial on the 8-aligned part, MathF.Exp on the tail) left unnormalised,
+// 1/sum per row (8 lane sums in key order, then the lanes, then the tail).
+__global__ void k_attn_rows(float* __restrict__ S, long long rows, int T, int H, const float* __restrict__ mask,
+                            int mask_rows, float* __restrict__ pinv) {
+  const int lane = threadIdx.x & 31;
+  const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
+  for (long long r = blockIdx.x * static_cast<long long>(blockDim.x >> 5) + (threadIdx.x >> 5); r < rows;
+       r += warps) {
+    float* sr = S + r * T;
+    const long long z = r / T;
+    const int t = static_cast<int>(r - z * T);
+    const int b = static_cast<int>(z / H);
+    if (mask != nullptr) {
+      const float* mr = mask + (static_cast<long long>(b) * mask_rows + (mask_rows == 1 ? 0 : t)) * T;
+      for (int j = lane; j < T; j += 32) sr[j] = __fadd_rn(sr[j], __ldg(mr + j));
+      __syncwarp();
+    }
+    float mx = -INFINITY;
+    for (int j = lane; j < T; j += 32) mx = fmaxf(mx, sr[j]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const int vend = T & ~7;
+    float part = 0.0f;
+    if (lane < 8)
+      for (int j = lane; j < vend; j += 8) {
+        const float e = ref_exp(__fsub_rn(sr[j], mx));
+        sr[j] = e;
+        part = __fadd_rn(part, e);
+      }
+    float total = 0.0f;
+    for (int l = 0; l < 8; ++l) total = __fadd_rn(total, __shfl_sync(0xffffffffu, part, l));
+    for (int j = vend; j < T; ++j) {  // scalar tail (uniform across the warp)
+      const float e = expf(__fsub_rn(sr[j], mx));
+      __syncwarp();
+      if (lane == 0) sr[j] = e;
+      total = __fadd_rn(total, e);
+    }
+    if (lane == 0) pinv[r] = __fdiv_rn(1.0f, total);
+  }
+}
+
+// FusedAttention for any T and head size: S = (q*scale) K^T per head on the
+// tensor cores, the lazy softmax above, O = e V with the 1/sum row scaling in
+// the product's epilogue (AttentionOps.cs:636-643), written straight into the
+// requested output layout.
+int attention_composed(osc_ctx* ctx, const float* q, const float* k, const float* v, const float* mask,
+                       int mask_rows, int B, int T, int H, int D, float scale, int out_head_space, float* out) {
+  const long long W = static_cast<long long>(H) * D;
+  const long long qn = static_cast<long long>(B) * T * W;
+  const long long sn = static_cast<long long>(B) * H * T * T;
+  const size_t q_bytes = round_up(static_cast<size_t>(qn) * 4, 256);
+  const size_t s_bytes = round_up(static_cast<size_t>(sn) * 4, 256);
+  const size_t p_bytes = round_up(static_cast<size_t>(B) * H * T * 4, 256);
+  const size_t w_bytes = std::max(batched_work_bytes(static_cast<long long>(B) * H, T, D, T),
+                                  batched_work_bytes(static_cast<long long>(B) * H, T, T, D));
+  void* buf = nullptr;
+  OSC_TRY(scratch(ctx, q_bytes + s_bytes + p_bytes + w_bytes, &buf));
+  uint8_t* base = static_cast<uint8_t*>(buf);
+  float* qs = reinterpret_cast<float*>(base);
+  float* S = reinterpret_cast<float*>(base + q_bytes);
+  float* pinv = reinterpret_cast<float*>(base + q_bytes + s_bytes);
+  void* work = base + q_bytes + s_bytes + p_bytes;
+  {
+    const int blocks = static_cast<int>(std::min<long long>((qn + 255) / 256, static_cast<long long>(ctx->num_sms) * 8));
+    prof_begin(ctx);
+    k_scale_copy<<<blocks, 256, 0, ctx->stream>>>(q, qn, scale, qs);
+    OSC_TRY(check_launch(ctx, "k_scale_copy"));
+  }
+  // S[b,h] = q'[b,:,h,:] K[b,:,h,:]^T : dense [B*H][T][T]
+  {
+    EpiAffine ep{1.0f, 0.0f, nullptr, 0, static_cast<long long>(H) * T * T, static_cast<long long>(T) * T, H, T, 1,
+                 nullptr};
+    OSC_TRY(batched_strided(ctx, B, H, T, D, T, qs, T * W, D, W, 1, k, T * W, D, 1, W, nullptr, ep, S, work));
+  }
+  {
+    const long long rows = static_cast<long long>(B) * H * T;
+    const int blocks = static_cast<int>(std::min<long long>((rows + 7) / 8, static_cast<long long>(ctx->num_sms) * 16));
+    prof_begin(ctx);
+    k_attn_rows<<<blocks, 256, 0, ctx->stream>>>(S, rows, T, H, mask, mask_rows, pinv);
+    OSC_TRY(check_launch(ctx, "k_attn_rows"));
+  }
+  // O[b,h] = e[b,h] V[b,:,h,:], times 1/sum per row, into [B,H,T,D] or [B,T,H*D]
+  EpiAffine ep{1.0f, 0.0f, nullptr, 0, 0, 0, H, 0, 1, pinv};
+  if (out_head_space) {
+    ep.y_outer = static_cast<long long>(H) * T * D;
+    ep.y_inner = static_cast<long long>(T) * D;
+    ep.y_ld = D;
+  } else {
+    ep.y_outer = T * W;
+    ep.y_inner = D;
+    ep.y_ld = W;
+  }
+  return batched_strided(ctx, B, H, T, T, D, S, static_cast<long long>(H) * T * T, static_cast<long long>(T) * T, T, 1,
+                         v, T * W, D, W, 1, nullptr, ep, out, work);
 }
 
 }  // namespace osc
@@ -719,22 +857,12 @@ OSC_API int osc_matmul_batched_f32(osc_ctx* ctx, int outer, int inner, int m, in
   if (a == nullptr || b == nullptr || y == nullptr) return fail(OSC_EINVAL, "osc_matmul_batched_f32: null pointer");
   if (batches > 65535) return fail(OSC_EUNSUPPORTED, "osc_matmul_batched_f32: %lld batches", batches);
   if (fault_injected("launch")) return fail(OSC_EFAULT_INJECTED, "injected failure (launch)");
-  const int kp = static_cast<int>(round_up(static_cast<size_t>(k), 4));
-  const size_t abytes = round_up(static_cast<size_t>(batches) * m * kp * sizeof(float), 256);
-  const size_t bbytes = round_up(static_cast<size_t>(batches) * n * kp * sizeof(float), 256);
   void* buf = nullptr;
-  OSC_TRY(scratch(ctx, 2 * abytes + 2 * bbytes, &buf));
-  uint8_t* p = static_cast<uint8_t*>(buf);
-  float* ahi = reinterpret_cast<float*>(p);
-  float* alo = reinterpret_cast<float*>(p + abytes);
-  float* bhi = reinterpret_cast<float*>(p + 2 * abytes);
-  float* blo = reinterpret_cast<float*>(p + 2 * abytes + bbytes);
-  const int nb = static_cast<int>(batches);
-  OSC_TRY(gather_split(ctx, a, nb, inner, a_outer, a_inner, a_row, a_col, m, k, kp, ahi, alo));
-  // B [k][n] with strides (b_row along k, b_col along n) -> K-major rows of n
-  OSC_TRY(gather_split(ctx, b, nb, inner, b_outer, b_inner, b_col, b_row, n, k, kp, bhi, blo));
-  EpiAffine ep{1.0f, 0.0f, nullptr, 0, static_cast<long long>(m) * n, n, 1};
-  return gemm_batched(ctx, ahi, alo, nb, m, kp, bhi, blo, nb, n, col_bias, OSC_ACT_NONE, ep, y);
+  OSC_TRY(scratch(ctx, batched_work_bytes(batches, m, k, n), &buf));
+  EpiAffine ep{1.0f, 0.0f, nullptr, 0, static_cast<long long>(inner) * m * n, static_cast<long long>(m) * n, inner, n,
+               1, nullptr};
+  return batched_strided(ctx, outer, inner, m, k, n, a, a_outer, a_inner, a_row, a_col, b, b_outer, b_inner, b_row,
+                         b_col, col_bias, ep, y, buf);
 }
 
 OSC_API int osc_gemm_onnx_f32(osc_ctx* ctx, const float* a, int trans_a, int m, int k, const osc_gemm_weights* w,
@@ -769,7 +897,7 @@ OSC_API int osc_gemm_onnx_f32(osc_ctx* ctx, const float* a, int trans_a, int m, 
   if (w == nullptr)  // B stored [k][n] (or [n][k] with trans_b) -> K-major [n][kp]
     OSC_TRY(gather_split(ctx, b, 1, 1, 0, 0, trans_b ? k : 1, trans_b ? 1 : n, n, k, kp, const_cast<float*>(bhi),
                          const_cast<float*>(blo)));
-  EpiAffine ep{alpha, beta, c, c_len, 0, n, 0};
+  EpiAffine ep{alpha, beta, c, c_len, 0, 0, 1, n, 0, nullptr};
   return gemm_batched(ctx, ahi, alo, 1, m, kp, bhi, blo, 1, n, nullptr, OSC_ACT_NONE, ep, y);
 }
 

@@ -53,6 +53,11 @@ bool fault_injected(const char* site);
 // Makes `ctx->device` current; returns OSC_OK or an error code.
 int enter(osc_ctx* ctx);
 
+// FusedAttention for T > 128 or head sizes other than 32 / 64, composed of
+// tensor-core batched products and a row softmax (gemm_tf32x3.cu).
+int attention_composed(osc_ctx* ctx, const float* q, const float* k, const float* v, const float* mask,
+                       int mask_rows, int B, int T, int H, int D, float scale, int out_head_space, float* out);
+
 // Scratch arena of at least `bytes`, 256-byte aligned. Fails during stream
 // capture if it would have to grow.
 int scratch(osc_ctx* ctx, size_t bytes, void** out);

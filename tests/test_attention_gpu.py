@@ -1,4 +1,5 @@
-"""FusedAttention (T <= 128) on the B200 against the oracle's restatement of
+"""FusedAttention on the B200 (one head per SM for T <= 128; a composed
+tensor-core path for longer sequences and other head sizes) against the oracle's restatement of
 AttentionLayer (ComputeBlocks for T > 64, ComputeRows otherwise). Tolerance:
 max |d| <= 1e-5 absolute (the reference's attention golden, AttentionTests.cs)
 and |d| / max(1, |ref|) <= 1e-4."""
@@ -93,12 +94,34 @@ def test_attention_block_with_projections(ctx):
     assert rel_err(yd.cpu().numpy(), y) <= 1e-4
 
 
-def test_attention_rejects_long_sequences(ctx):
+def test_attention_rejects_bad_mask_rows(ctx):
+    """A mask must be [B, 1, 1|T, T] (AttentionOps.cs:249-351)."""
     import torch
 
     from onnxsharp_b200 import OscError
     from onnxsharp_b200.runtime import attention
 
     z = torch.zeros(1, 129, 64, device="cuda")
+    m = torch.zeros(1, 1, 7, 129, device="cuda")
     with pytest.raises(OscError):
-        attention(ctx, z, z, z, 1, 0.125)
+        attention(ctx, z, z, z, 1, 0.125, m)
+
+
+@pytest.mark.parametrize("B,T,H,D,mask_rows,head_space", [
+    (2, 200, 2, 64, 0, False),     # beyond one 128-key tile
+    (1, 1000, 4, 32, 1, True),     # long sequence, [B,1,1,T] key mask, head-space output
+    (1, 300, 3, 48, 300, False),   # head size outside {32, 64}, full [B,1,T,T] mask
+    (2, 64, 2, 16, 0, False),      # short sequence, small head (composed path by head size)
+    (1, 4096, 1, 64, 0, False),    # the fusion limit (GraphFusion admits T <= 4096)
+])
+def test_attention_long_sequences(ctx, B, T, H, D, mask_rows, head_space):
+    """T > 128 and other head sizes take the composed path (tensor-core QK^T and
+    e.V, the reference's lazy softmax with its 8-lane sum order in between)."""
+    q, k, v = _qkv(T + D, B, T, H * D)
+    mask = None
+    if mask_rows:
+        rng = np.random.default_rng(T)
+        mask = np.where(rng.uniform(0, 1, (B, 1, mask_rows, T)) < 0.2, -1e4, 0.0).astype(np.float32)
+    s = 1.0 / np.sqrt(D)
+    _check(_attn(ctx, q, k, v, H, s, mask, head_space),
+           oracle.attention(q, k, v, heads=H, scale=s, mask=mask, out_head_space=int(head_space)))
