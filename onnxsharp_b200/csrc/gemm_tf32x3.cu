@@ -283,24 +283,33 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
       if (row >= M) break;
       float* yrow = Yz + static_cast<size_t>(row) * ep.y_ld;
       const float rs = ep.row_scale != nullptr ? ep.row_scale[static_cast<size_t>(z) * M + row] : 1.0f;
+      const bool vec_row = (reinterpret_cast<uintptr_t>(yrow) & 15u) == 0;
 #pragma unroll
       for (int h = 0; h < Cfg::BN; h += 128) {
+        const int j0 = n0 + h + lane * 4;
+        float v[4];
 #pragma unroll
         for (int t = 0; t < 4; ++t) {
-          const int j = n0 + h + lane * 4 + t;
-          if (j >= N) break;
-          float v = stage[r * kPitch + h + lane * 4 + t];
-          if (col_bias != nullptr) v = __fadd_rn(v, sbias[h + lane * 4 + t]);
+          const int j = j0 + t;
+          v[t] = stage[r * kPitch + h + lane * 4 + t];
+          if (col_bias != nullptr) v[t] = __fadd_rn(v[t], sbias[h + lane * 4 + t]);
           if (affine) {  // Gemm (AttnOps.cs:100-128): alpha * d, then + beta * c
-            if (ep.alpha != 1.0f) v = __fmul_rn(ep.alpha, v);
-            if (ep.beta != 0.0f && ep.c != nullptr && ep.c_len > 0) {
+            if (ep.alpha != 1.0f) v[t] = __fmul_rn(ep.alpha, v[t]);
+            if (ep.beta != 0.0f && ep.c != nullptr && ep.c_len > 0 && j < N) {
               const float cv = full_c ? ep.c[static_cast<size_t>(row) * N + j]
                                       : (ep.c_len == 1 ? ep.c[0] : ep.c[j % ep.c_len]);
-              v = __fadd_rn(v, __fmul_rn(ep.beta, cv));
+              v[t] = __fadd_rn(v[t], __fmul_rn(ep.beta, cv));
             }
           }
-          if (ep.row_scale != nullptr) v = __fmul_rn(v, rs);
-          yrow[j] = apply_act(v, act);
+          if (ep.row_scale != nullptr) v[t] = __fmul_rn(v[t], rs);
+          v[t] = apply_act(v[t], act);
+        }
+        if (vec_row && j0 + 4 <= N) {  // 16-byte stores: whole 32-byte sectors per lane pair
+          *reinterpret_cast<float4*>(yrow + j0) = make_float4(v[0], v[1], v[2], v[3]);
+        } else {
+#pragma unroll
+          for (int t = 0; t < 4; ++t)
+            if (j0 + t < N) yrow[j0 + t] = v[t];
         }
       }
     }
@@ -630,6 +639,101 @@ int attention_composed(osc_ctx* ctx, const float* q, const float* k, const float
   }
   return batched_strided(ctx, B, H, T, T, D, S, static_cast<long long>(H) * T * T, static_cast<long long>(T) * T, T, 1,
                          v, T * W, D, W, 1, nullptr, ep, out, work);
+}
+
+// The reference's Softmax op (DnnOps.cs:2547; the order of k_softmax_rows:
+// row max, e = exp(s - max) summed in 8 lanes over the 8-aligned part, the
+// scalar tail, p = e * (1/sum)) on rows of S [rows][len], written as the
+// hi/lo split MMA operand [rows][kp] (zero for len <= j < kp). One warp per
+// row; e is parked in `hi` between the passes.
+__global__ void k_softmax_split(const float* __restrict__ S, long long rows, int len, int kp, float* __restrict__ hi,
+                                float* __restrict__ lo) {
+  const int lane = threadIdx.x & 31;
+  const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
+  for (long long r = blockIdx.x * static_cast<long long>(blockDim.x >> 5) + (threadIdx.x >> 5); r < rows;
+       r += warps) {
+    const float* sr = S + r * len;
+    float* hr = hi + r * kp;
+    float* lr = lo + r * kp;
+    float mx = -INFINITY;
+    for (int j = lane; j < len; j += 32) mx = fmaxf(mx, __ldg(sr + j));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const int vend = len & ~7;
+    float part = 0.0f;
+    if (lane < 8)
+      for (int j = lane; j < vend; j += 8) {
+        const float e = ref_exp(__fsub_rn(__ldg(sr + j), mx));
+        hr[j] = e;
+        part = __fadd_rn(part, e);
+      }
+    float total = 0.0f;
+    for (int l = 0; l < 8; ++l) total = __fadd_rn(total, __shfl_sync(0xffffffffu, part, l));
+    for (int j = vend; j < len; ++j) {  // scalar tail (uniform across the warp)
+      const float e = expf(__fsub_rn(__ldg(sr + j), mx));
+      if (lane == 0) hr[j] = e;
+      total = __fadd_rn(total, e);
+    }
+    __syncwarp();
+    const float inv = __fdiv_rn(1.0f, total);
+    for (int j = lane; j < kp; j += 32) {
+      const float p = j < len ? __fmul_rn(hr[j], inv) : 0.0f;
+      const float h = to_tf32(p);
+      hr[j] = h;
+      lr[j] = __fsub_rn(p, h);
+    }
+  }
+}
+
+// YOLO11's PSA attention (the exported MatMul -> Mul -> Softmax -> MatMul
+// chain) on the tensor cores, per image b and head h of qkv [B][heads*(2kd+hd)][T]:
+//   S = (q^T k) * scale        [T][T]   (batched 3xTF32 product, scale in the epilogue)
+//   P = softmax_rows(S)                  (straight into the split operand)
+//   out[b][h*hd + d][n] = sum_m v[d][m] P[n][m]
+int psa_composed(osc_ctx* ctx, const float* qkv, long long qkv_nstride, int B, int heads, int kd, int hd, int T,
+                 float scale, float* out, long long out_nstride) {
+  const long long Z = static_cast<long long>(B) * heads;
+  if (Z > 65535) return fail(OSC_EUNSUPPORTED, "psa attention: %lld image-heads (65535 at most)", Z);
+  const int kq = static_cast<int>(round_up(static_cast<size_t>(kd), 4));
+  const int kt = static_cast<int>(round_up(static_cast<size_t>(T), 4));
+  const size_t q_bytes = round_up(static_cast<size_t>(Z) * T * kq * 4, 256);
+  const size_t s_bytes = round_up(static_cast<size_t>(Z) * T * T * 4, 256);
+  const size_t p_bytes = round_up(static_cast<size_t>(Z) * T * kt * 4, 256);
+  const size_t v_bytes = round_up(static_cast<size_t>(Z) * hd * kt * 4, 256);
+  void* buf = nullptr;
+  OSC_TRY(scratch(ctx, 4 * q_bytes + s_bytes + 2 * p_bytes + 2 * v_bytes, &buf));
+  uint8_t* p = static_cast<uint8_t*>(buf);
+  float* qhi = reinterpret_cast<float*>(p);
+  float* qlo = reinterpret_cast<float*>(p + q_bytes);
+  float* khi = reinterpret_cast<float*>(p + 2 * q_bytes);
+  float* klo = reinterpret_cast<float*>(p + 3 * q_bytes);
+  float* S = reinterpret_cast<float*>(p + 4 * q_bytes);
+  float* phi = reinterpret_cast<float*>(p + 4 * q_bytes + s_bytes);
+  float* plo = reinterpret_cast<float*>(p + 4 * q_bytes + s_bytes + p_bytes);
+  float* vhi = reinterpret_cast<float*>(p + 4 * q_bytes + s_bytes + 2 * p_bytes);
+  float* vlo = reinterpret_cast<float*>(p + 4 * q_bytes + s_bytes + 2 * p_bytes + v_bytes);
+  const long long per = static_cast<long long>(2 * kd + hd) * T;  // one head's q, k, v channels
+  const int nz = static_cast<int>(Z);
+  // q^T and k^T as [z][token][channel]: the source is channel-major (tokens contiguous)
+  OSC_TRY(gather_split(ctx, qkv, nz, heads, qkv_nstride, per, 1, T, T, kd, kq, qhi, qlo));
+  OSC_TRY(gather_split(ctx, qkv + static_cast<long long>(kd) * T, nz, heads, qkv_nstride, per, 1, T, T, kd, kq, khi,
+                       klo));
+  {
+    EpiAffine ep{scale, 0.0f, nullptr, 0, static_cast<long long>(heads) * T * T, static_cast<long long>(T) * T, heads,
+                 T, 1, nullptr};
+    OSC_TRY(gemm_batched(ctx, qhi, qlo, nz, T, kq, khi, klo, nz, T, nullptr, OSC_ACT_NONE, ep, S));
+  }
+  {
+    const long long rows = Z * T;
+    const int blocks = static_cast<int>(std::min<long long>((rows + 7) / 8, static_cast<long long>(ctx->num_sms) * 16));
+    prof_begin(ctx);
+    k_softmax_split<<<blocks, 256, 0, ctx->stream>>>(S, rows, T, kt, phi, plo);
+    OSC_TRY(check_launch(ctx, "k_softmax_split"));
+  }
+  // v as [z][channel][token] (already K-major)
+  OSC_TRY(gather_split(ctx, qkv + 2LL * kd * T, nz, heads, qkv_nstride, per, T, 1, hd, T, kt, vhi, vlo));
+  EpiAffine ep{1.0f, 0.0f, nullptr, 0, out_nstride, static_cast<long long>(hd) * T, heads, T, 1, nullptr};
+  return gemm_batched(ctx, vhi, vlo, nz, hd, kt, phi, plo, nz, T, nullptr, OSC_ACT_NONE, ep, out);
 }
 
 }  // namespace osc

@@ -1,9 +1,10 @@
 // glue.cu — the memory-bound operators around the tensor-core kernels on the
 // YOLO11n-shaped graph and the attention block: direct conv (first layer /
 // depthwise), MaxPool, nearest Resize, broadcasting binary ops, unary
-// activations, Softmax, DflSoftmax, the fused YOLO head decode, LayerNorm and
-// the C2PSA attention (T = H*W > 128). CUDA cores, 128-bit accesses where the
-// layout allows, warp-shuffle reductions. Reference file:line per kernel.
+// activations, Softmax, DflSoftmax, the fused YOLO head decode and LayerNorm
+// (CUDA cores, 128-bit accesses where the layout allows, warp-shuffle
+// reductions), and the entry of the C2PSA attention, whose products run on the
+// tensor cores (gemm_tf32x3.cu). Reference file:line per kernel.
 //
 // NCHW tensors may be channel slices of larger buffers: `*_nstride` is the
 // element distance between consecutive images (0 = dense), so Split outputs
@@ -373,53 +374,76 @@ int conv_tile_by_m(osc_ctx* ctx, const float* x, long long x_nstride, int N, int
 }
 
 // ---------------------------------------------------------------- MaxPool
-// Ops/DnnOps.cs:1335 (MaxPoolLayer): max over the window's in-bounds elements.
-__global__ void k_maxpool(const float* __restrict__ x, long long x_nstride, int N, int C, int H, int W, int kh, int kw,
-                          int sh, int sw, int pt, int pl, float* __restrict__ y, long long y_nstride, int OH, int OW) {
-  const long long total = static_cast<long long>(N) * C * OH * OW;
-  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    long long t = i;
-    const int ox = static_cast<int>(t % OW);
-    t /= OW;
-    const int oy = static_cast<int>(t % OH);
-    t /= OH;
-    const int c = static_cast<int>(t % C);
-    const int n = static_cast<int>(t / C);
-    const float* xc = x + static_cast<size_t>(n) * x_nstride + static_cast<size_t>(c) * H * W;
+// Ops/DnnOps.cs:1335 (MaxPoolLayer): max over the window's in-bounds elements,
+// taken row by row, column by column (the reference's order, which decides
+// which operand survives when a NaN is met). One CTA row per plane (n, c),
+// 4 outputs per thread; the window re-reads hit L1.
+constexpr int kPoolThreads = 128, kPoolPerThread = 4;
+
+__global__ void __launch_bounds__(kPoolThreads) k_maxpool(const float* __restrict__ x, long long x_nstride, int C,
+                                                          int H, int W, int kh, int kw, int sh, int sw, int pt, int pl,
+                                                          float* __restrict__ y, long long y_nstride, int OH, int OW) {
+  const int plane = blockIdx.x;
+  const int n = plane / C, c = plane - n * C;
+  const float* xc = x + static_cast<size_t>(n) * x_nstride + static_cast<size_t>(c) * H * W;
+  float* yc = y + static_cast<size_t>(n) * y_nstride + static_cast<size_t>(c) * OH * OW;
+  const int total = OH * OW;
+  const int base = blockIdx.y * (kPoolThreads * kPoolPerThread) + threadIdx.x;
+#pragma unroll
+  for (int j = 0; j < kPoolPerThread; ++j) {
+    const int o = base + j * kPoolThreads;
+    if (o >= total) break;
+    const int oy = o / OW, ox = o - oy * OW;
     float m = -INFINITY;
     for (int ky = 0; ky < kh; ++ky) {
       const int iy = oy * sh - pt + ky;
       if (iy < 0 || iy >= H) continue;
+      const float* row = xc + static_cast<size_t>(iy) * W;
       for (int kx = 0; kx < kw; ++kx) {
         const int ix = ox * sw - pl + kx;
         if (ix < 0 || ix >= W) continue;
-        m = maxps(__ldg(xc + static_cast<size_t>(iy) * W + ix), m);
+        m = maxps(__ldg(row + ix), m);
       }
     }
-    y[static_cast<size_t>(n) * y_nstride + (static_cast<size_t>(c) * OH + oy) * OW + ox] = m;
+    yc[o] = m;
   }
 }
 
 // ---------------------------------------------------------------- Resize (nearest, integer up-scale)
 // Ops/DnnOps.cs:2215 (ResizeLayer), nearest mode with integer scales:
-// out[y][x] = in[y / sy][x / sx].
-__global__ void k_resize_nearest(const float* __restrict__ x, long long x_nstride, int N, int C, int H, int W, int sy,
-                                 int sx, float* __restrict__ y, long long y_nstride) {
+// out[y][x] = in[y / sy][x / sx]. Grid: (planes, tiles of a plane).
+__global__ void __launch_bounds__(256) k_resize_nearest(const float* __restrict__ x, long long x_nstride, int C, int H,
+                                                        int W, int sy, int sx, float* __restrict__ y,
+                                                        long long y_nstride) {
+  const int plane = blockIdx.x;
+  const int n = plane / C, c = plane - n * C;
   const int OH = H * sy, OW = W * sx;
-  const long long total = static_cast<long long>(N) * C * OH * OW;
-  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    long long t = i;
-    const int ox = static_cast<int>(t % OW);
-    t /= OW;
-    const int oy = static_cast<int>(t % OH);
-    t /= OH;
-    const int c = static_cast<int>(t % C);
-    const int n = static_cast<int>(t / C);
-    y[static_cast<size_t>(n) * y_nstride + (static_cast<size_t>(c) * OH + oy) * OW + ox] =
-        __ldg(x + static_cast<size_t>(n) * x_nstride + (static_cast<size_t>(c) * H + oy / sy) * W + ox / sx);
-  }
+  const float* xc = x + static_cast<size_t>(n) * x_nstride + static_cast<size_t>(c) * H * W;
+  float* yc = y + static_cast<size_t>(n) * y_nstride + static_cast<size_t>(c) * OH * OW;
+  const int o = blockIdx.y * 256 + threadIdx.x;
+  if (o >= OH * OW) return;
+  const int oy = o / OW, ox = o - oy * OW;
+  yc[o] = __ldg(xc + (oy / sy) * W + ox / sx);
+}
+
+// 2x nearest up-scale: each thread reads 2 adjacent inputs (8 bytes) and writes
+// the 2x4 output block as two 16-byte stores. Needs an even W and 16-byte
+// aligned output rows (checked by the launcher).
+__global__ void __launch_bounds__(256) k_resize_nearest2x(const float* __restrict__ x, long long x_nstride, int C,
+                                                          int H, int W, float* __restrict__ y, long long y_nstride) {
+  const int plane = blockIdx.x;
+  const int n = plane / C, c = plane - n * C;
+  const int hw2 = (H * W) >> 1;
+  const int i = blockIdx.y * 256 + threadIdx.x;
+  if (i >= hw2) return;
+  const float2 v = __ldg(reinterpret_cast<const float2*>(x + static_cast<size_t>(n) * x_nstride +
+                                                         static_cast<size_t>(c) * H * W) + i);
+  const int e = 2 * i, h = e / W, w = e - h * W;
+  float* yc = y + static_cast<size_t>(n) * y_nstride + static_cast<size_t>(c) * 4 * H * W;
+  const float4 q = make_float4(v.x, v.x, v.y, v.y);
+  float4* r0 = reinterpret_cast<float4*>(yc + static_cast<size_t>(2 * h) * (2 * W) + 2 * w);
+  r0[0] = q;
+  r0[W >> 1] = q;  // the next output row starts 2W floats later
 }
 
 // ---------------------------------------------------------------- binary (numpy broadcasting, rank <= 4)
@@ -652,182 +676,6 @@ __global__ void k_layernorm(const float* __restrict__ x, int outer, int inner, c
   }
 }
 
-// ---------------------------------------------------------------- C2PSA attention (T = H*W)
-// The attention of YOLO11's PSA block (model.10.m.0.attn, exported as
-// Reshape/Split/Transpose/MatMul/Mul/Softmax/MatMul, shapes in the reference's
-// tests/data/yolo11n.shapes.tsv nodes 123-134): from qkv [B, heads*(2*kd+hd), T]
-// per head q [kd][T], k [kd][T], v [hd][T];
-//   S[i][j] = (sum_c q[c][i] * k[c][j]) * scale   (MatMul FMA chain, then Mul)
-//   P = SoftmaxRow(S)                            (VectorMath.SoftmaxRow)
-//   out[d][i] = sum_j v[d][j] * P[i][j]           (MatMul FMA chain over j)
-// One CTA per (b, head, block of 16 query rows); S rows live in shared memory.
-constexpr int kPsaRows = 16;
-
-__global__ void k_psa_attention(const float* __restrict__ qkv, long long qkv_nstride, int heads, int kd, int hd,
-                                int T, float scale, float* __restrict__ out, long long out_nstride) {
-  extern __shared__ float sm[];
-  float* S = sm;                         // [kPsaRows][T]
-  float* qs = sm + kPsaRows * T;         // [kd][kPsaRows]
-  const int bh = blockIdx.y;
-  const int b = bh / heads, h = bh % heads;
-  const int i0 = blockIdx.x * kPsaRows;
-  const int rows = min(kPsaRows, T - i0);
-  const int per_head = 2 * kd + hd;
-  const float* base = qkv + static_cast<size_t>(b) * qkv_nstride + static_cast<size_t>(h) * per_head * T;
-  const float* q = base;
-  const float* k = base + static_cast<size_t>(kd) * T;
-  const float* v = base + static_cast<size_t>(2 * kd) * T;
-  for (int idx = threadIdx.x; idx < kd * kPsaRows; idx += blockDim.x) {
-    const int c = idx / kPsaRows, r = idx % kPsaRows;
-    qs[idx] = r < rows ? __ldg(q + static_cast<size_t>(c) * T + i0 + r) : 0.0f;
-  }
-  __syncthreads();
-  // S = (q^T k) * scale
-  for (int idx = threadIdx.x; idx < kPsaRows * T; idx += blockDim.x) {
-    const int r = idx / T, j = idx % T;
-    float acc = 0.0f;
-    for (int c = 0; c < kd; ++c) acc = __fmaf_rn(qs[c * kPsaRows + r], __ldg(k + static_cast<size_t>(c) * T + j), acc);
-    S[idx] = __fmul_rn(acc, scale);
-  }
-  __syncthreads();
-  // softmax rows: one warp per row (same reduction order as k_softmax_rows)
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
-  for (int r = warp; r < rows; r += nwarps) {
-    float* sr = S + r * T;
-    float mx = -INFINITY;
-    for (int j = lane; j < T; j += 32) mx = fmaxf(mx, sr[j]);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    const int vend = T & ~7;
-    float part = 0.0f;
-    if (lane < 8)
-      for (int j = lane; j < vend; j += 8) {
-        const float e = ref_exp(__fsub_rn(sr[j], mx));
-        sr[j] = e;
-        part = __fadd_rn(part, e);
-      }
-    float total = 0.0f;
-    for (int l = 0; l < 8; ++l) total = __fadd_rn(total, __shfl_sync(0xffffffffu, part, l));
-    __syncwarp();
-    for (int j = vend; j < T; ++j) {
-      const float e = expf(__fsub_rn(sr[j], mx));
-      total = __fadd_rn(total, e);
-      __syncwarp();
-      if (lane == 0) sr[j] = e;
-      __syncwarp();
-    }
-    const float inv = __fdiv_rn(1.0f, total);
-    __syncwarp();
-    for (int j = lane; j < T; j += 32) sr[j] = __fmul_rn(sr[j], inv);
-  }
-  __syncthreads();
-  // out[h*hd + d][i0 + r] = sum_j v[d][j] * P[r][j]
-  float* ob = out + static_cast<size_t>(b) * out_nstride + static_cast<size_t>(h) * hd * T;
-  for (int idx = threadIdx.x; idx < hd * rows; idx += blockDim.x) {
-    const int d = idx / rows, r = idx % rows;
-    const float* vd = v + static_cast<size_t>(d) * T;
-    const float* pr = S + r * T;
-    float acc = 0.0f;
-    for (int j = 0; j < T; ++j) acc = __fmaf_rn(__ldg(vd + j), pr[j], acc);
-    ob[static_cast<size_t>(d) * T + i0 + r] = acc;
-  }
-}
-
-// Same computation with the head's K and V resident in shared memory and
-// register blocking (32 query rows per CTA, 256 threads): S rows are padded
-// to T+1 floats so the P reads of 32 different rows hit 32 banks.
-constexpr int kPsaR = 32;
-
-__global__ void __launch_bounds__(256) k_psa_attention_smem(const float* __restrict__ qkv, long long qkv_nstride,
-                                                            int heads, int kd, int hd, int T, float scale,
-                                                            float* __restrict__ out, long long out_nstride) {
-  extern __shared__ float sm[];
-  const int TP = T + 1;
-  float* ks = sm;                      // [kd][T]
-  float* vs = ks + kd * T;             // [hd][T]
-  float* S = vs + hd * T;              // [kPsaR][T+1]
-  float* qs = S + kPsaR * TP;          // [kd][kPsaR]
-  const int bh = blockIdx.y;
-  const int b = bh / heads, h = bh % heads;
-  const int i0 = blockIdx.x * kPsaR;
-  const int rows = min(kPsaR, T - i0);
-  const int per_head = 2 * kd + hd;
-  const float* base = qkv + static_cast<size_t>(b) * qkv_nstride + static_cast<size_t>(h) * per_head * T;
-  for (int i = threadIdx.x; i < (kd + hd) * T; i += blockDim.x) ks[i] = __ldg(base + static_cast<size_t>(kd) * T + i);
-  for (int idx = threadIdx.x; idx < kd * kPsaR; idx += blockDim.x) {
-    const int c = idx / kPsaR, r = idx % kPsaR;
-    qs[idx] = r < rows ? __ldg(base + static_cast<size_t>(c) * T + i0 + r) : 0.0f;
-  }
-  __syncthreads();
-  // S = (q^T k) * scale: each thread 4 rows x 1 key, FMA chain over c.
-  for (int idx = threadIdx.x; idx < (kPsaR / 4) * T; idx += blockDim.x) {
-    const int rg = idx / T, j = idx - rg * T;
-    float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
-    for (int c = 0; c < kd; ++c) {
-      const float kv = ks[c * T + j];
-      const float* qc = qs + c * kPsaR + rg * 4;
-      a0 = __fmaf_rn(qc[0], kv, a0);
-      a1 = __fmaf_rn(qc[1], kv, a1);
-      a2 = __fmaf_rn(qc[2], kv, a2);
-      a3 = __fmaf_rn(qc[3], kv, a3);
-    }
-    float* sr = S + (rg * 4) * TP + j;
-    sr[0] = __fmul_rn(a0, scale);
-    sr[TP] = __fmul_rn(a1, scale);
-    sr[2 * TP] = __fmul_rn(a2, scale);
-    sr[3 * TP] = __fmul_rn(a3, scale);
-  }
-  __syncthreads();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
-  for (int r = warp; r < rows; r += nwarps) {
-    float* sr = S + r * TP;
-    float mx = -INFINITY;
-    for (int j = lane; j < T; j += 32) mx = fmaxf(mx, sr[j]);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    const int vend = T & ~7;
-    float part = 0.0f;
-    if (lane < 8)
-      for (int j = lane; j < vend; j += 8) {
-        const float e = ref_exp(__fsub_rn(sr[j], mx));
-        sr[j] = e;
-        part = __fadd_rn(part, e);
-      }
-    float total = 0.0f;
-    for (int l = 0; l < 8; ++l) total = __fadd_rn(total, __shfl_sync(0xffffffffu, part, l));
-    __syncwarp();
-    for (int j = vend; j < T; ++j) {
-      const float e = expf(__fsub_rn(sr[j], mx));
-      total = __fadd_rn(total, e);
-      __syncwarp();
-      if (lane == 0) sr[j] = e;
-      __syncwarp();
-    }
-    const float inv = __fdiv_rn(1.0f, total);
-    __syncwarp();
-    for (int j = lane; j < T; j += 32) sr[j] = __fmul_rn(sr[j], inv);
-  }
-  __syncthreads();
-  // out[h*hd + d][i0 + r]: lane = query row, warp = a group of hd/8 output channels.
-  float* ob = out + static_cast<size_t>(b) * out_nstride + static_cast<size_t>(h) * hd * T;
-  const int dper = (hd + nwarps - 1) / nwarps;
-  for (int d0 = warp * dper; d0 < min(hd, (warp + 1) * dper); d0 += 8) {
-    const int nd = min(8, min(hd, (warp + 1) * dper) - d0);
-    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    const float* pr = S + lane * TP;
-    for (int j = 0; j < T; ++j) {
-      const float p = pr[j];
-#pragma unroll
-      for (int q = 0; q < 8; ++q)
-        if (q < nd) acc[q] = __fmaf_rn(vs[(d0 + q) * T + j], p, acc[q]);
-    }
-    if (lane < rows)
-#pragma unroll
-      for (int q = 0; q < 8; ++q)
-        if (q < nd) ob[static_cast<size_t>(d0 + q) * T + i0 + lane] = acc[q];
-  }
-}
-
 // Exhaustive check of recip_1up against the IEEE division over [1, 2^126).
 __global__ void k_selfcheck_recip(unsigned long long* mismatches, unsigned int* first_bad) {
   const unsigned int lo = 0x3F800000u, hi = 0x7E800000u;  // bits of 1.0f and 2^126
@@ -968,9 +816,14 @@ OSC_API int osc_maxpool2d_f32(osc_ctx* ctx, const float* x, long long x_nstride,
   if (x_nstride == 0) x_nstride = static_cast<long long>(C) * H * W;
   if (y_nstride == 0) y_nstride = static_cast<long long>(C) * OH * OW;
   if (N == 0) return OSC_OK;
+  const long long planes = static_cast<long long>(N) * C;
+  const long long tiles = (static_cast<long long>(OH) * OW + kPoolThreads * kPoolPerThread - 1) /
+                          (kPoolThreads * kPoolPerThread);
+  if (planes > 0x7fffffffLL || tiles > 65535 || static_cast<long long>(H) * W > 0x7fffffffLL)
+    return fail(OSC_EINVAL, "osc_maxpool2d_f32: %lld planes of %dx%d exceed the launch limits", planes, OH, OW);
   prof_begin(ctx);
-  k_maxpool<<<blocks_for(ctx, static_cast<long long>(N) * C * OH * OW), 256, 0, ctx->stream>>>(
-      x, x_nstride, N, C, H, W, kh, kw, stride_h, stride_w, pad_t, pad_l, y, y_nstride, OH, OW);
+  k_maxpool<<<dim3(static_cast<unsigned>(planes), static_cast<unsigned>(tiles)), kPoolThreads, 0, ctx->stream>>>(
+      x, x_nstride, C, H, W, kh, kw, stride_h, stride_w, pad_t, pad_l, y, y_nstride, OH, OW);
   return check_launch(ctx, "k_maxpool");
 }
 
@@ -982,9 +835,22 @@ OSC_API int osc_resize_nearest_f32(osc_ctx* ctx, const float* x, long long x_nst
   if (x_nstride == 0) x_nstride = static_cast<long long>(C) * H * W;
   if (y_nstride == 0) y_nstride = static_cast<long long>(C) * H * scale_h * W * scale_w;
   if (N == 0) return OSC_OK;
+  const long long planes = static_cast<long long>(N) * C;
+  const long long outs = static_cast<long long>(H) * scale_h * W * scale_w;
+  if (planes > 0x7fffffffLL || (outs + 255) / 256 > 65535)
+    return fail(OSC_EINVAL, "osc_resize_nearest_f32: %lld planes of %lld outputs exceed the launch limits", planes,
+                outs);
+  const bool vec2x = scale_h == 2 && scale_w == 2 && W % 2 == 0 && reinterpret_cast<uintptr_t>(x) % 8 == 0 &&
+                     x_nstride % 2 == 0 && reinterpret_cast<uintptr_t>(y) % 16 == 0 && y_nstride % 4 == 0;
   prof_begin(ctx);
-  k_resize_nearest<<<blocks_for(ctx, static_cast<long long>(N) * C * H * scale_h * W * scale_w), 256, 0,
-                     ctx->stream>>>(x, x_nstride, N, C, H, W, scale_h, scale_w, y, y_nstride);
+  if (vec2x) {
+    const long long pairs = static_cast<long long>(H) * W / 2;
+    k_resize_nearest2x<<<dim3(static_cast<unsigned>(planes), static_cast<unsigned>((pairs + 255) / 256)), 256, 0,
+                         ctx->stream>>>(x, x_nstride, C, H, W, y, y_nstride);
+    return check_launch(ctx, "k_resize_nearest2x");
+  }
+  k_resize_nearest<<<dim3(static_cast<unsigned>(planes), static_cast<unsigned>((outs + 255) / 256)), 256, 0,
+                     ctx->stream>>>(x, x_nstride, C, H, W, scale_h, scale_w, y, y_nstride);
   return check_launch(ctx, "k_resize_nearest");
 }
 
@@ -1085,31 +951,24 @@ OSC_API int osc_layernorm_f32(osc_ctx* ctx, const float* x, int outer, int inner
   return check_launch(ctx, "k_layernorm");
 }
 
+// The attention of YOLO11's PSA block (model.10.m.0.attn, exported as
+// Reshape/Split/Transpose/MatMul/Mul/Softmax/MatMul, shapes in the reference's
+// tests/data/yolo11n.shapes.tsv nodes 123-134): from qkv [B, heads*(2*kd+hd), T]
+// per head q [kd][T], k [kd][T], v [hd][T];
+//   S[i][j] = (sum_c q[c][i] * k[c][j]) * scale   (MatMul, then Mul)
+//   P = SoftmaxRow(S)                            (VectorMath.SoftmaxRow)
+//   out[d][i] = sum_j v[d][j] * P[i][j]           (MatMul over j)
+// Both products on the tensor cores (psa_composed).
 OSC_API int osc_psa_attention_f32(osc_ctx* ctx, const float* qkv, long long qkv_nstride, int B, int heads, int kd,
                                   int hd, int T, float scale, float* out, long long out_nstride) {
   OSC_TRY(enter(ctx));
   if (B < 0 || heads <= 0 || kd <= 0 || hd <= 0 || T <= 0) return fail(OSC_EINVAL, "osc_psa_attention_f32: bad shape");
-  const size_t smem = (static_cast<size_t>(kPsaRows) * T + static_cast<size_t>(kd) * kPsaRows) * sizeof(float);
-  if (smem > 200 * 1024) return fail(OSC_EUNSUPPORTED, "osc_psa_attention_f32: T=%d too long", T);
   if (qkv_nstride == 0) qkv_nstride = static_cast<long long>(heads) * (2 * kd + hd) * T;
   if (out_nstride == 0) out_nstride = static_cast<long long>(heads) * hd * T;
   if (B == 0) return OSC_OK;
-  const size_t smem_full =
-      (static_cast<size_t>(kd + hd) * T + static_cast<size_t>(kPsaR) * (T + 1) + static_cast<size_t>(kd) * kPsaR) *
-      sizeof(float);
-  if (smem_full <= 220 * 1024) {
-    OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(k_psa_attention_smem), static_cast<int>(smem_full)));
-    dim3 grid((T + kPsaR - 1) / kPsaR, B * heads);
-    prof_begin(ctx);
-    k_psa_attention_smem<<<grid, 256, smem_full, ctx->stream>>>(qkv, qkv_nstride, heads, kd, hd, T, scale, out,
-                                                                out_nstride);
-    return check_launch(ctx, "k_psa_attention");
-  }
-  OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(k_psa_attention), static_cast<int>(smem)));
-  dim3 grid((T + kPsaRows - 1) / kPsaRows, B * heads);
-  prof_begin(ctx);
-  k_psa_attention<<<grid, 256, smem, ctx->stream>>>(qkv, qkv_nstride, heads, kd, hd, T, scale, out, out_nstride);
-  return check_launch(ctx, "k_psa_attention");
+  if ((reinterpret_cast<uintptr_t>(out) & 15u) != 0 || out_nstride % 4 != 0)
+    return fail(OSC_EINVAL, "osc_psa_attention_f32: out must be 16-byte aligned with a 4-element image stride");
+  return psa_composed(ctx, qkv, qkv_nstride, B, heads, kd, hd, T, scale, out, out_nstride);
 }
 
 }  // extern "C"

@@ -53,6 +53,10 @@ bool fault_injected(const char* site);
 // Makes `ctx->device` current; returns OSC_OK or an error code.
 int enter(osc_ctx* ctx);
 
+// YOLO11 PSA attention on the tensor cores (gemm_tf32x3.cu).
+int psa_composed(osc_ctx* ctx, const float* qkv, long long qkv_nstride, int B, int heads, int kd, int hd, int T,
+                 float scale, float* out, long long out_nstride);
+
 // FusedAttention for T > 128 or head sizes other than 32 / 64, composed of
 // tensor-core batched products and a row softmax (gemm_tf32x3.cu).
 int attention_composed(osc_ctx* ctx, const float* q, const float* k, const float* v, const float* mask,
