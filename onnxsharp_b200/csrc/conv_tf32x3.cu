@@ -120,43 +120,358 @@ __global__ void __launch_bounds__(ConvCfg::THREADS, 1)
     constexpr int kPitch = Cfg::BN + 4;
     const float* stage = reinterpret_cast<const float*>(tiles);
     const float* sbias = stage + kBM * kPitch;
-    for (int r = warp; r < kBM; r += Cfg::THREADS / 32) {
-      const int oc = m0 + r;
-      if (oc >= g.M) break;
-      const float b = sbias[r];
-      const size_t plane_off = static_cast<size_t>(oc) * g.OH * g.OW;
-      float* yplane = y + static_cast<size_t>(n) * g.y_nstride + plane_off;
-      const float* rplane = g.res ? g.res + static_cast<size_t>(n) * g.res_nstride + plane_off : nullptr;
+    with_act(g.act, [&](auto tag) {
+      constexpr int ACT = decltype(tag)::value;
+      for (int r = warp; r < kBM; r += Cfg::THREADS / 32) {
+        const int oc = m0 + r;
+        if (oc >= g.M) break;
+        const float b = sbias[r];
+        const size_t plane_off = static_cast<size_t>(oc) * g.OH * g.OW;
+        float* yplane = y + static_cast<size_t>(n) * g.y_nstride + plane_off;
+        const float* rplane = g.res ? g.res + static_cast<size_t>(n) * g.res_nstride + plane_off : nullptr;
 #pragma unroll
-      for (int h = 0; h < Cfg::BN; h += 128) {
-        const int p = h + lane * 4;  // 4 consecutive pixels of one box row (BW >= 8)
-        const int oy = oy0 + (p >> g.bw_log2), ox = ox0 + (p & (g.BW - 1));
-        if (oy >= g.OH) continue;
-        const float4 sv = *reinterpret_cast<const float4*>(stage + r * kPitch + p);
-        const float v[4] = {sv.x, sv.y, sv.z, sv.w};
-        float* dst = yplane + static_cast<size_t>(oy) * g.OW + ox;
-        const float* rsrc = rplane ? rplane + static_cast<size_t>(oy) * g.OW + ox : nullptr;
-        float o[4];
+        for (int h = 0; h < Cfg::BN; h += 128) {
+          const int p = h + lane * 4;  // 4 consecutive pixels of one box row (BW >= 8)
+          const int oy = oy0 + (p >> g.bw_log2), ox = ox0 + (p & (g.BW - 1));
+          if (oy >= g.OH) continue;
+          const float4 sv = *reinterpret_cast<const float4*>(stage + r * kPitch + p);
+          const float v[4] = {sv.x, sv.y, sv.z, sv.w};
+          float* dst = yplane + static_cast<size_t>(oy) * g.OW + ox;
+          const float* rsrc = rplane ? rplane + static_cast<size_t>(oy) * g.OW + ox : nullptr;
+          float o[4];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) o[q] = apply_act(__fadd_rn(v[q], b), g.act);
-        if (g.vec4 && ox + 4 <= g.OW) {  // one 16-byte store: whole 32-byte sectors per warp
-          if (rsrc) {
-            const float4 rv = __ldg(reinterpret_cast<const float4*>(rsrc));
-            o[0] = __fadd_rn(rv.x, o[0]);  // residual Add(x, act(conv)) as in the graph
-            o[1] = __fadd_rn(rv.y, o[1]);
-            o[2] = __fadd_rn(rv.z, o[2]);
-            o[3] = __fadd_rn(rv.w, o[3]);
+          for (int q = 0; q < 4; ++q) o[q] = act_t<ACT>(__fadd_rn(v[q], b));
+          if (g.vec4 && ox + 4 <= g.OW) {  // one 16-byte store: whole 32-byte sectors per warp
+            if (rsrc) {
+              const float4 rv = __ldg(reinterpret_cast<const float4*>(rsrc));
+              o[0] = __fadd_rn(rv.x, o[0]);  // residual Add(x, act(conv)) as in the graph
+              o[1] = __fadd_rn(rv.y, o[1]);
+              o[2] = __fadd_rn(rv.z, o[2]);
+              o[3] = __fadd_rn(rv.w, o[3]);
+            }
+            *reinterpret_cast<float4*>(dst) = make_float4(o[0], o[1], o[2], o[3]);
+          } else {
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              if (ox + q < g.OW) dst[q] = rsrc ? __fadd_rn(rsrc[q], o[q]) : o[q];
           }
-          *reinterpret_cast<float4*>(dst) = make_float4(o[0], o[1], o[2], o[3]);
-        } else {
+        }
+      }
+    });
+  }
+  pipe_teardown<Cfg>(pb, tmem);
+}
+
+// ------------------------------------------------------------ pointwise (1x1)
+// A 1x1, stride-1, unpadded conv is a GEMM per image, D[px][oc] =
+// X[px][c] * W[oc][c]^T, whose A operand is the NCHW input itself: for a fixed
+// channel the pixels are contiguous, i.e. A is MN-major. So the input is read
+// straight from NCHW by TMA (no transform pass, 4 bytes per element instead of
+// the transform's 4 + 8 and the conv's 8), split into hi/lo in shared memory
+// by two converter warps, and fed to tcgen05 with the A-MN-major descriptor.
+//  - tile: 128 pixels (TMEM lanes) x up to 128 output channels (columns; the
+//    MMA's N is the tile's channel count rounded to 16);
+//  - stage: A as 4 TMA boxes of 32 pixels x 32 channels (4 KB each; the
+//    128-byte swizzle with 32-byte atoms that MN-major TF32 operands need:
+//    4-channel groups 512 bytes apart, 32-pixel groups 4 KB apart), its lo
+//    part, and the prepacked weight hi/lo boxes (K-major);
+//  - persistent CTAs walk the tiles; TMEM holds two accumulators, so the
+//    epilogue of one tile overlaps the main loop of the next;
+//  - epilogue (8 warps, two per TMEM lane quadrant): lane = pixel, so each
+//    warp store writes 32 consecutive pixels of one output channel (128
+//    bytes): NCHW without a staging tile. Biases come from a shared-memory
+//    table filled once per CTA.
+namespace pw {
+constexpr int kStages = 3;
+constexpr int kBN = 128;                  // output channels per tile
+constexpr int kA = kBM * kBK * 4;         // 16 KB: 128 px x 32 ch
+constexpr int kB = kBN * kBK * 4;         // 16 KB: 128 oc x 32 ch
+constexpr int kStage = 2 * kA + 2 * kB;   // A (hi after the split) | A lo | W hi | W lo
+constexpr int kTx = kA + 2 * kB;          // bytes TMA lands per stage
+constexpr int kConvWarps = 2;
+constexpr int kEpiWarps = 8;              // two per TMEM lane quadrant, 64 columns each
+constexpr int kEpiBase = 2 + kConvWarps;  // first epilogue warp (a multiple of 4: warp % 4 = lane quadrant)
+constexpr int kThreads = 32 * (kEpiBase + kEpiWarps);  // producer, MMA, converters, epilogue
+constexpr int kKC = 2;                    // k-blocks per TMEM chunk
+constexpr int kTmemCols = 2 * kBN;
+struct Bars {
+  uint64_t full[kStages], conv[kStages], empty[kStages];
+  uint64_t acc_full[2], acc_empty[2];
+  uint64_t mma_done;
+  uint32_t tmem_slot;
+  int abort_flag;
+};
+constexpr int kMaxBias = 4096;            // output channels whose biases fit the shared-memory table
+constexpr int kSmemBase = kStages * kStage + 1024 + 256;  // + the bias table (M floats, rounded to 16 bytes)
+static_assert(kSmemBase + kMaxBias * 4 <= 232448, "shared memory budget");
+static_assert(kEpiBase % 4 == 0, "epilogue warps must start on a lane-quadrant boundary");
+static_assert(sizeof(Bars) <= 256, "barrier block");
+}  // namespace pw
+
+struct PwGeom {
+  int C, HW, M;            // input channels, pixels per image, output channels
+  int ptiles, otiles;      // pixel tiles per image, channel tiles
+  long long tiles;
+  int num_kb;
+  int act;
+  long long y_nstride, res_nstride;
+  const float* res;
+};
+
+__global__ void __launch_bounds__(pw::kThreads, 1)
+    k_conv1x1_tf32x3(const __grid_constant__ CUtensorMap mX, const __grid_constant__ CUtensorMap mWh,
+                     const __grid_constant__ CUtensorMap mWl, const __grid_constant__ PwGeom g,
+                     const float* __restrict__ bias, float* __restrict__ y, int* __restrict__ err) {
+  using namespace pw;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* tiles = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Bars* pb = reinterpret_cast<Bars*>(tiles + kStages * kStage);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&pb->full[s], 1);
+      mbar_init(&pb->conv[s], kConvWarps);
+      mbar_init(&pb->empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&pb->acc_full[b], 1);
+      mbar_init(&pb->acc_empty[b], kEpiWarps);
+    }
+    mbar_init(&pb->mma_done, 1);
+    pb->abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch(&mX);
+    tma_prefetch(&mWh);
+    tma_prefetch(&mWl);
+  }
+  if (warp == 1) {
+    tmem_alloc(&pb->tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  // every output channel's bias, read once per CTA (the epilogue reads it from
+  // shared memory instead of a global load in each store's dependency chain)
+  float* s_bias = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(pb) + 256);
+  for (int j = threadIdx.x; j < g.M; j += kThreads) s_bias[j] = bias != nullptr ? __ldg(bias + j) : 0.0f;
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = pb->tmem_slot;
+  const int nchunks = (g.num_kb + kKC - 1) / kKC;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int i = 0;
+      bool ok = true;
+      for (long long t = blockIdx.x; t < g.tiles && ok; t += gridDim.x) {
+        const int ot = static_cast<int>(t % g.otiles);
+        const long long r = t / g.otiles;
+        const int pt = static_cast<int>(r % g.ptiles);
+        const int n = static_cast<int>(r / g.ptiles);
+        const int p0 = pt * kBM, oc0 = ot * kBN;
+        for (int kb = 0; kb < g.num_kb; ++kb) {
+          const int s = i % kStages;
+          const uint32_t ph = (i / kStages) & 1u;
+          if (!mbar_wait(&pb->empty[s], ph ^ 1u, &pb->abort_flag, err)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&pb->full[s], kTx);
+          uint8_t* st = tiles + s * kStage;
 #pragma unroll
-          for (int q = 0; q < 4; ++q)
-            if (ox + q < g.OW) dst[q] = rsrc ? __fadd_rn(rsrc[q], o[q]) : o[q];
+          for (int q = 0; q < 4; ++q) tma_load_3d(st + q * 4096, &mX, &pb->full[s], p0 + 32 * q, kb * kBK, n);
+          tma_load_2d(st + 2 * kA, &mWh, &pb->full[s], kb * kBK, oc0);
+          tma_load_2d(st + 2 * kA + kB, &mWl, &pb->full[s], kb * kBK, oc0);
+          ++i;
+        }
+      }
+      if (!ok) {  // error path: let the copies in flight land before the CTA exits
+        for (int j = i > kStages ? i - kStages : 0; j < i; ++j) {
+          const uint64_t t0 = globaltimer_ns();
+          while (!mbar_try_wait(&pb->full[j % kStages], (j / kStages) & 1u) &&
+                 globaltimer_ns() - t0 < 50ull * 1000ull * 1000ull) {
+          }
         }
       }
     }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int i = 0, gc = 0;
+      bool ok = true;
+      for (long long t = blockIdx.x; t < g.tiles && ok; t += gridDim.x) {
+        const int oc0 = static_cast<int>(t % g.otiles) * kBN;
+        const int nn = min(kBN, ((g.M - oc0) + 15) & ~15);
+        const uint32_t idesc = idesc_tf32_amn(kBM, nn);
+        int kb = 0;
+        for (int c = 0; c < nchunks && ok; ++c, ++gc) {
+          const int buf = gc & 1;
+          if (!mbar_wait(&pb->acc_empty[buf], ((gc >> 1) & 1u) ^ 1u, &pb->abort_flag, err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t d = tmem + static_cast<uint32_t>(buf * kBN);
+          const int kb_end = min(g.num_kb, kb + kKC);
+          uint32_t acc = 0u;
+          for (; kb < kb_end; ++kb, ++i) {
+            const int s = i % kStages;
+            const uint32_t ph = (i / kStages) & 1u;
+            // conv[s] follows full[s] (the converters waited on it); the
+            // second wait returns at once and orders the weight boxes too.
+            if (!mbar_wait(&pb->conv[s], ph, &pb->abort_flag, err) ||
+                !mbar_wait(&pb->full[s], ph, &pb->abort_flag, err)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t base = smem_addr(tiles + s * kStage);
+            const uint64_t dAh = sdesc_mnmajor_sw128_32b(base, 4096, 512);
+            const uint64_t dAl = sdesc_mnmajor_sw128_32b(base + kA, 4096, 512);
+            const uint64_t dBh = sdesc_kmajor_sw128(base + 2 * kA);
+            const uint64_t dBl = sdesc_kmajor_sw128(base + 2 * kA + kB);
+#pragma unroll
+            for (int kk = 0; kk < kBK / 8; ++kk) {
+              const uint64_t ao = static_cast<uint64_t>(kk * 64);  // +1024 bytes: the next 8 channel rows
+              const uint64_t bo = static_cast<uint64_t>(kk * 2);   // +32 bytes inside the K-major row
+              mma_tf32(d, dAh + ao, dBh + bo, idesc, acc);
+              acc = 1u;
+              mma_tf32(d, dAh + ao, dBl + bo, idesc, 1u);
+              mma_tf32(d, dAl + ao, dBh + bo, idesc, 1u);
+            }
+            mma_commit(&pb->empty[s]);
+          }
+          if (ok) mma_commit(&pb->acc_full[buf]);
+        }
+      }
+      // Every MMA issued so far completes before TMEM is released.
+      mma_commit(&pb->mma_done);
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(&pb->mma_done, 0u) && globaltimer_ns() - t0 < 50ull * 1000ull * 1000ull) {
+      }
+    }
+  } else if (warp < kEpiBase) {
+    // converters: A (fp32 from TMA) -> hi in place, lo beside it
+    const int ct = threadIdx.x - 64;
+    int i = 0;
+    bool ok = true;
+    for (long long t = blockIdx.x; t < g.tiles && ok; t += gridDim.x) {
+      for (int kb = 0; kb < g.num_kb; ++kb, ++i) {
+        const int s = i % kStages;
+        const uint32_t ph = (i / kStages) & 1u;
+        bool got = mbar_wait(&pb->full[s], ph, &pb->abort_flag, err);
+        got = __all_sync(0xffffffffu, got);
+        if (!got) {
+          ok = false;
+          break;
+        }
+        float4* a = reinterpret_cast<float4*>(tiles + s * kStage);
+        float4* al = reinterpret_cast<float4*>(tiles + s * kStage + kA);
+#pragma unroll 4
+        for (int j = ct; j < kA / 16; j += 32 * kConvWarps) {
+          const float4 v = a[j];
+          float4 h, l;
+          h.x = to_tf32(v.x);
+          h.y = to_tf32(v.y);
+          h.z = to_tf32(v.z);
+          h.w = to_tf32(v.w);
+          l.x = __fsub_rn(v.x, h.x);
+          l.y = __fsub_rn(v.y, h.y);
+          l.z = __fsub_rn(v.z, h.z);
+          l.w = __fsub_rn(v.w, h.w);
+          a[j] = h;
+          al[j] = l;
+        }
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&pb->conv[s]);
+      }
+    }
+  } else {
+    // epilogue: warp kEpiBase + 4h + q drains TMEM lanes 32q.. (pixels p0 + 32q + lane),
+    // columns 64h.. (output channels oc0 + 64h ..)
+    const int q = warp & 3;
+    const int h = (warp - kEpiBase) >> 2;
+    int gc = 0;
+    bool ok = true;
+    for (long long t = blockIdx.x; t < g.tiles && ok; t += gridDim.x) {
+      const int ot = static_cast<int>(t % g.otiles);
+      const long long r = t / g.otiles;
+      const int pt = static_cast<int>(r % g.ptiles);
+      const int n = static_cast<int>(r / g.ptiles);
+      const int oc0 = ot * kBN + h * 64;
+      const int nvalid = min(64, g.M - oc0);  // may be <= 0 for the upper half of a narrow tile
+      float acc[64];
+      for (int c = 0; c < nchunks; ++c, ++gc) {
+        const int buf = gc & 1;
+        bool got = mbar_wait(&pb->acc_full[buf], (gc >> 1) & 1u, &pb->abort_flag, err);
+        got = __all_sync(0xffffffffu, got);
+        if (!got) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t base =
+            tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * kBN + h * 64);
+#pragma unroll
+        for (int gg = 0; gg < 4; gg += 2) {
+          uint32_t r0[16], r1[16];
+          tmem_ld16(base + gg * 16, r0);
+          tmem_ld16(base + (gg + 1) * 16, r1);
+          tmem_wait_ld();
+          if (c == 0) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              acc[gg * 16 + j] = __uint_as_float(r0[j]);
+              acc[(gg + 1) * 16 + j] = __uint_as_float(r1[j]);
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              acc[gg * 16 + j] = __fadd_rn(acc[gg * 16 + j], __uint_as_float(r0[j]));
+              acc[(gg + 1) * 16 + j] = __fadd_rn(acc[(gg + 1) * 16 + j], __uint_as_float(r1[j]));
+            }
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&pb->acc_empty[buf]);
+      }
+      if (!ok) break;
+      const int p = pt * kBM + q * 32 + lane;
+      if (p < g.HW && nvalid > 0) {
+        float* yp = y + static_cast<size_t>(n) * g.y_nstride + static_cast<size_t>(oc0) * g.HW + p;
+        const float* rp =
+            g.res ? g.res + static_cast<size_t>(n) * g.res_nstride + static_cast<size_t>(oc0) * g.HW + p : nullptr;
+        const float* sb = s_bias + oc0;
+        with_act(g.act, [&](auto tag) {
+          constexpr int ACT = decltype(tag)::value;
+#pragma unroll
+          for (int j0 = 0; j0 < 64; j0 += 8) {
+            // residuals of 8 channels in flight at once (clamped rows, no branch between the loads)
+            float rv[8];
+            if (rp) {
+#pragma unroll
+              for (int j = 0; j < 8; ++j)
+                rv[j] = __ldg(rp + static_cast<size_t>(min(j0 + j, nvalid - 1)) * g.HW);
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const int jj = min(j0 + j, nvalid - 1);
+              float o = act_t<ACT>(__fadd_rn(acc[j0 + j], sb[jj]));
+              if (rp) o = __fadd_rn(rv[j], o);  // residual Add(x, act(conv)) as in the graph
+              if (j0 + j < nvalid) yp[static_cast<size_t>(j0 + j) * g.HW] = o;
+            }
+          }
+        });
+      }
+    }
   }
-  pipe_teardown<Cfg>(pb, tmem);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
 }
 
 // NCHW x -> phase-split NHWC hi/lo: out[(phase*N + n)][h'][w'][c], Cp channels.
@@ -283,9 +598,64 @@ static void choose_box(int OH, int OW, int* BW, int* BH) {
   }
 }
 
+// 1x1 / stride 1 / no padding, NCHW input with 4-aligned pixel planes: the
+// transform-free pointwise kernel.
+static bool pointwise_ok(const osc_conv_weights* w, const float* x, long long x_nstride, int H, int W, int sh,
+                         int sw, int pt, int pl, int OH, int OW) {
+  static const bool off = [] {
+    const char* v = std::getenv("OSC_CONV_PW");
+    return v != nullptr && v[0] == '0';
+  }();
+  return !off && w->kh == 1 && w->kw == 1 && w->M <= pw::kMaxBias && sh == 1 && sw == 1 && pt == 0 && pl == 0 &&
+         OH == H && OW == W &&
+         (static_cast<long long>(H) * W) % 4 == 0 && x_nstride % 4 == 0 &&
+         (reinterpret_cast<uintptr_t>(x) & 15u) == 0;
+}
+
+static int conv1x1_tf32x3(osc_ctx* ctx, const float* x, long long x_nstride, int N, int C, int HW,
+                          const osc_conv_weights* w, const float* bias, int act, const float* res,
+                          long long res_nstride, float* y, long long y_nstride) {
+  PwGeom g{};
+  g.C = C;
+  g.HW = HW;
+  g.M = w->M;
+  g.ptiles = (HW + kBM - 1) / kBM;
+  g.otiles = (w->M + pw::kBN - 1) / pw::kBN;
+  g.tiles = static_cast<long long>(N) * g.ptiles * g.otiles;
+  g.num_kb = w->Cp / kBK;
+  g.act = act;
+  g.y_nstride = y_nstride;
+  g.res_nstride = res_nstride;
+  g.res = res;
+  CUtensorMap mX, mWh, mWl;
+  {
+    const uint64_t dims[3] = {static_cast<uint64_t>(HW), static_cast<uint64_t>(C), static_cast<uint64_t>(N)};
+    const uint64_t pitch[2] = {static_cast<uint64_t>(HW) * 4, static_cast<uint64_t>(x_nstride) * 4};
+    const uint32_t box[3] = {32, kBK, 1};
+    OSC_TRY(encode_tiled(&mX, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, x, dims, pitch, box,
+                         CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B));
+  }
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(w->Kp), static_cast<uint64_t>(w->M)};
+    const uint64_t pitch[1] = {static_cast<uint64_t>(w->Kp) * 4};
+    const uint32_t box[2] = {kBK, pw::kBN};
+    OSC_TRY(encode_tiled(&mWh, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, w->hi, dims, pitch, box, CU_TENSOR_MAP_SWIZZLE_128B));
+    OSC_TRY(encode_tiled(&mWl, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, w->lo, dims, pitch, box, CU_TENSOR_MAP_SWIZZLE_128B));
+  }
+  const int smem = pw::kSmemBase + static_cast<int>(round_up(static_cast<size_t>(w->M) * 4, 16));
+  OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(k_conv1x1_tf32x3), smem));
+  const long long grid = std::min<long long>(g.tiles, ctx->num_sms);
+  prof_begin(ctx);
+  k_conv1x1_tf32x3<<<static_cast<unsigned>(grid), pw::kThreads, smem, ctx->stream>>>(mX, mWh, mWl, g, bias, y,
+                                                                                         ctx->d_err);
+  return check_launch(ctx, "k_conv1x1_tf32x3");
+}
+
 int conv_tf32x3(osc_ctx* ctx, const float* x, long long x_nstride, int N, int C, int H, int W, const osc_conv_weights* w,
                 int sh, int sw, int pt, int pl, int dh, int dw, const float* bias, int act, const float* res,
                 long long res_nstride, float* y, long long y_nstride, int OH, int OW) {
+  if (pointwise_ok(w, x, x_nstride, H, W, sh, sw, pt, pl, OH, OW))
+    return conv1x1_tf32x3(ctx, x, x_nstride, N, C, H * W, w, bias, act, res, res_nstride, y, y_nstride);
   if (sh != sw) return fail(OSC_EUNSUPPORTED, "conv: unequal strides %d x %d", sh, sw);
   const int s = sh;
   const int Hp = (H + s - 1) / s, Wp = (W + s - 1) / s;

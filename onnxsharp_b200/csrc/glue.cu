@@ -315,31 +315,34 @@ __global__ void __launch_bounds__(32 * G * P) k_conv_tile(
   const size_t plane = static_cast<size_t>(OH) * OW;
   float* yn = y + static_cast<size_t>(n) * y_nstride + static_cast<size_t>(oy) * OW + ox;
   const float* rn = res ? res + static_cast<size_t>(n) * res_nstride + static_cast<size_t>(oy) * OW + ox : nullptr;
+  with_act(act, [&](auto tag) {
+    constexpr int ACT = decltype(tag)::value;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int oc = oc0 + og * 8 + i;
-    if (oc >= M) break;
-    float v[4];
+    for (int i = 0; i < 8; ++i) {
+      const int oc = oc0 + og * 8 + i;
+      if (oc >= M) break;
+      float v[4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) v[j] = apply_act(acc[i][j], act);
-    const size_t off = static_cast<size_t>(oc) * plane;
-    if (vec4 && ox + 4 <= OW) {
-      if (rn) {
-        const float4 rv = *reinterpret_cast<const float4*>(rn + off);
-        v[0] = __fadd_rn(rv.x, v[0]);
-        v[1] = __fadd_rn(rv.y, v[1]);
-        v[2] = __fadd_rn(rv.z, v[2]);
-        v[3] = __fadd_rn(rv.w, v[3]);
-      }
-      *reinterpret_cast<float4*>(yn + off) = make_float4(v[0], v[1], v[2], v[3]);
-    } else {
+      for (int j = 0; j < 4; ++j) v[j] = act_t<ACT>(acc[i][j]);
+      const size_t off = static_cast<size_t>(oc) * plane;
+      if (vec4 && ox + 4 <= OW) {
+        if (rn) {
+          const float4 rv = *reinterpret_cast<const float4*>(rn + off);
+          v[0] = __fadd_rn(rv.x, v[0]);
+          v[1] = __fadd_rn(rv.y, v[1]);
+          v[2] = __fadd_rn(rv.z, v[2]);
+          v[3] = __fadd_rn(rv.w, v[3]);
+        }
+        *reinterpret_cast<float4*>(yn + off) = make_float4(v[0], v[1], v[2], v[3]);
+      } else {
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        if (ox + j >= OW) break;
-        yn[off + j] = rn ? __fadd_rn(rn[off + j], v[j]) : v[j];
+        for (int j = 0; j < 4; ++j) {
+          if (ox + j >= OW) break;
+          yn[off + j] = rn ? __fadd_rn(rn[off + j], v[j]) : v[j];
+        }
       }
     }
-  }
+  });
 }
 
 template <int K, int S, int G, int P>

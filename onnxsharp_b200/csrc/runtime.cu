@@ -12,6 +12,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <map>
 #include <mutex>
 #include <set>
 #include <thread>
@@ -163,14 +164,17 @@ int check_launch(osc_ctx* ctx, const char* what) {
 }
 
 int set_smem_attr(osc_ctx* ctx, const void* func, int bytes) {
+  // The attribute is raised whenever a launch needs more than was set before
+  // (kernels whose shared memory depends on the shape).
   static std::mutex mu;
-  static std::set<std::pair<int, const void*>> done;
+  static std::map<std::pair<int, const void*>, int> set_bytes;
   std::lock_guard<std::mutex> lock(mu);
   const auto key = std::make_pair(ctx->device, func);
-  if (done.count(key)) return OSC_OK;
+  const auto it = set_bytes.find(key);
+  if (it != set_bytes.end() && it->second >= bytes) return OSC_OK;
   OSC_CUDA(cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes),
            "cudaFuncSetAttribute (dynamic shared memory)");
-  done.insert(key);
+  set_bytes[key] = bytes;
   return OSC_OK;
 }
 

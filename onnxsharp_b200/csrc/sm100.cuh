@@ -230,6 +230,24 @@ __device__ __forceinline__ uint64_t sdesc_kmajor_sw128(uint32_t saddr) {
   return d;
 }
 
+// Shared-memory matrix descriptor for an MN-major TF32 operand tile. For
+// 32-bit elements the MN-major layout the tensor core accepts is the 128-byte
+// swizzle with 32-byte atomicity (layout type 1): rows of 128 bytes along M
+// (or N) = 32 elements, rows along K, and the 32-byte chunk c of row r stored
+// at chunk c ^ (r % 4) -- what a TMA tiled load with
+// CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B and a 32-element inner box writes.
+// 4-row K groups are `sbo` bytes apart, 32-element M groups `lbo` bytes
+// apart; one 8-wide tf32 K step covers two K groups. Tile base 1024-aligned.
+__device__ __forceinline__ uint64_t sdesc_mnmajor_sw128_32b(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);          // start address  [0,14)
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;       // leading byte offset: M-group pitch
+  d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;       // stride byte offset: 4-row K-group pitch
+  d |= static_cast<uint64_t>(1u) << 46;                          // descriptor version for sm_100
+  d |= static_cast<uint64_t>(1u) << 61;                          // layout: SWIZZLE_128B_BASE32B
+  return d;
+}
+
 // ---------------------------------------------------------------- CTA pairs (cta_group::2)
 // A cluster of two CTAs shares one MMA: the even CTA (rank 0) issues
 // tcgen05.mma.cta_group::2 with M = 256, reading A rows 0-127 from its own
@@ -308,6 +326,8 @@ __host__ __device__ constexpr uint32_t idesc_tf32(int M, int N) {
          | (static_cast<uint32_t>(N >> 3) << 17)     // N / 8
          | (static_cast<uint32_t>(M >> 4) << 24);    // M / 16
 }
+// The same with A read MN-major (bit 15); B stays K-major.
+__host__ __device__ constexpr uint32_t idesc_tf32_amn(int M, int N) { return idesc_tf32(M, N) | (1u << 15); }
 __host__ __device__ constexpr uint32_t idesc_u8s8(int M, int N) {
   return (2u << 4)                                   // D format: S32
          | (0u << 7)                                 // A: unsigned 8-bit

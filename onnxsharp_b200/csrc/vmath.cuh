@@ -75,4 +75,33 @@ __device__ __forceinline__ float apply_act(float v, int act) {
   }
 }
 
+// The activation as a compile-time constant: a loop over act_t<ACT> has no
+// branch per element, so the compiler interleaves the independent exp /
+// reciprocal chains of consecutive elements (with a runtime switch inside
+// the loop each element's chain runs alone, latency-bound).
+template <int ACT>
+__device__ __forceinline__ float act_t(float v) {
+  if constexpr (ACT == ACT_SILU) return ref_silu(v);
+  else if constexpr (ACT == ACT_RELU) return v > 0.0f ? v : 0.0f;
+  else if constexpr (ACT == ACT_SIGMOID) return ref_sigmoid(v);
+  else return v;
+}
+
+template <int A>
+struct ActTag {
+  static constexpr int value = A;
+};
+
+// Calls f(ActTag<ACT>{}) with the runtime code `act` turned into a constant;
+// f is a generic lambda that reads decltype(tag)::value.
+template <class F>
+__device__ __forceinline__ void with_act(int act, F&& f) {
+  switch (act) {
+    case ACT_SILU: f(ActTag<ACT_SILU>{}); break;
+    case ACT_RELU: f(ActTag<ACT_RELU>{}); break;
+    case ACT_SIGMOID: f(ActTag<ACT_SIGMOID>{}); break;
+    default: f(ActTag<ACT_NONE>{}); break;
+  }
+}
+
 }  // namespace osc

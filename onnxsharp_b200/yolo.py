@@ -301,15 +301,19 @@ class Net:
 
     @staticmethod
     def tensor_core(node) -> bool:
-        """Tensor-core implicit GEMM for group-1 convs, except the narrow layers:
-        16 or fewer output channels, or a reduction C_in*k*k <= 144 with C_in < 64
-        (stem, 16->32 3x3, the 8/16-channel bottlenecks, 32/48-channel 1x1s).
-        There a 128-channel MMA tile and the 32-channel K padding of the hi/lo
-        transform waste most of the work, and the register-blocked CUDA-core
-        kernel is faster (measured per layer at B=64 on B200)."""
+        """Tensor cores for the group-1 convs except the narrow layers: 16 or
+        fewer output channels, or a reduction C_in*k*k <= 144 with C_in < 64
+        (stem, 16->32 3x3, the 8/16-channel bottlenecks, the 32/48-channel 1x1s
+        at 160x160). There the register-blocked CUDA-core kernel is faster: the
+        tensor-core kernels' fixed cost per 128-pixel tile dominates when a
+        tile holds few channels (measured per layer at B=64 on B200). 1x1
+        convs with C_in >= 64 take the pointwise kernel, which reads NCHW
+        directly."""
         if node.attrs["group"] != 1:
             return False
         cin, cout, k = node.ins[0].c, node.outs[0].c, node.attrs["k"]
+        if k == 1 and node.attrs["s"] == 1 and cin >= 64:
+            return True
         return not (cout <= 16 or (cin * k * k <= 144 and cin < 64))
 
     def view(self, r: Ref):

@@ -99,3 +99,44 @@ def test_conv_rejects_bad_output_size_and_groups(ctx):
     with pytest.raises(OscError):  # grouped conv is a different entry point
         _lib.call("osc_conv2d_bias_act_f32", ctx.handle, x.data_ptr(), 1, 8, 10, 10, cw.handle, 1, 1, 1, 1, 1, 1, 1,
                   1, 2, None, 0, y.data_ptr(), 10, 10)
+
+
+@pytest.mark.parametrize(
+    "N,C,H,W,M,act",
+    [
+        (3, 96, 40, 40, 128, 1),    # 12.5 pixel tiles per image
+        (1, 32, 160, 160, 32, 1),   # narrow: MMA N = 32
+        (2, 80, 80, 80, 80, 1),     # MMA N = 80, K padded to 96
+        (1, 512, 20, 20, 256, 0),   # K = 512: 16 k-blocks in 8 TMEM chunks, 2 channel tiles
+        (2, 7, 6, 6, 5, 3),         # C = 7, M = 5 (N rounded to 16), Sigmoid
+        (1, 16, 5, 5, 16, 1),       # 25-pixel planes: not 16-byte aligned, implicit-GEMM fallback
+    ],
+)
+def test_conv_pointwise(ctx, N, C, H, W, M, act):
+    """1x1 convs read NCHW directly (A operand MN-major, hi/lo split in shared memory)."""
+    x, w, b = _case(N * 7 + C + M, N, C, H, W, M, 1)
+    y = _conv(ctx, x, w, b, act=act)
+    assert rel_err(y, oracle.conv2d(x, w, b, act=act)) <= TOL
+
+
+def test_conv_pointwise_views_and_residual(ctx):
+    """The C3k2 / C2PSA pattern: input a channel slice (Split), output a slice of
+    a Concat buffer, residual Add fused: y = res + SiLU(conv1x1(x) + b)."""
+    import torch
+
+    from onnxsharp_b200 import ops
+    from onnxsharp_b200.runtime import ConvWeights
+
+    rng = np.random.default_rng(31)
+    big_x = rng.uniform(0, 1, (3, 200, 20, 20)).astype(np.float32)
+    w = (rng.normal(0, 1, (64, 128, 1, 1)) * np.sqrt(2.0 / 128)).astype(np.float32)
+    b = rng.normal(0, 0.01, 64).astype(np.float32)
+    res = rng.normal(0, 1, (3, 64, 20, 20)).astype(np.float32)
+    out_big = torch.zeros(3, 192, 20, 20, device="cuda")
+    ops.conv2d_ex(ctx, torch.from_numpy(big_x).cuda()[:, 36:164], ConvWeights(ctx, torch.from_numpy(w).cuda(), w.shape),
+                  torch.from_numpy(b).cuda(), out_big[:, 64:128], 1, 0, 1, 1, torch.from_numpy(res).cuda())
+    ctx.synchronize()
+    ref = res + oracle.conv2d(np.ascontiguousarray(big_x[:, 36:164]), w, b, act=1)
+    got = out_big.cpu().numpy()
+    assert rel_err(got[:, 64:128], ref) <= TOL
+    assert not got[:, :64].any() and not got[:, 128:].any()
