@@ -359,8 +359,15 @@ OSC_API int osc_yolo_detect_f32(osc_ctx* ctx, const float* output, int B, int fi
                                 float iou, int max_det, int max_candidates, int class_agnostic,
                                 const float* transforms, float* dets, int* counts);
 
+/* Diagnostics (no counterpart in the reference): the maximum error, over
+ * every finite float x, of the hardware-instruction Sigmoid and SiLU used in
+ * the tensor-core conv epilogues against the exact VectorMath restatement, in
+ * the parity metric |fast - exact| / max(1, |exact|). */
+OSC_API int osc_selfcheck_fast_act(osc_ctx* ctx, float* max_sigmoid_err, float* max_silu_err);
+
 /* Diagnostics (no counterpart in the reference): checks on the device that the
- * branch-free reciprocal inside the fused Sigmoid/SiLU epilogues returns the
+ * branch-free reciprocal inside the exact Sigmoid/SiLU (the CUDA-core
+ * epilogues and the activation ops) returns the
  * same bits as the IEEE division 1/d for every float d in [1, 2^126) (the
  * range of 1 + exp(-x) after the reference's clamp). *mismatches gets the
  * count, *first_bad the first differing d's bits (0 if none); both are host

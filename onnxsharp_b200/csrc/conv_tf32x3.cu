@@ -16,8 +16,9 @@
 //    the image are zeros written by the transform or TMA's out-of-bounds
 //    fill (negative box coordinates are legal for loads; the channel
 //    coordinate, innermost, is always a multiple of 32).
-//  - Epilogue: bias[oc] + activation (VectorMath SiLU restated) and
-//    coalesced NCHW stores through a shared-memory staging tile.
+//  - Epilogue: bias[oc] + activation (Sigmoid/SiLU from the hardware ex2 /
+//    rcp instructions, act_fast) and coalesced NCHW stores through a
+//    shared-memory staging tile.
 // The reference's im2col path accumulates acc = b[oc], then FMA over
 // (ic, ky, kx) (Kernels/ConvKernels.cs:262-462); the tensor cores sum in a
 // different order, so parity is |d| / max(1, |ref|) <= 1e-4.
@@ -140,7 +141,7 @@ __global__ void __launch_bounds__(ConvCfg::THREADS, 1)
           const float* rsrc = rplane ? rplane + static_cast<size_t>(oy) * g.OW + ox : nullptr;
           float o[4];
 #pragma unroll
-          for (int q = 0; q < 4; ++q) o[q] = act_t<ACT>(__fadd_rn(v[q], b));
+          for (int q = 0; q < 4; ++q) o[q] = act_fast<ACT>(__fadd_rn(v[q], b));
           if (g.vec4 && ox + 4 <= g.OW) {  // one 16-byte store: whole 32-byte sectors per warp
             if (rsrc) {
               const float4 rv = __ldg(reinterpret_cast<const float4*>(rsrc));
@@ -457,7 +458,7 @@ __global__ void __launch_bounds__(pw::kThreads, 1)
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
               const int jj = min(j0 + j, nvalid - 1);
-              float o = act_t<ACT>(__fadd_rn(acc[j0 + j], sb[jj]));
+              float o = act_fast<ACT>(__fadd_rn(acc[j0 + j], sb[jj]));
               if (rp) o = __fadd_rn(rv[j], o);  // residual Add(x, act(conv)) as in the graph
               if (j0 + j < nvalid) yp[static_cast<size_t>(j0 + j) * g.HW] = o;
             }

@@ -11,6 +11,7 @@
 // are pointer offsets and Concat inputs are written in place.
 #include <algorithm>
 #include <cmath>
+#include <cstring>
 
 #include "runtime.h"
 #include "vmath.cuh"
@@ -694,12 +695,56 @@ __global__ void k_selfcheck_recip(unsigned long long* mismatches, unsigned int* 
   if ((threadIdx.x & 31) == 0 && bad) atomicAdd(mismatches, bad);
 }
 
+// The hardware-instruction sigmoid / SiLU of the tensor-core epilogues
+// against the exact restatement, over every finite float x, in the parity
+// metric |fast - exact| / max(1, |exact|). The maxima are non-negative floats,
+// so their bit patterns order like the values (atomicMax on the bits).
+__global__ void k_selfcheck_fast_act(unsigned int* max_sigmoid, unsigned int* max_silu) {
+  float ms = 0.0f, mu = 0.0f;
+  for (unsigned long long i = blockIdx.x * static_cast<unsigned long long>(blockDim.x) + threadIdx.x;
+       i < 0x100000000ull; i += static_cast<unsigned long long>(gridDim.x) * blockDim.x) {
+    const float x = __uint_as_float(static_cast<unsigned int>(i));
+    if (!isfinite(x)) continue;
+    const float s0 = ref_sigmoid(x), s1 = act_fast<ACT_SIGMOID>(x);
+    const float u0 = ref_silu(x), u1 = act_fast<ACT_SILU>(x);
+    ms = fmaxf(ms, fabsf(s1 - s0) / fmaxf(1.0f, fabsf(s0)));
+    mu = fmaxf(mu, fabsf(u1 - u0) / fmaxf(1.0f, fabsf(u0)));
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    ms = fmaxf(ms, __shfl_xor_sync(0xffffffffu, ms, o));
+    mu = fmaxf(mu, __shfl_xor_sync(0xffffffffu, mu, o));
+  }
+  if ((threadIdx.x & 31) == 0) {
+    atomicMax(max_sigmoid, __float_as_uint(ms));
+    atomicMax(max_silu, __float_as_uint(mu));
+  }
+}
+
 }  // namespace
 }  // namespace osc
 
 using namespace osc;
 
 extern "C" {
+
+OSC_API int osc_selfcheck_fast_act(osc_ctx* ctx, float* max_sigmoid_err, float* max_silu_err) {
+  OSC_TRY(enter(ctx));
+  if (max_sigmoid_err == nullptr || max_silu_err == nullptr)
+    return fail(OSC_EINVAL, "osc_selfcheck_fast_act: null output");
+  void* buf = nullptr;
+  OSC_TRY(scratch(ctx, 256, &buf));
+  auto* d = static_cast<unsigned int*>(buf);
+  OSC_CUDA(cudaMemsetAsync(d, 0, 2 * sizeof(unsigned int), ctx->stream), "selfcheck reset");
+  prof_begin(ctx);
+  k_selfcheck_fast_act<<<ctx->num_sms * 8, 256, 0, ctx->stream>>>(d, d + 1);
+  OSC_TRY(check_launch(ctx, "k_selfcheck_fast_act"));
+  unsigned int h[2] = {0, 0};
+  OSC_CUDA(cudaMemcpyAsync(h, d, sizeof(h), cudaMemcpyDeviceToHost, ctx->stream), "selfcheck read");
+  OSC_CUDA(cudaStreamSynchronize(ctx->stream), "selfcheck sync");
+  std::memcpy(max_sigmoid_err, &h[0], sizeof(float));
+  std::memcpy(max_silu_err, &h[1], sizeof(float));
+  return OSC_OK;
+}
 
 OSC_API int osc_selfcheck_recip(osc_ctx* ctx, unsigned long long* mismatches, unsigned int* first_bad) {
   OSC_TRY(enter(ctx));

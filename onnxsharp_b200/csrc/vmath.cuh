@@ -87,6 +87,31 @@ __device__ __forceinline__ float act_t(float v) {
   else return v;
 }
 
+// Sigmoid and SiLU for the tensor-core conv epilogues: 1 / (1 + 2^(-x log2 e))
+// from the hardware ex2.approx and rcp.approx instructions (relative errors
+// 2^-22 and 2^-23), 5 instructions instead of the ~25 of the exact restatement
+// above. The error of the result stays below 1e-6 relative for |x| < 10
+// (beyond, the rounding of the exponent's argument grows with |x| while the
+// sigmoid saturates, and SiLU's absolute error stays below 1e-7). Those
+// epilogues take the sum of a 3xTF32 tensor-core product, which already
+// differs from the reference's FMA-chain sum at the 1e-6 level, so the
+// bit-exact polynomial cannot make their outputs bit-identical anyway; the
+// CUDA-core kernels whose sums are bit-identical keep act_t.
+__device__ __forceinline__ float fast_sigmoid(float x) {
+  float e, r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(__fmul_rn(x, -1.4426950408889634f)));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(__fadd_rn(1.0f, e)));
+  return r;
+}
+
+template <int ACT>
+__device__ __forceinline__ float act_fast(float v) {
+  if constexpr (ACT == ACT_SILU) return __fmul_rn(v, fast_sigmoid(v));
+  else if constexpr (ACT == ACT_RELU) return v > 0.0f ? v : 0.0f;
+  else if constexpr (ACT == ACT_SIGMOID) return fast_sigmoid(v);
+  else return v;
+}
+
 template <int A>
 struct ActTag {
   static constexpr int value = A;

@@ -20,3 +20,16 @@ def test_branch_free_reciprocal_equals_ieee_division_exhaustively(ctx):
     first = C.c_uint(0)
     call("osc_selfcheck_recip", ctx.handle, C.byref(bad), C.byref(first))
     assert bad.value == 0, f"{bad.value} mismatches, first at bits {first.value:#010x}"
+
+
+def test_fast_epilogue_activation_within_parity_tolerance(ctx):
+    """The tensor-core conv epilogues use hardware ex2/rcp for Sigmoid and SiLU.
+    Over every finite float the result stays within 2e-6 of the exact
+    restatement in the parity metric |d| / max(1, |ref|) (tolerance 1e-4)."""
+    from onnxsharp_b200._lib import call
+
+    sig = C.c_float(0)
+    silu = C.c_float(0)
+    call("osc_selfcheck_fast_act", ctx.handle, C.byref(sig), C.byref(silu))
+    assert sig.value <= 2e-6, sig.value
+    assert silu.value <= 2e-6, silu.value
