@@ -475,43 +475,65 @@ __global__ void __launch_bounds__(pw::kThreads, 1)
   }
 }
 
-// NCHW x -> phase-split NHWC hi/lo: out[(phase*N + n)][h'][w'][c], Cp channels.
-// One block per (n, phase-row h' of phase py, 32-wide w' strip, 32-channel
-// strip): reads 32 channels x 32 pixels of one input row, writes them
-// channel-innermost.
-__global__ void k_nchw_to_phase_nhwc(const float* __restrict__ x, long long x_nstride, int N, int C, int H, int W,
-                                     int s, int Hp, int Wp, int Cp, int z_base, float* __restrict__ hi,
-                                     float* __restrict__ lo) {
-  __shared__ float tile[32][33];
-  const int wq = blockIdx.x * 32;        // w' strip start
-  const int c0 = blockIdx.y * 32;        // channel strip
-  int z = z_base + blockIdx.z;           // ((py*s + px) * N + n) * Hp + h'
-  const int hq = z % Hp;
-  z /= Hp;
-  const int n = z % N;
-  const int phase = z / N;
-  const int py = phase / s, px = phase % s;
-  const int ih = hq * s + py;
-  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8
-  for (int yy = ty; yy < 32; yy += 8) {
-    const int c = c0 + yy;
-    const int iw = (wq + tx) * s + px;
-    float v = 0.0f;
-    if (c < C && ih < H && iw < W && (wq + tx) < Wp)
-      v = x[static_cast<size_t>(n) * x_nstride + (static_cast<size_t>(c) * H + ih) * W + iw];
-    tile[yy][tx] = v;
+// NCHW x -> phase-split NHWC hi/lo: out[(phase*N + n)][h'][w'][c], Cp channels,
+// phase = py*s + px for input pixel (h'*s + py, w'*s + px). One block per
+// (input row h < Hp*s, strip of 32*s input pixels, 32-channel strip; rows past
+// the image give the zeros of the last phase rows): the row strip is
+// read once with 16-byte loads (contiguous, all s phases at a time) and each
+// of the s phase rows it feeds is written channel-innermost with 16-byte hi/lo
+// stores.
+constexpr int kPhaseMaxS = 4;
+__global__ void __launch_bounds__(256) k_nchw_to_phase_nhwc(const float* __restrict__ x, long long x_nstride, int N,
+                                                            int C, int H, int W, int s, int Hp, int Wp, int Cp,
+                                                            int z_base, float* __restrict__ hi,
+                                                            float* __restrict__ lo) {
+  __shared__ float tile[32][32 * kPhaseMaxS + 1];
+  const int span = 32 * s;               // input pixels of this strip
+  const int w0 = blockIdx.x * span;      // first input pixel
+  const int c0 = blockIdx.y * 32;
+  const int z = z_base + blockIdx.z;     // n * Hp*s + ih: rows ih >= H are the zero rows of the last phase row
+  const int ih = z % (Hp * s), n = z / (Hp * s);
+  const int tid = threadIdx.x;
+  // read: thread -> channel tid/8, pixels (tid%8)*4 + 32*k for k < s
+  {
+    const int c = c0 + (tid >> 3);
+    const float* src = x + static_cast<size_t>(n) * x_nstride + (static_cast<size_t>(c) * H + ih) * W;
+    for (int k = 0; k < s; ++k) {
+      const int wl = (tid & 7) * 4 + 32 * k, w = w0 + wl;
+      float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      if (c < C && ih < H) {
+        if (w + 4 <= W && (reinterpret_cast<uintptr_t>(src + w) & 15u) == 0) {
+          const float4 t = __ldg(reinterpret_cast<const float4*>(src + w));
+          v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+        } else {
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            if (w + q < W) v[q] = __ldg(src + w + q);
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < 4; ++q) tile[tid >> 3][wl + q] = v[q];
+    }
   }
   __syncthreads();
-  for (int yy = ty; yy < 32; yy += 8) {
-    const int wqq = wq + yy;
-    const int c = c0 + tx;
-    if (wqq < Wp && c < Cp) {
-      const float v = tile[tx][yy];
-      const float h = to_tf32(v);
-      const size_t o = (((static_cast<size_t>(phase) * N + n) * Hp + hq) * Wp + wqq) * Cp + c;
-      hi[o] = h;
-      lo[o] = __fsub_rn(v, h);
+  // write: for each column phase px, thread -> w' = tid/8 of the strip, channels (tid%8)*4..+3
+  const int py = ih % s, hq = ih / s;
+  const int wq = blockIdx.x * 32 + (tid >> 3);
+  const int cq = (tid & 7) * 4;
+  if (hq >= Hp || wq >= Wp || c0 + cq >= Cp) return;
+  for (int px = 0; px < s; ++px) {
+    const int wl = (tid >> 3) * s + px;  // input pixel of w' in this strip
+    float h4[4], l4[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float v = tile[cq + q][wl];
+      h4[q] = to_tf32(v);
+      l4[q] = __fsub_rn(v, h4[q]);
     }
+    const int phase = py * s + px;
+    const size_t o = (((static_cast<size_t>(phase) * N + n) * Hp + hq) * Wp + wq) * Cp + c0 + cq;
+    *reinterpret_cast<float4*>(hi + o) = make_float4(h4[0], h4[1], h4[2], h4[3]);
+    *reinterpret_cast<float4*>(lo + o) = make_float4(l4[0], l4[1], l4[2], l4[3]);
   }
 }
 
@@ -669,7 +691,9 @@ int conv_tf32x3(osc_ctx* ctx, const float* x, long long x_nstride, int N, int C,
   float* xh = static_cast<float*>(buf);
   float* xl = reinterpret_cast<float*>(static_cast<uint8_t*>(buf) + half);
   {
-    const long zt = static_cast<long>(s) * s * N * Hp;
+    if (s > kPhaseMaxS) return fail(OSC_EUNSUPPORTED, "conv: stride %d (at most %d)", s, kPhaseMaxS);
+    // s == 1: one z per output row; s > 1: one z per input row (all phases of it), Hp*s rows per image
+    const long zt = s == 1 ? static_cast<long>(N) * Hp : static_cast<long>(N) * Hp * s;
     const long zmax = 65535;  // gridDim.z limit: split into several launches
     for (long z0 = 0; z0 < zt; z0 += zmax) {
       dim3 grid((Wp + 31) / 32, Cp / 32, static_cast<unsigned>(std::min(zmax, zt - z0)));
