@@ -55,8 +55,14 @@ enum osc_status {
   OSC_EUNSUPPORTED = 7       /* valid ONNX, not implemented by this backend */
 };
 
-/* Fused activation codes (Conv.FusedActivation, Ops/DnnOps.cs:104, :493-499). */
-enum osc_act { OSC_ACT_NONE = 0, OSC_ACT_SILU = 1, OSC_ACT_RELU = 2, OSC_ACT_SIGMOID = 3 };
+/* Fused activation codes (Conv.FusedActivation, Ops/DnnOps.cs:104, :493-499).
+ * OSC_ACT_FAST may be OR-ed into the code given to osc_conv2d_direct_f32:
+ * Sigmoid / SiLU then come from the hardware ex2 / rcp instructions (within
+ * 2e-6 of the exact form in |d| / max(1, |ref|), see osc_selfcheck_fast_act)
+ * instead of the reference's VectorMath restated bit for bit. The tensor-core
+ * conv entries always compute the fast form (their sums are not bit-identical
+ * to the reference's anyway); the other entries accept the plain codes. */
+enum osc_act { OSC_ACT_NONE = 0, OSC_ACT_SILU = 1, OSC_ACT_RELU = 2, OSC_ACT_SIGMOID = 3, OSC_ACT_FAST = 16 };
 
 typedef struct osc_ctx osc_ctx;
 typedef struct osc_gemm_weights osc_gemm_weights;

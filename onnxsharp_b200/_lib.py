@@ -30,6 +30,7 @@ STATUS_NAMES = {
 
 # activation codes (enum osc_act)
 ACT_NONE, ACT_SILU, ACT_RELU, ACT_SIGMOID = 0, 1, 2, 3
+ACT_FAST = 16  # OR into conv2d_direct's activation: hardware ex2/rcp Sigmoid/SiLU
 
 
 class OscError(RuntimeError):

@@ -781,7 +781,9 @@ OSC_API int osc_conv2d_direct_f32(osc_ctx* ctx, const float* x, long long x_nstr
   const int ow = (W + pad_l + pad_r - ((kw - 1) * dil_w + 1)) / stride_w + 1;
   if (oh != OH || ow != OW || oh <= 0 || ow <= 0)
     return fail(OSC_EINVAL, "osc_conv2d_direct_f32: output must be %dx%d, got %dx%d", oh, ow, OH, OW);
-  if (act < OSC_ACT_NONE || act > OSC_ACT_SIGMOID) return fail(OSC_EINVAL, "osc_conv2d_direct_f32: act=%d", act);
+  const int act_code = act & ~OSC_ACT_FAST;
+  if (act_code < OSC_ACT_NONE || act_code > OSC_ACT_SIGMOID)
+    return fail(OSC_EINVAL, "osc_conv2d_direct_f32: act=%d", act);
   if (x_nstride == 0) x_nstride = static_cast<long long>(C) * H * W;
   if (y_nstride == 0) y_nstride = static_cast<long long>(M) * OH * OW;
   if (res_nstride == 0) res_nstride = static_cast<long long>(M) * OH * OW;

@@ -64,28 +64,14 @@ __device__ __forceinline__ float ref_sigmoid(float x) {
 __device__ __forceinline__ float ref_silu(float x) { return __fmul_rn(x, ref_sigmoid(x)); }
 
 // Activation codes shared by every fused epilogue (match osc_act in the C ABI).
-enum : int { ACT_NONE = 0, ACT_SILU = 1, ACT_RELU = 2, ACT_SIGMOID = 3 };
-
-__device__ __forceinline__ float apply_act(float v, int act) {
-  switch (act) {
-    case ACT_SILU: return ref_silu(v);
-    case ACT_RELU: return v > 0.0f ? v : 0.0f;
-    case ACT_SIGMOID: return ref_sigmoid(v);
-    default: return v;
-  }
-}
+// ACT_FAST may be OR-ed into SiLU / Sigmoid: the hardware-instruction form
+// (fast_sigmoid below) instead of the exact restatement.
+enum : int { ACT_NONE = 0, ACT_SILU = 1, ACT_RELU = 2, ACT_SIGMOID = 3, ACT_FAST = 16 };
 
 // The activation as a compile-time constant: a loop over act_t<ACT> has no
 // branch per element, so the compiler interleaves the independent exp /
 // reciprocal chains of consecutive elements (with a runtime switch inside
 // the loop each element's chain runs alone, latency-bound).
-template <int ACT>
-__device__ __forceinline__ float act_t(float v) {
-  if constexpr (ACT == ACT_SILU) return ref_silu(v);
-  else if constexpr (ACT == ACT_RELU) return v > 0.0f ? v : 0.0f;
-  else if constexpr (ACT == ACT_SIGMOID) return ref_sigmoid(v);
-  else return v;
-}
 
 // Sigmoid and SiLU for the tensor-core conv epilogues: 1 / (1 + 2^(-x log2 e))
 // from the hardware ex2.approx and rcp.approx instructions (relative errors
@@ -106,10 +92,37 @@ __device__ __forceinline__ float fast_sigmoid(float x) {
 
 template <int ACT>
 __device__ __forceinline__ float act_fast(float v) {
-  if constexpr (ACT == ACT_SILU) return __fmul_rn(v, fast_sigmoid(v));
-  else if constexpr (ACT == ACT_RELU) return v > 0.0f ? v : 0.0f;
-  else if constexpr (ACT == ACT_SIGMOID) return fast_sigmoid(v);
+  constexpr int A = ACT & ~ACT_FAST;
+  if constexpr (A == ACT_SILU) return __fmul_rn(v, fast_sigmoid(v));
+  else if constexpr (A == ACT_RELU) return v > 0.0f ? v : 0.0f;
+  else if constexpr (A == ACT_SIGMOID) return fast_sigmoid(v);
   else return v;
+}
+
+// The activation as a compile-time constant: a loop over act_t<ACT> has no
+// branch per element, so the compiler interleaves the independent exp /
+// reciprocal chains of consecutive elements (with a runtime switch inside
+// the loop each element's chain runs alone, latency-bound). ACT_FAST picks
+// the hardware-instruction form.
+template <int ACT>
+__device__ __forceinline__ float act_t(float v) {
+  if constexpr ((ACT & ACT_FAST) != 0) return act_fast<ACT>(v);
+  else if constexpr (ACT == ACT_SILU) return ref_silu(v);
+  else if constexpr (ACT == ACT_RELU) return v > 0.0f ? v : 0.0f;
+  else if constexpr (ACT == ACT_SIGMOID) return ref_sigmoid(v);
+  else return v;
+}
+
+__device__ __forceinline__ float apply_act(float v, int act) {
+  switch (act) {
+    case ACT_SILU: return ref_silu(v);
+    case ACT_RELU:
+    case ACT_RELU | ACT_FAST: return v > 0.0f ? v : 0.0f;
+    case ACT_SIGMOID: return ref_sigmoid(v);
+    case ACT_SILU | ACT_FAST: return act_fast<ACT_SILU>(v);
+    case ACT_SIGMOID | ACT_FAST: return act_fast<ACT_SIGMOID>(v);
+    default: return v;
+  }
 }
 
 template <int A>
@@ -123,8 +136,11 @@ template <class F>
 __device__ __forceinline__ void with_act(int act, F&& f) {
   switch (act) {
     case ACT_SILU: f(ActTag<ACT_SILU>{}); break;
-    case ACT_RELU: f(ActTag<ACT_RELU>{}); break;
+    case ACT_RELU:
+    case ACT_RELU | ACT_FAST: f(ActTag<ACT_RELU>{}); break;
     case ACT_SIGMOID: f(ActTag<ACT_SIGMOID>{}); break;
+    case ACT_SILU | ACT_FAST: f(ActTag<ACT_SILU | ACT_FAST>{}); break;
+    case ACT_SIGMOID | ACT_FAST: f(ActTag<ACT_SIGMOID | ACT_FAST>{}); break;
     default: f(ActTag<ACT_NONE>{}); break;
   }
 }

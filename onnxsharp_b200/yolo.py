@@ -303,16 +303,16 @@ class Net:
     def tensor_core(node) -> bool:
         """Tensor cores for the group-1 convs except the narrow layers: 16 or
         fewer output channels, or a reduction C_in*k*k <= 144 with C_in < 64
-        (stem, 16->32 3x3, the 8/16-channel bottlenecks, the 32/48-channel 1x1s
-        at 160x160). There the register-blocked CUDA-core kernel is faster: the
+        (stem, 16->32 3x3, the 8/16-channel bottlenecks, the 32->32 1x1 at
+        160x160). There the register-blocked CUDA-core kernel is faster: the
         tensor-core kernels' fixed cost per 128-pixel tile dominates when a
         tile holds few channels (measured per layer at B=64 on B200). 1x1
-        convs with C_in >= 64 take the pointwise kernel, which reads NCHW
-        directly."""
+        convs with 64 or more input or output channels take the pointwise
+        kernel, which reads NCHW directly."""
         if node.attrs["group"] != 1:
             return False
         cin, cout, k = node.ins[0].c, node.outs[0].c, node.attrs["k"]
-        if k == 1 and node.attrs["s"] == 1 and cin >= 64:
+        if k == 1 and node.attrs["s"] == 1 and (cin >= 64 or cout >= 64):
             return True
         return not (cout <= 16 or (cin * k * k <= 144 and cin < 64))
 
@@ -323,7 +323,7 @@ class Net:
         return self.inputs[slot]
 
     def _run_nodes(self):
-        from . import ops
+        from . import _lib, ops
 
         ctx = self.ctx
         for node in self.g.nodes:
@@ -334,9 +334,10 @@ class Net:
                 b = self.dev_params[node.name + ".b"]
                 if node.name in self.packed:
                     ops.conv2d_ex(ctx, x, self.packed[node.name], b, y, a["s"], a["p"], 1, a["act"], res)
-                else:
+                else:  # hardware-instruction SiLU, as in the tensor-core epilogues
+                    act = a["act"] | _lib.ACT_FAST if a["act"] != ACT_NONE else ACT_NONE
                     ops.conv2d_direct(ctx, x, self.dev_params[node.name + ".w"], b, y, a["s"], a["p"], 1, a["group"],
-                                      a["act"], res)
+                                      act, res)
             elif node.op == "maxpool":
                 ops.maxpool2d(ctx, self.view(node.ins[0]), self.view(node.outs[0]), a["k"], a["s"], a["p"])
             elif node.op == "upsample":

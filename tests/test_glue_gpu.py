@@ -77,6 +77,27 @@ def test_conv_tile_bit_exact(ctx, C, M, k, s, H, W, resid):
     assert not got[:, :4].any()
 
 
+@pytest.mark.parametrize("C,M,k,s,act", [(16, 32, 3, 2, 1), (32, 32, 1, 1, 1), (8, 16, 3, 1, 3)])
+def test_conv_tile_fast_activation(ctx, C, M, k, s, act):
+    """OSC_ACT_FAST: the same sums with the hardware-instruction SiLU/Sigmoid,
+    within 2e-6 of the oracle's exact activation in |d| / max(1, |ref|)."""
+    import torch
+
+    from onnxsharp_b200 import _lib, ops
+
+    rng = np.random.default_rng(C + M + k)
+    x = rng.uniform(-2, 2, (2, C, 40, 40)).astype(np.float32)
+    w = (rng.normal(0, 1, (M, C, k, k)) * np.sqrt(2 / (C * k * k))).astype(np.float32)
+    b = rng.normal(0, 0.01, M).astype(np.float32)
+    p = k // 2
+    oh = ops.out_size(40, k, s, p, p)
+    y = torch.empty(2, M, oh, oh, device="cuda")
+    ops.conv2d_direct(ctx, T(x), T(w), T(b), y, s, p, 1, 1, act | _lib.ACT_FAST)
+    ctx.synchronize()
+    ref = oracle.conv2d(x, w, b, (s, s), (p, p, p, p), (1, 1), 1, act)
+    assert rel_err(y.cpu().numpy(), ref) <= 2e-6
+
+
 def test_conv_ex_views_and_residual(ctx):
     """Input and output are channel slices of larger buffers; y = res + SiLU(conv(x) + b)."""
     import torch
