@@ -14,6 +14,7 @@
 #include <cstring>
 
 #include "runtime.h"
+#include "sm100.cuh"
 #include "vmath.cuh"
 
 namespace osc {
@@ -191,8 +192,10 @@ __global__ void __launch_bounds__(256) k_conv_depthwise(const float* __restrict_
 // MMA and the hi/lo transform would dominate). Output tile per CTA: 8*G
 // channels x (4*P rows x 32 columns); each thread owns 8 channels x 4
 // adjacent pixels (32 accumulators). Input channels are staged CC at a time
-// (tile + halo, zero-filled padding via cp.async src-size 0) together with
-// the matching weights in [c][ky][kx][oc] order, double buffered. Per output
+// (tile + halo) together with the matching weights in [c][ky][kx][oc]
+// order, double buffered: the halo tile by one TMA copy when the NCHW rows
+// are 16-byte aligned (out-of-image rows, columns and channels arrive as
+// zeros), else by 4-byte cp.async with src-size 0 for the padding. Per output
 // the chain is acc = bias, then fmaf over (ic, ky, kx) ascending, the im2col
 // order of ConvKernels.cs:525-654, so the result equals the reference's
 // im2col path (padded taps give fmaf(w, 0, acc)).
@@ -204,24 +207,33 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int NPEND>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(NPEND) : "memory"); }
 
-template <int K, int S, int G, int P>
+template <int K, int S, int G, int P, bool TMA>
 struct TileConv {
   static constexpr int OCB = 8 * G, TH = 4 * P, TW = 32;
-  static constexpr int IH = (TH - 1) * S + K, IW = (TW - 1) * S + K, IP = (IW + 3) / 4 * 4;
+  static constexpr int IH = (TH - 1) * S + K, IW = (TW - 1) * S + K;
+  // TMA staging reads the halo row from the 16-byte aligned column below its
+  // first column (pad_left = K/2 is required), so the halo starts D floats
+  // into the shared row.
+  static constexpr int D = TMA ? (4 - (K / 2) % 4) % 4 : 0;
+  static constexpr int IP = (IW + D + 3) / 4 * 4;
   static constexpr int CC = S == 1 ? 8 : 4;
-  static constexpr int NX = 3 * S + K;  // input columns one thread reads per row
+  static constexpr int NX = 3 * S + K;             // input columns one thread reads per row
+  static constexpr int NXL = (D + NX + 3) / 4 * 4;  // floats loaded per row (16-byte loads)
   static constexpr int THREADS = 32 * G * P;
-  static constexpr int XS = CC * IH * IP, WS = CC * K * K * OCB, STAGE = XS + WS;
-  static constexpr int SMEM = 2 * STAGE * static_cast<int>(sizeof(float));
+  static constexpr int XS = CC * IH * IP, WS = CC * K * K * OCB;
+  static constexpr int STAGE = (XS + WS + 31) / 32 * 32;  // 128-byte aligned stages
+  static constexpr int SMEM = 2 * STAGE * static_cast<int>(sizeof(float)) + (TMA ? 32 : 0);
+  static_assert(IP <= 256, "TMA box width");
 };
 
-template <int K, int S, int G, int P>
+template <int K, int S, int G, int P, bool TMA>
 __global__ void __launch_bounds__(32 * G * P) k_conv_tile(
-    const float* __restrict__ x, long long x_nstride, int C, int H, int W, const float* __restrict__ w, int M, int pt,
-    int pl, const float* __restrict__ bias, int act, const float* __restrict__ res, long long res_nstride,
-    float* __restrict__ y, long long y_nstride, int OH, int OW, int tiles_x, bool vec4) {
-  using T = TileConv<K, S, G, P>;
-  extern __shared__ __align__(16) float smem_tile[];
+    const __grid_constant__ CUtensorMap xmap, const float* __restrict__ x, long long x_nstride, int C, int H, int W,
+    const float* __restrict__ w, int M, int pt, int pl, const float* __restrict__ bias, int act,
+    const float* __restrict__ res, long long res_nstride, float* __restrict__ y, long long y_nstride, int OH, int OW,
+    int tiles_x, bool vec4, int* __restrict__ err) {
+  using T = TileConv<K, S, G, P, TMA>;
+  extern __shared__ __align__(128) float smem_tile[];
   const int tid = threadIdx.x;
   const int n = blockIdx.z;
   const int oc0 = blockIdx.y * T::OCB;
@@ -229,20 +241,41 @@ __global__ void __launch_bounds__(32 * G * P) k_conv_tile(
   const int gy0 = ty0 * S - pt, gx0 = tx0 * S - pl;
   const float* xn = x + static_cast<size_t>(n) * x_nstride;
   const int chunks = (C + T::CC - 1) / T::CC;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem_tile + 2 * T::STAGE);  // TMA: one barrier per stage
+  int* abort_flag = reinterpret_cast<int*>(full + 2);
+  if constexpr (TMA) {
+    if (tid == 0) {
+      mbar_init(&full[0], 1);
+      mbar_init(&full[1], 1);
+      *abort_flag = 0;
+      fence_mbar_init();
+      tma_prefetch(&xmap);
+    }
+    __syncthreads();
+  }
 
   auto issue = [&](int chunk) {
     float* xs = smem_tile + (chunk & 1) * T::STAGE;
     float* ws = xs + T::XS;
     const int c0 = chunk * T::CC;
     const int nc = min(T::CC, C - c0);
-    for (int i = tid; i < nc * T::IH * T::IW; i += T::THREADS) {
-      const int c = i / (T::IH * T::IW);
-      const int rem = i - c * (T::IH * T::IW);
-      const int iy = rem / T::IW, ix = rem - iy * T::IW;
-      const int gy = gy0 + iy, gx = gx0 + ix;
-      const bool ok = gy >= 0 && gy < H && gx >= 0 && gx < W;
-      const float* src = ok ? xn + (static_cast<size_t>(c0 + c) * H + gy) * W + gx : xn;
-      cp_async4(xs + (c * T::IH + iy) * T::IP + ix, src, ok);
+    if constexpr (TMA) {
+      // the whole [CC][IH][IP] halo tile in one copy; out-of-image rows,
+      // columns and channels read as zeros
+      if (tid == 0) {
+        mbar_arrive_expect_tx(&full[chunk & 1], T::XS * 4);
+        tma_load_4d(xs, &xmap, &full[chunk & 1], gx0 - T::D, gy0, c0, n);
+      }
+    } else {
+      for (int i = tid; i < nc * T::IH * T::IW; i += T::THREADS) {
+        const int c = i / (T::IH * T::IW);
+        const int rem = i - c * (T::IH * T::IW);
+        const int iy = rem / T::IW, ix = rem - iy * T::IW;
+        const int gy = gy0 + iy, gx = gx0 + ix;
+        const bool ok = gy >= 0 && gy < H && gx >= 0 && gx < W;
+        const float* src = ok ? xn + (static_cast<size_t>(c0 + c) * H + gy) * W + gx : xn;
+        cp_async4(xs + (c * T::IH + iy) * T::IP + ix, src, ok);
+      }
     }
     for (int i = tid; i < nc * K * K * T::OCB; i += T::THREADS) {
       const int o = i % T::OCB;
@@ -275,26 +308,26 @@ __global__ void __launch_bounds__(32 * G * P) k_conv_tile(
     } else {
       cp_async_wait<0>();
     }
+    if constexpr (TMA) mbar_wait(&full[chunk & 1], (chunk >> 1) & 1u, abort_flag, err);
     __syncthreads();
     const float* xs = smem_tile + (chunk & 1) * T::STAGE;
     const float* ws = xs + T::XS + og * 8;
     const int nc = min(T::CC, C - chunk * T::CC);
+    // this thread's input columns start at cg*4*S + D; read 16-byte aligned
     const float* xrow0 = xs + ((pg * 4 + r) * S) * T::IP + cg * 4 * S;
     for (int c = 0; c < nc; ++c) {
 #pragma unroll
       for (int ky = 0; ky < K; ++ky) {
         const float* xp = xrow0 + (c * T::IH + ky) * T::IP;
-        float xr[T::NX];
+        float xl[T::NXL];
 #pragma unroll
-        for (int q = 0; q + 4 <= T::NX; q += 4) {
+        for (int q = 0; q < T::NXL; q += 4) {
           const float4 v = *reinterpret_cast<const float4*>(xp + q);
-          xr[q] = v.x;
-          xr[q + 1] = v.y;
-          xr[q + 2] = v.z;
-          xr[q + 3] = v.w;
+          xl[q] = v.x;
+          xl[q + 1] = v.y;
+          xl[q + 2] = v.z;
+          xl[q + 3] = v.w;
         }
-#pragma unroll
-        for (int q = T::NX / 4 * 4; q < T::NX; ++q) xr[q] = xp[q];
 #pragma unroll
         for (int kx = 0; kx < K; ++kx) {
           const float* wp = ws + ((c * K + ky) * K + kx) * T::OCB;
@@ -304,11 +337,22 @@ __global__ void __launch_bounds__(32 * G * P) k_conv_tile(
 #pragma unroll
           for (int i = 0; i < 8; ++i)
 #pragma unroll
-            for (int j = 0; j < 4; ++j) acc[i][j] = __fmaf_rn(wv[i], xr[j * S + kx], acc[i][j]);
+            for (int j = 0; j < 4; ++j) acc[i][j] = __fmaf_rn(wv[i], xl[T::D + j * S + kx], acc[i][j]);
         }
       }
     }
     __syncthreads();
+  }
+  if constexpr (TMA) {
+    // error path: a copy still in flight must land before the CTA exits
+    // (each buffer's phases complete in order, so the last two chunks cover all)
+    if (tid == 0 && *abort_flag) {
+      for (int c = max(0, chunks - 2); c < chunks; ++c) {
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(&full[c & 1], (c >> 1) & 1u) && globaltimer_ns() - t0 < 50ull * 1000ull * 1000ull) {
+        }
+      }
+    }
   }
 
   const int oy = ty0 + pg * 4 + r, ox = tx0 + cg * 4;
@@ -350,16 +394,38 @@ template <int K, int S, int G, int P>
 int launch_conv_tile(osc_ctx* ctx, const float* x, long long x_nstride, int N, int C, int H, int W, const float* w,
                      int M, int pt, int pl, const float* bias, int act, const float* res, long long res_nstride,
                      float* y, long long y_nstride, int OH, int OW) {
-  using T = TileConv<K, S, G, P>;
-  OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(k_conv_tile<K, S, G, P>), T::SMEM));
-  const int tiles_x = (OW + T::TW - 1) / T::TW, tiles_y = (OH + T::TH - 1) / T::TH;
+  const int tiles_x = (OW + 31) / 32, tiles_y = (OH + 4 * P - 1) / (4 * P);
   auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
   const bool vec4 = OW % 4 == 0 && y_nstride % 4 == 0 && al16(y) &&
                     (res == nullptr || (res_nstride % 4 == 0 && al16(res)));
-  dim3 grid(static_cast<unsigned>(tiles_x) * tiles_y, (M + T::OCB - 1) / T::OCB, N);
+  dim3 grid(static_cast<unsigned>(tiles_x) * tiles_y, (M + 8 * G - 1) / (8 * G), N);
+  // TMA-staged input tile when the NCHW rows are 16-byte aligned and the left
+  // padding is K/2 (the halo column the tile's shared rows are aligned to)
+  const bool tma = W % 4 == 0 && x_nstride % 4 == 0 && al16(x) && pl == K / 2 &&
+                   static_cast<long long>(H) * W * 4 < (1ll << 40);
+  CUtensorMap xmap{};
+  if (tma) {
+    using T = TileConv<K, S, G, P, true>;
+    const uint64_t dims[4] = {static_cast<uint64_t>(W), static_cast<uint64_t>(H), static_cast<uint64_t>(C),
+                              static_cast<uint64_t>(N)};
+    const uint64_t pitch[3] = {static_cast<uint64_t>(W) * 4, static_cast<uint64_t>(H) * W * 4,
+                               static_cast<uint64_t>(x_nstride) * 4};
+    const uint32_t box[4] = {static_cast<uint32_t>(T::IP), static_cast<uint32_t>(T::IH), static_cast<uint32_t>(T::CC),
+                             1};
+    OSC_TRY(encode_tiled(&xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, x, dims, pitch, box, CU_TENSOR_MAP_SWIZZLE_NONE));
+    OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(k_conv_tile<K, S, G, P, true>), T::SMEM));
+    prof_begin(ctx);
+    k_conv_tile<K, S, G, P, true><<<grid, T::THREADS, T::SMEM, ctx->stream>>>(
+        xmap, x, x_nstride, C, H, W, w, M, pt, pl, bias, act, res, res_nstride, y, y_nstride, OH, OW, tiles_x, vec4,
+        ctx->d_err);
+    return check_launch(ctx, "k_conv_tile");
+  }
+  using T = TileConv<K, S, G, P, false>;
+  OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(k_conv_tile<K, S, G, P, false>), T::SMEM));
   prof_begin(ctx);
-  k_conv_tile<K, S, G, P><<<grid, T::THREADS, T::SMEM, ctx->stream>>>(
-      x, x_nstride, C, H, W, w, M, pt, pl, bias, act, res, res_nstride, y, y_nstride, OH, OW, tiles_x, vec4);
+  k_conv_tile<K, S, G, P, false><<<grid, T::THREADS, T::SMEM, ctx->stream>>>(
+      xmap, x, x_nstride, C, H, W, w, M, pt, pl, bias, act, res, res_nstride, y, y_nstride, OH, OW, tiles_x, vec4,
+      ctx->d_err);
   return check_launch(ctx, "k_conv_tile");
 }
 

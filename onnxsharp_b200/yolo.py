@@ -303,16 +303,16 @@ class Net:
     def tensor_core(node) -> bool:
         """Tensor cores for the group-1 convs except the narrow layers: 16 or
         fewer output channels, or a reduction C_in*k*k <= 144 with C_in < 64
-        (stem, 16->32 3x3, the 8/16-channel bottlenecks, the 32->32 1x1 at
-        160x160). There the register-blocked CUDA-core kernel is faster: the
-        tensor-core kernels' fixed cost per 128-pixel tile dominates when a
-        tile holds few channels (measured per layer at B=64 on B200). 1x1
-        convs with 64 or more input or output channels take the pointwise
+        (stem, 16->32 3x3, the 8/16-channel bottlenecks, the 32/48-channel
+        1x1s at 160x160). There the register-blocked CUDA-core kernel is
+        faster: the tensor-core kernels' fixed cost per 128-pixel tile
+        dominates when a tile holds few channels (measured per layer at B=64
+        on B200). 1x1 convs with 64 or more input channels take the pointwise
         kernel, which reads NCHW directly."""
         if node.attrs["group"] != 1:
             return False
         cin, cout, k = node.ins[0].c, node.outs[0].c, node.attrs["k"]
-        if k == 1 and node.attrs["s"] == 1 and (cin >= 64 or cout >= 64):
+        if k == 1 and node.attrs["s"] == 1 and cin >= 64:
             return True
         return not (cout <= 16 or (cin * k * k <= 144 and cin < 64))
 
