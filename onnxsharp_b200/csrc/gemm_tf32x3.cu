@@ -37,11 +37,9 @@ struct osc_gemm_weights {
 namespace osc {
 namespace {
 
-// Epilogue of one 128-row CTA tile, in two parts. gemm_stage (epilogue warps):
-// the drained accumulator goes to the (free) operand ring at a pitch of BN+4
-// floats and the tile's column bias next to it. gemm_writeout (every warp of
-// the CTA, after a CTA-wide named barrier; the producer and MMA warps are
-// idle by then): bias + activation and coalesced 16-byte row stores.
+// Staging of one 128-row CTA tile for the batched kernel's epilogue (epilogue
+// warps): the drained accumulator goes to the (free) operand ring at a pitch
+// of BN+4 floats and the tile's column bias next to it.
 template <class Cfg>
 __device__ __forceinline__ void gemm_stage(uint8_t* tiles, const float (&acc)[128], bool ok, int n0, int N,
                                            const float* __restrict__ col_bias) {
@@ -52,48 +50,73 @@ __device__ __forceinline__ void gemm_stage(uint8_t* tiles, const float (&acc)[12
   sbias[jj] = (col_bias != nullptr && n0 + jj < N) ? __ldg(col_bias + n0 + jj) : 0.0f;
 }
 
+// TMA-store epilogue (C 16-byte aligned with a 16-byte row pitch), in two
+// parts like gemm_stage / gemm_writeout. gemm_stage_boxes (epilogue warps,
+// right after the drain): bias + activation of the thread's row of 128
+// columns into 32-column boxes in the free operand ring (128 rows x 128 bytes
+// each, 128-byte swizzle: 16-byte chunk c of row r at chunk c ^ (r % 8), so a
+// warp's 32 rows hit every bank once). gemm_store_boxes (every thread, after
+// the CTA barrier): one thread stores the BN/32 boxes with TMA (rows and
+// columns outside C are clipped) and waits until they have been read.
+// The tile's column biases in the shared words past the barriers, written by
+// the epilogue warps before their drain (named barrier 2 among them).
 template <class Cfg>
-__device__ __forceinline__ void gemm_writeout(uint8_t* tiles, bool ok, int m0, int n0, int M, int N, bool has_bias,
-                                              int act, float* __restrict__ C, int ldc) {
-  asm volatile("bar.sync 1, %0;" ::"r"(Cfg::THREADS) : "memory");
-  if (!ok) return;
-  constexpr int kPitch = Cfg::BN + 4;
-  const float* stage = reinterpret_cast<const float*>(tiles);
-  const float* sbias = stage + kBM * kPitch;
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const bool vec = ((ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(C) & 15u) == 0);
-  for (int r = warp; r < kBM; r += Cfg::THREADS / 32) {
-    const int row = m0 + r;
-    if (row >= M) break;
-    float* crow = C + static_cast<size_t>(row) * ldc;
-#pragma unroll
-    for (int h = 0; h < Cfg::BN; h += 128) {
-      const int c = n0 + h + lane * 4;
-      if (c >= N) continue;
-      const float4 sv = *reinterpret_cast<const float4*>(stage + r * kPitch + h + lane * 4);
-      float v[4] = {sv.x, sv.y, sv.z, sv.w};
-#pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        if (has_bias) v[t] = __fadd_rn(v[t], sbias[h + lane * 4 + t]);
-        v[t] = apply_act(v[t], act);
-      }
-      if (vec && c + 4 <= N) {
-        *reinterpret_cast<float4*>(crow + c) = make_float4(v[0], v[1], v[2], v[3]);
-      } else {
-#pragma unroll
-        for (int t = 0; t < 4; ++t)
-          if (c + t < N) crow[c + t] = v[t];
-      }
-    }
-  }
+__device__ __forceinline__ float* tile_bias(uint8_t* tiles) {
+  return reinterpret_cast<float*>(tiles + Cfg::TILE_BYTES + 256);
 }
 
 template <class Cfg>
+__device__ __forceinline__ void load_tile_bias(uint8_t* tiles, int n0, int N, const float* __restrict__ col_bias) {
+  const int jj = threadIdx.x - 64;  // epilogue thread index: BN of them
+  tile_bias<Cfg>(tiles)[jj] = (col_bias != nullptr && n0 + jj < N) ? __ldg(col_bias + n0 + jj) : 0.0f;
+  asm volatile("bar.sync 2, %0;" ::"r"(Cfg::EPI_WARPS * 32) : "memory");
+}
+
+template <class Cfg, int ACT>
+__device__ __forceinline__ void gemm_stage_boxes(uint8_t* tiles, const float (&acc)[128], bool ok, bool has_bias) {
+  if (!ok) return;
+  const int warp = threadIdx.x >> 5;
+  const int row = (warp & 3) * 32 + (threadIdx.x & 31);
+  const int half = (warp - 2) >> 2;
+  const float* sb = tile_bias<Cfg>(tiles) + half * 128;
+#pragma unroll
+  for (int b = 0; b < 4; ++b) {
+    uint8_t* box = tiles + (half * 4 + b) * (kBM * 128) + row * 128;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      const float4 bv = *reinterpret_cast<const float4*>(sb + b * 32 + c * 4);  // broadcast
+      const float bb[4] = {bv.x, bv.y, bv.z, bv.w};
+      float v[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const int j = b * 32 + c * 4 + t;
+        v[t] = act_t<ACT>(has_bias ? __fadd_rn(acc[j], bb[t]) : acc[j]);
+      }
+      *reinterpret_cast<float4*>(box + ((c ^ (row & 7)) << 4)) = make_float4(v[0], v[1], v[2], v[3]);
+    }
+  }
+  fence_async_smem();
+}
+
+template <class Cfg>
+__device__ __forceinline__ void gemm_store_boxes(uint8_t* tiles, bool ok, const CUtensorMap* mC, int m0, int n0) {
+  asm volatile("bar.sync 1, %0;" ::"r"(Cfg::THREADS) : "memory");
+  if (threadIdx.x == 0 && ok) {
+#pragma unroll
+    for (int b = 0; b < Cfg::BN / 32; ++b) tma_store_2d(mC, tiles + b * (kBM * 128), n0 + 32 * b, m0);
+    bulk_commit();
+    bulk_wait_read_all();  // the shared-memory boxes must outlive the copy's reads
+  }
+}
+
+static_assert(kBM * 128 * 8 <= Tf32x3Cfg<256, 2, 2>::TILE_BYTES, "TMA-store boxes fit the operand ring");
+
+// ACT: the fused activation as a compile-time constant (no per-element switch).
+template <class Cfg, int ACT>
 __global__ void __launch_bounds__(Cfg::THREADS, 1)
     k_gemm_tf32x3(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUtensorMap mAl,
                   const __grid_constant__ CUtensorMap mBh, const __grid_constant__ CUtensorMap mBl, int M, int N,
-                  int Kp, const float* __restrict__ col_bias, int act, float* __restrict__ C, int ldc,
+                  int Kp, const float* __restrict__ col_bias, const __grid_constant__ CUtensorMap mC,
                   int* __restrict__ err) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* tiles = tiles_base<Cfg>(smem_raw);
@@ -124,11 +147,12 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
   } else if (warp == 1) {
     if (lane == 0) mma_loop<Cfg>(tiles, pb, tmem, num_kb, err);
   } else {
+    load_tile_bias<Cfg>(tiles, n0, N, col_bias);
     float acc[128];
     const bool ok = drain_loop<Cfg>(pb, tmem, num_kb, acc, err);
-    gemm_stage<Cfg>(tiles, acc, ok, n0, N, col_bias);
+    gemm_stage_boxes<Cfg, ACT>(tiles, acc, ok, col_bias != nullptr);
   }
-  gemm_writeout<Cfg>(tiles, !pb->abort_flag, m0, n0, M, N, col_bias != nullptr, act, C, ldc);
+  gemm_store_boxes<Cfg>(tiles, !pb->abort_flag, &mC, m0, n0);
   pipe_teardown<Cfg>(pb, tmem);
 }
 
@@ -137,11 +161,11 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
 // n0 + r*BN/2 .. of B, so each CTA streams 2/3 of the single-CTA operand bytes
 // for the same MMA work. Grid: x = 2 * column tiles (clusters of 2 along x),
 // y = 256-row tiles.
-template <class Cfg>
+template <class Cfg, int ACT>
 __global__ void __launch_bounds__(Cfg::THREADS, 1)
     k_gemm_tf32x3_pair(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUtensorMap mAl,
                        const __grid_constant__ CUtensorMap mBh, const __grid_constant__ CUtensorMap mBl, int M, int N,
-                       int Kp, const float* __restrict__ col_bias, int act, float* __restrict__ C, int ldc,
+                       int Kp, const float* __restrict__ col_bias, const __grid_constant__ CUtensorMap mC,
                        int* __restrict__ err) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* tiles = tiles_base<Cfg>(smem_raw);
@@ -174,11 +198,12 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
   } else if (warp == 1) {
     if (lane == 0 && rank == 0) mma_loop_pair<Cfg>(tiles, pb, tmem, num_kb, err);
   } else {
+    load_tile_bias<Cfg>(tiles, n0, N, col_bias);
     float acc[128];
     const bool ok = drain_loop_pair<Cfg>(pb, tmem, num_kb, acc, err);
-    gemm_stage<Cfg>(tiles, acc, ok, n0, N, col_bias);
+    gemm_stage_boxes<Cfg, ACT>(tiles, acc, ok, col_bias != nullptr);
   }
-  gemm_writeout<Cfg>(tiles, !pb->abort_flag, m0, n0, M, N, col_bias != nullptr, act, C, ldc);
+  gemm_store_boxes<Cfg>(tiles, !pb->abort_flag, &mC, m0, n0);
   pipe_teardown_pair<Cfg>(pb, tmem, rank, err);
 }
 
@@ -369,6 +394,39 @@ __global__ void k_pack_b_kn(const float* __restrict__ b, int k, int n, int kp, f
   }
 }
 
+// The kernel instantiation for a runtime activation code.
+template <class Cfg>
+auto gemm_kernel(int act) {
+  switch (act) {
+    case ACT_SILU: return k_gemm_tf32x3<Cfg, ACT_SILU>;
+    case ACT_RELU: return k_gemm_tf32x3<Cfg, ACT_RELU>;
+    case ACT_SIGMOID: return k_gemm_tf32x3<Cfg, ACT_SIGMOID>;
+    default: return k_gemm_tf32x3<Cfg, ACT_NONE>;
+  }
+}
+template <class Cfg>
+auto gemm_pair_kernel(int act) {
+  switch (act) {
+    case ACT_SILU: return k_gemm_tf32x3_pair<Cfg, ACT_SILU>;
+    case ACT_RELU: return k_gemm_tf32x3_pair<Cfg, ACT_RELU>;
+    case ACT_SIGMOID: return k_gemm_tf32x3_pair<Cfg, ACT_SIGMOID>;
+    default: return k_gemm_tf32x3_pair<Cfg, ACT_NONE>;
+  }
+}
+
+// Tensor map of C for the TMA-store epilogue (32 x 128 boxes, 128-byte
+// swizzle). C's base and row pitch must be 16-byte aligned (c_tma_ok).
+static bool c_tma_ok(const float* C, int N, int ldc) {
+  return (reinterpret_cast<uintptr_t>(C) & 15u) == 0 && ldc % 4 == 0 && ldc >= N;
+}
+
+static int store_map(CUtensorMap* map, float* C, int M, int N, int ldc) {
+  const uint64_t dims[2] = {static_cast<uint64_t>(N), static_cast<uint64_t>(M)};
+  const uint64_t pitch[1] = {static_cast<uint64_t>(ldc) * 4};
+  const uint32_t box[2] = {32, kBM};
+  return encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, C, dims, pitch, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
 template <class Cfg>
 int launch_gemm(osc_ctx* ctx, const float* ahi, const float* alo, int M, int Kp, const osc_gemm_weights* w,
                 const float* bias, int act, float* C, int ldc) {
@@ -382,12 +440,13 @@ int launch_gemm(osc_ctx* ctx, const float* ahi, const float* alo, int M, int Kp,
   OSC_TRY(encode_tiled(&mAl, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, alo, dimsA, pitch, boxA, CU_TENSOR_MAP_SWIZZLE_128B));
   OSC_TRY(encode_tiled(&mBh, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, w->hi, dimsB, pitch, boxB, CU_TENSOR_MAP_SWIZZLE_128B));
   OSC_TRY(encode_tiled(&mBl, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, w->lo, dimsB, pitch, boxB, CU_TENSOR_MAP_SWIZZLE_128B));
-  auto kern = k_gemm_tf32x3<Cfg>;
+  CUtensorMap mC{};
+  OSC_TRY(store_map(&mC, C, M, w->n, ldc));
+  auto kern = gemm_kernel<Cfg>(act);
   OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(kern), Cfg::SMEM_BYTES));
   dim3 grid((w->n + Cfg::BN - 1) / Cfg::BN, (M + kBM - 1) / kBM);
   prof_begin(ctx);
-  kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, ctx->stream>>>(mAh, mAl, mBh, mBl, M, w->n, Kp, bias, act, C, ldc,
-                                                              ctx->d_err);
+  kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, ctx->stream>>>(mAh, mAl, mBh, mBl, M, w->n, Kp, bias, mC, ctx->d_err);
   return check_launch(ctx, "k_gemm_tf32x3");
 }
 
@@ -404,7 +463,7 @@ int launch_gemm_pair(osc_ctx* ctx, const float* ahi, const float* alo, int M, in
   OSC_TRY(encode_tiled(&mAl, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, alo, dimsA, pitch, boxA, CU_TENSOR_MAP_SWIZZLE_128B));
   OSC_TRY(encode_tiled(&mBh, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, w->hi, dimsB, pitch, boxB, CU_TENSOR_MAP_SWIZZLE_128B));
   OSC_TRY(encode_tiled(&mBl, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, w->lo, dimsB, pitch, boxB, CU_TENSOR_MAP_SWIZZLE_128B));
-  auto kern = k_gemm_tf32x3_pair<Cfg>;
+  auto kern = gemm_pair_kernel<Cfg>(act);
   OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(kern), Cfg::SMEM_BYTES));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * ((w->n + Cfg::BN - 1) / Cfg::BN), (M + 2 * kBM - 1) / (2 * kBM));
@@ -419,7 +478,9 @@ int launch_gemm_pair(osc_ctx* ctx, const float* ahi, const float* alo, int M, in
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   prof_begin(ctx);
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, mAh, mAl, mBh, mBl, M, w->n, Kp, bias, act, C, ldc, ctx->d_err);
+  CUtensorMap mC{};
+  OSC_TRY(store_map(&mC, C, M, w->n, ldc));
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, mAh, mAl, mBh, mBl, M, w->n, Kp, bias, mC, ctx->d_err);
   if (e != cudaSuccess) return cuda_fail(e, "k_gemm_tf32x3_pair launch");
   return check_launch(ctx, "k_gemm_tf32x3");
 }
@@ -441,6 +502,10 @@ int split_tf32(osc_ctx* ctx, const float* src, int rows, int k, int ld, int kp, 
   return check_launch(ctx, "k_split_rows");
 }
 
+static int gemm_batched(osc_ctx* ctx, const float* ahi, const float* alo, int batches, int M, int Kp,
+                        const float* bhi, const float* blo, int b_batches, int N, const float* col_bias, int act,
+                        const EpiAffine& ep, float* y);
+
 int gemm_tf32x3(osc_ctx* ctx, const float* a, int m, int k, int lda, const osc_gemm_weights* w,
                 const float* col_bias, int act, float* c, int ldc) {
   const int kp = w->kp;
@@ -450,6 +515,10 @@ int gemm_tf32x3(osc_ctx* ctx, const float* a, int m, int k, int lda, const osc_g
   float* ahi = static_cast<float*>(buf);
   float* alo = reinterpret_cast<float*>(static_cast<uint8_t*>(buf) + half);
   OSC_TRY(split_tf32(ctx, a, m, k, lda, kp, ahi, alo));
+  if (!c_tma_ok(c, w->n, ldc)) {  // C not 16-byte aligned: the batched kernel's plain-store epilogue
+    const EpiAffine ep{1.0f, 0.0f, nullptr, 0, 0, 0, 1, ldc, 0, nullptr};
+    return gemm_batched(ctx, ahi, alo, 1, m, kp, w->hi, w->lo, 1, w->n, col_bias, act, ep, c);
+  }
   static const int bn_env = [] {
     const char* v = std::getenv("OSC_GEMM_BN");
     return v ? std::atoi(v) : 0;
@@ -894,11 +963,12 @@ int launch_gemm_noalloc(osc_ctx* ctx, const float* ahi, const float* alo, int M,
   OSC_TRY(encode_tiled(&mAl, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, alo, dimsA, pitch, boxA, CU_TENSOR_MAP_SWIZZLE_128B));
   OSC_TRY(encode_tiled(&mBh, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, w->hi, dimsB, pitch, boxB, CU_TENSOR_MAP_SWIZZLE_128B));
   OSC_TRY(encode_tiled(&mBl, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, w->lo, dimsB, pitch, boxB, CU_TENSOR_MAP_SWIZZLE_128B));
-  auto kern = k_gemm_tf32x3<Cfg>;
+  CUtensorMap mC{};
+  OSC_TRY(store_map(&mC, C, M, w->n, ldc));
+  auto kern = gemm_kernel<Cfg>(act);
   OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(kern), Cfg::SMEM_BYTES));
   dim3 grid((w->n + Cfg::BN - 1) / Cfg::BN, (M + kBM - 1) / kBM);
-  kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, ctx->stream>>>(mAh, mAl, mBh, mBl, M, w->n, Kp, bias, act, C, ldc,
-                                                              ctx->d_err);
+  kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, ctx->stream>>>(mAh, mAl, mBh, mBl, M, w->n, Kp, bias, mC, ctx->d_err);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "k_gemm_tf32x3 (no-alloc)");
   return OSC_OK;
@@ -944,6 +1014,10 @@ OSC_API int osc_gemm_bias_f32_noalloc(osc_ctx* ctx, const float* a, int m, int k
   }
   const long tiles256 = static_cast<long>((w->n + 255) / 256) * ((m + kBM - 1) / kBM);
   const bool wide = w->n > 128 && tiles256 >= ctx->num_sms * 3 / 4;
+  if (!c_tma_ok(c, w->n, ldc)) {  // C not 16-byte aligned: the batched kernel's plain-store epilogue
+    const EpiAffine ep{1.0f, 0.0f, nullptr, 0, 0, 0, 1, ldc, 0, nullptr};
+    return gemm_batched(ctx, ahi, alo, 1, m, kp, w->hi, w->lo, 1, w->n, col_bias, act, ep, c);
+  }
   if (wide) return launch_gemm_noalloc<Tf32x3Cfg<256, 2, 2>>(ctx, ahi, alo, m, kp, w, col_bias, act, c, ldc);
   return launch_gemm_noalloc<Tf32x3Cfg<128, 3, 2>>(ctx, ahi, alo, m, kp, w, col_bias, act, c, ldc);
 }

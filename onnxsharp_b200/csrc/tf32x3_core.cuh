@@ -36,7 +36,8 @@ struct Tf32x3Cfg {
   static constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
   static constexpr int TILE_BYTES = STAGES * STAGE_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;       // two accumulator buffers
-  static constexpr int SMEM_BYTES = TILE_BYTES + 1024 + 256;
+  // ring | barriers (256 bytes) | column biases of the tile (BN floats)
+  static constexpr int SMEM_BYTES = TILE_BYTES + 1024 + 256 + BN * 4;
   static_assert(BN == 128 || BN == 256, "BN");
   static_assert(STAGES <= 8, "stages");
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
@@ -256,7 +257,7 @@ struct Tf32x3PairCfg {
   static constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
   static constexpr int TILE_BYTES = STAGES * STAGE_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int SMEM_BYTES = TILE_BYTES + 1024 + 256;
+  static constexpr int SMEM_BYTES = TILE_BYTES + 1024 + 256 + BN * 4;  // + the tile's column biases
   static_assert(BN == 128 || BN == 256, "BN");
   static_assert(STAGES <= 8, "stages");
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
