@@ -210,18 +210,29 @@ static_assert(sizeof(Bars) <= 256, "barrier block");
 }  // namespace pw
 
 struct PwGeom {
-  int C, HW, M;            // input channels, pixels per image, output channels
+  int C, HW, M;            // input channels, output pixels per image (OH*OW), output channels
   int ptiles, otiles;      // pixel tiles per image, channel tiles
   long long tiles;
   int num_kb;
   int act;
   long long y_nstride, res_nstride;
   const float* res;
+  // TAPS form only: output geometry, the pixel box (BW x BH <= 128 pixels),
+  // images per phase image, 32-channel blocks per tap, bytes of one A box
+  int OW, OH, BW, BH, tiles_w, N, cp_blocks, a_bytes;
 };
 
+// TAPS = false: the pointwise form above. TAPS = true: any K x K / stride
+// conv on the same pixel-major tiles, its A operand read from the phase
+// images of the NHWC hi/lo transform (K-major, one box of BW x BH pixels x 32
+// channels per tap and channel block, hi and lo), no converter warps. Pixels
+// as M spare the MMA the empty rows a channel-major tile has when the layer
+// has only 32 or 64 output channels.
+template <bool TAPS>
 __global__ void __launch_bounds__(pw::kThreads, 1)
-    k_conv1x1_tf32x3(const __grid_constant__ CUtensorMap mX, const __grid_constant__ CUtensorMap mWh,
-                     const __grid_constant__ CUtensorMap mWl, const __grid_constant__ PwGeom g,
+    k_conv_px_tf32x3(const __grid_constant__ CUtensorMap mX, const __grid_constant__ CUtensorMap mXl,
+                     const __grid_constant__ CUtensorMap mWh, const __grid_constant__ CUtensorMap mWl,
+                     const __grid_constant__ PwGeom g, const __grid_constant__ ConvTaps taps,
                      const float* __restrict__ bias, float* __restrict__ y, int* __restrict__ err) {
   using namespace pw;
   extern __shared__ uint8_t smem_raw[];
@@ -243,6 +254,7 @@ __global__ void __launch_bounds__(pw::kThreads, 1)
     pb->abort_flag = 0;
     fence_mbar_init();
     tma_prefetch(&mX);
+    if (TAPS) tma_prefetch(&mXl);
     tma_prefetch(&mWh);
     tma_prefetch(&mWl);
   }
@@ -264,12 +276,14 @@ __global__ void __launch_bounds__(pw::kThreads, 1)
     if (lane == 0) {
       int i = 0;
       bool ok = true;
+      const uint32_t tx_bytes = TAPS ? static_cast<uint32_t>(2 * g.a_bytes + 2 * kB) : static_cast<uint32_t>(kTx);
       for (long long t = blockIdx.x; t < g.tiles && ok; t += gridDim.x) {
         const int ot = static_cast<int>(t % g.otiles);
         const long long r = t / g.otiles;
         const int pt = static_cast<int>(r % g.ptiles);
         const int n = static_cast<int>(r / g.ptiles);
         const int p0 = pt * kBM, oc0 = ot * kBN;
+        const int ox0 = TAPS ? (pt % g.tiles_w) * g.BW : 0, oy0 = TAPS ? (pt / g.tiles_w) * g.BH : 0;
         for (int kb = 0; kb < g.num_kb; ++kb) {
           const int s = i % kStages;
           const uint32_t ph = (i / kStages) & 1u;
@@ -277,10 +291,18 @@ __global__ void __launch_bounds__(pw::kThreads, 1)
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&pb->full[s], kTx);
+          mbar_arrive_expect_tx(&pb->full[s], tx_bytes);
           uint8_t* st = tiles + s * kStage;
+          if constexpr (TAPS) {
+            const int tap = kb / g.cp_blocks;
+            const int c0 = (kb - tap * g.cp_blocks) * kBK;
+            const int xx = ox0 + taps.dx[tap], yy = oy0 + taps.dy[tap], nn = taps.phase[tap] * g.N + n;
+            tma_load_4d(st, &mX, &pb->full[s], c0, xx, yy, nn);
+            tma_load_4d(st + kA, &mXl, &pb->full[s], c0, xx, yy, nn);
+          } else {
 #pragma unroll
-          for (int q = 0; q < 4; ++q) tma_load_3d(st + q * 4096, &mX, &pb->full[s], p0 + 32 * q, kb * kBK, n);
+            for (int q = 0; q < 4; ++q) tma_load_3d(st + q * 4096, &mX, &pb->full[s], p0 + 32 * q, kb * kBK, n);
+          }
           tma_load_2d(st + 2 * kA, &mWh, &pb->full[s], kb * kBK, oc0);
           tma_load_2d(st + 2 * kA + kB, &mWl, &pb->full[s], kb * kBK, oc0);
           ++i;
@@ -302,7 +324,7 @@ __global__ void __launch_bounds__(pw::kThreads, 1)
       for (long long t = blockIdx.x; t < g.tiles && ok; t += gridDim.x) {
         const int oc0 = static_cast<int>(t % g.otiles) * kBN;
         const int nn = min(kBN, ((g.M - oc0) + 15) & ~15);
-        const uint32_t idesc = idesc_tf32_amn(kBM, nn);
+        const uint32_t idesc = TAPS ? idesc_tf32(kBM, nn) : idesc_tf32_amn(kBM, nn);
         int kb = 0;
         for (int c = 0; c < nchunks && ok; ++c, ++gc) {
           const int buf = gc & 1;
@@ -317,22 +339,23 @@ __global__ void __launch_bounds__(pw::kThreads, 1)
           for (; kb < kb_end; ++kb, ++i) {
             const int s = i % kStages;
             const uint32_t ph = (i / kStages) & 1u;
-            // conv[s] follows full[s] (the converters waited on it); the
-            // second wait returns at once and orders the weight boxes too.
-            if (!mbar_wait(&pb->conv[s], ph, &pb->abort_flag, err) ||
+            // pointwise: conv[s] follows full[s] (the converters waited on it);
+            // the second wait returns at once and orders the weight boxes too
+            if ((!TAPS && !mbar_wait(&pb->conv[s], ph, &pb->abort_flag, err)) ||
                 !mbar_wait(&pb->full[s], ph, &pb->abort_flag, err)) {
               ok = false;
               break;
             }
             tc_fence_after();
             const uint32_t base = smem_addr(tiles + s * kStage);
-            const uint64_t dAh = sdesc_mnmajor_sw128_32b(base, 4096, 512);
-            const uint64_t dAl = sdesc_mnmajor_sw128_32b(base + kA, 4096, 512);
+            const uint64_t dAh = TAPS ? sdesc_kmajor_sw128(base) : sdesc_mnmajor_sw128_32b(base, 4096, 512);
+            const uint64_t dAl = TAPS ? sdesc_kmajor_sw128(base + kA) : sdesc_mnmajor_sw128_32b(base + kA, 4096, 512);
             const uint64_t dBh = sdesc_kmajor_sw128(base + 2 * kA);
             const uint64_t dBl = sdesc_kmajor_sw128(base + 2 * kA + kB);
 #pragma unroll
             for (int kk = 0; kk < kBK / 8; ++kk) {
-              const uint64_t ao = static_cast<uint64_t>(kk * 64);  // +1024 bytes: the next 8 channel rows
+              // +1024 bytes: the next 8 channel rows (MN-major); +32 bytes inside the K-major row
+              const uint64_t ao = static_cast<uint64_t>(TAPS ? kk * 2 : kk * 64);
               const uint64_t bo = static_cast<uint64_t>(kk * 2);   // +32 bytes inside the K-major row
               mma_tf32(d, dAh + ao, dBh + bo, idesc, acc);
               acc = 1u;
@@ -351,10 +374,10 @@ __global__ void __launch_bounds__(pw::kThreads, 1)
       }
     }
   } else if (warp < kEpiBase) {
-    // converters: A (fp32 from TMA) -> hi in place, lo beside it
+    // converters: A (fp32 from TMA) -> hi in place, lo beside it (pointwise form only)
     const int ct = threadIdx.x - 64;
     int i = 0;
-    bool ok = true;
+    bool ok = !TAPS;
     for (long long t = blockIdx.x; t < g.tiles && ok; t += gridDim.x) {
       for (int kb = 0; kb < g.num_kb; ++kb, ++i) {
         const int s = i % kStages;
@@ -438,8 +461,20 @@ __global__ void __launch_bounds__(pw::kThreads, 1)
         if (lane == 0) mbar_arrive(&pb->acc_empty[buf]);
       }
       if (!ok) break;
-      const int p = pt * kBM + q * 32 + lane;
-      if (p < g.HW && nvalid > 0) {
+      // this lane's output pixel: linear in the plane (pointwise) or inside the BW x BH box (taps)
+      int p;
+      bool pvalid;
+      if constexpr (TAPS) {
+        const int pb_ = q * 32 + lane;
+        const int iy = pb_ / g.BW, ix = pb_ - iy * g.BW;
+        const int oy = (pt / g.tiles_w) * g.BH + iy, ox = (pt % g.tiles_w) * g.BW + ix;
+        pvalid = iy < g.BH && oy < g.OH && ox < g.OW;
+        p = oy * g.OW + ox;
+      } else {
+        p = pt * kBM + q * 32 + lane;
+        pvalid = p < g.HW;
+      }
+      if (pvalid && nvalid > 0) {
         float* yp = y + static_cast<size_t>(n) * g.y_nstride + static_cast<size_t>(oc0) * g.HW + p;
         const float* rp =
             g.res ? g.res + static_cast<size_t>(n) * g.res_nstride + static_cast<size_t>(oc0) * g.HW + p : nullptr;
@@ -666,12 +701,94 @@ static int conv1x1_tf32x3(osc_ctx* ctx, const float* x, long long x_nstride, int
     OSC_TRY(encode_tiled(&mWl, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, w->lo, dims, pitch, box, CU_TENSOR_MAP_SWIZZLE_128B));
   }
   const int smem = pw::kSmemBase + static_cast<int>(round_up(static_cast<size_t>(w->M) * 4, 16));
-  OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(k_conv1x1_tf32x3), smem));
+  OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(k_conv_px_tf32x3<false>), smem));
   const long long grid = std::min<long long>(g.tiles, ctx->num_sms);
   prof_begin(ctx);
-  k_conv1x1_tf32x3<<<static_cast<unsigned>(grid), pw::kThreads, smem, ctx->stream>>>(mX, mWh, mWl, g, bias, y,
+  const ConvTaps no_taps{};
+  k_conv_px_tf32x3<false><<<static_cast<unsigned>(grid), pw::kThreads, smem, ctx->stream>>>(mX, mX, mWh, mWl, g,
+                                                                                             no_taps, bias, y,
                                                                                          ctx->d_err);
-  return check_launch(ctx, "k_conv1x1_tf32x3");
+  return check_launch(ctx, "k_conv_px_tf32x3");
+}
+
+// Pixel-major tiles for K x K convs with few output channels on small images
+// (measured on B200, YOLO shapes at B=64: 256->64 and 64->64 3x3 at 20x20
+// 19-24 % faster; at 40x40 and above the channel-major kernel's 256-pixel
+// tiles move fewer operand bytes per output and win). OSC_CONV_PX=0 / 1
+// forces the choice for measurements.
+static bool px_taps_ok(int M, int OH, int OW) {
+  static const int mode = [] {
+    const char* v = std::getenv("OSC_CONV_PX");
+    return v == nullptr ? -1 : std::atoi(v);
+  }();
+  if (mode == 0) return false;
+  return mode == 1 ? M <= 4096 : (M <= 64 && static_cast<long>(OH) * OW <= 576);
+}
+
+// The pixel box of the pixel-major conv: BW x BH <= 128 pixels, the shape
+// with the fewest tiles (then the widest rows).
+static void choose_px_box(int OH, int OW, int* BW, int* BH) {
+  long best = -1;
+  const int cands[6] = {OW, 128, 64, 32, 16, 8};
+  for (int bw : cands) {
+    if (bw < 1 || bw > 128) continue;
+    const int bh = 128 / bw;
+    const long tiles = static_cast<long>((OW + bw - 1) / bw) * ((OH + bh - 1) / bh);
+    if (best < 0 || tiles < best || (tiles == best && bw > *BW)) {
+      best = tiles;
+      *BW = bw;
+      *BH = bh;
+    }
+  }
+}
+
+static int conv_px_taps(osc_ctx* ctx, const float* xh, const float* xl, int N, int Hp, int Wp, int s,
+                        const osc_conv_weights* w, const ConvTaps& taps, const float* bias, int act, const float* res,
+                        long long res_nstride, float* y, long long y_nstride, int OH, int OW) {
+  if (w->M > pw::kMaxBias) return fail(OSC_EUNSUPPORTED, "conv: %d output channels", w->M);
+  PwGeom g{};
+  g.C = w->C;
+  g.HW = OH * OW;
+  g.M = w->M;
+  g.OW = OW;
+  g.OH = OH;
+  choose_px_box(OH, OW, &g.BW, &g.BH);
+  g.tiles_w = (OW + g.BW - 1) / g.BW;
+  g.ptiles = g.tiles_w * ((OH + g.BH - 1) / g.BH);
+  g.otiles = (w->M + pw::kBN - 1) / pw::kBN;
+  g.tiles = static_cast<long long>(N) * g.ptiles * g.otiles;
+  g.cp_blocks = w->Cp / kBK;
+  g.num_kb = taps.n_taps * g.cp_blocks;
+  g.N = N;
+  g.a_bytes = g.BW * g.BH * kBK * 4;
+  g.act = act;
+  g.y_nstride = y_nstride;
+  g.res_nstride = res_nstride;
+  g.res = res;
+  CUtensorMap mXh, mXl, mWh, mWl;
+  {
+    const uint64_t dims[4] = {static_cast<uint64_t>(w->Cp), static_cast<uint64_t>(Wp), static_cast<uint64_t>(Hp),
+                              static_cast<uint64_t>(s) * s * N};
+    const uint64_t pitch[3] = {static_cast<uint64_t>(w->Cp) * 4, static_cast<uint64_t>(w->Cp) * 4 * Wp,
+                               static_cast<uint64_t>(w->Cp) * 4 * Wp * Hp};
+    const uint32_t box[4] = {kBK, static_cast<uint32_t>(g.BW), static_cast<uint32_t>(g.BH), 1};
+    OSC_TRY(encode_tiled(&mXh, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, xh, dims, pitch, box, CU_TENSOR_MAP_SWIZZLE_128B));
+    OSC_TRY(encode_tiled(&mXl, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, xl, dims, pitch, box, CU_TENSOR_MAP_SWIZZLE_128B));
+  }
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(w->Kp), static_cast<uint64_t>(w->M)};
+    const uint64_t pitch[1] = {static_cast<uint64_t>(w->Kp) * 4};
+    const uint32_t box[2] = {kBK, pw::kBN};
+    OSC_TRY(encode_tiled(&mWh, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, w->hi, dims, pitch, box, CU_TENSOR_MAP_SWIZZLE_128B));
+    OSC_TRY(encode_tiled(&mWl, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, w->lo, dims, pitch, box, CU_TENSOR_MAP_SWIZZLE_128B));
+  }
+  const int smem = pw::kSmemBase + static_cast<int>(round_up(static_cast<size_t>(w->M) * 4, 16));
+  OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(k_conv_px_tf32x3<true>), smem));
+  const long long grid = std::min<long long>(g.tiles, ctx->num_sms);
+  prof_begin(ctx);
+  k_conv_px_tf32x3<true><<<static_cast<unsigned>(grid), pw::kThreads, smem, ctx->stream>>>(mXh, mXl, mWh, mWl, g,
+                                                                                            taps, bias, y, ctx->d_err);
+  return check_launch(ctx, "k_conv_px_tf32x3");
 }
 
 int conv_tf32x3(osc_ctx* ctx, const float* x, long long x_nstride, int N, int C, int H, int W, const osc_conv_weights* w,
@@ -722,6 +839,8 @@ int conv_tf32x3(osc_ctx* ctx, const float* x, long long x_nstride, int N, int C,
       taps.dy[t] = static_cast<short>(floor_div(oy - py, s));
       taps.dx[t] = static_cast<short>(floor_div(ox - px, s));
     }
+  if (px_taps_ok(w->M, OH, OW)) return conv_px_taps(ctx, xh, xl, N, Hp, Wp, s, w, taps, bias, act, res, res_nstride, y,
+                                              y_nstride, OH, OW);
   ConvGeom g{};
   g.N = N;
   g.M = w->M;
