@@ -186,6 +186,137 @@ __global__ void __launch_bounds__(256) k_conv_depthwise(const float* __restrict_
   }
 }
 
+// Depthwise 3x3, stride 1, pad 1: one thread per (plane, strip of kDw3Rows
+// output rows, column). The (kDw3Rows + 2) x 3 input window goes into
+// registers first (all its loads independent, so each thread keeps many in
+// flight; the neighbouring columns are L1 hits), then each output takes
+// acc = bias and the nine FMAs in (ky, kx) order with zero taps outside the
+// image: the same arithmetic as k_conv_depthwise.
+constexpr int kDw3Rows = 8;
+constexpr int kDw3Threads = 256;
+
+template <int ACT>
+__global__ void __launch_bounds__(kDw3Threads) k_dw3s1(const float* __restrict__ x, long long x_nstride, int C, int H,
+                                                       int W, const float* __restrict__ w,
+                                                       const float* __restrict__ bias, const float* __restrict__ res,
+                                                       long long res_nstride, float* __restrict__ y,
+                                                       long long y_nstride, unsigned strips, unsigned total) {
+  const unsigned t = blockIdx.x * kDw3Threads + threadIdx.x;
+  if (t >= total) return;
+  const unsigned ps = t / static_cast<unsigned>(W);
+  const int ox = static_cast<int>(t - ps * static_cast<unsigned>(W));
+  const unsigned plane = ps / strips;
+  const int oy0 = static_cast<int>(ps - plane * strips) * kDw3Rows;
+  const unsigned n = plane / static_cast<unsigned>(C);
+  const int c = static_cast<int>(plane - n * static_cast<unsigned>(C));
+  const long long plane_off = static_cast<long long>(c) * H * W;
+  const float* xc = x + static_cast<long long>(n) * x_nstride + plane_off;
+  float in[kDw3Rows + 2][3];
+#pragma unroll
+  for (int r = 0; r < kDw3Rows + 2; ++r) {
+    const int iy = oy0 - 1 + r;
+    const bool row_ok = iy >= 0 && iy < H;
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+      const int ix = ox - 1 + k;
+      in[r][k] = (row_ok && ix >= 0 && ix < W) ? __ldg(xc + static_cast<long long>(iy) * W + ix) : 0.0f;
+    }
+  }
+  float wr[9];
+#pragma unroll
+  for (int i = 0; i < 9; ++i) wr[i] = __ldg(w + c * 9 + i);
+  const float b = bias ? __ldg(bias + c) : 0.0f;
+  float* yc = y + static_cast<long long>(n) * y_nstride + plane_off;
+  const float* rc = res ? res + static_cast<long long>(n) * res_nstride + plane_off : nullptr;
+#pragma unroll
+  for (int r = 0; r < kDw3Rows; ++r) {
+    const int oy = oy0 + r;
+    if (oy < H) {
+      float acc = b;
+#pragma unroll
+      for (int ky = 0; ky < 3; ++ky)
+#pragma unroll
+        for (int kx = 0; kx < 3; ++kx) acc = __fmaf_rn(wr[ky * 3 + kx], in[r + ky][kx], acc);
+      float v = act_t<ACT>(acc);
+      const long long off = static_cast<long long>(oy) * W + ox;
+      if (rc) v = __fadd_rn(__ldg(rc + off), v);
+      yc[off] = v;
+    }
+  }
+}
+
+// The same with four adjacent columns per thread (W % 4 == 0, 16-byte
+// aligned planes): per input row one float4 load plus the two halo columns,
+// per output row one float4 store.
+template <int ACT>
+__global__ void __launch_bounds__(kDw3Threads) k_dw3s1_v4(const float* __restrict__ x, long long x_nstride, int C,
+                                                          int H, int W, const float* __restrict__ w,
+                                                          const float* __restrict__ bias,
+                                                          const float* __restrict__ res, long long res_nstride,
+                                                          float* __restrict__ y, long long y_nstride, unsigned strips,
+                                                          unsigned total) {
+  const unsigned t = blockIdx.x * kDw3Threads + threadIdx.x;
+  if (t >= total) return;
+  const unsigned W4 = static_cast<unsigned>(W) >> 2;
+  const unsigned ps = t / W4;
+  const int ox = static_cast<int>(t - ps * W4) * 4;
+  const unsigned plane = ps / strips;
+  const int oy0 = static_cast<int>(ps - plane * strips) * kDw3Rows;
+  const unsigned n = plane / static_cast<unsigned>(C);
+  const int c = static_cast<int>(plane - n * static_cast<unsigned>(C));
+  const long long plane_off = static_cast<long long>(c) * H * W;
+  const float* xc = x + static_cast<long long>(n) * x_nstride + plane_off;
+  float in[kDw3Rows + 2][6];  // columns ox-1 .. ox+4
+#pragma unroll
+  for (int r = 0; r < kDw3Rows + 2; ++r) {
+    const int iy = oy0 - 1 + r;
+    if (iy >= 0 && iy < H) {
+      const float* xr = xc + static_cast<long long>(iy) * W + ox;
+      const float4 v = __ldg(reinterpret_cast<const float4*>(xr));
+      in[r][0] = ox > 0 ? __ldg(xr - 1) : 0.0f;
+      in[r][1] = v.x;
+      in[r][2] = v.y;
+      in[r][3] = v.z;
+      in[r][4] = v.w;
+      in[r][5] = ox + 4 < W ? __ldg(xr + 4) : 0.0f;
+    } else {
+#pragma unroll
+      for (int k = 0; k < 6; ++k) in[r][k] = 0.0f;
+    }
+  }
+  float wr[9];
+#pragma unroll
+  for (int i = 0; i < 9; ++i) wr[i] = __ldg(w + c * 9 + i);
+  const float b = bias ? __ldg(bias + c) : 0.0f;
+  float* yc = y + static_cast<long long>(n) * y_nstride + plane_off;
+  const float* rc = res ? res + static_cast<long long>(n) * res_nstride + plane_off : nullptr;
+#pragma unroll
+  for (int r = 0; r < kDw3Rows; ++r) {
+    const int oy = oy0 + r;
+    if (oy < H) {
+      float o[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float acc = b;
+#pragma unroll
+        for (int ky = 0; ky < 3; ++ky)
+#pragma unroll
+          for (int kx = 0; kx < 3; ++kx) acc = __fmaf_rn(wr[ky * 3 + kx], in[r + ky][j + kx], acc);
+        o[j] = act_t<ACT>(acc);
+      }
+      const long long off = static_cast<long long>(oy) * W + ox;
+      if (rc) {
+        const float4 rv = __ldg(reinterpret_cast<const float4*>(rc + off));
+        o[0] = __fadd_rn(rv.x, o[0]);
+        o[1] = __fadd_rn(rv.y, o[1]);
+        o[2] = __fadd_rn(rv.z, o[2]);
+        o[3] = __fadd_rn(rv.w, o[3]);
+      }
+      *reinterpret_cast<float4*>(yc + off) = make_float4(o[0], o[1], o[2], o[3]);
+    }
+  }
+}
+
 // Register-blocked tiled conv on CUDA cores for group-1 K x K (K = 1, 3)
 // convs with few channels (the YOLO stem and the 8/16/32-channel layers, where
 // a 128-row tensor-core tile and 32-channel K padding would waste most of the
@@ -476,6 +607,77 @@ __global__ void __launch_bounds__(kPoolThreads) k_maxpool(const float* __restric
       }
     }
     yc[o] = m;
+  }
+}
+
+// Planes up to 256 columns wide (the SPPF pools: 20x20): several planes per
+// CTA, staged in shared memory inside a -inf border of the padding width, so
+// no window tap needs a bounds check (maxps(-inf, m) keeps m, exactly as
+// skipping the tap). One thread per (plane, column) stages its input column
+// (loads in independent batches of kPoolBatch) and then slides down its output
+// column: the row maxima of the last K rows sit in a register ring, and each
+// output takes their maximum. With maxps(x, m) a NaN x never replaces m and m
+// starts at -inf, so NaNs are skipped; among equal maxima the first in (ky, kx)
+// order is kept both by the reference's row-major scan and by this separable
+// form (the first row that attains the maximum, its first column), so signed
+// zeros come out the same too.
+constexpr int kPoolColThreads = 256;
+constexpr int kPoolBatch = 8;
+
+template <int K>
+__global__ void __launch_bounds__(kPoolColThreads) k_maxpool_cols(
+    const float* __restrict__ x, long long x_nstride, int C, int H, int W, int sh, int sw, int pt, int pl,
+    float* __restrict__ y, long long y_nstride, int OH, int OW, long long planes, int ppc, int PH, int PW) {
+  extern __shared__ float pool_sm[];  // [ppc][PH][PW]
+  const int PHW = PH * PW;
+  const long long plane0 = static_cast<long long>(blockIdx.x) * ppc;
+  const int np = static_cast<int>(min(static_cast<long long>(ppc), planes - plane0));
+  for (int i = threadIdx.x; i < np * PHW; i += kPoolColThreads) pool_sm[i] = -INFINITY;
+  __syncthreads();
+  {
+    const int p = threadIdx.x / W, col = threadIdx.x - p * W;
+    if (p < np) {
+      const long long g = plane0 + p, n = g / C, c = g - n * C;
+      const float* src = x + n * x_nstride + c * H * W + col;
+      float* dst = pool_sm + p * PHW + pt * PW + pl + col;
+      for (int h0 = 0; h0 < H; h0 += kPoolBatch) {
+        float v[kPoolBatch];
+#pragma unroll
+        for (int j = 0; j < kPoolBatch; ++j)
+          v[j] = h0 + j < H ? __ldg(src + static_cast<long long>(h0 + j) * W) : 0.0f;
+#pragma unroll
+        for (int j = 0; j < kPoolBatch; ++j)
+          if (h0 + j < H) dst[(h0 + j) * PW] = v[j];
+      }
+    }
+  }
+  __syncthreads();
+  const int p = threadIdx.x / OW, ox = threadIdx.x - p * OW;
+  if (p >= np) return;
+  const long long g = plane0 + p, n = g / C, c = g - n * C;
+  float* dst = y + n * y_nstride + c * OH * OW + ox;
+  const float* colp = pool_sm + p * PHW + ox * sw;
+  auto row_max = [&](int h) {
+    const float* r = colp + h * PW;
+    float m = -INFINITY;
+#pragma unroll
+    for (int kx = 0; kx < K; ++kx) m = maxps(r[kx], m);
+    return m;
+  };
+  float ring[K];  // ring[0] = oldest row of the window
+#pragma unroll
+  for (int k = 0; k + 1 < K; ++k) ring[k + 1] = row_max(k);
+  for (int oy = 0, h = K - 1; oy < OH; ++h) {
+#pragma unroll
+    for (int k = 0; k + 1 < K; ++k) ring[k] = ring[k + 1];
+    ring[K - 1] = row_max(h);
+    if (h - (K - 1) == oy * sh) {
+      float m = -INFINITY;
+#pragma unroll
+      for (int k = 0; k < K; ++k) m = maxps(ring[k], m);
+      dst[static_cast<long long>(oy) * OW] = m;
+      ++oy;
+    }
   }
 }
 
@@ -858,6 +1060,37 @@ OSC_API int osc_conv2d_direct_f32(osc_ctx* ctx, const float* x, long long x_nstr
   if (fault_injected("launch")) return fail(OSC_EFAULT_INJECTED, "injected failure (launch)");
   const int mpg = M / group;
   const bool unit_dil = dil_h == 1 && dil_w == 1;
+  // Depthwise 3x3, stride 1, "same" padding (the head's DWConv, PSA's
+  // position encoding): register-window kernel.
+  if (group == C && group == M && kh == 3 && kw == 3 && stride_h == 1 && stride_w == 1 && pad_t == 1 &&
+      pad_l == 1 && OH == H && OW == W && unit_dil) {
+    const long long strips = (H + kDw3Rows - 1) / kDw3Rows;
+    const long long total = static_cast<long long>(N) * C * strips * W;
+    const bool vec4 = W % 4 == 0 && reinterpret_cast<uintptr_t>(x) % 16 == 0 && x_nstride % 4 == 0 &&
+                      reinterpret_cast<uintptr_t>(y) % 16 == 0 && y_nstride % 4 == 0 &&
+                      (residual == nullptr || (reinterpret_cast<uintptr_t>(residual) % 16 == 0 && res_nstride % 4 == 0));
+    if (vec4 && total <= 0x7fffffffLL) {
+      prof_begin(ctx);
+      const long long total4 = total / 4;
+      const unsigned blocks = static_cast<unsigned>((total4 + kDw3Threads - 1) / kDw3Threads);
+      with_act(act, [&](auto tag) {
+        k_dw3s1_v4<decltype(tag)::value><<<blocks, kDw3Threads, 0, ctx->stream>>>(
+            x, x_nstride, C, H, W, w, bias, residual, res_nstride, y, y_nstride, static_cast<unsigned>(strips),
+            static_cast<unsigned>(total4));
+      });
+      return check_launch(ctx, "k_dw3s1_v4");
+    }
+    if (total <= 0x7fffffffLL) {
+      prof_begin(ctx);
+      const unsigned blocks = static_cast<unsigned>((total + kDw3Threads - 1) / kDw3Threads);
+      with_act(act, [&](auto tag) {
+        k_dw3s1<decltype(tag)::value><<<blocks, kDw3Threads, 0, ctx->stream>>>(
+            x, x_nstride, C, H, W, w, bias, residual, res_nstride, y, y_nstride, static_cast<unsigned>(strips),
+            static_cast<unsigned>(total));
+      });
+      return check_launch(ctx, "k_dw3s1");
+    }
+  }
   // Depthwise (group == C == M), square 3/5/7 kernels: band-tiled kernel.
   if (group == C && group == M && kh == kw && (kh == 3 || kh == 5 || kh == 7) && unit_dil) {
     const int in_cols = (OW - 1) * stride_w + kw;
@@ -937,6 +1170,32 @@ OSC_API int osc_maxpool2d_f32(osc_ctx* ctx, const float* x, long long x_nstride,
                           (kPoolThreads * kPoolPerThread);
   if (planes > 0x7fffffffLL || tiles > 65535 || static_cast<long long>(H) * W > 0x7fffffffLL)
     return fail(OSC_EINVAL, "osc_maxpool2d_f32: %lld planes of %dx%d exceed the launch limits", planes, OH, OW);
+  // square 2/3/5/7 windows on planes up to 256 columns wide whose bordered
+  // copy fits 48 KB: column-sliding kernel, several planes per CTA
+  const int PH = std::max(H + pad_t + pad_b, (OH - 1) * stride_h + kh);
+  const int PW = std::max(W + pad_l + pad_r, (OW - 1) * stride_w + kw);
+  const long long plane_bytes = static_cast<long long>(PH) * PW * 4;
+  if (kh == kw && (kh == 2 || kh == 3 || kh == 5 || kh == 7) && pad_t >= 0 && pad_l >= 0 && pad_b >= 0 &&
+      pad_r >= 0 && std::max(W, OW) <= kPoolColThreads && plane_bytes <= 48 * 1024) {
+    const int ppc = static_cast<int>(
+        std::min<long long>(kPoolColThreads / std::max(W, OW), (48 * 1024) / plane_bytes));
+    const long long ctas = (planes + ppc - 1) / ppc;
+    const size_t smem = static_cast<size_t>(ppc * plane_bytes);
+    if (ctas <= 0x7fffffffLL) {
+      prof_begin(ctx);
+      const dim3 grid(static_cast<unsigned>(ctas));
+#define OSC_POOL_LAUNCH(KS)                                                                                      \
+  k_maxpool_cols<KS><<<grid, kPoolColThreads, smem, ctx->stream>>>(x, x_nstride, C, H, W, stride_h, stride_w,  \
+                                                                   pad_t, pad_l, y, y_nstride, OH, OW, planes, \
+                                                                   ppc, PH, PW)
+      if (kh == 2) OSC_POOL_LAUNCH(2);
+      else if (kh == 3) OSC_POOL_LAUNCH(3);
+      else if (kh == 5) OSC_POOL_LAUNCH(5);
+      else OSC_POOL_LAUNCH(7);
+#undef OSC_POOL_LAUNCH
+      return check_launch(ctx, "k_maxpool_cols");
+    }
+  }
   prof_begin(ctx);
   k_maxpool<<<dim3(static_cast<unsigned>(planes), static_cast<unsigned>(tiles)), kPoolThreads, 0, ctx->stream>>>(
       x, x_nstride, C, H, W, kh, kw, stride_h, stride_w, pad_t, pad_l, y, y_nstride, OH, OW);

@@ -133,7 +133,7 @@ struct ActTag {
 // Calls f(ActTag<ACT>{}) with the runtime code `act` turned into a constant;
 // f is a generic lambda that reads decltype(tag)::value.
 template <class F>
-__device__ __forceinline__ void with_act(int act, F&& f) {
+__host__ __device__ __forceinline__ void with_act(int act, F&& f) {
   switch (act) {
     case ACT_SILU: f(ActTag<ACT_SILU>{}); break;
     case ACT_RELU:

@@ -38,6 +38,54 @@ def test_conv_direct(ctx, C, M, k, s, group):
     assert rel_err(y.cpu().numpy(), ref) <= 1e-5
 
 
+@pytest.mark.parametrize("C,k,s,H,W", [(16, 3, 2, 33, 30), (6, 5, 1, 150, 41), (4, 3, 1, 20, 700), (8, 7, 1, 70, 70)])
+def test_conv_depthwise_geometries(ctx, C, k, s, H, W):
+    """Depthwise bands: stride 2, 5x5 / 7x7, images taller than one 64-row band,
+    rows wide enough to shrink the band to fit 48 KB of shared memory."""
+    import torch
+
+    from onnxsharp_b200 import ops
+
+    rng = np.random.default_rng(C * k + H)
+    x = rng.uniform(-1, 1, (2, C, H, W)).astype(np.float32)
+    w = (rng.normal(0, 1, (C, 1, k, k)) * np.sqrt(2 / (k * k))).astype(np.float32)
+    b = rng.normal(0, 0.01, C).astype(np.float32)
+    p = k // 2
+    oh, ow = ops.out_size(H, k, s, p, p), ops.out_size(W, k, s, p, p)
+    y = torch.empty(2, C, oh, ow, device="cuda")
+    ops.conv2d_direct(ctx, T(x), T(w), T(b), y, s, p, 1, C, 1)
+    ctx.synchronize()
+    ref = oracle.conv2d(x, w, b, (s, s), (p, p, p, p), (1, 1), C, 1)
+    assert rel_err(y.cpu().numpy(), ref) <= 1e-5
+
+
+@pytest.mark.parametrize("C,H,W,act,resid", [(80, 80, 80, 1, False), (7, 9, 100, 0, True), (128, 20, 20, 17, True),
+                                                (5, 17, 99, 1, True)])
+def test_conv_depthwise3_register_window(ctx, C, H, W, act, resid):
+    """Depthwise 3x3 stride 1 (the register-window kernels; four columns per
+    thread when W % 4 == 0, one otherwise): channel-slice views on input and
+    output, partial row strips, fused residual, fast activation."""
+    import torch
+
+    from onnxsharp_b200 import ops
+
+    rng = np.random.default_rng(C + H + W)
+    x = rng.uniform(-1, 1, (3, C + 2, H, W)).astype(np.float32)
+    w = (rng.normal(0, 1, (C, 1, 3, 3)) * np.sqrt(2 / 9)).astype(np.float32)
+    b = rng.normal(0, 0.01, C).astype(np.float32)
+    res = rng.normal(0, 1, (3, C, H, W)).astype(np.float32) if resid else None
+    out_big = torch.zeros(3, C + 4, H, W, device="cuda")
+    ops.conv2d_direct(ctx, T(x)[:, 2:], T(w), T(b), out_big[:, 4:], 1, 1, 1, C, act,
+                      T(res) if resid else None)
+    ctx.synchronize()
+    ref = oracle.conv2d(np.ascontiguousarray(x[:, 2:]), w, b, (1, 1), (1, 1, 1, 1), (1, 1), C, act & 15)
+    if resid:
+        ref = res + ref
+    got = out_big.cpu().numpy()
+    assert rel_err(got[:, 4:], ref) <= (2e-6 if act & 16 else 1e-5)
+    assert not got[:, :4].any()
+
+
 @pytest.mark.parametrize(
     "C,M,k,s,H,W,resid",
     [
@@ -138,10 +186,12 @@ def test_maxpool_and_resize(ctx):
     assert np.array_equal(z.cpu().numpy(), np.repeat(np.repeat(x, 2, 2), 2, 3))
 
 
-@pytest.mark.parametrize("shape,k,s,p", [((2, 5, 33, 47), 3, 2, 1), ((1, 3, 700, 9), 5, 1, 2), ((3, 2, 8, 8), 2, 2, 0)])
+@pytest.mark.parametrize("shape,k,s,p", [((2, 5, 33, 47), 3, 2, 1), ((1, 3, 700, 9), 5, 1, 2), ((3, 2, 8, 8), 2, 2, 0),
+                                         ((40, 7, 20, 20), 5, 1, 2), ((1, 2, 10, 300), 3, 1, 1), ((2, 3, 30, 30), 4, 2, 1)])
 def test_maxpool_geometries(ctx, shape, k, s, p):
-    """Odd sizes, stride 2, planes larger than one CTA's 512 outputs, and a
-    channel slice of a wider buffer on both sides (SPPF's layout)."""
+    """Odd sizes, stride 2, tall planes, planes packed several to a CTA (and a
+    partial last CTA), rows wider than 256 and a 4x4 window (the generic
+    kernel), and a channel slice of a wider buffer on both sides (SPPF's layout)."""
     import torch
 
     from onnxsharp_b200 import ops
