@@ -338,6 +338,23 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int NPEND>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(NPEND) : "memory"); }
 
+// Packed FP32 (two lanes of a 64-bit register): fma.rn.f32x2 rounds each
+// lane exactly as fmaf, so a pair of accumulators takes one instruction.
+__device__ __forceinline__ unsigned long long f2_pack(float lo, float hi) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(unsigned long long v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ unsigned long long f2_fma(unsigned long long a, unsigned long long b,
+                                                     unsigned long long c) {
+  unsigned long long d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
 template <int K, int S, int G, int P, bool TMA>
 struct TileConv {
   static constexpr int OCB = 8 * G, TH = 4 * P, TW = 32;
@@ -422,13 +439,15 @@ __global__ void __launch_bounds__(32 * G * P) k_conv_tile(
   const int lane = tid & 31, wid = tid >> 5;
   const int og = wid % G, pg = wid / G;
   const int r = lane >> 3, cg = lane & 7;
-  float acc[8][4];
+  // accp[ip][j]: output channels 2ip (low lane) and 2ip+1 (high lane) at pixel j
+  unsigned long long accp[4][4];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int oc = oc0 + og * 8 + i;
-    const float b = (bias && oc < M) ? __ldg(bias + oc) : 0.0f;
+  for (int ip = 0; ip < 4; ++ip) {
+    const int oc = oc0 + og * 8 + 2 * ip;
+    const float b0 = (bias && oc < M) ? __ldg(bias + oc) : 0.0f;
+    const float b1 = (bias && oc + 1 < M) ? __ldg(bias + oc + 1) : 0.0f;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) acc[i][j] = b;
+    for (int j = 0; j < 4; ++j) accp[ip][j] = f2_pack(b0, b1);
   }
 
   issue(0);
@@ -459,16 +478,18 @@ __global__ void __launch_bounds__(32 * G * P) k_conv_tile(
           xl[q + 2] = v.z;
           xl[q + 3] = v.w;
         }
+        unsigned long long xd[T::NX];  // (x, x): each input column in both lanes
+#pragma unroll
+        for (int q = 0; q < T::NX; ++q) xd[q] = f2_pack(xl[T::D + q], xl[T::D + q]);
 #pragma unroll
         for (int kx = 0; kx < K; ++kx) {
-          const float* wp = ws + ((c * K + ky) * K + kx) * T::OCB;
-          const float4 w0 = *reinterpret_cast<const float4*>(wp);
-          const float4 w1 = *reinterpret_cast<const float4*>(wp + 4);
-          const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+          const ulonglong2* wp = reinterpret_cast<const ulonglong2*>(ws + ((c * K + ky) * K + kx) * T::OCB);
+          const ulonglong2 wa = wp[0], wb = wp[1];  // channel pairs (0,1) (2,3) | (4,5) (6,7)
+          const unsigned long long wv[4] = {wa.x, wa.y, wb.x, wb.y};
 #pragma unroll
-          for (int i = 0; i < 8; ++i)
+          for (int ip = 0; ip < 4; ++ip)
 #pragma unroll
-            for (int j = 0; j < 4; ++j) acc[i][j] = __fmaf_rn(wv[i], xl[T::D + j * S + kx], acc[i][j]);
+            for (int j = 0; j < 4; ++j) accp[ip][j] = f2_fma(wv[ip], xd[j * S + kx], accp[ip][j]);
         }
       }
     }
@@ -486,6 +507,11 @@ __global__ void __launch_bounds__(32 * G * P) k_conv_tile(
     }
   }
 
+  float acc[8][4];
+#pragma unroll
+  for (int ip = 0; ip < 4; ++ip)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) f2_unpack(accp[ip][j], acc[2 * ip][j], acc[2 * ip + 1][j]);
   const int oy = ty0 + pg * 4 + r, ox = tx0 + cg * 4;
   if (oy >= OH || ox >= OW) return;
   const size_t plane = static_cast<size_t>(OH) * OW;
