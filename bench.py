@@ -438,7 +438,8 @@ class YoloWorkload(Workload):
 
     e2e_mode = ("pipelined: yolo.HostPipeline, depth 2 (H2D of batch i, plan of batch i-1 and D2H of batch "
                 "i-2 overlap on three streams); each step copies its own 315 MB input from pinned host memory "
-                "and reads its 181 MB output back; per-step inputs exceed L2, so no flush")
+                "and reads its 181 MB output back; device-timed from the first H2D to the last D2H, pipeline "
+                "fill and drain included; per-step inputs exceed L2, so no flush")
 
     def e2e_pipelined(self, warmup: int, steps: int, barrier) -> float:
         """ms per step of the serving loop, device-timed from the first H2D to the last D2H."""
@@ -633,6 +634,9 @@ def run_ours(args, peaks, peaks_kind) -> dict | None:
     # e2e through the public API with pinned host buffers
     KE = max(1, min(K, args.e2e_steps))
     if hasattr(wl, "e2e_pipelined"):
+        # a serving loop: its own step count (not capped by --steps), so the
+        # pipeline's fill (first H2D) and drain (last D2H) stay a small part
+        KE = max(1, args.e2e_steps)
         e2e_ms = wl.e2e_pipelined(args.warmup, KE, barrier)
         e2e_mode = wl.e2e_mode
     else:
@@ -887,7 +891,7 @@ def main() -> int:
     if args.profile_steps is None:
         args.profile_steps = 5 if args.workload == "yolo" else 50
     if args.e2e_steps is None:
-        args.e2e_steps = {"yolo": 10, "conv": 50}.get(args.workload, 200)
+        args.e2e_steps = {"yolo": 30, "conv": 50}.get(args.workload, 200)
     if args.steps is None:
         args.steps = DEFAULT_STEPS.get(args.workload, 100)
     args.warmup = max(3, args.warmup)

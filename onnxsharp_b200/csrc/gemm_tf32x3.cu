@@ -62,7 +62,7 @@ __device__ __forceinline__ void gemm_stage(uint8_t* tiles, const float (&acc)[12
 // the epilogue warps before their drain (named barrier 2 among them).
 template <class Cfg>
 __device__ __forceinline__ float* tile_bias(uint8_t* tiles) {
-  return reinterpret_cast<float*>(tiles + Cfg::TILE_BYTES + 256);
+  return reinterpret_cast<float*>(tiles + Cfg::RING_BYTES + 256);
 }
 
 template <class Cfg>
@@ -272,6 +272,10 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
   const int n0 = blockIdx.x * Cfg::BN;
   const int z = blockIdx.z, zb = ep.b_batched ? z : 0;
   const int num_kb = (Kp + kBK - 1) / kBK;
+  if (Cfg::TMEM_COLS < 2 * Cfg::BN && num_kb > Cfg::KC) {  // one accumulator buffer: one chunk at most
+    if (threadIdx.x == 0) atomicCAS(err, 0, OSC_EINVAL);
+    return;
+  }
   if (threadIdx.x == 0) {
     tma_prefetch(&mAh);
     tma_prefetch(&mAl);
@@ -552,10 +556,10 @@ static int gather_split(osc_ctx* ctx, const float* src, int batches, int inner, 
 
 // C[z] = A[z] (M x K) * B[zb] (K x N) on split operands Ahi/lo [batches][M][Kp],
 // Bhi/lo [b_batches][N][Kp].
-static int gemm_batched(osc_ctx* ctx, const float* ahi, const float* alo, int batches, int M, int Kp,
-                        const float* bhi, const float* blo, int b_batches, int N, const float* col_bias, int act,
-                        const EpiAffine& ep, float* y) {
-  using Cfg = Tf32x3Cfg<128, 3, 2>;
+template <class Cfg>
+static int gemm_batched_cfg(osc_ctx* ctx, const float* ahi, const float* alo, int batches, int M, int Kp,
+                            const float* bhi, const float* blo, int b_batches, int N, const float* col_bias, int act,
+                            const EpiAffine& ep, float* y) {
   CUtensorMap mAh, mAl, mBh, mBl;
   const uint64_t dimsA[3] = {static_cast<uint64_t>(Kp), static_cast<uint64_t>(M), static_cast<uint64_t>(batches)};
   const uint64_t dimsB[3] = {static_cast<uint64_t>(Kp), static_cast<uint64_t>(N), static_cast<uint64_t>(b_batches)};
@@ -575,6 +579,21 @@ static int gemm_batched(osc_ctx* ctx, const float* ahi, const float* alo, int ba
   kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, ctx->stream>>>(mAh, mAl, mBh, mBl, M, N, Kp, col_bias, act, ep, y,
                                                               ctx->d_err);
   return check_launch(ctx, "k_gemm_tf32x3");
+}
+
+// Products of at most two k-blocks (K <= 64: PSA's q.k^T with 32 channels)
+// take the one-stage configuration: ~70 KB of shared memory and one
+// 128-column accumulator, so three CTAs share an SM and one CTA's loads and
+// MMAs run under another's epilogue (with the three-stage ring a CTA holds
+// the SM alone and every tile's setup, load, MMA and stores run in series).
+static int gemm_batched(osc_ctx* ctx, const float* ahi, const float* alo, int batches, int M, int Kp,
+                        const float* bhi, const float* blo, int b_batches, int N, const float* col_bias, int act,
+                        const EpiAffine& ep, float* y) {
+  if ((Kp + kBK - 1) / kBK <= 2)
+    return gemm_batched_cfg<Tf32x3Cfg<128, 1, 2>>(ctx, ahi, alo, batches, M, Kp, bhi, blo, b_batches, N, col_bias,
+                                                  act, ep, y);
+  return gemm_batched_cfg<Tf32x3Cfg<128, 3, 2>>(ctx, ahi, alo, batches, M, Kp, bhi, blo, b_batches, N, col_bias, act,
+                                                ep, y);
 }
 
 // Bytes of work space batched_strided needs for its split operands.

@@ -892,13 +892,13 @@ struct YoloScales {
   int nc, total_anchors;
 };
 
+// Grid: x over anchors, y over images (strided when B exceeds the grid), so
+// no per-element division splits a flat index.
 __global__ void k_yolo_decode(const __grid_constant__ YoloScales s, int B, float* __restrict__ out) {
   const int A = s.total_anchors;
-  const long long total = static_cast<long long>(B) * A;
-  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const int a = static_cast<int>(i % A);
-    const int n = static_cast<int>(i / A);
+  const int a = blockIdx.x * blockDim.x + threadIdx.x;
+  if (a >= A) return;
+  for (int n = blockIdx.y; n < B; n += gridDim.y) {
     int sc = 0, base = 0;
     while (sc < 2 && a >= base + s.h[sc] * s.w[sc]) {
       base += s.h[sc] * s.w[sc];
@@ -925,6 +925,7 @@ __global__ void k_yolo_decode(const __grid_constant__ YoloScales s, int B, float
     o[2 * static_cast<size_t>(A)] = __fmul_rn(bw, st);
     o[3 * static_cast<size_t>(A)] = __fmul_rn(bh, st);
     const float* cl = s.cls[sc] + static_cast<size_t>(n) * s.cls_nstride[sc] + p;
+#pragma unroll 4
     for (int c = 0; c < s.nc; ++c)
       o[static_cast<size_t>(4 + c) * A] = ref_sigmoid(__ldg(cl + static_cast<size_t>(c) * hw));
   }
@@ -1335,9 +1336,12 @@ OSC_API int osc_yolo_decode_f32(osc_ctx* ctx, int B, int nc, const float* const*
     s.cls_nstride[i] = cls_nstride[i] ? cls_nstride[i] : static_cast<long long>(nc) * hs[i] * ws[i];
     s.total_anchors += hs[i] * ws[i];
   }
+  if (s.total_anchors <= 0 || hs[0] <= 0 || hs[1] <= 0 || hs[2] <= 0 || ws[0] <= 0 || ws[1] <= 0 || ws[2] <= 0)
+    return fail(OSC_EINVAL, "osc_yolo_decode_f32: empty scale");
   if (B == 0) return OSC_OK;
   prof_begin(ctx);
-  k_yolo_decode<<<blocks_for(ctx, static_cast<long long>(B) * s.total_anchors), 256, 0, ctx->stream>>>(s, B, out);
+  const dim3 grid(static_cast<unsigned>((s.total_anchors + 255) / 256), static_cast<unsigned>(std::min(B, 65535)));
+  k_yolo_decode<<<grid, 256, 0, ctx->stream>>>(s, B, out);
   return check_launch(ctx, "k_yolo_decode");
 }
 

@@ -35,9 +35,17 @@ struct Tf32x3Cfg {
   static constexpr int B_BYTES = BN * kBK * 4;
   static constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
   static constexpr int TILE_BYTES = STAGES * STAGE_BYTES;
-  static constexpr int TMEM_COLS = 2 * BN;       // two accumulator buffers
+  // The epilogue's row staging (gemm_stage: kBM x (BN + 4) floats + BN
+  // biases) reuses the ring; a one-stage ring is smaller than that, so the
+  // region is the larger of the two.
+  static constexpr int STAGING_BYTES = kBM * (BN + 4) * 4 + BN * 4;
+  static constexpr int RING_BYTES =
+      TILE_BYTES >= STAGING_BYTES ? TILE_BYTES : (STAGING_BYTES + 1023) / 1024 * 1024;
+  // Two accumulator buffers; a one-stage configuration serves only GEMMs of
+  // at most KC k-blocks (one chunk), so it holds one.
+  static constexpr int TMEM_COLS = (STAGES == 1 ? 1 : 2) * BN;
   // ring | barriers (256 bytes) | column biases of the tile (BN floats)
-  static constexpr int SMEM_BYTES = TILE_BYTES + 1024 + 256 + BN * 4;
+  static constexpr int SMEM_BYTES = RING_BYTES + 1024 + 256 + BN * 4;
   static_assert(BN == 128 || BN == 256, "BN");
   static_assert(STAGES <= 8, "stages");
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
@@ -59,7 +67,7 @@ __device__ __forceinline__ uint8_t* tiles_base(uint8_t* smem_raw) {
 
 template <class Cfg>
 __device__ __forceinline__ PipeBarriers* barriers(uint8_t* tiles) {
-  return reinterpret_cast<PipeBarriers*>(tiles + Cfg::TILE_BYTES);
+  return reinterpret_cast<PipeBarriers*>(tiles + Cfg::RING_BYTES);
 }
 
 // Barrier init + TMEM allocation; every thread of the CTA calls it.
@@ -256,6 +264,7 @@ struct Tf32x3PairCfg {
   static constexpr int B_BYTES = (BN / 2) * kBK * 4;  // this CTA's half of B
   static constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
   static constexpr int TILE_BYTES = STAGES * STAGE_BYTES;
+  static constexpr int RING_BYTES = TILE_BYTES;  // the staging fits the ring (asserted below)
   static constexpr int TMEM_COLS = 2 * BN;
   static constexpr int SMEM_BYTES = TILE_BYTES + 1024 + 256 + BN * 4;  // + the tile's column biases
   static_assert(BN == 128 || BN == 256, "BN");
