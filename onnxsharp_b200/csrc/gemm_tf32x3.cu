@@ -258,7 +258,7 @@ __global__ void k_gather_split(const float* __restrict__ src, int inner, long lo
 }
 
 template <class Cfg>
-__global__ void __launch_bounds__(Cfg::THREADS, 1)
+__global__ void __launch_bounds__(Cfg::THREADS, Cfg::STAGES == 1 ? 2 : 1)
     k_gemm_tf32x3_batched(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUtensorMap mAl,
                           const __grid_constant__ CUtensorMap mBh, const __grid_constant__ CUtensorMap mBl, int M,
                           int N, int Kp, const float* __restrict__ col_bias, int act,
@@ -301,47 +301,67 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
   }
   asm volatile("bar.sync 1, %0;" ::"r"(Cfg::THREADS) : "memory");
   if (!pb->abort_flag) {
+    // Every warp copies rows out: 4 rows per warp in flight, 16-byte shared
+    // loads, the per-element steps (bias, alpha, beta * C, row scale,
+    // activation) decided once per tile. Per element the order is unchanged.
     constexpr int kPitch = Cfg::BN + 4;
+    constexpr int kWarps = Cfg::THREADS / 32;
     const float* stage = reinterpret_cast<const float*>(tiles);
     const float* sbias = stage + kBM * kPitch;
     float* Yz = Y + static_cast<long long>(z / ep.inner) * ep.y_outer + static_cast<long long>(z % ep.inner) * ep.y_inner;
-    const bool affine = ep.alpha != 1.0f || (ep.beta != 0.0f && ep.c != nullptr && ep.c_len > 0);
+    const bool has_bias = col_bias != nullptr;
+    const bool scale_a = ep.alpha != 1.0f;
+    const bool add_c = ep.beta != 0.0f && ep.c != nullptr && ep.c_len > 0;
     const bool full_c = ep.c_len >= static_cast<long long>(M) * N;
-    for (int r = warp; r < kBM; r += Cfg::THREADS / 32) {
-      const int row = m0 + r;
-      if (row >= M) break;
-      float* yrow = Yz + static_cast<size_t>(row) * ep.y_ld;
-      const float rs = ep.row_scale != nullptr ? ep.row_scale[static_cast<size_t>(z) * M + row] : 1.0f;
-      const bool vec_row = (reinterpret_cast<uintptr_t>(yrow) & 15u) == 0;
+    const bool has_rs = ep.row_scale != nullptr;
+    with_act(act, [&](auto tag) {
+      constexpr int ACT = decltype(tag)::value;
+      for (int r0 = warp; r0 < kBM; r0 += 4 * kWarps) {
 #pragma unroll
-      for (int h = 0; h < Cfg::BN; h += 128) {
-        const int j0 = n0 + h + lane * 4;
-        float v[4];
+        for (int u = 0; u < 4; ++u) {
+          const int r = r0 + u * kWarps;
+          const int row = m0 + r;
+          if (r < kBM && row < M) {
+            float* yrow = Yz + static_cast<size_t>(row) * ep.y_ld;
+            const float rs = has_rs ? ep.row_scale[static_cast<size_t>(z) * M + row] : 1.0f;
+            const bool vec_row = (reinterpret_cast<uintptr_t>(yrow) & 15u) == 0;
 #pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          const int j = j0 + t;
-          v[t] = stage[r * kPitch + h + lane * 4 + t];
-          if (col_bias != nullptr) v[t] = __fadd_rn(v[t], sbias[h + lane * 4 + t]);
-          if (affine) {  // Gemm (AttnOps.cs:100-128): alpha * d, then + beta * c
-            if (ep.alpha != 1.0f) v[t] = __fmul_rn(ep.alpha, v[t]);
-            if (ep.beta != 0.0f && ep.c != nullptr && ep.c_len > 0 && j < N) {
-              const float cv = full_c ? ep.c[static_cast<size_t>(row) * N + j]
-                                      : (ep.c_len == 1 ? ep.c[0] : ep.c[j % ep.c_len]);
-              v[t] = __fadd_rn(v[t], __fmul_rn(ep.beta, cv));
+            for (int h = 0; h < Cfg::BN; h += 128) {
+              const int c0 = h + lane * 4;
+              const int j0 = n0 + c0;
+              const float4 sv = *reinterpret_cast<const float4*>(stage + r * kPitch + c0);
+              float v[4] = {sv.x, sv.y, sv.z, sv.w};
+              if (has_bias) {
+                const float4 bv = *reinterpret_cast<const float4*>(sbias + c0);
+                v[0] = __fadd_rn(v[0], bv.x);
+                v[1] = __fadd_rn(v[1], bv.y);
+                v[2] = __fadd_rn(v[2], bv.z);
+                v[3] = __fadd_rn(v[3], bv.w);
+              }
+#pragma unroll
+              for (int t = 0; t < 4; ++t) {
+                const int j = j0 + t;
+                if (scale_a) v[t] = __fmul_rn(ep.alpha, v[t]);  // Gemm (AttnOps.cs:100-128): alpha * d, then + beta * c
+                if (add_c && j < N) {
+                  const float cv = full_c ? ep.c[static_cast<size_t>(row) * N + j]
+                                          : (ep.c_len == 1 ? ep.c[0] : ep.c[j % ep.c_len]);
+                  v[t] = __fadd_rn(v[t], __fmul_rn(ep.beta, cv));
+                }
+                if (has_rs) v[t] = __fmul_rn(v[t], rs);
+                v[t] = act_t<ACT>(v[t]);
+              }
+              if (vec_row && j0 + 4 <= N) {  // 16-byte stores: whole 32-byte sectors per lane pair
+                *reinterpret_cast<float4*>(yrow + j0) = make_float4(v[0], v[1], v[2], v[3]);
+              } else {
+#pragma unroll
+                for (int t = 0; t < 4; ++t)
+                  if (j0 + t < N) yrow[j0 + t] = v[t];
+              }
             }
           }
-          if (ep.row_scale != nullptr) v[t] = __fmul_rn(v[t], rs);
-          v[t] = apply_act(v[t], act);
-        }
-        if (vec_row && j0 + 4 <= N) {  // 16-byte stores: whole 32-byte sectors per lane pair
-          *reinterpret_cast<float4*>(yrow + j0) = make_float4(v[0], v[1], v[2], v[3]);
-        } else {
-#pragma unroll
-          for (int t = 0; t < 4; ++t)
-            if (j0 + t < N) yrow[j0 + t] = v[t];
         }
       }
-    }
+    });
   }
   pipe_teardown<Cfg>(pb, tmem);
 }
@@ -773,6 +793,75 @@ __global__ void k_softmax_split(const float* __restrict__ S, long long rows, int
   }
 }
 
+// The same for rows of at most kSoftRegs * 32 split columns (PSA: 400): the
+// row lives in registers (element j in lane j % 32, slot j / 32), so S is
+// read once and nothing is parked in global memory. All 32 lanes compute the
+// exponentials; the reference's 8 partial sums keep their order: chain l
+// (lanes 0..7) adds e[l], e[l+8], e[l+16], e[l+24], e[l+32], ... fetched by
+// shuffles, then the chains are summed 0..7 and the scalar tail follows.
+constexpr int kSoftRegs = 16;
+
+__global__ void k_softmax_split_reg(const float* __restrict__ S, long long rows, int len, int kp,
+                                    float* __restrict__ hi, float* __restrict__ lo) {
+  const int lane = threadIdx.x & 31;
+  const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
+  const int vend = len & ~7;
+  for (long long r = blockIdx.x * static_cast<long long>(blockDim.x >> 5) + (threadIdx.x >> 5); r < rows;
+       r += warps) {
+    const float* sr = S + r * len;
+    float v[kSoftRegs];
+#pragma unroll
+    for (int k = 0; k < kSoftRegs; ++k) {
+      const int j = lane + 32 * k;
+      v[k] = j < len ? __ldg(sr + j) : -INFINITY;
+    }
+    float mx = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < kSoftRegs; ++k) mx = fmaxf(mx, v[k]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float e[kSoftRegs];
+#pragma unroll
+    for (int k = 0; k < kSoftRegs; ++k) {
+      const int j = lane + 32 * k;
+      e[k] = j < vend ? ref_exp(__fsub_rn(v[k], mx)) : (j < len ? expf(__fsub_rn(v[k], mx)) : 0.0f);
+    }
+    float part = 0.0f;  // chain (lane & 7), meaningful in lanes 0..7
+#pragma unroll
+    for (int k = 0; k < kSoftRegs; ++k) {
+      if (32 * k >= vend) break;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float t = __shfl_sync(0xffffffffu, e[k], (lane & 7) + 8 * q);
+        if (32 * k + 8 * q + (lane & 7) < vend) part = __fadd_rn(part, t);
+      }
+    }
+    float total = 0.0f;
+    for (int l = 0; l < 8; ++l) total = __fadd_rn(total, __shfl_sync(0xffffffffu, part, l));
+    for (int j = vend; j < len; ++j) {  // scalar tail in order (uniform across the warp)
+      const int kk = j >> 5;
+      float mine = 0.0f;
+#pragma unroll
+      for (int k = 0; k < kSoftRegs; ++k)
+        if (k == kk) mine = e[k];
+      total = __fadd_rn(total, __shfl_sync(0xffffffffu, mine, j & 31));
+    }
+    const float inv = __fdiv_rn(1.0f, total);
+    float* hr = hi + r * kp;
+    float* lr = lo + r * kp;
+#pragma unroll
+    for (int k = 0; k < kSoftRegs; ++k) {
+      const int j = lane + 32 * k;
+      if (j < kp) {
+        const float p = j < len ? __fmul_rn(e[k], inv) : 0.0f;
+        const float h = to_tf32(p);
+        hr[j] = h;
+        lr[j] = __fsub_rn(p, h);
+      }
+    }
+  }
+}
+
 // YOLO11's PSA attention (the exported MatMul -> Mul -> Softmax -> MatMul
 // chain) on the tensor cores, per image b and head h of qkv [B][heads*(2kd+hd)][T]:
 //   S = (q^T k) * scale        [T][T]   (batched 3xTF32 product, scale in the epilogue)
@@ -815,8 +904,13 @@ int psa_composed(osc_ctx* ctx, const float* qkv, long long qkv_nstride, int B, i
     const long long rows = Z * T;
     const int blocks = static_cast<int>(std::min<long long>((rows + 7) / 8, static_cast<long long>(ctx->num_sms) * 16));
     prof_begin(ctx);
-    k_softmax_split<<<blocks, 256, 0, ctx->stream>>>(S, rows, T, kt, phi, plo);
-    OSC_TRY(check_launch(ctx, "k_softmax_split"));
+    if (kt <= kSoftRegs * 32) {
+      k_softmax_split_reg<<<blocks, 256, 0, ctx->stream>>>(S, rows, T, kt, phi, plo);
+      OSC_TRY(check_launch(ctx, "k_softmax_split_reg"));
+    } else {
+      k_softmax_split<<<blocks, 256, 0, ctx->stream>>>(S, rows, T, kt, phi, plo);
+      OSC_TRY(check_launch(ctx, "k_softmax_split"));
+    }
   }
   // v as [z][channel][token] (already K-major)
   OSC_TRY(gather_split(ctx, qkv + 2LL * kd * T, nz, heads, qkv_nstride, per, T, 1, hd, T, kt, vhi, vlo));
