@@ -121,11 +121,16 @@ __global__ void __launch_bounds__(ConvCfg::THREADS, 1)
     constexpr int kPitch = Cfg::BN + 4;
     const float* stage = reinterpret_cast<const float*>(tiles);
     const float* sbias = stage + kBM * kPitch;
+    constexpr int kWarps = Cfg::THREADS / 32;
     with_act(g.act, [&](auto tag) {
       constexpr int ACT = decltype(tag)::value;
-      for (int r = warp; r < kBM; r += Cfg::THREADS / 32) {
+      // 4 channel rows per warp in flight (their residual loads overlap)
+      for (int r0 = warp; r0 < kBM; r0 += 4 * kWarps) {
+#pragma unroll
+       for (int u = 0; u < 4; ++u) {
+        const int r = r0 + u * kWarps;
         const int oc = m0 + r;
-        if (oc >= g.M) break;
+        if (r >= kBM || oc >= g.M) continue;
         const float b = sbias[r];
         const size_t plane_off = static_cast<size_t>(oc) * g.OH * g.OW;
         float* yplane = y + static_cast<size_t>(n) * g.y_nstride + plane_off;
@@ -157,6 +162,7 @@ __global__ void __launch_bounds__(ConvCfg::THREADS, 1)
               if (ox + q < g.OW) dst[q] = rsrc ? __fadd_rn(rsrc[q], o[q]) : o[q];
           }
         }
+       }
       }
     });
   }
