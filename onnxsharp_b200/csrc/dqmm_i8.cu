@@ -370,50 +370,60 @@ __global__ void __launch_bounds__(kDqlThreads, 1)
       params_out[1] = static_cast<float>(p.zp);
     }
   }
-  // quantize the CTA's rows from shared memory: 4-element groups over all
-  // threads (a row's kp/4 groups are a multiple of 32, so a warp stays in one row)
+  // quantize the CTA's rows from shared memory: one warp per row, 4-element
+  // groups, four groups per lane in flight; the row's sum stays in registers
+  // and is reduced once per row (integer sums: any order gives the same value)
   const float inv = p.inverse, zpf = static_cast<float>(p.zp);
-  const int gpr = kp >> 2;
+  const int gpr = kp >> 2;  // a multiple of 32
   const bool vk = (k & 3) == 0;
-  for (int g = tid; g < nrows * gpr; g += kDqlThreads) {
-    const int row = g / gpr, c0 = (g - row * gpr) * 4;
+  for (int row = wid; row < nrows; row += kDqlThreads / 32) {
     const float* xr = rows_s + static_cast<size_t>(row) * k;
-    float xv[4];
-    if (vk && c0 + 4 <= k) {
-      const float4 t4 = *reinterpret_cast<const float4*>(xr + c0);
-      xv[0] = t4.x;
-      xv[1] = t4.y;
-      xv[2] = t4.z;
-      xv[3] = t4.w;
-    } else {
-#pragma unroll
-      for (int t = 0; t < 4; ++t) xv[t] = c0 + t < k ? xr[c0 + t] : 0.0f;
-    }
-    uint32_t packed = 0;
+    uint8_t* qr = q + static_cast<size_t>(r0 + row) * kp;
     int sum = 0, nan = 0;
+    for (int g0 = 0; g0 < gpr; g0 += 4 * 32) {
 #pragma unroll
-    for (int t = 0; t < 4; ++t) {
-      uint32_t v = 0;
-      if (c0 + t < k) {
-        const float sv = __fmul_rn(xv[t], inv);
-        if (sv != sv) {
-          nan = 1;
-        } else {
-          v = static_cast<uint32_t>(minps(255.0f, maxps(0.0f, __fadd_rn(rintf(sv), zpf))));
+      for (int u = 0; u < 4; ++u) {
+        const int g = g0 + u * 32 + lane;
+        if (g < gpr) {
+          const int c0 = g * 4;
+          float xv[4];
+          if (vk && c0 + 4 <= k) {
+            const float4 t4 = *reinterpret_cast<const float4*>(xr + c0);
+            xv[0] = t4.x;
+            xv[1] = t4.y;
+            xv[2] = t4.z;
+            xv[3] = t4.w;
+          } else {
+#pragma unroll
+            for (int t = 0; t < 4; ++t) xv[t] = c0 + t < k ? xr[c0 + t] : 0.0f;
+          }
+          uint32_t packed = 0;
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            uint32_t v = 0;
+            if (c0 + t < k) {
+              const float sv = __fmul_rn(xv[t], inv);
+              if (sv != sv) {
+                nan = 1;
+              } else {
+                v = static_cast<uint32_t>(minps(255.0f, maxps(0.0f, __fadd_rn(rintf(sv), zpf))));
+              }
+            }
+            sum += static_cast<int>(v);
+            packed |= v << (8 * t);
+          }
+          *reinterpret_cast<uint32_t*>(qr + c0) = packed;
         }
       }
-      sum += static_cast<int>(v);
-      packed |= v << (8 * t);
     }
-    *reinterpret_cast<uint32_t*>(q + static_cast<size_t>(r0 + row) * kp + c0) = packed;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
       sum += __shfl_xor_sync(0xffffffffu, sum, o);
       nan |= __shfl_xor_sync(0xffffffffu, nan, o);
     }
     if (lane == 0) {
-      atomicAdd(&s_sum[row], sum);
-      if (nan) s_nan[row] = 1;
+      s_sum[row] = sum;
+      s_nan[row] = nan;
     }
   }
   __syncthreads();
