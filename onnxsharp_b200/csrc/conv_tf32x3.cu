@@ -418,7 +418,9 @@ __global__ void __launch_bounds__(pw::kThreads, 1)
     }
   } else {
     // epilogue: warp kEpiBase + 4h + q drains TMEM lanes 32q.. (pixels p0 + 32q + lane),
-    // columns 64h.. (output channels oc0 + 64h ..)
+    // columns cpw*h .. (output channels oc0 + cpw*h ..): cpw = 64, or 32 when
+    // the tile has at most 64 channels, so that both warp halves share the
+    // drain, the activations and the stores of narrow tiles
     const int q = warp & 3;
     const int h = (warp - kEpiBase) >> 2;
     int gc = 0;
@@ -428,8 +430,9 @@ __global__ void __launch_bounds__(pw::kThreads, 1)
       const long long r = t / g.otiles;
       const int pt = static_cast<int>(r % g.ptiles);
       const int n = static_cast<int>(r / g.ptiles);
-      const int oc0 = ot * kBN + h * 64;
-      const int nvalid = min(64, g.M - oc0);  // may be <= 0 for the upper half of a narrow tile
+      const int cpw = g.M - ot * kBN <= 64 ? 32 : 64;  // channels per warp
+      const int oc0 = ot * kBN + h * cpw;
+      const int nvalid = min(cpw, g.M - oc0);  // may be <= 0 for the upper half of a narrow tile
       float acc[64];
       for (int c = 0; c < nchunks; ++c, ++gc) {
         const int buf = gc & 1;
@@ -441,9 +444,10 @@ __global__ void __launch_bounds__(pw::kThreads, 1)
         }
         tc_fence_after();
         const uint32_t base =
-            tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * kBN + h * 64);
+            tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * kBN + h * cpw);
 #pragma unroll
         for (int gg = 0; gg < 4; gg += 2) {
+          if (gg * 16 >= cpw) break;
           uint32_t r0[16], r1[16];
           tmem_ld16(base + gg * 16, r0);
           tmem_ld16(base + (gg + 1) * 16, r1);
@@ -489,6 +493,7 @@ __global__ void __launch_bounds__(pw::kThreads, 1)
           constexpr int ACT = decltype(tag)::value;
 #pragma unroll
           for (int j0 = 0; j0 < 64; j0 += 8) {
+            if (j0 >= cpw) break;
             // residuals of 8 channels in flight at once (clamped rows, no branch between the loads)
             float rv[8];
             if (rp) {
