@@ -196,7 +196,9 @@ constexpr int kB = kBN * kBK * 4;         // 16 KB: 128 oc x 32 ch
 constexpr int kStage = 2 * kA + 2 * kB;   // A (hi after the split) | A lo | W hi | W lo
 constexpr int kTx = kA + 2 * kB;          // bytes TMA lands per stage
 constexpr int kConvWarps = 2;
-constexpr int kEpiWarps = 8;              // two per TMEM lane quadrant, 64 columns each
+constexpr int kEpiWarps = 16;             // kEpiGroups per TMEM lane quadrant
+constexpr int kEpiGroups = kEpiWarps / 4;
+constexpr int kColsMax = 128 / kEpiGroups;  // output channels per epilogue warp on a full tile
 constexpr int kEpiBase = 2 + kConvWarps;  // first epilogue warp (a multiple of 4: warp % 4 = lane quadrant)
 constexpr int kThreads = 32 * (kEpiBase + kEpiWarps);  // producer, MMA, converters, epilogue
 constexpr int kKC = 2;                    // k-blocks per TMEM chunk
@@ -418,9 +420,9 @@ __global__ void __launch_bounds__(pw::kThreads, 1)
     }
   } else {
     // epilogue: warp kEpiBase + 4h + q drains TMEM lanes 32q.. (pixels p0 + 32q + lane),
-    // columns cpw*h .. (output channels oc0 + cpw*h ..): cpw = 64, or 32 when
-    // the tile has at most 64 channels, so that both warp halves share the
-    // drain, the activations and the stores of narrow tiles
+    // columns cpw*h .. (output channels oc0 + cpw*h ..): cpw = kColsMax, or half
+    // of it when the tile has at most 64 channels, so that every warp group
+    // shares the drain, the activations and the stores of narrow tiles
     const int q = warp & 3;
     const int h = (warp - kEpiBase) >> 2;
     int gc = 0;
@@ -430,10 +432,10 @@ __global__ void __launch_bounds__(pw::kThreads, 1)
       const long long r = t / g.otiles;
       const int pt = static_cast<int>(r % g.ptiles);
       const int n = static_cast<int>(r / g.ptiles);
-      const int cpw = g.M - ot * kBN <= 64 ? 32 : 64;  // channels per warp
+      const int cpw = g.M - ot * kBN <= kBN / 2 ? kColsMax / 2 : kColsMax;  // channels per warp
       const int oc0 = ot * kBN + h * cpw;
-      const int nvalid = min(cpw, g.M - oc0);  // may be <= 0 for the upper half of a narrow tile
-      float acc[64];
+      const int nvalid = min(cpw, g.M - oc0);  // may be <= 0 for the upper groups of a narrow tile
+      float acc[kColsMax];
       for (int c = 0; c < nchunks; ++c, ++gc) {
         const int buf = gc & 1;
         bool got = mbar_wait(&pb->acc_full[buf], (gc >> 1) & 1u, &pb->abort_flag, err);
@@ -446,23 +448,27 @@ __global__ void __launch_bounds__(pw::kThreads, 1)
         const uint32_t base =
             tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * kBN + h * cpw);
 #pragma unroll
-        for (int gg = 0; gg < 4; gg += 2) {
+        for (int gg = 0; gg < kColsMax / 16; gg += kColsMax > 32 ? 2 : 1) {
           if (gg * 16 >= cpw) break;
+          const bool two = kColsMax > 32 && (gg + 1) * 16 < cpw;  // 16-column groups in pairs on wide warps
           uint32_t r0[16], r1[16];
           tmem_ld16(base + gg * 16, r0);
-          tmem_ld16(base + (gg + 1) * 16, r1);
+          if (two) tmem_ld16(base + (gg + 1) * 16, r1);
           tmem_wait_ld();
           if (c == 0) {
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              acc[gg * 16 + j] = __uint_as_float(r0[j]);
-              acc[(gg + 1) * 16 + j] = __uint_as_float(r1[j]);
+            for (int j = 0; j < 16; ++j) acc[gg * 16 + j] = __uint_as_float(r0[j]);
+            if (two) {
+#pragma unroll
+              for (int j = 0; j < 16; ++j) acc[(gg + 1) * 16 + j] = __uint_as_float(r1[j]);
             }
           } else {
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              acc[gg * 16 + j] = __fadd_rn(acc[gg * 16 + j], __uint_as_float(r0[j]));
-              acc[(gg + 1) * 16 + j] = __fadd_rn(acc[(gg + 1) * 16 + j], __uint_as_float(r1[j]));
+            for (int j = 0; j < 16; ++j) acc[gg * 16 + j] = __fadd_rn(acc[gg * 16 + j], __uint_as_float(r0[j]));
+            if (two) {
+#pragma unroll
+              for (int j = 0; j < 16; ++j)
+                acc[(gg + 1) * 16 + j] = __fadd_rn(acc[(gg + 1) * 16 + j], __uint_as_float(r1[j]));
             }
           }
         }
@@ -492,7 +498,7 @@ __global__ void __launch_bounds__(pw::kThreads, 1)
         with_act(g.act, [&](auto tag) {
           constexpr int ACT = decltype(tag)::value;
 #pragma unroll
-          for (int j0 = 0; j0 < 64; j0 += 8) {
+          for (int j0 = 0; j0 < kColsMax; j0 += 8) {
             if (j0 >= cpw) break;
             // residuals of 8 channels in flight at once (clamped rows, no branch between the loads)
             float rv[8];
