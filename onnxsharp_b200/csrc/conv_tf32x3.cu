@@ -189,30 +189,41 @@ __global__ void __launch_bounds__(ConvCfg::THREADS, 1)
 //    bytes): NCHW without a staging tile. Biases come from a shared-memory
 //    table filled once per CTA.
 namespace pw {
-constexpr int kStages = 3;
-constexpr int kBN = 128;                  // output channels per tile
 constexpr int kA = kBM * kBK * 4;         // 16 KB: 128 px x 32 ch
-constexpr int kB = kBN * kBK * 4;         // 16 KB: 128 oc x 32 ch
-constexpr int kStage = 2 * kA + 2 * kB;   // A (hi after the split) | A lo | W hi | W lo
-constexpr int kTx = kA + 2 * kB;          // bytes TMA lands per stage
 constexpr int kConvWarps = 2;
 constexpr int kEpiWarps = 16;             // kEpiGroups per TMEM lane quadrant
 constexpr int kEpiGroups = kEpiWarps / 4;
-constexpr int kColsMax = 128 / kEpiGroups;  // output channels per epilogue warp on a full tile
 constexpr int kEpiBase = 2 + kConvWarps;  // first epilogue warp (a multiple of 4: warp % 4 = lane quadrant)
 constexpr int kThreads = 32 * (kEpiBase + kEpiWarps);  // producer, MMA, converters, epilogue
 constexpr int kKC = 2;                    // k-blocks per TMEM chunk
-constexpr int kTmemCols = 2 * kBN;
+constexpr int kMaxStages = 4;
+constexpr int kMaxBias = 4096;            // output channels whose biases fit the shared-memory table
 struct Bars {
-  uint64_t full[kStages], conv[kStages], empty[kStages];
+  uint64_t full[kMaxStages], conv[kMaxStages], empty[kMaxStages];
   uint64_t acc_full[2], acc_empty[2];
   uint64_t mma_done;
   uint32_t tmem_slot;
   int abort_flag;
 };
-constexpr int kMaxBias = 4096;            // output channels whose biases fit the shared-memory table
-constexpr int kSmemBase = kStages * kStage + 1024 + 256;  // + the bias table (M floats, rounded to 16 bytes)
-static_assert(kSmemBase + kMaxBias * 4 <= 232448, "shared memory budget");
+// Per tile width: 128 output channels (3 stages of 64 KB) or 64 (4 stages of
+// 48 KB): a stage is released only when its MMAs complete, so on layers with
+// at most 64 output channels the narrower weight tile buys a deeper ring,
+// i.e. more k-blocks in flight.
+template <int BN>
+struct Cfg {
+  static constexpr int kBN = BN;                          // output channels per tile
+  static constexpr int kStages = BN == 64 ? 4 : 3;
+  static constexpr int kB = BN * kBK * 4;                 // one weight part: BN oc x 32 ch
+  static constexpr int kStage = 2 * kA + 2 * kB;          // A (hi after the split) | A lo | W hi | W lo
+  static constexpr int kTx = kA + 2 * kB;                 // bytes TMA lands per stage
+  static constexpr int kTmemCols = 2 * BN;                // two accumulators
+  static constexpr int kColsMax = BN / kEpiGroups;        // output channels per epilogue warp on a full tile
+  static constexpr int kSmemBase = kStages * kStage + 1024 + 256;  // + the bias table (M floats, rounded to 16 bytes)
+  static_assert(kStages <= kMaxStages, "stages");
+  static_assert(kStage % 1024 == 0 && kA % 1024 == 0 && kB % 1024 == 0, "1024-byte aligned operand boxes");
+  static_assert(kColsMax % 16 == 0, "TMEM drain granularity");
+  static_assert(kSmemBase + kMaxBias * 4 <= 232448, "shared memory budget");
+};
 static_assert(kEpiBase % 4 == 0, "epilogue warps must start on a lane-quadrant boundary");
 static_assert(sizeof(Bars) <= 256, "barrier block");
 }  // namespace pw
@@ -236,20 +247,21 @@ struct PwGeom {
 // channels per tap and channel block, hi and lo), no converter warps. Pixels
 // as M spare the MMA the empty rows a channel-major tile has when the layer
 // has only 32 or 64 output channels.
-template <bool TAPS>
+template <bool TAPS, int BN>
 __global__ void __launch_bounds__(pw::kThreads, 1)
     k_conv_px_tf32x3(const __grid_constant__ CUtensorMap mX, const __grid_constant__ CUtensorMap mXl,
                      const __grid_constant__ CUtensorMap mWh, const __grid_constant__ CUtensorMap mWl,
                      const __grid_constant__ PwGeom g, const __grid_constant__ ConvTaps taps,
                      const float* __restrict__ bias, float* __restrict__ y, int* __restrict__ err) {
   using namespace pw;
+  using CF = Cfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* tiles = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  Bars* pb = reinterpret_cast<Bars*>(tiles + kStages * kStage);
+  Bars* pb = reinterpret_cast<Bars*>(tiles + CF::kStages * CF::kStage);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < CF::kStages; ++s) {
       mbar_init(&pb->full[s], 1);
       mbar_init(&pb->conv[s], kConvWarps);
       mbar_init(&pb->empty[s], 1);
@@ -267,7 +279,7 @@ __global__ void __launch_bounds__(pw::kThreads, 1)
     tma_prefetch(&mWl);
   }
   if (warp == 1) {
-    tmem_alloc(&pb->tmem_slot, kTmemCols);
+    tmem_alloc(&pb->tmem_slot, CF::kTmemCols);
     tmem_relinquish();
   }
   // every output channel's bias, read once per CTA (the epilogue reads it from
@@ -284,23 +296,23 @@ __global__ void __launch_bounds__(pw::kThreads, 1)
     if (lane == 0) {
       int i = 0;
       bool ok = true;
-      const uint32_t tx_bytes = TAPS ? static_cast<uint32_t>(2 * g.a_bytes + 2 * kB) : static_cast<uint32_t>(kTx);
+      const uint32_t tx_bytes = TAPS ? static_cast<uint32_t>(2 * g.a_bytes + 2 * CF::kB) : static_cast<uint32_t>(CF::kTx);
       for (long long t = blockIdx.x; t < g.tiles && ok; t += gridDim.x) {
         const int ot = static_cast<int>(t % g.otiles);
         const long long r = t / g.otiles;
         const int pt = static_cast<int>(r % g.ptiles);
         const int n = static_cast<int>(r / g.ptiles);
-        const int p0 = pt * kBM, oc0 = ot * kBN;
+        const int p0 = pt * kBM, oc0 = ot * CF::kBN;
         const int ox0 = TAPS ? (pt % g.tiles_w) * g.BW : 0, oy0 = TAPS ? (pt / g.tiles_w) * g.BH : 0;
         for (int kb = 0; kb < g.num_kb; ++kb) {
-          const int s = i % kStages;
-          const uint32_t ph = (i / kStages) & 1u;
+          const int s = i % CF::kStages;
+          const uint32_t ph = (i / CF::kStages) & 1u;
           if (!mbar_wait(&pb->empty[s], ph ^ 1u, &pb->abort_flag, err)) {
             ok = false;
             break;
           }
           mbar_arrive_expect_tx(&pb->full[s], tx_bytes);
-          uint8_t* st = tiles + s * kStage;
+          uint8_t* st = tiles + s * CF::kStage;
           if constexpr (TAPS) {
             const int tap = kb / g.cp_blocks;
             const int c0 = (kb - tap * g.cp_blocks) * kBK;
@@ -312,14 +324,14 @@ __global__ void __launch_bounds__(pw::kThreads, 1)
             for (int q = 0; q < 4; ++q) tma_load_3d(st + q * 4096, &mX, &pb->full[s], p0 + 32 * q, kb * kBK, n);
           }
           tma_load_2d(st + 2 * kA, &mWh, &pb->full[s], kb * kBK, oc0);
-          tma_load_2d(st + 2 * kA + kB, &mWl, &pb->full[s], kb * kBK, oc0);
+          tma_load_2d(st + 2 * kA + CF::kB, &mWl, &pb->full[s], kb * kBK, oc0);
           ++i;
         }
       }
       if (!ok) {  // error path: let the copies in flight land before the CTA exits
-        for (int j = i > kStages ? i - kStages : 0; j < i; ++j) {
+        for (int j = i > CF::kStages ? i - CF::kStages : 0; j < i; ++j) {
           const uint64_t t0 = globaltimer_ns();
-          while (!mbar_try_wait(&pb->full[j % kStages], (j / kStages) & 1u) &&
+          while (!mbar_try_wait(&pb->full[j % CF::kStages], (j / CF::kStages) & 1u) &&
                  globaltimer_ns() - t0 < 50ull * 1000ull * 1000ull) {
           }
         }
@@ -330,8 +342,8 @@ __global__ void __launch_bounds__(pw::kThreads, 1)
       int i = 0, gc = 0;
       bool ok = true;
       for (long long t = blockIdx.x; t < g.tiles && ok; t += gridDim.x) {
-        const int oc0 = static_cast<int>(t % g.otiles) * kBN;
-        const int nn = min(kBN, ((g.M - oc0) + 15) & ~15);
+        const int oc0 = static_cast<int>(t % g.otiles) * CF::kBN;
+        const int nn = min(CF::kBN, ((g.M - oc0) + 15) & ~15);
         const uint32_t idesc = TAPS ? idesc_tf32(kBM, nn) : idesc_tf32_amn(kBM, nn);
         int kb = 0;
         for (int c = 0; c < nchunks && ok; ++c, ++gc) {
@@ -341,12 +353,12 @@ __global__ void __launch_bounds__(pw::kThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t d = tmem + static_cast<uint32_t>(buf * kBN);
+          const uint32_t d = tmem + static_cast<uint32_t>(buf * CF::kBN);
           const int kb_end = min(g.num_kb, kb + kKC);
           uint32_t acc = 0u;
           for (; kb < kb_end; ++kb, ++i) {
-            const int s = i % kStages;
-            const uint32_t ph = (i / kStages) & 1u;
+            const int s = i % CF::kStages;
+            const uint32_t ph = (i / CF::kStages) & 1u;
             // pointwise: conv[s] follows full[s] (the converters waited on it);
             // the second wait returns at once and orders the weight boxes too
             if ((!TAPS && !mbar_wait(&pb->conv[s], ph, &pb->abort_flag, err)) ||
@@ -355,11 +367,11 @@ __global__ void __launch_bounds__(pw::kThreads, 1)
               break;
             }
             tc_fence_after();
-            const uint32_t base = smem_addr(tiles + s * kStage);
+            const uint32_t base = smem_addr(tiles + s * CF::kStage);
             const uint64_t dAh = TAPS ? sdesc_kmajor_sw128(base) : sdesc_mnmajor_sw128_32b(base, 4096, 512);
             const uint64_t dAl = TAPS ? sdesc_kmajor_sw128(base + kA) : sdesc_mnmajor_sw128_32b(base + kA, 4096, 512);
             const uint64_t dBh = sdesc_kmajor_sw128(base + 2 * kA);
-            const uint64_t dBl = sdesc_kmajor_sw128(base + 2 * kA + kB);
+            const uint64_t dBl = sdesc_kmajor_sw128(base + 2 * kA + CF::kB);
 #pragma unroll
             for (int kk = 0; kk < kBK / 8; ++kk) {
               // +1024 bytes: the next 8 channel rows (MN-major); +32 bytes inside the K-major row
@@ -388,16 +400,16 @@ __global__ void __launch_bounds__(pw::kThreads, 1)
     bool ok = !TAPS;
     for (long long t = blockIdx.x; t < g.tiles && ok; t += gridDim.x) {
       for (int kb = 0; kb < g.num_kb; ++kb, ++i) {
-        const int s = i % kStages;
-        const uint32_t ph = (i / kStages) & 1u;
+        const int s = i % CF::kStages;
+        const uint32_t ph = (i / CF::kStages) & 1u;
         bool got = mbar_wait(&pb->full[s], ph, &pb->abort_flag, err);
         got = __all_sync(0xffffffffu, got);
         if (!got) {
           ok = false;
           break;
         }
-        float4* a = reinterpret_cast<float4*>(tiles + s * kStage);
-        float4* al = reinterpret_cast<float4*>(tiles + s * kStage + kA);
+        float4* a = reinterpret_cast<float4*>(tiles + s * CF::kStage);
+        float4* al = reinterpret_cast<float4*>(tiles + s * CF::kStage + kA);
 #pragma unroll 4
         for (int j = ct; j < kA / 16; j += 32 * kConvWarps) {
           const float4 v = a[j];
@@ -420,7 +432,7 @@ __global__ void __launch_bounds__(pw::kThreads, 1)
     }
   } else {
     // epilogue: warp kEpiBase + 4h + q drains TMEM lanes 32q.. (pixels p0 + 32q + lane),
-    // columns cpw*h .. (output channels oc0 + cpw*h ..): cpw = kColsMax, or half
+    // columns cpw*h .. (output channels oc0 + cpw*h ..): cpw = CF::kColsMax, or half
     // of it when the tile has at most 64 channels, so that every warp group
     // shares the drain, the activations and the stores of narrow tiles
     const int q = warp & 3;
@@ -432,10 +444,10 @@ __global__ void __launch_bounds__(pw::kThreads, 1)
       const long long r = t / g.otiles;
       const int pt = static_cast<int>(r % g.ptiles);
       const int n = static_cast<int>(r / g.ptiles);
-      const int cpw = g.M - ot * kBN <= kBN / 2 ? kColsMax / 2 : kColsMax;  // channels per warp
-      const int oc0 = ot * kBN + h * cpw;
+      const int cpw = CF::kColsMax >= 32 && g.M - ot * CF::kBN <= CF::kBN / 2 ? CF::kColsMax / 2 : CF::kColsMax;  // channels per warp
+      const int oc0 = ot * CF::kBN + h * cpw;
       const int nvalid = min(cpw, g.M - oc0);  // may be <= 0 for the upper groups of a narrow tile
-      float acc[kColsMax];
+      float acc[CF::kColsMax];
       for (int c = 0; c < nchunks; ++c, ++gc) {
         const int buf = gc & 1;
         bool got = mbar_wait(&pb->acc_full[buf], (gc >> 1) & 1u, &pb->abort_flag, err);
@@ -446,11 +458,11 @@ __global__ void __launch_bounds__(pw::kThreads, 1)
         }
         tc_fence_after();
         const uint32_t base =
-            tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * kBN + h * cpw);
+            tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * CF::kBN + h * cpw);
 #pragma unroll
-        for (int gg = 0; gg < kColsMax / 16; gg += kColsMax > 32 ? 2 : 1) {
+        for (int gg = 0; gg < CF::kColsMax / 16; gg += CF::kColsMax > 32 ? 2 : 1) {
           if (gg * 16 >= cpw) break;
-          const bool two = kColsMax > 32 && (gg + 1) * 16 < cpw;  // 16-column groups in pairs on wide warps
+          const bool two = CF::kColsMax > 32 && (gg + 1) * 16 < cpw;  // 16-column groups in pairs on wide warps
           uint32_t r0[16], r1[16];
           tmem_ld16(base + gg * 16, r0);
           if (two) tmem_ld16(base + (gg + 1) * 16, r1);
@@ -498,7 +510,7 @@ __global__ void __launch_bounds__(pw::kThreads, 1)
         with_act(g.act, [&](auto tag) {
           constexpr int ACT = decltype(tag)::value;
 #pragma unroll
-          for (int j0 = 0; j0 < kColsMax; j0 += 8) {
+          for (int j0 = 0; j0 < CF::kColsMax; j0 += 8) {
             if (j0 >= cpw) break;
             // residuals of 8 channels in flight at once (clamped rows, no branch between the loads)
             float rv[8];
@@ -523,7 +535,7 @@ __global__ void __launch_bounds__(pw::kThreads, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, kTmemCols);
+    tmem_dealloc(tmem, CF::kTmemCols);
   }
 }
 
@@ -687,7 +699,8 @@ static bool pointwise_ok(const osc_conv_weights* w, const float* x, long long x_
          (reinterpret_cast<uintptr_t>(x) & 15u) == 0;
 }
 
-static int conv1x1_tf32x3(osc_ctx* ctx, const float* x, long long x_nstride, int N, int C, int HW,
+template <int BN>
+static int conv1x1_launch(osc_ctx* ctx, const float* x, long long x_nstride, int N, int C, int HW,
                           const osc_conv_weights* w, const float* bias, int act, const float* res,
                           long long res_nstride, float* y, long long y_nstride) {
   PwGeom g{};
@@ -695,7 +708,7 @@ static int conv1x1_tf32x3(osc_ctx* ctx, const float* x, long long x_nstride, int
   g.HW = HW;
   g.M = w->M;
   g.ptiles = (HW + kBM - 1) / kBM;
-  g.otiles = (w->M + pw::kBN - 1) / pw::kBN;
+  g.otiles = (w->M + pw::Cfg<BN>::kBN - 1) / pw::Cfg<BN>::kBN;
   g.tiles = static_cast<long long>(N) * g.ptiles * g.otiles;
   g.num_kb = w->Cp / kBK;
   g.act = act;
@@ -713,19 +726,29 @@ static int conv1x1_tf32x3(osc_ctx* ctx, const float* x, long long x_nstride, int
   {
     const uint64_t dims[2] = {static_cast<uint64_t>(w->Kp), static_cast<uint64_t>(w->M)};
     const uint64_t pitch[1] = {static_cast<uint64_t>(w->Kp) * 4};
-    const uint32_t box[2] = {kBK, pw::kBN};
+    const uint32_t box[2] = {kBK, pw::Cfg<BN>::kBN};
     OSC_TRY(encode_tiled(&mWh, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, w->hi, dims, pitch, box, CU_TENSOR_MAP_SWIZZLE_128B));
     OSC_TRY(encode_tiled(&mWl, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, w->lo, dims, pitch, box, CU_TENSOR_MAP_SWIZZLE_128B));
   }
-  const int smem = pw::kSmemBase + static_cast<int>(round_up(static_cast<size_t>(w->M) * 4, 16));
-  OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(k_conv_px_tf32x3<false>), smem));
+  const int smem = pw::Cfg<BN>::kSmemBase + static_cast<int>(round_up(static_cast<size_t>(w->M) * 4, 16));
+  OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(k_conv_px_tf32x3<false, BN>), smem));
   const long long grid = std::min<long long>(g.tiles, ctx->num_sms);
   prof_begin(ctx);
   const ConvTaps no_taps{};
-  k_conv_px_tf32x3<false><<<static_cast<unsigned>(grid), pw::kThreads, smem, ctx->stream>>>(mX, mX, mWh, mWl, g,
+  k_conv_px_tf32x3<false, BN><<<static_cast<unsigned>(grid), pw::kThreads, smem, ctx->stream>>>(mX, mX, mWh, mWl, g,
                                                                                              no_taps, bias, y,
                                                                                          ctx->d_err);
   return check_launch(ctx, "k_conv_px_tf32x3");
+}
+
+// Layers with at most 64 output channels take the 64-channel tile (4-stage
+// ring), wider ones the 128-channel tile.
+static int conv1x1_tf32x3(osc_ctx* ctx, const float* x, long long x_nstride, int N, int C, int HW,
+                          const osc_conv_weights* w, const float* bias, int act, const float* res,
+                          long long res_nstride, float* y, long long y_nstride) {
+  if (w->M <= 64)
+    return conv1x1_launch<64>(ctx, x, x_nstride, N, C, HW, w, bias, act, res, res_nstride, y, y_nstride);
+  return conv1x1_launch<128>(ctx, x, x_nstride, N, C, HW, w, bias, act, res, res_nstride, y, y_nstride);
 }
 
 // Pixel-major tiles for K x K convs with few output channels on small images
@@ -772,7 +795,7 @@ static int conv_px_taps(osc_ctx* ctx, const float* xh, const float* xl, int N, i
   choose_px_box(OH, OW, &g.BW, &g.BH);
   g.tiles_w = (OW + g.BW - 1) / g.BW;
   g.ptiles = g.tiles_w * ((OH + g.BH - 1) / g.BH);
-  g.otiles = (w->M + pw::kBN - 1) / pw::kBN;
+  g.otiles = (w->M + pw::Cfg<128>::kBN - 1) / pw::Cfg<128>::kBN;
   g.tiles = static_cast<long long>(N) * g.ptiles * g.otiles;
   g.cp_blocks = w->Cp / kBK;
   g.num_kb = taps.n_taps * g.cp_blocks;
@@ -795,15 +818,15 @@ static int conv_px_taps(osc_ctx* ctx, const float* xh, const float* xl, int N, i
   {
     const uint64_t dims[2] = {static_cast<uint64_t>(w->Kp), static_cast<uint64_t>(w->M)};
     const uint64_t pitch[1] = {static_cast<uint64_t>(w->Kp) * 4};
-    const uint32_t box[2] = {kBK, pw::kBN};
+    const uint32_t box[2] = {kBK, pw::Cfg<128>::kBN};
     OSC_TRY(encode_tiled(&mWh, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, w->hi, dims, pitch, box, CU_TENSOR_MAP_SWIZZLE_128B));
     OSC_TRY(encode_tiled(&mWl, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, w->lo, dims, pitch, box, CU_TENSOR_MAP_SWIZZLE_128B));
   }
-  const int smem = pw::kSmemBase + static_cast<int>(round_up(static_cast<size_t>(w->M) * 4, 16));
-  OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(k_conv_px_tf32x3<true>), smem));
+  const int smem = pw::Cfg<128>::kSmemBase + static_cast<int>(round_up(static_cast<size_t>(w->M) * 4, 16));
+  OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(k_conv_px_tf32x3<true, 128>), smem));
   const long long grid = std::min<long long>(g.tiles, ctx->num_sms);
   prof_begin(ctx);
-  k_conv_px_tf32x3<true><<<static_cast<unsigned>(grid), pw::kThreads, smem, ctx->stream>>>(mXh, mXl, mWh, mWl, g,
+  k_conv_px_tf32x3<true, 128><<<static_cast<unsigned>(grid), pw::kThreads, smem, ctx->stream>>>(mXh, mXl, mWh, mWl, g,
                                                                                             taps, bias, y, ctx->d_err);
   return check_launch(ctx, "k_conv_px_tf32x3");
 }

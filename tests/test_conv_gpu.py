@@ -110,6 +110,8 @@ def test_conv_rejects_bad_output_size_and_groups(ctx):
         (1, 512, 20, 20, 256, 0),   # K = 512: 16 k-blocks in 8 TMEM chunks, 2 channel tiles
         (2, 7, 6, 6, 5, 3),         # C = 7, M = 5 (N rounded to 16), Sigmoid
         (1, 16, 5, 5, 16, 1),       # 25-pixel planes: not 16-byte aligned, implicit-GEMM fallback
+        (1, 256, 20, 20, 64, 1),    # 64-channel tile: 8 k-blocks around the 4-stage ring
+        (2, 64, 12, 12, 48, 0),     # 64-channel tile, 48 channels: the last epilogue warp group idle
     ],
 )
 def test_conv_pointwise(ctx, N, C, H, W, M, act):
