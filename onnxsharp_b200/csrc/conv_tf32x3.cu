@@ -394,7 +394,10 @@ __global__ void __launch_bounds__(pw::kThreads, 1)
       }
     }
   } else if (warp < kEpiBase) {
-    // converters: A (fp32 from TMA) -> hi in place, lo beside it (pointwise form only)
+    // converters (pointwise form only): the landed fp32 A stays in place as the
+    // hi operand (a tf32 operand is read as its top 19 bits, i.e. trunc(x)),
+    // and lo = x - trunc(x) (exact) is written beside it: one 16 KB write per
+    // k-block instead of two, on a path bound by shared-memory bandwidth
     const int ct = threadIdx.x - 64;
     int i = 0;
     bool ok = !TAPS;
@@ -413,16 +416,12 @@ __global__ void __launch_bounds__(pw::kThreads, 1)
 #pragma unroll 4
         for (int j = ct; j < kA / 16; j += 32 * kConvWarps) {
           const float4 v = a[j];
-          float4 h, l;
-          h.x = to_tf32(v.x);
-          h.y = to_tf32(v.y);
-          h.z = to_tf32(v.z);
-          h.w = to_tf32(v.w);
-          l.x = __fsub_rn(v.x, h.x);
-          l.y = __fsub_rn(v.y, h.y);
-          l.z = __fsub_rn(v.z, h.z);
-          l.w = __fsub_rn(v.w, h.w);
-          a[j] = h;
+          constexpr uint32_t kTf32Mask = 0xffffe000u;  // sign, exponent, top 10 mantissa bits
+          float4 l;
+          l.x = __fsub_rn(v.x, __uint_as_float(__float_as_uint(v.x) & kTf32Mask));
+          l.y = __fsub_rn(v.y, __uint_as_float(__float_as_uint(v.y) & kTf32Mask));
+          l.z = __fsub_rn(v.z, __uint_as_float(__float_as_uint(v.z) & kTf32Mask));
+          l.w = __fsub_rn(v.w, __uint_as_float(__float_as_uint(v.w) & kTf32Mask));
           al[j] = l;
         }
         fence_async_smem();
