@@ -174,17 +174,20 @@ __global__ void __launch_bounds__(ConvCfg::THREADS, 1)
 // X[px][c] * W[oc][c]^T, whose A operand is the NCHW input itself: for a fixed
 // channel the pixels are contiguous, i.e. A is MN-major. So the input is read
 // straight from NCHW by TMA (no transform pass, 4 bytes per element instead of
-// the transform's 4 + 8 and the conv's 8), split into hi/lo in shared memory
-// by two converter warps, and fed to tcgen05 with the A-MN-major descriptor.
+// the transform's 4 + 8 and the conv's 8); two converter warps write its lo
+// part (x - trunc_tf32(x)) beside it in shared memory, the landed fp32 tile
+// being the hi part (a tf32 operand is read as its top 19 bits), and both
+// feed tcgen05 through the A-MN-major descriptor.
 //  - tile: 128 pixels (TMEM lanes) x up to 128 output channels (columns; the
-//    MMA's N is the tile's channel count rounded to 16);
+//    MMA's N is the tile's channel count rounded to 16), or a 64-channel
+//    tile with a deeper ring for layers of at most 64 output channels;
 //  - stage: A as 4 TMA boxes of 32 pixels x 32 channels (4 KB each; the
 //    128-byte swizzle with 32-byte atoms that MN-major TF32 operands need:
 //    4-channel groups 512 bytes apart, 32-pixel groups 4 KB apart), its lo
 //    part, and the prepacked weight hi/lo boxes (K-major);
 //  - persistent CTAs walk the tiles; TMEM holds two accumulators, so the
 //    epilogue of one tile overlaps the main loop of the next;
-//  - epilogue (8 warps, two per TMEM lane quadrant): lane = pixel, so each
+//  - epilogue (16 warps, four per TMEM lane quadrant): lane = pixel, so each
 //    warp store writes 32 consecutive pixels of one output channel (128
 //    bytes): NCHW without a staging tile. Biases come from a shared-memory
 //    table filled once per CTA.
