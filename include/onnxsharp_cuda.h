@@ -380,6 +380,18 @@ OSC_API int osc_selfcheck_fast_act(osc_ctx* ctx, float* max_sigmoid_err, float* 
  * pointers and the call synchronises the context's stream. */
 OSC_API int osc_selfcheck_recip(osc_ctx* ctx, unsigned long long* mismatches, unsigned int* first_bad);
 
+/* Failure detection (no counterpart in the reference, which has no device
+ * waits): every wait inside this library's kernels gives up after a bounded
+ * time (about 1.5 s at full clock), sets the context's device error word and
+ * lets the kernel return, so a wait that can never complete reports an error
+ * instead of hanging the GPU. This call enqueues a kernel whose wait cannot
+ * complete, without faulting anything: which = 0 is the grid barrier of the
+ * DynamicQuantizeLinear kernel told to expect one CTA more than it launched;
+ * which = 1 an mbarrier no thread arrives on. The next osc_synchronize then
+ * returns OSC_ETIMEDOUT and clears the error word and the barrier counters, and
+ * the context stays usable. */
+OSC_API int osc_selfcheck_timeout(osc_ctx* ctx, int which);
+
 #ifdef __cplusplus
 }
 #endif

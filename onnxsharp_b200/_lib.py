@@ -70,6 +70,7 @@ SIGNATURES: dict[str, tuple] = {
     "osc_launch_count": (C.c_ulonglong, [vp]),
     "osc_selfcheck_recip": (i32, [vp, C.POINTER(C.c_ulonglong), C.POINTER(C.c_uint)]),
     "osc_selfcheck_fast_act": (i32, [vp, C.POINTER(C.c_float), C.POINTER(C.c_float)]),
+    "osc_selfcheck_timeout": (i32, [vp, i32]),
     "osc_dynamic_quantize_linear_f32": (i32, [vp, vp, i64, vp, vp, vp]),
     "osc_letterbox_u8": (i32, [vp, vp, i32, i32, i32, i32, i32, i32, i32, vp, C.POINTER(i32)]),
     "osc_yolo_detect_f32": (i32, [vp, vp, i32, i32, i32, C.c_float, C.c_float, i32, i32, i32, vp, vp, vp]),

@@ -691,11 +691,7 @@ static void choose_box(int OH, int OW, int* BW, int* BH) {
 // transform-free pointwise kernel.
 static bool pointwise_ok(const osc_conv_weights* w, const float* x, long long x_nstride, int H, int W, int sh,
                          int sw, int pt, int pl, int OH, int OW) {
-  static const bool off = [] {
-    const char* v = std::getenv("OSC_CONV_PW");
-    return v != nullptr && v[0] == '0';
-  }();
-  return !off && w->kh == 1 && w->kw == 1 && w->M <= pw::kMaxBias && sh == 1 && sw == 1 && pt == 0 && pl == 0 &&
+  return w->kh == 1 && w->kw == 1 && w->M <= pw::kMaxBias && sh == 1 && sw == 1 && pt == 0 && pl == 0 &&
          OH == H && OW == W &&
          (static_cast<long long>(H) * W) % 4 == 0 && x_nstride % 4 == 0 &&
          (reinterpret_cast<uintptr_t>(x) & 15u) == 0;
@@ -756,15 +752,9 @@ static int conv1x1_tf32x3(osc_ctx* ctx, const float* x, long long x_nstride, int
 // Pixel-major tiles for K x K convs with few output channels on small images
 // (measured on B200, YOLO shapes at B=64: 256->64 and 64->64 3x3 at 20x20
 // 19-24 % faster; at 40x40 and above the channel-major kernel's 256-pixel
-// tiles move fewer operand bytes per output and win). OSC_CONV_PX=0 / 1
-// forces the choice for measurements.
+// tiles move fewer operand bytes per output and win).
 static bool px_taps_ok(int M, int OH, int OW) {
-  static const int mode = [] {
-    const char* v = std::getenv("OSC_CONV_PX");
-    return v == nullptr ? -1 : std::atoi(v);
-  }();
-  if (mode == 0) return false;
-  return mode == 1 ? M <= 4096 : (M <= 64 && static_cast<long>(OH) * OW <= 576);
+  return M <= 64 && static_cast<long>(OH) * OW <= 576;
 }
 
 // The pixel box of the pixel-major conv: BW x BH <= 128 pixels, the shape

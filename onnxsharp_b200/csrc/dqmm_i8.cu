@@ -234,7 +234,7 @@ __device__ __forceinline__ QParams dql_params_from(float mn, float mx) {
 }
 
 __global__ void __launch_bounds__(kDqlThreads, 1)
-    k_dql_fused(const float* __restrict__ a, int m, int k, int lda, int kp, int rows_per_cta,
+    k_dql_fused(const float* __restrict__ a, int m, int k, int lda, int kp, int rows_per_cta, int extra_arrivals,
                 const float* __restrict__ override_mm, float2* __restrict__ part, unsigned* __restrict__ sync,
                 QParams* __restrict__ qp_out, float* __restrict__ params_out, uint8_t* __restrict__ q,
                 int32_t* __restrict__ rowsum, int32_t* __restrict__ nanrow, int* __restrict__ err) {
@@ -318,7 +318,8 @@ __global__ void __launch_bounds__(kDqlThreads, 1)
         // grid barrier: bounded spin until every CTA has published its range
         const long long c0 = clock64();
         int ok = 1;
-        while (*reinterpret_cast<volatile unsigned*>(&sync[0]) < static_cast<unsigned>(G)) {
+        const unsigned want = static_cast<unsigned>(G + extra_arrivals);
+        while (*reinterpret_cast<volatile unsigned*>(&sync[0]) < want) {
           if (clock64() - c0 > kWaitLimitCycles) {
             ok = 0;
             atomicExch(err, DEV_ERR_TIMEOUT);
@@ -361,7 +362,16 @@ __global__ void __launch_bounds__(kDqlThreads, 1)
     sp = dql_params_from(fminf(0.0f, override_mm[0]), fmaxf(0.0f, override_mm[1]));
   }
   __syncthreads();
-  if (!s_ok) return;
+  if (!s_ok) {
+    // gave up at the barrier (error word set): still count the departure so
+    // the last CTA out leaves the counters at zero for the next launch
+    if (override_mm == nullptr && tid == 0 && atomicAdd(&sync[1], 1u) == static_cast<unsigned>(G) - 1u) {
+      sync[0] = 0u;
+      sync[1] = 0u;
+      __threadfence();
+    }
+    return;
+  }
   const QParams p = sp;
   if (blockIdx.x == 0 && tid == 0) {
     *qp_out = p;
@@ -1100,11 +1110,7 @@ static int int8_gemm(osc_ctx* ctx, const uint8_t* q, size_t q_pitch, int q_cols,
     OSC_TRY(encode_tiled(&mW, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, w->wt, dims, pitch, box, CU_TENSOR_MAP_SWIZZLE_128B));
   }
   const uint32_t b_fmt = w->is_signed ? 1u : 0u;
-  static const bool force_tiles = [] {
-    const char* e = std::getenv("OSC_DQMM_PERSISTENT");
-    return e != nullptr && e[0] == '0';
-  }();
-  if (!force_tiles && w->n % 4 == 0 && (reinterpret_cast<uintptr_t>(y) & 15u) == 0) {
+  if (w->n % 4 == 0 && (reinterpret_cast<uintptr_t>(y) & 15u) == 0) {
     // persistent transposed tiles with TMA stores (row pitch N*4 bytes is a multiple of 16)
     CUtensorMap mQp, mY;
     {
@@ -1130,11 +1136,7 @@ static int int8_gemm(osc_ctx* ctx, const uint8_t* q, size_t q_pitch, int q_cols,
     const uint32_t idesc_p = (2u << 4) | (b_fmt << 7) | (q_fmt << 10) | (static_cast<uint32_t>(kPBN >> 3) << 17) |
                              (static_cast<uint32_t>(kQBM >> 4) << 24);
     const int mt = (m + kPBN - 1) / kPBN, nt = (w->n + kQBM - 1) / kQBM;
-    static const bool qres_off = [] {
-      const char* e = std::getenv("OSC_DQMM_QRES");
-      return e != nullptr && e[0] == '0';
-    }();
-    if (args.num_kb <= kRMaxKb && !qres_off) {
+    if (args.num_kb <= kRMaxKb) {
       // q-resident: cpm CTAs share each 128-row block, each walking every cpm-th column block
       args.cpm = std::max(1, std::min(nt, ctx->num_sms / std::max(1, mt)));
       OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(k_dqmm_i8_persistent<true>), kRSmem));
@@ -1277,11 +1279,7 @@ OSC_API int osc_dqmm_f32(osc_ctx* ctx, const float* a, int m, int k, int lda, co
   const int dql_ctas = std::min(m, ctx->num_sms);
   const int rows_per_cta = (m + dql_ctas - 1) / dql_ctas;
   const size_t dql_smem = static_cast<size_t>(rows_per_cta) * (static_cast<size_t>(k) * sizeof(float) + 8);
-  static const bool split_dql = [] {
-    const char* e = std::getenv("OSC_DQL_FUSED");
-    return e != nullptr && e[0] == '0';
-  }();
-  if (!split_dql && dql_smem <= 200 * 1024) {
+  if (dql_smem <= 200 * 1024) {
     // one cooperative launch: range, grid barrier, quantisation
     OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(k_dql_fused), static_cast<int>(dql_smem)));
     cudaLaunchConfig_t cfg = {};
@@ -1296,7 +1294,7 @@ OSC_API int osc_dqmm_f32(osc_ctx* ctx, const float* a, int m, int k, int lda, co
     cfg.numAttrs = 1;
     unsigned* sync = reinterpret_cast<unsigned*>(ctx->d_err) + 4;
     prof_begin(ctx);
-    const cudaError_t le = cudaLaunchKernelEx(&cfg, k_dql_fused, a, m, k, lda, kp, rows_per_cta, minmax_override,
+    const cudaError_t le = cudaLaunchKernelEx(&cfg, k_dql_fused, a, m, k, lda, kp, rows_per_cta, 0, minmax_override,
                                               reinterpret_cast<float2*>(base), sync, qp, params_out, q, rowsum,
                                               nanrow, ctx->d_err);
     if (le != cudaSuccess) return cuda_fail(le, "k_dql_fused launch");
@@ -1414,6 +1412,68 @@ OSC_API int osc_matmul_integer_i8(osc_ctx* ctx, const void* a, int a_signed, int
   args.has_wzp = w->has_zp;
   args.int_out = 1;
   return int8_gemm(ctx, q, q_pitch, k, a_signed, m, w, args);
+}
+
+
+// ---- failure detection: bounded device waits that run out.
+// A kernel stuck behind a wait that can never complete (a CTA that never
+// arrives, a copy that never lands) must end with an error the host can read
+// instead of hanging the GPU. These probes make a wait run out on purpose,
+// without faulting anything: the host then sees OSC_ETIMEDOUT from
+// osc_synchronize, which also clears the error word and barrier counters.
+__global__ void k_mbar_starved(int* err) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    mbar_init(&bar, 1);  // one arrival expected; none is ever made
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) mbar_wait(&bar, 0, &abort_flag, err);
+}
+
+OSC_API int osc_selfcheck_timeout(osc_ctx* ctx, int which) {
+  OSC_TRY(enter(ctx));
+  if (which == 1) {
+    prof_begin(ctx);
+    k_mbar_starved<<<1, 32, 0, ctx->stream>>>(ctx->d_err);
+    return check_launch(ctx, "k_mbar_starved");
+  }
+  if (which != 0) return fail(OSC_EINVAL, "osc_selfcheck_timeout: which=%d (0: grid barrier, 1: mbarrier)", which);
+  // The DynamicQuantizeLinear kernel's grid barrier told to expect one CTA
+  // more than the grid has: every CTA gives up after the wait limit.
+  const int m = ctx->num_sms, k = 128, kp = 128;
+  const size_t a_bytes = round_up(static_cast<size_t>(m) * k * sizeof(float), 256);
+  const size_t off_part = a_bytes, off_params = off_part + 8192, off_q = off_params + 256;
+  const size_t off_rs = off_q + round_up(static_cast<size_t>(m) * kp, 256);
+  const size_t off_nan = off_rs + round_up(sizeof(int32_t) * m, 256);
+  const size_t total = off_nan + round_up(sizeof(int32_t) * m, 256);
+  void* buf = nullptr;
+  OSC_TRY(scratch(ctx, total, &buf));
+  uint8_t* base = static_cast<uint8_t*>(buf);
+  OSC_CUDA(cudaMemsetAsync(base, 0, a_bytes, ctx->stream), "zero probe input");
+  const size_t smem = static_cast<size_t>(k) * sizeof(float) + 8;
+  OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(k_dql_fused), static_cast<int>(smem)));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(m));
+  cfg.blockDim = dim3(kDqlThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = ctx->stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  unsigned* sync = reinterpret_cast<unsigned*>(ctx->d_err) + 4;
+  prof_begin(ctx);
+  const cudaError_t le = cudaLaunchKernelEx(
+      &cfg, k_dql_fused, reinterpret_cast<const float*>(base), m, k, k, kp, 1, 1, static_cast<const float*>(nullptr),
+      reinterpret_cast<float2*>(base + off_part), sync, reinterpret_cast<QParams*>(base + off_params),
+      static_cast<float*>(nullptr), base + off_q, reinterpret_cast<int32_t*>(base + off_rs),
+      reinterpret_cast<int32_t*>(base + off_nan), ctx->d_err);
+  if (le != cudaSuccess) return cuda_fail(le, "k_dql_fused launch (timeout probe)");
+  return check_launch(ctx, "k_dql_fused");
 }
 
 }  // extern "C"

@@ -530,6 +530,24 @@ static int gemm_batched(osc_ctx* ctx, const float* ahi, const float* alo, int ba
                         const float* bhi, const float* blo, int b_batches, int N, const float* col_bias, int act,
                         const EpiAffine& ep, float* y);
 
+// Routes an A already split into K-major hi/lo parts [m][kp] to the GEMM
+// kernel for its shape. Allocates nothing.
+int gemm_presplit(osc_ctx* ctx, const float* ahi, const float* alo, int m, int kp, const osc_gemm_weights* w,
+                  const float* col_bias, int act, float* c, int ldc) {
+  if (!c_tma_ok(c, w->n, ldc)) {  // C not 16-byte aligned: the batched kernel's plain-store epilogue
+    const EpiAffine ep{1.0f, 0.0f, nullptr, 0, 0, 0, 1, ldc, 0, nullptr};
+    return gemm_batched(ctx, ahi, alo, 1, m, kp, w->hi, w->lo, 1, w->n, col_bias, act, ep, c);
+  }
+  // Prefer the wider tile (less operand traffic per FLOP) unless it leaves
+  // most SMs idle; wide tiles of more than one row block run on CTA pairs.
+  const long tiles256 = static_cast<long>((w->n + 255) / 256) * ((m + kBM - 1) / kBM);
+  const bool wide = w->n > 128 && tiles256 >= ctx->num_sms * 3 / 4;
+  if (wide && m > kBM)
+    return launch_gemm_pair<Tf32x3PairCfg<256, 3, 2>>(ctx, ahi, alo, m, kp, w, col_bias, act, c, ldc);
+  if (wide) return launch_gemm<Tf32x3Cfg<256, 2, 2>>(ctx, ahi, alo, m, kp, w, col_bias, act, c, ldc);
+  return launch_gemm<Tf32x3Cfg<128, 3, 2>>(ctx, ahi, alo, m, kp, w, col_bias, act, c, ldc);
+}
+
 int gemm_tf32x3(osc_ctx* ctx, const float* a, int m, int k, int lda, const osc_gemm_weights* w,
                 const float* col_bias, int act, float* c, int ldc) {
   const int kp = w->kp;
@@ -539,29 +557,7 @@ int gemm_tf32x3(osc_ctx* ctx, const float* a, int m, int k, int lda, const osc_g
   float* ahi = static_cast<float*>(buf);
   float* alo = reinterpret_cast<float*>(static_cast<uint8_t*>(buf) + half);
   OSC_TRY(split_tf32(ctx, a, m, k, lda, kp, ahi, alo));
-  if (!c_tma_ok(c, w->n, ldc)) {  // C not 16-byte aligned: the batched kernel's plain-store epilogue
-    const EpiAffine ep{1.0f, 0.0f, nullptr, 0, 0, 0, 1, ldc, 0, nullptr};
-    return gemm_batched(ctx, ahi, alo, 1, m, kp, w->hi, w->lo, 1, w->n, col_bias, act, ep, c);
-  }
-  static const int bn_env = [] {
-    const char* v = std::getenv("OSC_GEMM_BN");
-    return v ? std::atoi(v) : 0;
-  }();
-  int bn = bn_env;
-  if (bn != 128 && bn != 256) {
-    // Prefer the wider tile (less operand traffic per FLOP) unless it leaves
-    // most SMs idle.
-    const long tiles256 = static_cast<long>((w->n + 255) / 256) * ((m + kBM - 1) / kBM);
-    bn = (tiles256 >= ctx->num_sms * 3 / 4 || w->n <= 128) ? (w->n <= 128 ? 128 : 256) : 128;
-  }
-  static const bool pair_off = [] {
-    const char* v = std::getenv("OSC_GEMM_PAIR");
-    return v != nullptr && v[0] == '0';
-  }();
-  if (bn == 256 && !pair_off && m > kBM)
-    return launch_gemm_pair<Tf32x3PairCfg<256, 3, 2>>(ctx, ahi, alo, m, kp, w, col_bias, act, c, ldc);
-  if (bn == 256) return launch_gemm<Tf32x3Cfg<256, 2, 2>>(ctx, ahi, alo, m, kp, w, col_bias, act, c, ldc);
-  return launch_gemm<Tf32x3Cfg<128, 3, 2>>(ctx, ahi, alo, m, kp, w, col_bias, act, c, ldc);
+  return gemm_presplit(ctx, ahi, alo, m, kp, w, col_bias, act, c, ldc);
 }
 
 // A strided view [batches][rows][cols] -> hi/lo [batches][rows][kp] in `dst_hi/lo`.
@@ -1061,32 +1057,6 @@ int noalloc_scratch(int device, float** out) {
   return OSC_OK;
 }
 
-// Same kernels and launch shapes as gemm_tf32x3(), minus the scratch arena and
-// the profiling events.
-template <class Cfg>
-int launch_gemm_noalloc(osc_ctx* ctx, const float* ahi, const float* alo, int M, int Kp, const osc_gemm_weights* w,
-                        const float* bias, int act, float* C, int ldc) {
-  CUtensorMap mAh, mAl, mBh, mBl;
-  const uint64_t dimsA[2] = {static_cast<uint64_t>(Kp), static_cast<uint64_t>(M)};
-  const uint64_t dimsB[2] = {static_cast<uint64_t>(Kp), static_cast<uint64_t>(w->n)};
-  const uint64_t pitch[1] = {static_cast<uint64_t>(Kp) * 4};
-  const uint32_t boxA[2] = {kBK, kBM};
-  const uint32_t boxB[2] = {kBK, static_cast<uint32_t>(Cfg::BN)};
-  OSC_TRY(encode_tiled(&mAh, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, ahi, dimsA, pitch, boxA, CU_TENSOR_MAP_SWIZZLE_128B));
-  OSC_TRY(encode_tiled(&mAl, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, alo, dimsA, pitch, boxA, CU_TENSOR_MAP_SWIZZLE_128B));
-  OSC_TRY(encode_tiled(&mBh, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, w->hi, dimsB, pitch, boxB, CU_TENSOR_MAP_SWIZZLE_128B));
-  OSC_TRY(encode_tiled(&mBl, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, w->lo, dimsB, pitch, boxB, CU_TENSOR_MAP_SWIZZLE_128B));
-  CUtensorMap mC{};
-  OSC_TRY(store_map(&mC, C, M, w->n, ldc));
-  auto kern = gemm_kernel<Cfg>(act);
-  OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(kern), Cfg::SMEM_BYTES));
-  dim3 grid((w->n + Cfg::BN - 1) / Cfg::BN, (M + kBM - 1) / kBM);
-  kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, ctx->stream>>>(mAh, mAl, mBh, mBl, M, w->n, Kp, bias, mC, ctx->d_err);
-  const cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "k_gemm_tf32x3 (no-alloc)");
-  return OSC_OK;
-}
-
 }  // namespace
 }  // namespace osc
 
@@ -1113,26 +1083,13 @@ OSC_API int osc_gemm_bias_f32_noalloc(osc_ctx* ctx, const float* a, int m, int k
   if (a == nullptr || c == nullptr) return fail(OSC_EINVAL, "osc_gemm_bias_f32_noalloc: null pointer");
   float* base = nullptr;
   OSC_TRY(noalloc_scratch(ctx->device, &base));
+  if (fault_injected("launch")) return fail(OSC_EFAULT_INJECTED, "injected failure (launch)");
   float* ahi = base;
   float* alo = base + kNoAllocMaxElems;
-  const int kp = w->kp;
-  {
-    const size_t work = static_cast<size_t>(m) * (kp / 4);
-    size_t blocks = (work + 255) / 256;
-    const size_t cap = static_cast<size_t>(ctx->num_sms) * 8;
-    if (blocks > cap) blocks = cap;
-    k_split_rows<<<static_cast<int>(blocks < 1 ? 1 : blocks), 256, 0, ctx->stream>>>(a, m, k, lda, kp, ahi, alo);
-    const cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return cuda_fail(e, "k_split_rows (no-alloc)");
-  }
-  const long tiles256 = static_cast<long>((w->n + 255) / 256) * ((m + kBM - 1) / kBM);
-  const bool wide = w->n > 128 && tiles256 >= ctx->num_sms * 3 / 4;
-  if (!c_tma_ok(c, w->n, ldc)) {  // C not 16-byte aligned: the batched kernel's plain-store epilogue
-    const EpiAffine ep{1.0f, 0.0f, nullptr, 0, 0, 0, 1, ldc, 0, nullptr};
-    return gemm_batched(ctx, ahi, alo, 1, m, kp, w->hi, w->lo, 1, w->n, col_bias, act, ep, c);
-  }
-  if (wide) return launch_gemm_noalloc<Tf32x3Cfg<256, 2, 2>>(ctx, ahi, alo, m, kp, w, col_bias, act, c, ldc);
-  return launch_gemm_noalloc<Tf32x3Cfg<128, 3, 2>>(ctx, ahi, alo, m, kp, w, col_bias, act, c, ldc);
+  // the same split kernel and GEMM routing as osc_gemm_bias_f32, with A's
+  // hi/lo parts in the fixed array instead of the scratch arena
+  OSC_TRY(split_tf32(ctx, a, m, k, lda, w->kp, ahi, alo));
+  return gemm_presplit(ctx, ahi, alo, m, w->kp, w, col_bias, act, c, ldc);
 }
 
 OSC_API int osc_matmul_batched_f32(osc_ctx* ctx, int outer, int inner, int m, int k, int n, const float* a,

@@ -7,8 +7,13 @@
    them (GEMM+bias, DQMM, conv+SiLU, attention, DFL, LayerNorm). GPU tests
    compare the CUDA path against these fixed vectors as well as against a
    fresh oracle run, so a change in the oracle itself is caught.
+3. ``yolo11n.shapes.tsv`` — the reference's own shape table of the exported
+   YOLO11n graph (tests/data/yolo11n.shapes.tsv in the reference checkout,
+   copied unchanged: node index, NODE/TENSOR, op type, name, batch flag,
+   shape). The YOLO plan is checked against it node by node
+   (tests/test_yolo_graph.py). Copied only when ``--reference DIR`` is given.
 
-Run from the repo root: ``python tests/golden/make_golden.py``.
+Run from the repo root: ``python tests/golden/make_golden.py [--reference DIR]``.
 """
 from __future__ import annotations
 
@@ -118,6 +123,11 @@ def main() -> None:
     (HERE / "kat.json").write_text(json.dumps(KAT, indent=1) + "\n")
     np.savez_compressed(HERE / "oracle_small.npz", **small_fixtures())
     print("wrote", HERE / "kat.json", HERE / "oracle_small.npz")
+    if "--reference" in sys.argv:
+        ref = Path(sys.argv[sys.argv.index("--reference") + 1])
+        tsv = (ref / "tests" / "data" / "yolo11n.shapes.tsv").read_bytes()
+        (HERE / "yolo11n.shapes.tsv").write_bytes(tsv)
+        print("wrote", HERE / "yolo11n.shapes.tsv")
 
 
 if __name__ == "__main__":

@@ -64,3 +64,140 @@ def test_yolo_arena_never_overlaps_live_buffers():
         live = not (max(last[a], first[a]) < first[b] or max(last[b], first[b]) < first[a])
         overlap = offs[i] < offs[j] + sizes[b] and offs[j] < offs[i] + sizes[a]
         assert not (live and overlap), (a, b)
+
+
+# ---------------------------------------------------------------- node-by-node shape check
+TSV = __import__("conftest").GOLDEN / "yolo11n.shapes.tsv"
+
+
+def _tsv_tensors():
+    """(node index, op type, tensor name, shape without the batch dim) of every TENSOR row."""
+    rows = []
+    for line in TSV.read_text().splitlines():
+        idx, kind, op, name, _batch, shape = line.split("\t")
+        if kind == "TENSOR":
+            dims = tuple(int(v) for v in shape.split(","))
+            assert dims[0] == 1, line  # the table is recorded at batch 1
+            rows.append((int(idx), op, name.lstrip("/"), dims[1:]))
+    return rows
+
+
+def _ir_shape(g, name, op):
+    """The shape our IR gives the exported tensor `name` (per image), or raises KeyError.
+
+    Convs keep their names: the exported module path minus the trailing
+    conv/Conv and minus every segment the next one extends ("m" before "m.0",
+    "ffn" before "ffn.0", "cv3.0" before "cv3.0.0"); activations, residual Adds, Splits and Concats
+    are fused into convs or are channel slices of buffers, so their shapes are
+    those of the conv output / slice / buffer that stands for them; the C2PSA
+    attention and Detect-tail internals follow from the psa / decode nodes'
+    attributes."""
+    convs = {n.name: n for n in g.nodes if n.op == "conv"}
+    psa = next(n for n in g.nodes if n.op == "psa")
+    dec = next(n for n in g.nodes if n.op == "decode")
+    A = sum((640 // s) ** 2 for s in g.strides)
+    nc = dec.attrs["nc"]
+    heads, kd, hd = psa.attrs["heads"], psa.attrs["kd"], psa.attrs["hd"]
+    ph, pw = g.hw(psa.ins[0])
+    T = ph * pw
+
+    def out(n):
+        r = n.outs[0]
+        return (r.c,) + g.hw(r)
+
+    def conv_shape(path):
+        seg = path.split("/")
+        if seg[-1] == "conv":
+            seg = seg[:-1]
+        key = ".".join(s for s, nxt in zip(seg, seg[1:] + [""]) if not nxt.startswith(s + "."))
+        if key in convs:
+            return out(convs[key]), convs[key]
+        parts = [convs[k] for k in convs if k.startswith(key + ".")]  # per-head slices of one conv
+        if not parts:
+            raise KeyError(name)
+        refs = sorted((p.outs[0] for p in parts), key=lambda r: r.c0)
+        assert all(r.buf == refs[0].buf for r in refs)
+        assert all(a.c0 + a.c == b.c0 for a, b in zip(refs, refs[1:]))
+        return (sum(r.c for r in refs),) + g.hw(refs[0]), parts[0]
+
+    path, leaf = name.rsplit("/", 1) if "/" in name else ("", name)
+    seg = path.split("/") if path else []
+    top = seg[0] if seg else ""
+    scale = {"": 0, "_1": 1, "_2": 2}
+    if name == "output0":
+        return (4 + nc, A)
+    if op == "Conv":
+        if seg[:2] == ["model.23", "dfl"]:
+            return (1, 4, A)
+        return conv_shape(path)[0]
+    if op in ("Sigmoid", "Mul") and seg and seg[-1] == "act":
+        return conv_shape("/".join(seg[:-1]))[0]
+    if top == "model.23":
+        if seg[1:] == ["dfl"]:
+            return {"Reshape_output_0": (4, 16, A), "Transpose_output_0": (16, 4, A), "Softmax_output_0": (16, 4, A),
+                    "Reshape_1_output_0": (4, A)}[leaf]
+        stem = leaf[: leaf.index("_output")]
+        if op in ("Concat", "Reshape") and stem.split("_")[0] in ("Concat", "Reshape") and stem[len(op):] in scale:
+            s = g.strides[scale[stem[len(op):]]]
+            hw = (640 // s, 640 // s)
+            return (64 + nc,) + (hw if op == "Concat" else (hw[0] * hw[1],))
+        return {"Concat_3": (64 + nc, A), "Concat_4": (4, A), "Mul_2": (4, A), "Sigmoid": (nc, A),
+                "Slice": (2, A), "Slice_1": (2, A), "Sub": (2, A), "Sub_1": (2, A), "Add_1": (2, A), "Add_2": (2, A),
+                "Div_1": (2, A)}.get(stem) or {"Split_output_0": (64, A), "Split_output_1": (nc, A)}[leaf]
+    if seg[-2:] == ["m.0", "attn"] and top == "model.10":
+        stem = leaf[: leaf.index("_output")]
+        return {"Reshape": (heads, 2 * kd + hd, T), "Transpose": (heads, T, kd), "MatMul": (heads, T, T),
+                "Mul": (heads, T, T), "Softmax": (heads, T, T), "Transpose_1": (heads, T, T),
+                "MatMul_1": (heads, hd, T), "Reshape_1": (heads * hd, ph, pw), "Reshape_2": (heads * hd, ph, pw),
+                "Add": out(psa)}.get(stem) or {"Split_output_0": (heads, kd, T), "Split_output_1": (heads, kd, T),
+                                              "Split_output_2": (heads, hd, T)}[leaf]
+    if op == "Split" and len(seg) == 1:
+        c, h, w = out(convs[top + ".cv1"])
+        return (c // 2, h, w)
+    if op == "Add":
+        if top == "model.10" and leaf.startswith("Add_output"):             # attn.proj + x
+            shape, node = conv_shape("model.10/m/m.0/attn/proj")
+        elif top == "model.10" and leaf.startswith("Add_1"):                # ffn + x
+            shape, node = conv_shape("model.10/m/m.0/ffn/ffn.1")
+        elif leaf.startswith("Add_output") and seg[-1].startswith("m."):   # bottleneck shortcut
+            shape, node = conv_shape(path + "/cv2")
+        else:
+            raise KeyError(name)
+        assert node.attrs["residual"], f"{name}: the Add is not fused into {node.name}"
+        return shape
+    if op == "Concat":
+        if len(seg) == 1 and top.split(".")[1] in ("12", "15", "18", "21"):  # neck Concat modules
+            return g.buffers["cat" + top.split(".")[1]]
+        return g.buffers[".".join(s for s in seg if s != "m") + ".cat"]
+    if op == "MaxPool":
+        suffix = {"m": 0, "m_1": 1, "m_2": 2}[seg[-1]]
+        return out(next(n for n in g.nodes if n.name == f"{top}.m{suffix}"))
+    if op == "Resize":
+        return out(next(n for n in g.nodes if n.name == top))
+    raise KeyError(name)
+
+
+def test_graph_matches_reference_shape_table_node_by_node():
+    """Every tensor of the reference's tests/data/yolo11n.shapes.tsv (the exported
+    YOLO11n at batch 1) has the same shape in the plan's IR, and every conv of
+    the IR stands for an exported Conv."""
+    g = yolo.build_yolo11n()
+    rows = _tsv_tensors()
+    assert len(rows) == 332
+    bad, seen_convs = [], set()
+    for idx, op, name, shape in rows:
+        try:
+            got = tuple(_ir_shape(g, name, op))
+        except KeyError:
+            bad.append((idx, name, "unmapped"))
+            continue
+        if got != shape:
+            bad.append((idx, name, f"IR {got} != table {shape}"))
+        if op == "Conv":
+            seen_convs.add(name)
+    assert not bad, bad[:10]
+    assert len(seen_convs) == 88
+    ir_convs = [n.name for n in g.nodes if n.op == "conv"]
+    # the exported graph's 88 Convs = our 87 conv names (the 128-channel PSA
+    # position encoding runs as 2 per-head depthwise convs) + the DFL 1x1 (in decode)
+    assert len(ir_convs) == 88 and sum(1 for n in ir_convs if ".attn.pe." in n) == 2
