@@ -3,20 +3,27 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
 
-One process per GPU (torchrun for N > 1, NCCL process group for the barrier
-and the max-over-ranks reduction). Each rank runs the same workload on its own
-seeded synthetic data (weak scaling: images / rows are independent, so the
-path shards with no data-path collective). Rank 0 prints ONE JSON line.
+One process per GPU (torchrun for N > 1, NCCL process group). The headline
+workload (default: the YOLO11n-shaped detector at a global batch of 64,
+BASELINE config 5) is sharded by image over the N GPUs and the shards'
+[B/N, 84, 8400] outputs are all-gathered over NVLink inside every timed step
+(strong scaling: the global batch is the same at every N). Every other
+BASELINE config (GEMM, conv B=1 / B=16, DQMM, the attention block, YOLO B=1 /
+B=8) is measured in the same process and reported under "configs", sharded the
+same way (rows, images or sequences; DQMM adds an NCCL all-reduce of the
+per-tensor range; a batch smaller than N runs as replicas).
 
 Timed region: W untimed warm-up steps, then exactly K steps bracketed by a
 barrier + cuda synchronize on both sides. Every step is timed with CUDA events
-on the stream the kernels run on; L2 is flushed (a 512 MiB device write)
-between steps, outside the events. `value` is the whole-job throughput with
-inputs resident in HBM; `e2e` is the same metric through the public API with
-pinned host buffers (H2D of the step's inputs + D2H of its output inside the
-timed region). `roofline` reports the dominant kernel against the measured
-peaks in MEASURED_PEAKS.json; `cpu_baseline` times the CPU oracle (a
-restatement of the reference's CPU kernels) on a bounded sample.
+on the stream the kernels and collectives run on; L2 is flushed (a 512 MiB
+device write) between steps, outside the events; the max over ranks is
+reported. `value` is the whole-job throughput with inputs resident in HBM;
+`e2e` is the same metric through the library's public API from pinned host
+memory (YOLO: frames in, detections out; the other configs: input tensor in,
+whole output tensor back on rank 0). `roofline` reports the dominant kernel
+against the measured peaks in MEASURED_PEAKS.json; `cpu_baseline` times the
+CPU oracle (a restatement of the reference's CPU kernels) on a bounded sample,
+beside the reference's own published CPU figures.
 
 --impl reference times the reference's CPU algorithm (the oracle port: the
 reference is C# and cannot run here) on the host cores, same metric/config.
@@ -132,106 +139,177 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(rows), "samples_under_load": len(loaded)}
 
 
+
+# ----------------------------------------------------------------- sharding
+class Shard:
+    """This rank's part of a batch-sharded job (one process per GPU).
+
+    Images (YOLO, conv), sequences (attention) and rows (GEMM, DQMM) are
+    independent, so each rank computes a contiguous shard; the shards' outputs
+    are all-gathered over NVLink (NCCL) inside the timed step so that every
+    rank ends the step holding the whole batch's output, as the reference's
+    single Net.Forward returns it (src/OnnxSharp/Core/Net.cs:258-262). A batch
+    smaller than the GPU count (B=1) cannot be split: every rank then runs its
+    own replica and nothing is exchanged ("replicas")."""
+
+    def __init__(self, world: int, rank: int, group=None):
+        self.world, self.rank, self.group = world, rank, group
+
+    def plan(self, n: int) -> tuple[int, int, bool]:
+        """(start, count, replicas) of this rank's part of n items."""
+        from onnxsharp_b200.shard import shard_range
+
+        if self.world == 1 or n % self.world != 0:
+            return 0, n, self.world > 1
+        lo, hi = shard_range(n, self.world, self.rank)
+        return lo, hi - lo, False
+
+    def all_gather(self, full, local) -> None:
+        import torch.distributed as dist
+
+        dist.all_gather_into_tensor(full, local, group=self.group)
+
+    def barrier(self) -> None:
+        import torch.distributed as dist
+
+        if self.world > 1:
+            dist.barrier(group=self.group)
+
+
 # ----------------------------------------------------------------- workloads
 class Workload:
-    """One pass of the hot path over one batch of synthetic input."""
+    """One BASELINE config, sharded over the ranks. A step = compute() (this
+    rank's shard; captured as one CUDA graph where `graphed`) + collect() (the
+    NCCL all-gather of the shards, or nothing on one GPU / for replicas)."""
 
+    key = ""
     name = ""
     unit = "TFLOP/s"
-    main_kernel = ""   # dominant kernel (profile prefix)
     bound = "tensor"
+    main_kernel: tuple = ()
+    graphed = True
+    long_step = False
+    replicas = False
 
-    def units_per_step(self) -> float:       # FLOPs (or images) per step
+    def units_per_step(self) -> float:    # whole job (all ranks) per step
         raise NotImplementedError
 
-    def step(self):                           # device-resident inputs
+    def compute(self):
         raise NotImplementedError
 
-    def e2e_step(self):                       # pinned host in, pinned host out
+    def collect(self):
+        pass
+
+    def collect_bytes(self) -> int:        # bytes each rank receives from the others per step
+        return 0
+
+    def e2e_step(self):
         raise NotImplementedError
 
-    def e2e_bytes(self) -> tuple[int, int]:
+    def e2e_bytes(self) -> tuple[int, int]:  # whole job per step
         raise NotImplementedError
 
-    def main_kernel_units(self) -> float:     # algorithmic FLOPs (or bytes) of one dominant-kernel launch
-        return self.units_per_step()
-
-    def cpu_sample(self, threads: int) -> dict:
+    def main_kernel_units(self) -> float:  # algorithmic FLOPs (or bytes) of one dominant-kernel launch
         raise NotImplementedError
 
+    def cpu_sample(self, threads: int, budget_s: float) -> dict:
+        raise NotImplementedError
 
-def _scale(v: float) -> float:
-    return v / 1e12
+    def close(self):
+        pass
+
+
+def _dev():
+    import torch
+
+    return torch.device("cuda", torch.cuda.current_device())
+
+
+def _tflops(x: float) -> float:
+    return x / 1e12
+
+
+def _timed(fn, budget_s: float, min_reps: int = 1):
+    """Repeat fn until budget_s seconds have passed (at least min_reps times); returns (reps, seconds)."""
+    t0 = time.perf_counter()
+    reps = 0
+    while reps < min_reps or time.perf_counter() - t0 < budget_s:
+        fn()
+        reps += 1
+    return reps, time.perf_counter() - t0
 
 
 class GemmWorkload(Workload):
-    """MatMul+Add(bias) A[2048,512] x B[512,2048] + bias[2048], U(-1,1)."""
+    """Config 1: MatMul+Add(bias) A[2048,512] x B[512,2048] + bias[2048], U(-1,1); rows of A sharded."""
 
-    graphed = True
+    key = "gemm"
     name = "matmul_bias_f32_2048x512x2048"
-    main_kernel = "k_gemm_tf32x3"
+    main_kernel = ("k_gemm_tf32x3",)
 
-    def __init__(self, ctx, rank: int, m=2048, k=512, n=2048):
+    def __init__(self, ctx, sh: Shard, m=2048, k=512, n=2048):
         import torch
 
         from onnxsharp_b200.runtime import GemmWeights
 
-        self.m, self.k, self.n = m, k, n
-        rng = np.random.default_rng(1234 + rank)
+        self.ctx, self.sh, self.m, self.k, self.n = ctx, sh, m, k, n
+        rng = np.random.default_rng(1234)
         self.a_h = rng.uniform(-1, 1, (m, k)).astype(np.float32)
         self.b_h = rng.uniform(-1, 1, (k, n)).astype(np.float32)
         self.bias_h = rng.uniform(-1, 1, n).astype(np.float32)
-        dev = torch.device("cuda", torch.cuda.current_device())
-        self.ctx = ctx
-        self.a = torch.from_numpy(self.a_h).to(dev)
+        lo, cnt, self.replicas = sh.plan(m)
+        self.rows = cnt
+        dev = _dev()
+        self.a = torch.from_numpy(self.a_h[lo:lo + cnt]).to(dev)
         self.bias = torch.from_numpy(self.bias_h).to(dev)
-        self.c = torch.empty((m, n), dtype=torch.float32, device=dev)
         self.w = GemmWeights(ctx, torch.from_numpy(self.b_h).to(dev), k, n)
-        # e2e: pinned host buffers and device staging
-        self.a_pin = torch.from_numpy(self.a_h).pin_memory()
-        self.c_pin = torch.empty((m, n), dtype=torch.float32).pin_memory()
-        self.a_dev2 = torch.empty_like(self.a)
-        self.c_dev2 = torch.empty_like(self.c)
-        self.config = {"workload": self.name, "m": m, "k": k, "n": n, "bias": True,
+        self.c = torch.empty((cnt, n), dtype=torch.float32, device=dev)
+        self.gather = sh.world > 1 and not self.replicas
+        self.c_full = torch.empty((m, n), dtype=torch.float32, device=dev) if self.gather else self.c
+        self.a_pin = torch.from_numpy(self.a_h[lo:lo + cnt].copy()).pin_memory()
+        self.c_pin = torch.empty(self.c_full.shape, dtype=torch.float32).pin_memory()
+        self.a2, self.c2 = torch.empty_like(self.a), torch.empty_like(self.c)
+        self.c2_full = torch.empty_like(self.c_full) if self.gather else self.c2
+        self.config = {"workload": self.name, "m": m, "k": k, "n": n, "rows_per_gpu": cnt, "bias": True,
                        "precision": "3xTF32 (tcgen05 kind::tf32), FP32 in/out"}
 
-    def units_per_step(self) -> float:
-        return 2.0 * self.m * self.k * self.n
+    def units_per_step(self):
+        return 2.0 * self.m * self.k * self.n * (self.sh.world if self.replicas else 1)
 
-    def step(self):
+    def main_kernel_units(self):
+        return 2.0 * self.rows * self.k * self.n
+
+    def compute(self):
         from onnxsharp_b200.runtime import gemm_bias
 
         gemm_bias(self.ctx, self.a, self.w, self.bias, out=self.c)
 
+    def collect(self):
+        if self.gather:
+            self.sh.all_gather(self.c_full, self.c)
+
+    def collect_bytes(self):
+        return (self.sh.world - 1) * self.c.numel() * 4 if self.gather else 0
+
     def e2e_step(self):
         from onnxsharp_b200.runtime import gemm_bias
 
-        self.ctx.memcpy_htod(self.a_dev2, self.a_pin, self.a_pin.numel() * 4)
-        gemm_bias(self.ctx, self.a_dev2, self.w, self.bias, out=self.c_dev2)
-        self.ctx.memcpy_dtoh(self.c_pin, self.c_dev2, self.c_pin.numel() * 4)
+        self.ctx.memcpy_htod(self.a2, self.a_pin, self.a_pin.numel() * 4)
+        gemm_bias(self.ctx, self.a2, self.w, self.bias, out=self.c2)
+        if self.gather:
+            self.sh.all_gather(self.c2_full, self.c2)
+        if self.sh.rank == 0:
+            self.ctx.memcpy_dtoh(self.c_pin, self.c2_full, self.c_pin.numel() * 4)
 
     def e2e_bytes(self):
-        return self.m * self.k * 4, self.m * self.n * 4
+        r = self.sh.world if self.replicas else 1
+        return self.m * self.k * 4 * r, self.m * self.n * 4
 
-    def cpu_sample(self, threads: int) -> dict:
-        import oracle
-
-        rows = self.m
-        t0 = time.perf_counter()
-        reps = 0
-        while True:
-            oracle.gemm(self.a_h[:rows], self.b_h, col_bias=self.bias_h, threads=threads)
-            reps += 1
-            if time.perf_counter() - t0 > 1.5:
-                break
-        dt = time.perf_counter() - t0
-        flops = 2.0 * rows * self.k * self.n * reps
-        return {"value": _scale(flops / dt), "unit": self.unit, "cores": threads,
-                "sample": f"{reps} x full GEMM {rows}x{self.k}x{self.n}+bias ({dt:.2f} s wall)"}
+    def cpu_sample(self, threads, budget_s):
+        return CpuGemm(self.a_h, self.b_h, self.bias_h).cpu_sample(threads, budget_s)
 
 
 def conv_inputs(seed: int, batch: int):
-    """BASELINE config 2 synthetic data: x U(0,1), W He-normal, b N(0, 0.01)."""
+    """Config 2 synthetic data: x U(0,1), W He-normal, b N(0, 0.01)."""
     rng = np.random.default_rng(seed)
     x = rng.uniform(0, 1, (batch, 64, 160, 160)).astype(np.float32)
     w = (rng.normal(0, 1, (128, 64, 3, 3)) * np.sqrt(2.0 / (64 * 9))).astype(np.float32)
@@ -243,36 +321,42 @@ CONV_FLOPS_PER_IMAGE = 2.0 * 128 * 160 * 160 * 64 * 9
 
 
 class ConvWorkload(Workload):
-    """fused Conv+SiLU, x[16,64,160,160] -> y[16,128,160,160], 3x3 s1 p1."""
+    """Config 2: fused Conv+SiLU, x[B,64,160,160] -> y[B,128,160,160], 3x3 s1 p1, B in {1, 16}; images sharded."""
 
-    graphed = True
-    name = "conv3x3_silu_f32_b16_64to128_160x160"
-    main_kernel = "k_conv_tf32x3"
+    main_kernel = ("k_conv_tf32x3",)
 
-    def __init__(self, ctx, rank: int, batch: int = 16):
+    def __init__(self, ctx, sh: Shard, batch: int = 16):
         import torch
 
         from onnxsharp_b200.runtime import ConvWeights
 
-        self.batch = batch
-        x, w, b = conv_inputs(4321 + rank, batch)
+        self.ctx, self.sh, self.batch = ctx, sh, batch
+        self.key = f"conv_b{batch}"
+        self.name = f"conv3x3_silu_f32_b{batch}_64to128_160x160"
+        x, w, b = conv_inputs(4321, batch)
         self.x_h, self.w_h, self.b_h = x, w, b
-        dev = torch.device("cuda", torch.cuda.current_device())
-        self.ctx = ctx
-        self.x = torch.from_numpy(x).to(dev)
+        lo, cnt, self.replicas = sh.plan(batch)
+        self.local = cnt
+        dev = _dev()
+        self.x = torch.from_numpy(x[lo:lo + cnt]).to(dev)
         self.b = torch.from_numpy(b).to(dev)
         self.w = ConvWeights(ctx, torch.from_numpy(w).to(dev), w.shape)
-        self.y = torch.empty((batch, 128, 160, 160), dtype=torch.float32, device=dev)
-        self.x_pin = torch.from_numpy(x).pin_memory()
-        self.y_pin = torch.empty(self.y.shape, dtype=torch.float32).pin_memory()
-        self.x2 = torch.empty_like(self.x)
-        self.y2 = torch.empty_like(self.y)
-        self.config = {"workload": self.name, "batch": batch, "in": [batch, 64, 160, 160], "weight": [128, 64, 3, 3],
-                       "stride": 1, "pad": 1, "act": "SiLU",
+        self.y = torch.empty((cnt, 128, 160, 160), dtype=torch.float32, device=dev)
+        self.gather = sh.world > 1 and not self.replicas
+        self.y_full = torch.empty((batch, 128, 160, 160), dtype=torch.float32, device=dev) if self.gather else self.y
+        self.x_pin = torch.from_numpy(x[lo:lo + cnt].copy()).pin_memory()
+        self.y_pin = torch.empty(self.y_full.shape, dtype=torch.float32).pin_memory()
+        self.x2, self.y2 = torch.empty_like(self.x), torch.empty_like(self.y)
+        self.y2_full = torch.empty_like(self.y_full) if self.gather else self.y2
+        self.config = {"workload": self.name, "batch": batch, "images_per_gpu": cnt, "in": [batch, 64, 160, 160],
+                       "weight": [128, 64, 3, 3], "stride": 1, "pad": 1, "act": "SiLU",
                        "precision": "3xTF32 implicit GEMM (tcgen05 kind::tf32), FP32 in/out"}
 
-    def units_per_step(self) -> float:
-        return CONV_FLOPS_PER_IMAGE * self.batch
+    def units_per_step(self):
+        return CONV_FLOPS_PER_IMAGE * self.batch * (self.sh.world if self.replicas else 1)
+
+    def main_kernel_units(self):
+        return CONV_FLOPS_PER_IMAGE * self.local
 
     def _run(self, x, y):
         from onnxsharp_b200 import ACT_SILU
@@ -280,23 +364,34 @@ class ConvWorkload(Workload):
 
         conv2d(self.ctx, x, self.w, self.b, (1, 1), (1, 1, 1, 1), (1, 1), 1, ACT_SILU, out=y)
 
-    def step(self):
+    def compute(self):
         self._run(self.x, self.y)
+
+    def collect(self):
+        if self.gather:
+            self.sh.all_gather(self.y_full, self.y)
+
+    def collect_bytes(self):
+        return (self.sh.world - 1) * self.y.numel() * 4 if self.gather else 0
 
     def e2e_step(self):
         self.ctx.memcpy_htod(self.x2, self.x_pin, self.x_pin.numel() * 4)
         self._run(self.x2, self.y2)
-        self.ctx.memcpy_dtoh(self.y_pin, self.y2, self.y_pin.numel() * 4)
+        if self.gather:
+            self.sh.all_gather(self.y2_full, self.y2)
+        if self.sh.rank == 0:
+            self.ctx.memcpy_dtoh(self.y_pin, self.y2_full, self.y_pin.numel() * 4)
 
     def e2e_bytes(self):
-        return self.x_pin.numel() * 4, self.y_pin.numel() * 4
+        r = self.sh.world if self.replicas else 1
+        return self.x_h.nbytes * r, self.y_pin.numel() * 4
 
-    def cpu_sample(self, threads: int) -> dict:
-        return CpuConv(self.x_h[:1], self.w_h, self.b_h).cpu_sample(threads)
+    def cpu_sample(self, threads, budget_s):
+        return CpuConv(self.x_h, self.w_h, self.b_h, self.batch).cpu_sample(threads, budget_s)
 
 
 def dqmm_inputs(seed: int, m=4096, k=512, n=2048):
-    """A N(0,1), W int8 U[-127,127], w_scale U(0.001,0.02), bias N(0, 0.01)."""
+    """Config 3: A N(0,1), W int8 U[-127,127], w_scale U(0.001,0.02), bias N(0, 0.01)."""
     rng = np.random.default_rng(seed)
     a = rng.normal(0, 1, (m, k)).astype(np.float32)
     w = rng.integers(-127, 128, (k, n)).astype(np.int8)
@@ -306,104 +401,228 @@ def dqmm_inputs(seed: int, m=4096, k=512, n=2048):
 
 
 class DqmmWorkload(Workload):
-    """DynamicQuantizeMatMul A[4096,512] f32 x W int8 [512,2048] -> Y[4096,2048] f32."""
+    """Config 3: DynamicQuantizeMatMul A[4096,512] f32 x W int8 [512,2048] -> Y[4096,2048] f32.
 
-    graphed = True
+    Rows are sharded; the per-tensor range is the one real exchange step: each
+    rank reduces its rows' {min, max}, the ranks all-reduce it (NCCL, 2 floats)
+    and every shard quantises with the global range, so q and the int32
+    accumulators are those of the unsharded tensor."""
+
+    key = "dqmm"
     name = "dqmm_u8s8_4096x512x2048"
     unit = "TOP/s"
-    main_kernel = "k_dqmm_i8"
+    main_kernel = ("k_dqmm_i8",)
     bound = "hbm"
 
-    def __init__(self, ctx, rank: int, m=4096, k=512, n=2048):
+    def __init__(self, ctx, sh: Shard, m=4096, k=512, n=2048):
         import torch
 
         from onnxsharp_b200.runtime import DqmmWeights
 
-        self.m, self.k, self.n = m, k, n
-        a, w, ws, b = dqmm_inputs(777 + rank, m, k, n)
+        self.ctx, self.sh, self.m, self.k, self.n = ctx, sh, m, k, n
+        a, w, ws, b = dqmm_inputs(777, m, k, n)
         self.a_h, self.w_h, self.ws_h, self.b_h = a, w, ws, b
-        dev = torch.device("cuda", torch.cuda.current_device())
-        self.ctx = ctx
-        self.a = torch.from_numpy(a).to(dev)
+        lo, cnt, self.replicas = sh.plan(m)
+        self.rows = cnt
+        dev = _dev()
+        self.a = torch.from_numpy(a[lo:lo + cnt]).to(dev)
         self.ws = torch.from_numpy(ws).to(dev)
         self.b = torch.from_numpy(b).to(dev)
         self.w = DqmmWeights(ctx, torch.from_numpy(w).to(dev), k, n, None)
-        self.y = torch.empty((m, n), dtype=torch.float32, device=dev)
-        self.a_pin = torch.from_numpy(a).pin_memory()
-        self.y_pin = torch.empty((m, n), dtype=torch.float32).pin_memory()
-        self.a2 = torch.empty_like(self.a)
-        self.y2 = torch.empty_like(self.y)
-        self.config = {"workload": self.name, "m": m, "k": k, "n": n,
+        self.y = torch.empty((cnt, n), dtype=torch.float32, device=dev)
+        self.sharded = sh.world > 1 and not self.replicas
+        self.graphed = not self.sharded  # the range all-reduce sits between two library calls
+        self.mm = torch.zeros(2, dtype=torch.float32, device=dev)
+        self.y_full = torch.empty((m, n), dtype=torch.float32, device=dev) if self.sharded else self.y
+        self.a_pin = torch.from_numpy(a[lo:lo + cnt].copy()).pin_memory()
+        self.y_pin = torch.empty(self.y_full.shape, dtype=torch.float32).pin_memory()
+        self.a2, self.y2 = torch.empty_like(self.a), torch.empty_like(self.y)
+        self.y2_full = torch.empty_like(self.y_full) if self.sharded else self.y2
+        self.config = {"workload": self.name, "m": m, "k": k, "n": n, "rows_per_gpu": cnt,
                        "precision": "dynamic per-tensor u8 activations x s8 weights -> s32 (tcgen05 kind::i8), "
                                     "FP32 epilogue bit-identical to the reference"}
+        if self.sharded:
+            self.config["exchange"] = "NCCL all-reduce of the shards' {min, max} (2 floats) before quantising"
 
-    def units_per_step(self) -> float:
-        return 2.0 * self.m * self.k * self.n
+    def units_per_step(self):
+        return 2.0 * self.m * self.k * self.n * (self.sh.world if self.replicas else 1)
 
-    def main_kernel_units(self) -> float:
+    def main_kernel_units(self):
         kp = (self.k + 127) // 128 * 128
-        return self.m * kp + self.n * kp + self.m * self.n * 4 + self.n * 16
+        return self.rows * kp + self.n * kp + self.rows * self.n * 4 + self.n * 16
 
-    def step(self):
-        from onnxsharp_b200.runtime import dqmm
+    def _run(self, a, y):
+        from onnxsharp_b200 import shard
+        from onnxsharp_b200.runtime import dqmm, minmax
 
-        dqmm(self.ctx, self.a, self.w, self.ws, self.b, out=self.y)
+        if self.sharded:
+            minmax(self.ctx, a, out=self.mm)
+            shard.global_minmax(self.mm, group=self.sh.group)
+            dqmm(self.ctx, a, self.w, self.ws, self.b, out=y, minmax_override=self.mm)
+        else:
+            dqmm(self.ctx, a, self.w, self.ws, self.b, out=y)
+
+    def compute(self):
+        self._run(self.a, self.y)
+
+    def collect(self):
+        if self.sharded:
+            self.sh.all_gather(self.y_full, self.y)
+
+    def collect_bytes(self):
+        return (self.sh.world - 1) * self.y.numel() * 4 if self.sharded else 0
 
     def e2e_step(self):
-        from onnxsharp_b200.runtime import dqmm
-
         self.ctx.memcpy_htod(self.a2, self.a_pin, self.a_pin.numel() * 4)
-        dqmm(self.ctx, self.a2, self.w, self.ws, self.b, out=self.y2)
-        self.ctx.memcpy_dtoh(self.y_pin, self.y2, self.y_pin.numel() * 4)
+        self._run(self.a2, self.y2)
+        if self.sharded:
+            self.sh.all_gather(self.y2_full, self.y2)
+        if self.sh.rank == 0:
+            self.ctx.memcpy_dtoh(self.y_pin, self.y2_full, self.y_pin.numel() * 4)
 
     def e2e_bytes(self):
-        return self.m * self.k * 4, self.m * self.n * 4
+        r = self.sh.world if self.replicas else 1
+        return self.a_h.nbytes * r, self.y_pin.numel() * 4
 
-    def cpu_sample(self, threads: int) -> dict:
-        return CpuDqmm(self.a_h, self.w_h, self.ws_h, self.b_h).cpu_sample(threads)
+    def cpu_sample(self, threads, budget_s):
+        return CpuDqmm(self.a_h, self.w_h, self.ws_h, self.b_h).cpu_sample(threads, budget_s)
+
+
+ATTN_FLOPS = 4 * 2.0 * 8192 * 512 * 512 + 2 * 2.0 * 64 * 8 * 128 * 128 * 64
+
+
+class AttentionWorkload(Workload):
+    """Config 4: X[64,128,512] N(0,1) -> Q/K/V projections (MatMul+bias, Xavier-uniform, zero bias)
+    -> FusedAttention (H=8, D=64, scale 1/8) -> output projection; sequences sharded."""
+
+    key = "attention"
+    name = "attention_block_b64_t128_h8_d64"
+    main_kernel = ("k_gemm_tf32x3",)
+
+    def __init__(self, ctx, sh: Shard):
+        import torch
+
+        from onnxsharp_b200.runtime import GemmWeights
+
+        self.ctx, self.sh = ctx, sh
+        rng = np.random.default_rng(5150)
+        self.B, self.T, self.C, self.H = 64, 128, 512, 8
+        x = rng.normal(0, 1, (self.B * self.T, self.C)).astype(np.float32)
+        lim = np.sqrt(6.0 / (self.C + self.C))
+        ws = [rng.uniform(-lim, lim, (self.C, self.C)).astype(np.float32) for _ in range(4)]
+        self.x_h, self.ws_h = x, ws
+        lo, cnt, self.replicas = sh.plan(self.B)
+        self.seqs = cnt
+        rows = slice(lo * self.T, (lo + cnt) * self.T)
+        dev = _dev()
+        self.x = torch.from_numpy(x[rows]).to(dev)
+        self.bias = torch.zeros(self.C, device=dev)
+        self.w = [GemmWeights(ctx, torch.from_numpy(w).to(dev), self.C, self.C) for w in ws]
+        self.qkv = [torch.empty(cnt * self.T, self.C, device=dev) for _ in range(3)]
+        self.o = torch.empty(cnt, self.T, self.C, device=dev)
+        self.y = torch.empty(cnt * self.T, self.C, device=dev)
+        self.gather = sh.world > 1 and not self.replicas
+        self.y_full = torch.empty(self.B * self.T, self.C, device=dev) if self.gather else self.y
+        self.x_pin = torch.from_numpy(x[rows].copy()).pin_memory()
+        self.y_pin = torch.empty(self.y_full.shape).pin_memory()
+        self.x2 = torch.empty_like(self.x)
+        self.config = {"workload": self.name, "x": [64, 128, 512], "heads": 8, "head_dim": 64,
+                       "sequences_per_gpu": cnt,
+                       "precision": "3xTF32 tcgen05 (projections and QK^T / PV), FP32 softmax"}
+
+    def units_per_step(self):
+        return ATTN_FLOPS * (self.sh.world if self.replicas else 1)
+
+    def main_kernel_units(self):
+        return 2.0 * self.seqs * self.T * 512 * 512
+
+    def _run(self, x):
+        from onnxsharp_b200.runtime import attention, gemm_bias
+
+        for w, out in zip(self.w[:3], self.qkv):
+            gemm_bias(self.ctx, x, w, self.bias, out=out)
+        q, k, v = (t.view(self.seqs, self.T, self.C) for t in self.qkv)
+        attention(self.ctx, q, k, v, self.H, 0.125, out=self.o)
+        gemm_bias(self.ctx, self.o.view(self.seqs * self.T, self.C), self.w[3], self.bias, out=self.y)
+
+    def compute(self):
+        self._run(self.x)
+
+    def collect(self):
+        if self.gather:
+            self.sh.all_gather(self.y_full, self.y)
+
+    def collect_bytes(self):
+        return (self.sh.world - 1) * self.y.numel() * 4 if self.gather else 0
+
+    def e2e_step(self):
+        self.ctx.memcpy_htod(self.x2, self.x_pin, self.x_pin.numel() * 4)
+        self._run(self.x2)
+        self.collect()
+        if self.sh.rank == 0:
+            self.ctx.memcpy_dtoh(self.y_pin, self.y_full, self.y_pin.numel() * 4)
+
+    def e2e_bytes(self):
+        r = self.sh.world if self.replicas else 1
+        return self.x_h.nbytes * r, self.y_pin.numel() * 4
+
+    def cpu_sample(self, threads, budget_s):
+        return CpuAttention(self.x_h, self.ws_h).cpu_sample(threads, budget_s)
+
+
+FRAME_HW = (720, 1280)  # source frames of the serving e2e: 1280x720 BGR u8 (letterboxed to 640x640 on the device)
 
 
 class YoloWorkload(Workload):
-    """random-init YOLO11n-shaped detector, [B,3,640,640] U(0,1) -> [B,84,8400], B = 64 per GPU.
+    """Config 5: random-init YOLO11n-shaped detector, [B,3,640,640] U(0,1) -> [B,84,8400], B in {1, 8, 64}
+    global, images sharded over the GPUs and the [B/N,84,8400] outputs all-gathered.
 
-    A step is one replay of the plan's CUDA graph. The dominant kernels are the
-    tensor-core convs (channel-major implicit GEMM, pixel-major 1x1 / small-
-    image convs); their roofline figures come from a profiled eager pass
-    (event timing cannot be inserted into a graph replay)."""
+    A step is one replay of the plan's CUDA graph plus the all-gather. The
+    dominant kernels are the tensor-core convs (channel-major implicit GEMM,
+    pixel-major 1x1 / small-image convs); their time comes from a profiled
+    eager pass (event timing cannot be inserted into a graph replay).
 
-    name = "yolo11n_shaped_b64_640"
+    e2e is the reference's YoloDetector.Detect path (frames in, detections
+    out, onnxsharp_b200.serve.DetectPipeline): u8 1280x720 frames from pinned
+    host memory, batched letterbox + forward + decode/NMS as one CUDA graph,
+    the packed detections all-gathered and read back on rank 0; batches are
+    pipelined (H2D, graph and D2H of consecutive batches overlap)."""
+
     unit = "images/s"
     main_kernel = ("k_conv_tf32x3", "k_conv_px_tf32x3")
-    bound = "tensor"
     long_step = True
 
-    def __init__(self, ctx, rank: int, batch: int = 64):
+    def __init__(self, ctx, sh: Shard, batch: int = 64, tensor_e2e: bool = False):
         import torch
 
         from onnxsharp_b200 import yolo
 
-        self.batch = batch
-        self.ctx = ctx
+        self.ctx, self.sh, self.batch = ctx, sh, batch
+        self.key = f"yolo_b{batch}"
+        self.name = f"yolo11n_shaped_b{batch}_640"
+        lo, cnt, self.replicas = sh.plan(batch)
+        self.local = cnt
         self.g = yolo.build_yolo11n()
         self.params = yolo.init_params(self.g, 2024)
-        self.net = yolo.Net(ctx, self.g, self.params, batch)
-        rng = np.random.default_rng(9000 + rank)
+        self.net = yolo.Net(ctx, self.g, self.params, cnt)
+        rng = np.random.default_rng(9000)
         self.images_h = rng.uniform(0, 1, (batch, 3, 640, 640)).astype(np.float32)
-        self.net.input_view().copy_(torch.from_numpy(self.images_h))
-        self.images_pin = torch.from_numpy(self.images_h).pin_memory()
-        self.out_pin = torch.empty(self.net.output.shape, dtype=torch.float32).pin_memory()
-        # a second host batch and output for the pipelined serving loop
-        self.images_pin2 = torch.from_numpy(rng.uniform(0, 1, (batch, 3, 640, 640)).astype(np.float32)).pin_memory()
-        self.out_pin2 = torch.empty(self.net.output.shape, dtype=torch.float32).pin_memory()
-        self.pipe = None
+        self.net.input_view().copy_(torch.from_numpy(self.images_h[lo:lo + cnt]))
+        self.gather = sh.world > 1 and not self.replicas
+        dev = _dev()
+        self.out_full = (torch.empty((batch, 84, 8400), dtype=torch.float32, device=dev) if self.gather
+                         else self.net.output)
         self.flops_img = yolo.flops_per_image(self.g)
         self.tc_flops = sum(self._node_flops(n) for n in self.g.nodes
-                            if n.op == "conv" and yolo.Net.tensor_core(n)) * batch
+                            if n.op == "conv" and yolo.Net.tensor_core(n)) * cnt
         self.tc_launches = sum(1 for n in self.g.nodes if n.op == "conv" and yolo.Net.tensor_core(n))
         self.net.forward(use_graph=True)  # capture
         ctx.synchronize()
-        self.config = {"workload": self.name, "batch_per_gpu": batch, "input": [batch, 3, 640, 640],
-                       "output": [batch, 84, 8400], "gflop_per_image": round(self.flops_img / 1e9, 3),
+        self.pipe = None
+        self.tensor_e2e = tensor_e2e
+        self.config = {"workload": self.name, "global_batch": batch, "images_per_gpu": cnt,
+                       "input": [batch, 3, 640, 640], "output": [batch, 84, 8400],
+                       "gflop_per_image": round(self.flops_img / 1e9, 3),
                        "arena_mib": round(self.net.arena_bytes / 2 ** 20, 1),
                        "precision": "FP32 in/out; wide convs 3xTF32 tcgen05 (k x k implicit GEMM on NHWC hi/lo, 1x1 "
                                     "straight from NCHW), narrow and depthwise convs FP32 CUDA-core FMA, glue FP32 CUDA "
@@ -415,135 +634,255 @@ class YoloWorkload(Workload):
         oh, ow = self.g.hw(y)
         return 2.0 * y.c * oh * ow * (n.ins[0].c // n.attrs["group"]) * n.attrs["k"] ** 2
 
-    def units_per_step(self) -> float:
-        return float(self.batch)
+    def units_per_step(self):
+        return float(self.batch * (self.sh.world if self.replicas else 1))
 
-    def main_kernel_units(self) -> float:
+    def main_kernel_units(self):
         return self.tc_flops / self.tc_launches
 
-    def step(self):
+    def compute(self):
         self.net.forward(use_graph=True)
 
-    def profile_step(self):
+    def profile_compute(self):
         self.net.forward(use_graph=False)
 
-    def e2e_step(self):
-        # torch copies on the caller stream (the plan orders itself after it)
-        self.net.input_view().copy_(self.images_pin, non_blocking=True)
-        self.net.forward(use_graph=True)
-        self.out_pin.copy_(self.net.output, non_blocking=True)
+    def collect(self):
+        if self.gather:
+            self.sh.all_gather(self.out_full, self.net.output)
+
+    def collect_bytes(self):
+        return (self.sh.world - 1) * self.net.output.numel() * 4 if self.gather else 0
+
+    # -- serving e2e: frames in, detections out
+    def _pipeline(self):
+        import torch
+
+        from onnxsharp_b200.serve import DetectPipeline
+
+        if self.pipe is None:
+            self.pipe = DetectPipeline(self.net, frame_hw=FRAME_HW, bgr=True, depth=2, gather=self.gather,
+                                       group=self.sh.group)
+            rng = np.random.default_rng(77 + self.sh.rank)
+            self.frames_pin, self.result_pin = [], []
+            for _ in range(2):
+                f, r = self.pipe.host_buffers()
+                f.copy_(torch.from_numpy(rng.integers(0, 256, f.shape, dtype=np.uint8)))
+                self.frames_pin.append(f)
+                self.result_pin.append(r if self.sh.rank == 0 or not self.gather else None)
+        return self.pipe
+
+    def e2e_pipelined(self, warmup: int, steps: int) -> float:
+        """ms per step of the serving loop, device-timed from the first H2D to the last D2H."""
+        import torch
+
+        pipe = self._pipeline()
+        for i in range(max(1, warmup)):
+            pipe.submit(self.frames_pin[i % 2], self.result_pin[i % 2])
+        pipe.synchronize()
+        self.sh.barrier()
+        torch.cuda.synchronize()
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(pipe.h2d)
+        for i in range(steps):
+            pipe.submit(self.frames_pin[i % 2], self.result_pin[i % 2])
+        stop.record(pipe.d2h)
+        stop.synchronize()
+        pipe.synchronize()
+        self.sh.barrier()
+        return start.elapsed_time(stop) / steps
 
     def e2e_bytes(self):
-        return self.images_pin.numel() * 4, self.out_pin.numel() * 4
+        r = self.sh.world if self.replicas else 1
+        h2d = self.batch * r * FRAME_HW[0] * FRAME_HW[1] * 3
+        pack = self.local * (300 * 6 + 1) * 4
+        return h2d, pack * self.sh.world  # gathered to rank 0, or one pack per replica
 
-    e2e_mode = ("pipelined: yolo.HostPipeline, depth 2 (H2D of batch i, plan of batch i-1 and D2H of batch "
-                "i-2 overlap on three streams); each step copies its own 315 MB input from pinned host memory "
-                "and reads its 181 MB output back; device-timed from the first H2D to the last D2H, pipeline "
-                "fill and drain included; per-step inputs exceed L2, so no flush")
+    e2e_mode = ("pipelined serving loop (onnxsharp_b200.serve.DetectPipeline, depth 2): per step each GPU copies "
+                "its images' 1280x720 BGR u8 frames from pinned host memory, one CUDA graph runs the batched "
+                "letterbox, the forward pass and decode + NMS (conf 0.25, IoU 0.45, max 300 per image), the packed "
+                "detections are all-gathered over NCCL and rank 0 reads the whole batch's detections back; device-"
+                "timed from the first H2D to the last D2H, fill and drain included")
 
-    def e2e_pipelined(self, warmup: int, steps: int, barrier) -> float:
-        """ms per step of the serving loop, device-timed from the first H2D to the last D2H."""
+    def e2e_tensor(self, warmup: int, steps: int) -> float:
+        """ms per step of FP32 tensor in / FP32 tensor out through yolo.HostPipeline (each rank its own images)."""
         import torch
 
         from onnxsharp_b200 import yolo
 
-        if self.pipe is None:
-            self.pipe = yolo.HostPipeline(self.net, depth=2)
-        ins, outs = (self.images_pin, self.images_pin2), (self.out_pin, self.out_pin2)
+        pipe = yolo.HostPipeline(self.net, depth=2)
+        rng = np.random.default_rng(5 + self.sh.rank)
+        ins = [torch.from_numpy(rng.uniform(0, 1, self.net.inputs[0].shape).astype(np.float32)).pin_memory()
+               for _ in range(2)]
+        outs = [torch.empty(self.net.outputs[0].shape, dtype=torch.float32).pin_memory() for _ in range(2)]
         for i in range(max(1, warmup)):
-            self.pipe.submit(ins[i % 2], outs[i % 2])
-        self.pipe.synchronize()
-        barrier()
+            pipe.submit(ins[i % 2], outs[i % 2])
+        pipe.synchronize()
+        self.sh.barrier()
         torch.cuda.synchronize()
         start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        start.record(self.pipe.h2d)
+        start.record(pipe.h2d)
         for i in range(steps):
-            self.pipe.submit(ins[i % 2], outs[i % 2])
-        stop.record(self.pipe.d2h)
+            pipe.submit(ins[i % 2], outs[i % 2])
+        stop.record(pipe.d2h)
         stop.synchronize()
-        barrier()
+        self.sh.barrier()
         return start.elapsed_time(stop) / steps
 
-    def cpu_sample(self, threads: int) -> dict:
-        return CpuYolo(self.g, self.params, self.images_h[:1]).cpu_sample(threads)
+    def cpu_sample(self, threads, budget_s):
+        return CpuYolo(self.g, self.params, self.images_h, self.batch).cpu_sample(threads, budget_s)
+
+    def close(self):
+        self.net.close()
 
 
-ATTN_FLOPS = 4 * 2.0 * 8192 * 512 * 512 + 2 * 2.0 * 64 * 8 * 128 * 128 * 64
-
-
-class AttentionWorkload(Workload):
-    """X[64,128,512] N(0,1) -> Q/K/V projections (MatMul+bias, Xavier-uniform, zero bias)
-    -> FusedAttention (H=8, D=64, scale 1/8) -> output projection."""
-
-    graphed = True
-    name = "attention_block_b64_t128_h8_d64"
-    main_kernel = "k_gemm_tf32x3"
-
-    def __init__(self, ctx, rank: int):
-        import torch
-
-        from onnxsharp_b200.runtime import GemmWeights
-
-        rng = np.random.default_rng(5150 + rank)
-        self.B, self.T, self.C, self.H = 64, 128, 512, 8
-        x = rng.normal(0, 1, (self.B * self.T, self.C)).astype(np.float32)
-        lim = np.sqrt(6.0 / (self.C + self.C))
-        ws = [rng.uniform(-lim, lim, (self.C, self.C)).astype(np.float32) for _ in range(4)]
-        dev = torch.device("cuda", torch.cuda.current_device())
-        self.ctx = ctx
-        self.x_h = x
-        self.ws_h = ws
-        self.x = torch.from_numpy(x).to(dev)
-        self.bias = torch.zeros(self.C, device=dev)
-        self.w = [GemmWeights(ctx, torch.from_numpy(w).to(dev), self.C, self.C) for w in ws]
-        self.qkv = [torch.empty(self.B * self.T, self.C, device=dev) for _ in range(3)]
-        self.o = torch.empty(self.B, self.T, self.C, device=dev)
-        self.y = torch.empty(self.B * self.T, self.C, device=dev)
-        self.x_pin = torch.from_numpy(x).pin_memory()
-        self.y_pin = torch.empty(self.B * self.T, self.C).pin_memory()
-        self.x2 = torch.empty_like(self.x)
-        self.config = {"workload": self.name, "x": [64, 128, 512], "heads": 8, "head_dim": 64,
-                       "precision": "3xTF32 tcgen05 (projections and QK^T / PV), FP32 softmax"}
-
-    def units_per_step(self) -> float:
-        return ATTN_FLOPS
-
-    def main_kernel_units(self) -> float:
-        return 2.0 * 8192 * 512 * 512
-
-    def _run(self, x):
-        from onnxsharp_b200.runtime import attention, gemm_bias
-
-        for w, out in zip(self.w[:3], self.qkv):
-            gemm_bias(self.ctx, x, w, self.bias, out=out)
-        q, k, v = (t.view(self.B, self.T, self.C) for t in self.qkv)
-        attention(self.ctx, q, k, v, self.H, 0.125, out=self.o)
-        gemm_bias(self.ctx, self.o.view(self.B * self.T, self.C), self.w[3], self.bias, out=self.y)
-
-    def step(self):
-        self._run(self.x)
-
-    def e2e_step(self):
-        self.ctx.memcpy_htod(self.x2, self.x_pin, self.x_pin.numel() * 4)
-        self._run(self.x2)
-        self.ctx.memcpy_dtoh(self.y_pin, self.y, self.y_pin.numel() * 4)
-
-    def e2e_bytes(self):
-        return self.x_pin.numel() * 4, self.y_pin.numel() * 4
-
-    def cpu_sample(self, threads: int) -> dict:
-        return CpuAttention(self.x_h, self.ws_h).cpu_sample(threads)
-
-
-WORKLOADS = {"gemm": GemmWorkload, "conv": ConvWorkload, "dqmm": DqmmWorkload, "yolo": YoloWorkload,
-             "attention": AttentionWorkload}
+WORKLOADS = {"gemm": lambda c, s: GemmWorkload(c, s), "conv_b16": lambda c, s: ConvWorkload(c, s, 16),
+             "conv_b1": lambda c, s: ConvWorkload(c, s, 1), "dqmm": lambda c, s: DqmmWorkload(c, s),
+             "attention": lambda c, s: AttentionWorkload(c, s), "yolo_b1": lambda c, s: YoloWorkload(c, s, 1),
+             "yolo_b8": lambda c, s: YoloWorkload(c, s, 8), "yolo": lambda c, s: YoloWorkload(c, s, 64)}
+ALIASES = {"conv": "conv_b16", "yolo_b64": "yolo"}
 DEFAULT_WORKLOAD = "yolo"
-DEFAULT_STEPS = {"gemm": 2000, "conv": 1000, "dqmm": 2000, "yolo": 100, "attention": 500}
+CONFIG_ORDER = ["gemm", "conv_b1", "conv_b16", "dqmm", "attention", "yolo_b1", "yolo_b8"]
+DEFAULT_STEPS = {"gemm": 1000, "conv_b16": 200, "conv_b1": 500, "dqmm": 1000, "attention": 300, "yolo_b1": 300,
+                 "yolo_b8": 150, "yolo": 100}
+CONFIG_STEPS = {"gemm": 200, "conv_b16": 40, "conv_b1": 200, "dqmm": 200, "attention": 100, "yolo_b1": 100,
+                "yolo_b8": 50}
+# The reference's own published CPU figures (4 threads, Ryzen 7 8845HS, .NET 10), shown beside the timed CPU baseline.
+PUBLISHED = {
+    "gemm": {"value": 0.3938, "unit": "TFLOP/s", "threads": 4,
+             "what": "packed GEMM 1028x384x1536, 393.8 GFLOPS", "source": "bench.md:961-970"},
+    "yolo": {"value": 1000.0 / 29.2, "unit": "images/s", "threads": 4,
+             "what": "yolo11n 640x640 batch 1, 29.2 ms median", "source": "README.md:1743-1748"},
+}
 
 
 # ----------------------------------------------------------------- timing
 def flush_l2(buf):
     buf.add_(1.0)
+
+
+def _events(n):
+    import torch
+
+    return [torch.cuda.Event(enable_timing=True) for _ in range(n)], [torch.cuda.Event(enable_timing=True)
+                                                                      for _ in range(n)]
+
+
+def time_steps(step, K, flush, stream, sh: Shard) -> float:
+    """Mean ms of K steps, each bracketed by CUDA events on `stream`, L2 flushed between steps."""
+    import torch
+
+    starts, stops = _events(K)
+    sh.barrier()
+    torch.cuda.synchronize()
+    for i in range(K):
+        starts[i].record(stream)
+        step()
+        stops[i].record(stream)
+        flush_l2(flush)
+    torch.cuda.synchronize()
+    sh.barrier()
+    return sum(s.elapsed_time(e) for s, e in zip(starts, stops)) / K
+
+
+def measure(wl: Workload, ctx, sh: Shard, K: int, W: int, flush, stream, profile_steps: int, e2e_steps: int,
+            tensor_e2e: bool = False) -> dict:
+    """Device-resident step time, dominant-kernel time, launches, collective time and e2e of one workload
+    (every rank calls this in the same order: the collectives inside line up)."""
+    graph = ctx.capture(wl.compute) if wl.graphed and not isinstance(wl, YoloWorkload) else None
+    compute = graph.launch if graph is not None else wl.compute
+    profile_compute = getattr(wl, "profile_compute", wl.compute)
+
+    def step():
+        compute()
+        wl.collect()
+
+    for _ in range(W):
+        step()
+        flush_l2(flush)
+    ctx.synchronize()
+    launches0 = ctx.launch_count()
+    step_ms = time_steps(step, K, flush, stream, sh)
+    if graph is None and not isinstance(wl, YoloWorkload):
+        launches = ctx.launch_count() - launches0
+    else:  # graph replays: count one eager pass's launches
+        l0 = ctx.launch_count()
+        profile_compute()
+        ctx.synchronize()
+        launches = (ctx.launch_count() - l0) * K
+    # the collective alone
+    coll_ms = time_steps(wl.collect, max(5, K // 4), flush, stream, sh) if wl.collect_bytes() else 0.0
+    # dominant kernel time from profiled eager passes
+    ctx.profile_reset()
+    ctx.profile(True)
+    for _ in range(profile_steps):
+        profile_compute()
+        flush_l2(flush)
+    ctx.synchronize()
+    ctx.profile(False)
+    kern_ms, kern_n = 0.0, 0
+    for name in wl.main_kernel:
+        ms_, n_ = ctx.profile_read(name)
+        kern_ms, kern_n = kern_ms + ms_, kern_n + n_
+    all_ms, _ = ctx.profile_read("")
+    ctx.profile_reset()
+    # e2e through the public API with pinned host buffers
+    e2e_tensor_ms = None
+    if isinstance(wl, YoloWorkload):
+        e2e_ms = wl.e2e_pipelined(W, e2e_steps)
+        e2e_mode = wl.e2e_mode
+        if tensor_e2e:
+            e2e_tensor_ms = wl.e2e_tensor(W, e2e_steps)
+    else:
+        import torch
+
+        for _ in range(W):
+            wl.e2e_step()
+        ctx.synchronize()
+        e2e_ms = time_steps(wl.e2e_step, e2e_steps, flush, stream, sh)
+        e2e_mode = ("serial: H2D of this GPU's shard, compute, all-gather of the shards (N > 1), D2H of the whole "
+                    "output on rank 0; L2 flushed between steps")
+        torch.cuda.synchronize()
+    if graph is not None:
+        graph.close()
+    return {"step_ms": step_ms, "kern_ms": kern_ms / max(1, kern_n), "kern_share": kern_ms / max(all_ms, 1e-12),
+            "launches": launches, "coll_ms": coll_ms, "e2e_ms": e2e_ms, "e2e_mode": e2e_mode,
+            "e2e_tensor_ms": e2e_tensor_ms}
+
+
+def roofline(wl: Workload, kern_ms: float, peaks: dict, peaks_kind: str, traffic) -> dict:
+    if wl.bound == "tensor":
+        pkey = "bf16_tflops_sustained" if wl.long_step else "bf16_tflops"
+        peak = peaks.get(pkey, FALLBACK_PEAKS[pkey]) / 2.0 / 3.0
+        achieved = _tflops(wl.main_kernel_units() / (kern_ms * 1e-3))
+        return {"bound": "tensor", "achieved": round(achieved, 2), "peak": round(peak, 2), "unit": "TFLOP/s",
+                "frac": round(achieved / peak, 4), "traffic": traffic, "kernel": "+".join(wl.main_kernel),
+                "kernel_ms": round(kern_ms, 5),
+                "peak_basis": f"3xTF32 = {pkey}/2 (kind::tf32 rate) /3 products, {pkey} {peaks.get(pkey)} "
+                              f"({peaks_kind}); frac of {peaks_kind}"}
+    peak = peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
+    achieved = wl.main_kernel_units() / (kern_ms * 1e-3) / 1e9
+    return {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+            "frac": round(achieved / peak, 4), "traffic": traffic, "kernel": "+".join(wl.main_kernel),
+            "kernel_ms": round(kern_ms, 5), "peak_basis": f"hbm_gbs ({peaks_kind}); frac of {peaks_kind}"}
+
+
+def _rate(wl: Workload, units: float, ms: float) -> float:
+    v = units / (ms * 1e-3)
+    return _tflops(v) if wl.unit in ("TFLOP/s", "TOP/s") else v
+
+
+def cpu_baseline(wl: Workload, budget_s: float) -> dict:
+    cores = physical_cores()
+    base = wl.cpu_sample(cores, budget_s)
+    base.update(kind="port", cpu=cpu_model())
+    try:
+        base["value_4_threads"] = wl.cpu_sample(min(4, cores), budget_s / 2)["value"]
+    except Exception:  # pragma: no cover
+        pass
+    pub = PUBLISHED.get(wl.key) or PUBLISHED.get(wl.key.split("_b")[0])
+    if pub is not None:
+        base["reference_published"] = pub
+    return base
 
 
 def run_ours(args, peaks, peaks_kind) -> dict | None:
@@ -558,158 +897,121 @@ def run_ours(args, peaks, peaks_kind) -> dict | None:
         from datetime import timedelta
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    sh = Shard(world, rank)
 
     from onnxsharp_b200.runtime import Context
 
-    # a capturable (non-legacy) stream for the library, the events and the L2 flush
+    # a capturable (non-legacy) stream for the library, the events, the collectives and the L2 flush
     torch.cuda.set_stream(torch.cuda.Stream())
     ctx = Context(local)
     ctx.use_torch_stream()
-    wl = WORKLOADS[args.workload](ctx, rank)
     stream = torch.cuda.current_stream()
-    graph = None
-    if getattr(wl, "graphed", False):
-        # The executor's form: the op's launches replayed as one CUDA graph per step;
-        # per-kernel times come from profiled eager passes of the same launches.
-        graph = ctx.capture(wl.step)
-        wl.profile_step = wl.step
-        wl.step = graph.launch
     flush = torch.empty(512 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
 
-    def barrier():
-        if world > 1:
-            dist.barrier()
-
-    # warm-up
-    for _ in range(args.warmup):
-        wl.step()
-        flush_l2(flush)
-    ctx.synchronize()
-
-    K = args.steps
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
-    stops = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    # --- headline
+    head = WORKLOADS[args.workload](ctx, sh)
     sampler = ClockSampler(local)
     sampler.start()
     time.sleep(0.3)
-    ctx.profile_reset()
-    ctx.profile(True)
-    launches0 = ctx.launch_count()
-    barrier()
-    torch.cuda.synchronize()
-    for i in range(K):
-        starts[i].record(stream)
-        wl.step()
-        stops[i].record(stream)
-        flush_l2(flush)
-    torch.cuda.synchronize()
-    barrier()
-    launches = ctx.launch_count() - launches0
-    ctx.profile(False)
-    ctx.synchronize()
-    step_ms = sum(s.elapsed_time(e) for s, e in zip(starts, stops)) / K
-    if hasattr(wl, "profile_step"):
-        # Graph replays carry no per-kernel events: count the plan's launches
-        # from one eager pass and time its kernels over a profiled eager pass.
-        ctx.profile_reset()
-        l0 = ctx.launch_count()
-        wl.profile_step()
-        ctx.synchronize()
-        launches = (ctx.launch_count() - l0) * K
-        ctx.profile_reset()
-        ctx.profile(True)
-        for _ in range(args.profile_steps):
-            wl.profile_step()
-            flush_l2(flush)
-        ctx.synchronize()
-        ctx.profile(False)
-    names = wl.main_kernel if isinstance(wl.main_kernel, tuple) else (wl.main_kernel,)
-    kern_ms, kern_n = 0.0, 0
-    for name in names:
-        ms_, n_ = ctx.profile_read(name)
-        kern_ms, kern_n = kern_ms + ms_, kern_n + n_
-    all_ms, _ = ctx.profile_read("")
-    ctx.profile_reset()
-
-    # e2e through the public API with pinned host buffers
-    KE = max(1, min(K, args.e2e_steps))
-    if hasattr(wl, "e2e_pipelined"):
-        # a serving loop: its own step count (not capped by --steps), so the
-        # pipeline's fill (first H2D) and drain (last D2H) stay a small part
-        KE = max(1, args.e2e_steps)
-        e2e_ms = wl.e2e_pipelined(args.warmup, KE, barrier)
-        e2e_mode = wl.e2e_mode
-    else:
-        for _ in range(max(1, args.warmup)):
-            wl.e2e_step()
-        ctx.synchronize()
-        e_starts = [torch.cuda.Event(enable_timing=True) for _ in range(KE)]
-        e_stops = [torch.cuda.Event(enable_timing=True) for _ in range(KE)]
-        barrier()
-        torch.cuda.synchronize()
-        for i in range(KE):
-            e_starts[i].record(stream)
-            wl.e2e_step()
-            e_stops[i].record(stream)
-            flush_l2(flush)
-        torch.cuda.synchronize()
-        barrier()
-        e2e_ms = sum(s.elapsed_time(e) for s, e in zip(e_starts, e_stops)) / KE
-        e2e_mode = "serial: H2D, compute, D2H per step, L2 flushed between steps"
+    m = measure(head, ctx, sh, args.steps, args.warmup, flush, stream, args.profile_steps, args.e2e_steps,
+                tensor_e2e=isinstance(head, YoloWorkload))
     clocks = sampler.stop()
+    weak_ms = None
+    if world > 1 and isinstance(head, YoloWorkload) and not args.no_weak:
+        # secondary: weak scaling, every GPU its own batch of 64 (no collective)
+        solo = YoloWorkload(ctx, Shard(1, 0), head.batch)
+        weak_ms = time_steps(solo.compute, max(10, args.steps // 2), flush, stream, sh)
+        solo.close()
+    head.close()
 
-    t = torch.tensor([step_ms, e2e_ms], dtype=torch.float64, device="cuda")
+    # --- every other BASELINE config, same process
+    sub = {}
+    if not args.no_configs:
+        for key in CONFIG_ORDER:
+            if key == args.workload:
+                continue
+            wl = WORKLOADS[key](ctx, sh)
+            K = CONFIG_STEPS[key]
+            sub[key] = (wl, measure(wl, ctx, sh, K, args.warmup, flush, stream, max(3, args.profile_steps // 2),
+                                    max(5, min(K, args.e2e_steps))), K)
+            wl.close()
+
+    # max over ranks of every timing, one collective
+    vals = [m["step_ms"], m["e2e_ms"], m["coll_ms"], m["e2e_tensor_ms"] or 0.0, weak_ms or 0.0]
+    for key in sub:
+        r = sub[key][1]
+        vals += [r["step_ms"], r["e2e_ms"], r["coll_ms"]]
+    t = torch.tensor(vals, dtype=torch.float64, device="cuda")
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    step_ms_max, e2e_ms_max = t.tolist()
+    vals = t.tolist()
 
     result = None
     if rank == 0:
-        units = wl.units_per_step() * world
-        value = _scale(units / (step_ms_max * 1e-3)) if wl.unit in ("TFLOP/s", "TOP/s") else units / (step_ms_max * 1e-3)
-        e2e_value = _scale(units / (e2e_ms_max * 1e-3)) if wl.unit in ("TFLOP/s", "TOP/s") else units / (e2e_ms_max * 1e-3)
-        kern_avg_ms = kern_ms / max(1, kern_n)
-        if wl.bound == "tensor":
-            # burst figure for a kernel timed alone; sustained for kernels timed inside a long step
-            pkey = "bf16_tflops_sustained" if getattr(wl, "long_step", False) else "bf16_tflops"
-            peak = peaks.get(pkey, FALLBACK_PEAKS[pkey]) / 2.0 / 3.0
-            achieved = _scale(wl.main_kernel_units() / (kern_avg_ms * 1e-3))
-            rl = {"bound": "tensor", "achieved": round(achieved, 2), "peak": round(peak, 2), "unit": "TFLOP/s",
-                  "frac": round(achieved / peak, 4), "traffic": args.traffic,
-                  "kernel": "+".join(names), "kernel_ms": round(kern_avg_ms, 5), "kernel_share": round(kern_ms / max(all_ms, 1e-12), 4),
-                  "peak_basis": f"3xTF32 = {pkey}/2 (kind::tf32 rate) /3 products, {pkey} of {peaks_kind} "
-                                f"{peaks.get(pkey)}; frac of {peaks_kind}"}
-        else:
-            peak = peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
-            achieved = wl.main_kernel_units() / (kern_avg_ms * 1e-3) / 1e9
-            rl = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                  "frac": round(achieved / peak, 4), "traffic": args.traffic, "kernel": "+".join(names),
-                  "kernel_ms": round(kern_avg_ms, 5), "peak_basis": f"hbm_gbs of {peaks_kind}"}
-        bi, bo = wl.e2e_bytes()
+        step_ms, e2e_ms, coll_ms, e2e_t_ms, weak_ms_max = vals[:5]
+        units = head.units_per_step()
+        bi, bo = head.e2e_bytes()
+        par = (f"dp{world}: batch sharded over {world} GPUs, shard outputs all-gathered over NVLink (NCCL) inside "
+               f"the timed step" if world > 1 and not head.replicas else
+               (f"{world} replicas (batch smaller than the GPU count)" if head.replicas else "single GPU"))
         result = {
-            "metric": METRIC, "value": round(value, 3), "unit": wl.unit, "n_gpus": world, "steps": K,
-            "warmup": args.warmup, "ms_per_step": round(step_ms_max, 5), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded numpy), per rank",
-            "config": dict(wl.config, l2="flushed between steps (512 MiB write outside the events)",
-                           parallelism=f"dp{world} (independent shards, no data-path collective)"),
-            "e2e": {"value": round(e2e_value, 3), "unit": wl.unit, "h2d_bytes_per_step": bi, "d2h_bytes_per_step": bo,
-                    "ms_per_step": round(e2e_ms_max, 5), "steps": KE, "mode": e2e_mode},
-            "roofline": rl,
-            "gpu_launches": int(launches),
+            "metric": METRIC, "value": round(_rate(head, units, step_ms), 3), "unit": head.unit, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 5), "higher_is_better": True,
+            "scaling": "weak" if head.replicas else "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded numpy, same global batch on every N)",
+            "config": dict(head.config, l2="flushed between steps (512 MiB write outside the events)",
+                           parallelism=par),
+            "e2e": {"value": round(_rate(head, units, e2e_ms), 3), "unit": head.unit, "h2d_bytes_per_step": bi,
+                    "d2h_bytes_per_step": bo, "ms_per_step": round(e2e_ms, 5), "steps": args.e2e_steps,
+                    "mode": m["e2e_mode"]},
+            "roofline": roofline(head, m["kern_ms"], peaks, peaks_kind, load_traffic(head.key)),
+            "gpu_launches": int(m["launches"]),
             "clocks": clocks,
         }
+        result["roofline"]["kernel_share"] = round(m["kern_share"], 4)
+        if head.collect_bytes():
+            cb = head.collect_bytes()
+            result["collective"] = {"op": "ncclAllGather (torch.distributed.all_gather_into_tensor)",
+                                    "bytes_received_per_gpu": cb, "ms_per_step": round(coll_ms, 5),
+                                    "algbw_gbs_per_gpu": round(cb / (coll_ms * 1e-3) / 1e9, 1),
+                                    "share_of_step": round(coll_ms / step_ms, 4)}
+        if e2e_t_ms:
+            result["e2e_tensor"] = {
+                "value": round(_rate(head, units, e2e_t_ms), 3),
+                "unit": head.unit, "ms_per_step": round(e2e_t_ms, 5),
+                "h2d_bytes_per_step": head.net.inputs[0].numel() * 4 * world,
+                "d2h_bytes_per_step": head.net.outputs[0].numel() * 4 * world,
+                "mode": "pipelined yolo.HostPipeline: each GPU copies its images' FP32 [B/N,3,640,640] tensor in and "
+                        "its FP32 [B/N,84,8400] output back (no gather)"}
+        if weak_ms_max:
+            result["weak"] = {"value": round(head.batch * world / (weak_ms_max * 1e-3), 3), "unit": head.unit,
+                              "ms_per_step": round(weak_ms_max, 5), "images_per_gpu": head.batch,
+                              "note": "secondary: every GPU its own batch, no collective"}
         if not args.no_cpu_baseline and world == 1:
-            cores = physical_cores()
-            base = wl.cpu_sample(cores)
-            base.update(kind="port", cpu=cpu_model())
-            try:
-                b4 = wl.cpu_sample(min(4, cores))
-                base["value_4_threads"] = b4["value"]
-            except Exception:  # pragma: no cover
-                pass
-            result["cpu_baseline"] = base
-    if graph is not None:
-        graph.close()
+            result["cpu_baseline"] = cpu_baseline(head, args.cpu_budget)
+        if sub:
+            cfgs = {}
+            off = 5
+            for key, (wl, r, K) in sub.items():
+                s_ms, e_ms, c_ms = vals[off:off + 3]
+                off += 3
+                u = wl.units_per_step()
+                bi, bo = wl.e2e_bytes()
+                entry = {"workload": wl.name, "value": round(_rate(wl, u, s_ms), 3), "unit": wl.unit,
+                         "ms_per_step": round(s_ms, 5), "steps": K,
+                         "scaling": "weak" if wl.replicas else "strong",
+                         "config": wl.config,
+                         "roofline": roofline(wl, r["kern_ms"], peaks, peaks_kind, load_traffic(wl.key)),
+                         "e2e": {"value": round(_rate(wl, u, e_ms), 3), "unit": wl.unit, "ms_per_step": round(e_ms, 5),
+                                 "h2d_bytes_per_step": bi, "d2h_bytes_per_step": bo, "mode": r["e2e_mode"]},
+                         "gpu_launches": int(r["launches"])}
+                entry["roofline"]["kernel_share"] = round(r["kern_share"], 4)
+                if wl.collect_bytes():
+                    entry["collective"] = {"bytes_received_per_gpu": wl.collect_bytes(), "ms_per_step": round(c_ms, 5)}
+                if not args.no_cpu_baseline and world == 1:
+                    entry["cpu_baseline"] = cpu_baseline(wl, args.cpu_budget / 4)
+                cfgs[key] = entry
+            result["configs"] = cfgs
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -718,84 +1020,91 @@ def run_ours(args, peaks, peaks_kind) -> dict | None:
 
 
 def run_reference(args) -> dict | None:
-    """Time the reference's CPU algorithm (oracle port) on the host cores."""
+    """Time the reference's CPU algorithm (the oracle port: the reference is C#) on the host cores."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return None
     cores = physical_cores()
     os.environ.setdefault("ONNXSHARP_THREADS", str(cores))
-
-    class _Ctx:  # the CPU arm needs no GPU context
-        pass
-
     wl = CPU_WORKLOADS[args.workload]()
+    budget = min(2.0, 90.0 / max(1, args.steps + args.warmup))
+    for _ in range(args.warmup):
+        wl.cpu_sample(cores, 0.0)
     vals = []
-    for _ in range(max(1, args.warmup)):
-        wl.cpu_sample(cores)
     t0 = time.perf_counter()
-    for _ in range(args.ref_steps):
-        vals.append(wl.cpu_sample(cores))
+    for _ in range(args.steps):
+        vals.append(wl.cpu_sample(cores, budget))
     dt = time.perf_counter() - t0
     value = statistics.median(v["value"] for v in vals)
     return {
         "metric": METRIC, "impl": "reference", "value": round(value, 5), "unit": wl.unit, "n_gpus": world,
-        "steps": args.ref_steps, "warmup": args.warmup, "ms_per_step": round(dt / args.ref_steps * 1e3, 3),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": wl.config,
         "cpu_baseline": {"value": round(value, 5), "unit": wl.unit, "cores": cores, "kind": "port",
-                         "sample": vals[0]["sample"], "cpu": cpu_model()},
+                         "sample": vals[0]["sample"], "cpu": cpu_model(),
+                         "reference_published": PUBLISHED.get(args.workload)},
         "e2e": {"value": round(value, 5), "unit": wl.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "reference is C# (OnnxSharp); no .NET runtime on this box, so the CPU restatement of its kernels "
                 "(oracle/) is timed with all physical cores",
     }
 
 
+# ----------------------------------------------------------------- CPU baselines (the oracle port)
 class CpuGemm:
+    """Config 1 through the oracle's GEMM (the reference's per-element FMA chain, register-blocked panels)."""
+
     unit = "TFLOP/s"
 
-    def __init__(self):
-        m, k, n = 2048, 512, 2048
-        rng = np.random.default_rng(1234)
-        self.a = rng.uniform(-1, 1, (m, k)).astype(np.float32)
-        self.b = rng.uniform(-1, 1, (k, n)).astype(np.float32)
-        self.bias = rng.uniform(-1, 1, n).astype(np.float32)
-        self.config = {"workload": GemmWorkload.name, "m": m, "k": k, "n": n, "bias": True}
+    def __init__(self, a=None, b=None, bias=None):
+        if a is None:
+            rng = np.random.default_rng(1234)
+            a = rng.uniform(-1, 1, (2048, 512)).astype(np.float32)
+            b = rng.uniform(-1, 1, (512, 2048)).astype(np.float32)
+            bias = rng.uniform(-1, 1, 2048).astype(np.float32)
+        self.a, self.b, self.bias = a, b, bias
+        self.config = {"workload": GemmWorkload.name, "m": 2048, "k": 512, "n": 2048, "bias": True}
 
-    def cpu_sample(self, threads):
+    def cpu_sample(self, threads, budget_s=1.0):
         import oracle
 
-        t0 = time.perf_counter()
-        oracle.gemm(self.a, self.b, col_bias=self.bias, threads=threads)
-        dt = time.perf_counter() - t0
-        return {"value": 2.0 * self.a.shape[0] * self.a.shape[1] * self.b.shape[1] / dt / 1e12,
-                "sample": "one full 2048x512x2048 GEMM+bias per step"}
+        reps, dt = _timed(lambda: oracle.gemm(self.a, self.b, col_bias=self.bias, threads=threads), budget_s)
+        flops = 2.0 * self.a.shape[0] * self.a.shape[1] * self.b.shape[1] * reps
+        return {"value": _tflops(flops / dt), "unit": self.unit, "cores": threads,
+                "sample": f"{reps} x full 2048x512x2048 GEMM+bias ({dt:.2f} s)"}
 
 
 class CpuConv:
-    """One image of BASELINE config 2 per step through the oracle's im2col-order conv + SiLU."""
+    """Config 2 images through the oracle's im2col-order conv + SiLU (one image per repetition)."""
 
     unit = "TFLOP/s"
 
-    def __init__(self, x=None, w=None, b=None):
+    def __init__(self, x=None, w=None, b=None, batch: int = 16):
         if x is None:
             x, w, b = conv_inputs(4321, 1)
-        self.x, self.w, self.b = x[:1], w, b
-        self.config = {"workload": ConvWorkload.name, "batch": 16, "in": [16, 64, 160, 160],
-                       "weight": [128, 64, 3, 3], "stride": 1, "pad": 1, "act": "SiLU"}
+        self.x, self.w, self.b, self.batch = x, w, b, batch
+        self.config = {"workload": f"conv3x3_silu_f32_b{batch}_64to128_160x160", "batch": batch,
+                       "in": [batch, 64, 160, 160], "weight": [128, 64, 3, 3], "stride": 1, "pad": 1, "act": "SiLU"}
 
-    def cpu_sample(self, threads):
+    def cpu_sample(self, threads, budget_s=1.0):
         import oracle
 
-        t0 = time.perf_counter()
-        oracle.conv2d(self.x, self.w, self.b, pads=(1, 1, 1, 1), act=1, threads=threads)
-        dt = time.perf_counter() - t0
-        return {"value": CONV_FLOPS_PER_IMAGE / dt / 1e12, "unit": self.unit, "cores": threads,
-                "sample": f"1 of 16 images per step (3x3 conv 64->128 @160x160 + SiLU), {dt:.2f} s"}
+        i = [0]
+
+        def one():
+            j = i[0] % self.x.shape[0]
+            oracle.conv2d(self.x[j:j + 1], self.w, self.b, pads=(1, 1, 1, 1), act=1, threads=threads)
+            i[0] += 1
+
+        reps, dt = _timed(one, budget_s)
+        return {"value": _tflops(CONV_FLOPS_PER_IMAGE * reps / dt), "unit": self.unit, "cores": threads,
+                "sample": f"{reps} image(s) of the batch of {self.batch} (3x3 conv 64->128 @160x160 + SiLU), "
+                          f"{dt:.2f} s"}
 
 
 class CpuDqmm:
-    """The full config-3 DynamicQuantizeMatMul per step through the oracle (F32-substitute GEMM, as the reference)."""
+    """The full config-3 DynamicQuantizeMatMul per repetition (F32-substitute GEMM, as the reference)."""
 
     unit = "TOP/s"
 
@@ -805,45 +1114,48 @@ class CpuDqmm:
         self.a, self.w, self.ws, self.b = a, w, ws, b
         self.config = {"workload": DqmmWorkload.name, "m": a.shape[0], "k": a.shape[1], "n": w.shape[1]}
 
-    def cpu_sample(self, threads):
+    def cpu_sample(self, threads, budget_s=1.0):
         import oracle
 
-        t0 = time.perf_counter()
-        oracle.dqmm(self.a, self.w, 0, self.ws, self.b, threads=threads)
-        dt = time.perf_counter() - t0
-        ops = 2.0 * self.a.shape[0] * self.a.shape[1] * self.w.shape[1]
-        return {"value": ops / dt / 1e12, "unit": self.unit, "cores": threads,
-                "sample": f"full {self.a.shape[0]}x{self.a.shape[1]}x{self.w.shape[1]} DQMM per step, {dt:.2f} s"}
+        reps, dt = _timed(lambda: oracle.dqmm(self.a, self.w, 0, self.ws, self.b, threads=threads), budget_s)
+        ops = 2.0 * self.a.shape[0] * self.a.shape[1] * self.w.shape[1] * reps
+        return {"value": _tflops(ops / dt), "unit": self.unit, "cores": threads,
+                "sample": f"{reps} x full {self.a.shape[0]}x{self.a.shape[1]}x{self.w.shape[1]} DQMM ({dt:.2f} s)"}
 
 
 class CpuYolo:
-    """One image per step through the oracle executor of the same plan."""
+    """Images through the oracle executor of the same plan (one image per repetition)."""
 
     unit = "images/s"
 
-    def __init__(self, g=None, params=None, images=None):
+    def __init__(self, g=None, params=None, images=None, batch: int = 64):
         from onnxsharp_b200 import yolo
 
         if g is None:
             g = yolo.build_yolo11n()
             params = yolo.init_params(g, 2024)
             images = np.random.default_rng(9000).uniform(0, 1, (1, 3, 640, 640)).astype(np.float32)
-        self.g, self.params, self.images = g, params, images[:1]
-        self.config = {"workload": YoloWorkload.name, "batch_per_gpu": 64, "input": [64, 3, 640, 640],
-                       "output": [64, 84, 8400]}
+        self.g, self.params, self.images, self.batch = g, params, images, batch
+        self.config = {"workload": f"yolo11n_shaped_b{batch}_640", "global_batch": batch,
+                       "input": [batch, 3, 640, 640], "output": [batch, 84, 8400]}
 
-    def cpu_sample(self, threads):
+    def cpu_sample(self, threads, budget_s=1.0):
         from oracle import yolo_ref
 
-        t0 = time.perf_counter()
-        yolo_ref.run(self.g, self.params, self.images, threads=threads)
-        dt = time.perf_counter() - t0
-        return {"value": 1.0 / dt, "unit": self.unit, "cores": threads,
-                "sample": f"1 image (of 64) per step through the plan, {dt:.2f} s"}
+        i = [0]
+
+        def one():
+            j = i[0] % self.images.shape[0]
+            yolo_ref.run(self.g, self.params, self.images[j:j + 1], threads=threads)
+            i[0] += 1
+
+        reps, dt = _timed(one, budget_s)
+        return {"value": reps / dt, "unit": self.unit, "cores": threads,
+                "sample": f"{reps} image(s) of the batch of {self.batch} through the plan, {dt:.2f} s"}
 
 
 class CpuAttention:
-    """8 of the 64 sequences per step through the oracle (projection GEMMs + ComputeBlocks)."""
+    """Sequences of config 4 through the oracle (projection GEMMs + ComputeBlocks), 8 per repetition."""
 
     unit = "TFLOP/s"
 
@@ -856,19 +1168,22 @@ class CpuAttention:
         self.x, self.ws = x[:8 * 128], ws
         self.config = {"workload": AttentionWorkload.name, "x": [64, 128, 512], "heads": 8, "head_dim": 64}
 
-    def cpu_sample(self, threads):
+    def cpu_sample(self, threads, budget_s=1.0):
         import oracle
 
-        t0 = time.perf_counter()
-        q, k, v = (oracle.gemm(self.x, w, threads=threads).reshape(8, 128, 512) for w in self.ws[:3])
-        o = oracle.attention(q, k, v, heads=8, scale=0.125, threads=threads)
-        oracle.gemm(o.reshape(8 * 128, 512), self.ws[3], threads=threads)
-        dt = time.perf_counter() - t0
-        return {"value": ATTN_FLOPS / 8 / dt / 1e12, "unit": self.unit, "cores": threads,
-                "sample": f"8 of 64 sequences per step, {dt:.2f} s"}
+        def one():
+            q, k, v = (oracle.gemm(self.x, w, threads=threads).reshape(8, 128, 512) for w in self.ws[:3])
+            o = oracle.attention(q, k, v, heads=8, scale=0.125, threads=threads)
+            oracle.gemm(o.reshape(8 * 128, 512), self.ws[3], threads=threads)
+
+        reps, dt = _timed(one, budget_s)
+        return {"value": _tflops(ATTN_FLOPS / 8 * reps / dt), "unit": self.unit, "cores": threads,
+                "sample": f"{reps} x 8 of the 64 sequences, {dt:.2f} s"}
 
 
-CPU_WORKLOADS = {"gemm": CpuGemm, "conv": CpuConv, "dqmm": CpuDqmm, "yolo": CpuYolo, "attention": CpuAttention}
+CPU_WORKLOADS = {"gemm": CpuGemm, "conv_b16": CpuConv, "conv_b1": lambda: CpuConv(batch=1), "dqmm": CpuDqmm,
+                 "yolo": CpuYolo, "yolo_b1": lambda: CpuYolo(batch=1), "yolo_b8": lambda: CpuYolo(batch=8),
+                 "attention": CpuAttention}
 
 
 def main() -> int:
@@ -876,22 +1191,22 @@ def main() -> int:
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--workload", default=DEFAULT_WORKLOAD, choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default=DEFAULT_WORKLOAD, choices=sorted(set(WORKLOADS) | set(ALIASES)))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--profile-steps", type=int, default=None,
-                    help="eager profiled steps for the dominant-kernel timing of graph-replayed workloads")
-    ap.add_argument("--ref-steps", type=int, default=5)
-    ap.add_argument("--traffic", type=float, default=None,
-                    help="dram bytes per dominant-kernel launch from an ncu capture (reported as-is)")
+                    help="eager profiled passes for the dominant-kernel timing of graph-replayed workloads")
+    ap.add_argument("--cpu-budget", type=float, default=12.0,
+                    help="seconds of CPU-baseline sampling for the headline (a quarter of it per other config)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-configs", action="store_true", help="time only the headline workload")
+    ap.add_argument("--no-weak", action="store_true", help="skip the secondary weak-scaling figure (N > 1)")
     args = ap.parse_args()
-    if args.traffic is None:
-        args.traffic = load_traffic(args.workload)
+    args.workload = ALIASES.get(args.workload, args.workload)
     if args.profile_steps is None:
-        args.profile_steps = 5 if args.workload == "yolo" else 50
+        args.profile_steps = 5 if args.workload.startswith("yolo") else 30
     if args.e2e_steps is None:
-        args.e2e_steps = {"yolo": 30, "conv": 50}.get(args.workload, 200)
+        args.e2e_steps = 30 if args.workload.startswith("yolo") else 100
     if args.steps is None:
         args.steps = DEFAULT_STEPS.get(args.workload, 100)
     args.warmup = max(3, args.warmup)

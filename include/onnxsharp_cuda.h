@@ -351,6 +351,15 @@ OSC_API int osc_matmul_integer_i8(osc_ctx* ctx, const void* a, int a_signed, int
 OSC_API int osc_letterbox_u8(osc_ctx* ctx, const uint8_t* pixels, int width, int height, int row_stride,
                              int bytes_per_pixel, int bgr, int target_w, int target_h, float* dst, int* placement);
 
+/* osc_letterbox_u8 over a batch of B frames of one size (a camera batch), one
+ * launch: frame z at pixels + z * image_stride bytes (0 = row_stride * height)
+ * -> dst + z * dst_nstride floats (0 = 3 * target_h * target_w), each
+ * bit-identical to osc_letterbox_u8 on that frame. placement as there (the
+ * same for every frame). */
+OSC_API int osc_letterbox_batch_u8(osc_ctx* ctx, const uint8_t* pixels, int B, long long image_stride, int width,
+                                   int height, int row_stride, int bytes_per_pixel, int bgr, int target_w,
+                                   int target_h, float* dst, long long dst_nstride, int* placement);
+
 /* The YOLO detect tail (YoloDecoder.Decode + DetectionNms.SuppressSorted,
  * Vision/YoloDecoder.cs:68-188, Vision/Detection.cs:62-107) on the device, one
  * image per CTA: output [B, fields, anchors] channels-first (fields = 4 +

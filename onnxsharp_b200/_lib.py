@@ -73,6 +73,7 @@ SIGNATURES: dict[str, tuple] = {
     "osc_selfcheck_timeout": (i32, [vp, i32]),
     "osc_dynamic_quantize_linear_f32": (i32, [vp, vp, i64, vp, vp, vp]),
     "osc_letterbox_u8": (i32, [vp, vp, i32, i32, i32, i32, i32, i32, i32, vp, C.POINTER(i32)]),
+    "osc_letterbox_batch_u8": (i32, [vp, vp, i32, i64, i32, i32, i32, i32, i32, i32, i32, vp, i64, C.POINTER(i32)]),
     "osc_yolo_detect_f32": (i32, [vp, vp, i32, i32, i32, C.c_float, C.c_float, i32, i32, i32, vp, vp, vp]),
     "osc_matmul_batched_f32": (i32, [vp, i32, i32, i32, i32, i32, vp, i64, i64, i64, i64, vp, i64, i64, i64, i64, vp,
                                      vp]),

@@ -31,9 +31,13 @@ struct LetterboxArgs {
   float pad, gain, bias;
 };
 
+// One image per blockIdx.y: image z reads px + z * px_stride bytes and writes
+// dst + z * dst_stride floats.
 __global__ void k_letterbox(const uint8_t* __restrict__ px, const __grid_constant__ LetterboxArgs a,
-                            float* __restrict__ dst) {
+                            float* __restrict__ dst, long long px_stride, long long dst_stride) {
   const long plane = static_cast<long>(a.th) * a.tw;
+  px += blockIdx.y * px_stride;
+  dst += blockIdx.y * dst_stride;
   for (long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < plane;
        i += static_cast<long>(gridDim.x) * blockDim.x) {
     const int y = static_cast<int>(i / a.tw), x = static_cast<int>(i - static_cast<long>(y) * a.tw);
@@ -258,49 +262,87 @@ __global__ void __launch_bounds__(kDetThreads, 1)
 
 using namespace osc;
 
-extern "C" {
+namespace {
 
-OSC_API int osc_letterbox_u8(osc_ctx* ctx, const uint8_t* pixels, int width, int height, int row_stride,
-                             int bytes_per_pixel, int bgr, int target_w, int target_h, float* dst, int* placement) {
-  OSC_TRY(enter(ctx));
+// ImageGeometry.Contain (Imaging/AxisMap.cs:97-112) in the reference's float
+// arithmetic, plus the Divide255 normalisation and the 114 grey pad.
+int letterbox_args(int width, int height, int row_stride, int bytes_per_pixel, int bgr, int target_w, int target_h,
+                   LetterboxArgs* a) {
   if (width <= 0 || height <= 0 || target_w <= 0 || target_h <= 0 || (bytes_per_pixel != 3 && bytes_per_pixel != 4))
-    return fail(OSC_EINVAL, "osc_letterbox_u8: bad geometry");
-  if (row_stride == 0) row_stride = width * bytes_per_pixel;
-  if (row_stride < width * bytes_per_pixel) return fail(OSC_EINVAL, "osc_letterbox_u8: row_stride %d", row_stride);
-  if (pixels == nullptr || dst == nullptr) return fail(OSC_EINVAL, "osc_letterbox_u8: null pointer");
-  if (fault_injected("launch")) return fail(OSC_EFAULT_INJECTED, "injected failure (launch)");
-  // ImageGeometry.Contain (AxisMap.cs:97-112), in the reference's float arithmetic
+    return fail(OSC_EINVAL, "letterbox: bad geometry");
+  if (row_stride < width * bytes_per_pixel) return fail(OSC_EINVAL, "letterbox: row_stride %d", row_stride);
   const float gx = static_cast<float>(target_w) / static_cast<float>(width);
   const float gy = static_cast<float>(target_h) / static_cast<float>(height);
   const float gain = std::min(gx, gy);
   const int rw = std::clamp(static_cast<int>(std::nearbyint(static_cast<float>(width) * gain)), 1, target_w);
   const int rh = std::clamp(static_cast<int>(std::nearbyint(static_cast<float>(height) * gain)), 1, target_h);
-  LetterboxArgs a{};
-  a.width = width;
-  a.height = height;
-  a.row_stride = row_stride;
-  a.bpp = bytes_per_pixel;
-  a.bgr = bgr ? 1 : 0;
-  a.tw = target_w;
-  a.th = target_h;
-  a.rw = rw;
-  a.rh = rh;
-  a.ox = (target_w - rw) / 2;
-  a.oy = (target_h - rh) / 2;
-  a.pad = 114.0f / 255.0f;
-  a.gain = 1.0f / (255.0f * 1.0f);  // Divide255: 1 / (255 * std)
-  a.bias = -0.0f / 1.0f;            // -mean / std
+  *a = LetterboxArgs{};
+  a->width = width;
+  a->height = height;
+  a->row_stride = row_stride;
+  a->bpp = bytes_per_pixel;
+  a->bgr = bgr ? 1 : 0;
+  a->tw = target_w;
+  a->th = target_h;
+  a->rw = rw;
+  a->rh = rh;
+  a->ox = (target_w - rw) / 2;
+  a->oy = (target_h - rh) / 2;
+  a->pad = 114.0f / 255.0f;
+  a->gain = 1.0f / (255.0f * 1.0f);  // Divide255: 1 / (255 * std)
+  a->bias = -0.0f / 1.0f;            // -mean / std
+  return OSC_OK;
+}
+
+int letterbox_launch(osc_ctx* ctx, const uint8_t* pixels, int B, long long image_stride, const LetterboxArgs& a,
+                     float* dst, long long dst_stride, int* placement) {
   if (placement != nullptr) {
-    placement[0] = rw;
-    placement[1] = rh;
+    placement[0] = a.rw;
+    placement[1] = a.rh;
     placement[2] = a.ox;
     placement[3] = a.oy;
   }
-  const long plane = static_cast<long>(target_h) * target_w;
-  const int blocks = static_cast<int>(std::min<long>((plane + 255) / 256, static_cast<long>(ctx->num_sms) * 16));
+  const long plane = static_cast<long>(a.th) * a.tw;
+  long blocks = std::min<long>((plane + 255) / 256, static_cast<long>(ctx->num_sms) * 16);
+  blocks = std::max<long>(1, std::min<long>(blocks, (static_cast<long>(ctx->num_sms) * 16 + B - 1) / B));
   prof_begin(ctx);
-  k_letterbox<<<blocks, 256, 0, ctx->stream>>>(pixels, a, dst);
+  k_letterbox<<<dim3(static_cast<unsigned>(blocks), static_cast<unsigned>(B)), 256, 0, ctx->stream>>>(
+      pixels, a, dst, image_stride, dst_stride);
   return check_launch(ctx, "k_letterbox");
+}
+
+}  // namespace
+
+extern "C" {
+
+OSC_API int osc_letterbox_u8(osc_ctx* ctx, const uint8_t* pixels, int width, int height, int row_stride,
+                             int bytes_per_pixel, int bgr, int target_w, int target_h, float* dst, int* placement) {
+  OSC_TRY(enter(ctx));
+  if (row_stride == 0) row_stride = width * bytes_per_pixel;
+  LetterboxArgs a;
+  OSC_TRY(letterbox_args(width, height, row_stride, bytes_per_pixel, bgr, target_w, target_h, &a));
+  if (pixels == nullptr || dst == nullptr) return fail(OSC_EINVAL, "osc_letterbox_u8: null pointer");
+  if (fault_injected("launch")) return fail(OSC_EFAULT_INJECTED, "injected failure (launch)");
+  return letterbox_launch(ctx, pixels, 1, 0, a, dst, 0, placement);
+}
+
+OSC_API int osc_letterbox_batch_u8(osc_ctx* ctx, const uint8_t* pixels, int B, long long image_stride, int width,
+                                   int height, int row_stride, int bytes_per_pixel, int bgr, int target_w,
+                                   int target_h, float* dst, long long dst_nstride, int* placement) {
+  OSC_TRY(enter(ctx));
+  if (B < 0 || B > 65535) return fail(OSC_EINVAL, "osc_letterbox_batch_u8: B=%d", B);
+  if (row_stride == 0) row_stride = width * bytes_per_pixel;
+  LetterboxArgs a;
+  OSC_TRY(letterbox_args(width, height, row_stride, bytes_per_pixel, bgr, target_w, target_h, &a));
+  if (image_stride == 0) image_stride = static_cast<long long>(row_stride) * height;
+  if (dst_nstride == 0) dst_nstride = 3ll * target_w * target_h;
+  if (image_stride < static_cast<long long>(row_stride) * height || dst_nstride < 3ll * target_w * target_h)
+    return fail(OSC_EINVAL, "osc_letterbox_batch_u8: image_stride %lld / dst_nstride %lld too small", image_stride,
+                dst_nstride);
+  if (B == 0) return OSC_OK;
+  if (pixels == nullptr || dst == nullptr) return fail(OSC_EINVAL, "osc_letterbox_batch_u8: null pointer");
+  if (fault_injected("launch")) return fail(OSC_EFAULT_INJECTED, "injected failure (launch)");
+  return letterbox_launch(ctx, pixels, B, image_stride, a, dst, dst_nstride, placement);
 }
 
 OSC_API int osc_yolo_detect_f32(osc_ctx* ctx, const float* output, int B, int fields, int anchors, float conf,

@@ -126,6 +126,25 @@ def letterbox(ctx, pixels, dst, bgr: bool = False):
     return tuple(pl)
 
 
+def letterbox_batch(ctx, frames, dst, bgr: bool = False):
+    """Letterbox a [B, H, W, 3|4] uint8 device batch of frames into dst [B, 3, th, tw] (or channel-
+    complete views of it) in one launch; returns the placement shared by every frame."""
+    B, h, w, bpp = frames.shape
+    _, _, th, tw = dst.shape
+    pl = (C.c_int * 4)()
+    call("osc_letterbox_batch_u8", ctx.handle, ptr(frames), B, int(frames.stride(0)), w, h, int(frames.stride(1)),
+         bpp, int(bgr), tw, th, ptr(dst), int(dst.stride(0)), pl)
+    return tuple(pl)
+
+
+def yolo_detect_into(ctx, output, dets, counts, conf: float = 0.25, iou: float = 0.45, max_candidates: int = 30000,
+                     class_agnostic: bool = False, transforms=None):
+    """osc_yolo_detect_f32 into caller buffers dets [B, max_det, 6] and counts [B] (int32)."""
+    B, fields, anchors = output.shape
+    call("osc_yolo_detect_f32", ctx.handle, ptr(output), B, fields, anchors, float(conf), float(iou),
+         int(dets.shape[1]), max_candidates, int(class_agnostic), ptr(transforms), ptr(dets), ptr(counts))
+
+
 def yolo_detect(ctx, output, conf: float = 0.25, iou: float = 0.45, max_det: int = 300, max_candidates: int = 30000,
                 class_agnostic: bool = False, transforms=None):
     """Detections of a [B, 4 + nc, A] output: (dets [B, max_det, 6] (class, score, x, y, w, h), counts [B])."""

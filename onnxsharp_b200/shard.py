@@ -22,16 +22,22 @@ def shard_range(n: int, world: int, rank: int) -> tuple[int, int]:
 
 def global_minmax(local, group=None):
     """All-reduce a local {min, max} pair (a 2-element float tensor on the
-    rank's device, or CPU for gloo) into the global range, in place."""
+    rank's device, or CPU for gloo) into the global range, in place, with ONE
+    collective: {-min, max} reduced by MAX (negation is exact, so the result
+    is the exact global minimum and maximum)."""
     import torch
     import torch.distributed as dist
 
-    lo = local[0:1].clone()
-    hi = local[1:2].clone()
-    dist.all_reduce(lo, op=dist.ReduceOp.MIN, group=group)
-    dist.all_reduce(hi, op=dist.ReduceOp.MAX, group=group)
-    local.copy_(torch.cat([lo, hi]))
+    sign = _SIGNS.get(local.device)
+    if sign is None:
+        sign = _SIGNS[local.device] = torch.tensor([-1.0, 1.0], dtype=local.dtype, device=local.device)
+    t = local * sign
+    dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+    torch.mul(t, sign, out=local)
     return local
+
+
+_SIGNS: dict = {}
 
 
 def max_over_ranks(values, group=None):

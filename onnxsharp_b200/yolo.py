@@ -297,6 +297,7 @@ class Net:
             if node.op == "conv" and self.tensor_core(node):
                 self.packed[node.name] = ConvWeights(ctx, self.dev_params[node.name + ".w"], g.params[node.name + ".w"])
         self.graphs = [None]
+        self.extra_graphs = []
         self.stream = None
 
     @staticmethod
@@ -403,6 +404,53 @@ class Net:
             self._bind(0)
             self.ctx.set_stream(prev)
 
+    def capture_slot(self, slot: int, before=None, after=None):
+        """Capture one CUDA graph that runs before(), the plan for `slot`, then
+        after() on the plan's stream (e.g. letterbox pre-processing and the
+        detect tail around the forward pass); returns the osc_graph handle, which
+        close() frees. The launches run once eagerly first (scratch sizes,
+        kernel attributes)."""
+        import ctypes as C
+
+        from ._lib import call
+
+        prev = self.ctx.get_stream()
+        self.ctx.set_stream(self.plan_stream().cuda_stream)
+        self._bind(slot)
+
+        def body():
+            if before is not None:
+                before()
+            self._run_nodes()
+            if after is not None:
+                after()
+
+        try:
+            body()
+            self.ctx.synchronize()
+            call("osc_graph_begin", self.ctx.handle)
+            h = C.c_void_p()
+            try:
+                body()
+            finally:
+                call("osc_graph_end", self.ctx.handle, C.byref(h))
+            self.extra_graphs.append(h)
+            return h
+        finally:
+            self._bind(0)
+            self.ctx.set_stream(prev)
+
+    def launch_graph(self, handle) -> None:
+        """Replay a graph from capture_slot on the plan's stream."""
+        from ._lib import call
+
+        prev = self.ctx.get_stream()
+        self.ctx.set_stream(self.plan_stream().cuda_stream)
+        try:
+            call("osc_graph_launch", self.ctx.handle, handle)
+        finally:
+            self.ctx.set_stream(prev)
+
     def forward(self, use_graph: bool = True, slot: int = 0):
         """Run the plan on the contents of input_view(slot); returns the slot's [B, 84, A] output tensor.
 
@@ -424,6 +472,9 @@ class Net:
             if h is not None:
                 _lib.load().osc_graph_free(h)
                 self.graphs[i] = None
+        for h in self.extra_graphs:
+            _lib.load().osc_graph_free(h)
+        self.extra_graphs = []
 
 
 class HostPipeline:

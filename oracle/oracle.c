@@ -11,6 +11,7 @@
  */
 #include "oracle.h"
 
+#include <immintrin.h>
 #include <math.h>
 #include <omp.h>
 #include <stdlib.h>
@@ -71,41 +72,120 @@ static int grouped_rows(int m, int mr12) {
   return row;
 }
 
+/* Register-blocked accumulation: acc[r][0..15] (row pitch ldacc) for R <= 6
+ * rows continues, for t = 0..K-1 in ascending order, the per-element chain
+ * acc = fma(A[r][t], B[t][j], acc) (A row r at A + r*lda, B row t at B + t*ldb).
+ * Each lane of _mm256_fmadd_ps is one fmaf, so every element's chain and
+ * rounding are those of the scalar loop; only the loop nest is blocked, as the
+ * reference's 12/6-row x 16-column micro-kernels block it
+ * (GemmKernel.cs:1070-1304). */
+static inline __attribute__((always_inline)) void mk_rows(int R, const float* A, long lda, const float* B, long ldb,
+                                                         int K, float* acc, long ldacc) {
+  __m256 c0[6], c1[6];
+  for (int r = 0; r < 6; ++r) {
+    if (r < R) {
+      c0[r] = _mm256_loadu_ps(acc + r * ldacc);
+      c1[r] = _mm256_loadu_ps(acc + r * ldacc + 8);
+    }
+  }
+  for (int t = 0; t < K; ++t) {
+    const __m256 b0 = _mm256_loadu_ps(B + (long)t * ldb);
+    const __m256 b1 = _mm256_loadu_ps(B + (long)t * ldb + 8);
+    for (int r = 0; r < 6; ++r) {
+      if (r < R) {
+        const __m256 av = _mm256_broadcast_ss(A + r * lda + t);
+        c0[r] = _mm256_fmadd_ps(av, b0, c0[r]);
+        c1[r] = _mm256_fmadd_ps(av, b1, c1[r]);
+      }
+    }
+  }
+  for (int r = 0; r < 6; ++r) {
+    if (r < R) {
+      _mm256_storeu_ps(acc + r * ldacc, c0[r]);
+      _mm256_storeu_ps(acc + r * ldacc + 8, c1[r]);
+    }
+  }
+}
+
+static void mk_block(int R, const float* A, long lda, const float* B, long ldb, int K, float* acc, long ldacc) {
+  switch (R) {
+    case 6: mk_rows(6, A, lda, B, ldb, K, acc, ldacc); break;
+    case 5: mk_rows(5, A, lda, B, ldb, K, acc, ldacc); break;
+    case 4: mk_rows(4, A, lda, B, ldb, K, acc, ldacc); break;
+    case 3: mk_rows(3, A, lda, B, ldb, K, acc, ldacc); break;
+    case 2: mk_rows(2, A, lda, B, ldb, K, acc, ldacc); break;
+    default: mk_rows(1, A, lda, B, ldb, K, acc, ldacc); break;
+  }
+}
+
+/* acc[r][j] for r < R, j < J (pitch ldacc): full 16-column panels through the
+ * blocked kernel, the remaining columns through the scalar chain. */
+static void accumulate(int R, int J, const float* A, long lda, const float* B, long ldb, int K, float* acc,
+                       long ldacc) {
+  const int J16 = J / 16 * 16;
+  for (int j = 0; j < J16; j += 16) mk_block(R, A, lda, B + j, ldb, K, acc + j, ldacc);
+  for (int r = 0; r < R; ++r)
+    for (int j = J16; j < J; ++j) {
+      float v = acc[r * ldacc + j];
+      for (int t = 0; t < K; ++t) v = fmaf(A[r * lda + t], B[(long)t * ldb + j], v);
+      acc[r * ldacc + j] = v;
+    }
+}
+
+enum { kGemmCols = 128 };
+
 void orc_gemm_f32(const float* a, int lda, const float* b, int ldb, int m, int k, int n, const float* row_bias,
                   const float* col_bias, const float* col_scale, int mr12, int act, float* c, int ldc, int threads) {
   const int fused_rows = col_scale ? grouped_rows(m, mr12) : m;
   const int full_cols = (n / 16) * 16;
+  const long nrb = (m + 5) / 6, ncb = (n + kGemmCols - 1) / kGemmCols;
+  /* B's full 16-column panels packed [n/16][k][16] (GemmKernel.Pack, :418-438), so a
+   * panel's k rows are contiguous */
+  float* bp = (float*)malloc(sizeof(float) * (size_t)(full_cols > 0 ? full_cols : 1) * (k > 0 ? k : 1));
 #pragma omp parallel num_threads(nthreads(threads))
   {
-    float* acc = (float*)malloc(sizeof(float) * (size_t)(n > 0 ? n : 1));
+    float acc[6 * kGemmCols];
 #pragma omp for schedule(static)
-    for (int i = 0; i < m; ++i) {
-      for (int j = 0; j < n; ++j)
-        acc[j] = col_scale ? 0.0f : (col_bias ? col_bias[j] : (row_bias ? row_bias[i] : 0.0f));
-      const float* ai = a + (size_t)i * lda;
-      for (int t = 0; t < k; ++t) {
-        const float av = ai[t];
-        const float* bt = b + (size_t)t * ldb;
-        for (int j = 0; j < n; ++j) acc[j] = fmaf(av, bt[j], acc[j]);
-      }
-      float* ci = c + (size_t)i * ldc;
-      if (col_scale) {
-        for (int j = 0; j < n; ++j) {
+    for (long pt = 0; pt < (long)(full_cols / 16) * k; ++pt) {
+      const long p = pt / k, t = pt % k;
+      memcpy(bp + (p * k + t) * 16, b + (size_t)t * ldb + p * 16, 16 * sizeof(float));
+    }
+    /* column block outer: a thread's consecutive row blocks reuse B's k x 128 block from cache */
+#pragma omp for schedule(static)
+    for (long task = 0; task < nrb * ncb; ++task) {
+      const int i0 = (int)(task % nrb) * 6, j0 = (int)(task / nrb) * kGemmCols;
+      const int R = m - i0 < 6 ? m - i0 : 6, J = n - j0 < kGemmCols ? n - j0 : kGemmCols;
+      for (int r = 0; r < R; ++r)
+        for (int jj = 0; jj < J; ++jj) {
+          const int i = i0 + r, j = j0 + jj;
+          acc[r * kGemmCols + jj] = col_scale ? 0.0f : (col_bias ? col_bias[j] : (row_bias ? row_bias[i] : 0.0f));
+        }
+      const int J16 = (j0 + J <= full_cols) ? J : full_cols - j0;
+      for (int jj = 0; jj < J16; jj += 16)
+        mk_block(R, a + (size_t)i0 * lda, lda, bp + (size_t)(j0 + jj) * k, 16, k, acc + jj, kGemmCols);
+      if (J16 < J)
+        accumulate(R, J - J16, a + (size_t)i0 * lda, lda, b + j0 + J16, ldb, k, acc + J16, kGemmCols);
+      for (int r = 0; r < R; ++r) {
+        const int i = i0 + r;
+        float* ci = c + (size_t)i * ldc;
+        for (int jj = 0; jj < J; ++jj) {
+          const int j = j0 + jj;
+          const float s = acc[r * kGemmCols + jj];
           float v;
-          if (i < fused_rows && j < full_cols) {
-            v = fmaf(acc[j], col_scale[j], col_bias ? col_bias[j] : 0.0f); /* Multiply12Rows epilogue :1210-1241 */
+          if (!col_scale) {
+            v = s;
+          } else if (i < fused_rows && j < full_cols) {
+            v = fmaf(s, col_scale[j], col_bias ? col_bias[j] : 0.0f); /* Multiply12Rows epilogue :1210-1241 */
           } else {
-            v = acc[j] * col_scale[j]; /* ScaleColumns :1594-1608 */
+            v = s * col_scale[j]; /* ScaleColumns :1594-1608 */
             if (col_bias) v = v + col_bias[j];
           }
           ci[j] = act_apply(v, act);
         }
-      } else {
-        for (int j = 0; j < n; ++j) ci[j] = act_apply(acc[j], act);
       }
     }
-    free(acc);
   }
+  free(bp);
 }
 
 void orc_minmax(const float* x, long n, float* out_min, float* out_max) {
@@ -206,36 +286,39 @@ void orc_conv2d(const float* x, int N, int C, int H, int W, const float* w, int 
                 int pt, int pl, int dh, int dw, int group, const float* bias, int act, float* y, int OH, int OW,
                 int threads) {
   const int cpg = C / group, mpg = M / group;
+  const int K = cpg * kh * kw; /* im2col row order (ic, ky, kx), ConvKernels.cs:262-462 */
   const long tasks = (long)N * group * OH;
 #pragma omp parallel num_threads(nthreads(threads))
   {
     float* accb = (float*)malloc(sizeof(float) * (size_t)mpg * OW);
-    float* col = (float*)malloc(sizeof(float) * (size_t)OW);
+    float* col = (float*)malloc(sizeof(float) * (size_t)K * OW);
 #pragma omp for schedule(static)
     for (long task = 0; task < tasks; ++task) {
       const int oy = (int)(task % OH);
       const int g = (int)((task / OH) % group);
       const int nb = (int)(task / ((long)OH * group));
-      for (int o = 0; o < mpg; ++o) {
-        const float b0 = bias ? bias[g * mpg + o] : 0.0f;
-        for (int ox = 0; ox < OW; ++ox) accb[(size_t)o * OW + ox] = b0;
-      }
-      for (int ic = 0; ic < cpg; ++ic) {
+      for (int ic = 0; ic < cpg; ++ic) { /* FillColumns (:525-654): zero outside the image */
         const float* xc = x + ((size_t)nb * C + (size_t)g * cpg + ic) * H * W;
         for (int ky = 0; ky < kh; ++ky) {
           const int iy = oy * sh - pt + ky * dh;
           for (int kx = 0; kx < kw; ++kx) {
+            float* cr = col + (size_t)((ic * kh + ky) * kw + kx) * OW;
             for (int ox = 0; ox < OW; ++ox) {
               const int ix = ox * sw - pl + kx * dw;
-              col[ox] = (iy >= 0 && iy < H && ix >= 0 && ix < W) ? xc[(size_t)iy * W + ix] : 0.0f; /* FillColumns */
-            }
-            for (int o = 0; o < mpg; ++o) {
-              const float wv = w[(((size_t)(g * mpg + o) * cpg + ic) * kh + ky) * kw + kx];
-              float* ao = accb + (size_t)o * OW;
-              for (int ox = 0; ox < OW; ++ox) ao[ox] = fmaf(wv, col[ox], ao[ox]);
+              cr[ox] = (iy >= 0 && iy < H && ix >= 0 && ix < W) ? xc[(size_t)iy * W + ix] : 0.0f;
             }
           }
         }
+      }
+      for (int o = 0; o < mpg; ++o) {
+        const float b0 = bias ? bias[g * mpg + o] : 0.0f;
+        for (int ox = 0; ox < OW; ++ox) accb[(size_t)o * OW + ox] = b0;
+      }
+      /* acc[o][ox] from the row bias, then fma(W[o][t], col[t][ox], acc) for t ascending */
+      const float* wg = w + (size_t)g * mpg * K;
+      for (int o0 = 0; o0 < mpg; o0 += 6) {
+        const int R = mpg - o0 < 6 ? mpg - o0 : 6;
+        accumulate(R, OW, wg + (size_t)o0 * K, K, col, OW, K, accb + (size_t)o0 * OW, OW);
       }
       for (int o = 0; o < mpg; ++o) {
         float* yo = y + (((size_t)nb * M + (size_t)g * mpg + o) * OH + oy) * OW;

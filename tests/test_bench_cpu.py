@@ -20,7 +20,7 @@ def _run(extra_env=None, *args):
 
 
 def test_reference_arm_prints_contract_line():
-    r = _run({"ONNXSHARP_THREADS": "4"}, "--workload", "gemm", "--warmup", "3", "--ref-steps", "1")
+    r = _run({"ONNXSHARP_THREADS": "4"}, "--workload", "gemm", "--warmup", "3", "--steps", "2")
     assert r.returncode == 0, r.stderr[-2000:]
     lines = [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
     assert len(lines) == 1
@@ -32,9 +32,11 @@ def test_reference_arm_prints_contract_line():
     assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["d2h_bytes_per_step"] == 0
     cb = d["cpu_baseline"]
     assert cb["kind"] == "port" and cb["cores"] >= 1 and cb["value"] == d["value"] and cb["sample"]
+    assert cb["reference_published"]["source"] == "bench.md:961-970"
+    assert d["steps"] == 2
 
 
 def test_reference_arm_other_ranks_are_silent():
-    r = _run({"RANK": "1", "WORLD_SIZE": "2"}, "--workload", "gemm", "--warmup", "3", "--ref-steps", "1")
+    r = _run({"RANK": "1", "WORLD_SIZE": "2"}, "--workload", "gemm", "--warmup", "3", "--steps", "2")
     assert r.returncode == 0, r.stderr[-2000:]
     assert not [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
