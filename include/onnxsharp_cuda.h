@@ -128,6 +128,39 @@ OSC_API int osc_free(osc_ctx* ctx, void* ptr);
 OSC_API int osc_memcpy_htod(osc_ctx* ctx, void* dst, const void* src, size_t bytes);
 OSC_API int osc_memcpy_dtoh(osc_ctx* ctx, void* dst, const void* src, size_t bytes);
 
+/* ------------------------------------------------------------ several GPUs of one node
+ * Batch-level inference sharded by image / row / sequence over the GPUs of a
+ * node, driven from ONE host process (a C# host keeps one Net): a context per
+ * GPU (osc_group_ctx; use it like any context, it is owned by the group) and
+ * an NCCL communicator clique among them. The reference has no multi-device
+ * path; its contract that one Forward() returns the whole batch's output
+ * (src/OnnxSharp/Core/Net.cs:258-262) is kept by all-gathering the shards.
+ * NCCL is loaded at run time (libnccl.so.2); without it these entries return
+ * OSC_ENCCL and everything else still works. Work is enqueued on each
+ * context's stream; osc_group_synchronize waits for all of them. */
+typedef struct osc_group osc_group;
+OSC_API int osc_group_create(int ndev, const int* devices, osc_group** out);
+OSC_API int osc_group_destroy(osc_group* g);
+OSC_API int osc_group_size(osc_group* g, int* n);
+OSC_API int osc_group_ctx(osc_group* g, int rank, osc_ctx** out);
+OSC_API int osc_group_synchronize(osc_group* g, int timeout_ms);
+
+/* All-gather: `bytes` from send[r] (a device buffer of rank r's GPU) land at
+ * recv[i] + r * bytes on every rank i (recv[i] holds ndev * bytes). */
+OSC_API int osc_group_allgather(osc_group* g, const void* const* send, void* const* recv, size_t bytes);
+
+/* DynamicQuantizeMatMul over row shards: minmax[r] (2 device floats on rank
+ * r, from osc_minmax_f32 on that rank's rows) becomes the global {min, max}
+ * on every rank, so each shard's osc_dqmm_f32(..., minmax_override = minmax[r])
+ * quantises exactly as the whole tensor would (QuantizedMatMulOps.cs:146-156). */
+OSC_API int osc_group_allreduce_minmax(osc_group* g, float* const* minmax);
+
+/* One sharded step: on every rank r, replay graphs[r] (the plan over that
+ * GPU's shard, captured on osc_group_ctx(g, r)), then all-gather the shard
+ * outputs shard_out[r] (shard_bytes each) into gathered_out[r]. */
+OSC_API int osc_group_run_sharded(osc_group* g, const osc_graph* const* graphs, const void* const* shard_out,
+                                  void* const* gathered_out, size_t shard_bytes);
+
 /* ------------------------------------------------------------ MatMul (+FusedBias)
  * Replaces MatMulLayer.Forward with FusedBias (src/OnnxSharp/Ops/DnnOps.cs:2789-3102)
  * over GemmKernel.Pack / MultiplyPacked (src/OnnxSharp/Tensors/GemmKernel.cs:503, :675-852).

@@ -83,6 +83,14 @@ SIGNATURES: dict[str, tuple] = {
     "osc_graph_end": (i32, [vp, pp]),
     "osc_graph_launch": (i32, [vp, vp]),
     "osc_graph_free": (i32, [vp]),
+    "osc_group_create": (i32, [i32, C.POINTER(i32), pp]),
+    "osc_group_destroy": (i32, [vp]),
+    "osc_group_size": (i32, [vp, C.POINTER(i32)]),
+    "osc_group_ctx": (i32, [vp, i32, pp]),
+    "osc_group_synchronize": (i32, [vp, i32]),
+    "osc_group_allgather": (i32, [vp, pp, pp, sz]),
+    "osc_group_allreduce_minmax": (i32, [vp, pp]),
+    "osc_group_run_sharded": (i32, [vp, pp, pp, pp, sz]),
     "osc_malloc": (i32, [vp, sz, pp]),
     "osc_free": (i32, [vp, vp]),
     "osc_memcpy_htod": (i32, [vp, vp, vp, sz]),

@@ -150,8 +150,9 @@ __global__ void __launch_bounds__(kDetThreads, 1)
     const float x = out[a], y = out[d.anchors + a], w = out[2 * d.anchors + a], h = out[3 * d.anchors + a];
     if (!isfinite(x) || !isfinite(y) || !isfinite(w) || !isfinite(h) || w <= 0.0f || h <= 0.0f) continue;
     const int slot = atomicAdd(&n_cand, 1);
-    // descending score, then ascending anchor: sort ascending on (~score key, anchor)
-    keys[slot] = (static_cast<unsigned long long>(~orderable(score)) << 32) | static_cast<unsigned long long>(a);
+    // descending score, then ascending anchor: sort ascending on (~score key, anchor, class)
+    keys[slot] = (static_cast<unsigned long long>(~orderable(score)) << 32) |
+                 (static_cast<unsigned long long>(a) << 16) | static_cast<unsigned long long>(cls);
   }
   __syncthreads();
   const int nc = n_cand;
@@ -176,52 +177,60 @@ __global__ void __launch_bounds__(kDetThreads, 1)
       __syncthreads();
     }
   }
-  // 3. greedy NMS in score order, one warp: lanes test the kept boxes, a ballot decides
+  // 3. greedy NMS in score order, a chunk of kDetThreads candidates at a time
+  // (one per thread). A candidate is suppressed when its IoU with a kept box of
+  // its class (any class if class_agnostic) exceeds the threshold. Each thread
+  // first tests its candidate against the boxes kept from earlier chunks; then
+  // the chunk is resolved in order: the lowest-index surviving candidate is
+  // kept and every later candidate of the chunk is tested against it, until no
+  // candidate survives. The decisions are those of the one-at-a-time greedy
+  // loop (DetectionNms.SuppressSorted): each candidate meets exactly the boxes
+  // kept before it, in the same order, and the loop stops at max_det kept.
   const int ncand = min(nc, d.max_candidates);
   const int keep_cap = min(d.max_det, kMaxKeep);
-  if (tid < 32) {
-    const int lane = tid;
-    int nk = 0;
-    for (int i = 0; i < ncand && nk < keep_cap; ++i) {
-      const int a = static_cast<int>(keys[i] & 0xFFFFFFFFull);
-      // class and score of the candidate: the first maximum again, over the lanes
-      float best = -INFINITY;
-      int cls = 0;
-      for (int c = 4 + lane; c < d.fields; c += 32) {
-        const float v = out[static_cast<size_t>(c) * d.anchors + a];
-        if (v > best) {
-          best = v;
-          cls = c - 4;
-        }
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {  // max, ties to the lower class index
-        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-        const int oc = __shfl_xor_sync(0xffffffffu, cls, o);
-        if (ov > best || (ov == best && oc < cls)) {
-          best = ov;
-          cls = oc;
-        }
-      }
-      const Box cb = cand_box(out, d.anchors, a, cls, best);
-      bool suppressed = false;
-      for (int j0 = 0; j0 < nk && !suppressed; j0 += 32) {
-        const int j = j0 + lane;
-        bool s = false;
-        if (j < nk) {
-          const Box kb = kept[j];
-          s = (d.class_agnostic || kb.cls == cls) && iou_ref(kb, cb) > d.iou;
-        }
-        suppressed = __any_sync(0xffffffffu, s);
-      }
-      if (!suppressed) {
-        if (lane == 0) kept[nk] = cb;
-        ++nk;
-        __syncwarp();
+  __shared__ unsigned alive_mask[kDetThreads / 32];
+  const int lane = tid & 31, warp = tid >> 5;
+  int nk = 0;  // uniform across the CTA
+  for (int base = 0; base < ncand && nk < keep_cap; base += kDetThreads) {
+    const int i = base + tid;
+    bool alive = i < ncand;
+    Box cb{};
+    if (alive) {
+      const unsigned long long key = keys[i];
+      const int a = static_cast<int>((key >> 16) & 0xFFFFull);
+      const int cls = static_cast<int>(key & 0xFFFFull);
+      cb = cand_box(out, d.anchors, a, cls, out[static_cast<size_t>(4 + cls) * d.anchors + a]);
+      for (int j = 0; j < nk && alive; ++j) {
+        const Box kb = kept[j];
+        if ((d.class_agnostic || kb.cls == cls) && iou_ref(kb, cb) > d.iou) alive = false;
       }
     }
-    if (lane == 0) n_kept = nk;
+    for (;;) {
+      const unsigned m = __ballot_sync(0xffffffffu, alive);
+      if (lane == 0) alive_mask[warp] = m;
+      __syncthreads();
+      int first = -1;
+      for (int w = 0; w < kDetThreads / 32; ++w) {
+        const unsigned mw = alive_mask[w];
+        if (mw != 0u) {
+          first = w * 32 + __ffs(mw) - 1;
+          break;
+        }
+      }
+      __syncthreads();  // every thread has read the masks before they are rewritten
+      if (first < 0) break;
+      if (tid == first) {
+        kept[nk] = cb;
+        alive = false;
+      }
+      __syncthreads();
+      const Box kb = kept[nk];
+      ++nk;
+      if (nk >= keep_cap) break;
+      if (alive && tid > first && (d.class_agnostic || kb.cls == cb.cls) && iou_ref(kb, cb) > d.iou) alive = false;
+    }
   }
+  if (tid == 0) n_kept = nk;
   __syncthreads();
   // 4. back to source pixels (Letterbox.ToSourceX/Y), clamped; zero-area boxes dropped (keeps order)
   if (tid == 0) {
@@ -353,6 +362,7 @@ OSC_API int osc_yolo_detect_f32(osc_ctx* ctx, const float* output, int B, int fi
     return fail(OSC_EINVAL, "osc_yolo_detect_f32: bad arguments");
   if (anchors > kMaxAnchors) return fail(OSC_EUNSUPPORTED, "osc_yolo_detect_f32: %d anchors > %d", anchors, kMaxAnchors);
   if (max_det > kMaxKeep) return fail(OSC_EUNSUPPORTED, "osc_yolo_detect_f32: max_det %d > %d", max_det, kMaxKeep);
+  if (fields - 4 > 65535) return fail(OSC_EUNSUPPORTED, "osc_yolo_detect_f32: %d classes > 65535", fields - 4);
   if (B == 0) return OSC_OK;
   if (output == nullptr || dets == nullptr || counts == nullptr)
     return fail(OSC_EINVAL, "osc_yolo_detect_f32: null pointer");

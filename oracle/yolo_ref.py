@@ -126,7 +126,7 @@ def iou(a, b) -> float:
 
 
 def detect(output: np.ndarray, conf: float = 0.25, iou_thr: float = 0.45, max_det: int = 300,
-           max_candidates: int = 30000) -> list[tuple]:
+           max_candidates: int = 30000, class_agnostic: bool = False) -> list[tuple]:
     """YoloDecoder.Decode + DetectionNms.Suppress for one image's [4 + nc, A] output.
     Returns (class, score, x, y, w, h, anchor) tuples in NMS order."""
     f = np.float32
@@ -148,7 +148,7 @@ def detect(output: np.ndarray, conf: float = 0.25, iou_thr: float = 0.45, max_de
     cands = cands[:max_candidates]
     kept = []
     for c in cands:
-        if any(k[0] == c[0] and iou(k[2:6], c[2:6]) > iou_thr for k in kept):
+        if any((class_agnostic or k[0] == c[0]) and iou(k[2:6], c[2:6]) > iou_thr for k in kept):
             continue
         kept.append(c)
         if len(kept) >= max_det:

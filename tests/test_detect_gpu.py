@@ -99,3 +99,27 @@ def test_detect_caps_and_empty(ctx):
     ref = yolo_ref.detect(outs[0], conf=0.25, iou_thr=0.45, max_det=5)
     assert counts.tolist() == [len(ref), 0] and len(ref) == 5
     assert dets.cpu().numpy()[0, :5, 0].astype(int).tolist() == [k[0] for k in ref]
+
+
+@pytest.mark.parametrize("case", ["dense_capped", "dense_uncapped", "agnostic"])
+def test_detect_dense_candidates_match_oracle(ctx, case):
+    """Every anchor a candidate (as with random-init weights, scores in a narrow
+    band): the block-parallel greedy NMS walks several 1024-candidate chunks
+    and must keep exactly the boxes of the one-at-a-time loop, in order."""
+    from onnxsharp_b200 import ops
+
+    rng = np.random.default_rng(31)
+    out = _synthetic_output(rng)
+    out[4:] = rng.uniform(0.2, 0.6, out[4:].shape).astype(np.float32)
+    out[2:4] = rng.uniform(4, 40, (2, out.shape[1])).astype(np.float32)  # small boxes: many survive
+    max_det = {"dense_capped": 300, "dense_uncapped": 1024, "agnostic": 300}[case]
+    agn = case == "agnostic"
+    dets, counts = ops.yolo_detect(ctx, T(out[None]), conf=0.25, iou=0.45, max_det=max_det, class_agnostic=agn)
+    ctx.synchronize()
+    kept = yolo_ref.detect(out, conf=0.25, iou_thr=0.45, max_det=max_det, class_agnostic=agn)
+    n = int(counts.cpu().numpy()[0])
+    assert n == len(kept) > 0
+    got = dets.cpu().numpy()[0, :n]
+    assert got[:, 0].astype(int).tolist() == [k[0] for k in kept]
+    ref = np.array([k[1:6] for k in kept], np.float32)
+    assert np.array_equal(got[:, 1:].view(np.uint32), ref.view(np.uint32))
