@@ -87,6 +87,61 @@ class Context:
         self._finalizer()
 
 
+class GroupContext(Context):
+    """A context owned by a Group (osc_group_ctx): usable like any Context,
+    destroyed with its group."""
+
+    def __init__(self, handle, device: int, group: "Group"):  # noqa: D107 - no osc_create
+        self.handle = handle
+        self.device = int(device)
+        self._group = group
+        self._finalizer = weakref.finalize(self, lambda: None)
+
+
+class Group:
+    """Several GPUs of one node driven from this process (osc_group_*): a
+    context per GPU and an NCCL communicator clique among them."""
+
+    def __init__(self, devices):
+        _lib.load()
+        self.devices = [int(d) for d in devices]
+        arr = (C.c_int * len(self.devices))(*self.devices)
+        h = C.c_void_p()
+        call("osc_group_create", len(self.devices), arr, C.byref(h))
+        self.handle = h
+        self._finalizer = weakref.finalize(self, _lib.load().osc_group_destroy, h)
+        self.ctxs = []
+        for r, d in enumerate(self.devices):
+            c = C.c_void_p()
+            call("osc_group_ctx", self.handle, r, C.byref(c))
+            self.ctxs.append(GroupContext(c, d, self))
+
+    def __len__(self):
+        return len(self.devices)
+
+    @staticmethod
+    def _ptrs(xs):
+        return (C.c_void_p * len(xs))(*[ptr(x) for x in xs])
+
+    def all_gather(self, send, recv, nbytes: int) -> None:
+        call("osc_group_allgather", self.handle, self._ptrs(send), self._ptrs(recv), int(nbytes))
+
+    def allreduce_minmax(self, minmax) -> None:
+        call("osc_group_allreduce_minmax", self.handle, self._ptrs(minmax))
+
+    def run_sharded(self, graphs, shard_out, gathered_out, shard_bytes: int) -> None:
+        hs = [getattr(x, "handle", x) for x in graphs]  # CapturedGraph or a raw osc_graph handle
+        g = (C.c_void_p * len(hs))(*[h.value if isinstance(h, C.c_void_p) else h for h in hs])
+        call("osc_group_run_sharded", self.handle, g, self._ptrs(shard_out), self._ptrs(gathered_out),
+             int(shard_bytes))
+
+    def synchronize(self, timeout_ms: int = 60000) -> None:
+        call("osc_group_synchronize", self.handle, int(timeout_ms))
+
+    def close(self) -> None:
+        self._finalizer()
+
+
 class CapturedGraph:
     """An instantiated CUDA graph of library launches (osc_graph_launch replays it on the context's stream)."""
 
