@@ -121,6 +121,75 @@ OSC_API int osc_graph_end(osc_ctx* ctx, osc_graph** out);
 OSC_API int osc_graph_launch(osc_ctx* ctx, const osc_graph* graph);
 OSC_API int osc_graph_free(osc_graph* graph);
 
+/* Static plan of fused nodes (the executor of NetImpl.PrepareForGraph /
+ * BufferAllocator.Assign / Interpreter.Run, src/OnnxSharp/Engine/NetImpl.cs:151-192,
+ * Engine/BufferAllocator.cs:41-138, Core/Interpreter.cs:30-186) for a host
+ * that hands the library its whole fused graph at once. Buffers are NCHW,
+ * described per image (C, H, W; the batch is the plan's); nodes read and write
+ * channel slices of them (osc_plan_ref), so Concat is producers writing into
+ * slices of one buffer and Split is slices of one buffer. osc_plan_build
+ * colours the buffers' live ranges into slots with the reference's rule (by
+ * first write; a slot is reused only when its last reader is strictly before
+ * the new first write; the largest buffer sizes the slot) and allocates one
+ * device arena. The buffer `input_buf` is not in the arena: osc_plan_run binds
+ * it to the caller's pointer. The first run with an (input, output) pointer
+ * pair runs the nodes once and captures them into a CUDA graph (the
+ * reference's per-signature plan cache, Core/LayerPlan.cs:32-94); later runs
+ * with that pair replay it (up to 8 pairs are kept). Weights: an
+ * osc_conv_weights* (OSC_OP_CONV), the raw [M, C/group, k, k] device tensor
+ * (OSC_OP_CONV_DIRECT), an osc_gemm_weights* (OSC_OP_MATMUL_BIAS); they must
+ * outlive the plan.
+ *
+ * Node attributes (iattr / fattr):
+ *   CONV, CONV_DIRECT  in = {x, residual?}; iattr = {stride, pad, dilation, act, k, group}
+ *                      (y = residual + act(conv(x) + bias); CONV is group 1, k from the weights)
+ *   MAXPOOL            iattr = {k, stride, pad}
+ *   RESIZE_NEAREST     iattr = {scale}
+ *   PSA                in = {qkv}; iattr = {heads, kd, hd}; fattr = {scale}
+ *   YOLO_DECODE        in = {box0, box1, box2, cls0, cls1, cls2}, no out (writes the plan
+ *                      output [B, 4 + nc, A]); iattr = {nc}; fattr = {stride0, stride1, stride2}
+ *   MATMUL_BIAS        whole buffers; rows = B*C*H, k = W; out W = n; iattr[3] = act
+ *   SOFTMAX            whole buffers; over W
+ *   UNARY              whole buffers; iattr[3] = act
+ *   ATTENTION          in = {q, k, v} whole buffers [B, T = C, 1, heads * D = W]; iattr = {heads};
+ *                      fattr = {scale}; out [B, T, 1, heads * D] */
+enum osc_plan_op {
+  OSC_OP_CONV = 1, OSC_OP_CONV_DIRECT = 2, OSC_OP_MAXPOOL = 3, OSC_OP_RESIZE_NEAREST = 4, OSC_OP_PSA = 5,
+  OSC_OP_YOLO_DECODE = 6, OSC_OP_MATMUL_BIAS = 7, OSC_OP_SOFTMAX = 8, OSC_OP_UNARY = 9, OSC_OP_ATTENTION = 10
+};
+#define OSC_PLAN_MAX_IN 6
+typedef struct osc_plan_ref { int buf, c0, c; } osc_plan_ref; /* channels [c0, c0 + c) of buffer buf */
+typedef struct osc_plan_node {
+  int op, n_in, n_out;
+  osc_plan_ref in[OSC_PLAN_MAX_IN];
+  osc_plan_ref out[1];
+  int iattr[8];
+  float fattr[4];
+  const void* weights;
+  const float* bias;
+} osc_plan_node;
+typedef struct osc_plan_desc {
+  int batch;
+  int n_buffers;
+  const int* buf_chw; /* [n_buffers][3] */
+  int input_buf;
+  int n_nodes;
+  const osc_plan_node* nodes;
+} osc_plan_desc;
+typedef struct osc_plan osc_plan;
+OSC_API int osc_plan_build(osc_ctx* ctx, const osc_plan_desc* desc, osc_plan** out);
+OSC_API int osc_plan_run(osc_plan* plan, const float* input, float* output);
+OSC_API int osc_plan_arena_bytes(const osc_plan* plan, size_t* bytes);
+/* Device address (and image stride in elements) of a buffer for a given input
+ * pointer: the arena slot of an activation, or `input` for the input buffer. */
+OSC_API int osc_plan_buffer(const osc_plan* plan, int buffer, const float* input, float** ptr, long long* nstride);
+OSC_API int osc_plan_free(osc_plan* plan);
+
+/* The colouring osc_plan_build uses, on the host (no device): byte offset per
+ * buffer (-1 if first_write < 0) and the arena size. */
+OSC_API int osc_arena_assign(int n, const int* first_write, const int* last_read, const size_t* bytes,
+                             long long* offsets, size_t* total);
+
 /* Device memory and copies, for callers without a framework allocator (the
  * reference's Tensor buffers are pinned host arrays, Tensors/Tensor.cs:65-155). */
 OSC_API int osc_malloc(osc_ctx* ctx, size_t bytes, void** out);

@@ -91,6 +91,12 @@ SIGNATURES: dict[str, tuple] = {
     "osc_group_allgather": (i32, [vp, pp, pp, sz]),
     "osc_group_allreduce_minmax": (i32, [vp, pp]),
     "osc_group_run_sharded": (i32, [vp, pp, pp, pp, sz]),
+    "osc_plan_build": (i32, [vp, vp, pp]),
+    "osc_plan_run": (i32, [vp, vp, vp]),
+    "osc_plan_arena_bytes": (i32, [vp, C.POINTER(sz)]),
+    "osc_plan_buffer": (i32, [vp, i32, vp, pp, C.POINTER(i64)]),
+    "osc_plan_free": (i32, [vp]),
+    "osc_arena_assign": (i32, [i32, vp, vp, vp, vp, C.POINTER(sz)]),
     "osc_malloc": (i32, [vp, sz, pp]),
     "osc_free": (i32, [vp, vp]),
     "osc_memcpy_htod": (i32, [vp, vp, vp, sz]),

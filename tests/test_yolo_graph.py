@@ -201,3 +201,28 @@ def test_graph_matches_reference_shape_table_node_by_node():
     # the exported graph's 88 Convs = our 87 conv names (the 128-channel PSA
     # position encoding runs as 2 per-head depthwise convs) + the DFL 1x1 (in decode)
     assert len(ir_convs) == 88 and sum(1 for n in ir_convs if ".attn.pe." in n) == 2
+
+
+def test_native_arena_colouring_matches_reference_rule():
+    """osc_arena_assign (the colouring osc_plan_build uses, run on the host) gives
+    the same offsets as the BufferAllocator restatement in arena.py, on the YOLO
+    plan's live ranges and on random ones."""
+    import random
+
+    from onnxsharp_b200 import plan
+
+    g = yolo.build_yolo11n()
+    names, first, last = yolo.buffer_lifetimes(g)
+    sizes = [64 * 4 * int(np.prod(g.buffers[n])) for n in names]
+    f, l_ = [first[n] for n in names], [last[n] for n in names]
+    want_off, want_total = arena.plan_offsets([arena.Lifetime(a, b, c) for a, b, c in zip(f, l_, sizes)])
+    got_off, got_total = plan.arena_assign(f, l_, sizes)
+    assert got_off == want_off and got_total == want_total
+    rnd = random.Random(5)
+    for _ in range(200):
+        n = rnd.randint(1, 30)
+        f = [rnd.randint(-1, 20) for _ in range(n)]
+        l_ = [max(0, x + rnd.randint(0, 6)) for x in f]
+        sz = [rnd.randint(1, 5000) for _ in range(n)]
+        want = arena.plan_offsets([arena.Lifetime(a, b, c) for a, b, c in zip(f, l_, sz)])
+        assert plan.arena_assign(f, l_, sz) == (list(want[0]), want[1])
