@@ -423,7 +423,7 @@ class DqmmWorkload(Workload):
         a, w, ws, b = dqmm_inputs(777, m, k, n)
         self.a_h, self.w_h, self.ws_h, self.b_h = a, w, ws, b
         lo, cnt, self.replicas = sh.plan(m)
-        self.rows = cnt
+        self.rows, self.row0 = cnt, lo
         dev = _dev()
         self.a = torch.from_numpy(a[lo:lo + cnt]).to(dev)
         self.ws = torch.from_numpy(ws).to(dev)
@@ -458,7 +458,8 @@ class DqmmWorkload(Workload):
         if self.sharded:
             minmax(self.ctx, a, out=self.mm)
             shard.global_minmax(self.mm, group=self.sh.group)
-            dqmm(self.ctx, a, self.w, self.ws, self.b, out=y, minmax_override=self.mm)
+            dqmm(self.ctx, a, self.w, self.ws, self.b, out=y, minmax_override=self.mm, row0=self.row0,
+                 rows_total=self.m)
         else:
             dqmm(self.ctx, a, self.w, self.ws, self.b, out=y)
 

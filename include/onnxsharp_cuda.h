@@ -320,6 +320,19 @@ OSC_API int osc_dqmm_f32(osc_ctx* ctx, const float* a, int m, int k, int lda, co
                          const float* w_scale, int n_scale, const float* bias, float* y, const float* minmax_override,
                          uint8_t* q_out, int32_t* acc_out, float* params_out);
 
+/* osc_dqmm_f32 for a row shard: A holds rows [row0, row0 + m) of a tensor of
+ * rows_total rows, quantised with that tensor's range minmax_global (device,
+ * {min, max}, e.g. all-reduced over the shards). The reference rounds a row's
+ * epilogue with one FMA when the row lies in the 12/6/4-row micro-kernel
+ * groups of the whole matrix and with mul+add otherwise
+ * (GemmKernel.cs:746-790, 1594-1608); this entry classifies the shard's rows
+ * by their index in the whole tensor, so the shards' q, accumulators AND y
+ * are bit-identical to the unsharded call's. */
+OSC_API int osc_dqmm_shard_f32(osc_ctx* ctx, const float* a, int m, int k, int lda, const osc_dqmm_weights* w,
+                               const float* w_scale, int n_scale, const float* bias, float* y,
+                               const float* minmax_global, int row0, int rows_total, uint8_t* q_out,
+                               int32_t* acc_out, float* params_out);
+
 /* minmax_out[0..1] (device) = {min(x, 0), max(x, 0)} over `count` floats, NaN
  * skipped (Quantizer.MinMax). */
 OSC_API int osc_minmax_f32(osc_ctx* ctx, const float* x, long count, float* minmax_out);

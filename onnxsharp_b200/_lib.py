@@ -115,6 +115,7 @@ SIGNATURES: dict[str, tuple] = {
     "osc_dqmm_prepack": (i32, [vp, vp, i32, i32, i32, vp, i32, i32, pp]),
     "osc_dqmm_weights_free": (i32, [vp]),
     "osc_dqmm_f32": (i32, [vp, vp, i32, i32, i32, vp, vp, i32, vp, vp, vp, vp, vp, vp]),
+    "osc_dqmm_shard_f32": (i32, [vp, vp, i32, i32, i32, vp, vp, i32, vp, vp, vp, i32, i32, vp, vp, vp]),
     "osc_minmax_f32": (i32, [vp, vp, C.c_long, vp]),
     # FusedAttention
     "osc_attention_f32": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, f32, i32, vp]),

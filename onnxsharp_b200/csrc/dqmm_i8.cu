@@ -1247,9 +1247,16 @@ OSC_API int osc_minmax_f32(osc_ctx* ctx, const float* x, long count, float* minm
   return check_launch(ctx, "k_minmax_final");
 }
 
-OSC_API int osc_dqmm_f32(osc_ctx* ctx, const float* a, int m, int k, int lda, const osc_dqmm_weights* w,
-                         const float* w_scale, int n_scale, const float* bias, float* y, const float* minmax_override,
-                         uint8_t* q_out, int32_t* acc_out, float* params_out) {
+}  // extern "C"
+
+// The DynamicQuantizeMatMul of rows [row0, row0 + m) of an A with rows_total
+// rows. The reference's epilogue rounds a row with one FMA when the row falls
+// in the 12/6/4-row micro-kernel groups of the WHOLE matrix and with mul+add
+// otherwise (GemmKernel.cs:746-790, 1594-1608); the grouped rows are a prefix
+// of the matrix, so a shard's grouped rows are a prefix of the shard.
+static int dqmm_rows(osc_ctx* ctx, const float* a, int m, int k, int lda, const osc_dqmm_weights* w,
+                     const float* w_scale, int n_scale, const float* bias, float* y, const float* minmax_override,
+                     int row0, int rows_total, uint8_t* q_out, int32_t* acc_out, float* params_out) {
   OSC_TRY(enter(ctx));
   if (w == nullptr) return fail(OSC_EINVAL, "osc_dqmm_f32: null weights");
   if (w->device != ctx->device) return fail(OSC_EINVAL, "osc_dqmm_f32: weights live on another device");
@@ -1313,7 +1320,7 @@ OSC_API int osc_dqmm_f32(osc_ctx* ctx, const float* a, int m, int k, int lda, co
   args.N = w->n;
   args.K = k;
   args.num_kb = kp / kQBK;
-  args.fused_rows = grouped_rows(m);
+  args.fused_rows = std::max(0, std::min(m, grouped_rows(rows_total) - row0));
   args.full_cols = (w->n / 16) * 16;
   args.qp = qp;
   args.rowsum = rowsum;
@@ -1328,6 +1335,27 @@ OSC_API int osc_dqmm_f32(osc_ctx* ctx, const float* a, int m, int k, int lda, co
   args.has_wzp = w->has_zp;
   args.int_out = 0;
   return int8_gemm(ctx, q, kp, kp, 0, m, w, args);
+}
+
+extern "C" {
+
+OSC_API int osc_dqmm_f32(osc_ctx* ctx, const float* a, int m, int k, int lda, const osc_dqmm_weights* w,
+                         const float* w_scale, int n_scale, const float* bias, float* y, const float* minmax_override,
+                         uint8_t* q_out, int32_t* acc_out, float* params_out) {
+  return dqmm_rows(ctx, a, m, k, lda, w, w_scale, n_scale, bias, y, minmax_override, 0, m, q_out, acc_out,
+                   params_out);
+}
+
+OSC_API int osc_dqmm_shard_f32(osc_ctx* ctx, const float* a, int m, int k, int lda, const osc_dqmm_weights* w,
+                               const float* w_scale, int n_scale, const float* bias, float* y,
+                               const float* minmax_global, int row0, int rows_total, uint8_t* q_out, int32_t* acc_out,
+                               float* params_out) {
+  if (minmax_global == nullptr) return fail(OSC_EINVAL, "osc_dqmm_shard_f32: the global range is required");
+  if (row0 < 0 || m < 0 || rows_total < row0 + m)
+    return fail(OSC_EINVAL, "osc_dqmm_shard_f32: rows [%d, %d) outside a tensor of %d rows", row0, row0 + m,
+                rows_total);
+  return dqmm_rows(ctx, a, m, k, lda, w, w_scale, n_scale, bias, y, minmax_global, row0, rows_total, q_out, acc_out,
+                   params_out);
 }
 
 OSC_API int osc_dynamic_quantize_linear_f32(osc_ctx* ctx, const float* x, long long count, uint8_t* y,

@@ -57,6 +57,11 @@ struct osc_plan {
   void* arena = nullptr;
   size_t arena_bytes = 0;
   std::vector<CacheEntry> cache;
+  // The plan runs and is captured on its own stream, ordered after the
+  // caller's stream (ev_in) and before later work on it (ev_out), so a caller
+  // on the legacy default stream can run it too.
+  cudaStream_t stream = nullptr;
+  cudaEvent_t ev_in = nullptr, ev_out = nullptr;
 };
 
 namespace {
@@ -253,6 +258,32 @@ int validate(const osc_plan_desc* d) {
   return OSC_OK;
 }
 
+// On the plan's stream (ctx->stream points at it): replay the graph cached for
+// (input, output), or run the nodes once eagerly (sizes the scratch arena),
+// capture them and cache the graph.
+int plan_launch(osc_plan* plan, const float* input, float* output) {
+  osc_ctx* ctx = plan->ctx;
+  for (const CacheEntry& e : plan->cache)
+    if (e.in == input && e.out == output) return osc_graph_launch(ctx, e.graph);
+  OSC_TRY(run_nodes(plan, input, output));
+  OSC_TRY(osc_synchronize(ctx, 0));
+  OSC_TRY(osc_graph_begin(ctx));
+  const int st = run_nodes(plan, input, output);
+  osc_graph* g = nullptr;
+  const int st2 = osc_graph_end(ctx, &g);
+  if (st != OSC_OK) {
+    osc_graph_free(g);
+    return st;
+  }
+  if (st2 != OSC_OK) return st2;
+  if (static_cast<int>(plan->cache.size()) >= kMaxCache) {
+    osc_graph_free(plan->cache.front().graph);
+    plan->cache.erase(plan->cache.begin());
+  }
+  plan->cache.push_back(CacheEntry{input, output, g});
+  return osc_graph_launch(ctx, g);
+}
+
 }  // namespace
 
 extern "C" {
@@ -317,6 +348,13 @@ OSC_API int osc_plan_build(osc_ctx* ctx, const osc_plan_desc* desc, osc_plan** o
     }
   }
   pl->arena_bytes = total;
+  cudaError_t e = cudaStreamCreateWithFlags(&pl->stream, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&pl->ev_in, cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&pl->ev_out, cudaEventDisableTiming);
+  if (e != cudaSuccess) {
+    osc_plan_free(pl);
+    return cuda_fail(e, "osc_plan_build: stream / events");
+  }
   *out = pl;
   return OSC_OK;
 }
@@ -347,35 +385,28 @@ OSC_API int osc_plan_run(osc_plan* plan, const float* input, float* output) {
     for (const osc_plan_node& n : plan->nodes)
       if (n.op == OSC_OP_YOLO_DECODE) return fail(OSC_EINVAL, "osc_plan_run: the plan writes an output; got null");
   if (fault_injected("launch")) return fail(OSC_EFAULT_INJECTED, "injected failure (launch)");
-  for (const CacheEntry& e : plan->cache)
-    if (e.in == input && e.out == output) return osc_graph_launch(ctx, e.graph);
   if (capturing(ctx)) return run_nodes(plan, input, output);  // the caller captures the whole plan itself
-  // first run with this signature: eager (sizes the scratch arena), then capture
-  OSC_TRY(run_nodes(plan, input, output));
-  OSC_TRY(osc_synchronize(ctx, 0));
-  OSC_TRY(osc_graph_begin(ctx));
-  const int st = run_nodes(plan, input, output);
-  osc_graph* g = nullptr;
-  const int st2 = osc_graph_end(ctx, &g);
-  if (st != OSC_OK) {
-    osc_graph_free(g);
-    return st;
-  }
-  if (st2 != OSC_OK) return st2;
-  if (static_cast<int>(plan->cache.size()) >= kMaxCache) {
-    osc_graph_free(plan->cache.front().graph);
-    plan->cache.erase(plan->cache.begin());
-  }
-  plan->cache.push_back(CacheEntry{input, output, g});
-  return osc_graph_launch(ctx, g);
+  cudaStream_t caller = ctx->stream;
+  OSC_CUDA(cudaEventRecord(plan->ev_in, caller), "osc_plan_run: record");
+  OSC_CUDA(cudaStreamWaitEvent(plan->stream, plan->ev_in, 0), "osc_plan_run: wait");
+  ctx->stream = plan->stream;
+  const int st = plan_launch(plan, input, output);
+  ctx->stream = caller;
+  if (st != OSC_OK) return st;
+  OSC_CUDA(cudaEventRecord(plan->ev_out, plan->stream), "osc_plan_run: record");
+  OSC_CUDA(cudaStreamWaitEvent(caller, plan->ev_out, 0), "osc_plan_run: wait");
+  return OSC_OK;
 }
 
 OSC_API int osc_plan_free(osc_plan* plan) {
   if (plan == nullptr) return OSC_OK;
   cudaSetDevice(plan->ctx->device);
-  cudaStreamSynchronize(plan->ctx->stream);
+  if (plan->stream) cudaStreamSynchronize(plan->stream);
   for (CacheEntry& e : plan->cache) osc_graph_free(e.graph);
   if (plan->arena) cudaFree(plan->arena);
+  if (plan->ev_in) cudaEventDestroy(plan->ev_in);
+  if (plan->ev_out) cudaEventDestroy(plan->ev_out);
+  if (plan->stream) cudaStreamDestroy(plan->stream);
   delete plan;
   return OSC_OK;
 }

@@ -218,13 +218,20 @@ class DqmmWeights:
 
 
 def dqmm(ctx: Context, a, w: DqmmWeights, w_scale, bias=None, out=None, minmax_override=None, q_out=None,
-         acc_out=None, params_out=None):
-    """DynamicQuantizeMatMul: y = (quant_u8(A) - zp) @ (W - wzp) * (a_scale * w_scale) + bias."""
+         acc_out=None, params_out=None, row0: int | None = None, rows_total: int | None = None):
+    """DynamicQuantizeMatMul: y = (quant_u8(A) - zp) @ (W - wzp) * (a_scale * w_scale) + bias.
+    With row0 / rows_total, A is the row shard [row0, row0 + m) of a tensor of rows_total rows
+    and minmax_override its global range (osc_dqmm_shard_f32)."""
     import torch
 
     m = a.shape[0]
     if out is None:
         out = torch.empty((m, w.n), dtype=torch.float32, device=a.device)
+    if row0 is not None:
+        call("osc_dqmm_shard_f32", ctx.handle, ptr(a), int(m), w.k, int(a.stride(0)), w.handle, ptr(w_scale),
+             int(w_scale.numel()), ptr(bias), ptr(out), ptr(minmax_override), int(row0), int(rows_total), ptr(q_out),
+             ptr(acc_out), ptr(params_out))
+        return out
     call("osc_dqmm_f32", ctx.handle, ptr(a), int(m), w.k, int(a.stride(0)), w.handle, ptr(w_scale),
          int(w_scale.numel()), ptr(bias), ptr(out), ptr(minmax_override), ptr(q_out), ptr(acc_out), ptr(params_out))
     return out

@@ -157,3 +157,34 @@ def test_dqmm_row_shards_with_global_range_match_whole(ctx):
     y = np.concatenate([p[0] for p in parts])
     # 1024-row shards: the 12/6/4 row grouping leaves 1024 = 12*85 + 4 -> all rows fused, as in the whole tensor
     assert np.array_equal(y.view(np.uint32), whole[0].view(np.uint32))
+
+
+def test_dqmm_row_shards_bit_exact_with_global_range(ctx):
+    """osc_dqmm_shard_f32 on one GPU: A split into uneven row shards, each
+    quantised with the whole tensor's range and classified by its rows' index
+    in the whole tensor, reproduces q, the int32 accumulators and y of the
+    unsharded oracle bit for bit (the reference's FMA / mul+add epilogue
+    boundary at the 12/6/4-row groups falls inside a shard here)."""
+    import torch
+
+    from onnxsharp_b200.runtime import DqmmWeights, dqmm, minmax
+
+    rng = np.random.default_rng(61)
+    m, k, n = 1027, 256, 384  # whole-matrix groups cover rows < 1026; row 1026 is a leftover row
+    a = rng.normal(0, 1, (m, k)).astype(np.float32)
+    w = rng.integers(-127, 128, (k, n)).astype(np.int8)
+    ws = rng.uniform(0.001, 0.02, n).astype(np.float32)
+    b = rng.normal(0, 0.01, n).astype(np.float32)
+    ry, rq, racc, _ = oracle.dqmm(a, w, 0, ws, b)
+    W = DqmmWeights(ctx, torch.from_numpy(w).cuda(), k, n, 0)
+    ta = torch.from_numpy(a).cuda()
+    mm = minmax(ctx, ta)
+    tws, tb = torch.from_numpy(ws).cuda(), torch.from_numpy(b).cuda()
+    for lo, hi in [(0, 515), (515, 1025), (1025, 1027)]:
+        q = torch.empty((hi - lo, k), dtype=torch.uint8, device="cuda")
+        acc = torch.empty((hi - lo, n), dtype=torch.int32, device="cuda")
+        y = dqmm(ctx, ta[lo:hi], W, tws, tb, minmax_override=mm, q_out=q, acc_out=acc, row0=lo, rows_total=m)
+        ctx.synchronize()
+        assert np.array_equal(q.cpu().numpy(), rq[lo:hi])
+        assert np.array_equal(acc.cpu().numpy(), racc[lo:hi])
+        assert np.array_equal(y.cpu().numpy().view(np.uint32), ry[lo:hi].view(np.uint32)), (lo, hi)

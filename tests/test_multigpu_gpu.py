@@ -83,9 +83,9 @@ def test_group_dqmm_row_shards_bit_exact(group):
         minmax(ctx, t["a"], out=t["mm"])
         per.append(t)
     group.allreduce_minmax([t["mm"] for t in per])
-    for ctx, t in zip(group.ctxs, per):
+    for r, (ctx, t) in enumerate(zip(group.ctxs, per)):
         dqmm(ctx, t["a"], t["W"], t["ws"], t["b"], out=t["y"], minmax_override=t["mm"], q_out=t["q"],
-             acc_out=t["acc"], params_out=t["params"])
+             acc_out=t["acc"], params_out=t["params"], row0=r * half, rows_total=m)
     group.all_gather([t["y"] for t in per], [t["yall"] for t in per], half * n * 4)
     group.synchronize()
     for r, t in enumerate(per):
