@@ -628,7 +628,7 @@ class YoloWorkload(Workload):
                        "precision": "FP32 in/out; wide convs 3xTF32 tcgen05 (k x k implicit GEMM on NHWC hi/lo, 1x1 "
                                     "straight from NCHW), narrow and depthwise convs FP32 CUDA-core FMA, glue FP32 CUDA "
                                     "cores; conv Sigmoid/SiLU from hardware ex2/rcp (<= 2e-6 from the exact form)",
-                       "plan": "static plan replayed as one CUDA graph"}
+                       "plan": "static plan replayed as one CUDA graph; the Detect head's box and class branches on two more streams (lanes) beside the neck"}
 
     def _node_flops(self, n):
         y = n.outs[0]
@@ -645,7 +645,8 @@ class YoloWorkload(Workload):
         self.net.forward(use_graph=True)
 
     def profile_compute(self):
-        self.net.forward(use_graph=False)
+        # one lane: every kernel on the profiled context, in plan order
+        self.net.forward(use_graph=False, serial=True)
 
     def collect(self):
         if self.gather:

@@ -215,6 +215,34 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// 32 TMEM lanes x 32 consecutive 32-bit columns from registers: thread i of
+// the warp writes lane (base_lane + i). tmem_wait_st() before the values are
+// consumed by a tcgen05.mma (then fence::before_thread_sync + an mbarrier).
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+      "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};\n" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// D[tmem] (+)= A[tmem] * B[smem], TF32: A (M rows = TMEM lanes, K along
+// columns, 8 columns per MMA) comes from tensor memory.
+__device__ __forceinline__ void mma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Shared-memory matrix descriptor for a K-major operand tile stored the way a
 // TMA tiled load with CU_TENSOR_MAP_SWIZZLE_128B writes it: rows of 128 bytes,
 // 8-row swizzle atoms 1024 bytes apart. The tile base must be 1024-aligned;
@@ -328,6 +356,8 @@ __host__ __device__ constexpr uint32_t idesc_tf32(int M, int N) {
 }
 // The same with A read MN-major (bit 15); B stays K-major.
 __host__ __device__ constexpr uint32_t idesc_tf32_amn(int M, int N) { return idesc_tf32(M, N) | (1u << 15); }
+// The same with B read MN-major (bit 16); A stays K-major.
+__host__ __device__ constexpr uint32_t idesc_tf32_bmn(int M, int N) { return idesc_tf32(M, N) | (1u << 16); }
 __host__ __device__ constexpr uint32_t idesc_u8s8(int M, int N) {
   return (2u << 4)                                   // D format: S32
          | (0u << 7)                                 // A: unsigned 8-bit

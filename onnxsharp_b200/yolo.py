@@ -259,25 +259,92 @@ def buffer_lifetimes(g: Graph):
     return names, first, last
 
 
+def node_lanes(g: Graph, lanes: int) -> list[int]:
+    """Stream (lane) of each node: the Detect head's box branches on lane 1 and
+    its class branches on lane 2 (each a chain of convs that depends only on
+    its neck level), everything else on lane 0. The head chains then run
+    beside the neck and beside each other, which fills the GPU when a batch
+    is too small for one layer to (strong scaling: 8 images per GPU)."""
+    out = []
+    for n in g.nodes:
+        lane = 0
+        if lanes > 1 and n.name.startswith("model.23.cv2."):
+            lane = 1
+        elif lanes > 1 and n.name.startswith("model.23.cv3."):
+            lane = 2 if lanes > 2 else 1
+        out.append(lane)
+    return out
+
+
+def node_deps(g: Graph) -> list[set]:
+    """Earlier nodes each node must wait for: every earlier node that writes a
+    channel slice it reads or writes, or reads a slice it writes (RAW, WAW, WAR
+    on the plan's buffers; reuse of arena memory is made safe separately)."""
+    def overlap(a: Ref, b: Ref) -> bool:
+        return a.buf == b.buf and a.c0 < b.c0 + b.c and b.c0 < a.c0 + a.c
+
+    deps = []
+    for i, n in enumerate(g.nodes):
+        d = set()
+        for j in range(i):
+            m = g.nodes[j]
+            if (any(overlap(w, r) for w in m.outs for r in n.ins) or any(overlap(w, x) for w in m.outs for x in n.outs)
+                    or any(overlap(r, x) for r in m.ins for x in n.outs)):
+                d.add(j)
+        deps.append(d)
+    return deps
+
+
+def happens_before(deps: list[set], lane_of: list[int]) -> list[int]:
+    """Bitmask per node of the nodes that complete before it starts: its data
+    dependencies, the previous node on its lane, and their ancestors."""
+    anc, last_on = [], {}
+    for i, d in enumerate(deps):
+        preds = set(d)
+        if lane_of[i] in last_on:
+            preds.add(last_on[lane_of[i]])
+        m = 0
+        for p in preds:
+            m |= anc[p] | (1 << p)
+        anc.append(m)
+        last_on[lane_of[i]] = i
+    return anc
+
+
 # ---------------------------------------------------------------------------- device executor
 class Net:
     """The static plan on one GPU: arena-planned activations, prepacked
     weights, one CUDA graph per batch size (osc_graph_*)."""
 
-    def __init__(self, ctx, g: Graph, params: dict, batch: int, size: int = 640):
+    def __init__(self, ctx, g: Graph, params: dict, batch: int, size: int = 640, lanes: int = 3):
         import torch
 
         from . import arena
-        from .runtime import ConvWeights
+        from .runtime import Context, ConvWeights
 
         self.ctx, self.g, self.batch, self.size = ctx, g, batch, size
         dev = torch.device("cuda", ctx.device)
+        # lanes: the plan's nodes run on `lanes` streams, each with its own
+        # context (stream + scratch arena, so concurrent layers never share
+        # per-call temporaries); cross-lane dependencies are events, captured
+        # into the same CUDA graph
+        self.lane_of = node_lanes(g, lanes)
+        self.lanes = max(self.lane_of) + 1
+        self.deps = node_deps(g)
+        anc = happens_before(self.deps, self.lane_of)
+        self.cross = [sorted(j for j in d if self.lane_of[j] != self.lane_of[i]) for i, d in enumerate(self.deps)]
+        self.signals = sorted({j for c in self.cross for j in c})
         names, first, last = buffer_lifetimes(g)
+        touch = {n: 0 for n in names}
+        for i, node in enumerate(g.nodes):
+            for r in list(node.ins) + list(node.outs):
+                if r.buf in touch:
+                    touch[r.buf] |= 1 << i
         lts = []
         for n in names:
             c, h, w = g.buffers[n]
             lts.append(arena.Lifetime(first[n], last[n], batch * c * h * w * 4))
-        offsets, total = arena.plan_offsets(lts)
+        offsets, total = arena.plan_offsets_dag(lts, [touch[n] for n in names], anc)
         self.arena_bytes = total
         self.arena = torch.empty(max(total, 256) // 4, dtype=torch.float32, device=dev)
         self.views = {}
@@ -299,6 +366,17 @@ class Net:
         self.graphs = [None]
         self.extra_graphs = []
         self.stream = None
+        self.lane_ctx = [ctx] + [Context(ctx.device) for _ in range(self.lanes - 1)]
+        self.lane_streams = [None] + [torch.cuda.Stream(device=dev) for _ in range(self.lanes - 1)]
+        for c, st in zip(self.lane_ctx[1:], self.lane_streams[1:]):
+            c.set_stream(st.cuda_stream)
+        self.events = {j: torch.cuda.Event() for j in self.signals}
+        self.ev_fork = torch.cuda.Event()
+        self.ev_join = [torch.cuda.Event() for _ in range(self.lanes)]
+
+    def launch_count(self) -> int:
+        """Library kernel launches made so far by all of the plan's lane contexts."""
+        return sum(c.launch_count() for c in self.lane_ctx)
 
     @staticmethod
     def tensor_core(node) -> bool:
@@ -323,35 +401,62 @@ class Net:
     def input_view(self, slot: int = 0):
         return self.inputs[slot]
 
-    def _run_nodes(self):
+    def _run_nodes(self, serial: bool = False):
+        """Enqueue every node. The main lane runs on the context's current
+        stream; with serial=False the other lanes fork from it, wait for their
+        cross-lane inputs on events and join it at the end (all of which a
+        stream capture records as graph edges). serial=True runs every node on
+        the main context in plan order (same kernels, same results)."""
+        import torch
+
+        if serial or self.lanes == 1:
+            for node in self.g.nodes:
+                self._run_node(self.ctx, node)
+            return
+        main = torch.cuda.ExternalStream(self.ctx.get_stream(), device=self.ctx.device)
+        streams = [main] + self.lane_streams[1:]
+        self.ev_fork.record(main)
+        for st in streams[1:]:
+            st.wait_event(self.ev_fork)
+        for i, node in enumerate(self.g.nodes):
+            lane = self.lane_of[i]
+            for j in self.cross[i]:
+                streams[lane].wait_event(self.events[j])
+            self._run_node(self.lane_ctx[lane], node)
+            if i in self.events:
+                self.events[i].record(streams[lane])
+        for lane in range(1, self.lanes):
+            self.ev_join[lane].record(streams[lane])
+            main.wait_event(self.ev_join[lane])
+
+    def _run_node(self, ctx, node):
+        """Enqueue one node's kernels on ctx (its stream and scratch arena)."""
         from . import _lib, ops
 
-        ctx = self.ctx
-        for node in self.g.nodes:
-            a = node.attrs
-            if node.op == "conv":
-                x, y = self.view(node.ins[0]), self.view(node.outs[0])
-                res = self.view(node.ins[1]) if a["residual"] else None
-                b = self.dev_params[node.name + ".b"]
-                if node.name in self.packed:
-                    ops.conv2d_ex(ctx, x, self.packed[node.name], b, y, a["s"], a["p"], 1, a["act"], res)
-                else:  # hardware-instruction SiLU, as in the tensor-core epilogues
-                    act = a["act"] | _lib.ACT_FAST if a["act"] != ACT_NONE else ACT_NONE
-                    ops.conv2d_direct(ctx, x, self.dev_params[node.name + ".w"], b, y, a["s"], a["p"], 1, a["group"],
-                                      act, res)
-            elif node.op == "maxpool":
-                ops.maxpool2d(ctx, self.view(node.ins[0]), self.view(node.outs[0]), a["k"], a["s"], a["p"])
-            elif node.op == "upsample":
-                ops.resize_nearest(ctx, self.view(node.ins[0]), self.view(node.outs[0]), a["scale"])
-            elif node.op == "psa":
-                ops.psa_attention(ctx, self.view(node.ins[0]), self.view(node.outs[0]), a["heads"], a["kd"], a["hd"],
-                                  a["scale"])
-            elif node.op == "decode":
-                k = len(node.ins) // 2
-                ops.yolo_decode(ctx, [self.view(r) for r in node.ins[:k]], [self.view(r) for r in node.ins[k:]],
-                                a["strides"], self.output)
-            else:  # pragma: no cover
-                raise ValueError(node.op)
+        a = node.attrs
+        if node.op == "conv":
+            x, y = self.view(node.ins[0]), self.view(node.outs[0])
+            res = self.view(node.ins[1]) if a["residual"] else None
+            b = self.dev_params[node.name + ".b"]
+            if node.name in self.packed:
+                ops.conv2d_ex(ctx, x, self.packed[node.name], b, y, a["s"], a["p"], 1, a["act"], res)
+            else:  # hardware-instruction SiLU, as in the tensor-core epilogues
+                act = a["act"] | _lib.ACT_FAST if a["act"] != ACT_NONE else ACT_NONE
+                ops.conv2d_direct(ctx, x, self.dev_params[node.name + ".w"], b, y, a["s"], a["p"], 1, a["group"],
+                                  act, res)
+        elif node.op == "maxpool":
+            ops.maxpool2d(ctx, self.view(node.ins[0]), self.view(node.outs[0]), a["k"], a["s"], a["p"])
+        elif node.op == "upsample":
+            ops.resize_nearest(ctx, self.view(node.ins[0]), self.view(node.outs[0]), a["scale"])
+        elif node.op == "psa":
+            ops.psa_attention(ctx, self.view(node.ins[0]), self.view(node.outs[0]), a["heads"], a["kd"], a["hd"],
+                              a["scale"])
+        elif node.op == "decode":
+            k = len(node.ins) // 2
+            ops.yolo_decode(ctx, [self.view(r) for r in node.ins[:k]], [self.view(r) for r in node.ins[k:]],
+                            a["strides"], self.output)
+        else:  # pragma: no cover
+            raise ValueError(node.op)
 
     def _bind(self, slot: int):
         """Point the plan at input/output slot `slot` (for eager runs and capture)."""
@@ -376,7 +481,7 @@ class Net:
             self.stream = torch.cuda.Stream(device=self.ctx.device)
         return self.stream
 
-    def _launch(self, slot: int, use_graph: bool):
+    def _launch(self, slot: int, use_graph: bool, serial: bool = False):
         """Enqueue one run of the plan for `slot` on the plan's stream."""
         import ctypes as C
 
@@ -387,7 +492,7 @@ class Net:
         self._bind(slot)
         try:
             if not use_graph:
-                self._run_nodes()
+                self._run_nodes(serial)
                 return
             if self.graphs[slot] is None:
                 self._run_nodes()  # sizes the scratch arena, sets kernel attributes
@@ -451,7 +556,7 @@ class Net:
         finally:
             self.ctx.set_stream(prev)
 
-    def forward(self, use_graph: bool = True, slot: int = 0):
+    def forward(self, use_graph: bool = True, slot: int = 0, serial: bool = False):
         """Run the plan on the contents of input_view(slot); returns the slot's [B, 84, A] output tensor.
 
         The plan runs on its own stream (a capturable one), ordered after the
@@ -461,7 +566,7 @@ class Net:
         stream = self.plan_stream()
         caller = torch.cuda.current_stream(self.ctx.device)
         stream.wait_stream(caller)
-        self._launch(slot, use_graph)
+        self._launch(slot, use_graph, serial)
         caller.wait_stream(stream)
         return self.outputs[slot]
 

@@ -226,3 +226,35 @@ def test_native_arena_colouring_matches_reference_rule():
         sz = [rnd.randint(1, 5000) for _ in range(n)]
         want = arena.plan_offsets([arena.Lifetime(a, b, c) for a, b, c in zip(f, l_, sz)])
         assert plan.arena_assign(f, l_, sz) == (list(want[0]), want[1])
+
+
+def test_concurrent_lanes_arena_is_race_free():
+    """With the Detect head's branches on their own streams, two buffers may
+    share arena memory only when every node touching one happens before the
+    first writer of the other (data dependencies and stream order)."""
+    g = yolo.build_yolo11n()
+    lane_of = yolo.node_lanes(g, 3)
+    assert set(lane_of) == {0, 1, 2}
+    deps = yolo.node_deps(g)
+    anc = yolo.happens_before(deps, lane_of)
+    names, first, last = yolo.buffer_lifetimes(g)
+    touch = {n: 0 for n in names}
+    for i, node in enumerate(g.nodes):
+        for r in list(node.ins) + list(node.outs):
+            if r.buf in touch:
+                touch[r.buf] |= 1 << i
+    sizes = {n: 4 * int(np.prod(g.buffers[n])) for n in names}
+    lts = [arena.Lifetime(first[n], last[n], sizes[n]) for n in names]
+    offs, _ = arena.plan_offsets_dag(lts, [touch[n] for n in names], anc)
+    for (i, a), (j, b) in itertools.combinations(enumerate(names), 2):
+        if offs[i] < 0 or offs[j] < 0:
+            continue
+        if not (offs[i] < offs[j] + sizes[b] and offs[j] < offs[i] + sizes[a]):
+            continue
+        a_before_b = touch[a] & ~anc[first[b]] == 0
+        b_before_a = touch[b] & ~anc[first[a]] == 0
+        assert a_before_b or b_before_a, (a, b)
+    # the head branches depend only on their neck level: the 80x80 box branch
+    # may run while the neck computes the 40x40 and 20x20 levels
+    idx = {n.name: k for k, n in enumerate(g.nodes)}
+    assert not anc[idx["model.23.cv2.0.0"]] >> idx["model.19.cv2"] & 1
