@@ -73,6 +73,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return done != 0;
 }
 
+// Non-blocking test of the phase with the given parity (for a thread that
+// polls several barriers in turn).
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(done)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
 // Bounded wait for the phase with the given parity. `abort_flag` is a shared
 // word: once any thread of the CTA gives up, every other waiter stops too.
 // On a timeout the launch's global error word gets DEV_ERR_TIMEOUT.

@@ -47,16 +47,18 @@ def test_attention_golden_fixture(ctx, golden):
     _check(_attn(ctx, g["attn_q"], g["attn_k"], g["attn_v"], 2, 0.25), g["attn_o"])
 
 
-@pytest.mark.parametrize("B,T,H,D", [(2, 40, 4, 64), (3, 127, 2, 64), (1, 1, 1, 64), (2, 64, 8, 32), (1, 100, 3, 32)])
+@pytest.mark.parametrize("B,T,H,D", [(2, 40, 4, 64), (3, 127, 2, 64), (1, 1, 1, 64), (2, 64, 8, 32), (1, 100, 3, 32),
+                                     (40, 77, 8, 32), (37, 128, 8, 64)])  # several heads per persistent CTA
 def test_attention_shapes(ctx, B, T, H, D):
     q, k, v = _qkv(B * 131 + T, B, T, H * D)
     s = 1.0 / np.sqrt(D)
     _check(_attn(ctx, q, k, v, H, s), oracle.attention(q, k, v, heads=H, scale=s))
 
 
-@pytest.mark.parametrize("rows", [1, 96])
-def test_attention_mask(ctx, rows):
-    B, T, H, D = 2, 96, 2, 64
+@pytest.mark.parametrize("full", [False, True], ids=["row_mask", "full_mask"])
+def test_attention_mask(ctx, full):
+    B, T, H, D = 40, 93, 8, 64  # 320 heads: each CTA walks several, T not a multiple of 8
+    rows = T if full else 1
     q, k, v = _qkv(rows, B, T, H * D)
     rng = np.random.default_rng(99)
     mask = np.where(rng.uniform(size=(B, 1, rows, T)) < 0.2, -1e4, 0.0).astype(np.float32)
