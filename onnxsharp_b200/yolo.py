@@ -637,3 +637,41 @@ class HostPipeline:
 
     def synchronize(self):
         self.d2h.synchronize()
+
+
+def _main(argv=None) -> int:
+    """Run the plan with random-init weights: `python -m onnxsharp_b200.yolo
+    --batch 64 --passes 2 [--lanes 1] [--graph]` (eager passes, every kernel on
+    the main context in plan order unless --graph replays the captured plan).
+    Prints the library launches per pass; used for profiler captures."""
+    import argparse
+
+    import torch
+
+    from .runtime import Context
+
+    ap = argparse.ArgumentParser(description=_main.__doc__)
+    ap.add_argument("--batch", type=int, default=8)
+    ap.add_argument("--passes", type=int, default=2)
+    ap.add_argument("--lanes", type=int, default=3)
+    ap.add_argument("--graph", action="store_true")
+    args = ap.parse_args(argv)
+    torch.cuda.set_stream(torch.cuda.Stream())
+    ctx = Context(0)
+    ctx.use_torch_stream()
+    g = build_yolo11n()
+    net = Net(ctx, g, init_params(g, 1), args.batch, lanes=args.lanes)
+    net.input_view().copy_(torch.rand(net.input_view().shape, device="cuda"))
+    l0 = net.launch_count()
+    for _ in range(args.passes):
+        net.forward(use_graph=args.graph, serial=not args.graph)
+    ctx.synchronize()
+    print(f"batch {args.batch}: {args.passes} passes, {(net.launch_count() - l0) // max(1, args.passes)} launches per pass")
+    net.close()
+    return 0
+
+
+if __name__ == "__main__":
+    import sys
+
+    sys.exit(_main())
