@@ -90,6 +90,8 @@ __global__ void __launch_bounds__(ConvCfg::THREADS, 1)
     tma_prefetch(&mXl);
   }
   const uint32_t tmem = pipe_setup<Cfg>(pb);
+  griddep_wait();  // launched with launch_pdl: the previous kernel has completed past here
+  griddep_launch();
 
   if (warp == 0) {
     if (lane == 0)
@@ -294,6 +296,8 @@ __global__ void __launch_bounds__(pw::kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = pb->tmem_slot;
   const int nchunks = (g.num_kb + kKC - 1) / kKC;
+  griddep_wait();  // launched with launch_pdl: the previous kernel has completed past here
+  griddep_launch();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -553,6 +557,8 @@ __global__ void __launch_bounds__(256) k_nchw_to_phase_nhwc(const float* __restr
                                                             int C, int H, int W, int s, int Hp, int Wp, int Cp,
                                                             int z_base, float* __restrict__ hi,
                                                             float* __restrict__ lo) {
+  griddep_wait();  // launched with launch_pdl: the previous kernel has completed past here
+  griddep_launch();
   __shared__ float tile[32][32 * kPhaseMaxS + 1];
   const int span = 32 * s;               // input pixels of this strip
   const int w0 = blockIdx.x * span;      // first input pixel
@@ -609,6 +615,8 @@ __global__ void __launch_bounds__(256) k_nchw_to_phase_nhwc(const float* __restr
 __global__ void __launch_bounds__(256) k_nchw_to_nhwc_split(const float* __restrict__ x, long long x_nstride, int N,
                                                             int C, int H, int W, int Cp, int z_base,
                                                             float* __restrict__ hi, float* __restrict__ lo) {
+  griddep_wait();  // launched with launch_pdl: the previous kernel has completed past here
+  griddep_launch();
   __shared__ float tile[32][33];
   const int w0 = blockIdx.x * 32;
   const int c0 = blockIdx.y * 32;
@@ -731,12 +739,9 @@ static int conv1x1_launch(osc_ctx* ctx, const float* x, long long x_nstride, int
   const int smem = pw::Cfg<BN>::kSmemBase + static_cast<int>(round_up(static_cast<size_t>(w->M) * 4, 16));
   OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(k_conv_px_tf32x3<false, BN>), smem));
   const long long grid = std::min<long long>(g.tiles, ctx->num_sms);
-  prof_begin(ctx);
   const ConvTaps no_taps{};
-  k_conv_px_tf32x3<false, BN><<<static_cast<unsigned>(grid), pw::kThreads, smem, ctx->stream>>>(mX, mX, mWh, mWl, g,
-                                                                                             no_taps, bias, y,
-                                                                                         ctx->d_err);
-  return check_launch(ctx, "k_conv_px_tf32x3");
+  return launch_pdl(ctx, k_conv_px_tf32x3<false, BN>, dim3(static_cast<unsigned>(grid)), dim3(pw::kThreads), smem,
+                    "k_conv_px_tf32x3", mX, mX, mWh, mWl, g, no_taps, bias, y, ctx->d_err);
 }
 
 // Layers with at most 64 output channels take the 64-channel tile (4-stage
@@ -752,9 +757,17 @@ static int conv1x1_tf32x3(osc_ctx* ctx, const float* x, long long x_nstride, int
 // Pixel-major tiles for K x K convs with few output channels on small images
 // (measured on B200, YOLO shapes at B=64: 256->64 and 64->64 3x3 at 20x20
 // 19-24 % faster; at 40x40 and above the channel-major kernel's 256-pixel
-// tiles move fewer operand bytes per output and win).
-static bool px_taps_ok(int M, int OH, int OW) {
-  return M <= 64 && static_cast<long>(OH) * OW <= 576;
+// tiles move fewer operand bytes per output and win) -- and at any image size
+// when the channel-major kernel would not fill two waves of the SMs (small
+// batches: its 128-channel tiles leave half the MMA rows empty at <= 64
+// output channels, and the persistent pixel-major kernel has twice the tiles).
+static bool px_taps_ok(const osc_ctx* ctx, int M, int N, int OH, int OW) {
+  if (M > 64) return false;
+  if (static_cast<long>(OH) * OW <= 576) return true;
+  int BW = 0, BH = 0;
+  choose_box(OH, OW, &BW, &BH);
+  const long tiles = static_cast<long>(N) * ((OW + BW - 1) / BW) * ((OH + BH - 1) / BH);
+  return tiles < 2L * ctx->num_sms;
 }
 
 // The pixel box of the pixel-major conv: BW x BH <= 128 pixels, the shape
@@ -817,10 +830,8 @@ static int conv_px_taps(osc_ctx* ctx, const float* xh, const float* xl, int N, i
   const int smem = pw::Cfg<128>::kSmemBase + static_cast<int>(round_up(static_cast<size_t>(w->M) * 4, 16));
   OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(k_conv_px_tf32x3<true, 128>), smem));
   const long long grid = std::min<long long>(g.tiles, ctx->num_sms);
-  prof_begin(ctx);
-  k_conv_px_tf32x3<true, 128><<<static_cast<unsigned>(grid), pw::kThreads, smem, ctx->stream>>>(mXh, mXl, mWh, mWl, g,
-                                                                                            taps, bias, y, ctx->d_err);
-  return check_launch(ctx, "k_conv_px_tf32x3");
+  return launch_pdl(ctx, k_conv_px_tf32x3<true, 128>, dim3(static_cast<unsigned>(grid)), dim3(pw::kThreads), smem,
+                    "k_conv_px_tf32x3", mXh, mXl, mWh, mWl, g, taps, bias, y, ctx->d_err);
 }
 
 int conv_tf32x3(osc_ctx* ctx, const float* x, long long x_nstride, int N, int C, int H, int W, const osc_conv_weights* w,
@@ -846,16 +857,12 @@ int conv_tf32x3(osc_ctx* ctx, const float* x, long long x_nstride, int N, int C,
     const long zmax = 65535;  // gridDim.z limit: split into several launches
     for (long z0 = 0; z0 < zt; z0 += zmax) {
       dim3 grid((Wp + 31) / 32, Cp / 32, static_cast<unsigned>(std::min(zmax, zt - z0)));
-      prof_begin(ctx);
-      if (s == 1) {
-        k_nchw_to_nhwc_split<<<grid, 256, 0, ctx->stream>>>(x, x_nstride, N, C, H, W, Cp, static_cast<int>(z0), xh,
-                                                             xl);
-        OSC_TRY(check_launch(ctx, "k_nchw_to_nhwc_split"));
-      } else {
-        k_nchw_to_phase_nhwc<<<grid, 256, 0, ctx->stream>>>(x, x_nstride, N, C, H, W, s, Hp, Wp, Cp,
-                                                            static_cast<int>(z0), xh, xl);
-        OSC_TRY(check_launch(ctx, "k_nchw_to_phase_nhwc"));
-      }
+      if (s == 1)
+        OSC_TRY(launch_pdl(ctx, k_nchw_to_nhwc_split, grid, dim3(256), 0, "k_nchw_to_nhwc_split", x, x_nstride, N, C,
+                           H, W, Cp, static_cast<int>(z0), xh, xl));
+      else
+        OSC_TRY(launch_pdl(ctx, k_nchw_to_phase_nhwc, grid, dim3(256), 0, "k_nchw_to_phase_nhwc", x, x_nstride, N, C,
+                           H, W, s, Hp, Wp, Cp, static_cast<int>(z0), xh, xl));
     }
   }
   // 2. tap table
@@ -871,7 +878,7 @@ int conv_tf32x3(osc_ctx* ctx, const float* x, long long x_nstride, int N, int C,
       taps.dy[t] = static_cast<short>(floor_div(oy - py, s));
       taps.dx[t] = static_cast<short>(floor_div(ox - px, s));
     }
-  if (px_taps_ok(w->M, OH, OW)) return conv_px_taps(ctx, xh, xl, N, Hp, Wp, s, w, taps, bias, act, res, res_nstride, y,
+  if (px_taps_ok(ctx, w->M, N, OH, OW)) return conv_px_taps(ctx, xh, xl, N, Hp, Wp, s, w, taps, bias, act, res, res_nstride, y,
                                               y_nstride, OH, OW);
   ConvGeom g{};
   g.N = N;
@@ -914,10 +921,8 @@ int conv_tf32x3(osc_ctx* ctx, const float* x, long long x_nstride, int N, int C,
   if (tiles > 2147483647L) return fail(OSC_EINVAL, "conv: too many tiles");
   OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(k_conv_tf32x3), ConvCfg::SMEM_BYTES));
   dim3 grid(static_cast<unsigned>(tiles), (w->M + kBM - 1) / kBM);
-  prof_begin(ctx);
-  k_conv_tf32x3<<<grid, ConvCfg::THREADS, ConvCfg::SMEM_BYTES, ctx->stream>>>(mWh, mWl, mXh, mXl, taps, g, bias, y,
-                                                                             ctx->d_err);
-  return check_launch(ctx, "k_conv_tf32x3");
+  return launch_pdl(ctx, k_conv_tf32x3, grid, dim3(ConvCfg::THREADS), ConvCfg::SMEM_BYTES, "k_conv_tf32x3", mWh, mWl,
+                    mXh, mXl, taps, g, bias, y, ctx->d_err);
 }
 
 }  // namespace osc

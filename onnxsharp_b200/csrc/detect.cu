@@ -35,6 +35,8 @@ struct LetterboxArgs {
 // dst + z * dst_stride floats.
 __global__ void k_letterbox(const uint8_t* __restrict__ px, const __grid_constant__ LetterboxArgs a,
                             float* __restrict__ dst, long long px_stride, long long dst_stride) {
+  griddep_wait();  // launched with launch_pdl: the previous kernel has completed past here
+  griddep_launch();
   const long plane = static_cast<long>(a.th) * a.tw;
   px += blockIdx.y * px_stride;
   dst += blockIdx.y * dst_stride;
@@ -127,6 +129,8 @@ __device__ __forceinline__ Box cand_box(const float* __restrict__ out, int ancho
 __global__ void __launch_bounds__(kDetThreads, 1)
     k_yolo_detect(const float* __restrict__ outputs, const __grid_constant__ DetectArgs d, float* __restrict__ dets,
                   int* __restrict__ counts) {
+  griddep_wait();  // launched with launch_pdl: the previous kernel has completed past here
+  griddep_launch();
   extern __shared__ __align__(16) uint8_t smem_det[];
   unsigned long long* keys = reinterpret_cast<unsigned long long*>(smem_det);  // [kMaxAnchors]
   Box* kept = reinterpret_cast<Box*>(keys + kMaxAnchors);                     // [kMaxKeep]
@@ -314,10 +318,8 @@ int letterbox_launch(osc_ctx* ctx, const uint8_t* pixels, int B, long long image
   const long plane = static_cast<long>(a.th) * a.tw;
   long blocks = std::min<long>((plane + 255) / 256, static_cast<long>(ctx->num_sms) * 16);
   blocks = std::max<long>(1, std::min<long>(blocks, (static_cast<long>(ctx->num_sms) * 16 + B - 1) / B));
-  prof_begin(ctx);
-  k_letterbox<<<dim3(static_cast<unsigned>(blocks), static_cast<unsigned>(B)), 256, 0, ctx->stream>>>(
-      pixels, a, dst, image_stride, dst_stride);
-  return check_launch(ctx, "k_letterbox");
+  return launch_pdl(ctx, k_letterbox, dim3(static_cast<unsigned>(blocks), static_cast<unsigned>(B)), dim3(256), 0,
+                    "k_letterbox", pixels, a, dst, image_stride, dst_stride);
 }
 
 }  // namespace
@@ -370,9 +372,7 @@ OSC_API int osc_yolo_detect_f32(osc_ctx* ctx, const float* output, int B, int fi
   DetectArgs d{fields, anchors, conf, iou, max_det, max_candidates, class_agnostic ? 1 : 0, transforms};
   const int smem = kMaxAnchors * 8 + kMaxKeep * static_cast<int>(sizeof(Box));
   OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(k_yolo_detect), smem));
-  prof_begin(ctx);
-  k_yolo_detect<<<B, kDetThreads, smem, ctx->stream>>>(output, d, dets, counts);
-  return check_launch(ctx, "k_yolo_detect");
+  return launch_pdl(ctx, k_yolo_detect, dim3(B), dim3(kDetThreads), smem, "k_yolo_detect", output, d, dets, counts);
 }
 
 }  // extern "C"

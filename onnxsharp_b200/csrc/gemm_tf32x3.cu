@@ -230,6 +230,8 @@ struct EpiAffine {
 __global__ void k_gather_split(const float* __restrict__ src, int inner, long long so, long long si, long long sr,
                                long long sc, int rows, int cols, int kp, float* __restrict__ hi,
                                float* __restrict__ lo) {
+  griddep_wait();  // launched with launch_pdl: the previous kernel has completed past here
+  griddep_launch();
   __shared__ float tile[32][33];
   const int z = blockIdx.z;
   const int r0 = blockIdx.y * 32, c0 = blockIdx.x * 32;
@@ -283,6 +285,8 @@ __global__ void __launch_bounds__(Cfg::THREADS, Cfg::STAGES == 1 ? 2 : 1)
     tma_prefetch(&mBl);
   }
   const uint32_t tmem = pipe_setup<Cfg>(pb);
+  griddep_wait();  // launched with launch_pdl: the previous kernel has completed past here
+  griddep_launch();
   if (warp == 0) {
     if (lane == 0)
       producer_loop<Cfg>(tiles, pb, num_kb, err, [&](int kb, uint8_t* st, uint64_t* bar) {
@@ -565,9 +569,8 @@ static int gather_split(osc_ctx* ctx, const float* src, int batches, int inner, 
                         long long sr, long long sc, int rows, int cols, int kp, float* hi, float* lo) {
   if (batches > 65535) return fail(OSC_EUNSUPPORTED, "matmul: %d batches (65535 at most)", batches);
   dim3 grid((kp + 31) / 32, (rows + 31) / 32, batches);
-  prof_begin(ctx);
-  k_gather_split<<<grid, 256, 0, ctx->stream>>>(src, inner, so, si, sr, sc, rows, cols, kp, hi, lo);
-  return check_launch(ctx, "k_gather_split");
+  return launch_pdl(ctx, k_gather_split, grid, dim3(256), 0, "k_gather_split", src, inner, so, si, sr, sc, rows, cols,
+                    kp, hi, lo);
 }
 
 // C[z] = A[z] (M x K) * B[zb] (K x N) on split operands Ahi/lo [batches][M][Kp],
@@ -591,10 +594,8 @@ static int gemm_batched_cfg(osc_ctx* ctx, const float* ahi, const float* alo, in
   OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(kern), Cfg::SMEM_BYTES));
   if (batches > 65535) return fail(OSC_EUNSUPPORTED, "matmul: %d batches (65535 at most)", batches);
   dim3 grid((N + Cfg::BN - 1) / Cfg::BN, (M + kBM - 1) / kBM, batches);
-  prof_begin(ctx);
-  kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, ctx->stream>>>(mAh, mAl, mBh, mBl, M, N, Kp, col_bias, act, ep, y,
-                                                              ctx->d_err);
-  return check_launch(ctx, "k_gemm_tf32x3");
+  return launch_pdl(ctx, kern, grid, dim3(Cfg::THREADS), Cfg::SMEM_BYTES, "k_gemm_tf32x3", mAh, mAl, mBh, mBl, M, N,
+                    Kp, col_bias, act, ep, y, ctx->d_err);
 }
 
 // Products of at most two k-blocks (K <= 64: PSA's q.k^T with 32 channels)
@@ -752,6 +753,8 @@ int attention_composed(osc_ctx* ctx, const float* q, const float* k, const float
 // row; e is parked in `hi` between the passes.
 __global__ void k_softmax_split(const float* __restrict__ S, long long rows, int len, int kp, float* __restrict__ hi,
                                 float* __restrict__ lo) {
+  griddep_wait();  // launched with launch_pdl: the previous kernel has completed past here
+  griddep_launch();
   const int lane = threadIdx.x & 31;
   const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
   for (long long r = blockIdx.x * static_cast<long long>(blockDim.x >> 5) + (threadIdx.x >> 5); r < rows;
@@ -799,6 +802,8 @@ constexpr int kSoftRegs = 16;
 
 __global__ void k_softmax_split_reg(const float* __restrict__ S, long long rows, int len, int kp,
                                     float* __restrict__ hi, float* __restrict__ lo) {
+  griddep_wait();  // launched with launch_pdl: the previous kernel has completed past here
+  griddep_launch();
   const int lane = threadIdx.x & 31;
   const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
   const int vend = len & ~7;
@@ -899,14 +904,12 @@ int psa_composed(osc_ctx* ctx, const float* qkv, long long qkv_nstride, int B, i
   {
     const long long rows = Z * T;
     const int blocks = static_cast<int>(std::min<long long>((rows + 7) / 8, static_cast<long long>(ctx->num_sms) * 16));
-    prof_begin(ctx);
-    if (kt <= kSoftRegs * 32) {
-      k_softmax_split_reg<<<blocks, 256, 0, ctx->stream>>>(S, rows, T, kt, phi, plo);
-      OSC_TRY(check_launch(ctx, "k_softmax_split_reg"));
-    } else {
-      k_softmax_split<<<blocks, 256, 0, ctx->stream>>>(S, rows, T, kt, phi, plo);
-      OSC_TRY(check_launch(ctx, "k_softmax_split"));
-    }
+    if (kt <= kSoftRegs * 32)
+      OSC_TRY(launch_pdl(ctx, k_softmax_split_reg, dim3(blocks), dim3(256), 0, "k_softmax_split_reg", S, rows, T, kt,
+                         phi, plo));
+    else
+      OSC_TRY(launch_pdl(ctx, k_softmax_split, dim3(blocks), dim3(256), 0, "k_softmax_split", S, rows, T, kt, phi,
+                         plo));
   }
   // v as [z][channel][token] (already K-major)
   OSC_TRY(gather_split(ctx, qkv + 2LL * kd * T, nz, heads, qkv_nstride, per, T, 1, hd, T, kt, vhi, vlo));

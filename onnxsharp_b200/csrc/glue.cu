@@ -201,6 +201,8 @@ __global__ void __launch_bounds__(kDw3Threads) k_dw3s1(const float* __restrict__
                                                        const float* __restrict__ bias, const float* __restrict__ res,
                                                        long long res_nstride, float* __restrict__ y,
                                                        long long y_nstride, unsigned strips, unsigned total) {
+  griddep_wait();  // launched with launch_pdl: the previous kernel has completed past here
+  griddep_launch();
   const unsigned t = blockIdx.x * kDw3Threads + threadIdx.x;
   if (t >= total) return;
   const unsigned ps = t / static_cast<unsigned>(W);
@@ -255,6 +257,8 @@ __global__ void __launch_bounds__(kDw3Threads) k_dw3s1_v4(const float* __restric
                                                           const float* __restrict__ res, long long res_nstride,
                                                           float* __restrict__ y, long long y_nstride, unsigned strips,
                                                           unsigned total) {
+  griddep_wait();  // launched with launch_pdl: the previous kernel has completed past here
+  griddep_launch();
   const unsigned t = blockIdx.x * kDw3Threads + threadIdx.x;
   if (t >= total) return;
   const unsigned W4 = static_cast<unsigned>(W) >> 2;
@@ -401,6 +405,8 @@ __global__ void __launch_bounds__(32 * G * P) k_conv_tile(
     }
     __syncthreads();
   }
+  griddep_wait();  // launched with launch_pdl: the previous kernel has completed past here
+  griddep_launch();
 
   auto issue = [&](int chunk) {
     float* xs = smem_tile + (chunk & 1) * T::STAGE;
@@ -571,19 +577,15 @@ int launch_conv_tile(osc_ctx* ctx, const float* x, long long x_nstride, int N, i
                              1};
     OSC_TRY(encode_tiled(&xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, x, dims, pitch, box, CU_TENSOR_MAP_SWIZZLE_NONE));
     OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(k_conv_tile<K, S, G, P, true>), T::SMEM));
-    prof_begin(ctx);
-    k_conv_tile<K, S, G, P, true><<<grid, T::THREADS, T::SMEM, ctx->stream>>>(
-        xmap, x, x_nstride, C, H, W, w, M, pt, pl, bias, act, res, res_nstride, y, y_nstride, OH, OW, tiles_x, vec4,
-        ctx->d_err);
-    return check_launch(ctx, "k_conv_tile");
+    return launch_pdl(ctx, k_conv_tile<K, S, G, P, true>, grid, dim3(T::THREADS), T::SMEM, "k_conv_tile", xmap, x,
+                      x_nstride, C, H, W, w, M, pt, pl, bias, act, res, res_nstride, y, y_nstride, OH, OW, tiles_x,
+                      vec4, ctx->d_err);
   }
   using T = TileConv<K, S, G, P, false>;
   OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(k_conv_tile<K, S, G, P, false>), T::SMEM));
-  prof_begin(ctx);
-  k_conv_tile<K, S, G, P, false><<<grid, T::THREADS, T::SMEM, ctx->stream>>>(
-      xmap, x, x_nstride, C, H, W, w, M, pt, pl, bias, act, res, res_nstride, y, y_nstride, OH, OW, tiles_x, vec4,
-      ctx->d_err);
-  return check_launch(ctx, "k_conv_tile");
+  return launch_pdl(ctx, k_conv_tile<K, S, G, P, false>, grid, dim3(T::THREADS), T::SMEM, "k_conv_tile", xmap, x,
+                    x_nstride, C, H, W, w, M, pt, pl, bias, act, res, res_nstride, y, y_nstride, OH, OW, tiles_x, vec4,
+                    ctx->d_err);
 }
 
 template <int K, int S>
@@ -654,6 +656,8 @@ template <int K>
 __global__ void __launch_bounds__(kPoolColThreads) k_maxpool_cols(
     const float* __restrict__ x, long long x_nstride, int C, int H, int W, int sh, int sw, int pt, int pl,
     float* __restrict__ y, long long y_nstride, int OH, int OW, long long planes, int ppc, int PH, int PW) {
+  griddep_wait();  // launched with launch_pdl: the previous kernel has completed past here
+  griddep_launch();
   extern __shared__ float pool_sm[];  // [ppc][PH][PW]
   const int PHW = PH * PW;
   const long long plane0 = static_cast<long long>(blockIdx.x) * ppc;
@@ -729,6 +733,8 @@ __global__ void __launch_bounds__(256) k_resize_nearest(const float* __restrict_
 // aligned output rows (checked by the launcher).
 __global__ void __launch_bounds__(256) k_resize_nearest2x(const float* __restrict__ x, long long x_nstride, int C,
                                                           int H, int W, float* __restrict__ y, long long y_nstride) {
+  griddep_wait();  // launched with launch_pdl: the previous kernel has completed past here
+  griddep_launch();
   const int plane = blockIdx.x;
   const int n = plane / C, c = plane - n * C;
   const int hw2 = (H * W) >> 1;
@@ -895,6 +901,8 @@ struct YoloScales {
 // Grid: x over anchors, y over images (strided when B exceeds the grid), so
 // no per-element division splits a flat index.
 __global__ void k_yolo_decode(const __grid_constant__ YoloScales s, int B, float* __restrict__ out) {
+  griddep_wait();  // launched with launch_pdl: the previous kernel has completed past here
+  griddep_launch();
   const int A = s.total_anchors;
   const int a = blockIdx.x * blockDim.x + threadIdx.x;
   if (a >= A) return;
@@ -1097,25 +1105,25 @@ OSC_API int osc_conv2d_direct_f32(osc_ctx* ctx, const float* x, long long x_nstr
                       reinterpret_cast<uintptr_t>(y) % 16 == 0 && y_nstride % 4 == 0 &&
                       (residual == nullptr || (reinterpret_cast<uintptr_t>(residual) % 16 == 0 && res_nstride % 4 == 0));
     if (vec4 && total <= 0x7fffffffLL) {
-      prof_begin(ctx);
       const long long total4 = total / 4;
       const unsigned blocks = static_cast<unsigned>((total4 + kDw3Threads - 1) / kDw3Threads);
+      int st = OSC_OK;
       with_act(act, [&](auto tag) {
-        k_dw3s1_v4<decltype(tag)::value><<<blocks, kDw3Threads, 0, ctx->stream>>>(
-            x, x_nstride, C, H, W, w, bias, residual, res_nstride, y, y_nstride, static_cast<unsigned>(strips),
-            static_cast<unsigned>(total4));
+        st = launch_pdl(ctx, k_dw3s1_v4<decltype(tag)::value>, dim3(blocks), dim3(kDw3Threads), 0, "k_dw3s1_v4", x,
+                        x_nstride, C, H, W, w, bias, residual, res_nstride, y, y_nstride,
+                        static_cast<unsigned>(strips), static_cast<unsigned>(total4));
       });
-      return check_launch(ctx, "k_dw3s1_v4");
+      return st;
     }
     if (total <= 0x7fffffffLL) {
-      prof_begin(ctx);
       const unsigned blocks = static_cast<unsigned>((total + kDw3Threads - 1) / kDw3Threads);
+      int st = OSC_OK;
       with_act(act, [&](auto tag) {
-        k_dw3s1<decltype(tag)::value><<<blocks, kDw3Threads, 0, ctx->stream>>>(
-            x, x_nstride, C, H, W, w, bias, residual, res_nstride, y, y_nstride, static_cast<unsigned>(strips),
-            static_cast<unsigned>(total));
+        st = launch_pdl(ctx, k_dw3s1<decltype(tag)::value>, dim3(blocks), dim3(kDw3Threads), 0, "k_dw3s1", x,
+                        x_nstride, C, H, W, w, bias, residual, res_nstride, y, y_nstride,
+                        static_cast<unsigned>(strips), static_cast<unsigned>(total));
       });
-      return check_launch(ctx, "k_dw3s1");
+      return st;
     }
   }
   // Depthwise (group == C == M), square 3/5/7 kernels: band-tiled kernel.
@@ -1209,18 +1217,15 @@ OSC_API int osc_maxpool2d_f32(osc_ctx* ctx, const float* x, long long x_nstride,
     const long long ctas = (planes + ppc - 1) / ppc;
     const size_t smem = static_cast<size_t>(ppc * plane_bytes);
     if (ctas <= 0x7fffffffLL) {
-      prof_begin(ctx);
       const dim3 grid(static_cast<unsigned>(ctas));
-#define OSC_POOL_LAUNCH(KS)                                                                                      \
-  k_maxpool_cols<KS><<<grid, kPoolColThreads, smem, ctx->stream>>>(x, x_nstride, C, H, W, stride_h, stride_w,  \
-                                                                   pad_t, pad_l, y, y_nstride, OH, OW, planes, \
-                                                                   ppc, PH, PW)
-      if (kh == 2) OSC_POOL_LAUNCH(2);
-      else if (kh == 3) OSC_POOL_LAUNCH(3);
-      else if (kh == 5) OSC_POOL_LAUNCH(5);
-      else OSC_POOL_LAUNCH(7);
+#define OSC_POOL_LAUNCH(KS)                                                                                        \
+  launch_pdl(ctx, k_maxpool_cols<KS>, grid, dim3(kPoolColThreads), smem, "k_maxpool_cols", x, x_nstride, C, H, W, \
+             stride_h, stride_w, pad_t, pad_l, y, y_nstride, OH, OW, planes, ppc, PH, PW)
+      if (kh == 2) return OSC_POOL_LAUNCH(2);
+      if (kh == 3) return OSC_POOL_LAUNCH(3);
+      if (kh == 5) return OSC_POOL_LAUNCH(5);
+      return OSC_POOL_LAUNCH(7);
 #undef OSC_POOL_LAUNCH
-      return check_launch(ctx, "k_maxpool_cols");
     }
   }
   prof_begin(ctx);
@@ -1244,13 +1249,13 @@ OSC_API int osc_resize_nearest_f32(osc_ctx* ctx, const float* x, long long x_nst
                 outs);
   const bool vec2x = scale_h == 2 && scale_w == 2 && W % 2 == 0 && reinterpret_cast<uintptr_t>(x) % 8 == 0 &&
                      x_nstride % 2 == 0 && reinterpret_cast<uintptr_t>(y) % 16 == 0 && y_nstride % 4 == 0;
-  prof_begin(ctx);
   if (vec2x) {
     const long long pairs = static_cast<long long>(H) * W / 2;
-    k_resize_nearest2x<<<dim3(static_cast<unsigned>(planes), static_cast<unsigned>((pairs + 255) / 256)), 256, 0,
-                         ctx->stream>>>(x, x_nstride, C, H, W, y, y_nstride);
-    return check_launch(ctx, "k_resize_nearest2x");
+    return launch_pdl(ctx, k_resize_nearest2x,
+                      dim3(static_cast<unsigned>(planes), static_cast<unsigned>((pairs + 255) / 256)), dim3(256), 0,
+                      "k_resize_nearest2x", x, x_nstride, C, H, W, y, y_nstride);
   }
+  prof_begin(ctx);
   k_resize_nearest<<<dim3(static_cast<unsigned>(planes), static_cast<unsigned>((outs + 255) / 256)), 256, 0,
                      ctx->stream>>>(x, x_nstride, C, H, W, scale_h, scale_w, y, y_nstride);
   return check_launch(ctx, "k_resize_nearest");
@@ -1339,10 +1344,8 @@ OSC_API int osc_yolo_decode_f32(osc_ctx* ctx, int B, int nc, const float* const*
   if (s.total_anchors <= 0 || hs[0] <= 0 || hs[1] <= 0 || hs[2] <= 0 || ws[0] <= 0 || ws[1] <= 0 || ws[2] <= 0)
     return fail(OSC_EINVAL, "osc_yolo_decode_f32: empty scale");
   if (B == 0) return OSC_OK;
-  prof_begin(ctx);
   const dim3 grid(static_cast<unsigned>((s.total_anchors + 255) / 256), static_cast<unsigned>(std::min(B, 65535)));
-  k_yolo_decode<<<grid, 256, 0, ctx->stream>>>(s, B, out);
-  return check_launch(ctx, "k_yolo_decode");
+  return launch_pdl(ctx, k_yolo_decode, grid, dim3(256), 0, "k_yolo_decode", s, B, out);
 }
 
 OSC_API int osc_layernorm_f32(osc_ctx* ctx, const float* x, int outer, int inner, const float* gamma,

@@ -88,6 +88,41 @@ int set_smem_attr(osc_ctx* ctx, const void* func, int bytes);
 
 inline size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
+// A kernel launched with programmatic stream serialization (launch_pdl) may
+// start while the previous kernel on its stream is still draining: its CTAs
+// set up (barriers, TMEM, tensor-map prefetch) and then griddep_wait() until
+// that kernel has completed and its memory is visible -- before reading what
+// it wrote or writing what it may still read. griddep_launch() lets the next
+// kernel be scheduled once every CTA of this one has started. Both are no-ops
+// for a kernel launched without the attribute.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Launch on the context's stream with programmatic stream serialization: the
+// kernel may begin while the previous kernel on the stream drains, so its
+// set-up overlaps that kernel's tail (in a captured graph this becomes a
+// programmatic edge). Only for kernels that call griddep_wait() before any
+// access to memory the previous kernel writes or reads. Records profiling
+// events and checks the launch like check_launch.
+template <typename... KArgs, typename... Args>
+int launch_pdl(osc_ctx* ctx, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, const char* what,
+               Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = ctx->stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  prof_begin(ctx);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+  if (e != cudaSuccess) return cuda_fail(e, what);
+  return check_launch(ctx, what);
+}
+
 }  // namespace osc
 
 #define OSC_TRY(expr)          \

@@ -67,6 +67,8 @@ def test_conv_config2_batch16_all_images(ctx):
         (3, 64, 9, 7, 96, 5, 1, (2, 2, 2, 2), 1, 1),       # 5x5, tiny spatial
         (1, 256, 20, 20, 256, 3, 1, (1, 1, 1, 1), 1, 1),   # K = 2304
         (1, 8, 17, 17, 8, 7, 3, (3, 3, 3, 3), 1, 0),       # stride 3, 7x7
+        (1, 64, 160, 160, 64, 3, 2, (1, 1, 1, 1), 1, 1),   # <= 64 channels, few tiles: pixel-major at 80x80
+        (2, 48, 83, 97, 40, 3, 1, (1, 1, 1, 1), 1, 1),     # pixel-major, ragged image, 40 channels
     ],
 )
 def test_conv_geometries(ctx, N, C, H, W, M, k, stride, pads, dil, act):
