@@ -362,6 +362,11 @@ __global__ void __launch_bounds__(kDqlThreads, 1)
     sp = dql_params_from(fminf(0.0f, override_mm[0]), fmaxf(0.0f, override_mm[1]));
   }
   __syncthreads();
+  // the GEMM that follows (launched with launch_pdl) may be scheduled once
+  // every CTA of this grid has passed here, i.e. all of them are running, so
+  // its CTAs never hold an SM this grid still needs; it waits for this
+  // grid's completion before it reads q
+  griddep_launch();
   if (!s_ok) {
     // gave up at the barrier (error word set): still count the departure so
     // the last CTA out leaves the counters at zero for the next launch
@@ -853,6 +858,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  griddep_wait();  // launched with launch_pdl: q, its row sums and the parameters are complete past here
+  griddep_launch();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -1140,16 +1147,12 @@ static int int8_gemm(osc_ctx* ctx, const uint8_t* q, size_t q_pitch, int q_cols,
       // q-resident: cpm CTAs share each 128-row block, each walking every cpm-th column block
       args.cpm = std::max(1, std::min(nt, ctx->num_sms / std::max(1, mt)));
       OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(k_dqmm_i8_persistent<true>), kRSmem));
-      prof_begin(ctx);
-      k_dqmm_i8_persistent<true><<<mt * args.cpm, kPThreads, kRSmem, ctx->stream>>>(mQp, mWp, mY, args, idesc_p,
-                                                                                    ctx->d_err);
-      return check_launch(ctx, "k_dqmm_i8");
+      return launch_pdl(ctx, k_dqmm_i8_persistent<true>, dim3(mt * args.cpm), dim3(kPThreads), kRSmem, "k_dqmm_i8",
+                        mQp, mWp, mY, args, idesc_p, ctx->d_err);
     }
     OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(k_dqmm_i8_persistent<false>), kPSmem));
-    prof_begin(ctx);
-    k_dqmm_i8_persistent<false><<<std::min(mt * nt, ctx->num_sms), kPThreads, kPSmem, ctx->stream>>>(
-        mQp, mWp, mY, args, idesc_p, ctx->d_err);
-    return check_launch(ctx, "k_dqmm_i8");
+    return launch_pdl(ctx, k_dqmm_i8_persistent<false>, dim3(std::min(mt * nt, ctx->num_sms)), dim3(kPThreads),
+                      kPSmem, "k_dqmm_i8", mQp, mWp, mY, args, idesc_p, ctx->d_err);
   }
   const uint32_t idesc = (2u << 4) | (q_fmt << 7) | (b_fmt << 10) |
                          (static_cast<uint32_t>(kQBN >> 3) << 17) | (static_cast<uint32_t>(kQBM >> 4) << 24);
