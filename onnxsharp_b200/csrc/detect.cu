@@ -125,49 +125,125 @@ __device__ __forceinline__ Box cand_box(const float* __restrict__ out, int ancho
   return b;
 }
 
-// One CTA per image.
-__global__ void __launch_bounds__(kDetThreads, 1)
-    k_yolo_detect(const float* __restrict__ outputs, const __grid_constant__ DetectArgs d, float* __restrict__ dets,
-                  int* __restrict__ counts) {
+// Candidate key of an anchor (YoloDecoder.Decode's filter): the first
+// maximum over the class fields, then the confidence and box checks. Keys sort
+// ascending in (descending score, ascending anchor) order.
+__device__ __forceinline__ bool anchor_key(const float* __restrict__ out, const DetectArgs& d, int a,
+                                           unsigned long long* key) {
+  float score = -INFINITY;
+  int cls = 0;
+  for (int c = 4; c < d.fields; ++c) {
+    const float v = out[static_cast<size_t>(c) * d.anchors + a];
+    if (v > score) {
+      score = v;
+      cls = c - 4;
+    }
+  }
+  if (!isfinite(score) || score < d.conf) return false;
+  const float x = out[a], y = out[d.anchors + a], w = out[2 * d.anchors + a], h = out[3 * d.anchors + a];
+  if (!isfinite(x) || !isfinite(y) || !isfinite(w) || !isfinite(h) || w <= 0.0f || h <= 0.0f) return false;
+  *key = (static_cast<unsigned long long>(~orderable(score)) << 32) | (static_cast<unsigned long long>(a) << 16) |
+         static_cast<unsigned long long>(cls);
+  return true;
+}
+
+// 1. Candidates of every image at once: blockIdx.x = image, blockIdx.y = a
+// block of 256 anchors (the class scan reads the whole [fields][anchors]
+// output, so it is spread over the SMs rather than one CTA per image). Keys are
+// appended to the image's list with one atomic per warp; their order there is
+// arbitrary, the sort makes it unique (keys are distinct).
+__global__ void __launch_bounds__(256) k_det_candidates(const float* __restrict__ outputs,
+                                                        const __grid_constant__ DetectArgs d,
+                                                        unsigned long long* __restrict__ keys,
+                                                        int* __restrict__ n_cand) {
   griddep_wait();  // launched with launch_pdl: the previous kernel has completed past here
   griddep_launch();
-  extern __shared__ __align__(16) uint8_t smem_det[];
-  unsigned long long* keys = reinterpret_cast<unsigned long long*>(smem_det);  // [kMaxAnchors]
-  Box* kept = reinterpret_cast<Box*>(keys + kMaxAnchors);                     // [kMaxKeep]
-  __shared__ int n_cand, n_kept;
-  const int img = blockIdx.x, tid = threadIdx.x;
+  const int img = blockIdx.x, lane = threadIdx.x & 31;
+  const int a = blockIdx.y * 256 + threadIdx.x;
   const float* out = outputs + static_cast<size_t>(img) * d.fields * d.anchors;
-  if (tid == 0) n_cand = 0;
-  __syncthreads();
-  // 1. per anchor: first maximum over the class fields, confidence and box checks
-  for (int a = tid; a < d.anchors; a += kDetThreads) {
-    float score = -INFINITY;
-    int cls = 0;
-    for (int c = 4; c < d.fields; ++c) {
-      const float v = out[static_cast<size_t>(c) * d.anchors + a];
-      if (v > score) {
-        score = v;
-        cls = c - 4;
+  unsigned long long key = 0;
+  const bool ok = a < d.anchors && anchor_key(out, d, a, &key);
+  const unsigned m = __ballot_sync(0xffffffffu, ok);
+  int base = 0;
+  if (lane == 0 && m != 0u) base = atomicAdd(n_cand + img, __popc(m));
+  base = __shfl_sync(0xffffffffu, base, 0);
+  if (ok) keys[static_cast<size_t>(img) * d.anchors + base + __popc(m & ((1u << lane) - 1u))] = key;
+}
+
+// Bitonic sort (ascending) of n = E * kDetThreads keys, thread t holding keys
+// t*E .. t*E+E-1 in registers: compare-exchange partners inside a thread are
+// register pairs, partners up to 32*E apart are lanes of the same warp
+// (shuffles), and only the strides of 32*E and more go through shared memory
+// (one store, one load and two barriers per stride, XOR-swizzled so a warp's
+// 64-bit accesses take the minimum two wavefronts). The network is the same
+// as the plain shared-memory one, so is the result.
+template <int E>
+__device__ void sort_keys_regs(unsigned long long* keys, const unsigned long long* __restrict__ src, int nsrc) {
+  const int t = threadIdx.x;
+  const int sw = ((t * E) >> 4) & (E - 1);  // swizzle of this thread's slots
+  unsigned long long r[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    const int i = t * E + e;
+    r[e] = i < nsrc ? src[i] : ~0ull;
+  }
+  const int n = E * kDetThreads;
+  for (int k = 2; k <= n; k <<= 1) {
+    const bool up = ((t * E) & k) == 0;  // k >= 2E here whenever it is used below (k > j >= E)
+    int j = k >> 1;
+    for (; j >= 32 * E; j >>= 1) {
+      __syncthreads();  // the previous stride's loads are done
+#pragma unroll
+      for (int e = 0; e < E; ++e) keys[t * E + (e ^ sw)] = r[e];
+      __syncthreads();
+      const int tp = t ^ (j / E);  // partner thread: same slot e, same swizzle (j / E >= 32)
+      const bool lower = (t & (j / E)) == 0;
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        const unsigned long long o = keys[tp * E + (e ^ sw)];
+        r[e] = (lower == up) ? (r[e] < o ? r[e] : o) : (r[e] > o ? r[e] : o);
       }
     }
-    if (!isfinite(score) || score < d.conf) continue;
-    const float x = out[a], y = out[d.anchors + a], w = out[2 * d.anchors + a], h = out[3 * d.anchors + a];
-    if (!isfinite(x) || !isfinite(y) || !isfinite(w) || !isfinite(h) || w <= 0.0f || h <= 0.0f) continue;
-    const int slot = atomicAdd(&n_cand, 1);
-    // descending score, then ascending anchor: sort ascending on (~score key, anchor, class)
-    keys[slot] = (static_cast<unsigned long long>(~orderable(score)) << 32) |
-                 (static_cast<unsigned long long>(a) << 16) | static_cast<unsigned long long>(cls);
+    for (; j >= E; j >>= 1) {
+      const int lm = j / E;  // lane distance (< 32)
+      const bool lower = (t & lm) == 0;
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        const unsigned long long o = __shfl_xor_sync(0xffffffffu, r[e], lm);
+        r[e] = (lower == up) ? (r[e] < o ? r[e] : o) : (r[e] > o ? r[e] : o);
+      }
+    }
+#pragma unroll
+    for (int jj = E / 2; jj >= 1; jj >>= 1) {
+      if (jj > (k >> 1)) continue;
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        if ((e & jj) != 0) continue;
+        const int f = e | jj;
+        const bool u = ((t * E + e) & k) == 0;
+        if ((r[e] > r[f]) == u) {
+          const unsigned long long x = r[e];
+          r[e] = r[f];
+          r[f] = x;
+        }
+      }
+    }
   }
   __syncthreads();
-  const int nc = n_cand;
-  int np2 = 1;
-  while (np2 < nc) np2 <<= 1;
-  for (int i = nc + tid; i < np2; i += kDetThreads) keys[i] = ~0ull;
+#pragma unroll
+  for (int e = 0; e < E; ++e) keys[t * E + e] = r[e];
   __syncthreads();
-  // 2. bitonic sort of keys[0, np2)
-  for (int k = 2; k <= np2; k <<= 1) {
+}
+
+// Plain shared-memory bitonic sort for short lists (n < kDetThreads).
+__device__ void sort_keys_smem(unsigned long long* keys, const unsigned long long* __restrict__ src, int nsrc,
+                               int n) {
+  const int tid = threadIdx.x;
+  for (int i = tid; i < n; i += kDetThreads) keys[i] = i < nsrc ? src[i] : ~0ull;
+  __syncthreads();
+  for (int k = 2; k <= n; k <<= 1) {
     for (int j = k >> 1; j > 0; j >>= 1) {
-      for (int i = tid; i < np2; i += kDetThreads) {
+      for (int i = tid; i < n; i += kDetThreads) {
         const int ixj = i ^ j;
         if (ixj > i) {
           const unsigned long long a = keys[i], b = keys[ixj];
@@ -181,58 +257,120 @@ __global__ void __launch_bounds__(kDetThreads, 1)
       __syncthreads();
     }
   }
-  // 3. greedy NMS in score order, a chunk of kDetThreads candidates at a time
-  // (one per thread). A candidate is suppressed when its IoU with a kept box of
-  // its class (any class if class_agnostic) exceeds the threshold. Each thread
-  // first tests its candidate against the boxes kept from earlier chunks; then
-  // the chunk is resolved in order: the lowest-index surviving candidate is
-  // kept and every later candidate of the chunk is tested against it, until no
-  // candidate survives. The decisions are those of the one-at-a-time greedy
-  // loop (DetectionNms.SuppressSorted): each candidate meets exactly the boxes
-  // kept before it, in the same order, and the loop stops at max_det kept.
+}
+
+constexpr int kChunk = 256;              // candidates resolved per NMS round
+constexpr int kChunkWords = kChunk / 32;
+
+// 2-4. One CTA per image: sort its candidate keys, greedy NMS, output.
+__global__ void __launch_bounds__(kDetThreads, 1)
+    k_yolo_detect(const float* __restrict__ outputs, const __grid_constant__ DetectArgs d,
+                  const unsigned long long* __restrict__ cand_keys, const int* __restrict__ n_cand,
+                  float* __restrict__ dets, int* __restrict__ counts) {
+  griddep_wait();  // launched with launch_pdl: the previous kernel has completed past here
+  griddep_launch();
+  extern __shared__ __align__(16) uint8_t smem_det[];
+  unsigned long long* keys = reinterpret_cast<unsigned long long*>(smem_det);  // [kMaxAnchors]
+  Box* kept = reinterpret_cast<Box*>(keys + kMaxAnchors);                     // [kMaxKeep]
+  Box* cbox = kept + kMaxKeep;                                                // [kChunk]
+  uint32_t* mat = reinterpret_cast<uint32_t*>(cbox + kChunk);                 // [kChunk][kChunkWords]
+  uint32_t* removed0 = mat + kChunk * kChunkWords;                            // [kChunkWords]
+  __shared__ int n_kept;
+  const int img = blockIdx.x, tid = threadIdx.x;
+  const float* out = outputs + static_cast<size_t>(img) * d.fields * d.anchors;
+  const int nc = min(n_cand[img], d.anchors);
+  const unsigned long long* src = cand_keys + static_cast<size_t>(img) * d.anchors;
+  // 2. sort the keys (a power-of-two network, padded with ~0)
+  int np2 = 1;
+  while (np2 < nc) np2 <<= 1;
+  switch (np2 / kDetThreads) {
+    case 0: sort_keys_smem(keys, src, nc, np2); break;
+    case 1: sort_keys_regs<1>(keys, src, nc); break;
+    case 2: sort_keys_regs<2>(keys, src, nc); break;
+    case 4: sort_keys_regs<4>(keys, src, nc); break;
+    case 8: sort_keys_regs<8>(keys, src, nc); break;
+    default: sort_keys_regs<16>(keys, src, nc); break;
+  }
+  // 3. greedy NMS in score order (DetectionNms.SuppressSorted), kChunk
+  // candidates per round. A candidate is suppressed when its IoU with a kept
+  // box of its class (any class if class_agnostic) exceeds the threshold.
+  //  a. each candidate is tested against the boxes kept in earlier rounds
+  //     (4 threads per candidate, every 4th kept box each);
+  //  b. the round's suppression matrix: bit j of row i is set when candidate
+  //     i, kept, would suppress the later candidate j (iou_ref(i, j), the
+  //     kept box first, as in the one-at-a-time loop);
+  //  c. one warp walks the round in order: the first candidate not yet
+  //     removed is kept and its row is ORed into the removed set.
+  // Each candidate thus meets exactly the boxes kept before it, in order, and
+  // the loop stops at max_det kept: the one-at-a-time greedy loop's decisions.
   const int ncand = min(nc, d.max_candidates);
   const int keep_cap = min(d.max_det, kMaxKeep);
-  __shared__ unsigned alive_mask[kDetThreads / 32];
   const int lane = tid & 31, warp = tid >> 5;
   int nk = 0;  // uniform across the CTA
-  for (int base = 0; base < ncand && nk < keep_cap; base += kDetThreads) {
-    const int i = base + tid;
-    bool alive = i < ncand;
-    Box cb{};
-    if (alive) {
-      const unsigned long long key = keys[i];
-      const int a = static_cast<int>((key >> 16) & 0xFFFFull);
-      const int cls = static_cast<int>(key & 0xFFFFull);
-      cb = cand_box(out, d.anchors, a, cls, out[static_cast<size_t>(4 + cls) * d.anchors + a]);
-      for (int j = 0; j < nk && alive; ++j) {
-        const Box kb = kept[j];
-        if ((d.class_agnostic || kb.cls == cls) && iou_ref(kb, cb) > d.iou) alive = false;
-      }
-    }
-    for (;;) {
-      const unsigned m = __ballot_sync(0xffffffffu, alive);
-      if (lane == 0) alive_mask[warp] = m;
-      __syncthreads();
-      int first = -1;
-      for (int w = 0; w < kDetThreads / 32; ++w) {
-        const unsigned mw = alive_mask[w];
-        if (mw != 0u) {
-          first = w * 32 + __ffs(mw) - 1;
-          break;
+  for (int base = 0; base < ncand && nk < keep_cap; base += kChunk) {
+    const int cnt = min(kChunk, ncand - base);
+    if (tid < kChunkWords) removed0[tid] = 0u;
+    __syncthreads();
+    {
+      const int c = tid >> 2, q = tid & 3;  // candidate base + c (c < kChunk), quarter q
+      bool sup = false;
+      Box cb{};
+      if (c < cnt) {
+        const unsigned long long key = keys[base + c];
+        const int a = static_cast<int>((key >> 16) & 0xFFFFull);
+        const int cls = static_cast<int>(key & 0xFFFFull);
+        cb = cand_box(out, d.anchors, a, cls, out[static_cast<size_t>(4 + cls) * d.anchors + a]);
+        for (int j = q; j < nk && !sup; j += 4) {
+          const Box kb = kept[j];
+          if ((d.class_agnostic || kb.cls == cls) && iou_ref(kb, cb) > d.iou) sup = true;
         }
       }
-      __syncthreads();  // every thread has read the masks before they are rewritten
-      if (first < 0) break;
-      if (tid == first) {
-        kept[nk] = cb;
-        alive = false;
+      sup = __shfl_xor_sync(0xffffffffu, sup, 1) || sup;
+      sup = __shfl_xor_sync(0xffffffffu, sup, 2) || sup;
+      if (q == 0) {
+        cbox[c] = cb;
+        if (c >= cnt || sup) atomicOr(removed0 + (c >> 5), 1u << (c & 31));
       }
-      __syncthreads();
-      const Box kb = kept[nk];
-      ++nk;
-      if (nk >= keep_cap) break;
-      if (alive && tid > first && (d.class_agnostic || kb.cls == cb.cls) && iou_ref(kb, cb) > d.iou) alive = false;
     }
+    __syncthreads();
+    {
+      const int i = tid >> 2, w0 = (tid & 3) * 2;  // row i, words w0 and w0 + 1
+      const bool row_live = i < cnt && ((removed0[i >> 5] >> (i & 31)) & 1u) == 0u;
+      const Box ci = cbox[i];
+#pragma unroll
+      for (int ww = 0; ww < 2; ++ww) {
+        const int w = w0 + ww;
+        uint32_t bits = 0u;
+        if (row_live && w * 32 + 31 > i) {
+          for (int b = 0; b < 32; ++b) {
+            const int j = w * 32 + b;
+            if (j <= i || j >= cnt) continue;
+            const Box bj = cbox[j];
+            if ((d.class_agnostic || ci.cls == bj.cls) && iou_ref(ci, bj) > d.iou) bits |= 1u << b;
+          }
+        }
+        mat[i * kChunkWords + w] = bits;
+      }
+    }
+    __syncthreads();
+    if (warp == 0) {
+      uint32_t rem = lane < kChunkWords ? removed0[lane] : 0xffffffffu;
+      int n = nk;
+      for (int w = 0; w < kChunkWords && n < keep_cap; ++w) {
+        uint32_t avail = ~__shfl_sync(0xffffffffu, rem, w);
+        while (avail != 0u && n < keep_cap) {
+          const int b = __ffs(avail) - 1;
+          const int i = w * 32 + b;
+          if (lane == 0) kept[n] = cbox[i];
+          ++n;
+          if (lane < kChunkWords) rem |= mat[i * kChunkWords + lane];
+          avail = ~__shfl_sync(0xffffffffu, rem, w) & ~((2u << b) - 1u);  // later bits of this word
+        }
+      }
+      if (lane == 0) n_kept = n;
+    }
+    __syncthreads();
+    nk = n_kept;
   }
   if (tid == 0) n_kept = nk;
   __syncthreads();
@@ -370,9 +508,20 @@ OSC_API int osc_yolo_detect_f32(osc_ctx* ctx, const float* output, int B, int fi
     return fail(OSC_EINVAL, "osc_yolo_detect_f32: null pointer");
   if (fault_injected("launch")) return fail(OSC_EFAULT_INJECTED, "injected failure (launch)");
   DetectArgs d{fields, anchors, conf, iou, max_det, max_candidates, class_agnostic ? 1 : 0, transforms};
-  const int smem = kMaxAnchors * 8 + kMaxKeep * static_cast<int>(sizeof(Box));
+  // candidate keys [B][anchors] and their counts [B] in the scratch arena
+  const size_t key_bytes = round_up(static_cast<size_t>(B) * anchors * 8, 256);
+  void* buf = nullptr;
+  OSC_TRY(scratch(ctx, key_bytes + static_cast<size_t>(B) * sizeof(int), &buf));
+  auto* cand_keys = static_cast<unsigned long long*>(buf);
+  int* n_cand = reinterpret_cast<int*>(static_cast<uint8_t*>(buf) + key_bytes);
+  OSC_CUDA(cudaMemsetAsync(n_cand, 0, static_cast<size_t>(B) * sizeof(int), ctx->stream), "cudaMemsetAsync (detect)");
+  OSC_TRY(launch_pdl(ctx, k_det_candidates, dim3(static_cast<unsigned>(B), static_cast<unsigned>((anchors + 255) / 256)),
+                     dim3(256), 0, "k_det_candidates", output, d, cand_keys, n_cand));
+  const int smem = kMaxAnchors * 8 + (kMaxKeep + kChunk) * static_cast<int>(sizeof(Box)) +
+                   (kChunk + 1) * kChunkWords * static_cast<int>(sizeof(uint32_t));
   OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(k_yolo_detect), smem));
-  return launch_pdl(ctx, k_yolo_detect, dim3(B), dim3(kDetThreads), smem, "k_yolo_detect", output, d, dets, counts);
+  return launch_pdl(ctx, k_yolo_detect, dim3(static_cast<unsigned>(B)), dim3(kDetThreads), smem, "k_yolo_detect",
+                    output, d, cand_keys, n_cand, dets, counts);
 }
 
 }  // extern "C"
