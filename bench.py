@@ -702,9 +702,10 @@ class YoloWorkload(Workload):
 
     e2e_mode = ("pipelined serving loop (onnxsharp_b200.serve.DetectPipeline, depth 2): per step each GPU copies "
                 "its images' 1280x720 BGR u8 frames from pinned host memory, one CUDA graph runs the batched "
-                "letterbox, the forward pass and decode + NMS (conf 0.25, IoU 0.45, max 300 per image), the packed "
-                "detections are all-gathered over NCCL and rank 0 reads the whole batch's detections back; device-"
-                "timed from the first H2D to the last D2H, fill and drain included")
+                "letterbox and the forward pass, a second one on its own stream decode + NMS (conf 0.25, IoU 0.45, "
+                "max 300 per image; beside the next batch's forward pass), the packed detections are all-gathered "
+                "over NCCL and rank 0 reads the whole batch's detections back; device-timed from the first H2D to "
+                "the last D2H, fill and drain included")
 
     def e2e_tensor(self, warmup: int, steps: int) -> float:
         """ms per step of FP32 tensor in / FP32 tensor out through yolo.HostPipeline (each rank its own images)."""
@@ -735,6 +736,8 @@ class YoloWorkload(Workload):
         return CpuYolo(self.g, self.params, self.images_h, self.batch).cpu_sample(threads, budget_s)
 
     def close(self):
+        if getattr(self, "pipe", None) is not None:
+            self.pipe.close()
         self.net.close()
 
 

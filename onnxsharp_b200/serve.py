@@ -6,15 +6,20 @@ sharded by image across the GPUs of one node.
 Per submitted batch (one input slot of the plan, `depth` slots round robin):
   1. H2D of the batch's u8 frames from pinned host memory (copy stream);
   2. one CUDA graph on the plan's stream: batched letterbox into the plan's
-     input, the forward pass, the detect tail (argmax, score sort, greedy NMS,
+     input and the forward pass into the slot's output;
+  3. one CUDA graph on the tail stream (its own library context, so its
+     scratch is its own): the detect tail (argmax, score sort, greedy NMS,
      mapping back to source pixels) into a packed detections buffer;
-  3. with a process group of N ranks: an NCCL all-gather of the packed
-     detections over NVLink, so rank 0 holds the whole global batch's result
-     (the single-Net contract: one Forward returns the whole batch);
-  4. D2H of the (gathered) detections on rank 0 (copy stream).
-Consecutive batches overlap: batch i's H2D, batch i-1's graph and batch
-i-2's D2H run at the same time. A slot is reused only after the graph that
-read its frames and the copy that read its detections finished (event waits).
+  4. with a process group of N ranks: an NCCL all-gather of the packed
+     detections over NVLink (tail stream), so rank 0 holds the whole global
+     batch's result (the single-Net contract: one Forward returns the whole
+     batch);
+  5. D2H of the (gathered) detections on rank 0 (copy stream).
+Consecutive batches overlap: batch i's H2D, batch i-1's forward pass, batch
+i-2's detect tail (whose CTAs are one per image, so the SMs it leaves idle run
+the next forward pass) and D2H run at the same time. A slot is reused only
+after the work that read it finished: its frames (the forward pass), its
+output (the detect tail) and its detections (the copy) -- event waits.
 
 Packed detections per image: max_det x 6 floats (class, score, x, y, w, h),
 then per batch B int32 counts, so one collective moves both.
@@ -24,6 +29,7 @@ from __future__ import annotations
 import numpy as np
 
 from . import ops
+from .runtime import Context
 
 
 def letterbox_transforms(batch: int, src_w: int, src_h: int, placement) -> np.ndarray:
@@ -64,6 +70,10 @@ class DetectPipeline:
         self.transforms = torch.from_numpy(letterbox_transforms(B, w, h, pl)).to(dev)
         self.placement = pl
         self.graphs = []
+        self.tail = torch.cuda.Stream(device=dev)
+        self.tail_ctx = Context(net.ctx.device)
+        self.tail_ctx.set_stream(self.tail.cuda_stream)
+        self.tail_graphs = []
         for s in range(depth):
             dets = self.pack[s][: B * max_det * 6].view(B, max_det, 6)
             counts = self.pack[s][B * max_det * 6:].view(torch.int32)
@@ -71,17 +81,28 @@ class DetectPipeline:
             def before(s=s):
                 ops.letterbox_batch(net.ctx, self.frames[s], net.inputs[s], bgr=bgr)
 
-            def after(s=s, dets=dets, counts=counts):
-                ops.yolo_detect_into(net.ctx, net.outputs[s], dets, counts, conf=conf, iou=iou,
+            def tail(s=s, dets=dets, counts=counts):
+                ops.yolo_detect_into(self.tail_ctx, net.outputs[s], dets, counts, conf=conf, iou=iou,
                                      transforms=self.transforms)
 
-            self.graphs.append(net.capture_slot(s, before, after))
+            self.graphs.append(net.capture_slot(s, before))
+            torch.cuda.synchronize(dev)
+            self.tail_graphs.append(self.tail_ctx.capture(tail))
         self.h2d = torch.cuda.Stream(device=dev)
         self.d2h = torch.cuda.Stream(device=dev)
         self.ev_h2d = [torch.cuda.Event() for _ in range(depth)]
-        self.ev_plan = [torch.cuda.Event() for _ in range(depth)]
+        self.ev_fwd = [torch.cuda.Event() for _ in range(depth)]
+        self.ev_plan = [torch.cuda.Event() for _ in range(depth)]  # the slot's detect tail (and gather) done
         self.ev_d2h = [torch.cuda.Event() for _ in range(depth)]
         torch.cuda.synchronize(dev)
+
+    def close(self):
+        """Free the tail graphs and context (the forward graphs belong to the Net)."""
+        self.synchronize()
+        for g in self.tail_graphs:
+            g.close()
+        self.tail_graphs = []
+        self.tail_ctx.close()
 
     def host_buffers(self):
         """(pinned frames [B, H, W, 3] u8, pinned result [world * pack_len] f32) for submit()."""
@@ -101,17 +122,22 @@ class DetectPipeline:
         plan = net.plan_stream()
         with torch.cuda.stream(self.h2d):
             if reuse:
-                self.h2d.wait_event(self.ev_plan[s])  # the graph that read these frames is done
+                self.h2d.wait_event(self.ev_fwd[s])  # the letterbox that read these frames is done
             self.frames[s].copy_(host_frames, non_blocking=True)
             self.ev_h2d[s].record(self.h2d)
         plan.wait_event(self.ev_h2d[s])
         if reuse:
-            plan.wait_event(self.ev_d2h[s])  # the copy that read this slot's detections is done
+            plan.wait_event(self.ev_plan[s])  # the detect tail that read this slot's output is done
         net.launch_graph(self.graphs[s])
+        self.ev_fwd[s].record(plan)
+        self.tail.wait_event(self.ev_fwd[s])
+        if reuse:
+            self.tail.wait_event(self.ev_d2h[s])  # the copy that read this slot's detections is done
+        self.tail_graphs[s].launch()
         if self.world > 1:
-            with torch.cuda.stream(plan):
+            with torch.cuda.stream(self.tail):
                 dist.all_gather_into_tensor(self.gathered[s], self.pack[s], group=self.group)
-        self.ev_plan[s].record(plan)
+        self.ev_plan[s].record(self.tail)
         with torch.cuda.stream(self.d2h):
             self.d2h.wait_event(self.ev_plan[s])
             if host_result is not None:
@@ -133,6 +159,7 @@ class DetectPipeline:
 
     def synchronize(self):
         self.d2h.synchronize()
+        self.tail.synchronize()
         self.net.plan_stream().synchronize()
 
     def bytes_per_step(self) -> tuple[int, int]:
