@@ -242,9 +242,36 @@ struct PwGeom {
   long long y_nstride, res_nstride;
   const float* res;
   // TAPS form only: output geometry, the pixel box (BW x BH <= 128 pixels),
-  // images per phase image, 32-channel blocks per tap, bytes of one A box
-  int OW, OH, BW, BH, tiles_w, N, cp_blocks, a_bytes;
+  // 32-channel blocks per tap, bytes of one A box
+  int OW, OH, BW, BH, tiles_w, cp_blocks, a_bytes;
+  int N;                   // images
+  // split-K (few output tiles, long K): tile t is output tile t % base_tiles,
+  // K slice t / base_tiles = TMEM chunks [slice * cps, slice * cps + cps);
+  // each slice writes its raw sums to ws [ksplit][N][M][HW] and
+  // k_conv_splitk_reduce adds them in slice order and applies the epilogue
+  long long base_tiles;
+  int ksplit, cps;
+  float* ws;
 };
+
+// The tile's output tile and TMEM chunk / k-block range.
+struct PwTile {
+  int ot, pt, n, ks, c_begin, c_end, kb_begin, kb_end;
+};
+__device__ __forceinline__ PwTile pw_tile(const PwGeom& g, long long t, int nchunks, int kkc) {
+  PwTile r;
+  const long long tb = t % g.base_tiles;
+  r.ks = static_cast<int>(t / g.base_tiles);
+  r.ot = static_cast<int>(tb % g.otiles);
+  const long long q = tb / g.otiles;
+  r.pt = static_cast<int>(q % g.ptiles);
+  r.n = static_cast<int>(q / g.ptiles);
+  r.c_begin = r.ks * g.cps;
+  r.c_end = min(nchunks, r.c_begin + g.cps);
+  r.kb_begin = r.c_begin * kkc;
+  r.kb_end = min(g.num_kb, r.c_end * kkc);
+  return r;
+}
 
 // TAPS = false: the pointwise form above. TAPS = true: any K x K / stride
 // conv on the same pixel-major tiles, its A operand read from the phase
@@ -305,13 +332,11 @@ __global__ void __launch_bounds__(pw::kThreads, 1)
       bool ok = true;
       const uint32_t tx_bytes = TAPS ? static_cast<uint32_t>(2 * g.a_bytes + 2 * CF::kB) : static_cast<uint32_t>(CF::kTx);
       for (long long t = blockIdx.x; t < g.tiles && ok; t += gridDim.x) {
-        const int ot = static_cast<int>(t % g.otiles);
-        const long long r = t / g.otiles;
-        const int pt = static_cast<int>(r % g.ptiles);
-        const int n = static_cast<int>(r / g.ptiles);
-        const int p0 = pt * kBM, oc0 = ot * CF::kBN;
+        const PwTile tl = pw_tile(g, t, nchunks, kKC);
+        const int pt = tl.pt, n = tl.n;
+        const int p0 = pt * kBM, oc0 = tl.ot * CF::kBN;
         const int ox0 = TAPS ? (pt % g.tiles_w) * g.BW : 0, oy0 = TAPS ? (pt / g.tiles_w) * g.BH : 0;
-        for (int kb = 0; kb < g.num_kb; ++kb) {
+        for (int kb = tl.kb_begin; kb < tl.kb_end; ++kb) {
           const int s = i % CF::kStages;
           const uint32_t ph = (i / CF::kStages) & 1u;
           if (!mbar_wait(&pb->empty[s], ph ^ 1u, &pb->abort_flag, err)) {
@@ -349,11 +374,12 @@ __global__ void __launch_bounds__(pw::kThreads, 1)
       int i = 0, gc = 0;
       bool ok = true;
       for (long long t = blockIdx.x; t < g.tiles && ok; t += gridDim.x) {
-        const int oc0 = static_cast<int>(t % g.otiles) * CF::kBN;
+        const PwTile tl = pw_tile(g, t, nchunks, kKC);
+        const int oc0 = tl.ot * CF::kBN;
         const int nn = min(CF::kBN, ((g.M - oc0) + 15) & ~15);
         const uint32_t idesc = TAPS ? idesc_tf32(kBM, nn) : idesc_tf32_amn(kBM, nn);
-        int kb = 0;
-        for (int c = 0; c < nchunks && ok; ++c, ++gc) {
+        int kb = tl.kb_begin;
+        for (int c = tl.c_begin; c < tl.c_end && ok; ++c, ++gc) {
           const int buf = gc & 1;
           if (!mbar_wait(&pb->acc_empty[buf], ((gc >> 1) & 1u) ^ 1u, &pb->abort_flag, err)) {
             ok = false;
@@ -409,7 +435,8 @@ __global__ void __launch_bounds__(pw::kThreads, 1)
     int i = 0;
     bool ok = !TAPS;
     for (long long t = blockIdx.x; t < g.tiles && ok; t += gridDim.x) {
-      for (int kb = 0; kb < g.num_kb; ++kb, ++i) {
+      const PwTile tl = pw_tile(g, t, nchunks, kKC);
+      for (int kb = tl.kb_begin; kb < tl.kb_end; ++kb, ++i) {
         const int s = i % CF::kStages;
         const uint32_t ph = (i / CF::kStages) & 1u;
         bool got = mbar_wait(&pb->full[s], ph, &pb->abort_flag, err);
@@ -446,15 +473,13 @@ __global__ void __launch_bounds__(pw::kThreads, 1)
     int gc = 0;
     bool ok = true;
     for (long long t = blockIdx.x; t < g.tiles && ok; t += gridDim.x) {
-      const int ot = static_cast<int>(t % g.otiles);
-      const long long r = t / g.otiles;
-      const int pt = static_cast<int>(r % g.ptiles);
-      const int n = static_cast<int>(r / g.ptiles);
+      const PwTile tl = pw_tile(g, t, nchunks, kKC);
+      const int ot = tl.ot, pt = tl.pt, n = tl.n;
       const int cpw = CF::kColsMax >= 32 && g.M - ot * CF::kBN <= CF::kBN / 2 ? CF::kColsMax / 2 : CF::kColsMax;  // channels per warp
       const int oc0 = ot * CF::kBN + h * cpw;
       const int nvalid = min(cpw, g.M - oc0);  // may be <= 0 for the upper groups of a narrow tile
       float acc[CF::kColsMax];
-      for (int c = 0; c < nchunks; ++c, ++gc) {
+      for (int c = tl.c_begin; c < tl.c_end; ++c, ++gc) {
         const int buf = gc & 1;
         bool got = mbar_wait(&pb->acc_full[buf], (gc >> 1) & 1u, &pb->abort_flag, err);
         got = __all_sync(0xffffffffu, got);
@@ -473,7 +498,7 @@ __global__ void __launch_bounds__(pw::kThreads, 1)
           tmem_ld16(base + gg * 16, r0);
           if (two) tmem_ld16(base + (gg + 1) * 16, r1);
           tmem_wait_ld();
-          if (c == 0) {
+          if (c == tl.c_begin) {
 #pragma unroll
             for (int j = 0; j < 16; ++j) acc[gg * 16 + j] = __uint_as_float(r0[j]);
             if (two) {
@@ -508,7 +533,15 @@ __global__ void __launch_bounds__(pw::kThreads, 1)
         p = pt * kBM + q * 32 + lane;
         pvalid = p < g.HW;
       }
-      if (pvalid && nvalid > 0) {
+      if (pvalid && nvalid > 0 && g.ksplit > 1) {  // this K slice's raw sums
+        float* wp = g.ws + (static_cast<size_t>(tl.ks) * g.N + n) * g.M * static_cast<size_t>(g.HW) +
+                    static_cast<size_t>(oc0) * g.HW + p;
+#pragma unroll
+        for (int j = 0; j < CF::kColsMax; ++j) {
+          if (j >= cpw) break;
+          if (j < nvalid) wp[static_cast<size_t>(j) * g.HW] = acc[j];
+        }
+      } else if (pvalid && nvalid > 0) {
         float* yp = y + static_cast<size_t>(n) * g.y_nstride + static_cast<size_t>(oc0) * g.HW + p;
         const float* rp =
             g.res ? g.res + static_cast<size_t>(n) * g.res_nstride + static_cast<size_t>(oc0) * g.HW + p : nullptr;
@@ -658,6 +691,31 @@ __global__ void __launch_bounds__(256) k_nchw_to_nhwc_split(const float* __restr
   }
 }
 
+// Split-K epilogue of the pixel-major conv: y = act(sum_s ws[s] + bias) (+
+// residual), the K slices added in slice order, then the same bias /
+// activation / residual arithmetic as the kernel's own epilogue.
+__global__ void __launch_bounds__(256) k_conv_splitk_reduce(const float* __restrict__ ws, int ksplit, int N, int M,
+                                                            int HW, const float* __restrict__ bias, int act,
+                                                            const float* __restrict__ res, long long res_nstride,
+                                                            float* __restrict__ y, long long y_nstride) {
+  griddep_wait();  // launched with launch_pdl: the previous kernel has completed past here
+  griddep_launch();
+  const long long total = static_cast<long long>(N) * M * HW;
+  with_act(act, [&](auto tag) {
+    constexpr int ACT = decltype(tag)::value;
+    for (long long i = blockIdx.x * 256ll + threadIdx.x; i < total; i += static_cast<long long>(gridDim.x) * 256) {
+      const int p = static_cast<int>(i % HW);
+      const long long r = i / HW;
+      const int oc = static_cast<int>(r % M), n = static_cast<int>(r / M);
+      float v = ws[i];
+      for (int k = 1; k < ksplit; ++k) v = __fadd_rn(v, ws[k * total + i]);
+      float o = act_fast<ACT>(__fadd_rn(v, bias != nullptr ? __ldg(bias + oc) : 0.0f));
+      if (res != nullptr) o = __fadd_rn(__ldg(res + n * res_nstride + static_cast<long long>(oc) * HW + p), o);
+      y[n * y_nstride + static_cast<long long>(oc) * HW + p] = o;
+    }
+  });
+}
+
 // W[M][C][kh][kw] -> hi/lo [M][(ky*kw + kx)*Cp + c], zero for c >= C.
 __global__ void k_pack_conv_w(const float* __restrict__ w, int M, int C, int kh, int kw, int Cp, float* __restrict__ hi,
                               float* __restrict__ lo) {
@@ -677,6 +735,34 @@ __global__ void k_pack_conv_w(const float* __restrict__ w, int M, int C, int kh,
 }
 
 int floor_div(int a, int b) { return a >= 0 ? a / b : -((-a + b - 1) / b); }
+
+// Split-K for the pixel-major conv when its output tiles would leave most SMs
+// idle (small batches, deep layers: e.g. 256 -> 64 3x3 at 20x20 and B=1 is 4
+// tiles of 72 k-blocks): K is cut into slices of at least two TMEM chunks so
+// that tiles x slices fills the SMs once. Sets base_tiles / ksplit / cps /
+// tiles; returns the workspace bytes (0 without a split).
+static size_t choose_ksplit(const osc_ctx* ctx, PwGeom& g) {
+  const int nchunks = (g.num_kb + pw::kKC - 1) / pw::kKC;
+  g.base_tiles = g.tiles;
+  g.ksplit = 1;
+  g.cps = nchunks;
+  g.ws = nullptr;
+  if (g.tiles >= ctx->num_sms || nchunks < 4) return 0;
+  const int s = static_cast<int>(std::min<long long>(ctx->num_sms / g.tiles, nchunks / 2));
+  if (s < 2) return 0;
+  g.cps = (nchunks + s - 1) / s;
+  g.ksplit = (nchunks + g.cps - 1) / g.cps;
+  g.tiles = g.base_tiles * g.ksplit;
+  return round_up(static_cast<size_t>(g.ksplit) * g.N * g.M * static_cast<size_t>(g.HW) * sizeof(float), 256);
+}
+
+static int splitk_reduce(osc_ctx* ctx, const PwGeom& g, const float* bias, int act, float* y) {
+  const long long total = static_cast<long long>(g.N) * g.M * g.HW;
+  const long long blocks = std::min<long long>((total + 255) / 256, static_cast<long long>(ctx->num_sms) * 8);
+  return launch_pdl(ctx, k_conv_splitk_reduce, dim3(static_cast<unsigned>(blocks)), dim3(256), 0,
+                    "k_conv_splitk_reduce", g.ws, g.ksplit, g.N, g.M, g.HW, bias, act, g.res, g.res_nstride, y,
+                    g.y_nstride);
+}
 
 }  // namespace
 
@@ -717,10 +803,16 @@ static int conv1x1_launch(osc_ctx* ctx, const float* x, long long x_nstride, int
   g.otiles = (w->M + pw::Cfg<BN>::kBN - 1) / pw::Cfg<BN>::kBN;
   g.tiles = static_cast<long long>(N) * g.ptiles * g.otiles;
   g.num_kb = w->Cp / kBK;
+  g.N = N;
   g.act = act;
   g.y_nstride = y_nstride;
   g.res_nstride = res_nstride;
   g.res = res;
+  if (const size_t ws_bytes = choose_ksplit(ctx, g)) {
+    void* ws = nullptr;
+    OSC_TRY(scratch(ctx, ws_bytes, &ws));
+    g.ws = static_cast<float*>(ws);
+  }
   CUtensorMap mX, mWh, mWl;
   {
     const uint64_t dims[3] = {static_cast<uint64_t>(HW), static_cast<uint64_t>(C), static_cast<uint64_t>(N)};
@@ -740,8 +832,9 @@ static int conv1x1_launch(osc_ctx* ctx, const float* x, long long x_nstride, int
   OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(k_conv_px_tf32x3<false, BN>), smem));
   const long long grid = std::min<long long>(g.tiles, ctx->num_sms);
   const ConvTaps no_taps{};
-  return launch_pdl(ctx, k_conv_px_tf32x3<false, BN>, dim3(static_cast<unsigned>(grid)), dim3(pw::kThreads), smem,
-                    "k_conv_px_tf32x3", mX, mX, mWh, mWl, g, no_taps, bias, y, ctx->d_err);
+  OSC_TRY(launch_pdl(ctx, k_conv_px_tf32x3<false, BN>, dim3(static_cast<unsigned>(grid)), dim3(pw::kThreads), smem,
+                     "k_conv_px_tf32x3", mX, mX, mWh, mWl, g, no_taps, bias, y, ctx->d_err));
+  return g.ksplit > 1 ? splitk_reduce(ctx, g, bias, act, y) : OSC_OK;
 }
 
 // Layers with at most 64 output channels take the 64-channel tile (4-stage
@@ -761,12 +854,17 @@ static int conv1x1_tf32x3(osc_ctx* ctx, const float* x, long long x_nstride, int
 // when the channel-major kernel would not fill two waves of the SMs (small
 // batches: its 128-channel tiles leave half the MMA rows empty at <= 64
 // output channels, and the persistent pixel-major kernel has twice the tiles).
+// Wider layers take pixel tiles when the channel-major grid is under one wave
+// (measured at B=8: 128->128 3x3 s2 at 40x40 16 % faster, at 20x20 10 %).
 static bool px_taps_ok(const osc_ctx* ctx, int M, int N, int OH, int OW) {
-  if (M > 64) return false;
-  if (static_cast<long>(OH) * OW <= 576) return true;
+  if (M > pw::kMaxBias) return false;
   int BW = 0, BH = 0;
   choose_box(OH, OW, &BW, &BH);
   const long tiles = static_cast<long>(N) * ((OW + BW - 1) / BW) * ((OH + BH - 1) / BH);
+  // wider layers: when the channel-major grid is under one wave, the pixel
+  // tiles (split along K where they are still few) fill the SMs
+  if (M > 64) return tiles * ((M + kBM - 1) / kBM) < ctx->num_sms;
+  if (static_cast<long>(OH) * OW <= 576) return true;
   return tiles < 2L * ctx->num_sms;
 }
 
@@ -787,11 +885,11 @@ static void choose_px_box(int OH, int OW, int* BW, int* BH) {
   }
 }
 
-static int conv_px_taps(osc_ctx* ctx, const float* xh, const float* xl, int N, int Hp, int Wp, int s,
-                        const osc_conv_weights* w, const ConvTaps& taps, const float* bias, int act, const float* res,
-                        long long res_nstride, float* y, long long y_nstride, int OH, int OW) {
-  if (w->M > pw::kMaxBias) return fail(OSC_EUNSUPPORTED, "conv: %d output channels", w->M);
-  PwGeom g{};
+// Geometry of the pixel-major K x K conv (split-K included); returns the
+// split workspace bytes (0 without a split).
+static size_t px_taps_geom(const osc_ctx* ctx, const osc_conv_weights* w, int N, int OH, int OW, int act,
+                           const float* res, long long res_nstride, long long y_nstride, PwGeom& g) {
+  g = PwGeom{};
   g.C = w->C;
   g.HW = OH * OW;
   g.M = w->M;
@@ -803,13 +901,20 @@ static int conv_px_taps(osc_ctx* ctx, const float* xh, const float* xl, int N, i
   g.otiles = (w->M + pw::Cfg<128>::kBN - 1) / pw::Cfg<128>::kBN;
   g.tiles = static_cast<long long>(N) * g.ptiles * g.otiles;
   g.cp_blocks = w->Cp / kBK;
-  g.num_kb = taps.n_taps * g.cp_blocks;
+  g.num_kb = w->kh * w->kw * g.cp_blocks;
   g.N = N;
   g.a_bytes = g.BW * g.BH * kBK * 4;
   g.act = act;
   g.y_nstride = y_nstride;
   g.res_nstride = res_nstride;
   g.res = res;
+  return choose_ksplit(ctx, g);
+}
+
+// g from px_taps_geom, with g.ws set when it asked for a workspace.
+static int conv_px_taps(osc_ctx* ctx, const float* xh, const float* xl, int N, int Hp, int Wp, int s,
+                        const osc_conv_weights* w, const ConvTaps& taps, const PwGeom& g, const float* bias,
+                        float* y) {
   CUtensorMap mXh, mXl, mWh, mWl;
   {
     const uint64_t dims[4] = {static_cast<uint64_t>(w->Cp), static_cast<uint64_t>(Wp), static_cast<uint64_t>(Hp),
@@ -830,8 +935,9 @@ static int conv_px_taps(osc_ctx* ctx, const float* xh, const float* xl, int N, i
   const int smem = pw::Cfg<128>::kSmemBase + static_cast<int>(round_up(static_cast<size_t>(w->M) * 4, 16));
   OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(k_conv_px_tf32x3<true, 128>), smem));
   const long long grid = std::min<long long>(g.tiles, ctx->num_sms);
-  return launch_pdl(ctx, k_conv_px_tf32x3<true, 128>, dim3(static_cast<unsigned>(grid)), dim3(pw::kThreads), smem,
-                    "k_conv_px_tf32x3", mXh, mXl, mWh, mWl, g, taps, bias, y, ctx->d_err);
+  OSC_TRY(launch_pdl(ctx, k_conv_px_tf32x3<true, 128>, dim3(static_cast<unsigned>(grid)), dim3(pw::kThreads), smem,
+                     "k_conv_px_tf32x3", mXh, mXl, mWh, mWl, g, taps, bias, y, ctx->d_err));
+  return g.ksplit > 1 ? splitk_reduce(ctx, g, bias, g.act, y) : OSC_OK;
 }
 
 int conv_tf32x3(osc_ctx* ctx, const float* x, long long x_nstride, int N, int C, int H, int W, const osc_conv_weights* w,
@@ -843,13 +949,17 @@ int conv_tf32x3(osc_ctx* ctx, const float* x, long long x_nstride, int N, int C,
   const int s = sh;
   const int Hp = (H + s - 1) / s, Wp = (W + s - 1) / s;
   const int Cp = w->Cp;
-  // 1. input transform into the scratch arena
+  const bool px = px_taps_ok(ctx, w->M, N, OH, OW);
+  PwGeom pg{};
+  const size_t ws_bytes = px ? px_taps_geom(ctx, w, N, OH, OW, act, res, res_nstride, y_nstride, pg) : 0;
+  // 1. input transform into the scratch arena (then the split-K workspace)
   const size_t plane = static_cast<size_t>(s) * s * N * Hp * Wp * Cp;
   const size_t half = round_up(plane * sizeof(float), 256);
   void* buf = nullptr;
-  OSC_TRY(scratch(ctx, 2 * half, &buf));
+  OSC_TRY(scratch(ctx, 2 * half + ws_bytes, &buf));
   float* xh = static_cast<float*>(buf);
   float* xl = reinterpret_cast<float*>(static_cast<uint8_t*>(buf) + half);
+  if (ws_bytes != 0) pg.ws = reinterpret_cast<float*>(static_cast<uint8_t*>(buf) + 2 * half);
   {
     if (s > kPhaseMaxS) return fail(OSC_EUNSUPPORTED, "conv: stride %d (at most %d)", s, kPhaseMaxS);
     // s == 1: one z per output row; s > 1: one z per input row (all phases of it), Hp*s rows per image
@@ -878,8 +988,7 @@ int conv_tf32x3(osc_ctx* ctx, const float* x, long long x_nstride, int N, int C,
       taps.dy[t] = static_cast<short>(floor_div(oy - py, s));
       taps.dx[t] = static_cast<short>(floor_div(ox - px, s));
     }
-  if (px_taps_ok(ctx, w->M, N, OH, OW)) return conv_px_taps(ctx, xh, xl, N, Hp, Wp, s, w, taps, bias, act, res, res_nstride, y,
-                                              y_nstride, OH, OW);
+  if (px) return conv_px_taps(ctx, xh, xl, N, Hp, Wp, s, w, taps, pg, bias, y);
   ConvGeom g{};
   g.N = N;
   g.M = w->M;

@@ -69,6 +69,9 @@ def test_conv_config2_batch16_all_images(ctx):
         (1, 8, 17, 17, 8, 7, 3, (3, 3, 3, 3), 1, 0),       # stride 3, 7x7
         (1, 64, 160, 160, 64, 3, 2, (1, 1, 1, 1), 1, 1),   # <= 64 channels, few tiles: pixel-major at 80x80
         (2, 48, 83, 97, 40, 3, 1, (1, 1, 1, 1), 1, 1),     # pixel-major, ragged image, 40 channels
+        (1, 256, 20, 20, 64, 3, 1, (1, 1, 1, 1), 1, 1),    # 4 pixel tiles of 72 k-blocks: K split in 18 slices
+        (1, 128, 40, 40, 128, 3, 2, (1, 1, 1, 1), 1, 1),   # under one channel-major wave: pixel tiles, 9 K slices
+        (2, 96, 13, 11, 200, 3, 1, (1, 1, 1, 1), 1, 3),    # split K, 2 channel tiles (200 = 128 + 72), ragged
     ],
 )
 def test_conv_geometries(ctx, N, C, H, W, M, k, stride, pads, dil, act):
@@ -144,3 +147,28 @@ def test_conv_pointwise_views_and_residual(ctx):
     got = out_big.cpu().numpy()
     assert rel_err(got[:, 64:128], ref) <= TOL
     assert not got[:, :64].any() and not got[:, 128:].any()
+
+
+@pytest.mark.parametrize("k,C,M", [(3, 256, 64), (1, 512, 128)])
+def test_conv_split_k_views_and_residual(ctx, k, C, M):
+    """Split-K (few output tiles, long K) through the view / residual path: the
+    K slices' partial sums are added by the reduce kernel, which then applies
+    bias, SiLU and the residual into a channel slice of a wider output."""
+    import torch
+
+    from onnxsharp_b200 import ops
+    from onnxsharp_b200.runtime import ConvWeights
+
+    rng = np.random.default_rng(37 + k)
+    x = rng.uniform(0, 1, (1, C, 20, 20)).astype(np.float32)
+    w = (rng.normal(0, 1, (M, C, k, k)) * np.sqrt(2.0 / (C * k * k))).astype(np.float32)
+    b = rng.normal(0, 0.01, M).astype(np.float32)
+    res = rng.normal(0, 1, (1, M, 20, 20)).astype(np.float32)
+    out_big = torch.zeros(1, M + 64, 20, 20, device="cuda")
+    ops.conv2d_ex(ctx, torch.from_numpy(x).cuda(), ConvWeights(ctx, torch.from_numpy(w).cuda(), w.shape),
+                  torch.from_numpy(b).cuda(), out_big[:, 32:32 + M], 1, k // 2, 1, 1, torch.from_numpy(res).cuda())
+    ctx.synchronize()
+    ref = res + oracle.conv2d(x, w, b, pads=(k // 2,) * 4, act=1)
+    got = out_big.cpu().numpy()
+    assert rel_err(got[:, 32:32 + M], ref) <= TOL
+    assert not got[:, :32].any() and not got[:, 32 + M:].any()
