@@ -642,51 +642,59 @@ __global__ void __launch_bounds__(256) k_nchw_to_phase_nhwc(const float* __restr
   }
 }
 
-// Stride-1 fast path of the transform (a single phase image): each block
-// moves a 32-channel x 32-pixel tile of one input row with one float4 load
-// and one float4 store (hi and lo) per thread.
+// Stride-1 fast path of the transform (a single phase image): NHWC of a
+// stride-1 conv is [n][h*W + w][c], so per image it is a plain transpose of
+// [C][HW] -> [HW][Cp] over the flattened plane (no per-row tiles, whose
+// short rows at 20x20 or 40x40 would leave a third of each tile empty). One
+// block moves 32 channels x 64 pixels: two 16-byte loads and two 16-byte hi
+// and lo stores per thread.
 __global__ void __launch_bounds__(256) k_nchw_to_nhwc_split(const float* __restrict__ x, long long x_nstride, int N,
-                                                            int C, int H, int W, int Cp, int z_base,
+                                                            int C, int HW, int Cp, int z_base,
                                                             float* __restrict__ hi, float* __restrict__ lo) {
   griddep_wait();  // launched with launch_pdl: the previous kernel has completed past here
   griddep_launch();
-  __shared__ float tile[32][33];
-  const int w0 = blockIdx.x * 32;
+  __shared__ float tile[32][65];
+  const int p0 = blockIdx.x * 64;
   const int c0 = blockIdx.y * 32;
-  const int z = z_base + blockIdx.z;  // n * H + h
-  const int h = z % H, n = z / H;
+  const int n = z_base + blockIdx.z;
   const int tid = threadIdx.x;
   {
-    const int c = c0 + (tid >> 3), w = w0 + (tid & 7) * 4;
-    float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    const int c = c0 + (tid >> 3), pl = (tid & 7) * 8, pp = p0 + pl;
+    float v[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) v[q] = 0.0f;
     if (c < C) {
-      const float* src = x + static_cast<size_t>(n) * x_nstride + (static_cast<size_t>(c) * H + h) * W + w;
-      if (w + 4 <= W && (reinterpret_cast<uintptr_t>(src) & 15u) == 0) {
-        const float4 t = __ldg(reinterpret_cast<const float4*>(src));
-        v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+      const float* src = x + static_cast<size_t>(n) * x_nstride + static_cast<size_t>(c) * HW + pp;
+      if (pp + 8 <= HW && (reinterpret_cast<uintptr_t>(src) & 15u) == 0) {
+        const float4 t0 = __ldg(reinterpret_cast<const float4*>(src));
+        const float4 t1 = __ldg(reinterpret_cast<const float4*>(src) + 1);
+        v[0] = t0.x; v[1] = t0.y; v[2] = t0.z; v[3] = t0.w;
+        v[4] = t1.x; v[5] = t1.y; v[6] = t1.z; v[7] = t1.w;
       } else {
 #pragma unroll
-        for (int q = 0; q < 4; ++q)
-          if (w + q < W) v[q] = src[q];
+        for (int q = 0; q < 8; ++q)
+          if (pp + q < HW) v[q] = __ldg(src + q);
       }
     }
 #pragma unroll
-    for (int q = 0; q < 4; ++q) tile[tid >> 3][(tid & 7) * 4 + q] = v[q];
+    for (int q = 0; q < 8; ++q) tile[tid >> 3][pl + q] = v[q];
   }
   __syncthreads();
   {
-    const int w = w0 + (tid >> 3), cq = (tid & 7) * 4;
-    if (w < W && c0 + cq < Cp) {
-      float h4[4], l4[4];
+    const int pl = tid >> 2, cq = (tid & 3) * 8, pp = p0 + pl;
+    if (pp < HW) {
+      float h8[8], l8[8];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const float v = tile[cq + q][tid >> 3];
-        h4[q] = to_tf32(v);
-        l4[q] = __fsub_rn(v, h4[q]);
+      for (int q = 0; q < 8; ++q) {
+        const float v = tile[cq + q][pl];
+        h8[q] = to_tf32(v);
+        l8[q] = __fsub_rn(v, h8[q]);
       }
-      const size_t o = ((static_cast<size_t>(n) * H + h) * W + w) * Cp + c0 + cq;
-      *reinterpret_cast<float4*>(hi + o) = make_float4(h4[0], h4[1], h4[2], h4[3]);
-      *reinterpret_cast<float4*>(lo + o) = make_float4(l4[0], l4[1], l4[2], l4[3]);
+      const size_t o = (static_cast<size_t>(n) * HW + pp) * Cp + c0 + cq;
+      *reinterpret_cast<float4*>(hi + o) = make_float4(h8[0], h8[1], h8[2], h8[3]);
+      *reinterpret_cast<float4*>(hi + o + 4) = make_float4(h8[4], h8[5], h8[6], h8[7]);
+      *reinterpret_cast<float4*>(lo + o) = make_float4(l8[0], l8[1], l8[2], l8[3]);
+      *reinterpret_cast<float4*>(lo + o + 4) = make_float4(l8[4], l8[5], l8[6], l8[7]);
     }
   }
 }
@@ -855,15 +863,19 @@ static int conv1x1_tf32x3(osc_ctx* ctx, const float* x, long long x_nstride, int
 // batches: its 128-channel tiles leave half the MMA rows empty at <= 64
 // output channels, and the persistent pixel-major kernel has twice the tiles).
 // Wider layers take pixel tiles when the channel-major grid is under one wave
-// (measured at B=8: 128->128 3x3 s2 at 40x40 16 % faster, at 20x20 10 %).
+// (measured at B=8: 128->128 3x3 s2 at 40x40 16 % faster, at 20x20 10 %),
+// and up to 128 channels on images of at most 24x24 (128->128 3x3 s2 at
+// 20x20 and B=64: 19 % faster).
 static bool px_taps_ok(const osc_ctx* ctx, int M, int N, int OH, int OW) {
   if (M > pw::kMaxBias) return false;
   int BW = 0, BH = 0;
   choose_box(OH, OW, &BW, &BH);
   const long tiles = static_cast<long>(N) * ((OW + BW - 1) / BW) * ((OH + BH - 1) / BH);
   // wider layers: when the channel-major grid is under one wave, the pixel
-  // tiles (split along K where they are still few) fill the SMs
-  if (M > 64) return tiles * ((M + kBM - 1) / kBM) < ctx->num_sms;
+  // tiles (split along K where they are still few) fill the SMs; up to 128
+  // channels also on small images
+  if (M > 64)
+    return tiles * ((M + kBM - 1) / kBM) < ctx->num_sms || (M <= 128 && static_cast<long>(OH) * OW <= 576);
   if (static_cast<long>(OH) * OW <= 576) return true;
   return tiles < 2L * ctx->num_sms;
 }
@@ -962,14 +974,16 @@ int conv_tf32x3(osc_ctx* ctx, const float* x, long long x_nstride, int N, int C,
   if (ws_bytes != 0) pg.ws = reinterpret_cast<float*>(static_cast<uint8_t*>(buf) + 2 * half);
   {
     if (s > kPhaseMaxS) return fail(OSC_EUNSUPPORTED, "conv: stride %d (at most %d)", s, kPhaseMaxS);
-    // s == 1: one z per output row; s > 1: one z per input row (all phases of it), Hp*s rows per image
-    const long zt = s == 1 ? static_cast<long>(N) * Hp : static_cast<long>(N) * Hp * s;
+    // s == 1: one z per image (flattened planes); s > 1: one z per input row (all phases of it), Hp*s rows per image
+    const long zt = s == 1 ? static_cast<long>(N) : static_cast<long>(N) * Hp * s;
     const long zmax = 65535;  // gridDim.z limit: split into several launches
     for (long z0 = 0; z0 < zt; z0 += zmax) {
-      dim3 grid((Wp + 31) / 32, Cp / 32, static_cast<unsigned>(std::min(zmax, zt - z0)));
+      const unsigned gx = s == 1 ? static_cast<unsigned>((static_cast<long>(H) * W + 63) / 64)
+                                 : static_cast<unsigned>((Wp + 31) / 32);
+      dim3 grid(gx, Cp / 32, static_cast<unsigned>(std::min(zmax, zt - z0)));
       if (s == 1)
         OSC_TRY(launch_pdl(ctx, k_nchw_to_nhwc_split, grid, dim3(256), 0, "k_nchw_to_nhwc_split", x, x_nstride, N, C,
-                           H, W, Cp, static_cast<int>(z0), xh, xl));
+                           H * W, Cp, static_cast<int>(z0), xh, xl));
       else
         OSC_TRY(launch_pdl(ctx, k_nchw_to_phase_nhwc, grid, dim3(256), 0, "k_nchw_to_phase_nhwc", x, x_nstride, N, C,
                            H, W, s, Hp, Wp, Cp, static_cast<int>(z0), xh, xl));
