@@ -863,6 +863,190 @@ __global__ void k_softmax_split_reg(const float* __restrict__ S, long long rows,
   }
 }
 
+// YOLO11's PSA attention fused in one kernel for its own head shape (key
+// dim 32, head dim 64, up to kPsaMaxT tokens): one CTA per (block of QB
+// query tokens, head, image), everything in shared memory, FP32 FMA on the
+// CUDA cores -- the products are small (32 x T and T x 64 per query), so the
+// composed path's S / P round trips through HBM and its six launches cost
+// more than the arithmetic.
+//   1. K^T [T][32] into shared memory; each thread keeps its query's 32 q
+//      values in registers: S[n][m] = fl(q_n . k_m) * scale (FMA over c);
+//   2. each warp takes rows of S through the reference's softmax (max, the
+//      8 partial-sum chains of ref_exp, the expf tail, one reciprocal: the
+//      same steps as k_softmax_split_reg), P in place, FP32;
+//   3. V^T [T][64] over K^T's space (copied while the softmax runs);
+//      out[d][n] = sum_m v[d][m] P[n][m] (FMA over m in order), written
+//      channel-major like the composed path.
+constexpr int kPsaKd = 32, kPsaHd = 64, kPsaMaxT = kSoftRegs * 32;
+constexpr int kPsaKPitch = kPsaKd + 4, kPsaVPitch = kPsaHd + 4;  // 16-byte rows, fewer bank conflicts
+
+template <int QB, int NT>
+__global__ void __launch_bounds__(NT, 1)
+    k_psa_fused(const float* __restrict__ qkv, long long qkv_nstride, int heads, int T, float scale,
+                float* __restrict__ out, long long out_nstride) {
+  griddep_wait();  // launched with launch_pdl: the previous kernel has completed past here
+  griddep_launch();
+  constexpr int G = NT / QB;            // thread groups (key groups in phase 1, channel groups in phase 3)
+  constexpr int DPT = kPsaHd / G;       // output channels per thread in phase 3
+  constexpr int NW = NT / 32;
+  static_assert(NT % QB == 0 && kPsaHd % G == 0 && DPT % 4 == 0, "PSA tile shape");
+  extern __shared__ __align__(16) float psa_smem[];
+  const int Tp = (T + 3) & ~3;
+  const int ppitch = Tp + 4;            // P rows: 16-byte aligned
+  float* kv = psa_smem;                 // K^T [Tp][36], later V^T [Tp][68]
+  float* P = psa_smem + static_cast<size_t>(Tp) * kPsaVPitch;  // [QB][ppitch]
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int n0 = blockIdx.x * QB;
+  const float* base = qkv + static_cast<long long>(b) * qkv_nstride +
+                      static_cast<long long>(h) * (2 * kPsaKd + kPsaHd) * T;
+  const float* qg = base;
+  const float* kg = base + static_cast<long long>(kPsaKd) * T;
+  const float* vg = base + static_cast<long long>(2 * kPsaKd) * T;
+  // 1. K^T (asynchronous 4-byte copies, all in flight at once) and S (four
+  //    keys per step: independent FMA chains)
+  for (int c = warp; c < kPsaKd; c += NW)
+    for (int m = lane; m < T; m += 32) cp_async4(kv + m * kPsaKPitch + c, kg + static_cast<long long>(c) * T + m, true);
+  cp_async_commit();
+  const int n = tid % QB, g = tid / QB;
+  const bool nvalid = n0 + n < T;
+  float q[kPsaKd];
+#pragma unroll
+  for (int c = 0; c < kPsaKd; ++c) q[c] = nvalid ? __ldg(qg + static_cast<long long>(c) * T + n0 + n) : 0.0f;
+  cp_async_wait<0>();
+  __syncthreads();
+  for (int m0 = g; m0 < T; m0 += 4 * G) {
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    const float4* kr[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) kr[u] = reinterpret_cast<const float4*>(kv + min(m0 + u * G, T - 1) * kPsaKPitch);
+#pragma unroll
+    for (int c4 = 0; c4 < kPsaKd / 4; ++c4) {
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const float4 k4 = kr[u][c4];
+        acc[u] = __fmaf_rn(q[4 * c4 + 0], k4.x, acc[u]);
+        acc[u] = __fmaf_rn(q[4 * c4 + 1], k4.y, acc[u]);
+        acc[u] = __fmaf_rn(q[4 * c4 + 2], k4.z, acc[u]);
+        acc[u] = __fmaf_rn(q[4 * c4 + 3], k4.w, acc[u]);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (m0 + u * G < T) P[n * ppitch + m0 + u * G] = __fmul_rn(acc[u], scale);
+  }
+  __syncthreads();
+  // V^T over K^T (zero rows up to Tp), landing while the softmax runs
+  for (int d = warp; d < kPsaHd; d += NW)
+    for (int m = lane; m < Tp; m += 32)
+      cp_async4(kv + m * kPsaVPitch + d, vg + static_cast<long long>(d) * T + min(m, T - 1), m < T);
+  cp_async_commit();
+  // 2. softmax per row (rows past T are never stored)
+  const int vend = T & ~7;
+  for (int r = warp; r < QB; r += NW) {
+    if (n0 + r >= T) break;
+    float* pr = P + r * ppitch;
+    float v[kSoftRegs];
+#pragma unroll
+    for (int k = 0; k < kSoftRegs; ++k) {
+      const int j = lane + 32 * k;
+      v[k] = j < T ? pr[j] : -INFINITY;
+    }
+    float mx = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < kSoftRegs; ++k) mx = fmaxf(mx, v[k]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float e[kSoftRegs];
+#pragma unroll
+    for (int k = 0; k < kSoftRegs; ++k) {
+      const int j = lane + 32 * k;
+      e[k] = j < vend ? ref_exp(__fsub_rn(v[k], mx)) : (j < T ? expf(__fsub_rn(v[k], mx)) : 0.0f);
+    }
+    float part = 0.0f;  // chain (lane & 7), meaningful in lanes 0..7
+#pragma unroll
+    for (int k = 0; k < kSoftRegs; ++k) {
+      if (32 * k >= vend) break;
+#pragma unroll
+      for (int qq = 0; qq < 4; ++qq) {
+        const float t = __shfl_sync(0xffffffffu, e[k], (lane & 7) + 8 * qq);
+        if (32 * k + 8 * qq + (lane & 7) < vend) part = __fadd_rn(part, t);
+      }
+    }
+    float total = 0.0f;
+    for (int l = 0; l < 8; ++l) total = __fadd_rn(total, __shfl_sync(0xffffffffu, part, l));
+    for (int j = vend; j < T; ++j) {  // scalar tail in order (uniform across the warp)
+      const int kk = j >> 5;
+      float mine = 0.0f;
+#pragma unroll
+      for (int k = 0; k < kSoftRegs; ++k)
+        if (k == kk) mine = e[k];
+      total = __fadd_rn(total, __shfl_sync(0xffffffffu, mine, j & 31));
+    }
+    const float inv = __fdiv_rn(1.0f, total);
+#pragma unroll
+    for (int k = 0; k < kSoftRegs; ++k) {
+      const int j = lane + 32 * k;
+      if (j < Tp) pr[j] = j < T ? __fmul_rn(e[k], inv) : 0.0f;
+    }
+  }
+  // 3. out = V P^T
+  cp_async_wait<0>();
+  __syncthreads();
+  if (!nvalid) return;
+  const int d0 = g * DPT;
+  float acc[DPT];
+#pragma unroll
+  for (int j = 0; j < DPT; ++j) acc[j] = 0.0f;
+  const float* pr = P + n * ppitch;
+  for (int m = 0; m < Tp; m += 4) {
+    const float4 p4 = *reinterpret_cast<const float4*>(pr + m);
+    const float pm[4] = {p4.x, p4.y, p4.z, p4.w};
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const float4* vr = reinterpret_cast<const float4*>(kv + (m + u) * kPsaVPitch + d0);
+#pragma unroll
+      for (int j4 = 0; j4 < DPT / 4; ++j4) {
+        const float4 v4 = vr[j4];
+        acc[4 * j4 + 0] = __fmaf_rn(v4.x, pm[u], acc[4 * j4 + 0]);
+        acc[4 * j4 + 1] = __fmaf_rn(v4.y, pm[u], acc[4 * j4 + 1]);
+        acc[4 * j4 + 2] = __fmaf_rn(v4.z, pm[u], acc[4 * j4 + 2]);
+        acc[4 * j4 + 3] = __fmaf_rn(v4.w, pm[u], acc[4 * j4 + 3]);
+      }
+    }
+  }
+  float* og = out + static_cast<long long>(b) * out_nstride + static_cast<long long>(h) * kPsaHd * T + n0 + n;
+#pragma unroll
+  for (int j = 0; j < DPT; ++j) og[static_cast<long long>(d0 + j) * T] = acc[j];
+}
+
+static size_t psa_fused_smem(int T, int QB) {
+  const size_t Tp = (static_cast<size_t>(T) + 3) & ~size_t(3);
+  return (Tp * kPsaVPitch + static_cast<size_t>(QB) * (Tp + 4)) * sizeof(float);
+}
+
+// The fused kernel when the head shape is YOLO11's and the tiles fit; returns
+// OSC_EUNSUPPORTED (nothing launched) otherwise. Small batches take 16-query
+// blocks (more CTAs), larger ones 64 (fewer K / V reloads).
+int psa_fused(osc_ctx* ctx, const float* qkv, long long qkv_nstride, int B, int heads, int kd, int hd, int T,
+              float scale, float* out, long long out_nstride) {
+  if (kd != kPsaKd || hd != kPsaHd || T > kPsaMaxT || heads > 65535 || B > 65535) return OSC_EUNSUPPORTED;
+  const long long blocks64 = static_cast<long long>(B) * heads * ((T + 63) / 64);
+  const bool small = blocks64 < 2LL * ctx->num_sms;
+  const int QB = small ? 16 : 64;
+  const size_t smem = psa_fused_smem(T, QB);
+  if (smem > 227 * 1024) return OSC_EUNSUPPORTED;
+  const dim3 grid(static_cast<unsigned>((T + QB - 1) / QB), static_cast<unsigned>(heads), static_cast<unsigned>(B));
+  if (small) {
+    OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(k_psa_fused<16, 256>), static_cast<int>(smem)));
+    return launch_pdl(ctx, k_psa_fused<16, 256>, grid, dim3(256), smem, "k_psa_fused", qkv, qkv_nstride, heads, T,
+                      scale, out, out_nstride);
+  }
+  OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(k_psa_fused<64, 512>), static_cast<int>(smem)));
+  return launch_pdl(ctx, k_psa_fused<64, 512>, grid, dim3(512), smem, "k_psa_fused", qkv, qkv_nstride, heads, T,
+                    scale, out, out_nstride);
+}
+
 // YOLO11's PSA attention (the exported MatMul -> Mul -> Softmax -> MatMul
 // chain) on the tensor cores, per image b and head h of qkv [B][heads*(2kd+hd)][T]:
 //   S = (q^T k) * scale        [T][T]   (batched 3xTF32 product, scale in the epilogue)

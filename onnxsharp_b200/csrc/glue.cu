@@ -334,13 +334,6 @@ __global__ void __launch_bounds__(kDw3Threads) k_dw3s1_v4(const float* __restric
 // the chain is acc = bias, then fmaf over (ic, ky, kx) ascending, the im2col
 // order of ConvKernels.cs:525-654, so the result equals the reference's
 // im2col path (padded taps give fmaf(w, 0, acc)).
-__device__ __forceinline__ void cp_async4(float* dst, const float* src, bool valid) {
-  const unsigned d = static_cast<unsigned>(__cvta_generic_to_shared(dst));
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(d), "l"(src), "r"(valid ? 4 : 0) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int NPEND>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(NPEND) : "memory"); }
 
 // Packed FP32 (two lanes of a 64-bit register): fma.rn.f32x2 rounds each
 // lane exactly as fmaf, so a pair of accumulators takes one instruction.
@@ -1366,7 +1359,9 @@ OSC_API int osc_layernorm_f32(osc_ctx* ctx, const float* x, int outer, int inner
 //   S[i][j] = (sum_c q[c][i] * k[c][j]) * scale   (MatMul, then Mul)
 //   P = SoftmaxRow(S)                            (VectorMath.SoftmaxRow)
 //   out[d][i] = sum_j v[d][j] * P[i][j]           (MatMul over j)
-// Both products on the tensor cores (psa_composed).
+// YOLO11's head shape (kd 32, hd 64, T <= 512) runs as one fused kernel
+// (psa_fused); other shapes take both products on the tensor cores
+// (psa_composed).
 OSC_API int osc_psa_attention_f32(osc_ctx* ctx, const float* qkv, long long qkv_nstride, int B, int heads, int kd,
                                   int hd, int T, float scale, float* out, long long out_nstride) {
   OSC_TRY(enter(ctx));
@@ -1376,6 +1371,8 @@ OSC_API int osc_psa_attention_f32(osc_ctx* ctx, const float* qkv, long long qkv_
   if (B == 0) return OSC_OK;
   if ((reinterpret_cast<uintptr_t>(out) & 15u) != 0 || out_nstride % 4 != 0)
     return fail(OSC_EINVAL, "osc_psa_attention_f32: out must be 16-byte aligned with a 4-element image stride");
+  const int st = psa_fused(ctx, qkv, qkv_nstride, B, heads, kd, hd, T, scale, out, out_nstride);
+  if (st != OSC_EUNSUPPORTED) return st;
   return psa_composed(ctx, qkv, qkv_nstride, B, heads, kd, hd, T, scale, out, out_nstride);
 }
 

@@ -56,6 +56,8 @@ int enter(osc_ctx* ctx);
 // YOLO11 PSA attention on the tensor cores (gemm_tf32x3.cu).
 int psa_composed(osc_ctx* ctx, const float* qkv, long long qkv_nstride, int B, int heads, int kd, int hd, int T,
                  float scale, float* out, long long out_nstride);
+int psa_fused(osc_ctx* ctx, const float* qkv, long long qkv_nstride, int B, int heads, int kd, int hd, int T,
+                 float scale, float* out, long long out_nstride);
 
 // FusedAttention for T > 128 or head sizes other than 32 / 64, composed of
 // tensor-core batched products and a row softmax (gemm_tf32x3.cu).

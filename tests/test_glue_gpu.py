@@ -296,13 +296,17 @@ def test_layernorm(ctx, golden):
 
 
 @pytest.mark.parametrize("B,heads,kd,hd,h,w,extra", [
-    (2, 2, 32, 64, 20, 20, 0),    # YOLO11n's C2PSA at 640x640
-    (3, 1, 16, 32, 7, 9, 0),      # odd token count (T = 63): padded K, unaligned rows
-    (1, 4, 32, 64, 40, 40, 24),   # T = 1600, qkv a channel slice of a wider buffer
+    (2, 2, 32, 64, 20, 20, 0),    # YOLO11n's C2PSA at 640x640: fused kernel, 16-query blocks
+    (32, 2, 32, 64, 20, 20, 8),   # fused, 64-query blocks, qkv a channel slice
+    (1, 2, 32, 64, 13, 11, 0),    # fused, T = 143: softmax tail, padded P / V rows
+    (1, 1, 32, 64, 23, 22, 0),    # fused, T = 506 (the largest row the softmax registers hold is 512)
+    (3, 1, 16, 32, 7, 9, 0),      # other head shape (T = 63): tensor-core path, padded K, unaligned rows
+    (1, 4, 32, 64, 40, 40, 24),   # T = 1600: tensor-core path, qkv a channel slice of a wider buffer
 ])
 def test_psa_attention(ctx, B, heads, kd, hd, h, w, extra):
-    """Tensor-core PSA attention against the oracle's MatMul -> Mul -> Softmax
-    -> MatMul chain at the FP32 tolerance |d| / max(1, |ref|) <= 1e-4."""
+    """PSA attention (one fused kernel for YOLO11's head shape, the tensor-core
+    composed path otherwise) against the oracle's MatMul -> Mul -> Softmax ->
+    MatMul chain at the FP32 tolerance |d| / max(1, |ref|) <= 1e-4."""
     import torch
 
     from onnxsharp_b200 import ops
