@@ -324,7 +324,7 @@ CONV_FLOPS_PER_IMAGE = 2.0 * 128 * 160 * 160 * 64 * 9
 class ConvWorkload(Workload):
     """Config 2: fused Conv+SiLU, x[B,64,160,160] -> y[B,128,160,160], 3x3 s1 p1, B in {1, 16}; images sharded."""
 
-    main_kernel = ("k_conv_tf32x3",)
+    main_kernel = ("k_conv_tf32x3", "k_conv_px_tf32x3")  # channel-major or pixel-major tiles, one launch per conv
 
     def __init__(self, ctx, sh: Shard, batch: int = 16):
         import torch
@@ -860,6 +860,9 @@ def measure(wl: Workload, ctx, sh: Shard, K: int, W: int, flush, stream, profile
 
 
 def roofline(wl: Workload, kern_ms: float, peaks: dict, peaks_kind: str, traffic) -> dict:
+    if kern_ms <= 0.0:  # the dominant kernel did not run in the profiled passes: no figure rather than a fake one
+        return {"bound": wl.bound, "achieved": None, "peak": None, "frac": None, "traffic": traffic,
+                "kernel": "+".join(wl.main_kernel), "kernel_ms": 0.0, "note": "main kernel not launched"}
     if wl.bound == "tensor":
         pkey = "bf16_tflops_sustained" if wl.long_step else "bf16_tflops"
         peak = peaks.get(pkey, FALLBACK_PEAKS[pkey]) / 2.0 / 3.0

@@ -862,8 +862,9 @@ static int conv1x1_tf32x3(osc_ctx* ctx, const float* x, long long x_nstride, int
 // when the channel-major kernel would not fill two waves of the SMs (small
 // batches: its 128-channel tiles leave half the MMA rows empty at <= 64
 // output channels, and the persistent pixel-major kernel has twice the tiles).
-// Wider layers take pixel tiles when the channel-major grid is under one wave
-// (measured at B=8: 128->128 3x3 s2 at 40x40 16 % faster, at 20x20 10 %),
+// Wider layers take pixel tiles when the channel-major grid fills at most
+// half the SMs (measured at B=8: 128->128 3x3 s2 at 40x40 16 % faster, at
+// 20x20 10 %; 64->128 at 160x160 and B=1, 100 channel-major tiles, stays),
 // and up to 128 channels on images of at most 24x24 (128->128 3x3 s2 at
 // 20x20 and B=64: 19 % faster).
 static bool px_taps_ok(const osc_ctx* ctx, int M, int N, int OH, int OW) {
@@ -871,11 +872,11 @@ static bool px_taps_ok(const osc_ctx* ctx, int M, int N, int OH, int OW) {
   int BW = 0, BH = 0;
   choose_box(OH, OW, &BW, &BH);
   const long tiles = static_cast<long>(N) * ((OW + BW - 1) / BW) * ((OH + BH - 1) / BH);
-  // wider layers: when the channel-major grid is under one wave, the pixel
-  // tiles (split along K where they are still few) fill the SMs; up to 128
-  // channels also on small images
+  // wider layers: when the channel-major grid fills at most half the SMs,
+  // the pixel tiles (split along K where they are still few) fill them; up to
+  // 128 channels also on small images
   if (M > 64)
-    return tiles * ((M + kBM - 1) / kBM) < ctx->num_sms || (M <= 128 && static_cast<long>(OH) * OW <= 576);
+    return 2 * tiles * ((M + kBM - 1) / kBM) <= ctx->num_sms || (M <= 128 && static_cast<long>(OH) * OW <= 576);
   if (static_cast<long>(OH) * OW <= 576) return true;
   return tiles < 2L * ctx->num_sms;
 }
