@@ -3,10 +3,12 @@ by pytest itself): the torch.distributed path bench.py uses.
 
 Each rank runs the YOLO plan on its half of a batch of 4 and the ranks
 all-gather the [2, 84, 8400] outputs (NCCL); rank 0 checks the gathered
-tensor against the single-GPU plan over the whole batch, bit for bit. Then the
-serving pipeline (frames in, detections out) runs sharded with its packed
-detections all-gathered, and rank 0 checks every image's detections against
-the unsharded pipeline. Exits non-zero on any mismatch."""
+tensor against the single-GPU plan over the whole batch within the plan's
+parity tolerance (a half batch may split a conv's K differently, so FP32 sums
+round differently). Then the serving pipeline (frames in, detections out)
+runs sharded with its packed detections all-gathered, and rank 0 checks every
+image's detections against the unsharded pipeline: the same count and
+classes, scores and boxes within 1e-4. Exits non-zero on any mismatch."""
 from __future__ import annotations
 
 import os
@@ -49,8 +51,11 @@ def main() -> int:
         solo.input_view().copy_(torch.from_numpy(images))
         want = solo.forward(use_graph=True).cpu().numpy()
         got = full.cpu().numpy()
-        if not np.array_equal(got.view(np.uint32), want.view(np.uint32)):
-            print("gathered plan output differs from the single-GPU plan", flush=True)
+        box_err = float(np.max(np.abs(got[:, :4] - want[:, :4]) / np.maximum(1.0, np.abs(want[:, :4]))))
+        cls_err = float(np.max(np.abs(got[:, 4:] - want[:, 4:])))
+        if box_err > 1e-4 or cls_err > 1e-4:
+            print(f"gathered plan output differs from the single-GPU plan: boxes {box_err}, scores {cls_err}",
+                  flush=True)
             ok = False
     # serving pipeline, sharded, detections gathered to rank 0
     hw = (360, 640)
@@ -68,8 +73,11 @@ def main() -> int:
         ref_pipe.submit(f2, r2)
         ref_pipe.synchronize()
         want = ref_pipe.unpack(r2.numpy())
-        if len(got) != B or any(a.shape != b.shape or not np.array_equal(a.view(np.uint32), b.view(np.uint32))
-                                for a, b in zip(got, want)):
+        def same(a, b):  # class ids exact, scores and boxes within the parity tolerance
+            return (a.shape == b.shape and np.array_equal(a[:, 0], b[:, 0])
+                    and bool(np.all(np.abs(a[:, 1:] - b[:, 1:]) <= 1e-4 * np.maximum(1.0, np.abs(b[:, 1:])))))
+
+        if len(got) != B or not all(same(a, b) for a, b in zip(got, want)):
             print("gathered detections differ from the single-GPU pipeline", flush=True)
             ok = False
         if sum(a.shape[0] for a in got) == 0:

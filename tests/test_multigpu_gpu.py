@@ -8,7 +8,9 @@ tests skip on a single-GPU box).
    the same on every GPU.
 2. osc_group_run_sharded: the YOLO plan captured per GPU on its half of the
    batch, replayed and all-gathered, equals the single-GPU plan over the whole
-   batch bit for bit on every GPU.
+   batch within the plan's parity tolerance (a half batch may split a conv's
+   K differently, so its FP32 sums round differently), and the gathered
+   tensor is the same on every GPU bit for bit.
 3. The torch.distributed path bench.py uses (one process per GPU, NCCL
    all_gather_into_tensor; the serving pipeline's gathered detections),
    checked by tests/dist_shard_check.py under torchrun."""
@@ -23,7 +25,7 @@ import numpy as np
 import pytest
 
 import oracle
-from conftest import ROOT
+from conftest import ROOT, rel_err
 
 pytestmark = pytest.mark.gpu
 
@@ -126,9 +128,10 @@ def test_group_run_sharded_yolo_matches_single_gpu(group):
         torch.cuda.synchronize(r)
     group.run_sharded(graphs, [n.outputs[0] for n in nets], gathered, 2 * 84 * 8400 * 4)
     group.synchronize()
-    for r in range(2):
-        got = gathered[r].cpu().numpy()
-        assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), f"rank {r}"
+    got0 = gathered[0].cpu().numpy()
+    assert rel_err(got0[:, :4], want[:, :4]) <= 1e-4  # boxes
+    assert np.max(np.abs(got0[:, 4:] - want[:, 4:])) <= 1e-4  # class scores
+    assert np.array_equal(gathered[1].cpu().numpy().view(np.uint32), got0.view(np.uint32))
     for n in nets:
         n.close()
 
