@@ -381,19 +381,20 @@ class Net:
     @staticmethod
     def tensor_core(node) -> bool:
         """Tensor cores for the group-1 convs except the narrow layers: 16 or
-        fewer output channels, or a reduction C_in*k*k <= 144 with C_in < 64
-        (stem, 16->32 3x3, the 8/16-channel bottlenecks, the 32/48-channel
-        1x1s at 160x160). There the register-blocked CUDA-core kernel is
-        faster: the tensor-core kernels' fixed cost per 128-pixel tile
-        dominates when a tile holds few channels (measured per layer at B=64
-        on B200). 1x1 convs with 64 or more input channels take the pointwise
+        fewer output channels, or a reduction C_in*k*k <= 144 with C_in < 48
+        (stem, 16->32 3x3, the 8/16-channel bottlenecks, the 32-channel 1x1s
+        at 160x160). There the register-blocked CUDA-core kernel is faster:
+        the tensor-core kernels' fixed cost per 128-pixel tile dominates when
+        a tile holds few channels (measured per layer at B=64 on B200: 32->32
+        1x1 at 160x160 131 us on CUDA cores, 191 on tensor cores; 48->64 316
+        and 235). 1x1 convs with 48 or more input channels take the pointwise
         kernel, which reads NCHW directly."""
         if node.attrs["group"] != 1:
             return False
         cin, cout, k = node.ins[0].c, node.outs[0].c, node.attrs["k"]
-        if k == 1 and node.attrs["s"] == 1 and cin >= 64:
+        if k == 1 and node.attrs["s"] == 1 and cin >= 48:
             return True
-        return not (cout <= 16 or (cin * k * k <= 144 and cin < 64))
+        return not (cout <= 16 or (cin * k * k <= 144 and cin < 48))
 
     def view(self, r: Ref):
         return self.views[r.buf][:, r.c0:r.c0 + r.c]
