@@ -63,6 +63,10 @@ struct ConvGeom {
   int vec4;                 // y (and res) rows allow 16-byte stores: OW, strides and bases multiples of 4 floats
 };
 
+// MROWS = 64 for layers of at most 64 output channels: weight boxes of 64
+// rows and M = 64 MMAs (no MMA work on zero weight rows, 80 KB stages instead
+// of 96 KB); MROWS = 128 otherwise.
+template <int MROWS>
 __global__ void __launch_bounds__(ConvCfg::THREADS, 1)
     k_conv_tf32x3(const __grid_constant__ CUtensorMap mWh, const __grid_constant__ CUtensorMap mWl,
                   const __grid_constant__ CUtensorMap mXh, const __grid_constant__ CUtensorMap mXl,
@@ -105,12 +109,12 @@ __global__ void __launch_bounds__(ConvCfg::THREADS, 1)
         const int nn = taps.phase[tap] * g.N + n;
         tma_load_4d(st + 2 * Cfg::A_BYTES, &mXh, bar, c0, x, yy, nn);
         tma_load_4d(st + 2 * Cfg::A_BYTES + Cfg::B_BYTES, &mXl, bar, c0, x, yy, nn);
-      });
+      }, static_cast<uint32_t>(Cfg::STAGE_BYTES - 2 * (kBM - MROWS) * kBK * 4));
   } else if (warp == 1) {
-    if (lane == 0) mma_loop<Cfg>(tiles, pb, tmem, num_kb, err);
+    if (lane == 0) mma_loop<Cfg, MROWS>(tiles, pb, tmem, num_kb, err);
   } else {
     float acc[128];
-    if (drain_loop<Cfg>(pb, tmem, num_kb, acc, err)) stage_tile<Cfg>(tiles, acc);
+    if (drain_loop<Cfg>(pb, tmem, num_kb, acc, err)) stage_tile<Cfg, MROWS>(tiles, acc);
     const int jj = threadIdx.x - 64;  // bias of this tile's 128 channels
     if (jj < kBM)
       reinterpret_cast<float*>(tiles)[kBM * (Cfg::BN + 4) + jj] =
@@ -187,8 +191,9 @@ __global__ void __launch_bounds__(ConvCfg::THREADS, 1)
 //    128-byte swizzle with 32-byte atoms that MN-major TF32 operands need:
 //    4-channel groups 512 bytes apart, 32-pixel groups 4 KB apart), its lo
 //    part, and the prepacked weight hi/lo boxes (K-major);
-//  - persistent CTAs walk the tiles; TMEM holds two accumulators, so the
-//    epilogue of one tile overlaps the main loop of the next;
+//  - persistent CTAs walk the tiles; TMEM holds 512 / BN accumulators (4 or
+//    8), so the epilogue of one tile overlaps the main loop of the next and
+//    the MMA runs several TMEM chunks ahead of the drain;
 //  - epilogue (16 warps, four per TMEM lane quadrant): lane = pixel, so each
 //    warp store writes 32 consecutive pixels of one output channel (128
 //    bytes): NCHW without a staging tile. Biases come from a shared-memory
@@ -203,9 +208,11 @@ constexpr int kThreads = 32 * (kEpiBase + kEpiWarps);  // producer, MMA, convert
 constexpr int kKC = 2;                    // k-blocks per TMEM chunk
 constexpr int kMaxStages = 4;
 constexpr int kMaxBias = 4096;            // output channels whose biases fit the shared-memory table
+constexpr int kMaxAcc = 8;                // TMEM accumulator buffers (all 512 columns on 64-channel tiles)
+constexpr int kBarsBytes = 512;           // the barrier block (the bias table follows it)
 struct Bars {
   uint64_t full[kMaxStages], conv[kMaxStages], empty[kMaxStages];
-  uint64_t acc_full[2], acc_empty[2];
+  uint64_t acc_full[kMaxAcc], acc_empty[kMaxAcc];
   uint64_t mma_done;
   uint32_t tmem_slot;
   int abort_flag;
@@ -221,16 +228,21 @@ struct Cfg {
   static constexpr int kB = BN * kBK * 4;                 // one weight part: BN oc x 32 ch
   static constexpr int kStage = 2 * kA + 2 * kB;          // A (hi after the split) | A lo | W hi | W lo
   static constexpr int kTx = kA + 2 * kB;                 // bytes TMA lands per stage
-  static constexpr int kTmemCols = 2 * BN;                // two accumulators
+  // Every TMEM column: 512 / BN accumulators, so the MMA runs up to that many
+  // TMEM chunks ahead of the epilogue warps, which drain a chunk every kKC
+  // k-blocks and also store the previous tile's outputs.
+  static constexpr int kAccBufs = 512 / BN;
+  static constexpr int kTmemCols = 512;
   static constexpr int kColsMax = BN / kEpiGroups;        // output channels per epilogue warp on a full tile
-  static constexpr int kSmemBase = kStages * kStage + 1024 + 256;  // + the bias table (M floats, rounded to 16 bytes)
+  static constexpr int kSmemBase = kStages * kStage + 1024 + kBarsBytes;  // + the bias table (M floats, rounded to 16 bytes)
   static_assert(kStages <= kMaxStages, "stages");
+  static_assert(kAccBufs <= kMaxAcc, "accumulator barriers");
   static_assert(kStage % 1024 == 0 && kA % 1024 == 0 && kB % 1024 == 0, "1024-byte aligned operand boxes");
   static_assert(kColsMax % 16 == 0, "TMEM drain granularity");
   static_assert(kSmemBase + kMaxBias * 4 <= 232448, "shared memory budget");
 };
 static_assert(kEpiBase % 4 == 0, "epilogue warps must start on a lane-quadrant boundary");
-static_assert(sizeof(Bars) <= 256, "barrier block");
+static_assert(sizeof(Bars) <= kBarsBytes, "barrier block");
 }  // namespace pw
 
 struct PwGeom {
@@ -298,7 +310,7 @@ __global__ void __launch_bounds__(pw::kThreads, 1)
       mbar_init(&pb->conv[s], kConvWarps);
       mbar_init(&pb->empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < CF::kAccBufs; ++b) {
       mbar_init(&pb->acc_full[b], 1);
       mbar_init(&pb->acc_empty[b], kEpiWarps);
     }
@@ -316,7 +328,7 @@ __global__ void __launch_bounds__(pw::kThreads, 1)
   }
   // every output channel's bias, read once per CTA (the epilogue reads it from
   // shared memory instead of a global load in each store's dependency chain)
-  float* s_bias = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(pb) + 256);
+  float* s_bias = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(pb) + kBarsBytes);
   for (int j = threadIdx.x; j < g.M; j += kThreads) s_bias[j] = bias != nullptr ? __ldg(bias + j) : 0.0f;
   tc_fence_before();
   __syncthreads();
@@ -380,8 +392,8 @@ __global__ void __launch_bounds__(pw::kThreads, 1)
         const uint32_t idesc = TAPS ? idesc_tf32(kBM, nn) : idesc_tf32_amn(kBM, nn);
         int kb = tl.kb_begin;
         for (int c = tl.c_begin; c < tl.c_end && ok; ++c, ++gc) {
-          const int buf = gc & 1;
-          if (!mbar_wait(&pb->acc_empty[buf], ((gc >> 1) & 1u) ^ 1u, &pb->abort_flag, err)) {
+          const int buf = gc % CF::kAccBufs;
+          if (!mbar_wait(&pb->acc_empty[buf], ((gc / CF::kAccBufs) & 1u) ^ 1u, &pb->abort_flag, err)) {
             ok = false;
             break;
           }
@@ -480,8 +492,8 @@ __global__ void __launch_bounds__(pw::kThreads, 1)
       const int nvalid = min(cpw, g.M - oc0);  // may be <= 0 for the upper groups of a narrow tile
       float acc[CF::kColsMax];
       for (int c = tl.c_begin; c < tl.c_end; ++c, ++gc) {
-        const int buf = gc & 1;
-        bool got = mbar_wait(&pb->acc_full[buf], (gc >> 1) & 1u, &pb->abort_flag, err);
+        const int buf = gc % CF::kAccBufs;
+        bool got = mbar_wait(&pb->acc_full[buf], (gc / CF::kAccBufs) & 1u, &pb->abort_flag, err);
         got = __all_sync(0xffffffffu, got);
         if (!got) {
           ok = false;
@@ -898,6 +910,11 @@ static void choose_px_box(int OH, int OW, int* BW, int* BH) {
   }
 }
 
+// Output channels per pixel-major K x K tile: layers of at most 64 output
+// channels take the 64-channel tile, whose weight boxes carry no zero rows and
+// whose 48 KB stages give a 4-deep ring.
+static int px_taps_bn(int M) { return M <= 64 ? 64 : 128; }
+
 // Geometry of the pixel-major K x K conv (split-K included); returns the
 // split workspace bytes (0 without a split).
 static size_t px_taps_geom(const osc_ctx* ctx, const osc_conv_weights* w, int N, int OH, int OW, int act,
@@ -911,7 +928,7 @@ static size_t px_taps_geom(const osc_ctx* ctx, const osc_conv_weights* w, int N,
   choose_px_box(OH, OW, &g.BW, &g.BH);
   g.tiles_w = (OW + g.BW - 1) / g.BW;
   g.ptiles = g.tiles_w * ((OH + g.BH - 1) / g.BH);
-  g.otiles = (w->M + pw::Cfg<128>::kBN - 1) / pw::Cfg<128>::kBN;
+  g.otiles = (w->M + px_taps_bn(w->M) - 1) / px_taps_bn(w->M);
   g.tiles = static_cast<long long>(N) * g.ptiles * g.otiles;
   g.cp_blocks = w->Cp / kBK;
   g.num_kb = w->kh * w->kw * g.cp_blocks;
@@ -925,6 +942,7 @@ static size_t px_taps_geom(const osc_ctx* ctx, const osc_conv_weights* w, int N,
 }
 
 // g from px_taps_geom, with g.ws set when it asked for a workspace.
+template <int BN>
 static int conv_px_taps(osc_ctx* ctx, const float* xh, const float* xl, int N, int Hp, int Wp, int s,
                         const osc_conv_weights* w, const ConvTaps& taps, const PwGeom& g, const float* bias,
                         float* y) {
@@ -941,14 +959,14 @@ static int conv_px_taps(osc_ctx* ctx, const float* xh, const float* xl, int N, i
   {
     const uint64_t dims[2] = {static_cast<uint64_t>(w->Kp), static_cast<uint64_t>(w->M)};
     const uint64_t pitch[1] = {static_cast<uint64_t>(w->Kp) * 4};
-    const uint32_t box[2] = {kBK, pw::Cfg<128>::kBN};
+    const uint32_t box[2] = {kBK, pw::Cfg<BN>::kBN};
     OSC_TRY(encode_tiled(&mWh, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, w->hi, dims, pitch, box, CU_TENSOR_MAP_SWIZZLE_128B));
     OSC_TRY(encode_tiled(&mWl, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, w->lo, dims, pitch, box, CU_TENSOR_MAP_SWIZZLE_128B));
   }
-  const int smem = pw::Cfg<128>::kSmemBase + static_cast<int>(round_up(static_cast<size_t>(w->M) * 4, 16));
-  OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(k_conv_px_tf32x3<true, 128>), smem));
+  const int smem = pw::Cfg<BN>::kSmemBase + static_cast<int>(round_up(static_cast<size_t>(w->M) * 4, 16));
+  OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(k_conv_px_tf32x3<true, BN>), smem));
   const long long grid = std::min<long long>(g.tiles, ctx->num_sms);
-  OSC_TRY(launch_pdl(ctx, k_conv_px_tf32x3<true, 128>, dim3(static_cast<unsigned>(grid)), dim3(pw::kThreads), smem,
+  OSC_TRY(launch_pdl(ctx, k_conv_px_tf32x3<true, BN>, dim3(static_cast<unsigned>(grid)), dim3(pw::kThreads), smem,
                      "k_conv_px_tf32x3", mXh, mXl, mWh, mWl, g, taps, bias, y, ctx->d_err));
   return g.ksplit > 1 ? splitk_reduce(ctx, g, bias, g.act, y) : OSC_OK;
 }
@@ -1003,7 +1021,9 @@ int conv_tf32x3(osc_ctx* ctx, const float* x, long long x_nstride, int N, int C,
       taps.dy[t] = static_cast<short>(floor_div(oy - py, s));
       taps.dx[t] = static_cast<short>(floor_div(ox - px, s));
     }
-  if (px) return conv_px_taps(ctx, xh, xl, N, Hp, Wp, s, w, taps, pg, bias, y);
+  if (px)
+    return px_taps_bn(w->M) == 64 ? conv_px_taps<64>(ctx, xh, xl, N, Hp, Wp, s, w, taps, pg, bias, y)
+                                  : conv_px_taps<128>(ctx, xh, xl, N, Hp, Wp, s, w, taps, pg, bias, y);
   ConvGeom g{};
   g.N = N;
   g.M = w->M;
@@ -1028,7 +1048,7 @@ int conv_tf32x3(osc_ctx* ctx, const float* x, long long x_nstride, int N, int C,
   {
     const uint64_t dims[2] = {static_cast<uint64_t>(w->Kp), static_cast<uint64_t>(w->M)};
     const uint64_t pitch[1] = {static_cast<uint64_t>(w->Kp) * 4};
-    const uint32_t box[2] = {kBK, kBM};
+    const uint32_t box[2] = {kBK, w->M <= 64 ? 64u : static_cast<uint32_t>(kBM)};
     OSC_TRY(encode_tiled(&mWh, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, w->hi, dims, pitch, box, CU_TENSOR_MAP_SWIZZLE_128B));
     OSC_TRY(encode_tiled(&mWl, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, w->lo, dims, pitch, box, CU_TENSOR_MAP_SWIZZLE_128B));
   }
@@ -1043,10 +1063,15 @@ int conv_tf32x3(osc_ctx* ctx, const float* x, long long x_nstride, int N, int C,
   }
   const long tiles = static_cast<long>(g.tiles_w) * g.tiles_h * N;
   if (tiles > 2147483647L) return fail(OSC_EINVAL, "conv: too many tiles");
-  OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(k_conv_tf32x3), ConvCfg::SMEM_BYTES));
   dim3 grid(static_cast<unsigned>(tiles), (w->M + kBM - 1) / kBM);
-  return launch_pdl(ctx, k_conv_tf32x3, grid, dim3(ConvCfg::THREADS), ConvCfg::SMEM_BYTES, "k_conv_tf32x3", mWh, mWl,
-                    mXh, mXl, taps, g, bias, y, ctx->d_err);
+  if (w->M <= 64) {
+    OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(k_conv_tf32x3<64>), ConvCfg::SMEM_BYTES));
+    return launch_pdl(ctx, k_conv_tf32x3<64>, grid, dim3(ConvCfg::THREADS), ConvCfg::SMEM_BYTES, "k_conv_tf32x3", mWh,
+                      mWl, mXh, mXl, taps, g, bias, y, ctx->d_err);
+  }
+  OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(k_conv_tf32x3<128>), ConvCfg::SMEM_BYTES));
+  return launch_pdl(ctx, k_conv_tf32x3<128>, grid, dim3(ConvCfg::THREADS), ConvCfg::SMEM_BYTES, "k_conv_tf32x3", mWh,
+                    mWl, mXh, mXl, taps, g, bias, y, ctx->d_err);
 }
 
 }  // namespace osc

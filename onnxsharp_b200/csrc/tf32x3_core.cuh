@@ -107,15 +107,17 @@ __device__ __forceinline__ void pipe_teardown(PipeBarriers* pb, uint32_t tmem) {
 }
 
 // Producer skeleton: `issue(kb, stage_ptr, bar)` enqueues the TMA loads of
-// k-block kb (STAGE_BYTES in total) on `bar`. Run by one thread.
+// k-block kb (`tx` bytes in total, STAGE_BYTES unless the A boxes are shorter
+// than kBM rows) on `bar`. Run by one thread.
 template <class Cfg, class Issue>
-__device__ __forceinline__ void producer_loop(uint8_t* tiles, PipeBarriers* pb, int num_kb, int* err, Issue issue) {
+__device__ __forceinline__ void producer_loop(uint8_t* tiles, PipeBarriers* pb, int num_kb, int* err, Issue issue,
+                                              uint32_t tx = Cfg::STAGE_BYTES) {
   int issued = 0;
   for (int kb = 0; kb < num_kb; ++kb) {
     const int s = kb % Cfg::STAGES;
     const uint32_t ph = (kb / Cfg::STAGES) & 1u;
     if (!mbar_wait(&pb->empty[s], ph ^ 1u, &pb->abort_flag, err)) break;
-    mbar_arrive_expect_tx(&pb->full[s], Cfg::STAGE_BYTES);
+    mbar_arrive_expect_tx(&pb->full[s], tx);
     issue(kb, tiles + s * Cfg::STAGE_BYTES, &pb->full[s]);
     issued = kb + 1;
   }
@@ -134,10 +136,13 @@ __device__ __forceinline__ void producer_loop(uint8_t* tiles, PipeBarriers* pb, 
 // MMA issuer: for each chunk of KC k-blocks, wait for the accumulator buffer
 // to be drained, then 3 MMAs per 8-wide K step (hi*hi, hi*lo, lo*hi); each
 // stage is released by tcgen05.commit, each finished chunk is signalled on
-// acc_full. Stage layout: A hi | A lo | B hi | B lo. Run by one thread.
-template <class Cfg>
+// acc_full. Stage layout: A hi | A lo | B hi | B lo. MROWS = 64 reads only
+// the first 64 A rows (D row r lands in TMEM lane 32 * (r / 16) + r % 16).
+// Run by one thread.
+template <class Cfg, int MROWS = kBM>
 __device__ __forceinline__ void mma_loop(uint8_t* tiles, PipeBarriers* pb, uint32_t tmem, int num_kb, int* err) {
-  constexpr uint32_t idesc = idesc_tf32(kBM, Cfg::BN);
+  static_assert(MROWS == 64 || MROWS == 128, "MMA rows");
+  constexpr uint32_t idesc = idesc_tf32(MROWS, Cfg::BN);
   const int nchunks = (num_kb + Cfg::KC - 1) / Cfg::KC;
   int kb = 0;
   for (int c = 0; c < nchunks; ++c) {
@@ -222,12 +227,16 @@ __device__ __forceinline__ bool drain_loop(PipeBarriers* pb, uint32_t tmem, int 
 // (the +4 keeps a quarter-warp's float4 stores to 8 different rows on 8
 // different bank groups). Each epilogue thread writes its row's 128 columns;
 // after epi_sync() the warps copy whole rows out with coalesced stores.
-template <class Cfg>
+// With MROWS = 64 only TMEM lanes 0-15 of each quadrant hold D rows (row
+// 16 * quadrant + lane); the other lanes' registers are not staged.
+template <class Cfg, int MROWS = kBM>
 __device__ __forceinline__ float* stage_tile(uint8_t* tiles, const float (&acc)[128]) {
   constexpr int kPitch = Cfg::BN + 4;
   float* stage = reinterpret_cast<float*>(tiles);
   const int warp = threadIdx.x >> 5;
-  const int row = (warp & 3) * 32 + (threadIdx.x & 31);
+  const int lane = threadIdx.x & 31;
+  if (MROWS == 64 && lane >= 16) return stage;
+  const int row = (warp & 3) * (MROWS / 4) + lane;
   float* dst = stage + row * kPitch + ((warp - 2) >> 2) * 128;
 #pragma unroll
   for (int j = 0; j < 128; j += 4)

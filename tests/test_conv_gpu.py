@@ -172,3 +172,19 @@ def test_conv_split_k_views_and_residual(ctx, k, C, M):
     got = out_big.cpu().numpy()
     assert rel_err(got[:, 32:32 + M], ref) <= TOL
     assert not got[:, :32].any() and not got[:, 32 + M:].any()
+
+
+@pytest.mark.parametrize("N,C,H,M,stride", [(36, 32, 40, 64, 1), (36, 64, 40, 32, 1), (36, 32, 40, 48, 1),
+                                            (36, 32, 80, 64, 2)])
+def test_conv_channel_major_narrow_layers(ctx, N, C, H, M, stride):
+    """Layers of at most 64 output channels on the channel-major kernel (many
+    256-pixel tiles): M = 64 MMAs over 64-row weight boxes, D rows read from
+    the first 16 TMEM lanes of each quadrant; 48 channels leave a partial
+    quadrant. The launch is checked to be the channel-major kernel."""
+    x, w, b = _case(50 + M + stride, N, C, H, H, M, 3)
+    ctx.profile_reset()
+    ctx.profile(True)
+    y = _conv(ctx, x, w, b, stride=(stride, stride), pads=(1, 1, 1, 1), act=1)
+    ctx.profile(False)
+    assert ctx.profile_read("k_conv_tf32x3")[1] == 1
+    assert rel_err(y, oracle.conv2d(x, w, b, stride=(stride, stride), pads=(1, 1, 1, 1), act=1)) <= TOL
