@@ -50,14 +50,13 @@ __device__ __forceinline__ void gemm_stage(uint8_t* tiles, const float (&acc)[12
   sbias[jj] = (col_bias != nullptr && n0 + jj < N) ? __ldg(col_bias + n0 + jj) : 0.0f;
 }
 
-// TMA-store epilogue (C 16-byte aligned with a 16-byte row pitch), in two
-// parts like gemm_stage / gemm_writeout. gemm_stage_boxes (epilogue warps,
-// right after the drain): bias + activation of the thread's row of 128
-// columns into 32-column boxes in the free operand ring (128 rows x 128 bytes
-// each, 128-byte swizzle: 16-byte chunk c of row r at chunk c ^ (r % 8), so a
-// warp's 32 rows hit every bank once). gemm_store_boxes (every thread, after
-// the CTA barrier): one thread stores the BN/32 boxes with TMA (rows and
-// columns outside C are clipped) and waits until they have been read.
+// TMA-store epilogue (C 16-byte aligned with a 16-byte row pitch),
+// gemm_stage_store_boxes (epilogue warps, right after the drain): bias +
+// activation of the thread's row of 128 columns into 32-column boxes in the
+// free operand ring (128 rows x 128 bytes each, 128-byte swizzle: 16-byte
+// chunk c of row r at chunk c ^ (r % 8), so a warp's 32 rows hit every bank
+// once), each box stored with TMA (rows and columns outside C are clipped) as
+// soon as its 128 rows are staged.
 // The tile's column biases in the shared words past the barriers, written by
 // the epilogue warps before their drain (named barrier 2 among them).
 template <class Cfg>
@@ -72,40 +71,44 @@ __device__ __forceinline__ void load_tile_bias(uint8_t* tiles, int n0, int N, co
   asm volatile("bar.sync 2, %0;" ::"r"(Cfg::EPI_WARPS * 32) : "memory");
 }
 
+// Epilogue warps: bias + activation of this thread's row into the 32-column
+// boxes, box by box; as soon as the four warps of a column half have staged a
+// box (named barrier 3 + half), one thread of the half issues its TMA store,
+// so the stores of the first boxes overlap the staging of the later ones. The
+// issuing threads wait for their copies' shared-memory reads before the CTA
+// may end. On a failed drain the boxes are not written and nothing is stored.
 template <class Cfg, int ACT>
-__device__ __forceinline__ void gemm_stage_boxes(uint8_t* tiles, const float (&acc)[128], bool ok, bool has_bias) {
-  if (!ok) return;
+__device__ __forceinline__ void gemm_stage_store_boxes(uint8_t* tiles, const float (&acc)[128], bool ok,
+                                                       bool has_bias, const CUtensorMap* mC, int m0, int n0) {
   const int warp = threadIdx.x >> 5;
   const int row = (warp & 3) * 32 + (threadIdx.x & 31);
   const int half = (warp - 2) >> 2;
+  const bool issuer = (threadIdx.x - 64) % 128 == 0;
   const float* sb = tile_bias<Cfg>(tiles) + half * 128;
 #pragma unroll
   for (int b = 0; b < 4; ++b) {
     uint8_t* box = tiles + (half * 4 + b) * (kBM * 128) + row * 128;
+    if (ok) {
 #pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      const float4 bv = *reinterpret_cast<const float4*>(sb + b * 32 + c * 4);  // broadcast
-      const float bb[4] = {bv.x, bv.y, bv.z, bv.w};
-      float v[4];
+      for (int c = 0; c < 8; ++c) {
+        const float4 bv = *reinterpret_cast<const float4*>(sb + b * 32 + c * 4);  // broadcast
+        const float bb[4] = {bv.x, bv.y, bv.z, bv.w};
+        float v[4];
 #pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        const int j = b * 32 + c * 4 + t;
-        v[t] = act_t<ACT>(has_bias ? __fadd_rn(acc[j], bb[t]) : acc[j]);
+        for (int t = 0; t < 4; ++t) {
+          const int j = b * 32 + c * 4 + t;
+          v[t] = act_t<ACT>(has_bias ? __fadd_rn(acc[j], bb[t]) : acc[j]);
+        }
+        *reinterpret_cast<float4*>(box + ((c ^ (row & 7)) << 4)) = make_float4(v[0], v[1], v[2], v[3]);
       }
-      *reinterpret_cast<float4*>(box + ((c ^ (row & 7)) << 4)) = make_float4(v[0], v[1], v[2], v[3]);
+      fence_async_smem();
     }
+    asm volatile("bar.sync %0, 128;" ::"r"(3 + half) : "memory");
+    if (issuer && ok) tma_store_2d(mC, tiles + (half * 4 + b) * (kBM * 128), n0 + 32 * (half * 4 + b), m0);
   }
-  fence_async_smem();
-}
-
-template <class Cfg>
-__device__ __forceinline__ void gemm_store_boxes(uint8_t* tiles, bool ok, const CUtensorMap* mC, int m0, int n0) {
-  asm volatile("bar.sync 1, %0;" ::"r"(Cfg::THREADS) : "memory");
-  if (threadIdx.x == 0 && ok) {
-#pragma unroll
-    for (int b = 0; b < Cfg::BN / 32; ++b) tma_store_2d(mC, tiles + b * (kBM * 128), n0 + 32 * b, m0);
+  if (issuer && ok) {
     bulk_commit();
-    bulk_wait_read_all();  // the shared-memory boxes must outlive the copy's reads
+    bulk_wait_read_all();  // the shared-memory boxes must outlive the copies' reads
   }
 }
 
@@ -134,6 +137,8 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
     tma_prefetch(&mBl);
   }
   const uint32_t tmem = pipe_setup<Cfg>(pb);
+  griddep_wait();  // launched with launch_pdl: the previous kernel has completed past here
+  griddep_launch();
 
   if (warp == 0) {
     if (lane == 0)
@@ -150,9 +155,8 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
     load_tile_bias<Cfg>(tiles, n0, N, col_bias);
     float acc[128];
     const bool ok = drain_loop<Cfg>(pb, tmem, num_kb, acc, err);
-    gemm_stage_boxes<Cfg, ACT>(tiles, acc, ok, col_bias != nullptr);
+    gemm_stage_store_boxes<Cfg, ACT>(tiles, acc, ok, col_bias != nullptr, &mC, m0, n0);
   }
-  gemm_store_boxes<Cfg>(tiles, !pb->abort_flag, &mC, m0, n0);
   pipe_teardown<Cfg>(pb, tmem);
 }
 
@@ -185,6 +189,8 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
     tma_prefetch(&mBl);
   }
   const uint32_t tmem = pipe_setup_pair<Cfg>(pb);
+  griddep_wait();  // launched with programmatic stream serialization: the previous kernel has completed
+  griddep_launch();
 
   if (warp == 0) {
     if (lane == 0)
@@ -201,9 +207,8 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
     load_tile_bias<Cfg>(tiles, n0, N, col_bias);
     float acc[128];
     const bool ok = drain_loop_pair<Cfg>(pb, tmem, num_kb, acc, err);
-    gemm_stage_boxes<Cfg, ACT>(tiles, acc, ok, col_bias != nullptr);
+    gemm_stage_store_boxes<Cfg, ACT>(tiles, acc, ok, col_bias != nullptr, &mC, m0, n0);
   }
-  gemm_store_boxes<Cfg>(tiles, !pb->abort_flag, &mC, m0, n0);
   pipe_teardown_pair<Cfg>(pb, tmem, rank, err);
 }
 
@@ -473,9 +478,8 @@ int launch_gemm(osc_ctx* ctx, const float* ahi, const float* alo, int M, int Kp,
   auto kern = gemm_kernel<Cfg>(act);
   OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(kern), Cfg::SMEM_BYTES));
   dim3 grid((w->n + Cfg::BN - 1) / Cfg::BN, (M + kBM - 1) / kBM);
-  prof_begin(ctx);
-  kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, ctx->stream>>>(mAh, mAl, mBh, mBl, M, w->n, Kp, bias, mC, ctx->d_err);
-  return check_launch(ctx, "k_gemm_tf32x3");
+  return launch_pdl(ctx, kern, grid, dim3(Cfg::THREADS), Cfg::SMEM_BYTES, "k_gemm_tf32x3", mAh, mAl, mBh, mBl, M, w->n,
+                    Kp, bias, mC, ctx->d_err);
 }
 
 template <class Cfg>
@@ -498,13 +502,15 @@ int launch_gemm_pair(osc_ctx* ctx, const float* ahi, const float* alo, int M, in
   cfg.blockDim = dim3(Cfg::THREADS);
   cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
   cfg.stream = ctx->stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // set-up overlaps the previous kernel's tail
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   prof_begin(ctx);
   CUtensorMap mC{};
   OSC_TRY(store_map(&mC, C, M, w->n, ldc));
