@@ -63,10 +63,11 @@ struct ConvGeom {
   int vec4;                 // y (and res) rows allow 16-byte stores: OW, strides and bases multiples of 4 floats
 };
 
-// MROWS = 64 for layers of at most 64 output channels: weight boxes of 64
-// rows and M = 64 MMAs (no MMA work on zero weight rows, 80 KB stages instead
-// of 96 KB); MROWS = 128 otherwise.
-template <int MROWS>
+// STACKED for layers of at most 64 output channels: 64-row weight boxes, the
+// lo box landing right below the hi box, so [W hi; W lo] is one 128-row A
+// operand; 2 MMAs per K step instead of 3 (see mma_loop), 80 KB stages
+// instead of 96 KB; the epilogue adds D rows r and r + 64.
+template <bool STACKED>
 __global__ void __launch_bounds__(ConvCfg::THREADS, 1)
     k_conv_tf32x3(const __grid_constant__ CUtensorMap mWh, const __grid_constant__ CUtensorMap mWl,
                   const __grid_constant__ CUtensorMap mXh, const __grid_constant__ CUtensorMap mXl,
@@ -104,17 +105,17 @@ __global__ void __launch_bounds__(ConvCfg::THREADS, 1)
         const int c0 = (kb - tap * taps.cp_blocks) * 32;
         const int kcol = kb * 32;  // == tap * Cp + c0
         tma_load_2d(st, &mWh, bar, kcol, m0);
-        tma_load_2d(st + Cfg::A_BYTES, &mWl, bar, kcol, m0);
+        tma_load_2d(st + (STACKED ? Cfg::A_BYTES / 2 : Cfg::A_BYTES), &mWl, bar, kcol, m0);
         const int x = ox0 + taps.dx[tap], yy = oy0 + taps.dy[tap];
         const int nn = taps.phase[tap] * g.N + n;
         tma_load_4d(st + 2 * Cfg::A_BYTES, &mXh, bar, c0, x, yy, nn);
         tma_load_4d(st + 2 * Cfg::A_BYTES + Cfg::B_BYTES, &mXl, bar, c0, x, yy, nn);
-      }, static_cast<uint32_t>(Cfg::STAGE_BYTES - 2 * (kBM - MROWS) * kBK * 4));
+      }, static_cast<uint32_t>(STACKED ? Cfg::STAGE_BYTES - Cfg::A_BYTES : Cfg::STAGE_BYTES));
   } else if (warp == 1) {
-    if (lane == 0) mma_loop<Cfg, MROWS>(tiles, pb, tmem, num_kb, err);
+    if (lane == 0) mma_loop<Cfg, STACKED>(tiles, pb, tmem, num_kb, err);
   } else {
     float acc[128];
-    if (drain_loop<Cfg>(pb, tmem, num_kb, acc, err)) stage_tile<Cfg, MROWS>(tiles, acc);
+    if (drain_loop<Cfg>(pb, tmem, num_kb, acc, err)) stage_tile<Cfg>(tiles, acc);
     const int jj = threadIdx.x - 64;  // bias of this tile's 128 channels
     if (jj < kBM)
       reinterpret_cast<float*>(tiles)[kBM * (Cfg::BN + 4) + jj] =
@@ -146,7 +147,11 @@ __global__ void __launch_bounds__(ConvCfg::THREADS, 1)
           const int p = h + lane * 4;  // 4 consecutive pixels of one box row (BW >= 8)
           const int oy = oy0 + (p >> g.bw_log2), ox = ox0 + (p & (g.BW - 1));
           if (oy >= g.OH) continue;
-          const float4 sv = *reinterpret_cast<const float4*>(stage + r * kPitch + p);
+          float4 sv = *reinterpret_cast<const float4*>(stage + r * kPitch + p);
+          if (STACKED) {  // W lo * X from D row r + 64
+            const float4 lv = *reinterpret_cast<const float4*>(stage + (r + 64) * kPitch + p);
+            sv = make_float4(__fadd_rn(sv.x, lv.x), __fadd_rn(sv.y, lv.y), __fadd_rn(sv.z, lv.z), __fadd_rn(sv.w, lv.w));
+          }
           const float v[4] = {sv.x, sv.y, sv.z, sv.w};
           float* dst = yplane + static_cast<size_t>(oy) * g.OW + ox;
           const float* rsrc = rplane ? rplane + static_cast<size_t>(oy) * g.OW + ox : nullptr;
@@ -1065,12 +1070,12 @@ int conv_tf32x3(osc_ctx* ctx, const float* x, long long x_nstride, int N, int C,
   if (tiles > 2147483647L) return fail(OSC_EINVAL, "conv: too many tiles");
   dim3 grid(static_cast<unsigned>(tiles), (w->M + kBM - 1) / kBM);
   if (w->M <= 64) {
-    OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(k_conv_tf32x3<64>), ConvCfg::SMEM_BYTES));
-    return launch_pdl(ctx, k_conv_tf32x3<64>, grid, dim3(ConvCfg::THREADS), ConvCfg::SMEM_BYTES, "k_conv_tf32x3", mWh,
+    OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(k_conv_tf32x3<true>), ConvCfg::SMEM_BYTES));
+    return launch_pdl(ctx, k_conv_tf32x3<true>, grid, dim3(ConvCfg::THREADS), ConvCfg::SMEM_BYTES, "k_conv_tf32x3", mWh,
                       mWl, mXh, mXl, taps, g, bias, y, ctx->d_err);
   }
-  OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(k_conv_tf32x3<128>), ConvCfg::SMEM_BYTES));
-  return launch_pdl(ctx, k_conv_tf32x3<128>, grid, dim3(ConvCfg::THREADS), ConvCfg::SMEM_BYTES, "k_conv_tf32x3", mWh,
+  OSC_TRY(set_smem_attr(ctx, reinterpret_cast<const void*>(k_conv_tf32x3<false>), ConvCfg::SMEM_BYTES));
+  return launch_pdl(ctx, k_conv_tf32x3<false>, grid, dim3(ConvCfg::THREADS), ConvCfg::SMEM_BYTES, "k_conv_tf32x3", mWh,
                     mWl, mXh, mXl, taps, g, bias, y, ctx->d_err);
 }
 

@@ -136,13 +136,15 @@ __device__ __forceinline__ void producer_loop(uint8_t* tiles, PipeBarriers* pb, 
 // MMA issuer: for each chunk of KC k-blocks, wait for the accumulator buffer
 // to be drained, then 3 MMAs per 8-wide K step (hi*hi, hi*lo, lo*hi); each
 // stage is released by tcgen05.commit, each finished chunk is signalled on
-// acc_full. Stage layout: A hi | A lo | B hi | B lo. MROWS = 64 reads only
-// the first 64 A rows (D row r lands in TMEM lane 32 * (r / 16) + r % 16).
-// Run by one thread.
-template <class Cfg, int MROWS = kBM>
+// acc_full. Stage layout: A hi | A lo | B hi | B lo.
+// STACKED (A of at most 64 rows): the A hi region holds [A hi; A lo] as one
+// 128-row operand, and 2 MMAs per K step (stack * B hi, stack * B lo) leave
+// A hi * B in D rows 0-63 and A lo * B in rows 64-127 (the lo * lo product
+// included), which the epilogue adds: 8 MMAs per k-block instead of 12, an
+// MMA of 64 rows costing about as much as one of 128. Run by one thread.
+template <class Cfg, bool STACKED = false>
 __device__ __forceinline__ void mma_loop(uint8_t* tiles, PipeBarriers* pb, uint32_t tmem, int num_kb, int* err) {
-  static_assert(MROWS == 64 || MROWS == 128, "MMA rows");
-  constexpr uint32_t idesc = idesc_tf32(MROWS, Cfg::BN);
+  constexpr uint32_t idesc = idesc_tf32(kBM, Cfg::BN);
   const int nchunks = (num_kb + Cfg::KC - 1) / Cfg::KC;
   int kb = 0;
   for (int c = 0; c < nchunks; ++c) {
@@ -168,7 +170,7 @@ __device__ __forceinline__ void mma_loop(uint8_t* tiles, PipeBarriers* pb, uint3
         mma_tf32(d, dAh + off, dBh + off, idesc, acc);
         acc = 1u;
         mma_tf32(d, dAh + off, dBl + off, idesc, 1u);
-        mma_tf32(d, dAl + off, dBh + off, idesc, 1u);
+        if (!STACKED) mma_tf32(d, dAl + off, dBh + off, idesc, 1u);
       }
       mma_commit(&pb->empty[s]);
     }
@@ -227,16 +229,12 @@ __device__ __forceinline__ bool drain_loop(PipeBarriers* pb, uint32_t tmem, int 
 // (the +4 keeps a quarter-warp's float4 stores to 8 different rows on 8
 // different bank groups). Each epilogue thread writes its row's 128 columns;
 // after epi_sync() the warps copy whole rows out with coalesced stores.
-// With MROWS = 64 only TMEM lanes 0-15 of each quadrant hold D rows (row
-// 16 * quadrant + lane); the other lanes' registers are not staged.
-template <class Cfg, int MROWS = kBM>
+template <class Cfg>
 __device__ __forceinline__ float* stage_tile(uint8_t* tiles, const float (&acc)[128]) {
   constexpr int kPitch = Cfg::BN + 4;
   float* stage = reinterpret_cast<float*>(tiles);
   const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  if (MROWS == 64 && lane >= 16) return stage;
-  const int row = (warp & 3) * (MROWS / 4) + lane;
+  const int row = (warp & 3) * 32 + (threadIdx.x & 31);
   float* dst = stage + row * kPitch + ((warp - 2) >> 2) * 128;
 #pragma unroll
   for (int j = 0; j < 128; j += 4)
