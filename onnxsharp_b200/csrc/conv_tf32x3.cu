@@ -233,10 +233,17 @@ struct Cfg {
   static constexpr int kB = BN * kBK * 4;                 // one weight part: BN oc x 32 ch
   static constexpr int kStage = 2 * kA + 2 * kB;          // A (hi after the split) | A lo | W hi | W lo
   static constexpr int kTx = kA + 2 * kB;                 // bytes TMA lands per stage
-  // Every TMEM column: 512 / BN accumulators, so the MMA runs up to that many
-  // TMEM chunks ahead of the epilogue warps, which drain a chunk every kKC
-  // k-blocks and also store the previous tile's outputs.
-  static constexpr int kAccBufs = 512 / BN;
+  // 64-channel tiles stack [W hi; W lo] along N: per K step one MMA of
+  // A hi against both weight parts (N = 64 + the tile's channels) and one of
+  // A lo against W hi, instead of three N = 64 MMAs (an MMA's issue cost
+  // hardly depends on N). The accumulator then spans 2 * BN columns: A*W hi
+  // in the first BN, A hi*W lo in the next, added by the drain.
+  static constexpr bool kStackN = BN == 64;
+  static constexpr int kAccCols = kStackN ? 2 * BN : BN;
+  // Every TMEM column: 512 / kAccCols accumulators, so the MMA runs up to that
+  // many TMEM chunks ahead of the epilogue warps, which drain a chunk every
+  // kKC k-blocks and also store the previous tile's outputs.
+  static constexpr int kAccBufs = 512 / kAccCols;
   static constexpr int kTmemCols = 512;
   static constexpr int kColsMax = BN / kEpiGroups;        // output channels per epilogue warp on a full tile
   static constexpr int kSmemBase = kStages * kStage + 1024 + kBarsBytes;  // + the bias table (M floats, rounded to 16 bytes)
@@ -395,6 +402,7 @@ __global__ void __launch_bounds__(pw::kThreads, 1)
         const int oc0 = tl.ot * CF::kBN;
         const int nn = min(CF::kBN, ((g.M - oc0) + 15) & ~15);
         const uint32_t idesc = TAPS ? idesc_tf32(kBM, nn) : idesc_tf32_amn(kBM, nn);
+        const uint32_t idesc_st = TAPS ? idesc_tf32(kBM, CF::kBN + nn) : idesc_tf32_amn(kBM, CF::kBN + nn);
         int kb = tl.kb_begin;
         for (int c = tl.c_begin; c < tl.c_end && ok; ++c, ++gc) {
           const int buf = gc % CF::kAccBufs;
@@ -403,7 +411,7 @@ __global__ void __launch_bounds__(pw::kThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t d = tmem + static_cast<uint32_t>(buf * CF::kBN);
+          const uint32_t d = tmem + static_cast<uint32_t>(buf * CF::kAccCols);
           const int kb_end = min(g.num_kb, kb + kKC);
           uint32_t acc = 0u;
           for (; kb < kb_end; ++kb, ++i) {
@@ -427,10 +435,16 @@ __global__ void __launch_bounds__(pw::kThreads, 1)
               // +1024 bytes: the next 8 channel rows (MN-major); +32 bytes inside the K-major row
               const uint64_t ao = static_cast<uint64_t>(TAPS ? kk * 2 : kk * 64);
               const uint64_t bo = static_cast<uint64_t>(kk * 2);   // +32 bytes inside the K-major row
-              mma_tf32(d, dAh + ao, dBh + bo, idesc, acc);
-              acc = 1u;
-              mma_tf32(d, dAh + ao, dBl + bo, idesc, 1u);
-              mma_tf32(d, dAl + ao, dBh + bo, idesc, 1u);
+              if constexpr (CF::kStackN) {
+                mma_tf32(d, dAh + ao, dBh + bo, idesc_st, acc);  // A hi * [W hi; W lo]
+                acc = 1u;
+                mma_tf32(d, dAl + ao, dBh + bo, idesc, 1u);      // A lo * W hi
+              } else {
+                mma_tf32(d, dAh + ao, dBh + bo, idesc, acc);
+                acc = 1u;
+                mma_tf32(d, dAh + ao, dBl + bo, idesc, 1u);
+                mma_tf32(d, dAl + ao, dBh + bo, idesc, 1u);
+              }
             }
             mma_commit(&pb->empty[s]);
           }
@@ -506,7 +520,19 @@ __global__ void __launch_bounds__(pw::kThreads, 1)
         }
         tc_fence_after();
         const uint32_t base =
-            tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * CF::kBN + h * cpw);
+            tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * CF::kAccCols + h * cpw);
+        if constexpr (CF::kStackN) {  // 16 channels per warp: A * W hi plus A hi * W lo
+          static_assert(CF::kColsMax == 16, "stacked drain");
+          uint32_t r0[16], r1[16];
+          tmem_ld16(base, r0);
+          tmem_ld16(base + CF::kBN, r1);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const float v = __fadd_rn(__uint_as_float(r0[j]), __uint_as_float(r1[j]));
+            acc[j] = c == tl.c_begin ? v : __fadd_rn(acc[j], v);
+          }
+        } else {
 #pragma unroll
         for (int gg = 0; gg < CF::kColsMax / 16; gg += CF::kColsMax > 32 ? 2 : 1) {
           if (gg * 16 >= cpw) break;
@@ -531,6 +557,7 @@ __global__ void __launch_bounds__(pw::kThreads, 1)
                 acc[(gg + 1) * 16 + j] = __fadd_rn(acc[(gg + 1) * 16 + j], __uint_as_float(r1[j]));
             }
           }
+        }
         }
         tc_fence_before();
         __syncwarp();
