@@ -196,9 +196,11 @@ __global__ void __launch_bounds__(ConvCfg::THREADS, 1)
 //    128-byte swizzle with 32-byte atoms that MN-major TF32 operands need:
 //    4-channel groups 512 bytes apart, 32-pixel groups 4 KB apart), its lo
 //    part, and the prepacked weight hi/lo boxes (K-major);
-//  - persistent CTAs walk the tiles; TMEM holds 512 / BN accumulators (4 or
-//    8), so the epilogue of one tile overlaps the main loop of the next and
-//    the MMA runs several TMEM chunks ahead of the drain;
+//  - persistent CTAs walk the tiles; TMEM holds 4 accumulators (all 512
+//    columns: 128 per accumulator on either tile width, the 64-channel tile
+//    stacking its hi / lo weight products side by side), so the epilogue of
+//    one tile overlaps the main loop of the next and the MMA runs several
+//    TMEM chunks ahead of the drain;
 //  - epilogue (16 warps, four per TMEM lane quadrant): lane = pixel, so each
 //    warp store writes 32 consecutive pixels of one output channel (128
 //    bytes): NCHW without a staging tile. Biases come from a shared-memory
