@@ -521,6 +521,7 @@ class AttentionWorkload(Workload):
         self.bias = torch.zeros(self.C, device=dev)
         self.w = [GemmWeights(ctx, torch.from_numpy(w).to(dev), self.C, self.C) for w in ws]
         self.qkv = [torch.empty(cnt * self.T, self.C, device=dev) for _ in range(3)]
+        self.x_split = (torch.empty(cnt * self.T, self.C, device=dev), torch.empty(cnt * self.T, self.C, device=dev))
         self.o = torch.empty(cnt, self.T, self.C, device=dev)
         self.y = torch.empty(cnt * self.T, self.C, device=dev)
         self.gather = sh.world > 1 and not self.replicas
@@ -539,10 +540,12 @@ class AttentionWorkload(Workload):
         return 2.0 * self.seqs * self.T * 512 * 512
 
     def _run(self, x):
-        from onnxsharp_b200.runtime import attention, gemm_bias
+        from onnxsharp_b200.runtime import attention, gemm_bias, gemm_bias_presplit, gemm_split_a
 
+        # the three projections share their input: split it once
+        split = gemm_split_a(self.ctx, x, self.C, out=self.x_split)
         for w, out in zip(self.w[:3], self.qkv):
-            gemm_bias(self.ctx, x, w, self.bias, out=out)
+            gemm_bias_presplit(self.ctx, split, w, self.bias, out=out)
         q, k, v = (t.view(self.seqs, self.T, self.C) for t in self.qkv)
         attention(self.ctx, q, k, v, self.H, 0.125, out=self.o)
         gemm_bias(self.ctx, self.o.view(self.seqs * self.T, self.C), self.w[3], self.bias, out=self.y)

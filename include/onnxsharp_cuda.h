@@ -251,6 +251,21 @@ OSC_API int osc_gemm_bias_f32(osc_ctx* ctx, const float* a, int m, int k, int ld
                               const osc_gemm_weights* w, const float* col_bias, int act, float* c,
                               int ldc);
 
+/* osc_gemm_bias_f32 in two steps, for an activation that feeds several
+ * MatMuls (the Q, K and V projections of one input, each its own MatMul node
+ * with FusedBias in the reference: Ops/DnnOps.cs:2902-3102): split A once,
+ * then multiply the split by each packed weight. Same kernels and results as
+ * osc_gemm_bias_f32. osc_gemm_split_a_f32 writes the K-major TF32 operands
+ * a_hi, a_lo [m][kp] (kp = k rounded up to a multiple of 4, the packed
+ * weights' kp; both 16-byte aligned, caller-allocated, m * kp floats each).
+ * osc_gemm_bias_presplit_f32 then computes C = A @ B + bias (then act) from
+ * them; its kp must match the weights'. */
+OSC_API int osc_gemm_split_a_f32(osc_ctx* ctx, const float* a, int m, int k, int lda, int kp,
+                                 float* a_hi, float* a_lo);
+OSC_API int osc_gemm_bias_presplit_f32(osc_ctx* ctx, const float* a_hi, const float* a_lo, int m,
+                                       int kp, const osc_gemm_weights* w, const float* col_bias,
+                                       int act, float* c, int ldc);
+
 /* Same as osc_gemm_bias_f32, but allocates no device memory: for callers that
  * must not call cudaMalloc while serving (a host that fixes its GPU memory
  * budget at start-up, or one sharing the GPU with other work, where an

@@ -107,6 +107,8 @@ SIGNATURES: dict[str, tuple] = {
     "osc_gemm_weights_free": (i32, [vp]),
     "osc_gemm_bias_f32": (i32, [vp, vp, i32, i32, i32, vp, vp, i32, vp, i32]),
     "osc_gemm_bias_f32_noalloc": (i32, [vp, vp, i32, i32, i32, vp, vp, i32, vp, i32]),
+    "osc_gemm_split_a_f32": (i32, [vp, vp, i32, i32, i32, i32, vp, vp]),
+    "osc_gemm_bias_presplit_f32": (i32, [vp, vp, vp, i32, i32, vp, vp, i32, vp, i32]),
     # Conv + FusedActivation
     "osc_conv_prepack_f32": (i32, [vp, vp, i32, i32, i32, i32, i32, pp]),
     "osc_conv_weights_free": (i32, [vp]),

@@ -1201,6 +1201,47 @@ OSC_API int osc_gemm_bias_f32(osc_ctx* ctx, const float* a, int m, int k, int ld
   return gemm_tf32x3(ctx, a, m, k, lda, w, col_bias, act, c, ldc);
 }
 
+// MatMul in two steps for activations that feed several MatMuls (the Q, K and
+// V projections of one input): split A once into its K-major TF32 hi/lo
+// operands, then multiply that split by each packed weight. Same kernels and
+// results as osc_gemm_bias_f32, without re-splitting A per weight.
+OSC_API int osc_gemm_split_a_f32(osc_ctx* ctx, const float* a, int m, int k, int lda, int kp, float* a_hi,
+                                 float* a_lo) {
+  OSC_TRY(enter(ctx));
+  if (m < 0 || k <= 0) return fail(OSC_EINVAL, "osc_gemm_split_a_f32: m=%d k=%d", m, k);
+  if (lda == 0) lda = k;
+  if (lda < k) return fail(OSC_EINVAL, "osc_gemm_split_a_f32: lda=%d < k=%d", lda, k);
+  if (kp != static_cast<int>(round_up(static_cast<size_t>(k), 4)))
+    return fail(OSC_EINVAL, "osc_gemm_split_a_f32: kp=%d, expected k rounded up to 4 (%d)", kp,
+                static_cast<int>(round_up(static_cast<size_t>(k), 4)));
+  if (m == 0) return OSC_OK;
+  if (a == nullptr || a_hi == nullptr || a_lo == nullptr) return fail(OSC_EINVAL, "osc_gemm_split_a_f32: null pointer");
+  auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  if (!al16(a_hi) || !al16(a_lo)) return fail(OSC_EINVAL, "osc_gemm_split_a_f32: a_hi / a_lo not 16-byte aligned");
+  if (fault_injected("launch")) return fail(OSC_EFAULT_INJECTED, "injected failure (launch)");
+  return split_tf32(ctx, a, m, k, lda, kp, a_hi, a_lo);
+}
+
+OSC_API int osc_gemm_bias_presplit_f32(osc_ctx* ctx, const float* a_hi, const float* a_lo, int m, int kp,
+                                       const osc_gemm_weights* w, const float* col_bias, int act, float* c, int ldc) {
+  OSC_TRY(enter(ctx));
+  if (w == nullptr) return fail(OSC_EINVAL, "osc_gemm_bias_presplit_f32: null weights");
+  if (w->device != ctx->device)
+    return fail(OSC_EINVAL, "osc_gemm_bias_presplit_f32: weights live on another device");
+  if (kp != w->kp) return fail(OSC_EINVAL, "osc_gemm_bias_presplit_f32: A split with kp=%d, packed B has kp=%d", kp, w->kp);
+  if (m < 0) return fail(OSC_EINVAL, "osc_gemm_bias_presplit_f32: m=%d", m);
+  if (act < OSC_ACT_NONE || act > OSC_ACT_SIGMOID) return fail(OSC_EINVAL, "osc_gemm_bias_presplit_f32: act=%d", act);
+  if (ldc == 0) ldc = w->n;
+  if (ldc < w->n) return fail(OSC_EINVAL, "osc_gemm_bias_presplit_f32: ldc=%d too small", ldc);
+  if (m == 0) return OSC_OK;
+  if (a_hi == nullptr || a_lo == nullptr || c == nullptr)
+    return fail(OSC_EINVAL, "osc_gemm_bias_presplit_f32: null pointer");
+  auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  if (!al16(a_hi) || !al16(a_lo)) return fail(OSC_EINVAL, "osc_gemm_bias_presplit_f32: a_hi / a_lo not 16-byte aligned");
+  if (fault_injected("launch")) return fail(OSC_EFAULT_INJECTED, "injected failure (launch)");
+  return gemm_presplit(ctx, a_hi, a_lo, m, kp, w, col_bias, act, c, ldc);
+}
+
 }  // extern "C"
 
 // ---------------------------------------------------------------------------

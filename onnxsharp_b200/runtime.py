@@ -336,6 +336,34 @@ def _is_device(x) -> bool:
     return bool(getattr(x, "is_cuda", False))
 
 
+def gemm_split_a(ctx: Context, a, k: int, out=None):
+    """The K-major TF32 hi/lo split of A [m, k] (FP32 on the device) that the
+    MatMul kernels read, as a (hi, lo) pair of [m, kp] tensors (kp = k rounded
+    up to 4): split once, then gemm_bias_presplit by several weights."""
+    import torch
+
+    m, kp = int(a.shape[0]), (int(k) + 3) // 4 * 4
+    if out is None:
+        out = (torch.empty((m, kp), dtype=torch.float32, device=a.device),
+               torch.empty((m, kp), dtype=torch.float32, device=a.device))
+    call("osc_gemm_split_a_f32", ctx.handle, ptr(a), m, int(k), int(a.stride(0)), kp, ptr(out[0]), ptr(out[1]))
+    return out
+
+
+def gemm_bias_presplit(ctx: Context, split, w: GemmWeights, bias=None, act: int = _lib.ACT_NONE, out=None,
+                       ldc: int = 0):
+    """C = A @ B + bias, then `act`, from A's split (gemm_split_a)."""
+    import torch
+
+    hi, lo = split
+    m, kp = int(hi.shape[0]), int(hi.shape[1])
+    if out is None:
+        out = torch.empty((m, w.n), dtype=torch.float32, device=hi.device)
+    call("osc_gemm_bias_presplit_f32", ctx.handle, ptr(hi), ptr(lo), m, kp, w.handle, ptr(bias), int(act), ptr(out),
+         int(ldc or out.stride(0)))
+    return out
+
+
 def gemm_bias(ctx: Context, a, w: GemmWeights, bias=None, act: int = _lib.ACT_NONE, out=None, lda: int = 0,
               ldc: int = 0):
     """C = A @ B + bias (FusedBias), then `act`; A is [m, k] FP32 on the device."""

@@ -139,3 +139,35 @@ def test_gemm_rejects_mismatched_k(ctx):
     w = GemmWeights(ctx, torch.ones(8, 8, device="cuda"), 8, 8)
     with pytest.raises(OscError):
         gemm_bias(ctx, torch.ones(4, 9, device="cuda"), type("W", (), {"k": 9, "n": 8, "handle": w.handle})())
+
+
+def test_gemm_split_once_three_weights(ctx):
+    """One activation split once (osc_gemm_split_a_f32, strided rows, k not a
+    multiple of 4) multiplied by three packed weights, as the Q/K/V
+    projections of one input; each product equals the oracle's and the
+    one-step entry point's results."""
+    import torch
+
+    from onnxsharp_b200 import OscError
+    from onnxsharp_b200.runtime import GemmWeights, gemm_bias, gemm_bias_presplit, gemm_split_a
+
+    rng = np.random.default_rng(11)
+    m, k, lda = 700, 301, 320
+    big = rng.uniform(-1, 1, (m, lda)).astype(np.float32)
+    a = np.ascontiguousarray(big[:, :k])
+    ta = torch.from_numpy(big).cuda()[:, :k]
+    split = gemm_split_a(ctx, ta, k)
+    assert split[0].shape == (m, 304)
+    for n, act in ((512, 0), (96, 1), (1500, 0)):
+        b = rng.uniform(-1, 1, (k, n)).astype(np.float32)
+        bias = rng.uniform(-1, 1, n).astype(np.float32)
+        w = GemmWeights(ctx, torch.from_numpy(b).cuda(), k, n)
+        tb = torch.from_numpy(bias).cuda()
+        got = gemm_bias_presplit(ctx, split, w, tb, act)
+        one = gemm_bias(ctx, ta, w, tb, act, lda=lda)
+        ctx.synchronize()
+        assert rel_err(got.cpu().numpy(), oracle.gemm(a, b, col_bias=bias, act=act)) <= TOL
+        assert torch.equal(got, one)
+    w_small = GemmWeights(ctx, torch.ones(64, 8, device="cuda"), 64, 8)
+    with pytest.raises(OscError, match="kp"):
+        gemm_bias_presplit(ctx, split, w_small)
