@@ -159,14 +159,18 @@ def conv_out(size: int, k: int, s: int, p0: int, p1: int, d: int) -> int:
     return (size + p0 + p1 - ((k - 1) * d + 1)) // s + 1
 
 
-def conv2d(x, w, bias=None, stride=(1, 1), pads=(0, 0, 0, 0), dil=(1, 1), group=1, act=0, threads: int = THREADS):
-    """NCHW conv; pads = (top, left, bottom, right)."""
+def conv2d(x, w, bias=None, stride=(1, 1), pads=(0, 0, 0, 0), dil=(1, 1), group=1, act=0, threads: int = THREADS,
+           out=None):
+    """NCHW conv; pads = (top, left, bottom, right). `out`: an optional
+    C-contiguous float32 [N, M, OH, OW] array to write into."""
     x, w = _c(x), _c(w)
     N, Cc, H, W = x.shape
     M, _, kh, kw = w.shape
     OH = conv_out(H, kh, stride[0], pads[0], pads[2], dil[0])
     OW = conv_out(W, kw, stride[1], pads[1], pads[3], dil[1])
-    y = np.empty((N, M, OH, OW), np.float32)
+    if out is not None and (out.shape != (N, M, OH, OW) or out.dtype != np.float32 or not out.flags.c_contiguous):
+        raise ValueError("conv2d: out must be a C-contiguous float32 array of the output shape")
+    y = np.empty((N, M, OH, OW), np.float32) if out is None else out
     b = _c(bias)
     lib().orc_conv2d(_p(x), N, Cc, H, W, _p(w), M, kh, kw, stride[0], stride[1], pads[0], pads[1], dil[0], dil[1], group,
                      _p(b), act, _p(y), OH, OW, threads)

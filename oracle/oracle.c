@@ -287,6 +287,34 @@ void orc_conv2d(const float* x, int N, int C, int H, int W, const float* w, int 
                 int threads) {
   const int cpg = C / group, mpg = M / group;
   const int K = cpg * kh * kw; /* im2col row order (ic, ky, kx), ConvKernels.cs:262-462 */
+  if (group == 1 && (OW < 64 || OW % 16 != 0)) {
+    /* Narrow images (an output row fills few or no 16-wide panels): the whole
+     * image's columns [K][OH*OW] (FillColumns, zero outside the image), then
+     * W [M][K] times them through orc_gemm_f32 with the bias as the row bias.
+     * Every output's chain is the same as below -- acc = bias, then
+     * fma(W[o][t], col[t][p], acc) for t ascending -- blocked over all of the
+     * image's pixels instead of one output row at a time. */
+    const long HW = (long)OH * OW;
+    float* col = (float*)malloc(sizeof(float) * (size_t)K * (size_t)(HW > 0 ? HW : 1));
+    for (int nb = 0; nb < N; ++nb) {
+#pragma omp parallel for num_threads(nthreads(threads)) schedule(static)
+      for (long r = 0; r < (long)K * OH; ++r) {
+        const int t = (int)(r / OH), oy = (int)(r % OH);
+        const int ic = t / (kh * kw), ky = (t / kw) % kh, kx = t % kw;
+        const float* xc = x + ((size_t)nb * C + ic) * H * W;
+        const int iy = oy * sh - pt + ky * dh;
+        float* cr = col + (size_t)t * HW + (size_t)oy * OW;
+        for (int ox = 0; ox < OW; ++ox) {
+          const int ix = ox * sw - pl + kx * dw;
+          cr[ox] = (iy >= 0 && iy < H && ix >= 0 && ix < W) ? xc[(size_t)iy * W + ix] : 0.0f;
+        }
+      }
+      orc_gemm_f32(w, K, col, (int)HW, M, K, (int)HW, bias, NULL, NULL, 0, act, y + (size_t)nb * M * HW, (int)HW,
+                   threads);
+    }
+    free(col);
+    return;
+  }
   const long tasks = (long)N * group * OH;
 #pragma omp parallel num_threads(nthreads(threads))
   {

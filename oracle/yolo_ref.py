@@ -73,10 +73,19 @@ def _decode(boxes, classes, strides, threads):
     return np.concatenate([dbox, oracle.unary(cls, 3, threads=threads)], 1)   # Sigmoid, Concat
 
 
+_BUFS: dict = {}
+
+
 def run(g, params: dict, images: np.ndarray, threads: int = 0) -> np.ndarray:
     """Run the plan on [B, 3, H, W] images; returns [B, 4 + nc, A]."""
     n = images.shape[0]
-    bufs = {name: np.zeros((n, c, h, w), np.float32) for name, (c, h, w) in g.buffers.items()}
+    # the activation buffers, allocated once per (graph, batch) like the
+    # reference's arena; every element is written by its producer before use
+    key = (id(g), n)
+    if key not in _BUFS:
+        _BUFS.clear()
+        _BUFS[key] = {name: np.empty((n, c, h, w), np.float32) for name, (c, h, w) in g.buffers.items()}
+    bufs = _BUFS[key]
     bufs[g.input][...] = images
 
     def view(r):
@@ -88,11 +97,14 @@ def run(g, params: dict, images: np.ndarray, threads: int = 0) -> np.ndarray:
         if node.op == "conv":
             x = np.ascontiguousarray(view(node.ins[0]))
             k, s, p = a["k"], a["s"], a["p"]
+            dst = view(node.outs[0])
+            direct = dst.flags.c_contiguous and not a["residual"]   # a channel slice of one image is contiguous
             y = oracle.conv2d(x, params[node.name + ".w"], params[node.name + ".b"], (s, s), (p, p, p, p), (1, 1),
-                              a["group"], a["act"], threads=threads)
+                              a["group"], a["act"], threads=threads, out=dst if direct else None)
             if a["residual"]:
-                y = (view(node.ins[1]) + y).astype(np.float32)   # Add(x, act(conv))
-            view(node.outs[0])[...] = y
+                np.add(view(node.ins[1]), y, out=y)   # Add(x, act(conv)), float32
+            if not direct:
+                dst[...] = y
         elif node.op == "maxpool":
             view(node.outs[0])[...] = _maxpool(view(node.ins[0]), a["k"], a["s"], a["p"])
         elif node.op == "upsample":
