@@ -178,9 +178,10 @@ def test_conv_split_k_views_and_residual(ctx, k, C, M):
                                             (36, 32, 80, 64, 2)])
 def test_conv_channel_major_narrow_layers(ctx, N, C, H, M, stride):
     """Layers of at most 64 output channels on the channel-major kernel (many
-    256-pixel tiles): M = 64 MMAs over 64-row weight boxes, D rows read from
-    the first 16 TMEM lanes of each quadrant; 48 channels leave a partial
-    quadrant. The launch is checked to be the channel-major kernel."""
+    256-pixel tiles): 64-row weight boxes stacked [W hi; W lo] into one
+    128-row operand, 2 MMAs per K step, the epilogue adding D rows r and
+    r + 64; 48 and 32 channels leave zero rows in both halves. The launch is
+    checked to be the channel-major kernel."""
     x, w, b = _case(50 + M + stride, N, C, H, H, M, 3)
     ctx.profile_reset()
     ctx.profile(True)
