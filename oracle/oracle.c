@@ -287,6 +287,16 @@ void orc_conv2d(const float* x, int N, int C, int H, int W, const float* w, int 
                 int threads) {
   const int cpg = C / group, mpg = M / group;
   const int K = cpg * kh * kw; /* im2col row order (ic, ky, kx), ConvKernels.cs:262-462 */
+  if (group == 1 && kh == 1 && kw == 1 && sh == 1 && sw == 1 && pt == 0 && pl == 0 && OH == H && OW == W) {
+    /* 1x1, stride 1, unpadded: the image [C][H*W] already is the column
+     * matrix, so W [M][C] times it through orc_gemm_f32 with the bias as the
+     * row bias -- the same chains (acc = bias, then fma over c ascending). */
+    const long HW = (long)H * W;
+    for (int nb = 0; nb < N; ++nb)
+      orc_gemm_f32(w, C, x + (size_t)nb * C * HW, (int)HW, M, C, (int)HW, bias, NULL, NULL, 0, act,
+                   y + (size_t)nb * M * HW, (int)HW, threads);
+    return;
+  }
   if (group == 1 && (OW < 64 || OW % 16 != 0)) {
     /* Narrow images (an output row fills few or no 16-wide panels): the whole
      * image's columns [K][OH*OW] (FillColumns, zero outside the image), then
