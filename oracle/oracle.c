@@ -118,12 +118,68 @@ static void mk_block(int R, const float* A, long lda, const float* B, long ldb, 
   }
 }
 
+/* The same chains for two 16-column panels at once (B0 / B1, row pitches
+ * ldb0 / ldb1, accumulators acc0 / acc1) with 512-bit vectors: each lane of
+ * _mm512_fmadd_ps is one fmaf, so the results equal mk_rows' bit for bit.
+ * Used only when the CPU reports AVX-512F (checked at run time). */
+static inline __attribute__((always_inline, target("avx512f"))) void mk_pair_rows(
+    int R, const float* A, long lda, const float* B0, long ldb0, const float* B1, long ldb1, int K, float* acc0,
+    float* acc1, long ldacc) {
+  __m512 c0[6], c1[6];
+  for (int r = 0; r < 6; ++r) {
+    if (r < R) {
+      c0[r] = _mm512_loadu_ps(acc0 + r * ldacc);
+      c1[r] = _mm512_loadu_ps(acc1 + r * ldacc);
+    }
+  }
+  for (int t = 0; t < K; ++t) {
+    const __m512 b0 = _mm512_loadu_ps(B0 + (long)t * ldb0);
+    const __m512 b1 = _mm512_loadu_ps(B1 + (long)t * ldb1);
+    for (int r = 0; r < 6; ++r) {
+      if (r < R) {
+        const __m512 av = _mm512_set1_ps(A[r * lda + t]);
+        c0[r] = _mm512_fmadd_ps(av, b0, c0[r]);
+        c1[r] = _mm512_fmadd_ps(av, b1, c1[r]);
+      }
+    }
+  }
+  for (int r = 0; r < 6; ++r) {
+    if (r < R) {
+      _mm512_storeu_ps(acc0 + r * ldacc, c0[r]);
+      _mm512_storeu_ps(acc1 + r * ldacc, c1[r]);
+    }
+  }
+}
+
+static __attribute__((target("avx512f"))) void mk_pair(int R, const float* A, long lda, const float* B0, long ldb0,
+                                                        const float* B1, long ldb1, int K, float* acc0, float* acc1,
+                                                        long ldacc) {
+  switch (R) {
+    case 6: mk_pair_rows(6, A, lda, B0, ldb0, B1, ldb1, K, acc0, acc1, ldacc); break;
+    case 5: mk_pair_rows(5, A, lda, B0, ldb0, B1, ldb1, K, acc0, acc1, ldacc); break;
+    case 4: mk_pair_rows(4, A, lda, B0, ldb0, B1, ldb1, K, acc0, acc1, ldacc); break;
+    case 3: mk_pair_rows(3, A, lda, B0, ldb0, B1, ldb1, K, acc0, acc1, ldacc); break;
+    case 2: mk_pair_rows(2, A, lda, B0, ldb0, B1, ldb1, K, acc0, acc1, ldacc); break;
+    default: mk_pair_rows(1, A, lda, B0, ldb0, B1, ldb1, K, acc0, acc1, ldacc); break;
+  }
+}
+
+static int have_avx512(void) {
+  static int v = -1;
+  if (v < 0) v = __builtin_cpu_supports("avx512f") ? 1 : 0;
+  return v;
+}
+
 /* acc[r][j] for r < R, j < J (pitch ldacc): full 16-column panels through the
- * blocked kernel, the remaining columns through the scalar chain. */
+ * blocked kernel (two at a time with AVX-512), the remaining columns through
+ * the scalar chain. */
 static void accumulate(int R, int J, const float* A, long lda, const float* B, long ldb, int K, float* acc,
                        long ldacc) {
   const int J16 = J / 16 * 16;
-  for (int j = 0; j < J16; j += 16) mk_block(R, A, lda, B + j, ldb, K, acc + j, ldacc);
+  int j0 = 0;
+  if (have_avx512())
+    for (; j0 + 32 <= J16; j0 += 32) mk_pair(R, A, lda, B + j0, ldb, B + j0 + 16, ldb, K, acc + j0, acc + j0 + 16, ldacc);
+  for (int j = j0; j < J16; j += 16) mk_block(R, A, lda, B + j, ldb, K, acc + j, ldacc);
   for (int r = 0; r < R; ++r)
     for (int j = J16; j < J; ++j) {
       float v = acc[r * ldacc + j];
@@ -161,7 +217,12 @@ void orc_gemm_f32(const float* a, int lda, const float* b, int ldb, int m, int k
           acc[r * kGemmCols + jj] = col_scale ? 0.0f : (col_bias ? col_bias[j] : (row_bias ? row_bias[i] : 0.0f));
         }
       const int J16 = (j0 + J <= full_cols) ? J : full_cols - j0;
-      for (int jj = 0; jj < J16; jj += 16)
+      int jj0 = 0;
+      if (have_avx512())
+        for (; jj0 + 32 <= J16; jj0 += 32)
+          mk_pair(R, a + (size_t)i0 * lda, lda, bp + (size_t)(j0 + jj0) * k, 16, bp + (size_t)(j0 + jj0 + 16) * k, 16,
+                  k, acc + jj0, acc + jj0 + 16, kGemmCols);
+      for (int jj = jj0; jj < J16; jj += 16)
         mk_block(R, a + (size_t)i0 * lda, lda, bp + (size_t)(j0 + jj) * k, 16, k, acc + jj, kGemmCols);
       if (J16 < J)
         accumulate(R, J - J16, a + (size_t)i0 * lda, lda, b + j0 + J16, ldb, k, acc + J16, kGemmCols);
