@@ -159,6 +159,38 @@ def test_conv_matches_float64_direct():
     assert rel_err(y, ref) < 1e-5
 
 
+def _conv64(x, w, b, s, p):
+    """float64 direct convolution, group 1, square stride s and padding p."""
+    N, C, H, W = x.shape
+    M, _, k, _ = w.shape
+    xp = np.pad(x.astype(np.float64), ((0, 0), (0, 0), (p, p), (p, p)))
+    OH, OW = (H + 2 * p - k) // s + 1, (W + 2 * p - k) // s + 1
+    ref = np.zeros((N, M, OH, OW)) + b.astype(np.float64)[None, :, None, None]
+    for ky in range(k):
+        for kx in range(k):
+            patch = xp[:, :, ky:ky + s * (OH - 1) + 1:s, kx:kx + s * (OW - 1) + 1:s]
+            ref += np.einsum("nchw,mc->nmhw", patch, w[:, :, ky, kx].astype(np.float64))
+    return ref
+
+
+@pytest.mark.parametrize("C,M,H,W,k,s,p", [
+    (40, 24, 20, 20, 1, 1, 0),    # 1x1: the blocked GEMM straight on the image
+    (16, 20, 20, 44, 3, 1, 1),    # narrow rows: whole-image columns times the GEMM
+    (12, 18, 9, 80, 3, 2, 1),     # 40-wide output rows (stride 2): whole-image columns
+    (8, 14, 6, 128, 3, 1, 1),     # 128-wide rows: the row-at-a-time path
+    (5, 7, 5, 64, 5, 1, 2),       # 64-wide rows, 5x5
+])
+def test_conv_paths_match_float64(C, M, H, W, k, s, p):
+    """Every group-1 conv route of the oracle (1x1 GEMM, whole-image columns,
+    row at a time) against a float64 convolution."""
+    rng = np.random.default_rng(C * 100 + W)
+    x = rng.uniform(-1, 1, (2, C, H, W)).astype(np.float32)
+    w = rng.normal(0, 0.3, (M, C, k, k)).astype(np.float32)
+    b = rng.normal(0, 0.1, M).astype(np.float32)
+    y = oracle.conv2d(x, w, b, stride=(s, s), pads=(p, p, p, p))
+    assert rel_err(y, _conv64(x, w, b, s, p)) < 1e-5
+
+
 def _attn_ref(q, k, v, heads, scale):
     B, T, Cw = q.shape
     D = Cw // heads
